@@ -1,0 +1,173 @@
+// Shared device helpers for the sm_100a kernels.
+//
+// Every kernel source is compiled with --fmad=false: the reference computes in
+// unfused float32 except where its amd64 assembly uses VFMADD231PS, and those
+// places call fmaf() explicitly here. Keeping contraction off is what makes the
+// element-wise kernels bit-identical to the reference's Go code.
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace sem {
+
+constexpr float kFloatMagic = 12582912.0f;      // 1.5 * 2^23
+constexpr int kFloatMagicBits = 0x4B400000;     // bit pattern of kFloatMagic
+
+// fastExp (internal/kernels/activation.go:100-145), restated operation by operation.
+__device__ __forceinline__ float fast_exp_ref(float x) {
+  if (x < -10.0f) return 0.0f;
+  if (x > 10.0f) return 22026.4657948f;
+  float y = __fmul_rn(x, 1.442695041f);
+  int ip = (int)y;  // Go int32(y): truncation toward zero
+  float f = __fsub_rn(y, (float)ip);
+  const float c1 = 0.693147180559945f, c2 = 0.240226506959101f, c3 = 0.055504108664821f,
+              c4 = 0.009676036358193f;
+  float poly = __fadd_rn(
+      1.0f, __fmul_rn(f, __fadd_rn(c1, __fmul_rn(f, __fadd_rn(c2, __fmul_rn(f, __fadd_rn(c3, __fmul_rn(f, c4))))))));
+  if (ip >= -126 && ip <= 127) return __fmul_rn(poly, __uint_as_float((uint32_t)(ip + 127) << 23));
+  if (ip < -126) return 0.0f;
+  return 3.402823e+38f;
+}
+
+// GELUQuickSIMD element (activation.go:47-95): x * sigmoid(1.702 x) through fastExp.
+__device__ __forceinline__ float gelu_quick_ref(float x) {
+  float sx = __fmul_rn(1.702f, x);
+  float sig;
+  if (sx >= 0.0f) {
+    float e = fast_exp_ref(-sx);
+    sig = __fdiv_rn(1.0f, __fadd_rn(1.0f, e));
+  } else {
+    float e = fast_exp_ref(sx);
+    sig = __fdiv_rn(e, __fadd_rn(1.0f, e));
+  }
+  return __fmul_rn(x, sig);
+}
+
+// Sum of squares of a row in the order of dotProductAVX2Asm
+// (internal/kernels/simd_amd64.s:19-76): 8 fused lane accumulators over the row
+// (lane l takes elements 8v+l), then the VEXTRACTF128/VADDPS/VHADDPS horizontal
+// sum. Computed by the 8 consecutive lanes of a warp that share `sub` = lane & 7;
+// every lane of the group receives the total. n must be a multiple of 8.
+__device__ __forceinline__ float row_sumsq_ref(const float* __restrict__ x, int n, int sub) {
+  float acc = 0.0f;
+#pragma unroll 8
+  for (int v = 0; v < n / 8; ++v) {
+    float t = x[8 * v + sub];
+    acc = fmaf(t, t, acc);
+  }
+  const unsigned full = 0xffffffffu;
+  float hi = __shfl_down_sync(full, acc, 4, 8);   // sub 0..3 receive acc[sub+4]
+  float s = __fadd_rn(acc, hi);                   // s_i = acc_i + acc_{i+4}
+  float s1 = __shfl_down_sync(full, s, 1, 8);
+  float p = __fadd_rn(s, s1);                     // sub0: s0+s1, sub2: s2+s3
+  float p2 = __shfl_down_sync(full, p, 2, 8);
+  float tot = __fadd_rn(p, p2);                   // sub0: (s0+s1)+(s2+s3)
+  return __shfl_sync(full, tot, 0, 8);
+}
+
+// RMSNorm inverse scale (internal/kernels/norm.go:8-36):
+// 1 / float32(sqrt(float64(sumSq/n + eps))).
+__device__ __forceinline__ float rms_inv_ref(float sumsq, int n, float eps) {
+  float mean = __fdiv_rn(sumsq, (float)n);
+  float rms = (float)sqrt((double)__fadd_rn(mean, eps));
+  return __fdiv_rn(1.0f, rms);
+}
+
+// Per-sequence activation scale (quantize.go:60-61) from an absmax bit pattern.
+__device__ __forceinline__ void seq_scale_ref(uint32_t absmax_bits, float* scale, float* inv) {
+  float m = __uint_as_float(absmax_bits);
+  if (m == 0.0f) {
+    *scale = 1.0f;
+    *inv = 0.0f;  // every code is 0 (quantize.go:50-58)
+    return;
+  }
+  float s = __fdiv_rn(m, 127.0f);
+  *scale = s;
+  *inv = __fdiv_rn(1.0f, s);
+}
+
+// quantizeInto element (quantize.go:92-103): round half away from zero of the
+// exact float64 product, clamped to [-127, 127].
+__device__ __forceinline__ int quant_code_ref(float x, float inv) {
+  double r = round((double)x * (double)inv);
+  r = fmin(fmax(r, -127.0), 127.0);
+  return (int)r;
+}
+
+__device__ __forceinline__ void atomic_max_abs(uint32_t* slot, float v) {
+  // non-negative floats order like their bit patterns
+  atomicMax(slot, __float_as_uint(fabsf(v)));
+}
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem, bool valid) {
+  uint32_t s = smem_u32(smem);
+  int sz = valid ? 16 : 0;
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(s), "l"(gmem), "r"(sz));
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;\n" ::"n"(N));
+}
+
+__device__ __forceinline__ void ldmatrix_x4(uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3,
+                                            const void* p) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];\n"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(smem_u32(p)));
+}
+__device__ __forceinline__ void ldmatrix_x4_trans(uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3,
+                                                  const void* p) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];\n"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(smem_u32(p)));
+}
+
+// D = A(16x16 f16) * B(16x8 f16) + C, fp32 accumulate.
+__device__ __forceinline__ void mma_f16(float* c, const uint32_t* a, const uint32_t* b) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};\n"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]));
+}
+
+// Packed fp32 pair arithmetic (sm_100+).
+__device__ __forceinline__ uint64_t pack2(float a, float b) {
+  return (uint64_t)__float_as_uint(a) | ((uint64_t)__float_as_uint(b) << 32);
+}
+__device__ __forceinline__ void unpack2(uint64_t v, float& a, float& b) {
+  a = __uint_as_float((uint32_t)v);
+  b = __uint_as_float((uint32_t)(v >> 32));
+}
+__device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+
+// Splits x into hi + lo halves (hi = fp16(x), lo = fp16(x - hi)) for the
+// three-term fp16 products that give near-fp32 accuracy on the tensor cores.
+__device__ __forceinline__ void split_half(float x, __half& hi, __half& lo) {
+  hi = __float2half_rn(x);
+  lo = __float2half_rn(__fsub_rn(x, __half2float(hi)));
+}
+
+}  // namespace sem

@@ -1,0 +1,97 @@
+// Host-side internals of libsemantica_b200: contexts, device buffers, errors.
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <cstdarg>
+#include <cstdint>
+#include <cstdio>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "../../../include/semantica_b200.h"
+#include "../kernels.h"
+
+namespace sem {
+
+// ---- thread-local error message ----
+int set_error(int code, const char* fmt, ...);
+const char* last_error();
+
+#define SEM_CUDA(call)                                                                             \
+  do {                                                                                             \
+    cudaError_t e_ = (call);                                                                       \
+    if (e_ != cudaSuccess) return ::sem::set_error(SEM_EDEVICE, "%s: %s", #call, cudaGetErrorString(e_)); \
+  } while (0)
+
+// A device allocation that only grows.
+struct DevBuf {
+  void* p = nullptr;
+  size_t bytes = 0;
+  DevBuf() = default;
+  DevBuf(const DevBuf&) = delete;
+  DevBuf& operator=(const DevBuf&) = delete;
+  ~DevBuf() { release(); }
+  void release() {
+    if (p) cudaFree(p);
+    p = nullptr;
+    bytes = 0;
+  }
+  cudaError_t ensure(size_t n) {
+    if (n <= bytes) return cudaSuccess;
+    release();
+    cudaError_t e = cudaMalloc(&p, n);
+    if (e == cudaSuccess) bytes = n;
+    else p = nullptr;
+    return e;
+  }
+  template <class T>
+  T* as() const { return static_cast<T*>(p); }
+};
+
+// Pinned host staging that only grows.
+struct HostBuf {
+  void* p = nullptr;
+  size_t bytes = 0;
+  HostBuf() = default;
+  HostBuf(const HostBuf&) = delete;
+  HostBuf& operator=(const HostBuf&) = delete;
+  ~HostBuf() { if (p) cudaFreeHost(p); }
+  cudaError_t ensure(size_t n) {
+    if (n <= bytes) return cudaSuccess;
+    if (p) cudaFreeHost(p);
+    p = nullptr;
+    bytes = 0;
+    cudaError_t e = cudaMallocHost(&p, n);
+    if (e == cudaSuccess) bytes = n;
+    return e;
+  }
+  template <class T>
+  T* as() const { return static_cast<T*>(p); }
+};
+
+// Makes ctx's device current for the lifetime of the guard.
+struct DeviceGuard {
+  int prev = -1;
+  explicit DeviceGuard(int dev) {
+    cudaGetDevice(&prev);
+    if (prev != dev) cudaSetDevice(dev);
+  }
+  ~DeviceGuard() {
+    int cur = -1;
+    cudaGetDevice(&cur);
+    if (prev >= 0 && cur != prev) cudaSetDevice(prev);
+  }
+};
+
+}  // namespace sem
+
+struct sem_context {
+  int device = 0;
+  cudaStream_t stream = nullptr;
+  std::mutex mu;
+  sem::DevBuf scratch;  // shared device scratch (candidate lists, staging)
+  sem::HostBuf pinned;
+};

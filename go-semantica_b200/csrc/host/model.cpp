@@ -1,0 +1,676 @@
+// Model loading and the batched forward pass (the host side of
+// internal/runtime: LoadModel model.go:233-315, ForwardWithDim model.go:661-666,
+// forwardINT8WithDim model_int8.go:148-256).
+#include <cmath>
+#include <cstring>
+#include <memory>
+#include <string>
+#include <vector>
+
+#include "gguf.h"
+#include "internal.h"
+
+namespace sem {
+
+namespace {
+thread_local std::string g_error;
+}
+
+int set_error(int code, const char* fmt, ...) {
+  char buf[1024];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof buf, fmt, ap);
+  va_end(ap);
+  g_error = buf;
+  return code;
+}
+
+const char* last_error() { return g_error.c_str(); }
+
+struct LayerW {
+  int8_t *qkv, *o, *gu, *down;
+  float *qkv_s, *o_s, *gu_s, *down_s;
+  float *attn_norm, *q_norm, *k_norm, *post_attn, *ffn_norm, *post_ffw;
+};
+
+}  // namespace sem
+
+struct sem_model {
+  sem_context* ctx = nullptr;
+  sem_model_config cfg{};
+  sem::DevBuf arena;  // all weights
+  int8_t* emb = nullptr;
+  float* emb_s = nullptr;
+  float* out_norm = nullptr;
+  float* rope_cos = nullptr;
+  float* rope_sin = nullptr;
+  std::vector<sem::LayerW> layers;
+  // forward workspaces (grow only)
+  sem::DevBuf hid, big, att, codes, halves, inv_rms, meta, absmax, ids, out, errflag;
+  int64_t ws_T = -1;
+  // cached metadata of the last batch shape
+  std::vector<int32_t> last_offsets, last_dims;
+  int32_t n_tiles = 0;
+  // optional per-launch timing
+  bool prof = false;
+  std::vector<cudaEvent_t> prof_events;  // pairs (before, after)
+  std::vector<int> prof_stage;           // stage of each pair
+  size_t prof_used = 0;                  // events recorded since the last read
+  double prof_ms[16] = {0};
+  int32_t prof_n[16] = {0};
+};
+
+struct sem_q8_weight {
+  sem_context* ctx = nullptr;
+  int32_t k_in = 0, n_out = 0;
+  sem::DevBuf codes, scales;
+};
+
+namespace sem {
+namespace {
+
+constexpr uint32_t kF32 = 0, kQ8 = 8;
+
+const sem_tensor_view* find_view(const sem_tensor_view* v, int n, const std::string& name) {
+  for (int i = 0; i < n; ++i)
+    if (v[i].name && name == v[i].name) return &v[i];
+  return nullptr;
+}
+
+size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+
+// Raw upload of one Q8_0 tensor into the staging buffer, then the repack kernel.
+int upload_q8(sem_context* ctx, DevBuf& staging, const sem_tensor_view* t, int64_t rows, int cols, int8_t* codes,
+              float* scales, int64_t row_off, int interleave, int part, bool gguf_dec) {
+  uint64_t need = (uint64_t)rows * (cols / 32) * 34;
+  if (t->nbytes < need) return set_error(SEM_EFORMAT, "tensor %s: %llu bytes, need %llu", t->name,
+                                         (unsigned long long)t->nbytes, (unsigned long long)need);
+  SEM_CUDA(staging.ensure(need));
+  SEM_CUDA(cudaMemcpyAsync(staging.p, t->data, need, cudaMemcpyHostToDevice, ctx->stream));
+  SEM_CUDA(launch_repack_q8_0(staging.as<uint8_t>(), rows, cols, codes, scales, row_off, interleave, part, gguf_dec,
+                              ctx->stream));
+  // the staging buffer is reused by the next tensor: finish this one first
+  SEM_CUDA(cudaStreamSynchronize(ctx->stream));
+  return SEM_OK;
+}
+
+int check_q8(const sem_tensor_view* t, const char* name, uint64_t k, uint64_t n) {
+  if (!t) return set_error(SEM_ENOTFOUND, "tensor not found: %s", name);
+  if (t->dtype != kQ8) return set_error(SEM_EFORMAT, "expected Q8_0, got dtype %u for %s", t->dtype, name);
+  if (t->n_dims < 2 || t->dims[0] != k || t->dims[1] != n)
+    return set_error(SEM_EFORMAT, "tensor %s: shape {%llu,%llu}, want {%llu,%llu}", name,
+                     (unsigned long long)t->dims[0], (unsigned long long)(t->n_dims > 1 ? t->dims[1] : 0),
+                     (unsigned long long)k, (unsigned long long)n);
+  return SEM_OK;
+}
+
+}  // namespace
+
+// ---------------------------------------------------------------------------
+// Model load
+// ---------------------------------------------------------------------------
+int model_load(sem_context* ctx, const sem_model_config* cfg_in, const sem_tensor_view* tv, int nt, sem_model** out) {
+  if (!ctx || !cfg_in || !tv || !out) return set_error(SEM_EINVAL, "null argument");
+  const sem_model_config c = *cfg_in;
+  const int H = c.embed_dim, F = c.interm_dim, L = c.num_layers, nh = c.num_heads, hd = c.head_dim;
+  // shapes the sm_100a kernels are built for (EmbeddingGemma-300M and its variants)
+  if (hd != 256 || c.num_kv_heads != 1 || nh < 1 || nh > 3 || H != nh * hd || H % 128 || F % 64 || L < 1 ||
+      c.vocab_size < 1 || c.max_seq_len < 1)
+    return set_error(SEM_EINVAL,
+                     "unsupported model shape: embed_dim=%d heads=%d kv_heads=%d head_dim=%d ffn=%d (need head_dim 256, "
+                     "1 KV head, <=3 query heads, embed_dim%%128==0, ffn%%64==0)",
+                     H, nh, c.num_kv_heads, hd, F);
+  DeviceGuard dg(ctx->device);
+  std::lock_guard<std::mutex> lk(ctx->mu);
+  std::unique_ptr<sem_model> m(new sem_model());
+  m->ctx = ctx;
+  m->cfg = c;
+  const int qkvN = nh * hd + 2 * hd;
+  const int64_t V = c.vocab_size;
+  // ---- arena layout ----
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    size_t o = off;
+    off = align256(off + bytes);
+    return o;
+  };
+  size_t o_emb = take((size_t)V * H), o_emb_s = take((size_t)V * (H / 32) * 4), o_onorm = take((size_t)H * 4);
+  size_t o_cos = take((size_t)c.max_seq_len * (hd / 2) * 4), o_sin = take((size_t)c.max_seq_len * (hd / 2) * 4);
+  struct LOff { size_t qkv, o, gu, down, qkv_s, o_s, gu_s, down_s, an, qn, kn, pa, fn, pf; };
+  std::vector<LOff> lo(L);
+  for (int l = 0; l < L; ++l) {
+    lo[l].qkv = take((size_t)qkvN * H);
+    lo[l].o = take((size_t)H * H);
+    lo[l].gu = take((size_t)2 * F * H);
+    lo[l].down = take((size_t)H * F);
+    lo[l].qkv_s = take((size_t)qkvN * (H / 32) * 4);
+    lo[l].o_s = take((size_t)H * (H / 32) * 4);
+    lo[l].gu_s = take((size_t)2 * F * (H / 32) * 4);
+    lo[l].down_s = take((size_t)H * (F / 32) * 4);
+    lo[l].an = take(H * 4); lo[l].qn = take(hd * 4); lo[l].kn = take(hd * 4);
+    lo[l].pa = take(H * 4); lo[l].fn = take(H * 4); lo[l].pf = take(H * 4);
+  }
+  cudaError_t e = m->arena.ensure(off);
+  if (e != cudaSuccess) return set_error(SEM_ENOMEM, "device allocation of %zu bytes failed: %s", off, cudaGetErrorString(e));
+  uint8_t* base = m->arena.as<uint8_t>();
+  SEM_CUDA(cudaMemsetAsync(base, 0, off, ctx->stream));
+  m->emb = reinterpret_cast<int8_t*>(base + o_emb);
+  m->emb_s = reinterpret_cast<float*>(base + o_emb_s);
+  m->rope_cos = reinterpret_cast<float*>(base + o_cos);
+  m->rope_sin = reinterpret_cast<float*>(base + o_sin);
+  DevBuf staging;
+  int rc;
+  // ---- token embedding (model.go:520-540), gguf f16 decoder ----
+  const sem_tensor_view* te = find_view(tv, nt, "token_embd.weight");
+  if (!te) te = find_view(tv, nt, "model.embed_tokens.weight");
+  if (!te) return set_error(SEM_ENOTFOUND, "load weights: token embedding tensor not found");
+  if (te->dtype != kQ8) return set_error(SEM_EFORMAT, "load weights: expected Q8_0 embeddings, got dtype %u", te->dtype);
+  if (te->dims[0] != (uint64_t)H || te->dims[1] < (uint64_t)V)
+    return set_error(SEM_EFORMAT, "token_embd.weight shape {%llu,%llu} does not cover vocab %lld x %d",
+                     (unsigned long long)te->dims[0], (unsigned long long)te->dims[1], (long long)V, H);
+  if ((rc = upload_q8(ctx, staging, te, V, H, m->emb, m->emb_s, 0, 0, 0, true))) return rc;
+  // ---- F32 tensors ----
+  auto up_f32 = [&](const char* name, size_t o, int n, bool required, float** dst) -> int {
+    const sem_tensor_view* t = find_view(tv, nt, name);
+    *dst = nullptr;
+    if (!t) return required ? set_error(SEM_ENOTFOUND, "tensor not found: %s", name) : SEM_OK;
+    if (t->dtype != kF32 || t->nbytes < (uint64_t)n * 4)
+      return set_error(SEM_EFORMAT, "tensor %s: expected %d F32 values", name, n);
+    *dst = reinterpret_cast<float*>(base + o);
+    SEM_CUDA(cudaMemcpyAsync(*dst, t->data, (size_t)n * 4, cudaMemcpyHostToDevice, ctx->stream));
+    return SEM_OK;
+  };
+  if ((rc = up_f32("output_norm.weight", o_onorm, H, false, &m->out_norm))) return rc;
+  m->layers.resize(L);
+  char nm[128];
+  for (int l = 0; l < L; ++l) {
+    LayerW& w = m->layers[l];
+    auto P = [&](const char* s) { snprintf(nm, sizeof nm, "blk.%d.%s", l, s); return (const char*)nm; };
+    if ((rc = up_f32(P("attn_norm.weight"), lo[l].an, H, true, &w.attn_norm))) return rc;
+    if ((rc = up_f32(P("ffn_norm.weight"), lo[l].fn, H, true, &w.ffn_norm))) return rc;
+    if ((rc = up_f32(P("attn_q_norm.weight"), lo[l].qn, hd, false, &w.q_norm))) return rc;
+    if ((rc = up_f32(P("attn_k_norm.weight"), lo[l].kn, hd, false, &w.k_norm))) return rc;
+    if ((rc = up_f32(P("post_attention_norm.weight"), lo[l].pa, H, false, &w.post_attn))) return rc;
+    if ((rc = up_f32(P("post_ffw_norm.weight"), lo[l].pf, H, false, &w.post_ffw))) return rc;
+    w.qkv = reinterpret_cast<int8_t*>(base + lo[l].qkv);
+    w.o = reinterpret_cast<int8_t*>(base + lo[l].o);
+    w.gu = reinterpret_cast<int8_t*>(base + lo[l].gu);
+    w.down = reinterpret_cast<int8_t*>(base + lo[l].down);
+    w.qkv_s = reinterpret_cast<float*>(base + lo[l].qkv_s);
+    w.o_s = reinterpret_cast<float*>(base + lo[l].o_s);
+    w.gu_s = reinterpret_cast<float*>(base + lo[l].gu_s);
+    w.down_s = reinterpret_cast<float*>(base + lo[l].down_s);
+    struct { const char* n; uint64_t k, rows; int8_t* c; float* s; int64_t roff; int il, part; } q8[] = {
+        {"attn_q.weight", (uint64_t)H, (uint64_t)nh * hd, w.qkv, w.qkv_s, 0, 0, 0},
+        {"attn_k.weight", (uint64_t)H, (uint64_t)hd, w.qkv, w.qkv_s, (int64_t)nh * hd, 0, 0},
+        {"attn_v.weight", (uint64_t)H, (uint64_t)hd, w.qkv, w.qkv_s, (int64_t)nh * hd + hd, 0, 0},
+        {"attn_output.weight", (uint64_t)H, (uint64_t)H, w.o, w.o_s, 0, 0, 0},
+        {"ffn_gate.weight", (uint64_t)H, (uint64_t)F, w.gu, w.gu_s, 0, 8, 0},
+        {"ffn_up.weight", (uint64_t)H, (uint64_t)F, w.gu, w.gu_s, 0, 8, 1},
+        {"ffn_down.weight", (uint64_t)F, (uint64_t)H, w.down, w.down_s, 0, 0, 0},
+    };
+    for (auto& q : q8) {
+      const char* name = P(q.n);
+      const sem_tensor_view* t = find_view(tv, nt, name);
+      if ((rc = check_q8(t, name, q.k, q.rows))) return rc;
+      if ((rc = upload_q8(ctx, staging, t, (int64_t)q.rows, (int)q.k, q.c, q.s, q.roff, q.il, q.part, false))) return rc;
+    }
+  }
+  // ---- RoPE tables (rope_cache.go:15-44) ----
+  {
+    const int half = hd / 2;
+    std::vector<float> freqs(half), cs((size_t)c.max_seq_len * half), sn((size_t)c.max_seq_len * half);
+    for (int i = 0; i < half; ++i) freqs[i] = (float)(1.0 / std::pow((double)c.rope_base, (double)(2 * i) / (double)hd));
+    for (int p = 0; p < c.max_seq_len; ++p)
+      for (int i = 0; i < half; ++i) {
+        float theta = (float)p * freqs[i];
+        cs[(size_t)p * half + i] = (float)std::cos((double)theta);
+        sn[(size_t)p * half + i] = (float)std::sin((double)theta);
+      }
+    SEM_CUDA(cudaMemcpy(m->rope_cos, cs.data(), cs.size() * 4, cudaMemcpyHostToDevice));
+    SEM_CUDA(cudaMemcpy(m->rope_sin, sn.data(), sn.size() * 4, cudaMemcpyHostToDevice));
+  }
+  SEM_CUDA(cudaStreamSynchronize(ctx->stream));
+  *out = m.release();
+  return SEM_OK;
+}
+
+// ---------------------------------------------------------------------------
+// Forward
+// ---------------------------------------------------------------------------
+namespace {
+
+int ensure_workspace(sem_model* m, int64_t T, int B, int64_t out_floats) {
+  const sem_model_config& c = m->cfg;
+  const int H = c.embed_dim, F = c.interm_dim, nh = c.num_heads, hd = c.head_dim;
+  const int qkvN = nh * hd + 2 * hd;
+  const int64_t Tp = T > 0 ? T : 1;
+  SEM_CUDA(m->hid.ensure((size_t)Tp * H * 4));
+  SEM_CUDA(m->big.ensure((size_t)Tp * (qkvN > F ? qkvN : F) * 4));
+  SEM_CUDA(m->att.ensure((size_t)Tp * H * 4));
+  SEM_CUDA(m->codes.ensure((size_t)Tp * (F > H ? F : H)));
+  SEM_CUDA(m->halves.ensure((size_t)Tp * (2 * nh * hd + 4 * hd) * 2));
+  SEM_CUDA(m->inv_rms.ensure((size_t)Tp * 4));
+  // meta: row_seq[T], row_pos[T], cu[B+1], tile_seq/tile_row0[2*(T/64+B)], out_dims[B], out_off (int64) [B]
+  size_t meta_ints = (size_t)2 * Tp + (B + 1) + 2 * ((size_t)Tp / 64 + B + 1) + B + 2 * (size_t)B + 8;
+  SEM_CUDA(m->meta.ensure(meta_ints * 4));
+  SEM_CUDA(m->absmax.ensure((size_t)(4 * c.num_layers + 1) * (B > 0 ? B : 1) * 4));
+  SEM_CUDA(m->ids.ensure((size_t)Tp * 4));
+  SEM_CUDA(m->out.ensure((size_t)(out_floats > 0 ? out_floats : 1) * 4));
+  SEM_CUDA(m->errflag.ensure(16));
+  return SEM_OK;
+}
+
+struct MetaPtrs {
+  SeqMeta seq;
+  AttnTiles tiles;
+  int32_t* out_dims;
+  int64_t* out_off;
+};
+
+// Builds the per-batch metadata on the host and uploads it (skipped when the
+// batch shape equals the previous call's).
+int upload_meta(sem_model* m, const int32_t* offsets, int B, const int32_t* dims, MetaPtrs* mp) {
+  const int64_t T = offsets[B];
+  int32_t* base = m->meta.as<int32_t>();
+  int32_t* d_row_seq = base;
+  int32_t* d_row_pos = d_row_seq + T;
+  int32_t* d_cu = d_row_pos + T;
+  int64_t max_tiles = T / 64 + B + 1;
+  int32_t* d_tseq = d_cu + (B + 1);
+  int32_t* d_trow = d_tseq + max_tiles;
+  int32_t* d_dims = d_trow + max_tiles;
+  uintptr_t p = reinterpret_cast<uintptr_t>(d_dims + B);
+  p = (p + 7) & ~uintptr_t(7);
+  int64_t* d_off = reinterpret_cast<int64_t*>(p);
+  bool same = (int)m->last_offsets.size() == B + 1 &&
+              std::memcmp(m->last_offsets.data(), offsets, sizeof(int32_t) * (B + 1)) == 0 &&
+              (int)m->last_dims.size() == B && std::memcmp(m->last_dims.data(), dims, sizeof(int32_t) * B) == 0;
+  if (!same) {
+    size_t bytes = (size_t)(reinterpret_cast<uint8_t*>(d_off + B) - reinterpret_cast<uint8_t*>(base));
+    HostBuf& hb = m->ctx->pinned;
+    SEM_CUDA(cudaStreamSynchronize(m->ctx->stream));  // the pinned buffer may still feed an earlier copy
+    SEM_CUDA(hb.ensure(bytes));
+    int32_t* h = hb.as<int32_t>();
+    int32_t* h_row_seq = h;
+    int32_t* h_row_pos = h_row_seq + T;
+    int32_t* h_cu = h_row_pos + T;
+    int32_t* h_tseq = h_cu + (B + 1);
+    int32_t* h_trow = h_tseq + max_tiles;
+    int32_t* h_dims = h_trow + max_tiles;
+    int64_t* h_off = reinterpret_cast<int64_t*>(reinterpret_cast<uint8_t*>(h) +
+                                                (reinterpret_cast<uint8_t*>(d_off) - reinterpret_cast<uint8_t*>(base)));
+    int32_t nt = 0;
+    int64_t acc = 0;
+    for (int s = 0; s < B; ++s) {
+      h_cu[s] = offsets[s];
+      for (int32_t r = offsets[s]; r < offsets[s + 1]; ++r) {
+        h_row_seq[r] = s;
+        h_row_pos[r] = r - offsets[s];
+      }
+      for (int32_t r = offsets[s]; r < offsets[s + 1]; r += 64) {
+        h_tseq[nt] = s;
+        h_trow[nt] = r;
+        ++nt;
+      }
+      h_dims[s] = dims[s];
+      h_off[s] = acc;
+      acc += dims[s];
+    }
+    h_cu[B] = offsets[B];
+    SEM_CUDA(cudaMemcpyAsync(base, h, bytes, cudaMemcpyHostToDevice, m->ctx->stream));
+    m->last_offsets.assign(offsets, offsets + B + 1);
+    m->last_dims.assign(dims, dims + B);
+    m->n_tiles = nt;
+  }
+  mp->seq = SeqMeta{d_row_seq, d_row_pos, d_cu, (int32_t)T, (int32_t)B};
+  mp->tiles = AttnTiles{d_tseq, d_trow, m->n_tiles};
+  mp->out_dims = d_dims;
+  mp->out_off = d_off;
+  return SEM_OK;
+}
+
+// Stage ids for the optional per-launch timing (sem_model_profile).
+enum Stage { kStEmbed, kStRowStats, kStQuant, kStGemmQKV, kStQKNormRope, kStAttention, kStGemmO, kStResidual,
+             kStGemmGateUp, kStGemmDown, kStPool, kStages };
+const char* const kStageNames[kStages] = {"embed", "row_stats", "quantize", "gemm_q8_qkv", "qk_norm_rope", "attention",
+                                          "gemm_q8_o", "residual_norm", "gemm_q8_gate_up", "gemm_q8_down", "pool_l2"};
+
+}  // namespace
+
+// Records an event before a launch when profiling (bracketing pairs).
+void prof_mark(sem_model* m, int stage, cudaStream_t st, bool after);
+
+namespace {
+
+#define SEM_LAUNCH(stage, call)                                                                 \
+  do {                                                                                          \
+    if (m->prof) prof_mark(m, (stage), st, false);                                              \
+    cudaError_t e_ = (call);                                                                    \
+    if (e_ != cudaSuccess) return set_error(SEM_EDEVICE, "forward: %s", cudaGetErrorString(e_)); \
+    if (m->prof) prof_mark(m, (stage), st, true);                                               \
+  } while (0)
+
+// The whole forward on `st`: ids already on the device in m->ids (or d_ids).
+int run_forward(sem_model* m, const int32_t* d_ids, const MetaPtrs& mp, float* d_out, cudaStream_t st) {
+  const sem_model_config& c = m->cfg;
+  const int H = c.embed_dim, F = c.interm_dim, L = c.num_layers, nh = c.num_heads, hd = c.head_dim;
+  const int qkvN = nh * hd + 2 * hd;
+  const SeqMeta& sm = mp.seq;
+  const int64_t T = sm.T;
+  const int B = sm.B;
+  float* hid = m->hid.as<float>();
+  float* big = m->big.as<float>();
+  float* att = m->att.as<float>();
+  int8_t* codes = m->codes.as<int8_t>();
+  float* inv = m->inv_rms.as<float>();
+  uint32_t* amax = m->absmax.as<uint32_t>();
+  __half* hb = m->halves.as<__half>();
+  __half *qh = hb, *ql = qh + T * nh * hd, *kh = ql + T * nh * hd, *kl = kh + T * hd, *vh = kl + T * hd,
+         *vl = vh + T * hd;
+  auto slot = [&](int l, int k) { return amax + (size_t)(4 * l + k) * B; };
+  SEM_LAUNCH(kStEmbed, cudaMemsetAsync(amax, 0, (size_t)(4 * L + 1) * B * 4, st));
+  SEM_LAUNCH(kStEmbed, launch_embed(d_ids, m->emb, m->emb_s, c.vocab_size, H, hid, (int)T, m->errflag.as<uint32_t>(), st));
+  SEM_LAUNCH(kStRowStats, launch_row_stats(hid, m->layers[0].attn_norm, H, c.norm_eps, sm, inv, slot(0, 0), st));
+  for (int l = 0; l < L; ++l) {
+    const LayerW& w = m->layers[l];
+    // attention block (model_int8.go:191-210)
+    SEM_LAUNCH(kStQuant, launch_quantize(hid, inv, w.attn_norm, H, sm, slot(l, 0), codes, st));
+    SEM_LAUNCH(kStGemmQKV, launch_gemm_q8(codes, w.qkv, w.qkv_s, (int)T, qkvN, H, slot(l, 0), sm.row_seq, big, kEpiStore, nullptr, st));
+    SEM_LAUNCH(kStQKNormRope, launch_qk_norm_rope(big, w.q_norm, w.k_norm, m->rope_cos, m->rope_sin, c.norm_eps, nh, sm, qh, ql, kh, kl,
+                                   vh, vl, st));
+    SEM_LAUNCH(kStAttention, launch_attention(qh, ql, kh, kl, vh, vl, nh, c.attention_scale, sm, mp.tiles, att, slot(l, 1), st));
+    SEM_LAUNCH(kStQuant, launch_quantize(att, nullptr, nullptr, H, sm, slot(l, 1), codes, st));
+    SEM_LAUNCH(kStGemmO, launch_gemm_q8(codes, w.o, w.o_s, (int)T, H, H, slot(l, 1), sm.row_seq, big, kEpiStore, nullptr, st));
+    SEM_LAUNCH(kStResidual, launch_residual_norm(big, w.post_attn, hid, w.ffn_norm, H, c.norm_eps, sm, inv, slot(l, 2), st));
+    // MLP block (model_int8.go:213-232)
+    SEM_LAUNCH(kStQuant, launch_quantize(hid, inv, w.ffn_norm, H, sm, slot(l, 2), codes, st));
+    SEM_LAUNCH(kStGemmGateUp, launch_gemm_q8(codes, w.gu, w.gu_s, (int)T, 2 * F, H, slot(l, 2), sm.row_seq, big, kEpiGeluUp, slot(l, 3),
+                              st));
+    SEM_LAUNCH(kStQuant, launch_quantize(big, nullptr, nullptr, F, sm, slot(l, 3), codes, st));
+    SEM_LAUNCH(kStGemmDown, launch_gemm_q8(codes, w.down, w.down_s, (int)T, H, F, slot(l, 3), sm.row_seq, att, kEpiStore, nullptr, st));
+    const bool last = l + 1 == L;
+    const float* next_w = last ? m->out_norm : m->layers[l + 1].attn_norm;
+    SEM_LAUNCH(kStResidual, launch_residual_norm(att, w.post_ffw, hid, next_w ? next_w : w.ffn_norm, H, c.norm_eps, sm, inv,
+                                    last ? nullptr : slot(l + 1, 0), st));
+  }
+  // output_norm + mean pool + L2 (model_int8.go:235-255)
+  SEM_LAUNCH(kStPool, launch_pool_l2(hid, m->out_norm ? inv : nullptr, m->out_norm, H, sm, mp.out_dims, mp.out_off, d_out, st));
+  return SEM_OK;
+}
+
+}  // namespace
+
+int model_embed(sem_model* m, const int32_t* ids, const int32_t* offsets, int32_t B, const int32_t* dims_in,
+                float* out) {
+  if (!m || (!ids && B > 0) || !offsets || (!out && B > 0)) return set_error(SEM_EINVAL, "null argument");
+  if (B < 0) return set_error(SEM_EINVAL, "negative sequence count");
+  const sem_model_config& c = m->cfg;
+  std::vector<int32_t> dims(B);
+  int64_t out_floats = 0;
+  for (int s = 0; s < B; ++s) {
+    int d = dims_in ? dims_in[s] : c.embed_dim;
+    // ForwardWithDim (model.go:661-666) then forwardINT8WithDim (model_int8.go:149-171)
+    if (d <= 0 || d > c.embed_dim)
+      return set_error(SEM_EINVAL, "target dimension %d out of range (1..%d)", d, c.embed_dim);
+    int len = offsets[s + 1] - offsets[s];
+    if (len <= 0) return set_error(SEM_EINVAL, "empty input");
+    if (len > c.max_seq_len) return set_error(SEM_EINVAL, "sequence too long: %d > %d", len, c.max_seq_len);
+    for (int32_t r = offsets[s]; r < offsets[s + 1]; ++r)
+      if (ids[r] < 0 || ids[r] >= c.vocab_size) return set_error(SEM_EINVAL, "token ID out of range: %d", ids[r]);
+    dims[s] = d;
+    out_floats += d;
+  }
+  if (B == 0) return SEM_OK;
+  if (offsets[0] != 0) return set_error(SEM_EINVAL, "offsets[0] must be 0");
+  sem_context* ctx = m->ctx;
+  DeviceGuard dg(ctx->device);
+  std::lock_guard<std::mutex> lk(ctx->mu);
+  const int64_t T = offsets[B];
+  int rc;
+  if ((rc = ensure_workspace(m, T, B, out_floats))) return rc;
+  MetaPtrs mp;
+  if ((rc = upload_meta(m, offsets, B, dims.data(), &mp))) return rc;
+  SEM_CUDA(cudaMemcpyAsync(m->ids.p, ids, (size_t)T * 4, cudaMemcpyHostToDevice, ctx->stream));
+  if ((rc = run_forward(m, m->ids.as<int32_t>(), mp, m->out.as<float>(), ctx->stream))) return rc;
+  SEM_CUDA(cudaMemcpyAsync(out, m->out.p, (size_t)out_floats * 4, cudaMemcpyDeviceToHost, ctx->stream));
+  SEM_CUDA(cudaStreamSynchronize(ctx->stream));
+  return SEM_OK;
+}
+
+int model_embed_device(sem_model* m, const int32_t* d_ids, const int32_t* h_offsets, int32_t B, int32_t dim,
+                       float* d_out, void* stream) {
+  if (!m || !d_ids || !h_offsets || !d_out) return set_error(SEM_EINVAL, "null argument");
+  const sem_model_config& c = m->cfg;
+  if (dim <= 0 || dim > c.embed_dim) return set_error(SEM_EINVAL, "target dimension %d out of range (1..%d)", dim, c.embed_dim);
+  for (int s = 0; s < B; ++s) {
+    int len = h_offsets[s + 1] - h_offsets[s];
+    if (len <= 0) return set_error(SEM_EINVAL, "empty input");
+    if (len > c.max_seq_len) return set_error(SEM_EINVAL, "sequence too long: %d > %d", len, c.max_seq_len);
+  }
+  if (B == 0) return SEM_OK;
+  sem_context* ctx = m->ctx;
+  DeviceGuard dg(ctx->device);
+  std::lock_guard<std::mutex> lk(ctx->mu);
+  cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : ctx->stream;
+  std::vector<int32_t> dims(B, dim);
+  int rc;
+  if ((rc = ensure_workspace(m, h_offsets[B], B, (int64_t)B * dim))) return rc;
+  MetaPtrs mp;
+  if ((rc = upload_meta(m, h_offsets, B, dims.data(), &mp))) return rc;
+  if (st != ctx->stream) {  // metadata was uploaded on the context stream
+    cudaEvent_t ev;
+    SEM_CUDA(cudaEventCreateWithFlags(&ev, cudaEventDisableTiming));
+    SEM_CUDA(cudaEventRecord(ev, ctx->stream));
+    SEM_CUDA(cudaStreamWaitEvent(st, ev, 0));
+    cudaEventDestroy(ev);
+  }
+  return run_forward(m, d_ids, mp, d_out, st);
+}
+
+// ---------------------------------------------------------------------------
+// Isolated Q8_0 projection (config-2 microbench)
+// ---------------------------------------------------------------------------
+int q8_weight_create(sem_context* ctx, const void* w_q8, int32_t k_in, int32_t n_out, sem_q8_weight** out) {
+  if (!ctx || !w_q8 || !out) return set_error(SEM_EINVAL, "null argument");
+  if (k_in <= 0 || n_out <= 0 || k_in % 128 || n_out % 128)
+    return set_error(SEM_EINVAL, "q8 weight %d x %d: both dimensions must be positive multiples of 128", k_in, n_out);
+  DeviceGuard dg(ctx->device);
+  std::lock_guard<std::mutex> lk(ctx->mu);
+  std::unique_ptr<sem_q8_weight> w(new sem_q8_weight());
+  w->ctx = ctx;
+  w->k_in = k_in;
+  w->n_out = n_out;
+  SEM_CUDA(w->codes.ensure((size_t)k_in * n_out));
+  SEM_CUDA(w->scales.ensure((size_t)n_out * (k_in / 32) * 4));
+  DevBuf staging;
+  sem_tensor_view t{"weight", kQ8, 2, {(uint64_t)k_in, (uint64_t)n_out, 0, 0}, w_q8,
+                    (uint64_t)n_out * (k_in / 32) * 34};
+  int rc = upload_q8(ctx, staging, &t, n_out, k_in, w->codes.as<int8_t>(), w->scales.as<float>(), 0, 0, 0, false);
+  if (rc) return rc;
+  *out = w.release();
+  return SEM_OK;
+}
+
+int q8_gemm(sem_q8_weight* w, const float* d_a, int32_t M, float* d_c, int8_t* d_codes, uint32_t* d_absmax,
+            void* stream) {
+  if (!w || !d_a || !d_c || !d_codes || !d_absmax) return set_error(SEM_EINVAL, "null argument");
+  DeviceGuard dg(w->ctx->device);
+  cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : w->ctx->stream;
+  // one scale for the whole activation buffer (QuantizeSymmetricINT8Into, quantize.go:29-69)
+  SEM_CUDA(cudaMemsetAsync(d_absmax, 0, 4, st));
+  SeqMeta meta{nullptr, nullptr, nullptr, M, 1};
+  SEM_CUDA(launch_absmax(d_a, (int64_t)M * w->k_in, d_absmax, st));
+  SEM_CUDA(launch_quantize(d_a, nullptr, nullptr, w->k_in, meta, d_absmax, d_codes, st));
+  SEM_CUDA(launch_gemm_q8(d_codes, w->codes.as<int8_t>(), w->scales.as<float>(), M, w->n_out, w->k_in, d_absmax, nullptr,
+                          d_c, kEpiStore, nullptr, st));
+  return SEM_OK;
+}
+
+void prof_mark(sem_model* m, int stage, cudaStream_t st, bool after) {
+  if (m->prof_used == m->prof_events.size()) {
+    cudaEvent_t e;
+    if (cudaEventCreate(&e) != cudaSuccess) return;
+    m->prof_events.push_back(e);
+  }
+  if (!after) m->prof_stage.push_back(stage);
+  cudaEventRecord(m->prof_events[m->prof_used++], st);
+}
+
+int profile_read(sem_model* m, const char** names, float* total_ms, int32_t* launches, int32_t cap, int32_t* n_out) {
+  DeviceGuard dg(m->ctx->device);
+  std::lock_guard<std::mutex> lk(m->ctx->mu);
+  SEM_CUDA(cudaDeviceSynchronize());
+  for (size_t i = 0; i + 1 < m->prof_used; i += 2) {
+    float ms = 0.0f;
+    SEM_CUDA(cudaEventElapsedTime(&ms, m->prof_events[i], m->prof_events[i + 1]));
+    int s = m->prof_stage[i / 2];
+    m->prof_ms[s] += ms;
+    m->prof_n[s] += 1;
+  }
+  int n = 0;
+  for (int s = 0; s < kStages && n < cap; ++s) {
+    if (names) names[n] = kStageNames[s];
+    if (total_ms) total_ms[n] = (float)m->prof_ms[s];
+    if (launches) launches[n] = m->prof_n[s];
+    ++n;
+  }
+  if (n_out) *n_out = n;
+  for (int s = 0; s < kStages; ++s) { m->prof_ms[s] = 0; m->prof_n[s] = 0; }
+  m->prof_used = 0;
+  m->prof_stage.clear();
+  return SEM_OK;
+}
+
+}  // namespace sem
+
+// ---------------------------------------------------------------------------
+// C ABI
+// ---------------------------------------------------------------------------
+extern "C" {
+
+const char* sem_last_error(void) { return sem::last_error(); }
+
+int sem_device_count(int* out) {
+  if (!out) return sem::set_error(SEM_EINVAL, "null argument");
+  int n = 0;
+  cudaError_t e = cudaGetDeviceCount(&n);
+  if (e != cudaSuccess) {
+    *out = 0;
+    return sem::set_error(SEM_EDEVICE, "cudaGetDeviceCount: %s", cudaGetErrorString(e));
+  }
+  *out = n;
+  return SEM_OK;
+}
+
+int sem_context_create(int device, sem_context** out) {
+  if (!out) return sem::set_error(SEM_EINVAL, "null argument");
+  int n = 0;
+  cudaError_t e = cudaGetDeviceCount(&n);
+  if (e != cudaSuccess || device < 0 || device >= n)
+    return sem::set_error(SEM_EDEVICE, "no CUDA device %d (%s)", device, e == cudaSuccess ? "out of range" : cudaGetErrorString(e));
+  sem::DeviceGuard dg(device);
+  std::unique_ptr<sem_context> c(new sem_context());
+  c->device = device;
+  e = cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking);
+  if (e != cudaSuccess) return sem::set_error(SEM_EDEVICE, "cudaStreamCreate: %s", cudaGetErrorString(e));
+  *out = c.release();
+  return SEM_OK;
+}
+
+int sem_context_destroy(sem_context* ctx) {
+  if (!ctx) return SEM_OK;
+  {
+    sem::DeviceGuard dg(ctx->device);
+    cudaStreamSynchronize(ctx->stream);
+    ctx->scratch.release();
+    cudaStreamDestroy(ctx->stream);
+  }
+  delete ctx;
+  return SEM_OK;
+}
+
+void* sem_context_stream(sem_context* ctx) { return ctx ? static_cast<void*>(ctx->stream) : nullptr; }
+
+int sem_model_load(sem_context* ctx, const sem_model_config* cfg, const sem_tensor_view* tensors, int32_t n,
+                   sem_model** out) {
+  return sem::model_load(ctx, cfg, tensors, n, out);
+}
+
+int sem_model_load_gguf(sem_context* ctx, const char* path, sem_model** out) {
+  if (!ctx || !path || !out) return sem::set_error(SEM_EINVAL, "null argument");
+  sem::GgufFile f;
+  int rc = f.open(path);
+  if (rc) return rc;
+  sem_model_config cfg;
+  if ((rc = sem::gguf_config(f, &cfg))) return rc;
+  std::vector<sem_tensor_view> views;
+  views.reserve(f.tensors.size());
+  for (const auto& t : f.tensors) {
+    sem_tensor_view v{};
+    v.name = t.name.c_str();
+    v.dtype = t.dtype;
+    v.n_dims = (uint32_t)t.dims.size();
+    for (size_t k = 0; k < t.dims.size() && k < 4; ++k) v.dims[k] = t.dims[k];
+    v.data = f.tensor_data(t);
+    v.nbytes = t.size;
+    views.push_back(v);
+  }
+  return sem::model_load(ctx, &cfg, views.data(), (int32_t)views.size(), out);
+}
+
+int sem_model_config_get(const sem_model* m, sem_model_config* out) {
+  if (!m || !out) return sem::set_error(SEM_EINVAL, "null argument");
+  *out = m->cfg;
+  return SEM_OK;
+}
+
+int sem_model_free(sem_model* m) {
+  if (!m) return SEM_OK;
+  sem::DeviceGuard dg(m->ctx->device);
+  cudaStreamSynchronize(m->ctx->stream);
+  for (cudaEvent_t e : m->prof_events) cudaEventDestroy(e);
+  delete m;
+  return SEM_OK;
+}
+
+int sem_model_profile(sem_model* m, int32_t enable) {
+  if (!m) return sem::set_error(SEM_EINVAL, "null argument");
+  m->prof = enable != 0;
+  return SEM_OK;
+}
+
+int sem_model_profile_read(sem_model* m, const char** names, float* total_ms, int32_t* launches, int32_t cap,
+                           int32_t* n_out) {
+  if (!m) return sem::set_error(SEM_EINVAL, "null argument");
+  return sem::profile_read(m, names, total_ms, launches, cap, n_out);
+}
+
+int sem_embed(sem_model* m, const int32_t* ids, const int32_t* offsets, int32_t n, const int32_t* dims, float* out) {
+  return sem::model_embed(m, ids, offsets, n, dims, out);
+}
+
+int sem_embed_device(sem_model* m, const int32_t* d_ids, const int32_t* h_offsets, int32_t n, int32_t dim, float* d_out,
+                     void* stream) {
+  return sem::model_embed_device(m, d_ids, h_offsets, n, dim, d_out, stream);
+}
+
+int sem_q8_weight_create(sem_context* ctx, const void* w_q8, int32_t k_in, int32_t n_out, sem_q8_weight** out) {
+  return sem::q8_weight_create(ctx, w_q8, k_in, n_out, out);
+}
+
+int sem_q8_weight_free(sem_q8_weight* w) {
+  if (!w) return SEM_OK;
+  sem::DeviceGuard dg(w->ctx->device);
+  cudaStreamSynchronize(w->ctx->stream);
+  delete w;
+  return SEM_OK;
+}
+
+int sem_q8_gemm(sem_q8_weight* w, const float* d_a, int32_t m, float* d_c, int8_t* d_codes, uint32_t* d_absmax,
+                void* stream) {
+  return sem::q8_gemm(w, d_a, m, d_c, d_codes, d_absmax, stream);
+}
+
+}  // extern "C"

@@ -1,0 +1,108 @@
+// Host-side launch wrappers for the sm_100a kernels. Plain pointers and sizes
+// only; every wrapper enqueues on `stream` and returns the launch status.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace sem {
+
+// ---- load-time repacking (model_kernels.cu) ----
+// Q8_0 blocks (fp16 scale + 32 int8, 34 bytes) of `rows` x `cols` -> an int8
+// plane (dst_codes[dst_row][cols]) and an fp32 scale plane
+// (dst_scales[dst_row][cols/32]). f16 decoding follows the reference's
+// runtime decoder (gguf_decoder = false, model_int8.go:571-597) or its gguf
+// decoder (true, gguf/tensor.go:207-240). Row r goes to dst_row_offset + map(r),
+// where map interleaves groups of `interleave` rows with a partner tensor
+// (part 0 or 1) when interleave > 0.
+cudaError_t launch_repack_q8_0(const uint8_t* raw, int64_t rows, int cols, int8_t* dst_codes,
+                               float* dst_scales, int64_t dst_row_offset, int interleave, int part,
+                               bool gguf_decoder, cudaStream_t stream);
+
+// ---- forward-pass element-wise kernels (model_kernels.cu) ----
+struct SeqMeta {
+  const int32_t* row_seq;   // [T] sequence of each packed row
+  const int32_t* row_pos;   // [T] position of each row within its sequence
+  const int32_t* cu_seqlens;// [B+1]
+  int32_t T;                // rows
+  int32_t B;                // sequences
+};
+
+cudaError_t launch_embed(const int32_t* ids, const int8_t* emb_codes, const float* emb_scales, int vocab,
+                         int H, float* hidden, int T, uint32_t* err_flag, cudaStream_t stream);
+
+// inv_rms[row] of hidden rows with the norm weight w, and atomically the
+// per-sequence absmax of the normed rows into absmax[seq] (absmax may be null).
+cudaError_t launch_row_stats(const float* x, const float* w, int H, float eps, SeqMeta meta, float* inv_rms,
+                             uint32_t* absmax, cudaStream_t stream);
+
+// codes = quantize((x * inv_rms[row]) * w) with the per-sequence scale; when
+// inv_rms is null the rows are quantized as they are; a null meta.row_seq
+// means one scale (absmax[0]) for every row.
+cudaError_t launch_quantize(const float* x, const float* inv_rms, const float* w, int K, SeqMeta meta,
+                            const uint32_t* absmax, int8_t* codes, cudaStream_t stream);
+
+// Max |x| over n values, atomically into slot[0].
+cudaError_t launch_absmax(const float* x, int64_t n, uint32_t* slot, cudaStream_t stream);
+
+// Per-head RMSNorm of q (num_heads heads) and k (1 head), NeoX RoPE, and the
+// hi/lo fp16 split of q, k, v for attention. qkv rows: [q (nh*256) | k (256) | v (256)].
+cudaError_t launch_qk_norm_rope(const float* qkv, const float* q_norm, const float* k_norm, const float* rope_cos,
+                                const float* rope_sin, float eps, int num_heads, SeqMeta meta, __half* qh,
+                                __half* ql, __half* kh, __half* kl, __half* vh, __half* vl,
+                                cudaStream_t stream);
+
+// hidden = rmsnorm(o, post_w) + hidden; then the statistics of the new hidden
+// rows for next_w (inv_rms, per-sequence absmax; absmax may be null).
+cudaError_t launch_residual_norm(const float* o, const float* post_w, float* hidden, const float* next_w, int H,
+                                 float eps, SeqMeta meta, float* inv_rms, uint32_t* absmax, cudaStream_t stream);
+
+// Mean pooling of the first out_dim[s] columns of (hidden * inv_rms) * w over
+// each sequence, then L2 normalisation; writes out + out_offset[s].
+cudaError_t launch_pool_l2(const float* hidden, const float* inv_rms, const float* w, int H, SeqMeta meta,
+                           const int32_t* out_dims, const int64_t* out_offsets, float* out, cudaStream_t stream);
+
+// ---- Q8_0 x INT8 projection (gemm_q8.cu) ----
+enum GemmEpilogue { kEpiStore = 0, kEpiGeluUp = 1 };
+// C[m, n] = in_scale[seq(m)] * sum_kb float(int32 block dot) * w_scales[n, kb].
+// kEpiGeluUp: weights rows interleave gate/up in groups of 8; writes
+// h[m, n/2] = gelu_quick(gate) * up and the per-sequence absmax of h.
+cudaError_t launch_gemm_q8(const int8_t* a_codes, const int8_t* w_codes, const float* w_scales, int M, int N,
+                           int K, const uint32_t* a_absmax, const int32_t* row_seq, float* c, int epilogue,
+                           uint32_t* out_absmax, cudaStream_t stream);
+
+// ---- attention (attention.cu) ----
+struct AttnTiles {
+  const int32_t* tile_seq;    // [n_tiles] sequence of each 64-query tile
+  const int32_t* tile_row0;   // [n_tiles] first packed row of the tile
+  int32_t n_tiles;
+};
+cudaError_t launch_attention(const __half* qh, const __half* ql, const __half* kh, const __half* kl,
+                             const __half* vh, const __half* vl, int num_heads, float scale, SeqMeta meta,
+                             AttnTiles tiles, float* out, uint32_t* absmax, cudaStream_t stream);
+
+// ---- brute search (brute_kernels.cu) ----
+// Exact integer scan: scores of nq queries against rows [0, count) of an
+// int8 (elem 1) or int16 (elem 2) corpus; per-chunk candidate lists.
+struct ScanPlan {
+  int32_t chunks;         // row chunks (grid x)
+  int64_t rows_per_chunk;
+  int64_t row_base;       // added to local rows in the emitted keys (index shards)
+};
+cudaError_t launch_scan_exact(const void* corpus, int elem, int64_t count, int dim, const void* qcodes, int nq,
+                              int k, ScanPlan plan, uint64_t* cand, cudaStream_t stream);
+cudaError_t launch_scan_float(const void* corpus, int elem, int64_t count, int dim, const float* queries, int nq,
+                              int k, ScanPlan plan, uint64_t* cand, cudaStream_t stream);
+// Merges `lists` candidate lists of k keys per query (list j of query q at
+// cand + q*q_stride + j*list_stride) into the final top-k_out, best first;
+// decodes (score, row) keys into the outputs (any may be null). float_keys:
+// keys hold float scores; elem picks the exact-mode distance scale.
+cudaError_t launch_topk_merge(const uint64_t* cand, int lists, int64_t list_stride, int64_t q_stride, int nq, int k,
+                              int k_out, bool float_keys, int elem, int32_t* out_rows, int32_t* out_scores,
+                              float* out_dist, uint64_t* out_keys, cudaStream_t stream);
+// Row-wise normalize (optional) + quantize (quant 1/2) or copy (quant 0) into
+// rows of out_row_bytes (zero padded).
+cudaError_t launch_normalize_quantize(const float* in, int64_t count, int dim, int quant, int out_row_bytes,
+                                      bool normalize, void* out, cudaStream_t stream);
+
+}  // namespace sem

@@ -1,0 +1,200 @@
+/*
+ * semantica_b200.h — C ABI of libsemantica_b200.so, the B200 (sm_100a)
+ * implementation of go-semantica's two data-parallel hot paths:
+ *
+ *   1. the EmbeddingGemma INT8 forward pass behind rt.Embed
+ *      (internal/runtime.(*Model).ForwardWithDim, model.go:661-666), and
+ *   2. search/brute's quantised scan + top-k behind Index.SearchVector and
+ *      the BRUT v1 Serializer (search/brute/index.go, storage.go).
+ *
+ * Plain C types only: pointers, sizes, status codes. Every call returns a
+ * SEM_* status; on failure sem_last_error() returns a message that matches the
+ * reference's error string where the reference has one. No call keeps a
+ * pointer to caller memory after it returns (the cgo rule): inputs are copied.
+ * A context is bound to one GPU; calls on one context are serialised.
+ *
+ * Citations are "file:line" inside the go-semantica source tree.
+ */
+#ifndef SEMANTICA_B200_H
+#define SEMANTICA_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes ---- */
+#define SEM_OK 0
+#define SEM_EINVAL 1    /* invalid argument (reference-style message in sem_last_error) */
+#define SEM_EDEVICE 2   /* CUDA error */
+#define SEM_ENOMEM 3    /* device or host allocation failed */
+#define SEM_EFORMAT 4   /* malformed GGUF or BRUT bytes */
+#define SEM_ENOTFOUND 5 /* tensor / id not found */
+
+typedef struct sem_context sem_context;
+typedef struct sem_model sem_model;
+typedef struct sem_index sem_index;
+typedef struct sem_q8_weight sem_q8_weight;
+
+/* Message of the last failed call on this thread (never NULL). */
+const char *sem_last_error(void);
+
+/* Number of visible CUDA devices. */
+int sem_device_count(int *out);
+
+/* A context owns one device, one stream and the device workspaces. */
+int sem_context_create(int device, sem_context **out);
+int sem_context_destroy(sem_context *ctx);
+/* The context's CUDA stream, as a cudaStream_t. */
+void *sem_context_stream(sem_context *ctx);
+
+/* ------------------------------------------------------------------------
+ * Model: replaces internal/runtime.LoadModel / loadModel (model.go:233-315)
+ * ---------------------------------------------------------------------- */
+
+/* Mirrors internal/runtime.ModelConfig (model.go:16-31). */
+typedef struct sem_model_config {
+  int32_t vocab_size, embed_dim, num_layers, num_heads, num_kv_heads, head_dim, interm_dim, max_seq_len;
+  float norm_eps, rope_base, attention_scale;
+} sem_model_config;
+
+/* A GGUF tensor as internal/gguf.Reader exposes it (reader.go:23-30,
+ * :332-346): dims are GGUF ne[] (ne0 contiguous), dtype is the GGUF type id
+ * (0 F32, 8 Q8_0), data points at the tensor bytes (e.g. into the mmap). */
+typedef struct sem_tensor_view {
+  const char *name;
+  uint32_t dtype;
+  uint32_t n_dims;
+  uint64_t dims[4];
+  const void *data;
+  uint64_t nbytes;
+} sem_tensor_view;
+
+/* Uploads the model named by `tensors` (token_embd.weight, output_norm.weight,
+ * blk.N.{attn_norm,attn_q,attn_k,attn_v,attn_output,attn_q_norm,attn_k_norm,
+ * post_attention_norm,ffn_norm,ffn_gate,ffn_up,ffn_down,post_ffw_norm}.weight,
+ * model_int8.go:54-119) to the context's device, repacking every Q8_0 tensor
+ * into an int8 plane and an fp32 block-scale plane. The caller's bytes may be
+ * released when the call returns. Replaces loadWeights + loadLayerINT8
+ * (model.go:520-552, model_int8.go:54-119). */
+int sem_model_load(sem_context *ctx, const sem_model_config *cfg, const sem_tensor_view *tensors, int32_t n_tensors,
+                   sem_model **out);
+
+/* Convenience: parses a GGUF v3 file the way internal/gguf + parseConfig do
+ * (reader.go:98-178, model.go:424-517) and calls sem_model_load. */
+int sem_model_load_gguf(sem_context *ctx, const char *path, sem_model **out);
+
+int sem_model_config_get(const sem_model *model, sem_model_config *out);
+int sem_model_free(sem_model *model);
+
+/* ------------------------------------------------------------------------
+ * Embedding forward: replaces (*Model).ForwardWithDim (model.go:661-666 →
+ * model_int8.go:148-256), batched. The reference runs one sequence per call
+ * and fans calls out over goroutines (pkg/ggufembed/api.go:237-295); here one
+ * call carries every sequence of a request.
+ * ---------------------------------------------------------------------- */
+
+/* ids: packed token ids of n_seqs sequences; offsets: n_seqs+1 prefix offsets
+ * into ids; dims: per-sequence output dimension (1..embed_dim; NULL = embed_dim
+ * for all); out: packed outputs, sequence s at sum(dims[0..s-1]), each the
+ * mean-pooled, L2-normalised first dims[s] channels.
+ * Errors (reference strings): "empty input", "sequence too long: %d > %d",
+ * "token ID out of range: %d", "target dimension %d out of range (1..%d)". */
+int sem_embed(sem_model *model, const int32_t *ids, const int32_t *offsets, int32_t n_seqs, const int32_t *dims,
+              float *out);
+
+/* Device-resident variant (no host copies): d_ids on the device, h_offsets on
+ * the host, d_out on the device (n_seqs x dim). Enqueued on `stream` (NULL =
+ * the context stream); returns without synchronising. */
+int sem_embed_device(sem_model *model, const int32_t *d_ids, const int32_t *h_offsets, int32_t n_seqs, int32_t dim,
+                     float *d_out, void *stream);
+
+/* Per-stage device timing of the forward pass (diagnostics; no reference
+ * counterpart). enable != 0 brackets every kernel launch of later forwards
+ * with CUDA events on the launching stream. profile_read synchronises the
+ * context stream, returns up to `cap` stages (static names, total ms, launch
+ * counts) accumulated since the last read, and resets the totals. */
+int sem_model_profile(sem_model *model, int32_t enable);
+int sem_model_profile_read(sem_model *model, const char **names, float *total_ms, int32_t *launches, int32_t cap,
+                           int32_t *n_out);
+
+/* ------------------------------------------------------------------------
+ * Isolated Q8_0 x INT8 projection: QuantizeSymmetricINT8Into + MatMulQ8_0INT8
+ * (internal/kernels/quantize.go:29-69, :346-458).
+ * ---------------------------------------------------------------------- */
+
+/* w_q8: raw Q8_0 bytes of an [n_out rows x k_in] weight (GGUF dims {k_in, n_out}). */
+int sem_q8_weight_create(sem_context *ctx, const void *w_q8, int32_t k_in, int32_t n_out, sem_q8_weight **out);
+int sem_q8_weight_free(sem_q8_weight *w);
+/* Device pointers: d_a fp32 [m x k_in] -> d_c fp32 [m x n_out], one activation
+ * scale for the whole of d_a as in the reference; d_codes (m x k_in int8) and
+ * d_absmax (one uint32) are caller-provided scratch. Enqueued on `stream`. */
+int sem_q8_gemm(sem_q8_weight *w, const float *d_a, int32_t m, float *d_c, int8_t *d_codes, uint32_t *d_absmax,
+                void *stream);
+
+/* ------------------------------------------------------------------------
+ * Brute-force index: replaces search/brute (builder.go, index.go, storage.go).
+ * quant: 0 float32, 1 int8, 2 int16 (brute.QuantizationMode, quant.go:8-15).
+ * ---------------------------------------------------------------------- */
+
+/* Builder.AddVector + Build (builder.go:52-127): vectors are normalised
+ * (builder.go:129-141) and quantised (quant.go:17-41) on the device.
+ * ids must be unique ("brute: duplicate id %d"). */
+int sem_index_build(sem_context *ctx, int32_t dim, int32_t quant, const float *vectors, const int32_t *ids,
+                    int64_t count, sem_index **out);
+
+/* An index from already-stored rows (codes as Build or Deserialize produce
+ * them): data is count x dim of int8 / int16 / float32. */
+int sem_index_create(sem_context *ctx, int32_t dim, int32_t quant, const void *data, const int32_t *ids, int64_t count,
+                     sem_index **out);
+
+int sem_index_free(sem_index *idx);
+int sem_index_count(const sem_index *idx, int64_t *out);
+int sem_index_dimension(const sem_index *idx, int32_t *out);
+int sem_index_quantization(const sem_index *idx, int32_t *out);
+
+#define SEM_SEARCH_REFERENCE 0 /* fp32 query x (code/127): the reference's own arithmetic */
+#define SEM_SEARCH_EXACT 1     /* query quantised like the rows, exact int32 dot products */
+
+/* Index.SearchVector (index.go:29-42) for nq queries (nq x dim floats, not
+ * yet normalised; normalize != 0 normalises them first as SearchVector does,
+ * 0 treats them as normalised like SearchNormalized, :44-53). Results per
+ * query: min(k, count) entries, best first; ties break toward the lower row.
+ * out_ids/out_dist are nq x k (unused tail entries: id -1). out_scores (exact
+ * mode, may be NULL) receives the int32 scores. Errors: "brute: topK must be
+ * positive", "brute: query dimension mismatch: got %d want %d". */
+int sem_index_search(sem_index *idx, const float *queries, int32_t nq, int32_t dim, int32_t k, int32_t mode,
+                     int32_t normalize, int32_t *out_ids, float *out_dist, int32_t *out_scores);
+
+/* Device-level search of one shard for multi-GPU merges: d_qcodes (exact
+ * mode, nq x dim codes of the index's element type) or d_queries (reference
+ * mode, normalised floats); writes nq x k 64-bit candidate keys
+ * ((order-preserving score << 32) | ~global_row) to d_keys, where global_row =
+ * row_base + local row. Enqueued on `stream`. */
+int sem_index_search_keys(sem_index *idx, const void *d_queries, int32_t nq, int32_t k, int32_t mode,
+                          int64_t row_base, uint64_t *d_keys, void *stream);
+
+/* Merges `lists` candidate-key lists of k per query (d_keys: lists x nq x k)
+ * into the best k_out per query. quant selects the distance scale (1: /127^2,
+ * 2: /32767^2) for exact-mode keys. Any output may be NULL. */
+int sem_topk_merge(sem_context *ctx, const uint64_t *d_keys, int32_t lists, int32_t nq, int32_t k, int32_t k_out,
+                   int32_t mode, int32_t quant, int32_t *d_rows, int32_t *d_scores, float *d_dist, void *stream);
+
+/* Quantises normalised queries exactly like stored rows (quant.go:17-41). */
+int sem_quantize_queries(const float *queries, int32_t nq, int32_t dim, int32_t quant, void *out_codes);
+
+/* Index.Vector (index.go:162-180): dequantised copy of the row with this id. */
+int sem_index_vector(sem_index *idx, int32_t id, float *out);
+
+/* BRUT v1 (storage.go:17-153): 20-byte header {"BRUT", u16 version 1, u16 dim,
+ * u32 count, u8 quantization, 7 pad}, int32 ids[count], row-major data; little
+ * endian. serialize: pass buf = NULL to get the size in *written. */
+int sem_index_serialize(sem_index *idx, void *buf, size_t cap, size_t *written);
+int sem_index_deserialize(sem_context *ctx, const void *bytes, size_t n, sem_index **out);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,131 @@
+"""search/brute on the GPU vs the CPU oracle, through the C ABI.
+
+Integer contract: scores and top-k ids bit-exact (ties to the lower row).
+Reference float contract: same arithmetic as the reference's AVX2 loops, so
+top-k ids and distances are compared exactly too.
+"""
+import struct
+
+import numpy as np
+import pytest
+
+import brute
+import oracle
+import synth
+
+pytestmark = pytest.mark.gpu
+
+
+def unit_rows(seed, n, dim):
+    return oracle.normalize(synth.normal_vectors(seed, n, dim))
+
+
+@pytest.mark.parametrize("quant", [1, 2])
+@pytest.mark.parametrize("dim", [768, 256, 100, 3])
+def test_exact_search_bit_exact(ctx, quant, dim):
+    n, nq, k = 3000 if dim > 3 else 500, 37, 10
+    vecs = unit_rows(1 + dim, n, dim)
+    vecs[7] = vecs[3]  # duplicate rows: ties must go to the lower row
+    idx = brute.Index.build(ctx, vecs, quantization=quant)
+    conv = oracle.quantize_int8_vec if quant == 1 else oracle.quantize_int16_vec
+    codes = conv(vecs)
+    queries = synth.normal_vectors(99 + dim, nq, dim)
+    queries[0] = vecs[3] * 2.0
+    ids, dist, scores = idx.search_batch(queries, k, brute.SEARCH_EXACT, normalize=True)
+    qcodes = conv(oracle.normalize(queries))
+    rrows, rscores, rdist = oracle.search_exact_batch(quant, codes, qcodes, k)
+    np.testing.assert_array_equal(ids, rrows)
+    np.testing.assert_array_equal(scores, rscores)
+    np.testing.assert_array_equal(dist, rdist)
+    assert ids[0, 0] == 3 and ids[0, 1] == 7
+
+
+@pytest.mark.parametrize("quant", [0, 1, 2])
+def test_reference_float_search_matches(ctx, quant):
+    dim, n, nq, k = 64, 256, 20, 10
+    vecs = unit_rows(456, n, dim)
+    ids_in = np.arange(1000, 1000 + n, dtype=np.int32)
+    idx = brute.Index.build(ctx, vecs, ids_in, quantization=quant)
+    conv = {0: lambda v: v, 1: oracle.quantize_int8_vec, 2: oracle.quantize_int16_vec}[quant]
+    data = conv(vecs)
+    queries = unit_rows(457, nq, dim)
+    gids, gdist, _ = idx.search_batch(queries, k, brute.SEARCH_REFERENCE, normalize=False)
+    for i in range(nq):
+        rid, rd = oracle.search_ref(quant, data, ids_in, queries[i], k)
+        np.testing.assert_array_equal(gids[i], rid)
+        np.testing.assert_array_equal(gdist[i], rd)
+
+
+def test_search_vector_api_and_errors(ctx):
+    # search/brute/index_test.go:10-64 (ids 10/11/12, query [1,0,0])
+    b = brute.Builder(ctx, dimension=3, quantization=brute.QuantizeInt8)
+    for i, v in {10: [1, 0, 0], 11: [0, 1, 0], 12: [0, 0, 1]}.items():
+        b.add_vector(i, v)
+    with pytest.raises(ValueError, match="duplicate id 10"):
+        b.add_vector(10, [1, 1, 1])
+    with pytest.raises(ValueError, match="vector dimension mismatch: got 2 want 3"):
+        b.add_vector(13, [1, 1])
+    idx = b.build()
+    res = idx.search_vector([1, 0, 0], 2)
+    assert res[0].ID == 10 and len(res) == 2
+    assert idx.count() == 3 and idx.dimension() == 3
+    res5 = idx.search_vector([1, 0, 0], 5)  # topK > count
+    assert [r.ID for r in res5] == [10, 11, 12]
+    import _lib
+    with pytest.raises(_lib.SemError, match="^brute: topK must be positive$"):
+        idx.search_vector([1, 0, 0], 0)
+    with pytest.raises(_lib.SemError, match=r"^brute: query dimension mismatch: got 2 want 3$"):
+        idx.search_vector([1, 0], 1)
+
+
+@pytest.mark.parametrize("quant,dt", [(0, np.float32), (1, np.int8), (2, np.int16)])
+def test_serializer_round_trip_byte_exact(ctx, quant, dt):
+    dim, n = 5, 9
+    vecs = unit_rows(77, n, dim)
+    ids = np.array([5, 3, 99, 1, 0, 7, 8, 2, 4], dtype=np.int32)
+    idx = brute.Index.build(ctx, vecs, ids, quantization=quant)
+    blob = brute.Serializer.serialize(idx)
+    conv = {0: lambda v: v, 1: oracle.quantize_int8_vec, 2: oracle.quantize_int16_vec}[quant]
+    want = b"BRUT" + struct.pack("<HHIB7x", 1, dim, n, quant) + ids.tobytes() + conv(vecs).astype(dt).tobytes()
+    assert blob == want
+    back = brute.Serializer.deserialize(blob, ctx)
+    assert back.count() == n and back.dimension() == dim and back.quantization() == quant
+    assert brute.Serializer.serialize(back) == blob
+    v = back.vector(99)
+    assert v is not None and v.shape == (dim,)
+    assert back.vector(12345) is None
+    import _lib
+    with pytest.raises(_lib.SemError, match="invalid magic"):
+        brute.Serializer.deserialize(b"XXXX" + blob[4:], ctx)
+    with pytest.raises(_lib.SemError, match="unsupported version 2"):
+        brute.Serializer.deserialize(blob[:4] + b"\x02\x00" + blob[6:], ctx)
+
+
+def test_sharded_keys_merge_equals_full_search(ctx):
+    import ctypes
+    import torch
+    import _lib
+    dim, n, nq, k = 256, 5000, 24, 10
+    vecs = unit_rows(5, n, dim)
+    codes = oracle.quantize_int8_vec(vecs)
+    bounds = [0, 1700, 3300, n]
+    shards = [brute.Index.from_codes(ctx, codes[a:b]) for a, b in zip(bounds, bounds[1:])]
+    q = oracle.quantize_int8_vec(unit_rows(6, nq, dim))
+    qpad = np.zeros((nq, 256), dtype=np.int8)
+    qpad[:, :dim] = q
+    d_q = torch.from_numpy(qpad).cuda()
+    keys = torch.zeros((3, nq, k), dtype=torch.int64, device="cuda")
+    torch.cuda.synchronize()
+    for s, (idx, base) in enumerate(zip(shards, bounds)):
+        _lib.check(_lib.load().sem_index_search_keys(idx.handle, ctypes.c_void_p(d_q.data_ptr()), nq, k, 1, base,
+                                                     ctypes.c_void_p(keys[s].data_ptr()), None))
+    rows = torch.empty((nq, k), dtype=torch.int32, device="cuda")
+    scores = torch.empty((nq, k), dtype=torch.int32, device="cuda")
+    st = ctypes.c_void_p(ctx.stream)
+    _lib.check(_lib.load().sem_topk_merge(ctx.handle, ctypes.c_void_p(keys.data_ptr()), 3, nq, k, k, 1, 1,
+                                          ctypes.c_void_p(rows.data_ptr()), ctypes.c_void_p(scores.data_ptr()),
+                                          None, st))
+    torch.cuda.synchronize()
+    rrows, rscores, _ = oracle.search_exact_batch(1, codes, q, k)
+    np.testing.assert_array_equal(rows.cpu().numpy(), rrows)
+    np.testing.assert_array_equal(scores.cpu().numpy(), rscores)

@@ -1,0 +1,112 @@
+"""Embedding forward on the GPU vs the CPU oracle, through the C ABI.
+
+Tolerance (written here): per embedding cosine >= 0.9995
+and max-abs error <= 2e-3 on the normalised vector.
+"""
+import numpy as np
+import pytest
+
+import synth
+from conftest import TEST_VOCAB, cosine
+
+pytestmark = pytest.mark.gpu
+
+COS_MIN = 0.9995
+MAX_ABS = 2e-3
+
+
+def compare(gpu_out, ref_out, label):
+    worst_cos, worst_abs = 1.0, 0.0
+    for g, r in zip(gpu_out, ref_out):
+        assert g.shape == r.shape
+        assert np.isfinite(g).all()
+        worst_cos = min(worst_cos, cosine(g, r))
+        worst_abs = max(worst_abs, float(np.abs(g - r).max()))
+    print(f"{label}: min cosine {worst_cos:.7f}  max abs {worst_abs:.2e}")
+    return worst_cos, worst_abs
+
+
+def test_config1_batch_8x64(gpu_model, oracle_model):
+    # 8 sequences x 64 tokens (BOS + uniform non-special ids), 768-dim output
+    ids, offs = synth.token_batch(101, [64] * 8, TEST_VOCAB)
+    ref = oracle_model.forward_batch(ids, offs, 768)
+    got = gpu_model.forward_batch(ids, offs, 768)
+    c, a = compare(got, ref, "8x64")
+    assert c >= COS_MIN
+    assert a <= MAX_ABS
+
+
+def test_ragged_lengths_and_matryoshka_dims(gpu_model, oracle_model):
+    # edge lengths (1, tile tails) and all four Matryoshka tiers in one batch
+    lengths = [1, 2, 3, 31, 33, 64, 65, 130]
+    dims = [768, 512, 256, 128, 768, 512, 256, 128]
+    ids, offs = synth.token_batch(202, lengths, TEST_VOCAB)
+    got = gpu_model.forward_batch(ids, offs, dims)
+    ref = [oracle_model.forward_with_dim(ids[offs[i]:offs[i + 1]], dims[i]) for i in range(len(lengths))]
+    c, a = compare(got, ref, "ragged")
+    assert c >= COS_MIN
+    assert a <= MAX_ABS
+
+
+def test_long_sequences_512(gpu_model, oracle_model):
+    ids, offs = synth.token_batch(303, [512, 512], TEST_VOCAB)
+    ref = oracle_model.forward_batch(ids, offs, 768)
+    got = gpu_model.forward_batch(ids, offs, 768)
+    c, a = compare(got, ref, "2x512")
+    assert c >= COS_MIN
+    assert a <= MAX_ABS
+
+
+def test_matryoshka_prefix_and_unit_norm(gpu_model):
+    ids, offs = synth.token_batch(404, [40, 40], TEST_VOCAB)
+    full = gpu_model.forward_batch(ids, offs, 768)
+    small = gpu_model.forward_batch(ids, offs, 128)
+    for f, s in zip(full, small):
+        assert abs(np.linalg.norm(s) - 1) < 1e-5
+        pre = f[:128] / np.linalg.norm(f[:128].astype(np.float64))
+        np.testing.assert_allclose(s, pre, atol=2e-6)
+
+
+def test_deterministic(gpu_model):
+    ids, offs = synth.token_batch(505, [17, 64, 3], TEST_VOCAB)
+    a = gpu_model.forward_batch(ids, offs, 768)
+    b = gpu_model.forward_batch(ids, offs, 768)
+    for x, y in zip(a, b):
+        np.testing.assert_array_equal(x, y)
+
+
+def test_errors_match_reference(gpu_model):
+    import _lib
+    with pytest.raises(_lib.SemError, match="^empty input$"):
+        gpu_model.forward_batch(np.array([2, 5], dtype=np.int32), np.array([0, 2, 2]), 768)
+    with pytest.raises(_lib.SemError, match=r"^sequence too long: 2049 > 2048$"):
+        gpu_model.forward_with_dim(np.full(2049, 5), 768)
+    with pytest.raises(_lib.SemError, match=r"^token ID out of range: 4096$"):
+        gpu_model.forward_with_dim([2, 4096], 768)
+    with pytest.raises(_lib.SemError, match=r"^target dimension 0 out of range \(1\.\.768\)$"):
+        gpu_model.forward_with_dim([2, 5], 0)
+
+
+def test_q8_gemm_matches_oracle(ctx):
+    # BASELINE config 2 shapes (one scale for the whole activation buffer)
+    import torch
+    import oracle
+    import runtime
+    rng = np.random.default_rng(11)
+    for K, N, M in ((768, 256, 64), (1152, 768, 200), (768, 3072, 33)):
+        raw = synth.q8_0_blocks(rng, N, K)
+        a = rng.standard_normal((M, K)).astype(np.float32)
+        w = runtime.Q8Weight(ctx, raw, K, N)
+        d_a = torch.from_numpy(a).cuda()
+        d_c = torch.empty((M, N), dtype=torch.float32, device="cuda")
+        d_codes = torch.empty((M, K), dtype=torch.int8, device="cuda")
+        d_abs = torch.zeros(4, dtype=torch.int32, device="cuda")
+        torch.cuda.synchronize()
+        w.run(d_a.data_ptr(), M, d_c.data_ptr(), d_codes.data_ptr(), d_abs.data_ptr(), ctx.stream)
+        torch.cuda.synchronize()
+        codes, scale = oracle.quantize_sym_int8(a)
+        np.testing.assert_array_equal(d_codes.cpu().numpy(), codes)
+        ref = oracle.matmul_q8_0_int8(raw, codes, scale, N)
+        got = d_c.cpu().numpy()
+        np.testing.assert_allclose(got, ref, rtol=2e-5, atol=2e-5 * np.abs(ref).max())
+        w.close()

@@ -1,0 +1,91 @@
+"""Host-side logic that needs no GPU: prompt templates, dimension rules, the
+C-ABI exports, and the synthetic GGUF layout."""
+import ctypes
+import os
+import re
+
+import numpy as np
+import pytest
+
+import ggufembed as ge
+from conftest import ROOT
+
+CONTENT = "neural networks are powerful"
+
+
+@pytest.mark.parametrize("inp,want", [
+    # pkg/ggufembed/api_test.go:12-105
+    (ge.EmbedInput(Task=ge.TaskNone, Content=CONTENT), CONTENT),
+    (ge.EmbedInput(Task=ge.TaskSearchQuery, Content=CONTENT), "task: search result | query: " + CONTENT),
+    (ge.EmbedInput(Task=ge.TaskQuestionAnswering, Content=CONTENT), "task: question answering | query: " + CONTENT),
+    (ge.EmbedInput(Task=ge.TaskFactVerification, Content=CONTENT), "task: fact checking | query: " + CONTENT),
+    (ge.EmbedInput(Task=ge.TaskClassification, Content=CONTENT), "task: classification | query: " + CONTENT),
+    (ge.EmbedInput(Task=ge.TaskClustering, Content=CONTENT), "task: clustering | query: " + CONTENT),
+    (ge.EmbedInput(Task=ge.TaskSemanticSimilarity, Content=CONTENT), "task: sentence similarity | query: " + CONTENT),
+    (ge.EmbedInput(Task=ge.TaskCodeRetrieval, Content=CONTENT), "task: code retrieval | query: " + CONTENT),
+    (ge.EmbedInput(Task=ge.TaskSearchDocument, Title="Doc", Content=CONTENT), "title: Doc | text: " + CONTENT),
+    (ge.EmbedInput(Task=ge.TaskSearchDocument, Content=CONTENT), "title: none | text: " + CONTENT),
+    (ge.EmbedInput(Task=ge.TaskSemanticSimilarity, Content=CONTENT, CustomTaskDescription="custom"),
+     "task: custom | query: " + CONTENT),
+])
+def test_build_prompt_matches_model_card(inp, want):
+    assert ge.build_prompt(inp) == want
+
+
+def test_build_prompt_errors():
+    with pytest.raises(ValueError, match="content must not be empty"):
+        ge.build_prompt(ge.EmbedInput(Task=ge.TaskSearchQuery))
+    with pytest.raises(ValueError, match="unsupported task"):
+        ge.build_prompt(ge.EmbedInput(Task=42, Content=CONTENT))
+
+
+def test_resolve_dim():
+    # tasks.go:101-116
+    assert ge.resolve_dim(0) == 512
+    for d in (768, 512, 256, 128):
+        assert ge.resolve_dim(d) == d
+    with pytest.raises(ValueError, match=r"unsupported embed dim 300 \(allowed: 768, 512, 256, 128\)"):
+        ge.resolve_dim(300)
+    assert ge.supported_dims() == [768, 512, 256, 128]
+
+
+def header_symbols():
+    text = open(os.path.join(ROOT, "include", "semantica_b200.h")).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(sem_[a-z0-9_]+)\s*\(", text)))
+
+
+def test_library_exports_every_declared_symbol():
+    import _lib
+    lib = ctypes.CDLL(_lib.LIB_PATH)  # loads without a GPU
+    syms = header_symbols()
+    assert len(syms) >= 25
+    for s in syms:
+        assert hasattr(lib, s), s
+    assert set(syms) == set(_lib.exported_symbols())
+
+
+def test_no_gpu_calls_fail_cleanly_without_device():
+    import _lib
+    if _lib.device_count() > 0:
+        pytest.skip("a GPU is visible")
+    with pytest.raises(_lib.SemError):
+        _lib.Context(0)
+
+
+def test_synthetic_gguf_parses_in_oracle(model_path):
+    import oracle
+    m = oracle.OracleModel(model_path)
+    c = m.config
+    assert (c.embed_dim, c.num_layers, c.num_heads, c.num_kv_heads, c.head_dim, c.interm_dim) == (768, 24, 3, 1, 256, 1152)
+    assert c.vocab_size == 4096 and c.max_seq_len == 2048
+    assert abs(c.attention_scale - 1 / 16) < 1e-9
+    m.close()
+
+
+def test_token_batch_layout():
+    import synth
+    ids, offs = synth.token_batch(5, [3, 1, 4], 100)
+    assert offs.tolist() == [0, 3, 4, 8]
+    assert ids[0] == ids[3] == ids[4] == synth.BOS_ID
+    assert (ids[[1, 2, 5, 6, 7]] >= synth.FIRST_NON_SPECIAL).all()
