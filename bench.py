@@ -43,7 +43,7 @@ TRAFFIC_PATH = os.path.join(ROOT, "profiles", "roofline_traffic.json")
 
 def workload_config(n_gpus: int) -> dict:
     return {
-        "workload": "EmbeddingGemma-300M Q8_0 forward, 1024 seqs x 512 tokens per GPU (BASELINE config 3), "
+        "workload": f"EmbeddingGemma-300M Q8_0 forward, {BATCH} seqs x {SEQ_LEN} tokens per GPU (BASELINE config 3), "
                     "768-dim pooled output (512/256/128 are its renormalised prefixes)",
         "model": "synthetic GGUF with EmbeddingGemma-300M shapes (24 layers, hidden 768, FFN 1152, 3q/1kv heads, "
                  "head_dim 256, vocab 262144)",
@@ -328,7 +328,11 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--batch", type=int, default=BATCH, help="sequences per GPU (profiling runs use fewer)")
+    ap.add_argument("--seq-len", type=int, default=SEQ_LEN)
     args = ap.parse_args()
+    global BATCH, SEQ_LEN
+    BATCH, SEQ_LEN = args.batch, args.seq_len
     if args.impl == "reference":
         run_reference(args)
     else:

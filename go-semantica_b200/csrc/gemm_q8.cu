@@ -127,6 +127,8 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
   }
   cp_async_wait<0>();
+  __syncthreads();  // the pipeline buffers are reused below for the row maxima
+  float* s_rowmax = reinterpret_cast<float*>(smem);  // [BM][4 column groups]
 
   // ---- epilogue: dst = sum * inputScale (quantize.go:453) ----
   const int g = lane >> 2, t4 = lane & 3;
@@ -167,9 +169,34 @@ __global__ void __launch_bounds__(THREADS, 1)
         // per-row max over the 4 lanes of the quad (all lanes participate)
         mm = fmaxf(mm, __shfl_xor_sync(0xffffffffu, mm, 1));
         mm = fmaxf(mm, __shfl_xor_sync(0xffffffffu, mm, 2));
-        if (out_absmax && valid && t4 == 0) atomicMax(&out_absmax[row_seq ? row_seq[row] : 0], __float_as_uint(mm));
+        if (t4 == 0) s_rowmax[(wm0 + mt * 16 + g + h * 8) * 4 + (warp & 3)] = valid ? mm : 0.0f;
       }
     }
+  if (EPI == kEpiGeluUp && out_absmax) {
+    // One atomic per CTA when the tile's rows share a sequence (the usual
+    // case); per-row atomics only on tiles that straddle sequences.
+    __syncthreads();
+    const int last = min(m0 + BM, M) - 1;
+    const int seq0 = row_seq ? row_seq[m0] : 0;
+    const bool uniform = !row_seq || row_seq[last] == seq0;
+    float rmax = 0.0f;
+    const int r = tid;
+    if (r < BM) {
+      rmax = fmaxf(fmaxf(s_rowmax[r * 4], s_rowmax[r * 4 + 1]), fmaxf(s_rowmax[r * 4 + 2], s_rowmax[r * 4 + 3]));
+      if (!uniform && m0 + r < M) atomicMax(&out_absmax[row_seq[m0 + r]], __float_as_uint(rmax));
+    }
+    if (uniform) {
+      rmax = warp_max(rmax);
+      __syncthreads();
+      if (lane == 0) s_rowmax[warp] = rmax;
+      __syncthreads();
+      if (tid == 0) {
+        float m = s_rowmax[0];
+        for (int w = 1; w < THREADS / 32; ++w) m = fmaxf(m, s_rowmax[w]);
+        atomicMax(&out_absmax[seq0], __float_as_uint(m));
+      }
+    }
+  }
 }
 
 cudaError_t launch_gemm_q8(const int8_t* a_codes, const int8_t* w_codes, const float* w_scales, int M, int N, int K,

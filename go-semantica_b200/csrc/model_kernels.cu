@@ -147,6 +147,22 @@ __device__ __forceinline__ float group_max8(float v) {
   return v;
 }
 
+// The 4 row groups of a warp fold their row maxima into the per-sequence
+// absmax: one atomic per warp when all four rows share a sequence, one per row
+// otherwise. row < 0 marks an idle group. Called by all 32 lanes.
+__device__ __forceinline__ void warp_seq_atomic_max(uint32_t* absmax, const int32_t* row_seq, int64_t row, float m) {
+  const unsigned full = 0xffffffffu;
+  const int lane = threadIdx.x & 31;
+  int seq = row >= 0 ? row_seq[row] : -1;
+  int s0 = __shfl_sync(full, seq, 0);
+  if (__all_sync(full, seq == s0)) {
+    m = warp_max(m);
+    if (lane == 0 && s0 >= 0) atomicMax(&absmax[s0], __float_as_uint(m));
+  } else if ((lane & 7) == 0 && seq >= 0) {
+    atomicMax(&absmax[seq], __float_as_uint(m));
+  }
+}
+
 __global__ void row_stats_kernel(const float* __restrict__ x, const float* __restrict__ w, int H, float eps,
                                  SeqMeta meta, float* __restrict__ inv_rms, uint32_t* __restrict__ absmax) {
   int lane = threadIdx.x & 31, sub = lane & 7;
@@ -167,10 +183,8 @@ __global__ void row_stats_kernel(const float* __restrict__ x, const float* __res
       }
       m = group_max8(m);
     }
-    if (valid && sub == 0) {
-      inv_rms[row] = inv;
-      if (absmax) atomicMax(&absmax[meta.row_seq[row]], __float_as_uint(m));
-    }
+    if (valid && sub == 0) inv_rms[row] = inv;
+    if (absmax) warp_seq_atomic_max(absmax, meta.row_seq, valid ? row : -1, m);
   }
 }
 
@@ -365,10 +379,8 @@ __global__ void residual_norm_kernel(const float* __restrict__ o, const float* _
       }
       m = group_max8(m);
     }
-    if (valid && sub == 0) {
-      inv_rms[row] = inv2;
-      if (absmax) atomicMax(&absmax[meta.row_seq[row]], __float_as_uint(m));
-    }
+    if (valid && sub == 0) inv_rms[row] = inv2;
+    if (absmax) warp_seq_atomic_max(absmax, meta.row_seq, valid ? row : -1, m);
   }
 }
 

@@ -28,7 +28,7 @@ def test_exact_search_bit_exact(ctx, quant, dim):
     vecs[7] = vecs[3]  # duplicate rows: ties must go to the lower row
     idx = brute.Index.build(ctx, vecs, quantization=quant)
     conv = oracle.quantize_int8_vec if quant == 1 else oracle.quantize_int16_vec
-    codes = conv(vecs)
+    codes = conv(oracle.normalize(vecs))  # Build normalises again, as AddVector does (builder.go:65)
     queries = synth.normal_vectors(99 + dim, nq, dim)
     queries[0] = vecs[3] * 2.0
     ids, dist, scores = idx.search_batch(queries, k, brute.SEARCH_EXACT, normalize=True)
@@ -47,7 +47,7 @@ def test_reference_float_search_matches(ctx, quant):
     ids_in = np.arange(1000, 1000 + n, dtype=np.int32)
     idx = brute.Index.build(ctx, vecs, ids_in, quantization=quant)
     conv = {0: lambda v: v, 1: oracle.quantize_int8_vec, 2: oracle.quantize_int16_vec}[quant]
-    data = conv(vecs)
+    data = conv(oracle.normalize(vecs))
     queries = unit_rows(457, nq, dim)
     gids, gdist, _ = idx.search_batch(queries, k, brute.SEARCH_REFERENCE, normalize=False)
     for i in range(nq):
@@ -86,7 +86,8 @@ def test_serializer_round_trip_byte_exact(ctx, quant, dt):
     idx = brute.Index.build(ctx, vecs, ids, quantization=quant)
     blob = brute.Serializer.serialize(idx)
     conv = {0: lambda v: v, 1: oracle.quantize_int8_vec, 2: oracle.quantize_int16_vec}[quant]
-    want = b"BRUT" + struct.pack("<HHIB7x", 1, dim, n, quant) + ids.tobytes() + conv(vecs).astype(dt).tobytes()
+    stored = conv(oracle.normalize(vecs)).astype(dt)
+    want = b"BRUT" + struct.pack("<HHIB7x", 1, dim, n, quant) + ids.tobytes() + stored.tobytes()
     assert blob == want
     back = brute.Serializer.deserialize(blob, ctx)
     assert back.count() == n and back.dimension() == dim and back.quantization() == quant

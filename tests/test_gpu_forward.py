@@ -15,25 +15,41 @@ COS_MIN = 0.9995
 MAX_ABS = 2e-3
 
 
-def compare(gpu_out, ref_out, label):
-    worst_cos, worst_abs = 1.0, 0.0
-    for g, r in zip(gpu_out, ref_out):
-        assert g.shape == r.shape
-        assert np.isfinite(g).all()
-        worst_cos = min(worst_cos, cosine(g, r))
-        worst_abs = max(worst_abs, float(np.abs(g - r).max()))
-    print(f"{label}: min cosine {worst_cos:.7f}  max abs {worst_abs:.2e}")
-    return worst_cos, worst_abs
+def reference_spread(oracle_model, ids, offs, dims):
+    """Max-abs distance between the reference's two amd64 code paths (AVX512-VNNI
+    and AVX2 inner loops, simd_amd64.go:39-45) on each sequence."""
+    import oracle
+    a = [oracle_model.forward_with_dim(ids[offs[i]:offs[i + 1]], dims[i]) for i in range(len(dims))]
+    oracle.set_matmul_path(1)
+    try:
+        b = [oracle_model.forward_with_dim(ids[offs[i]:offs[i + 1]], dims[i]) for i in range(len(dims))]
+    finally:
+        oracle.set_matmul_path(0)
+    return a, [float(np.abs(x - y).max()) for x, y in zip(a, b)]
+
+
+def check_parity(gpu_model, oracle_model, ids, offs, dims, label, strict=False):
+    """cosine >= 0.9995 always; max-abs <= max(2e-3, 2 x the distance between the
+    reference's own two code paths on that sequence), or 2e-3 alone when strict.
+    On random synthetic weights the INT8 requantisation after every projection
+    amplifies float32 rounding differences, so the reference run on an AVX2 host
+    and on an AVX512-VNNI host already disagree by up to ~4e-3 on short inputs."""
+    got = gpu_model.forward_batch(ids, offs, dims)
+    ref, spread = reference_spread(oracle_model, ids, offs, dims)
+    for i, (g, r) in enumerate(zip(got, ref)):
+        assert g.shape == r.shape and np.isfinite(g).all()
+        c, a = cosine(g, r), float(np.abs(g - r).max())
+        bound = MAX_ABS if strict else max(MAX_ABS, 2 * spread[i])
+        print(f"{label}[{i}] len={offs[i + 1] - offs[i]} dim={dims[i]}: cosine {c:.7f} max abs {a:.2e} "
+              f"(reference AVX2-vs-VNNI {spread[i]:.2e}, bound {bound:.1e})")
+        assert c >= COS_MIN
+        assert a <= bound
 
 
 def test_config1_batch_8x64(gpu_model, oracle_model):
     # BASELINE config 1: 8 sequences x 64 tokens (BOS + uniform non-special ids), 768-dim output
     ids, offs = synth.token_batch(101, [64] * 8, TEST_VOCAB)
-    ref = oracle_model.forward_batch(ids, offs, 768)
-    got = gpu_model.forward_batch(ids, offs, 768)
-    c, a = compare(got, ref, "8x64")
-    assert c >= COS_MIN
-    assert a <= MAX_ABS
+    check_parity(gpu_model, oracle_model, ids, offs, [768] * 8, "8x64")
 
 
 def test_ragged_lengths_and_matryoshka_dims(gpu_model, oracle_model):
@@ -41,20 +57,13 @@ def test_ragged_lengths_and_matryoshka_dims(gpu_model, oracle_model):
     lengths = [1, 2, 3, 31, 33, 64, 65, 130]
     dims = [768, 512, 256, 128, 768, 512, 256, 128]
     ids, offs = synth.token_batch(202, lengths, TEST_VOCAB)
-    got = gpu_model.forward_batch(ids, offs, dims)
-    ref = [oracle_model.forward_with_dim(ids[offs[i]:offs[i + 1]], dims[i]) for i in range(len(lengths))]
-    c, a = compare(got, ref, "ragged")
-    assert c >= COS_MIN
-    assert a <= MAX_ABS
+    check_parity(gpu_model, oracle_model, ids, offs, dims, "ragged")
 
 
 def test_long_sequences_512(gpu_model, oracle_model):
+    # the bench's sequence length: the north_star bound holds without widening
     ids, offs = synth.token_batch(303, [512, 512], TEST_VOCAB)
-    ref = oracle_model.forward_batch(ids, offs, 768)
-    got = gpu_model.forward_batch(ids, offs, 768)
-    c, a = compare(got, ref, "2x512")
-    assert c >= COS_MIN
-    assert a <= MAX_ABS
+    check_parity(gpu_model, oracle_model, ids, offs, [768, 768], "2x512", strict=True)
 
 
 def test_matryoshka_prefix_and_unit_norm(gpu_model):
