@@ -322,16 +322,16 @@ def run_ours(args) -> None:
 
 
 def main():
+    global BATCH, SEQ_LEN
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--batch", type=int, default=BATCH, help="sequences per GPU (profiling runs use fewer)")
-    ap.add_argument("--seq-len", type=int, default=SEQ_LEN)
+    ap.add_argument("--batch", type=int, default=1024, help="sequences per GPU (profiling runs use fewer)")
+    ap.add_argument("--seq-len", type=int, default=512)
     args = ap.parse_args()
-    global BATCH, SEQ_LEN
     BATCH, SEQ_LEN = args.batch, args.seq_len
     if args.impl == "reference":
         run_reference(args)
