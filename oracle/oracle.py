@@ -261,5 +261,6 @@ def search_exact_batch(quant: int, data: np.ndarray, qcodes: np.ndarray, topk: i
 
 
 def set_matmul_path(path: int) -> None:
-    """0: the reference's AVX512-VNNI inner loop (default); 1: its AVX2 inner loop."""
+    """Reference build to follow: 0 amd64 on an AVX512-VNNI host (default),
+    1 amd64 on an AVX2-only host, 2 the portable (noasm) build."""
     lib().orc_set_matmul_path(path)

@@ -40,6 +40,16 @@ static void seterr(char *err, int errlen, const char *fmt, ...) {
 }
 
 static inline float bits_to_f32(uint32_t b) { float f; memcpy(&f, &b, 4); return f; }
+
+/* Which build of the reference to follow. The reference selects its kernels at
+ * build and run time: 0 = amd64 on an AVX512-VNNI host (matmulInnerLoopVNNIAsm,
+ * simd_amd64.go:41-45; the default here), 1 = amd64 on an AVX2-only host
+ * (matmulInnerLoopAsm), 2 = the portable build (noasm tag or another GOARCH:
+ * simd_generic.go, matmul_inner_loop_fallback.go, dotProductInline for the
+ * attention scores, attention.go:294-298). The three differ only in float32
+ * summation order. */
+static int g_matmul_path = 0;
+void orc_set_matmul_path(int path) { g_matmul_path = path; }
 static inline uint32_t f32_to_bits(float f) { uint32_t b; memcpy(&b, &f, 4); return b; }
 
 /* ------------------------------------------------------------------------
@@ -189,7 +199,7 @@ static inline float hsum8(const float acc[8]) {
  * sum, then an unfused scalar tail), scalar loop otherwise. */
 float orc_dot_f32(const float *a, const float *b, int n) {
     if (n == 0) return 0.0f;
-    if (n < 8) {
+    if (n < 8 || g_matmul_path == 2) { /* dotProductScalar / sumSquaresScalar (simd_generic.go, norm.go:94-100) */
         float s = 0.0f;
         for (int i = 0; i < n; i++) s += a[i] * b[i];
         return s;
@@ -204,6 +214,22 @@ float orc_dot_f32(const float *a, const float *b, int n) {
         s = s + p;
     }
     return s;
+}
+
+/* dotProductInline (internal/kernels/attention.go:316-341): the attention score
+ * dot product of builds without AVX2. */
+static float dot_inline(const float *a, const float *b, int n) {
+    float s0 = 0, s1 = 0, s2 = 0, s3 = 0;
+    int i = 0;
+    for (; i + 16 <= n; i += 16) {
+        s0 += ((a[i] * b[i] + a[i + 1] * b[i + 1]) + a[i + 2] * b[i + 2]) + a[i + 3] * b[i + 3];
+        s1 += ((a[i + 4] * b[i + 4] + a[i + 5] * b[i + 5]) + a[i + 6] * b[i + 6]) + a[i + 7] * b[i + 7];
+        s2 += ((a[i + 8] * b[i + 8] + a[i + 9] * b[i + 9]) + a[i + 10] * b[i + 10]) + a[i + 11] * b[i + 11];
+        s3 += ((a[i + 12] * b[i + 12] + a[i + 13] * b[i + 13]) + a[i + 14] * b[i + 14]) + a[i + 15] * b[i + 15];
+    }
+    for (; i + 4 <= n; i += 4) s0 += ((a[i] * b[i] + a[i + 1] * b[i + 1]) + a[i + 2] * b[i + 2]) + a[i + 3] * b[i + 3];
+    for (; i < n; i++) s0 += a[i] * b[i];
+    return (s0 + s1) + (s2 + s3);
 }
 
 /* internal/kernels/norm.go:8-36 (AVX2 branch: VecScaleF32 then VecMulF32, two
@@ -268,12 +294,6 @@ void orc_extract_q8_0_scales(const uint8_t *data, int64_t rows, int cols, float 
         }
 }
 
-/* Which of the reference's two amd64 inner loops to follow (simd_amd64.go:39-45
- * picks by CPU feature): 0 = matmulInnerLoopVNNIAsm (AVX512-VNNI hosts, the
- * default here), 1 = matmulInnerLoopAsm (AVX2-only hosts). */
-static int g_matmul_path = 0;
-void orc_set_matmul_path(int path) { g_matmul_path = path; }
-
 /* Both inner loops (internal/kernels/simd_amd64.s:164-237 and :241-304) keep 8
  * float accumulators; per 32-byte block, lane l receives an exact int32 sum of
  * 4 products, converted to float and FMA'd with the block scale, and the lanes
@@ -282,6 +302,18 @@ void orc_set_matmul_path(int path) { g_matmul_path = path; }
  * (VPMOVSXBW + VPMADDWD on each 16-byte half, then VPADDD) sums bytes 2l, 2l+1,
  * 16+2l, 17+2l. */
 static float q8_inner_loop(const int8_t *in, const uint8_t *w, const float *scales, int nblocks) {
+    if (g_matmul_path == 2) { /* matmul_inner_loop_fallback.go:16-39 */
+        float sum = 0.0f;
+        for (int b = 0; b < nblocks; b++) {
+            const int8_t *x = in + 32 * b;
+            const int8_t *q = (const int8_t *)(w + 34 * b + 2);
+            int32_t acc = 0;
+            for (int t = 0; t < 32; t++) acc += (int32_t)x[t] * (int32_t)q[t];
+            float p = (float)acc * scales[b];
+            sum = sum + p;
+        }
+        return sum;
+    }
     float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
     for (int b = 0; b < nblocks; b++) {
         const int8_t *x = in + 32 * b;
@@ -741,7 +773,8 @@ int orc_forward(const orc_model *m, const int32_t *ids, int S, int target_dim, f
             for (int i = 0; i < S; i++) {
                 const float *qr = q + (size_t)i * H + (size_t)h * hd;
                 for (int j = 0; j < S; j++) {
-                    float d = orc_dot_f32(qr, ke + (size_t)j * H + (size_t)h * hd, hd);
+                    const float *kr = ke + (size_t)j * H + (size_t)h * hd;
+                    float d = g_matmul_path == 2 ? dot_inline(qr, kr, hd) : orc_dot_f32(qr, kr, hd);
                     scores[(size_t)i * S + j] = d * c->attention_scale;
                 }
             }

@@ -33,7 +33,7 @@ void  orc_quantize_sym_int8(const float *x, int64_t n, int8_t *codes, float *sca
 void  orc_matmul_q8_0_int8(float *dst, const uint8_t *w_q8, const float *w_scales,
                            const int8_t *a, float a_scale, int batch, int in_dim, int out_dim);
                                                    /* quantize.go:346-458, simd_amd64.s:164-304 */
-/* 0 = AVX512-VNNI inner loop (default), 1 = AVX2 inner loop (simd_amd64.go:39-45) */
+/* reference build to follow: 0 amd64 AVX512-VNNI (default), 1 amd64 AVX2, 2 portable noasm */
 void  orc_set_matmul_path(int path);
 void  orc_extract_q8_0_scales(const uint8_t *w_q8, int64_t rows, int cols, float *scales);
                                                    /* model_int8.go:543-569 */
