@@ -95,3 +95,11 @@ struct sem_context {
   sem::DevBuf scratch;  // shared device scratch (candidate lists, staging)
   sem::HostBuf pinned;
 };
+
+// A Q8_0 weight repacked for the device: int8 plane [n_out][k_in] and fp32
+// block scales [n_out][k_in/32].
+struct sem_q8_weight {
+  sem_context* ctx = nullptr;
+  int32_t k_in = 0, n_out = 0;
+  sem::DevBuf codes, scales;
+};

@@ -61,11 +61,6 @@ struct sem_model {
   int32_t prof_n[16] = {0};
 };
 
-struct sem_q8_weight {
-  sem_context* ctx = nullptr;
-  int32_t k_in = 0, n_out = 0;
-  sem::DevBuf codes, scales;
-};
 
 namespace sem {
 namespace {

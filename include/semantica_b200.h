@@ -134,6 +134,20 @@ int sem_q8_weight_free(sem_q8_weight *w);
 int sem_q8_gemm(sem_q8_weight *w, const float *d_a, int32_t m, float *d_c, int8_t *d_codes, uint32_t *d_absmax,
                 void *stream);
 
+/* sem_q8_gemm without caller scratch, for callers that cannot allocate device
+ * memory (a host runtime that owns the whole device pool and passes only input
+ * and output buffers, or a request path with a memory budget fixed at start-up
+ * where an allocation may neither grow nor fail). It has no counterpart in the
+ * reference. The codes and the absmax word live in a static device array of
+ * 8 MiB + 256 bytes that every GPU loading the library holds until exit, so
+ * m * k_in must not exceed 8 MiB (larger calls fail with SEM_EINVAL); the call
+ * performs no allocation. The first call on a device resolves the array's
+ * address on that device (cudaGetSymbolAddress); make that first call before
+ * any stream capture. All calls share the one array: calls that overlap on
+ * the GPU (other streams, other threads) race on it. Enqueued on `stream`
+ * (NULL = the weight's context stream). */
+int sem_q8_gemm_noalloc(sem_q8_weight *w, const float *d_a, int32_t m, float *d_c, void *stream);
+
 /* ------------------------------------------------------------------------
  * Brute-force index: replaces search/brute (builder.go, index.go, storage.go).
  * quant: 0 float32, 1 int8, 2 int16 (brute.QuantizationMode, quant.go:8-15).
