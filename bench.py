@@ -321,19 +321,215 @@ def run_ours(args) -> None:
         dist.destroy_process_group()
 
 
+# ---------------------------------------------------------------------------
+# --workload gemm: BASELINE config 2, the isolated Q8_0 x activation projection
+# ---------------------------------------------------------------------------
+GEMM_SHAPES = [(768, 768, "q/o"), (768, 256, "k/v"), (768, 1152, "gate/up"), (1152, 768, "down"),
+               (768, 3072, "dense up"), (3072, 768, "dense down")]
+GEMM_M = [1, 64, 512, 4096, 32768]
+GEMM_HEAD_M = 32768
+GEMM_METRIC = "Q8_0 projection TFLOP/s (kernel on pre-quantised activations, 6 model shapes, M=32768)"
+
+
+def gemm_config(n_gpus: int) -> dict:
+    return {"workload": "BASELINE config 2: MatMulQ8_0INT8 on the model's projection shapes (K x N = "
+                        + ", ".join(f"{k}x{n}" for k, n, _ in GEMM_SHAPES) + f"), M in {GEMM_M}",
+            "weights": "int8 uniform [-127,127], fp16 block scales |N(0,0.02)| max/127",
+            "activations": "fp32 N(0,1), one quantisation scale per call", "parallelism": f"replicas x{n_gpus}",
+            "l2": "L2 flushed (256 MB write) before every timed launch"}
+
+
+def gemm_algorithmic(K: int, N: int, M: int, prequant: bool) -> tuple[float, float]:
+    """FLOPs and algorithmic bytes of one call: A (fp32, or its int8 codes), the
+    34-byte-per-32 Q8_0 weight, fp32 C."""
+    a_bytes = M * K * (1 if prequant else 4)
+    return 2.0 * M * K * N, a_bytes + 34.0 / 32.0 * K * N + 4.0 * M * N
+
+
+def gemm_cpu_baseline(rows_per_thread: int = 1536) -> dict:
+    """The oracle's MatMulQ8_0INT8 restatement on every host thread: each thread
+    takes its own slice of rows of each config-2 shape (ctypes releases the GIL)."""
+    import concurrent.futures as cf
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle  # the CPU baseline leg is one of the places allowed to run the oracle
+    threads = max(1, min(os.cpu_count() or 1, 64))
+    rng = np.random.default_rng(77)
+    work = []
+    for K, N, _ in GEMM_SHAPES:
+        raw = synth.q8_0_blocks(rng, N, K)
+        codes, scale = oracle.quantize_sym_int8(rng.standard_normal((rows_per_thread * threads, K)).astype(np.float32))
+        work.append((raw, codes, scale, N, K))
+    flops = sum(2.0 * c.shape[0] * K * N for _, c, _, N, K in work)
+    t0 = time.perf_counter()
+    with cf.ThreadPoolExecutor(threads) as ex:
+        futs = [ex.submit(oracle.matmul_q8_0_int8, raw, codes[i * rows_per_thread:(i + 1) * rows_per_thread], scale, N)
+                for raw, codes, scale, N, _ in work for i in range(threads)]
+        for f in futs:
+            f.result()
+    dt = time.perf_counter() - t0
+    return {"value": flops / dt / 1e12, "unit": "TFLOP/s", "cores": threads, "kind": "port",
+            "sample": f"{rows_per_thread} rows per thread x {threads} threads on each of the 6 shapes ({dt:.1f} s); "
+                      "C restatement of MatMulQ8_0INT8 (oracle/semantica_oracle.c)"}
+
+
+def run_gemm_reference(args) -> None:
+    if int(os.environ.get("RANK", "0")) != 0:
+        return
+    times = []
+    cb = None
+    for _ in range(max(args.steps, 1)):
+        cb = gemm_cpu_baseline()
+        times.append(cb["value"])
+    value = statistics.median(times)
+    cb["value"] = value
+    print(json.dumps({"metric": GEMM_METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": args.gpus,
+                      "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
+                      "vs_baseline": None, "dtype": "int8", "data": "synthetic", "impl": "reference",
+                      "config": gemm_config(args.gpus), "cpu_baseline": cb,
+                      "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}),
+          flush=True)
+
+
+def run_gemm(args) -> None:
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        dist.init_process_group("nccl", timeout=__import__("datetime").timedelta(seconds=600))
+    torch.cuda.set_device(local)
+    import _lib
+    import runtime
+
+    ctx = _lib.Context(local)
+    stream = torch.cuda.ExternalStream(ctx.stream)
+    flush = torch.empty(64 << 20, dtype=torch.float32, device="cuda")  # 256 MB > L2
+    peaks = json.load(open(PEAKS_PATH)) if os.path.exists(PEAKS_PATH) else {}
+    tc_peak = peaks.get("bf16_tflops") or 1590.0
+    bw_peak = peaks.get("hbm_gbs") or 6650.0
+    rng = np.random.default_rng(2 + rank)
+    results = {}
+    head_flops = head_ms = 0.0
+    head_e2e_s = 0.0
+    h2d = d2h = 0
+    launches = 0
+    clocks = ClockSampler(None)
+    clocks.start()
+    for K, N, name in GEMM_SHAPES:
+        w = runtime.Q8Weight(ctx, synth.q8_0_blocks(rng, N, K), K, N)
+        for M in GEMM_M:
+            a = torch.randn((M, K), dtype=torch.float32, device="cuda")
+            codes = torch.empty((M, K), dtype=torch.float16, device="cuda")
+            absmax = torch.zeros(4, dtype=torch.int32, device="cuda")
+            c = torch.empty((M, N), dtype=torch.float32, device="cuda")
+            torch.cuda.synchronize()
+            w.run(a.data_ptr(), M, c.data_ptr(), codes.data_ptr(), absmax.data_ptr(), ctx.stream)  # quantises A
+
+            def timed(fn, n):
+                ts = []
+                for _ in range(n):
+                    with torch.cuda.stream(stream):
+                        flush.zero_()
+                    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                    e0.record(stream)
+                    fn()
+                    e1.record(stream)
+                    e1.synchronize()
+                    ts.append(e0.elapsed_time(e1))
+                return statistics.median(ts)
+
+            kern = lambda: w.matmul_int8(codes.data_ptr(), absmax.data_ptr(), M, c.data_ptr(), ctx.stream)
+            full = lambda: w.run(a.data_ptr(), M, c.data_ptr(), codes.data_ptr(), absmax.data_ptr(), ctx.stream)
+            timed(kern, max(args.warmup, 3))
+            ms_k = timed(kern, args.steps)
+            ms_f = timed(full, args.steps)
+            launches += 2 * args.steps * (1 + 3)
+            fl, by_k = gemm_algorithmic(K, N, M, True)
+            _, by_f = gemm_algorithmic(K, N, M, False)
+            tf_k = fl / (ms_k * 1e-3) / 1e12
+            gb_k = by_k / (ms_k * 1e-3) / 1e9
+            # roofline time of the launch: the slower of bytes over HBM and FLOPs over the tensor peak
+            t_roof = max(by_k / (bw_peak * 1e9), fl / (tc_peak * 1e12))
+            results[f"{K}x{N} M={M}"] = {
+                "kernel_ms": round(ms_k, 4), "kernel_tflops": round(tf_k, 2), "kernel_gbs": round(gb_k, 1),
+                "kernel_roofline_frac": round(t_roof / (ms_k * 1e-3), 3),
+                "bound": "hbm" if by_k / (bw_peak * 1e9) > fl / (tc_peak * 1e12) else "tensor",
+                "with_quantize_ms": round(ms_f, 4), "with_quantize_tflops": round(fl / (ms_f * 1e-3) / 1e12, 2)}
+            if M == GEMM_HEAD_M:
+                head_flops += fl
+                head_ms += ms_k
+                # e2e through the public call with host buffers: pinned A in, C out
+                a_h = torch.empty((M, K), dtype=torch.float32, pin_memory=True)
+                a_h.copy_(a.cpu())
+                c_h = torch.empty((M, N), dtype=torch.float32, pin_memory=True)
+                torch.cuda.synchronize()
+                t0 = time.perf_counter()
+                with torch.cuda.stream(stream):
+                    a.copy_(a_h, non_blocking=True)
+                full()
+                with torch.cuda.stream(stream):
+                    c_h.copy_(c, non_blocking=True)
+                stream.synchronize()
+                head_e2e_s += time.perf_counter() - t0
+                h2d += M * K * 4
+                d2h += M * N * 4
+                # pinned buffers used on the library's stream are released while that stream exists
+                del a_h, c_h
+            del a, codes, c
+        w.close()
+    clk = clocks.stop()
+    t = torch.tensor([head_ms, head_e2e_s], dtype=torch.float64, device="cuda")
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    head_ms, head_e2e_s = float(t[0]), float(t[1])
+    if rank == 0:
+        value = world * head_flops / (head_ms * 1e-3) / 1e12
+        dom = max(((k, v) for k, v in results.items() if k.endswith(f"M={GEMM_HEAD_M}")),
+                  key=lambda kv: kv[1]["kernel_ms"])
+        K, N = (int(x) for x in dom[0].split()[0].split("x"))
+        fl, _ = gemm_algorithmic(K, N, GEMM_HEAD_M, True)
+        ach = fl / (dom[1]["kernel_ms"] * 1e-3) / 1e12
+        line = {"metric": GEMM_METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": head_ms, "higher_is_better": True, "scaling": "weak",
+                "vs_baseline": None, "dtype": "int8 codes in fp16 MMAs, fp32 accumulate", "data": "synthetic",
+                "config": gemm_config(world), "clocks": clk,
+                "e2e": {"value": world * head_flops / head_e2e_s / 1e12, "unit": "TFLOP/s",
+                        "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+                "gpu_launches": launches,
+                "roofline": {"kernel": f"gemm_q8_tc {dom[0]}", "bound": "tensor", "achieved": ach, "peak": tc_peak,
+                             "unit": "TFLOP/s", "frac": ach / tc_peak,
+                             "peak_source": "measured bf16_tflops (burst; fp16 MMAs run at the bf16 rate)",
+                             "algorithmic_flops_per_launch": fl, "traffic": None},
+                "shapes": results}
+        if world == 1 and not args.no_cpu_baseline:
+            line["cpu_baseline"] = gemm_cpu_baseline()
+        print(json.dumps(line), flush=True)
+    ctx.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def main():
     global BATCH, SEQ_LEN
+    import faulthandler
+    faulthandler.enable()  # a crash prints the Python stack
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--workload", default="embed", choices=["embed", "gemm"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--batch", type=int, default=1024, help="sequences per GPU (profiling runs use fewer)")
     ap.add_argument("--seq-len", type=int, default=512)
     args = ap.parse_args()
     BATCH, SEQ_LEN = args.batch, args.seq_len
-    if args.impl == "reference":
+    if args.workload == "gemm":
+        run_gemm_reference(args) if args.impl == "reference" else run_gemm(args)
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_ours(args)

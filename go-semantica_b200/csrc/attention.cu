@@ -96,16 +96,23 @@ __global__ void __launch_bounds__(THREADS, 1)
     cp_async_wait<1>();
     __syncthreads();
     const __half* sK = sKV + (kt & 1) * 4 * KV_HALVES;
-    float s[2][4] = {{0, 0, 0, 0}, {0, 0, 0, 0}};
+    // four independent accumulator chains (k-step parity x key half) keep the
+    // tensor pipe busy; they are summed once per tile
+    float s4[2][2][4] = {};
 #pragma unroll 4
     for (int ks = 0; ks < HD / 16; ++ks) {
       uint32_t a[4], b[2][2];
       ldmatrix_x4(a[0], a[1], a[2], a[3], sQh + (r0 + (lane & 7) + ((lane >> 3) & 1) * 8) * LDH + (2 * ks + (lane >> 4)) * 8);
       ldmatrix_x4(b[0][0], b[0][1], b[1][0], b[1][1],
                   sK + (kk0 + (lane & 7) + (lane >> 4) * 8) * LDH + (2 * ks + ((lane >> 3) & 1)) * 8);
-      mma_f16(s[0], a, b[0]);
-      mma_f16(s[1], a, b[1]);
+      mma_f16(s4[ks & 1][0], a, b[0]);
+      mma_f16(s4[ks & 1][1], a, b[1]);
     }
+    float s[2][4];
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) s[nt][e] = __fadd_rn(s4[0][nt][e], s4[1][nt][e]);
 #pragma unroll
     for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
@@ -147,7 +154,9 @@ __global__ void __launch_bounds__(THREADS, 1)
     const __half* sVh = sKl + KV_HALVES;
     const __half* sVl = sVh + KV_HALVES;
     // scores of rows r0..r0+15 x keys kk0..kk0+15
-    float s[2][4] = {{0, 0, 0, 0}, {0, 0, 0, 0}};
+    // hi*hi and the two cross terms accumulate in separate chains, alternating
+    // by k-step parity: eight independent MMA chains per warp instead of two
+    float sm[2][2][4] = {}, sx[2][2][4] = {};
 #pragma unroll 2
     for (int ks = 0; ks < HD / 16; ++ks) {
       uint32_t ah[4], al[4], bh[2][2], bl[2][2];
@@ -159,11 +168,17 @@ __global__ void __launch_bounds__(THREADS, 1)
       ldmatrix_x4(bl[0][0], bl[0][1], bl[1][0], bl[1][1], sKl + koff);
 #pragma unroll
       for (int nt = 0; nt < 2; ++nt) {
-        mma_f16(s[nt], al, bh[nt]);
-        mma_f16(s[nt], ah, bl[nt]);
-        mma_f16(s[nt], ah, bh[nt]);
+        mma_f16(sx[ks & 1][nt], al, bh[nt]);
+        mma_f16(sx[ks & 1][nt], ah, bl[nt]);
+        mma_f16(sm[ks & 1][nt], ah, bh[nt]);
       }
     }
+    float s[2][4];
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+      for (int e = 0; e < 4; ++e)
+        s[nt][e] = __fadd_rn(__fadd_rn(sm[0][nt][e], sm[1][nt][e]), __fadd_rn(sx[0][nt][e], sx[1][nt][e]));
 #pragma unroll
     for (int nt = 0; nt < 2; ++nt) {
       float p[4];

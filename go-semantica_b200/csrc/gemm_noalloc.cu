@@ -1,7 +1,8 @@
 // sem_q8_gemm_noalloc: the Q8_0 projection for callers that cannot allocate.
 //
 // sem_q8_gemm needs two pieces of device scratch besides its input and output:
-// the INT8 activation codes (m x k_in bytes) and one absmax word. Its callers
+// the INT8 activation codes (m x k_in of them, held as fp16 for the tensor
+// cores) and one absmax word. Its callers
 // pass that scratch in. Some callers cannot provide or allocate it: a host
 // runtime that reserves all device memory for its own pool and hands out only
 // the buffers it manages (input and output), or a request path whose memory
@@ -9,7 +10,7 @@
 // also synchronises the device, which such a path cannot afford.
 //
 // This variant keeps the scratch in a file-scope static __device__ array of
-// fixed size (256 bytes for the absmax word + kNoAllocCodesBytes of codes).
+// fixed size (256 bytes for the absmax word + room for kNoAllocMaxCodes codes).
 // Every GPU that loads the library holds that array until the process exits.
 // The call makes no allocation: no cudaMalloc/cudaFree and no allocating
 // library routine.
@@ -21,8 +22,9 @@
 
 namespace {
 
-constexpr size_t kNoAllocHeaderBytes = 256;            // absmax word, padded to keep codes 256-byte aligned
-constexpr size_t kNoAllocCodesBytes = size_t(8) << 20; // 8 MiB of INT8 activation codes
+constexpr size_t kNoAllocHeaderBytes = 256;          // absmax word, padded to keep codes 256-byte aligned
+constexpr size_t kNoAllocMaxCodes = size_t(8) << 20;  // 8 Mi activation codes (m * k_in)
+constexpr size_t kNoAllocCodesBytes = kNoAllocMaxCodes * sizeof(__half);
 constexpr int kMaxDevices = 64;
 
 // In host code this name is only a host-side stand-in; kernels receive the
@@ -54,24 +56,24 @@ extern "C" int sem_q8_gemm_noalloc(sem_q8_weight* w, const float* d_a, int32_t m
   if (!w || !d_a || !d_c) return sem::set_error(SEM_EINVAL, "null argument");
   if (m <= 0) return sem::set_error(SEM_EINVAL, "sem_q8_gemm_noalloc: m must be positive, got %d", m);
   const size_t need = (size_t)m * (size_t)w->k_in;
-  if (need > kNoAllocCodesBytes)
+  if (need > kNoAllocMaxCodes)
     return sem::set_error(SEM_EINVAL,
-                          "sem_q8_gemm_noalloc: %d rows x %d inputs need %zu bytes of scratch, above the static "
-                          "maximum of %zu bytes (at most %zu rows for this weight)",
-                          m, w->k_in, need, kNoAllocCodesBytes, kNoAllocCodesBytes / (size_t)w->k_in);
+                          "sem_q8_gemm_noalloc: %d rows x %d inputs need %zu activation codes of scratch, above the "
+                          "static maximum of %zu (at most %zu rows for this weight)",
+                          m, w->k_in, need, kNoAllocMaxCodes, kNoAllocMaxCodes / (size_t)w->k_in);
   sem::DeviceGuard dg(w->ctx->device);
   uint8_t* scratch = nullptr;
   int rc = scratch_for_device(w->ctx->device, &scratch);
   if (rc) return rc;
   uint32_t* absmax = reinterpret_cast<uint32_t*>(scratch);
-  int8_t* codes = reinterpret_cast<int8_t*>(scratch + kNoAllocHeaderBytes);
+  __half* codes = reinterpret_cast<__half*>(scratch + kNoAllocHeaderBytes);
   cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : w->ctx->stream;
   // The array keeps the previous call's contents: the absmax word must start at zero.
   SEM_CUDA(cudaMemsetAsync(absmax, 0, sizeof(uint32_t), st));
   SEM_CUDA(sem::launch_absmax(d_a, (int64_t)need, absmax, st));
   sem::SeqMeta meta{nullptr, nullptr, nullptr, m, 1};
   SEM_CUDA(sem::launch_quantize(d_a, nullptr, nullptr, w->k_in, meta, absmax, codes, st));
-  SEM_CUDA(sem::launch_gemm_q8(codes, w->codes.as<int8_t>(), w->scales.as<float>(), m, w->n_out, w->k_in, absmax,
-                               nullptr, d_c, sem::kEpiStore, nullptr, st));
+  SEM_CUDA(sem::launch_gemm_q8(codes, w->codes.as<__half>(), w->scales.as<float>(), m, w->n_out, w->k_in, absmax,
+                               nullptr, d_c, sem::kEpiStore, nullptr, nullptr, st));
   return SEM_OK;
 }

@@ -1,221 +1,517 @@
-// Q8_0 weights x INT8 activations (MatMulQ8_0INT8, internal/kernels/quantize.go:346-458).
+// Q8_0 weights x INT8 activations (MatMulQ8_0INT8, internal/kernels/quantize.go:346-458)
+// on the sm_100a tensor cores (tcgen05, accumulators in TMEM).
 //
-// The reference sums int8 products exactly inside each 32-element Q8_0 block
-// and only then applies the block's fp16 scale in float32. One int8 tensor-core
-// MMA with K = 32 (mma.m16n8k32.s8) computes exactly one such block sum, so the
-// int32 block dot products here are bit-identical to the reference's; the
-// float rescale accumulates blocks in order (one accumulator instead of the
-// reference's 8 SIMD lanes, so results agree to float32 rounding).
+// The reference sums the int8 products of each 32-element Q8_0 block exactly
+// and only then applies the block's fp16 scale in float32:
+//   dst[t, j] = inScale * sum_kb float32(sum_{k in kb} a[t, k] * q[j, k]) * d[j, kb].
+// Here both operands hold those integers as fp16 (|a|, |q| <= 127 are exact)
+// and one K = 32 block is two kind::f16 MMAs with an fp32 accumulator: the
+// products and their sums (|sum| < 2^19) are integers below 2^24, so every
+// block sum lands in TMEM exactly. The epilogue warps read each block's sums
+// from TMEM and apply the block scale with packed fp32 FMAs into register
+// accumulators, blocks in ascending order -- the reference's arithmetic up to
+// the float32 order of the block accumulation.
 //
-// The MMA accumulator is seeded with the bit pattern of 1.5*2^23: for block
-// sums |s| < 2^22 the int32 result, read as a float, is exactly 1.5*2^23 + s,
-// so converting to float costs one packed add and the rescale one packed FMA
-// (f32x2 on sm_100). Tiles: 128x128 outputs, 128-byte K stages (4 Q8_0 blocks),
-// 4-stage cp.async pipeline, 8 warps of 64x32.
+// Roles: the weight rows (output channels) are the MMA's M = 128 (TMEM lanes),
+// so each epilogue thread owns one channel and its block scale is a scalar;
+// the tokens are N. Warp 0 issues TMA loads (128-byte swizzled K-major tiles,
+// 4-stage ring of 64-wide K slices), warp 1 issues the MMAs, warps 4-15 drain
+// TMEM: three groups of four warps (one per TMEM lane quarter), each group a
+// third of the tile's tokens, so a thread accumulates 64 values and every
+// block costs it one batch of TMEM loads and one wait. TMEM holds two block
+// buffers: the MMA of block kb+1 overlaps the epilogue of block kb.
+// Results leave through shared-memory staging and asynchronous TMA stores of
+// 16-token boxes, so the next tile's MMAs are not held up by the stores.
+// The gate/up projection (runMLPINT8, model_int8.go:510-538) runs both weight
+// matrices against the same token tile into two TMEM regions; its epilogue
+// forms GELUQuick(gate) * up in shared memory and the per-sequence absmax.
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
 #include "common.cuh"
 #include "kernels.h"
+#include "sm100.cuh"
 
 namespace sem {
 
 namespace {
-constexpr int BM = 128, BN = 128, BK = 128, STAGES = 4, THREADS = 256;
-constexpr int A_BYTES = BM * BK, B_BYTES = BN * BK, S_BYTES = BN * (BK / 32) * 4;
-constexpr int STAGE_BYTES = A_BYTES + B_BYTES + S_BYTES;
-constexpr int SMEM_BYTES = STAGES * STAGE_BYTES;
 
-__device__ __forceinline__ int swz(int r, int c) { return r * BK + ((c ^ (r & 7)) << 4); }
+constexpr int kBM = 128;       // weight rows per tile (TMEM lanes)
+constexpr int kBKS = 64;       // K elements per pipeline stage: two Q8_0 blocks, 128 bytes of fp16
+constexpr int kStages = 4;
+constexpr int kGroups = 3;     // token groups of epilogue warps
+constexpr int kEpiWarps = 4 * kGroups;
+constexpr int kEpiThreads = kEpiWarps * 32;
+// warpgroup 0: TMA warp, MMA warp, two idle warps; warpgroups 1-3: epilogue
+constexpr int kThreads = 128 + kEpiThreads;
+// register split (setmaxnreg): 128 x 56 + 384 x 152 = 512 x 128, the launch's share
+constexpr int kRegsProducer = 56, kRegsEpilogue = 152;
+static_assert(128 * kRegsProducer + kEpiThreads * kRegsEpilogue <= kThreads * 128, "register split");
+constexpr int kATile = kBM * kBKS * 2;      // 16 KB
+constexpr int kSubTok = 16;                 // tokens per output box
+constexpr int kOutBox = kSubTok * kBM * 4;  // 8 KB: one fp32 box of 16 tokens x 128 channels
+constexpr int kBarBytes = 112;              // 13 mbarriers + TMEM address + abort flag, 16-byte padded
 
-__device__ __forceinline__ void mma_s8_biased(int* d, const uint32_t* a, const uint32_t* b) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-      "{%10,%10,%10,%10};\n"
-      : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
-      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]), "r"(kFloatMagicBits));
+template <int NA, int NT>
+struct TileCfg {
+  static constexpr int kTG = NT / kGroups;    // tokens per epilogue group
+  static constexpr int kCPO = kTG / 16;       // TMEM chunks of 16 columns per operand
+  static constexpr int kChunks = NA * kCPO;
+  static constexpr int kPairs = kChunks * 8;  // packed fp32 pairs accumulated per thread
+  static constexpr int kBTile = NT * kBKS * 2;
+  static constexpr int kStage = NA * kATile + kBTile;  // bytes per stage (also the TMA transaction count)
+  static constexpr int kBufCols = NA * NT;             // TMEM columns of one block buffer
+  static constexpr int kTmemCols = 2 * kBufCols <= 256 ? 256 : 512;
+  static constexpr int kOutBytes = kGroups * 2 * kOutBox;  // per group: two boxes (double buffer, or gate + up)
+  static constexpr int kSmem = 1024 + kStages * kStage + kOutBytes + kBarBytes + NT * 16;
+  static_assert(NT % (16 * kGroups) == 0 && kTG % kSubTok == 0, "token tile must split into 16-token boxes");
+  static_assert(2 * kBufCols <= 512, "two block buffers must fit TMEM");
+  static_assert(kChunks <= 4, "register budget: at most 64 accumulators and 64 staging registers per thread");
+  static_assert(kSmem <= 232448, "shared memory per CTA");
+};
+
+__device__ uint32_t g_tc_error;  // error bits of launches given no error word
+
+// TMEM column of chunk c (16 columns) of a group's share of a block buffer:
+// operand c / kCPO, then the group's third of the tokens.
+template <int NA, int NT>
+__device__ __forceinline__ uint32_t chunk_col(int grp, int c) {
+  constexpr int cpo = TileCfg<NA, NT>::kCPO;
+  return (uint32_t)((c / cpo) * NT + grp * TileCfg<NA, NT>::kTG + (c % cpo) * 16);
 }
+
+__device__ __forceinline__ float f4_get(const float4& v, int i) {
+  return i == 0 ? v.x : i == 1 ? v.y : i == 2 ? v.z : v.w;
+}
+
+__device__ __forceinline__ void tmem_wait_ld_regs(uint32_t (&r)[16]) {
+  // Ties the loaded registers to the wait so that no use is scheduled before it.
+  asm volatile("tcgen05.wait::ld.sync.aligned;"
+               : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
+                 "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]),
+                 "+r"(r[15])
+               :
+               : "memory");
+}
+
+// GELUQuick(gate * rs) * (up * rs), kept out of line so that the epilogue's
+// rolled loop stays small.
+__device__ __noinline__ float gelu_up(float g, float u, float rs) {
+  return __fmul_rn(gelu_quick_ref(__fmul_rn(g, rs)), __fmul_rn(u, rs));
+}
+
 }  // namespace
 
-template <int EPI>
-__global__ void __launch_bounds__(THREADS, 1)
-    gemm_q8_kernel(const int8_t* __restrict__ A, const int8_t* __restrict__ W, const float* __restrict__ WS, int M,
-                   int N, int K, const uint32_t* __restrict__ a_absmax, const int32_t* __restrict__ row_seq,
-                   float* __restrict__ C, uint32_t* __restrict__ out_absmax) {
-  extern __shared__ __align__(128) uint8_t smem[];
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int wm0 = (warp >> 2) * 64, wn0 = (warp & 3) * 32;
-  const int m0 = blockIdx.y * BM, n0 = blockIdx.x * BN;
-  const int nkb = K / 32, KT = K / BK;
+// One persistent CTA per SM walks tiles (128 weight rows x NT tokens), tile
+// index = token tile * n_mt + weight tile, so the CTAs working at one time
+// share a few token tiles through L2.
+template <int NA, int NT, int EPI>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_q8_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_a,
+                      const __grid_constant__ CUtensorMap tm_c, const float* __restrict__ ws, int w_rows,
+                      int n_per_a, int T, int K, const uint32_t* __restrict__ a_absmax,
+                      const int32_t* __restrict__ row_seq, uint32_t* __restrict__ out_absmax,
+                      uint32_t* __restrict__ err) {
+  using G = TileCfg<NA, NT>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
+  uint8_t* stages = smem;
+  uint8_t* outbuf = smem + kStages * G::kStage;
+  uint64_t* full = reinterpret_cast<uint64_t*>(outbuf + G::kOutBytes);
+  uint64_t* empty = full + kStages;
+  uint64_t* tfull = empty + kStages;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* drain = tempty + 2;
+  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(s_tmem + 1);
+  float* s_rs = reinterpret_cast<float*>(outbuf + G::kOutBytes + kBarBytes);
+  int* s_seq = reinterpret_cast<int*>(s_rs + 2 * NT);
+  if (!err) err = &g_tc_error;
 
-  auto load_stage = [&](int stage, int kt) {
-    uint8_t* sa = smem + stage * STAGE_BYTES;
-    uint8_t* sb = sa + A_BYTES;
-    float* ss = reinterpret_cast<float*>(sb + B_BYTES);
-    const int k0 = kt * BK;
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      int idx = tid + i * THREADS;  // 0..1023
-      int r = idx >> 3, c = idx & 7;
-      bool va = (m0 + r) < M;
-      const int8_t* ga = A + (int64_t)(va ? m0 + r : 0) * K + k0 + c * 16;
-      cp_async16(sa + swz(r, c), ga, va);
-      const int8_t* gb = W + (int64_t)(n0 + r) * K + k0 + c * 16;
-      cp_async16(sb + swz(r, c), gb, true);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n_mt = n_per_a / kBM;
+  const int total = n_mt * ((T + NT - 1) / NT);
+  const int nks = K / kBKS, nkb = K / 32;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
     }
-    if (tid < BN) {
-      const float* gs = WS + (int64_t)(n0 + tid) * nkb + kt * (BK / 32);
-      cp_async16(ss + tid * 4, gs, true);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], kEpiWarps);
     }
-  };
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) tmem_alloc(s_tmem, G::kTmemCols);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *s_tmem;
+  if (warp < 4) {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kRegsProducer));
+  if (warp == 0) {
+    // ---------------- TMA producer ----------------
+    if (lane == 0) {
+      tma_prefetch_desc(&tm_w);
+      tma_prefetch_desc(&tm_a);
+      uint32_t it = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; ok && tile < total; tile += gridDim.x) {
+        const int tt = tile / n_mt, mt = tile % n_mt;
+        for (int ks = 0; ks < nks; ++ks, ++it) {
+          const uint32_t s = it % kStages, u = it / kStages;
+          if (!mbar_wait(&empty[s], (u & 1) ^ 1, abort_flag, err, 1u)) {
+            ok = false;
+            break;
+          }
+          uint8_t* st = stages + s * G::kStage;
+          mbar_arrive_expect_tx(&full[s], G::kStage);
+#pragma unroll
+          for (int a = 0; a < NA; ++a) tma_load_2d(&tm_w, &full[s], st + a * kATile, ks * kBKS, a * n_per_a + mt * kBM);
+          tma_load_2d(&tm_a, &full[s], st + NA * kATile, ks * kBKS, tt * NT);
+        }
+      }
+      // the copies in flight land before the CTA's shared memory is released
+      for (uint32_t j = it > (uint32_t)kStages ? it - kStages : 0; j < it; ++j)
+        mbar_wait_drain(&full[j % kStages], (j / kStages) & 1);
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
+      constexpr uint32_t idesc = umma_idesc_f16_f32(kBM, NT);
+      uint32_t it = 0, blk = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; ok && tile < total; tile += gridDim.x) {
+        for (int ks = 0; ks < nks; ++ks, ++it) {
+          const uint32_t s = it % kStages, u = it / kStages;
+          if (!mbar_wait(&full[s], u & 1, abort_flag, err, 2u)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sa = smem_u32(stages + s * G::kStage);
+          for (int h = 0; h < 2 && ok; ++h, ++blk) {
+            const uint32_t b = blk & 1, ub = blk >> 1;
+            if (!mbar_wait(&tempty[b], (ub & 1) ^ 1, abort_flag, err, 2u)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+#pragma unroll
+            for (int a = 0; a < NA; ++a)
+#pragma unroll
+              for (int kk = 0; kk < 2; ++kk) {
+                const uint32_t koff = (uint32_t)(h * 2 + kk) * 32;
+                umma_f16(tmem_base + b * G::kBufCols + a * NT, umma_desc_k_sw128(sa + a * kATile + koff),
+                         umma_desc_k_sw128(sa + NA * kATile + koff), idesc, (uint32_t)kk);
+              }
+            umma_commit(&tfull[b]);
+          }
+          if (!ok) break;
+          umma_commit(&empty[s]);
+        }
+      }
+      umma_commit(drain);  // every MMA has finished writing TMEM before it is freed
+      mbar_wait_drain(drain, 0);
+    }
+  }
+  } else {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kRegsEpilogue));
+    // ---------------- epilogue: TMEM -> scaled fp32 accumulators -> output ----------------
+    constexpr int CH = G::kChunks, NP = G::kPairs, NPA = NP / NA, TG = G::kTG;
+    const int e = warp - 4;
+    const int q = warp & 3;      // the TMEM lane quarter this warp may access
+    const int grp = e >> 2;      // which third of the tile's tokens
+    const int etid = e * 32 + lane;
+    const int ch = q * 32 + lane;  // channel within the tile
+    const bool leader = (e & 3) == 0 && lane == 0;  // issues the group's TMA stores
+    float* gbox = reinterpret_cast<float*>(outbuf + grp * 2 * kOutBox);  // two [16][128] fp32 boxes
+    const uint32_t t_lane = tmem_base + ((uint32_t)(q * 32) << 16);
+    uint32_t blk = 0;
+    int nstore = 0;  // stores issued by this group (double-buffer index)
+    bool ok = true;  // after an abort every warp still walks the same named barriers
+    // per-token activation scale and sequence of a tile, double-buffered: the
+    // next tile's entries are loaded while this tile accumulates
+    auto tile_token = [&](int tile_idx) { return (tile_idx / n_mt) * NT + etid; };
+    auto seq_of = [&](int t) { return t < T ? (row_seq ? row_seq[t] : 0) : -1; };
+    if (etid < NT && (int)blockIdx.x < total) {
+      const int sq = seq_of(tile_token(blockIdx.x));
+      float rs = 0.0f, inv;
+      if (sq >= 0) seq_scale_ref(a_absmax[sq], &rs, &inv);
+      s_rs[etid] = rs;
+      s_seq[etid] = sq;
+    }
+    // block scales of this thread's weight row(s), row-major [row][K/32]: one
+    // 16-byte load covers four blocks and is issued a group of four ahead
+    auto scale_rows = [&](int mt_, int a) {
+      return reinterpret_cast<const float4*>(ws + (size_t)(a * n_per_a + mt_ * kBM + ch) * nkb);
+    };
+    float4 sa_nxt = make_float4(0.f, 0.f, 0.f, 0.f), sb_nxt = sa_nxt;
+    int tix = 0;
+    for (int tile = blockIdx.x; tile < total; tile += gridDim.x, ++tix) {
+      const int tt = tile / n_mt, mt = tile % n_mt;
+      const int t0 = tt * NT;
+      const int cur = tix & 1;
+      // this tile's scales are complete; the previous tile's output is done with the other buffer
+      named_bar_sync(1, kEpiThreads);
+      const float* c_rs = s_rs + cur * NT;
+      const int* c_seq = s_seq + cur * NT;
+      const int nxt_tile = tile + gridDim.x;
+      int nsq = -1;
+      uint32_t nrs_bits = 0;
+      if (etid < NT && nxt_tile < total) nsq = seq_of(tile_token(nxt_tile));
 
-  uint64_t acc[4][4][2];
+      uint64_t acc[NP];
 #pragma unroll
-  for (int mt = 0; mt < 4; ++mt)
+      for (int i = 0; i < NP; ++i) acc[i] = 0;
+      const float4* wsa = scale_rows(mt, 0);
+      const float4* wsb = scale_rows(mt, 1);
+      if (tix == 0) {
+        sa_nxt = wsa[0];
+        if (NA == 2) sb_nxt = wsb[0];
+      }
+      for (int kg = 0; kg < nkb / 4; ++kg) {
+        const float4 sa_cur = sa_nxt, sb_cur = sb_nxt;
+        if (kg + 1 < nkb / 4) {
+          sa_nxt = wsa[kg + 1];
+          if (NA == 2) sb_nxt = wsb[kg + 1];
+        } else if (nxt_tile < total) {  // the next tile's first group
+          sa_nxt = scale_rows(nxt_tile % n_mt, 0)[0];
+          if (NA == 2) sb_nxt = scale_rows(nxt_tile % n_mt, 1)[0];
+        }
+        if (kg == 1) {  // the next tile's activation scales: second, dependent load
+          nrs_bits = nsq >= 0 ? a_absmax[nsq] : 0u;
+        }
 #pragma unroll
-    for (int nt = 0; nt < 4; ++nt) acc[mt][nt][0] = acc[mt][nt][1] = 0;
-  const uint64_t neg_magic = pack2(-kFloatMagic, -kFloatMagic);
+        for (int u = 0; u < 4; ++u, ++blk) {
+        const uint32_t b = blk & 1, ub = blk >> 1;
+        if (ok) ok = mbar_wait(&tfull[b], ub & 1, abort_flag, err, 4u);
+        ok = __all_sync(0xffffffffu, ok);  // converged (and agreed) before the .sync.aligned TMEM loads
+        if (ok) {
+          tc_fence_after();
+          const uint32_t tb = t_lane + b * G::kBufCols;
+          const float da = f4_get(sa_cur, u), db = f4_get(sb_cur, u);
+          const uint64_t dd0 = pack2(da, da), dd1 = pack2(db, db);
+          // two chunks per TMEM wait; the buffer goes back to the MMA after the last wait
+#pragma unroll
+          for (int hh = 0; hh < CH / 2; ++hh) {
+            uint32_t r[2][16];
+            tmem_ld16(tb + chunk_col<NA, NT>(grp, 2 * hh), r[0]);
+            tmem_ld16(tb + chunk_col<NA, NT>(grp, 2 * hh + 1), r[1]);
+            tmem_wait_ld_regs(r[0]);
+            reg_barrier16(r[1]);
+            if (hh == CH / 2 - 1) {
+              tc_fence_before();
+              __syncwarp();
+              if (lane == 0) mbar_arrive(&tempty[b]);
+            }
+#pragma unroll
+            for (int cc = 0; cc < 2; ++cc) {
+              const int c = 2 * hh + cc;
+              const uint64_t dd = (c / G::kCPO) ? dd1 : dd0;
+#pragma unroll
+              for (int i = 0; i < 8; ++i)
+                acc[c * 8 + i] = fma2(pack2u(r[cc][2 * i], r[cc][2 * i + 1]), dd, acc[c * 8 + i]);
+            }
+          }
+        }
+        }
+      }
 
+      if (etid < NT && nxt_tile < total) {
+        float rs = 0.0f, inv;
+        if (nsq >= 0) {
+          if (nkb < 8) nrs_bits = a_absmax[nsq];  // no second group: the dependent load was not issued
+          seq_scale_ref(nrs_bits, &rs, &inv);
+        }
+        s_rs[(cur ^ 1) * NT + etid] = rs;
+        s_seq[(cur ^ 1) * NT + etid] = nsq;
+      }
+
+      // ---- output: 16-token boxes through shared memory and TMA stores ----
+      const int tg0 = grp * TG;  // first token of this group within the tile
 #pragma unroll
-  for (int s = 0; s < STAGES - 1; ++s) {
-    if (s < KT) load_stage(s, s);
-    cp_async_commit();
+      for (int sbx = 0; sbx < TG / kSubTok; ++sbx) {
+        const int box = NA == 1 ? (nstore & 1) : 0;
+        float* out = gbox + box * (kSubTok * kBM);
+        // the store that last read this box has finished reading it
+        if (leader) {
+          if (NA == 1) bulk_wait_read<1>();
+          else bulk_wait_read<0>();
+        }
+        named_bar_sync(2 + grp, 128);
+        if (EPI == kEpiStore) {
+          // dst = sum * inputScale (quantize.go:453)
+#pragma unroll
+          for (int p = 0; p < kSubTok / 2; ++p) {
+            float v0, v1;
+            unpack2(acc[sbx * (kSubTok / 2) + p], v0, v1);
+            const int i = tg0 + sbx * kSubTok + 2 * p;
+            out[(2 * p) * kBM + ch] = __fmul_rn(v0, c_rs[i]);
+            out[(2 * p + 1) * kBM + ch] = __fmul_rn(v1, c_rs[i + 1]);
+          }
+        } else {
+          // runMLPINT8 (model_int8.go:523-530): gate and up scaled, GELUQuick(gate) * up,
+          // and the absmax of each sequence's rows for the next quantisation.
+          // gate goes to box 0, up to box 1; h overwrites gate (each thread its own column).
+          float* ubox = gbox + kSubTok * kBM;
+#pragma unroll
+          for (int p = 0; p < kSubTok / 2; ++p) {
+            float g0, g1, u0, u1;
+            unpack2(acc[sbx * (kSubTok / 2) + p], g0, g1);
+            unpack2(acc[NPA + sbx * (kSubTok / 2) + p], u0, u1);
+            out[(2 * p) * kBM + ch] = g0;
+            out[(2 * p + 1) * kBM + ch] = g1;
+            ubox[(2 * p) * kBM + ch] = u0;
+            ubox[(2 * p + 1) * kBM + ch] = u1;
+          }
+          int cur = -1;
+          float run = 0.0f;
+#pragma unroll 1
+          for (int x = 0; x < kSubTok; ++x) {
+            const int i = tg0 + sbx * kSubTok + x;
+            const int sq = c_seq[i];  // the same for every lane: warp-uniform branches
+            if (sq != cur) {
+              if (cur >= 0 && out_absmax) {
+                const float m = warp_max(run);
+                if (lane == 0) atomicMax(&out_absmax[cur], __float_as_uint(m));
+              }
+              cur = sq;
+              run = 0.0f;
+            }
+            const float h = gelu_up(out[x * kBM + ch], ubox[x * kBM + ch], c_rs[i]);
+            out[x * kBM + ch] = h;
+            if (sq >= 0) run = fmaxf(run, fabsf(h));
+          }
+          if (cur >= 0 && out_absmax) {
+            const float m = warp_max(run);
+            if (lane == 0) atomicMax(&out_absmax[cur], __float_as_uint(m));
+          }
+        }
+        fence_proxy_async_smem();
+        named_bar_sync(2 + grp, 128);
+        if (leader) {
+          tma_store_2d(&tm_c, out, mt * kBM, t0 + tg0 + sbx * kSubTok);
+          bulk_commit();
+        }
+        ++nstore;
+      }
+    }
+    if (leader) bulk_wait_all();
   }
 
-  for (int kt = 0; kt < KT; ++kt) {
-    cp_async_wait<STAGES - 2>();
-    __syncthreads();
-    {
-      int nk = kt + STAGES - 1;
-      if (nk < KT) load_stage(nk % STAGES, nk);
-      cp_async_commit();
-    }
-    const int stage = kt % STAGES;
-    const uint8_t* sa = smem + stage * STAGE_BYTES;
-    const uint8_t* sb = sa + A_BYTES;
-    const float* ss = reinterpret_cast<const float*>(sb + B_BYTES);
-#pragma unroll
-    for (int kb = 0; kb < BK / 32; ++kb) {
-      const int c0 = kb * 2;
-      uint32_t a[4][4], b[4][2];
-#pragma unroll
-      for (int mt = 0; mt < 4; ++mt) {
-        int r = wm0 + mt * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
-        int c = c0 + (lane >> 4);
-        ldmatrix_x4(a[mt][0], a[mt][1], a[mt][2], a[mt][3], sa + swz(r, c));
-      }
-#pragma unroll
-      for (int p = 0; p < 2; ++p) {
-        int r = wn0 + p * 16 + (lane & 7) + (lane >> 4) * 8;
-        int c = c0 + ((lane >> 3) & 1);
-        ldmatrix_x4(b[2 * p][0], b[2 * p][1], b[2 * p + 1][0], b[2 * p + 1][1], sb + swz(r, c));
-      }
-      uint64_t sc[4];
-#pragma unroll
-      for (int nt = 0; nt < 4; ++nt) {
-        int col = wn0 + nt * 8 + (lane & 3) * 2;
-        sc[nt] = pack2(ss[col * 4 + kb], ss[(col + 1) * 4 + kb]);
-      }
-#pragma unroll
-      for (int mt = 0; mt < 4; ++mt)
-#pragma unroll
-        for (int nt = 0; nt < 4; ++nt) {
-          int d[4];
-          mma_s8_biased(d, a[mt], b[nt]);
-          uint64_t f01 = add2(pack2(__int_as_float(d[0]), __int_as_float(d[1])), neg_magic);
-          uint64_t f23 = add2(pack2(__int_as_float(d[2]), __int_as_float(d[3])), neg_magic);
-          acc[mt][nt][0] = fma2(f01, sc[nt], acc[mt][nt][0]);
-          acc[mt][nt][1] = fma2(f23, sc[nt], acc[mt][nt][1]);
-        }
-    }
-  }
-  cp_async_wait<0>();
-  __syncthreads();  // the pipeline buffers are reused below for the row maxima
-  float* s_rowmax = reinterpret_cast<float*>(smem);  // [BM][4 column groups]
-
-  // ---- epilogue: dst = sum * inputScale (quantize.go:453) ----
-  const int g = lane >> 2, t4 = lane & 3;
-#pragma unroll
-  for (int mt = 0; mt < 4; ++mt)
-#pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      const int row = m0 + wm0 + mt * 16 + g + h * 8;
-      const bool valid = row < M;
-      float rs = 0.0f;
-      if (valid) {
-        float inv;
-        seq_scale_ref(a_absmax[row_seq ? row_seq[row] : 0], &rs, &inv);
-      }
-      if (EPI == kEpiStore) {
-#pragma unroll
-        for (int nt = 0; nt < 4; ++nt) {
-          float v0, v1;
-          unpack2(acc[mt][nt][h], v0, v1);
-          const int col = n0 + wn0 + nt * 8 + t4 * 2;
-          if (valid)
-            *reinterpret_cast<float2*>(C + (int64_t)row * N + col) = make_float2(__fmul_rn(v0, rs), __fmul_rn(v1, rs));
-        }
-      } else {
-        // runMLPINT8 (model_int8.go:523-530): gate and up scaled, GELUQuick(gate) * up
-        float mm = 0.0f;
-#pragma unroll
-        for (int p = 0; p < 2; ++p) {
-          float g0, g1, u0, u1;
-          unpack2(acc[mt][2 * p][h], g0, g1);
-          unpack2(acc[mt][2 * p + 1][h], u0, u1);
-          const float h0 = __fmul_rn(gelu_quick_ref(__fmul_rn(g0, rs)), __fmul_rn(u0, rs));
-          const float h1 = __fmul_rn(gelu_quick_ref(__fmul_rn(g1, rs)), __fmul_rn(u1, rs));
-          const int ch = ((n0 + wn0) >> 1) + p * 8 + t4 * 2;
-          if (valid) *reinterpret_cast<float2*>(C + (int64_t)row * (N / 2) + ch) = make_float2(h0, h1);
-          mm = fmaxf(mm, fmaxf(fabsf(h0), fabsf(h1)));
-        }
-        // per-row max over the 4 lanes of the quad (all lanes participate)
-        mm = fmaxf(mm, __shfl_xor_sync(0xffffffffu, mm, 1));
-        mm = fmaxf(mm, __shfl_xor_sync(0xffffffffu, mm, 2));
-        if (t4 == 0) s_rowmax[(wm0 + mt * 16 + g + h * 8) * 4 + (warp & 3)] = valid ? mm : 0.0f;
-      }
-    }
-  if (EPI == kEpiGeluUp && out_absmax) {
-    // One atomic per CTA when the tile's rows share a sequence (the usual
-    // case); per-row atomics only on tiles that straddle sequences.
-    __syncthreads();
-    const int last = min(m0 + BM, M) - 1;
-    const int seq0 = row_seq ? row_seq[m0] : 0;
-    const bool uniform = !row_seq || row_seq[last] == seq0;
-    float rmax = 0.0f;
-    const int r = tid;
-    if (r < BM) {
-      rmax = fmaxf(fmaxf(s_rowmax[r * 4], s_rowmax[r * 4 + 1]), fmaxf(s_rowmax[r * 4 + 2], s_rowmax[r * 4 + 3]));
-      if (!uniform && m0 + r < M) atomicMax(&out_absmax[row_seq[m0 + r]], __float_as_uint(rmax));
-    }
-    if (uniform) {
-      rmax = warp_max(rmax);
-      __syncthreads();
-      if (lane == 0) s_rowmax[warp] = rmax;
-      __syncthreads();
-      if (tid == 0) {
-        float m = s_rowmax[0];
-        for (int w = 1; w < THREADS / 32; ++w) m = fmaxf(m, s_rowmax[w]);
-        atomicMax(&out_absmax[seq0], __float_as_uint(m));
-      }
-    }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem_base, G::kTmemCols);
   }
 }
 
-cudaError_t launch_gemm_q8(const int8_t* a_codes, const int8_t* w_codes, const float* w_scales, int M, int N, int K,
-                           const uint32_t* a_absmax, const int32_t* row_seq, float* c, int epilogue,
-                           uint32_t* out_absmax, cudaStream_t stream) {
-  if (M == 0) return cudaSuccess;
-  if (N % BN != 0 || K % BK != 0) return cudaErrorInvalidValue;
-  dim3 grid(N / BN, (M + BM - 1) / BM);
-  // the attribute is per device context: set it on every launch (cheap host call)
-  if (epilogue == kEpiStore) {
-    cudaFuncSetAttribute(gemm_q8_kernel<kEpiStore>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
-    gemm_q8_kernel<kEpiStore><<<grid, THREADS, SMEM_BYTES, stream>>>(a_codes, w_codes, w_scales, M, N, K, a_absmax,
-                                                                     row_seq, c, out_absmax);
-  } else {
-    cudaFuncSetAttribute(gemm_q8_kernel<kEpiGeluUp>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
-    gemm_q8_kernel<kEpiGeluUp><<<grid, THREADS, SMEM_BYTES, stream>>>(a_codes, w_codes, w_scales, M, N, K, a_absmax,
-                                                                      row_seq, c, out_absmax);
+namespace {
+
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+// Row-major [rows][cols] 2-D map with a box of box_cols x box_rows.
+cudaError_t encode_2d(CUtensorMap* map, CUtensorMapDataType dtype, int esize, const void* base, int64_t rows,
+                      int64_t cols, int box_cols, int box_rows, CUtensorMapSwizzle swz) {
+  auto enc = tensor_map_encoder();
+  if (!enc) return cudaErrorNotSupported;
+  if ((reinterpret_cast<uintptr_t>(base) & 15) || (cols * esize) % 16) return cudaErrorMisalignedAddress;
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)(cols * esize)};
+  cuuint32_t box[2] = {(cuuint32_t)box_cols, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(map, dtype, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+}
+
+// Per device: SM count and whether each kernel's shared-memory limit was raised.
+struct DevState {
+  int sms = 0;
+  bool attr[4] = {false, false, false, false};
+};
+DevState g_dev[64];
+std::mutex g_dev_mu;
+
+template <int NA, int NT, int EPI>
+cudaError_t launch_tc(int slot, const __half* a_codes, int T, int K, const __half* w_codes, const float* ws,
+                      int w_rows, const uint32_t* a_absmax, const int32_t* row_seq, float* c, uint32_t* out_absmax,
+                      uint32_t* err, cudaStream_t stream) {
+  using G = TileCfg<NA, NT>;
+  auto kern = gemm_q8_tc_kernel<NA, NT, EPI>;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  int sms;
+  {
+    std::lock_guard<std::mutex> lk(g_dev_mu);
+    DevState& ds = g_dev[dev];
+    if (!ds.sms && (e = cudaDeviceGetAttribute(&ds.sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess)
+      return e;
+    if (!ds.attr[slot]) {
+      if ((e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, G::kSmem)) != cudaSuccess)
+        return e;
+      ds.attr[slot] = true;
+    }
+    sms = ds.sms;
   }
+  const int n_per_a = w_rows / NA;
+  CUtensorMap tm_w, tm_a, tm_c;
+  if ((e = encode_2d(&tm_w, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, w_codes, w_rows, K, kBKS, kBM,
+                     CU_TENSOR_MAP_SWIZZLE_128B)) != cudaSuccess)
+    return e;
+  if ((e = encode_2d(&tm_a, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, a_codes, T, K, kBKS, NT,
+                     CU_TENSOR_MAP_SWIZZLE_128B)) != cudaSuccess)
+    return e;
+  if ((e = encode_2d(&tm_c, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, c, T, n_per_a, kBM, kSubTok,
+                     CU_TENSOR_MAP_SWIZZLE_NONE)) != cudaSuccess)
+    return e;
+  const int total = (n_per_a / kBM) * ((T + NT - 1) / NT);
+  const int grid = total < sms ? total : sms;
+  kern<<<grid, kThreads, G::kSmem, stream>>>(tm_w, tm_a, tm_c, ws, w_rows, n_per_a, T, K, a_absmax, row_seq,
+                                             out_absmax, err);
   return cudaGetLastError();
+}
+
+}  // namespace
+
+cudaError_t launch_gemm_q8(const __half* a_codes, const __half* w_codes, const float* w_scales, int M, int N, int K,
+                           const uint32_t* a_absmax, const int32_t* row_seq, float* c, int epilogue,
+                           uint32_t* out_absmax, uint32_t* err, cudaStream_t stream) {
+  if (M == 0) return cudaSuccess;
+  if (M < 0 || K <= 0 || K % 128 != 0) return cudaErrorInvalidValue;  // four Q8_0 blocks per scale load
+  if (epilogue == kEpiGeluUp) {
+    if (N % (2 * kBM) != 0) return cudaErrorInvalidValue;
+    return launch_tc<2, 96, kEpiGeluUp>(0, a_codes, M, K, w_codes, w_scales, N, a_absmax, row_seq, c, out_absmax,
+                                        err, stream);
+  }
+  if (N % kBM != 0) return cudaErrorInvalidValue;
+  // small batches: narrower token tiles keep more SMs busy
+  if ((N / kBM) * ((M + 191) / 192) < 148)
+    return launch_tc<1, 96, kEpiStore>(1, a_codes, M, K, w_codes, w_scales, N, a_absmax, row_seq, c, nullptr, err,
+                                       stream);
+  return launch_tc<1, 192, kEpiStore>(2, a_codes, M, K, w_codes, w_scales, N, a_absmax, row_seq, c, nullptr, err,
+                                      stream);
 }
 
 }  // namespace sem

@@ -96,8 +96,8 @@ struct sem_context {
   sem::HostBuf pinned;
 };
 
-// A Q8_0 weight repacked for the device: int8 plane [n_out][k_in] and fp32
-// block scales [n_out][k_in/32].
+// A Q8_0 weight repacked for the device: fp16 codes [n_out][k_in] (exact
+// integers) and fp32 block scales [n_out][k_in/32].
 struct sem_q8_weight {
   sem_context* ctx = nullptr;
   int32_t k_in = 0, n_out = 0;

@@ -29,7 +29,8 @@ int set_error(int code, const char* fmt, ...) {
 const char* last_error() { return g_error.c_str(); }
 
 struct LayerW {
-  int8_t *qkv, *o, *gu, *down;
+  __half *qkv, *o, *gu, *down;  // fp16 codes [rows][K]; gu = gate rows then up rows
+  // block scales [rows][K/32]
   float *qkv_s, *o_s, *gu_s, *down_s;
   float *attn_norm, *q_norm, *k_norm, *post_attn, *ffn_norm, *post_ffw;
 };
@@ -90,6 +91,20 @@ int upload_q8(sem_context* ctx, DevBuf& staging, const sem_tensor_view* t, int64
   return SEM_OK;
 }
 
+// Same for a projection weight: fp16 codes and fp32 block scales at rows
+// [row_off, row_off + rows) (the tensor-core GEMM's layout).
+int upload_q8_proj(sem_context* ctx, DevBuf& staging, const sem_tensor_view* t, int64_t rows, int cols, __half* codes,
+                   float* scales, int64_t row_off) {
+  uint64_t need = (uint64_t)rows * (cols / 32) * 34;
+  if (t->nbytes < need) return set_error(SEM_EFORMAT, "tensor %s: %llu bytes, need %llu", t->name,
+                                         (unsigned long long)t->nbytes, (unsigned long long)need);
+  SEM_CUDA(staging.ensure(need));
+  SEM_CUDA(cudaMemcpyAsync(staging.p, t->data, need, cudaMemcpyHostToDevice, ctx->stream));
+  SEM_CUDA(launch_repack_q8_0_f16(staging.as<uint8_t>(), rows, cols, codes, scales, row_off, ctx->stream));
+  SEM_CUDA(cudaStreamSynchronize(ctx->stream));
+  return SEM_OK;
+}
+
 int check_q8(const sem_tensor_view* t, const char* name, uint64_t k, uint64_t n) {
   if (!t) return set_error(SEM_ENOTFOUND, "tensor not found: %s", name);
   if (t->dtype != kQ8) return set_error(SEM_EFORMAT, "expected Q8_0, got dtype %u for %s", t->dtype, name);
@@ -110,11 +125,11 @@ int model_load(sem_context* ctx, const sem_model_config* cfg_in, const sem_tenso
   const sem_model_config c = *cfg_in;
   const int H = c.embed_dim, F = c.interm_dim, L = c.num_layers, nh = c.num_heads, hd = c.head_dim;
   // shapes the sm_100a kernels are built for (EmbeddingGemma-300M and its variants)
-  if (hd != 256 || c.num_kv_heads != 1 || nh < 1 || nh > 3 || H != nh * hd || H % 128 || F % 64 || L < 1 ||
+  if (hd != 256 || c.num_kv_heads != 1 || nh < 1 || nh > 3 || H != nh * hd || H % 128 || F % 128 || L < 1 ||
       c.vocab_size < 1 || c.max_seq_len < 1)
     return set_error(SEM_EINVAL,
                      "unsupported model shape: embed_dim=%d heads=%d kv_heads=%d head_dim=%d ffn=%d (need head_dim 256, "
-                     "1 KV head, <=3 query heads, embed_dim%%128==0, ffn%%64==0)",
+                     "1 KV head, <=3 query heads, embed_dim%%128==0, ffn%%128==0)",
                      H, nh, c.num_kv_heads, hd, F);
   DeviceGuard dg(ctx->device);
   std::lock_guard<std::mutex> lk(ctx->mu);
@@ -135,10 +150,10 @@ int model_load(sem_context* ctx, const sem_model_config* cfg_in, const sem_tenso
   struct LOff { size_t qkv, o, gu, down, qkv_s, o_s, gu_s, down_s, an, qn, kn, pa, fn, pf; };
   std::vector<LOff> lo(L);
   for (int l = 0; l < L; ++l) {
-    lo[l].qkv = take((size_t)qkvN * H);
-    lo[l].o = take((size_t)H * H);
-    lo[l].gu = take((size_t)2 * F * H);
-    lo[l].down = take((size_t)H * F);
+    lo[l].qkv = take((size_t)qkvN * H * 2);
+    lo[l].o = take((size_t)H * H * 2);
+    lo[l].gu = take((size_t)2 * F * H * 2);
+    lo[l].down = take((size_t)H * F * 2);
     lo[l].qkv_s = take((size_t)qkvN * (H / 32) * 4);
     lo[l].o_s = take((size_t)H * (H / 32) * 4);
     lo[l].gu_s = take((size_t)2 * F * (H / 32) * 4);
@@ -188,28 +203,29 @@ int model_load(sem_context* ctx, const sem_model_config* cfg_in, const sem_tenso
     if ((rc = up_f32(P("attn_k_norm.weight"), lo[l].kn, hd, false, &w.k_norm))) return rc;
     if ((rc = up_f32(P("post_attention_norm.weight"), lo[l].pa, H, false, &w.post_attn))) return rc;
     if ((rc = up_f32(P("post_ffw_norm.weight"), lo[l].pf, H, false, &w.post_ffw))) return rc;
-    w.qkv = reinterpret_cast<int8_t*>(base + lo[l].qkv);
-    w.o = reinterpret_cast<int8_t*>(base + lo[l].o);
-    w.gu = reinterpret_cast<int8_t*>(base + lo[l].gu);
-    w.down = reinterpret_cast<int8_t*>(base + lo[l].down);
+    w.qkv = reinterpret_cast<__half*>(base + lo[l].qkv);
+    w.o = reinterpret_cast<__half*>(base + lo[l].o);
+    w.gu = reinterpret_cast<__half*>(base + lo[l].gu);
+    w.down = reinterpret_cast<__half*>(base + lo[l].down);
     w.qkv_s = reinterpret_cast<float*>(base + lo[l].qkv_s);
     w.o_s = reinterpret_cast<float*>(base + lo[l].o_s);
     w.gu_s = reinterpret_cast<float*>(base + lo[l].gu_s);
     w.down_s = reinterpret_cast<float*>(base + lo[l].down_s);
-    struct { const char* n; uint64_t k, rows; int8_t* c; float* s; int64_t roff; int il, part; } q8[] = {
-        {"attn_q.weight", (uint64_t)H, (uint64_t)nh * hd, w.qkv, w.qkv_s, 0, 0, 0},
-        {"attn_k.weight", (uint64_t)H, (uint64_t)hd, w.qkv, w.qkv_s, (int64_t)nh * hd, 0, 0},
-        {"attn_v.weight", (uint64_t)H, (uint64_t)hd, w.qkv, w.qkv_s, (int64_t)nh * hd + hd, 0, 0},
-        {"attn_output.weight", (uint64_t)H, (uint64_t)H, w.o, w.o_s, 0, 0, 0},
-        {"ffn_gate.weight", (uint64_t)H, (uint64_t)F, w.gu, w.gu_s, 0, 8, 0},
-        {"ffn_up.weight", (uint64_t)H, (uint64_t)F, w.gu, w.gu_s, 0, 8, 1},
-        {"ffn_down.weight", (uint64_t)F, (uint64_t)H, w.down, w.down_s, 0, 0, 0},
+    // Q|K|V fused into one [qkvN][H] matrix, gate rows then up rows in [2F][H]
+    struct { const char* n; uint64_t k, rows; __half* c; float* s; int64_t roff; } q8[] = {
+        {"attn_q.weight", (uint64_t)H, (uint64_t)nh * hd, w.qkv, w.qkv_s, 0},
+        {"attn_k.weight", (uint64_t)H, (uint64_t)hd, w.qkv, w.qkv_s, (int64_t)nh * hd},
+        {"attn_v.weight", (uint64_t)H, (uint64_t)hd, w.qkv, w.qkv_s, (int64_t)nh * hd + hd},
+        {"attn_output.weight", (uint64_t)H, (uint64_t)H, w.o, w.o_s, 0},
+        {"ffn_gate.weight", (uint64_t)H, (uint64_t)F, w.gu, w.gu_s, 0},
+        {"ffn_up.weight", (uint64_t)H, (uint64_t)F, w.gu, w.gu_s, F},
+        {"ffn_down.weight", (uint64_t)F, (uint64_t)H, w.down, w.down_s, 0},
     };
     for (auto& q : q8) {
       const char* name = P(q.n);
       const sem_tensor_view* t = find_view(tv, nt, name);
       if ((rc = check_q8(t, name, q.k, q.rows))) return rc;
-      if ((rc = upload_q8(ctx, staging, t, (int64_t)q.rows, (int)q.k, q.c, q.s, q.roff, q.il, q.part, false))) return rc;
+      if ((rc = upload_q8_proj(ctx, staging, t, (int64_t)q.rows, (int)q.k, q.c, q.s, q.roff))) return rc;
     }
   }
   // ---- RoPE tables (rope_cache.go:15-44) ----
@@ -244,7 +260,7 @@ int ensure_workspace(sem_model* m, int64_t T, int B, int64_t out_floats) {
   SEM_CUDA(m->hid.ensure((size_t)Tp * H * 4));
   SEM_CUDA(m->big.ensure((size_t)Tp * (qkvN > F ? qkvN : F) * 4));
   SEM_CUDA(m->att.ensure((size_t)Tp * H * 4));
-  SEM_CUDA(m->codes.ensure((size_t)Tp * (F > H ? F : H)));
+  SEM_CUDA(m->codes.ensure((size_t)Tp * (F > H ? F : H) * 2));
   SEM_CUDA(m->halves.ensure((size_t)Tp * (2 * nh * hd + 4 * hd) * 2));
   SEM_CUDA(m->inv_rms.ensure((size_t)Tp * 4));
   // meta: row_seq[T], row_pos[T], cu[B+1], tile_seq/tile_row0[2*(T/64+B)], out_dims[B], out_off (int64) [B]
@@ -358,7 +374,8 @@ int run_forward(sem_model* m, const int32_t* d_ids, const MetaPtrs& mp, float* d
   float* hid = m->hid.as<float>();
   float* big = m->big.as<float>();
   float* att = m->att.as<float>();
-  int8_t* codes = m->codes.as<int8_t>();
+  __half* codes = m->codes.as<__half>();
+  uint32_t* err = m->errflag.as<uint32_t>() + 1;
   float* inv = m->inv_rms.as<float>();
   uint32_t* amax = m->absmax.as<uint32_t>();
   __half* hb = m->halves.as<__half>();
@@ -366,25 +383,26 @@ int run_forward(sem_model* m, const int32_t* d_ids, const MetaPtrs& mp, float* d
          *vl = vh + T * hd;
   auto slot = [&](int l, int k) { return amax + (size_t)(4 * l + k) * B; };
   SEM_LAUNCH(kStEmbed, cudaMemsetAsync(amax, 0, (size_t)(4 * L + 1) * B * 4, st));
+  SEM_LAUNCH(kStEmbed, cudaMemsetAsync(m->errflag.p, 0, 8, st));
   SEM_LAUNCH(kStEmbed, launch_embed(d_ids, m->emb, m->emb_s, c.vocab_size, H, hid, (int)T, m->errflag.as<uint32_t>(), st));
   SEM_LAUNCH(kStRowStats, launch_row_stats(hid, m->layers[0].attn_norm, H, c.norm_eps, sm, inv, slot(0, 0), st));
   for (int l = 0; l < L; ++l) {
     const LayerW& w = m->layers[l];
     // attention block (model_int8.go:191-210)
     SEM_LAUNCH(kStQuant, launch_quantize(hid, inv, w.attn_norm, H, sm, slot(l, 0), codes, st));
-    SEM_LAUNCH(kStGemmQKV, launch_gemm_q8(codes, w.qkv, w.qkv_s, (int)T, qkvN, H, slot(l, 0), sm.row_seq, big, kEpiStore, nullptr, st));
+    SEM_LAUNCH(kStGemmQKV, launch_gemm_q8(codes, w.qkv, w.qkv_s, (int)T, qkvN, H, slot(l, 0), sm.row_seq, big, kEpiStore, nullptr, err, st));
     SEM_LAUNCH(kStQKNormRope, launch_qk_norm_rope(big, w.q_norm, w.k_norm, m->rope_cos, m->rope_sin, c.norm_eps, nh, sm, qh, ql, kh, kl,
                                    vh, vl, st));
     SEM_LAUNCH(kStAttention, launch_attention(qh, ql, kh, kl, vh, vl, nh, c.attention_scale, sm, mp.tiles, att, slot(l, 1), st));
     SEM_LAUNCH(kStQuant, launch_quantize(att, nullptr, nullptr, H, sm, slot(l, 1), codes, st));
-    SEM_LAUNCH(kStGemmO, launch_gemm_q8(codes, w.o, w.o_s, (int)T, H, H, slot(l, 1), sm.row_seq, big, kEpiStore, nullptr, st));
+    SEM_LAUNCH(kStGemmO, launch_gemm_q8(codes, w.o, w.o_s, (int)T, H, H, slot(l, 1), sm.row_seq, big, kEpiStore, nullptr, err, st));
     SEM_LAUNCH(kStResidual, launch_residual_norm(big, w.post_attn, hid, w.ffn_norm, H, c.norm_eps, sm, inv, slot(l, 2), st));
     // MLP block (model_int8.go:213-232)
     SEM_LAUNCH(kStQuant, launch_quantize(hid, inv, w.ffn_norm, H, sm, slot(l, 2), codes, st));
     SEM_LAUNCH(kStGemmGateUp, launch_gemm_q8(codes, w.gu, w.gu_s, (int)T, 2 * F, H, slot(l, 2), sm.row_seq, big, kEpiGeluUp, slot(l, 3),
-                              st));
+                              err, st));
     SEM_LAUNCH(kStQuant, launch_quantize(big, nullptr, nullptr, F, sm, slot(l, 3), codes, st));
-    SEM_LAUNCH(kStGemmDown, launch_gemm_q8(codes, w.down, w.down_s, (int)T, H, F, slot(l, 3), sm.row_seq, att, kEpiStore, nullptr, st));
+    SEM_LAUNCH(kStGemmDown, launch_gemm_q8(codes, w.down, w.down_s, (int)T, H, F, slot(l, 3), sm.row_seq, att, kEpiStore, nullptr, err, st));
     const bool last = l + 1 == L;
     const float* next_w = last ? m->out_norm : m->layers[l + 1].attn_norm;
     SEM_LAUNCH(kStResidual, launch_residual_norm(att, w.post_ffw, hid, next_w ? next_w : w.ffn_norm, H, c.norm_eps, sm, inv,
@@ -430,7 +448,11 @@ int model_embed(sem_model* m, const int32_t* ids, const int32_t* offsets, int32_
   SEM_CUDA(cudaMemcpyAsync(m->ids.p, ids, (size_t)T * 4, cudaMemcpyHostToDevice, ctx->stream));
   if ((rc = run_forward(m, m->ids.as<int32_t>(), mp, m->out.as<float>(), ctx->stream))) return rc;
   SEM_CUDA(cudaMemcpyAsync(out, m->out.p, (size_t)out_floats * 4, cudaMemcpyDeviceToHost, ctx->stream));
+  SEM_CUDA(ctx->pinned.ensure(64));
+  uint32_t* flags = ctx->pinned.as<uint32_t>();
+  SEM_CUDA(cudaMemcpyAsync(flags, m->errflag.p, 8, cudaMemcpyDeviceToHost, ctx->stream));
   SEM_CUDA(cudaStreamSynchronize(ctx->stream));
+  if (flags[1]) return set_error(SEM_EDEVICE, "forward: a tensor-core pipeline wait timed out (error bits 0x%x)", flags[1]);
   return SEM_OK;
 }
 
@@ -477,29 +499,45 @@ int q8_weight_create(sem_context* ctx, const void* w_q8, int32_t k_in, int32_t n
   w->ctx = ctx;
   w->k_in = k_in;
   w->n_out = n_out;
-  SEM_CUDA(w->codes.ensure((size_t)k_in * n_out));
+  SEM_CUDA(w->codes.ensure((size_t)k_in * n_out * 2));
   SEM_CUDA(w->scales.ensure((size_t)n_out * (k_in / 32) * 4));
   DevBuf staging;
   sem_tensor_view t{"weight", kQ8, 2, {(uint64_t)k_in, (uint64_t)n_out, 0, 0}, w_q8,
                     (uint64_t)n_out * (k_in / 32) * 34};
-  int rc = upload_q8(ctx, staging, &t, n_out, k_in, w->codes.as<int8_t>(), w->scales.as<float>(), 0, 0, 0, false);
+  int rc = upload_q8_proj(ctx, staging, &t, n_out, k_in, w->codes.as<__half>(), w->scales.as<float>(), 0);
   if (rc) return rc;
   *out = w.release();
   return SEM_OK;
 }
 
-int q8_gemm(sem_q8_weight* w, const float* d_a, int32_t M, float* d_c, int8_t* d_codes, uint32_t* d_absmax,
+int q8_gemm(sem_q8_weight* w, const float* d_a, int32_t M, float* d_c, void* d_codes, uint32_t* d_absmax,
             void* stream) {
   if (!w || !d_a || !d_c || !d_codes || !d_absmax) return set_error(SEM_EINVAL, "null argument");
+  if (M < 0) return set_error(SEM_EINVAL, "q8 gemm: negative row count %d", M);
+  if (reinterpret_cast<uintptr_t>(d_codes) & 15)
+    return set_error(SEM_EINVAL, "q8 gemm: the codes scratch must be 16-byte aligned");
   DeviceGuard dg(w->ctx->device);
   cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : w->ctx->stream;
   // one scale for the whole activation buffer (QuantizeSymmetricINT8Into, quantize.go:29-69)
   SEM_CUDA(cudaMemsetAsync(d_absmax, 0, 4, st));
   SeqMeta meta{nullptr, nullptr, nullptr, M, 1};
   SEM_CUDA(launch_absmax(d_a, (int64_t)M * w->k_in, d_absmax, st));
-  SEM_CUDA(launch_quantize(d_a, nullptr, nullptr, w->k_in, meta, d_absmax, d_codes, st));
-  SEM_CUDA(launch_gemm_q8(d_codes, w->codes.as<int8_t>(), w->scales.as<float>(), M, w->n_out, w->k_in, d_absmax, nullptr,
-                          d_c, kEpiStore, nullptr, st));
+  __half* codes = static_cast<__half*>(d_codes);
+  SEM_CUDA(launch_quantize(d_a, nullptr, nullptr, w->k_in, meta, d_absmax, codes, st));
+  SEM_CUDA(launch_gemm_q8(codes, w->codes.as<__half>(), w->scales.as<float>(), M, w->n_out, w->k_in, d_absmax, nullptr,
+                          d_c, kEpiStore, nullptr, nullptr, st));
+  return SEM_OK;
+}
+
+int q8_matmul_int8(sem_q8_weight* w, const void* d_codes, const uint32_t* d_absmax, int32_t M, float* d_c,
+                   void* stream) {
+  if (!w || !d_codes || !d_absmax || !d_c) return set_error(SEM_EINVAL, "null argument");
+  if (M < 0) return set_error(SEM_EINVAL, "q8 matmul: negative row count %d", M);
+  if (reinterpret_cast<uintptr_t>(d_codes) & 15) return set_error(SEM_EINVAL, "q8 matmul: codes must be 16-byte aligned");
+  DeviceGuard dg(w->ctx->device);
+  cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : w->ctx->stream;
+  SEM_CUDA(launch_gemm_q8(static_cast<const __half*>(d_codes), w->codes.as<__half>(), w->scales.as<float>(), M, w->n_out,
+                          w->k_in, d_absmax, nullptr, d_c, kEpiStore, nullptr, nullptr, st));
   return SEM_OK;
 }
 
@@ -663,7 +701,12 @@ int sem_q8_weight_free(sem_q8_weight* w) {
   return SEM_OK;
 }
 
-int sem_q8_gemm(sem_q8_weight* w, const float* d_a, int32_t m, float* d_c, int8_t* d_codes, uint32_t* d_absmax,
+int sem_q8_matmul_int8(sem_q8_weight* w, const void* d_codes, const uint32_t* d_absmax, int32_t m, float* d_c,
+                       void* stream) {
+  return sem::q8_matmul_int8(w, d_codes, d_absmax, m, d_c, stream);
+}
+
+int sem_q8_gemm(sem_q8_weight* w, const float* d_a, int32_t m, float* d_c, void* d_codes, uint32_t* d_absmax,
                 void* stream) {
   return sem::q8_gemm(w, d_a, m, d_c, d_codes, d_absmax, stream);
 }

@@ -2,6 +2,7 @@
 // only; every wrapper enqueues on `stream` and returns the launch status.
 #pragma once
 
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -18,6 +19,13 @@ namespace sem {
 cudaError_t launch_repack_q8_0(const uint8_t* raw, int64_t rows, int cols, int8_t* dst_codes,
                                float* dst_scales, int64_t dst_row_offset, int interleave, int part,
                                bool gguf_decoder, cudaStream_t stream);
+
+// Projection weights for the tensor-core GEMM: Q8_0 blocks of `rows` x `cols`
+// -> fp16 codes (exact integers) dst_codes[dst_row_offset + r][cols] and fp32
+// block scales dst_scales[dst_row_offset + r][cols/32] (runtime f16 decoder,
+// model_int8.go:571-597).
+cudaError_t launch_repack_q8_0_f16(const uint8_t* raw, int64_t rows, int cols, __half* dst_codes,
+                                   float* dst_scales, int64_t dst_row_offset, cudaStream_t stream);
 
 // ---- forward-pass element-wise kernels (model_kernels.cu) ----
 struct SeqMeta {
@@ -38,9 +46,10 @@ cudaError_t launch_row_stats(const float* x, const float* w, int H, float eps, S
 
 // codes = quantize((x * inv_rms[row]) * w) with the per-sequence scale; when
 // inv_rms is null the rows are quantized as they are; a null meta.row_seq
-// means one scale (absmax[0]) for every row.
+// means one scale (absmax[0]) for every row. The INT8 codes are stored as
+// fp16 (exact), the tensor-core GEMM's operand type.
 cudaError_t launch_quantize(const float* x, const float* inv_rms, const float* w, int K, SeqMeta meta,
-                            const uint32_t* absmax, int8_t* codes, cudaStream_t stream);
+                            const uint32_t* absmax, __half* codes, cudaStream_t stream);
 
 // Max |x| over n values, atomically into slot[0].
 cudaError_t launch_absmax(const float* x, int64_t n, uint32_t* slot, cudaStream_t stream);
@@ -64,12 +73,15 @@ cudaError_t launch_pool_l2(const float* hidden, const float* inv_rms, const floa
 
 // ---- Q8_0 x INT8 projection (gemm_q8.cu) ----
 enum GemmEpilogue { kEpiStore = 0, kEpiGeluUp = 1 };
-// C[m, n] = in_scale[seq(m)] * sum_kb float(int32 block dot) * w_scales[n, kb].
-// kEpiGeluUp: weights rows interleave gate/up in groups of 8; writes
-// h[m, n/2] = gelu_quick(gate) * up and the per-sequence absmax of h.
-cudaError_t launch_gemm_q8(const int8_t* a_codes, const int8_t* w_codes, const float* w_scales, int M, int N,
+// C[m, n] = in_scale[seq(m)] * sum_kb float(exact block dot) * w_scales[n, kb].
+// a_codes: fp16 INT8 codes [M][K]; w_codes: fp16 codes [N][K]; w_scales fp32
+// [N][K/32]; all 16-byte aligned, K % 128 == 0, N % 128 == 0. kEpiGeluUp: rows [0, N/2) are gate and
+// [N/2, N) up (N/2 % 128 == 0); writes h[m, n] = gelu_quick(gate) * up for
+// n < N/2 and the per-sequence absmax of h. `err` (nullable) receives error
+// bits if a pipeline wait times out.
+cudaError_t launch_gemm_q8(const __half* a_codes, const __half* w_codes, const float* w_scales, int M, int N,
                            int K, const uint32_t* a_absmax, const int32_t* row_seq, float* c, int epilogue,
-                           uint32_t* out_absmax, cudaStream_t stream);
+                           uint32_t* out_absmax, uint32_t* err, cudaStream_t stream);
 
 // ---- attention (attention.cu) ----
 struct AttnTiles {

@@ -95,6 +95,35 @@ cudaError_t launch_repack_q8_0(const uint8_t* raw, int64_t rows, int cols, int8_
   return cudaGetLastError();
 }
 
+// Projection weights: fp16 codes and fp32 block scales, one thread per block.
+__global__ void repack_q8_0_f16_kernel(const uint8_t* __restrict__ raw, int64_t rows, int nb, __half* __restrict__ codes,
+                                       float* __restrict__ scales, int64_t dst_row_offset) {
+  int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= rows * nb) return;
+  int64_t r = i / nb;
+  int b = (int)(i % nb);
+  const uint8_t* blk = raw + i * 34;
+  const uint16_t h = reinterpret_cast<const uint16_t*>(blk)[0];  // 34-byte blocks are 2-byte aligned
+  const int64_t dr = dst_row_offset + r;
+  scales[dr * nb + b] = f16_runtime(h);
+  __align__(16) __half v[32];
+#pragma unroll
+  for (int k = 0; k < 32; ++k) v[k] = __int2half_rn((int)(int8_t)blk[2 + k]);
+  uint4* dst = reinterpret_cast<uint4*>(codes + dr * (int64_t)nb * 32 + (int64_t)b * 32);
+  const uint4* src = reinterpret_cast<const uint4*>(v);
+#pragma unroll
+  for (int k = 0; k < 4; ++k) dst[k] = src[k];
+}
+
+cudaError_t launch_repack_q8_0_f16(const uint8_t* raw, int64_t rows, int cols, __half* dst_codes, float* dst_scales,
+                                   int64_t dst_row_offset, cudaStream_t stream) {
+  int nb = cols / 32;
+  int64_t n = rows * nb;
+  int64_t blocks = (n + 255) / 256;
+  repack_q8_0_f16_kernel<<<(unsigned)blocks, 256, 0, stream>>>(raw, rows, nb, dst_codes, dst_scales, dst_row_offset);
+  return cudaGetLastError();
+}
+
 // ---------------------------------------------------------------------------
 // Token embedding: DequantizeQ8_0Row then the sqrt(H) scale
 // (model_int8.go:167-184, gguf/tensor.go:157-177). 16 elements per thread.
@@ -207,7 +236,7 @@ cudaError_t launch_row_stats(const float* x, const float* w, int H, float eps, S
 // ---------------------------------------------------------------------------
 __global__ void quantize_kernel(const float* __restrict__ x, const float* __restrict__ inv_rms,
                                 const float* __restrict__ w, int K, SeqMeta meta,
-                                const uint32_t* __restrict__ absmax, int8_t* __restrict__ codes) {
+                                const uint32_t* __restrict__ absmax, __half* __restrict__ codes) {
   int per_row = K / 16;
   int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= (int64_t)meta.T * per_row) return;
@@ -227,19 +256,16 @@ __global__ void quantize_kernel(const float* __restrict__ x, const float* __rest
 #pragma unroll
     for (int k = 0; k < 16; ++k) v[k] = __fmul_rn(__fmul_rn(v[k], r), w[c + k]);
   }
-  uint32_t packed[4];
+  __align__(16) __half h[16];
 #pragma unroll
-  for (int k = 0; k < 4; ++k) {
-    uint32_t p = 0;
-#pragma unroll
-    for (int j = 0; j < 4; ++j) p |= ((uint32_t)(uint8_t)(int8_t)quant_code_ref(v[4 * k + j], inv)) << (8 * j);
-    packed[k] = p;
-  }
-  *reinterpret_cast<uint4*>(codes + row * K + c) = make_uint4(packed[0], packed[1], packed[2], packed[3]);
+  for (int k = 0; k < 16; ++k) h[k] = __int2half_rn(quant_code_ref(v[k], inv));
+  uint4* dst = reinterpret_cast<uint4*>(codes + row * K + c);
+  dst[0] = reinterpret_cast<const uint4*>(h)[0];
+  dst[1] = reinterpret_cast<const uint4*>(h)[1];
 }
 
 cudaError_t launch_quantize(const float* x, const float* inv_rms, const float* w, int K, SeqMeta meta,
-                            const uint32_t* absmax, int8_t* codes, cudaStream_t stream) {
+                            const uint32_t* absmax, __half* codes, cudaStream_t stream) {
   if (meta.T == 0) return cudaSuccess;
   int64_t n = (int64_t)meta.T * (K / 16);
   quantize_kernel<<<(unsigned)((n + 255) / 256), 256, 0, stream>>>(x, inv_rms, w, K, meta, absmax, codes);

@@ -128,6 +128,11 @@ class Q8Weight:
         check(load().sem_q8_gemm(self.handle, C.c_void_p(d_a), m, C.c_void_p(d_c), C.c_void_p(d_codes),
                                  C.c_void_p(d_absmax), C.c_void_p(stream or None)))
 
+    def matmul_int8(self, d_codes: int, d_absmax: int, m: int, d_c: int, stream: int = 0) -> None:
+        """MatMulQ8_0INT8 on codes already quantised (fp16-held INT8 codes, absmax bit pattern)."""
+        check(load().sem_q8_matmul_int8(self.handle, C.c_void_p(d_codes), C.c_void_p(d_absmax), m, C.c_void_p(d_c),
+                                        C.c_void_p(stream or None)))
+
     def close(self):
         if self.handle:
             load().sem_q8_weight_free(self.handle)

@@ -129,18 +129,29 @@ int sem_model_profile_read(sem_model *model, const char **names, float *total_ms
 int sem_q8_weight_create(sem_context *ctx, const void *w_q8, int32_t k_in, int32_t n_out, sem_q8_weight **out);
 int sem_q8_weight_free(sem_q8_weight *w);
 /* Device pointers: d_a fp32 [m x k_in] -> d_c fp32 [m x n_out], one activation
- * scale for the whole of d_a as in the reference; d_codes (m x k_in int8) and
- * d_absmax (one uint32) are caller-provided scratch. Enqueued on `stream`. */
-int sem_q8_gemm(sem_q8_weight *w, const float *d_a, int32_t m, float *d_c, int8_t *d_codes, uint32_t *d_absmax,
+ * scale for the whole of d_a as in the reference; d_codes and d_absmax (one
+ * uint32) are caller-provided scratch. d_codes holds the m x k_in INT8 codes
+ * as fp16 (the tensor cores' operand type; 2 * m * k_in bytes, 16-byte
+ * aligned). Enqueued on `stream`. */
+int sem_q8_gemm(sem_q8_weight *w, const float *d_a, int32_t m, float *d_c, void *d_codes, uint32_t *d_absmax,
                 void *stream);
+
+/* MatMulQ8_0INT8 alone (quantize.go:346-458) on activations already quantised
+ * by QuantizeSymmetricINT8Into: d_codes holds the m x k_in INT8 codes as fp16
+ * (16-byte aligned), *d_absmax the float32 bit pattern of the absmax they were
+ * quantised with (scale = absmax / 127, as quantize.go:60-61); d_c fp32
+ * [m x n_out]. Enqueued on `stream`. */
+int sem_q8_matmul_int8(sem_q8_weight *w, const void *d_codes, const uint32_t *d_absmax, int32_t m, float *d_c,
+                       void *stream);
 
 /* sem_q8_gemm without caller scratch, for callers that cannot allocate device
  * memory (a host runtime that owns the whole device pool and passes only input
  * and output buffers, or a request path with a memory budget fixed at start-up
  * where an allocation may neither grow nor fail). It has no counterpart in the
  * reference. The codes and the absmax word live in a static device array of
- * 8 MiB + 256 bytes that every GPU loading the library holds until exit, so
- * m * k_in must not exceed 8 MiB (larger calls fail with SEM_EINVAL); the call
+ * 16 MiB + 256 bytes that every GPU loading the library holds until exit, so
+ * m * k_in must not exceed 8 Mi (8,388,608) elements (larger calls fail with
+ * SEM_EINVAL); the call
  * performs no allocation. The first call on a device resolves the array's
  * address on that device (cudaGetSymbolAddress); make that first call before
  * any stream capture. All calls share the one array: calls that overlap on

@@ -107,19 +107,21 @@ def test_q8_gemm_matches_oracle(ctx):
     import oracle
     import runtime
     rng = np.random.default_rng(11)
-    for K, N, M in ((768, 256, 64), (1152, 768, 200), (768, 3072, 33)):
+    # tile edges: M below, between and above the 128/256-token tiles; K = 1152
+    # wraps the 4-stage ring several times; N = 3072 spans 24 weight tiles
+    for K, N, M in ((768, 256, 64), (1152, 768, 200), (768, 3072, 33), (768, 768, 4133), (1152, 1152, 1)):
         raw = synth.q8_0_blocks(rng, N, K)
         a = rng.standard_normal((M, K)).astype(np.float32)
         w = runtime.Q8Weight(ctx, raw, K, N)
         d_a = torch.from_numpy(a).cuda()
         d_c = torch.empty((M, N), dtype=torch.float32, device="cuda")
-        d_codes = torch.empty((M, K), dtype=torch.int8, device="cuda")
+        d_codes = torch.empty((M, K), dtype=torch.float16, device="cuda")  # INT8 codes held as fp16
         d_abs = torch.zeros(4, dtype=torch.int32, device="cuda")
         torch.cuda.synchronize()
         w.run(d_a.data_ptr(), M, d_c.data_ptr(), d_codes.data_ptr(), d_abs.data_ptr(), ctx.stream)
         torch.cuda.synchronize()
         codes, scale = oracle.quantize_sym_int8(a)
-        np.testing.assert_array_equal(d_codes.cpu().numpy(), codes)
+        np.testing.assert_array_equal(d_codes.cpu().numpy().astype(np.int8), codes)
         ref = oracle.matmul_q8_0_int8(raw, codes, scale, N)
         got = d_c.cpu().numpy()
         np.testing.assert_allclose(got, ref, rtol=2e-5, atol=2e-5 * np.abs(ref).max())

@@ -32,7 +32,7 @@ def test_noalloc_matches_scratch_variant_twice(ctx):
         a = (rng.standard_normal((m, K)) * scale).astype(np.float32)
         d_a = torch.from_numpy(a).cuda()
         ref_out = torch.empty((m, N), dtype=torch.float32, device="cuda")
-        codes = torch.empty((m, K), dtype=torch.int8, device="cuda")
+        codes = torch.empty((m, K), dtype=torch.float16, device="cuda")  # INT8 codes held as fp16
         absmax = torch.zeros(4, dtype=torch.int32, device="cuda")
         got_out = torch.full((m, N), float("nan"), dtype=torch.float32, device="cuda")
         torch.cuda.synchronize()
