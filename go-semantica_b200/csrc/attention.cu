@@ -1,277 +1,491 @@
-// Bidirectional GQA attention for EmbeddingGemma (runAttentionINT8 →
+// Bidirectional GQA attention for EmbeddingGemma (runAttentionINT8 ->
 // MultiHeadAttentionChunked, internal/runtime/model_int8.go:455-500,
-// internal/kernels/attention.go:178-310, softmax activation.go:161-213).
+// internal/kernels/attention.go:178-310, softmax activation.go:161-213) on the
+// sm_100a tensor cores (tcgen05, accumulators in TMEM).
 //
 // The reference materialises the scores of every query row, takes the exact
 // row max, applies its polynomial fastExp (which clamps arguments below -10 to
 // zero) and multiplies by 1/sum. Because of that clamp an online-softmax
-// rescale would change results, so this kernel makes two passes over the keys:
-//   pass 1: fp16 scores on the tensor cores, only to find each row's max;
+// rescale would change results, so the keys are visited twice:
+//   pass 1: scores from the fp16 high halves only, to find each row's max;
 //   pass 2: scores with three-term fp16 products (hi*hi + hi*lo + lo*hi, where
-//           x = hi + lo exactly to ~22 bits) for near-fp32 accuracy,
+//           x = hi + lo to ~22 bits) for near-fp32 accuracy,
 //           p = fastExp(score - max), row sums, and O += P V, again with
 //           three-term products of split P and V.
 // The max from pass 1 differs from the exact max by the fp16 error of one
 // score; fastExp(x - d) = fastExp(x) * e^-d up to O(1e-3 d), and the common
 // factor cancels in the normalisation.
 //
-// One CTA = 64 query rows of one (sequence, head); 8 warps. K/V tiles of 32
-// keys are double-buffered with cp.async; all three query heads read the same
-// single KV head (GQA), so K/V are shared in L2.
+// One CTA = 128 query rows of one (sequence, head). Q (hi and lo, 128 KB)
+// stays in shared memory; K and V stream through a ring of four 16 KB slots
+// (one fp16 plane of 64 keys x 128 dims each), loaded by TMA. Scores of a
+// 64-key tile land in TMEM (two buffers), O accumulates in TMEM (256 fp32
+// columns). Warp 0 issues TMA, warp 1 the MMAs, warps 4-11 (two per TMEM lane
+// quarter, each half of a tile's keys) do the softmax: they read scores from
+// TMEM, write P = p_hi, p_lo in the 128-byte-swizzled K-major layout the MMA
+// reads, and at the end scale O by 1/sum and store it. V is read MN-major
+// straight from its row-major [token][dim] layout, so sequences may start at
+// any token. All three query heads read the single KV head (GQA) through L2.
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
 #include "common.cuh"
 #include "kernels.h"
+#include "sm100.cuh"
 
 namespace sem {
 
 namespace {
-constexpr int HD = 256;           // head_dim
-constexpr int QT = 64;            // query rows per CTA
-constexpr int KT = 32;            // keys per tile
-constexpr int LDH = HD + 8;       // padded smem row (halves): 528 bytes, conflict-free ldmatrix
-constexpr int LDP = KT + 8;       // padded P row (halves): 80 bytes
-constexpr int THREADS = 256;
-constexpr int Q_HALVES = QT * LDH;
-constexpr int KV_HALVES = KT * LDH;
-constexpr int SMEM_BYTES = (2 * Q_HALVES + 2 * 4 * KV_HALVES + 2 * QT * LDP) * 2 + 4 * QT * 4;
+
+constexpr int HD = 256;      // head_dim
+constexpr int QT = 128;      // query rows per CTA (TMEM lanes)
+constexpr int KT = 64;       // keys per tile
+constexpr int NSLOT = 4;     // K/V ring slots
+constexpr int SLOT = KT * 128 * 2;       // 16 KB: 64 keys x 128 dims, one plane
+constexpr int QBLK = QT * 128;           // 16 KB: 128 rows x 64 dims
+constexpr int PPLANE = QT * KT * 2;      // 16 KB: 128 rows x 64 keys
+constexpr int SMEM_Q = 2 * 4 * QBLK;     // hi, lo x 4 dim blocks: 128 KB
+constexpr int SMEM_RING = NSLOT * SLOT;  // 64 KB
+constexpr int SMEM_P = 2 * PPLANE;       // 32 KB
+constexpr int NBAR = 1 + 2 * NSLOT + 2 + 2 + 2 + 1 + 1;  // q, ring full/empty, S full/empty, P full/free, O, drain
+constexpr int SMEM_MISC = 160 + 2 * QT * 4;              // barriers, TMEM address, [2][QT] reductions
+constexpr int SMEM_BYTES = 1024 + SMEM_Q + SMEM_RING + SMEM_P + SMEM_MISC;
+constexpr int THREADS = 384;  // warpgroup 0: TMA, MMA, 2 idle; warpgroups 1-2: softmax / epilogue
+constexpr int SM_WARPS = 8;
+constexpr uint32_t TM_O = 0, TM_S = 256;  // TMEM columns: O [0,256), scores [256,320) and [320,384)
+static_assert(SMEM_BYTES <= 232448, "shared memory per CTA");
+static_assert(NBAR * 8 + 8 <= 160, "barrier block");
+
+__device__ uint32_t g_attn_error;
+
+__device__ __forceinline__ void tmem_ld16_w(uint32_t taddr, uint32_t (&r)[16]) { tmem_ld16(taddr, r); }
+__device__ __forceinline__ void tmem_wait_regs(uint32_t (&r)[16]) {
+  asm volatile("tcgen05.wait::ld.sync.aligned;"
+               : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
+                 "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]),
+                 "+r"(r[15])
+               :
+               : "memory");
+}
+
+// Shared-memory descriptor of an MN-major operand tile with 128-byte swizzle:
+// rows of 128 bytes hold 64 consecutive MN elements, 8-row groups along K are
+// 1024 bytes apart (SBO), and the next 64 MN elements sit `lbo` bytes further.
+__device__ __forceinline__ uint64_t umma_desc_mn_sw128(uint32_t saddr, uint32_t lbo) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr & 0x3FFFFu) >> 4);
+  d |= (uint64_t)((lbo >> 4) & 0x3FFFu) << 16;
+  d |= (uint64_t)(1024 >> 4) << 32;
+  d |= (uint64_t)1 << 46;
+  d |= (uint64_t)2 << 61;
+  return d;
+}
+
 }  // namespace
 
 __global__ void __launch_bounds__(THREADS, 1)
-    attention_kernel(const __half* __restrict__ qh, const __half* __restrict__ ql, const __half* __restrict__ kh,
-                     const __half* __restrict__ kl, const __half* __restrict__ vh, const __half* __restrict__ vl,
-                     int nh, float scale, SeqMeta meta, AttnTiles tiles, float* __restrict__ out,
-                     uint32_t* __restrict__ absmax) {
-  extern __shared__ __align__(128) uint8_t smem_raw[];
-  __half* sQh = reinterpret_cast<__half*>(smem_raw);
-  __half* sQl = sQh + Q_HALVES;
-  __half* sKV = sQl + Q_HALVES;  // [stage][4][KT][LDH]: Kh, Kl, Vh, Vl
-  __half* sPh = sKV + 2 * 4 * KV_HALVES;
-  __half* sPl = sPh + QT * LDP;
-  float* sRed = reinterpret_cast<float*>(sPl + QT * LDP);  // [2][QT] maxima, then [2][QT] sums
+    attention_tc_kernel(const __grid_constant__ CUtensorMap tm_qh, const __grid_constant__ CUtensorMap tm_ql,
+                        const __grid_constant__ CUtensorMap tm_kh, const __grid_constant__ CUtensorMap tm_kl,
+                        const __grid_constant__ CUtensorMap tm_vh, const __grid_constant__ CUtensorMap tm_vl, int nh,
+                        float scale, SeqMeta meta, AttnTiles tiles, float* __restrict__ out,
+                        uint32_t* __restrict__ absmax, uint32_t* __restrict__ err) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
+  uint8_t* sQ = smem;                      // [plane][dblock][128 rows x 128 B]
+  uint8_t* sRing = sQ + SMEM_Q;            // [slot][2 boxes of 64 keys x 128 B]
+  uint8_t* sP = sRing + SMEM_RING;         // [plane][128 rows x 128 B]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + SMEM_P);
+  uint64_t* qfull = bars;
+  uint64_t* rfull = bars + 1;
+  uint64_t* rempty = rfull + NSLOT;
+  uint64_t* sfull = rempty + NSLOT;
+  uint64_t* sempty = sfull + 2;
+  uint64_t* pfull = sempty + 2;
+  uint64_t* pfree = pfull + 1;
+  uint64_t* ofull = pfree + 1;
+  uint64_t* drain = ofull + 1;
+  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(bars + NBAR);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(s_tmem + 1);
+  float* s_red = reinterpret_cast<float*>(sP + SMEM_P + 160);  // [2 halves][QT]: maxima, later sums
+  if (!err) err = &g_attn_error;
 
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int g = lane >> 2, t4 = lane & 3;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int tile = blockIdx.x, head = blockIdx.y;
   const int seq = tiles.tile_seq[tile];
   const int row0 = tiles.tile_row0[tile];
   const int s_beg = meta.cu_seqlens[seq], s_end = meta.cu_seqlens[seq + 1];
   const int n_rows = min(QT, s_end - row0);
   const int n_keys = s_end - s_beg;
-  const int n_kt = (n_keys + KT - 1) / KT;
+  const int nkt = (n_keys + KT - 1) / KT;
 
-  // ---- load Q (hi, lo) ----
-  for (int i = tid; i < QT * (HD / 8); i += THREADS) {
-    int r = i / (HD / 8), c = i % (HD / 8);
-    bool v = r < n_rows;
-    int64_t src = ((int64_t)(v ? row0 + r : row0) * nh + head) * HD + c * 8;
-    cp_async16(sQh + r * LDH + c * 8, qh + src, v);
-    cp_async16(sQl + r * LDH + c * 8, ql + src, v);
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < NBAR; ++i) mbar_init(&bars[i], 1);
+    mbar_init(sempty, SM_WARPS);
+    mbar_init(sempty + 1, SM_WARPS);
+    mbar_init(pfull, SM_WARPS);
+    *abort_flag = 0;
+    fence_mbar_init();
   }
-  cp_async_commit();
-
-  auto load_kv = [&](int stage, int kt, bool with_lo_v) {
-    __half* base = sKV + stage * 4 * KV_HALVES;
-    const int nparts = with_lo_v ? 4 : 1;
-    for (int i = tid; i < nparts * KT * (HD / 8); i += THREADS) {
-      int part = i / (KT * (HD / 8));
-      int rem = i % (KT * (HD / 8));
-      int r = rem / (HD / 8), c = rem % (HD / 8);
-      int key = kt * KT + r;
-      bool v = key < n_keys;
-      const __half* src = part == 0 ? kh : part == 1 ? kl : part == 2 ? vh : vl;
-      cp_async16(base + part * KV_HALVES + r * LDH + c * 8, src + (int64_t)(s_beg + (v ? key : 0)) * HD + c * 8, v);
-    }
-  };
-
-  const int r0 = 16 * (warp & 3);    // query rows of this warp (both passes)
-  const int kk0 = 16 * (warp >> 2);  // key half of the tile for the score phase
-  const int d0 = 128 * (warp >> 2);  // output dims for the PV phase
-
-  // ================= pass 1: row maxima =================
-  float mrun[2] = {-INFINITY, -INFINITY};
-  load_kv(0, 0, false);
-  cp_async_commit();
-  for (int kt = 0; kt < n_kt; ++kt) {
-    if (kt + 1 < n_kt) load_kv((kt + 1) & 1, kt + 1, false);
-    cp_async_commit();
-    cp_async_wait<1>();
-    __syncthreads();
-    const __half* sK = sKV + (kt & 1) * 4 * KV_HALVES;
-    // four independent accumulator chains (k-step parity x key half) keep the
-    // tensor pipe busy; they are summed once per tile
-    float s4[2][2][4] = {};
-#pragma unroll 4
-    for (int ks = 0; ks < HD / 16; ++ks) {
-      uint32_t a[4], b[2][2];
-      ldmatrix_x4(a[0], a[1], a[2], a[3], sQh + (r0 + (lane & 7) + ((lane >> 3) & 1) * 8) * LDH + (2 * ks + (lane >> 4)) * 8);
-      ldmatrix_x4(b[0][0], b[0][1], b[1][0], b[1][1],
-                  sK + (kk0 + (lane & 7) + (lane >> 4) * 8) * LDH + (2 * ks + ((lane >> 3) & 1)) * 8);
-      mma_f16(s4[ks & 1][0], a, b[0]);
-      mma_f16(s4[ks & 1][1], a, b[1]);
-    }
-    float s[2][4];
-#pragma unroll
-    for (int nt = 0; nt < 2; ++nt)
-#pragma unroll
-      for (int e = 0; e < 4; ++e) s[nt][e] = __fadd_rn(s4[0][nt][e], s4[1][nt][e]);
-#pragma unroll
-    for (int nt = 0; nt < 2; ++nt)
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        int key = kt * KT + kk0 + nt * 8 + t4 * 2 + (e & 1);
-        if (key < n_keys) mrun[e >> 1] = fmaxf(mrun[e >> 1], __fmul_rn(s[nt][e], scale));
-      }
-    __syncthreads();  // the buffer just read is refilled two iterations later
-  }
-#pragma unroll
-  for (int h = 0; h < 2; ++h) {
-    mrun[h] = fmaxf(mrun[h], __shfl_xor_sync(0xffffffffu, mrun[h], 1));
-    mrun[h] = fmaxf(mrun[h], __shfl_xor_sync(0xffffffffu, mrun[h], 2));
-  }
-  if (t4 == 0) {
-    sRed[(warp >> 2) * QT + r0 + g] = mrun[0];
-    sRed[(warp >> 2) * QT + r0 + g + 8] = mrun[1];
-  }
+  if (warp == 1) tmem_alloc(s_tmem, 512);
+  tc_fence_before();
   __syncthreads();
-  float mrow[2];
-  mrow[0] = fmaxf(sRed[r0 + g], sRed[QT + r0 + g]);
-  mrow[1] = fmaxf(sRed[r0 + g + 8], sRed[QT + r0 + g + 8]);
+  tc_fence_after();
+  const uint32_t tmem = *s_tmem;
 
-  // ================= pass 2: P, row sums, O = P V =================
-  float o[16][4];
+  // Ring consumption order: pass 1 = Kh of each key tile (two dim halves);
+  // pass 2 = K(0), then for j = 1..: K(j), V(j-1); finally V(last). A K(j)
+  // item is (hi, lo) of dim half 0 then 1 (4 slots), a V(j) item the same.
+  if (warp < 4) {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 56;");
+    if (warp == 0 && lane == 0) {
+      // ---------------- TMA producer ----------------
+      uint32_t it = 0;
+      bool ok = true;
+      mbar_arrive_expect_tx(qfull, SMEM_Q);
 #pragma unroll
-  for (int nt = 0; nt < 16; ++nt) o[nt][0] = o[nt][1] = o[nt][2] = o[nt][3] = 0.0f;
-  float lsum[2] = {0.0f, 0.0f};
-
-  load_kv(0, 0, true);
-  cp_async_commit();
-  for (int kt = 0; kt < n_kt; ++kt) {
-    if (kt + 1 < n_kt) load_kv((kt + 1) & 1, kt + 1, true);
-    cp_async_commit();
-    cp_async_wait<1>();
-    __syncthreads();
-    const __half* sKh = sKV + (kt & 1) * 4 * KV_HALVES;
-    const __half* sKl = sKh + KV_HALVES;
-    const __half* sVh = sKl + KV_HALVES;
-    const __half* sVl = sVh + KV_HALVES;
-    // scores of rows r0..r0+15 x keys kk0..kk0+15
-    // hi*hi and the two cross terms accumulate in separate chains, alternating
-    // by k-step parity: eight independent MMA chains per warp instead of two
-    float sm[2][2][4] = {}, sx[2][2][4] = {};
-#pragma unroll 2
-    for (int ks = 0; ks < HD / 16; ++ks) {
-      uint32_t ah[4], al[4], bh[2][2], bl[2][2];
-      const int qoff = (r0 + (lane & 7) + ((lane >> 3) & 1) * 8) * LDH + (2 * ks + (lane >> 4)) * 8;
-      const int koff = (kk0 + (lane & 7) + (lane >> 4) * 8) * LDH + (2 * ks + ((lane >> 3) & 1)) * 8;
-      ldmatrix_x4(ah[0], ah[1], ah[2], ah[3], sQh + qoff);
-      ldmatrix_x4(al[0], al[1], al[2], al[3], sQl + qoff);
-      ldmatrix_x4(bh[0][0], bh[0][1], bh[1][0], bh[1][1], sKh + koff);
-      ldmatrix_x4(bl[0][0], bl[0][1], bl[1][0], bl[1][1], sKl + koff);
-#pragma unroll
-      for (int nt = 0; nt < 2; ++nt) {
-        mma_f16(sx[ks & 1][nt], al, bh[nt]);
-        mma_f16(sx[ks & 1][nt], ah, bl[nt]);
-        mma_f16(sm[ks & 1][nt], ah, bh[nt]);
+      for (int b = 0; b < 4; ++b) {
+        tma_load_3d(&tm_qh, qfull, sQ + b * QBLK, b * 64, head, row0);
+        tma_load_3d(&tm_ql, qfull, sQ + (4 + b) * QBLK, b * 64, head, row0);
       }
-    }
-    float s[2][4];
-#pragma unroll
-    for (int nt = 0; nt < 2; ++nt)
-#pragma unroll
-      for (int e = 0; e < 4; ++e)
-        s[nt][e] = __fadd_rn(__fadd_rn(sm[0][nt][e], sm[1][nt][e]), __fadd_rn(sx[0][nt][e], sx[1][nt][e]));
-#pragma unroll
-    for (int nt = 0; nt < 2; ++nt) {
-      float p[4];
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        int key = kt * KT + kk0 + nt * 8 + t4 * 2 + (e & 1);
-        float sc = __fmul_rn(s[nt][e], scale);  // score *= scale (attention.go:300)
-        p[e] = key < n_keys ? fast_exp_ref(__fsub_rn(sc, mrow[e >> 1])) : 0.0f;
-        lsum[e >> 1] = __fadd_rn(lsum[e >> 1], p[e]);
+      auto load_slot = [&](const CUtensorMap* map, int key0, int dim0) -> bool {
+        const uint32_t s = it % NSLOT, u = it / NSLOT;
+        if (!mbar_wait(&rempty[s], (u & 1) ^ 1, abort_flag, err, 1u)) return false;
+        uint8_t* dst = sRing + s * SLOT;
+        mbar_arrive_expect_tx(&rfull[s], SLOT);
+        tma_load_2d(map, &rfull[s], dst, dim0, key0);
+        tma_load_2d(map, &rfull[s], dst + SLOT / 2, dim0 + 64, key0);
+        ++it;
+        return true;
+      };
+      for (int j = 0; ok && j < nkt; ++j)
+        for (int h = 0; ok && h < 2; ++h) ok = load_slot(&tm_kh, s_beg + j * KT, h * 128);
+      for (int j = 0; ok && j <= nkt; ++j) {
+        if (j < nkt)
+          for (int h = 0; ok && h < 2; ++h) {
+            ok = ok && load_slot(&tm_kh, s_beg + j * KT, h * 128);
+            ok = ok && load_slot(&tm_kl, s_beg + j * KT, h * 128);
+          }
+        if (j >= 1)
+          for (int h = 0; ok && h < 2; ++h) {
+            ok = ok && load_slot(&tm_vh, s_beg + (j - 1) * KT, h * 128);
+            ok = ok && load_slot(&tm_vl, s_beg + (j - 1) * KT, h * 128);
+          }
       }
-      __half h0, l0, h1, l1;
-      const int col = kk0 + nt * 8 + t4 * 2;
-      split_half(p[0], h0, l0);
-      split_half(p[1], h1, l1);
-      *reinterpret_cast<__half2*>(sPh + (r0 + g) * LDP + col) = __halves2half2(h0, h1);
-      *reinterpret_cast<__half2*>(sPl + (r0 + g) * LDP + col) = __halves2half2(l0, l1);
-      split_half(p[2], h0, l0);
-      split_half(p[3], h1, l1);
-      *reinterpret_cast<__half2*>(sPh + (r0 + g + 8) * LDP + col) = __halves2half2(h0, h1);
-      *reinterpret_cast<__half2*>(sPl + (r0 + g + 8) * LDP + col) = __halves2half2(l0, l1);
-    }
-    __syncthreads();
-    // O[r0..r0+15][d0..d0+127] += P[r0.., 0..31] V[0..31][d0..]
+      for (uint32_t j = it > (uint32_t)NSLOT ? it - NSLOT : 0; j < it; ++j)
+        mbar_wait_drain(&rfull[j % NSLOT], (j / NSLOT) & 1);
+      mbar_wait_drain(qfull, 0);
+    } else if (warp == 1 && lane == 0) {
+      // ---------------- MMA issuer ----------------
+      constexpr uint32_t idesc_qk = umma_idesc_f16_f32(QT, KT);
+      constexpr uint32_t idesc_pv = umma_idesc_f16_f32(QT, 128) | (1u << 16);  // B (V) MN-major
+      uint32_t it = 0, sfill = 0;
+      bool ok = mbar_wait(qfull, 0, abort_flag, err, 2u);
+      tc_fence_after();
+      const uint32_t q_hi = smem_u32(sQ), q_lo = smem_u32(sQ + 4 * QBLK);
+      auto take_slot = [&](uint32_t& addr) -> bool {
+        const uint32_t s = it % NSLOT, u = it / NSLOT;
+        if (!mbar_wait(&rfull[s], u & 1, abort_flag, err, 2u)) return false;
+        tc_fence_after();
+        addr = smem_u32(sRing + s * SLOT);
+        return true;
+      };
+      auto free_slot = [&]() { umma_commit(&rempty[it % NSLOT]); ++it; };
+      // S[buf] = scores of key tile j (terms: 1 in pass 1, 3 in pass 2)
+      auto qk = [&](bool three) -> bool {
+        const uint32_t b = sfill & 1, ub = sfill >> 1;
+        if (!mbar_wait(&sempty[b], (ub & 1) ^ 1, abort_flag, err, 2u)) return false;
+        tc_fence_after();
+        const uint32_t d_s = tmem + TM_S + b * KT;
+        for (int h = 0; h < 2; ++h) {
+          uint32_t kh_a, kl_a = 0;
+          if (!take_slot(kh_a)) return false;
+          if (three) {  // the lo plane is the next ring slot
+            const uint32_t s = (it + 1) % NSLOT, u = (it + 1) / NSLOT;
+            if (!mbar_wait(&rfull[s], u & 1, abort_flag, err, 2u)) return false;
+            tc_fence_after();
+            kl_a = smem_u32(sRing + s * SLOT);
+          }
 #pragma unroll
-    for (int kstep = 0; kstep < KT / 16; ++kstep) {
-      uint32_t ph[4], pl[4];
-      const int poff = (r0 + (lane & 7) + ((lane >> 3) & 1) * 8) * LDP + (2 * kstep + (lane >> 4)) * 8;
-      ldmatrix_x4(ph[0], ph[1], ph[2], ph[3], sPh + poff);
-      ldmatrix_x4(pl[0], pl[1], pl[2], pl[3], sPl + poff);
-#pragma unroll
-      for (int dp = 0; dp < 8; ++dp) {
-        uint32_t vhf[2][2], vlf[2][2];
-        const int voff = (16 * kstep + (lane & 7) + ((lane >> 3) & 1) * 8) * LDH + ((d0 + 16 * dp) / 8 + (lane >> 4)) * 8;
-        ldmatrix_x4_trans(vhf[0][0], vhf[0][1], vhf[1][0], vhf[1][1], sVh + voff);
-        ldmatrix_x4_trans(vlf[0][0], vlf[0][1], vlf[1][0], vlf[1][1], sVl + voff);
-#pragma unroll
-        for (int j = 0; j < 2; ++j) {
-          mma_f16(o[2 * dp + j], pl, vhf[j]);
-          mma_f16(o[2 * dp + j], ph, vlf[j]);
-          mma_f16(o[2 * dp + j], ph, vhf[j]);
+          for (int k16 = 0; k16 < 8; ++k16) {
+            const int db = 2 * h + k16 / 4;               // Q dim block
+            const uint32_t koff = (uint32_t)(k16 % 4) * 32;  // K=16 slice within the 128-byte row
+            const uint32_t kb = (uint32_t)(k16 / 4) * (SLOT / 2) + koff;
+            const uint32_t acc = (h | k16) ? 1u : 0u;
+            umma_f16(d_s, umma_desc_k_sw128(q_hi + db * QBLK + koff), umma_desc_k_sw128(kh_a + kb), idesc_qk, acc);
+            if (three) {
+              umma_f16(d_s, umma_desc_k_sw128(q_hi + db * QBLK + koff), umma_desc_k_sw128(kl_a + kb), idesc_qk, 1u);
+              umma_f16(d_s, umma_desc_k_sw128(q_lo + db * QBLK + koff), umma_desc_k_sw128(kh_a + kb), idesc_qk, 1u);
+            }
+          }
+          free_slot();
+          if (three) free_slot();
         }
+        umma_commit(&sfull[b]);
+        ++sfill;
+        return true;
+      };
+      // O += P(j) V(j), three terms
+      auto pv = [&](int j) -> bool {
+        if (!mbar_wait(pfull, j & 1, abort_flag, err, 2u)) return false;
+        tc_fence_after();
+        const uint32_t p_hi = smem_u32(sP), p_lo = smem_u32(sP + PPLANE);
+        for (int h = 0; h < 2; ++h) {
+          uint32_t vh_a, vl_a;
+          if (!take_slot(vh_a)) return false;
+          {
+            const uint32_t s = (it + 1) % NSLOT, u = (it + 1) / NSLOT;
+            if (!mbar_wait(&rfull[s], u & 1, abort_flag, err, 2u)) return false;
+            tc_fence_after();
+            vl_a = smem_u32(sRing + s * SLOT);
+          }
+          const uint32_t d_o = tmem + TM_O + h * 128;
+#pragma unroll
+          for (int k16 = 0; k16 < KT / 16; ++k16) {
+            const uint32_t poff = (uint32_t)k16 * 32;    // keys 16k16.. in the 128-byte P row
+            const uint32_t voff = (uint32_t)k16 * 2048;  // two 8-key groups of V rows
+            const uint32_t acc0 = (j > 0 || k16 > 0) ? 1u : 0u;
+            umma_f16(d_o, umma_desc_k_sw128(p_hi + poff), umma_desc_mn_sw128(vh_a + voff, SLOT / 2), idesc_pv, acc0);
+            umma_f16(d_o, umma_desc_k_sw128(p_hi + poff), umma_desc_mn_sw128(vl_a + voff, SLOT / 2), idesc_pv, 1u);
+            umma_f16(d_o, umma_desc_k_sw128(p_lo + poff), umma_desc_mn_sw128(vh_a + voff, SLOT / 2), idesc_pv, 1u);
+          }
+          free_slot();
+          free_slot();
+        }
+        umma_commit(pfree);
+        return true;
+      };
+      for (int j = 0; ok && j < nkt; ++j) ok = qk(false);
+      for (int j = 0; ok && j <= nkt; ++j) {
+        if (j < nkt) ok = qk(true);
+        if (ok && j >= 1) ok = pv(j - 1);
+      }
+      umma_commit(ofull);
+      umma_commit(drain);
+      mbar_wait_drain(drain, 0);
+    }
+  } else {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 192;");
+    // ---------------- softmax and epilogue ----------------
+    const int w = warp - 4;
+    const int q = warp & 3;       // TMEM lane quarter
+    const int half = w >> 2;      // keys [32*half, 32*half + 32) of each tile; O columns [128*half, +128)
+    const int r = q * 32 + lane;  // query row within the tile
+    const uint32_t t_lane = tmem + ((uint32_t)(q * 32) << 16);
+    uint32_t sfill = 0;
+    bool ok = true;
+    auto wait_s = [&](uint32_t& col) {
+      const uint32_t b = sfill & 1, ub = sfill >> 1;
+      if (ok) ok = mbar_wait(&sfull[b], ub & 1, abort_flag, err, 4u);
+      ok = __all_sync(0xffffffffu, ok);
+      tc_fence_after();
+      col = TM_S + b * KT + half * 32;
+    };
+    auto release_s = [&]() {
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sempty[sfill & 1]);
+      ++sfill;
+    };
+    // ---- pass 1: row max of the fp16 scores ----
+    float m = -INFINITY;
+    for (int j = 0; j < nkt; ++j) {
+      uint32_t col;
+      wait_s(col);
+      if (ok) {
+        uint32_t s[2][16];
+        tmem_ld16_w(t_lane + col, s[0]);
+        tmem_ld16_w(t_lane + col + 16, s[1]);
+        tmem_wait_regs(s[0]);
+        reg_barrier16(s[1]);
+        release_s();
+#pragma unroll
+        for (int c = 0; c < 32; ++c) {
+          const int key = j * KT + half * 32 + c;
+          if (key < n_keys) m = fmaxf(m, __fmul_rn(__uint_as_float(s[c >> 4][c & 15]), scale));
+        }
+      } else {
+        release_s();
       }
     }
-    __syncthreads();  // P and this K/V buffer are rewritten next
+    s_red[half * QT + r] = m;
+    named_bar_sync(1, SM_WARPS * 32);
+    m = fmaxf(s_red[r], s_red[QT + r]);
+    // ---- pass 2: p = fastExp(s - max), row sums, P for the MMA ----
+    float l = 0.0f;
+    uint8_t* prow_hi = sP + r * 128;
+    uint8_t* prow_lo = sP + PPLANE + r * 128;
+    for (int j = 0; j < nkt; ++j) {
+      uint32_t col;
+      wait_s(col);
+      if (ok && j >= 1) ok = mbar_wait(pfree, (j - 1) & 1, abort_flag, err, 4u);  // PV(j-1) is done with P
+      ok = __all_sync(0xffffffffu, ok);
+      if (ok) {
+        uint32_t s[2][16];
+        tmem_ld16_w(t_lane + col, s[0]);
+        tmem_ld16_w(t_lane + col + 16, s[1]);
+        tmem_wait_regs(s[0]);
+        reg_barrier16(s[1]);
+        release_s();
+        uint32_t ph[16], pl[16];  // 32 keys as packed fp16 pairs
+#pragma unroll
+        for (int c = 0; c < 32; c += 2) {
+          float p2[2];
+#pragma unroll
+          for (int x = 0; x < 2; ++x) {
+            const int key = j * KT + half * 32 + c + x;
+            const float sc = __fmul_rn(__uint_as_float(s[(c + x) >> 4][(c + x) & 15]), scale);  // attention.go:300
+            p2[x] = key < n_keys ? fast_exp_ref(__fsub_rn(sc, m)) : 0.0f;
+            l = __fadd_rn(l, p2[x]);
+          }
+          __half h0, l0, h1, l1;
+          split_half(p2[0], h0, l0);
+          split_half(p2[1], h1, l1);
+          ph[c >> 1] = (uint32_t)__half_as_ushort(h0) | ((uint32_t)__half_as_ushort(h1) << 16);
+          pl[c >> 1] = (uint32_t)__half_as_ushort(l0) | ((uint32_t)__half_as_ushort(l1) << 16);
+        }
+        // 16-byte chunk c of the row goes to chunk (c ^ (row & 7)): the 128-byte swizzle
+#pragma unroll
+        for (int cc = 0; cc < 4; ++cc) {
+          const int chunk = (half * 4 + cc) ^ (r & 7);
+          *reinterpret_cast<uint4*>(prow_hi + chunk * 16) =
+              make_uint4(ph[4 * cc], ph[4 * cc + 1], ph[4 * cc + 2], ph[4 * cc + 3]);
+          *reinterpret_cast<uint4*>(prow_lo + chunk * 16) =
+              make_uint4(pl[4 * cc], pl[4 * cc + 1], pl[4 * cc + 2], pl[4 * cc + 3]);
+        }
+        fence_proxy_async_smem();  // generic-proxy writes before the tensor core reads P
+      } else {
+        release_s();
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(pfull);
+    }
+    // ---- epilogue: O / sum, store, absmax ----
+    named_bar_sync(1, SM_WARPS * 32);  // every thread has read its row max from s_red
+    s_red[half * QT + r] = l;
+    if (ok) ok = mbar_wait(ofull, 0, abort_flag, err, 8u);
+    ok = __all_sync(0xffffffffu, ok);
+    named_bar_sync(1, SM_WARPS * 32);
+    tc_fence_after();
+    const float lt = __fadd_rn(s_red[r], s_red[QT + r]);
+    const float inv = lt > 0.0f ? __fdiv_rn(1.0f, lt) : 0.0f;
+    const bool valid = r < n_rows;
+    float amax = 0.0f;
+    float* dst = out + (int64_t)(row0 + (valid ? r : 0)) * (nh * HD) + head * HD + half * 128;
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {
+      uint32_t o[16];
+      if (ok) {
+        tmem_ld16_w(t_lane + TM_O + half * 128 + c * 16, o);
+        tmem_wait_regs(o);
+      } else {
+#pragma unroll
+        for (int i = 0; i < 16; ++i) o[i] = 0u;
+      }
+      float v[16];
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        v[i] = __fmul_rn(__uint_as_float(o[i]), inv);
+        amax = fmaxf(amax, fabsf(v[i]));
+      }
+      if (valid) {
+        float4* d4 = reinterpret_cast<float4*>(dst + c * 16);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) d4[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+      }
+    }
+    amax = warp_max(valid ? amax : 0.0f);
+    if (lane == 0 && absmax) atomicMax(&absmax[seq], __float_as_uint(amax));
   }
 
-  // ---- row sums over both key halves, normalise, store, absmax ----
-#pragma unroll
-  for (int h = 0; h < 2; ++h) {
-    lsum[h] = __fadd_rn(lsum[h], __shfl_xor_sync(0xffffffffu, lsum[h], 1));
-    lsum[h] = __fadd_rn(lsum[h], __shfl_xor_sync(0xffffffffu, lsum[h], 2));
-  }
-  float* sSum = sRed + 2 * QT;
-  if (t4 == 0) {
-    sSum[(warp >> 2) * QT + r0 + g] = lsum[0];
-    sSum[(warp >> 2) * QT + r0 + g + 8] = lsum[1];
-  }
+  tc_fence_before();
   __syncthreads();
-  float inv[2];
-#pragma unroll
-  for (int h = 0; h < 2; ++h) {
-    float l = __fadd_rn(sSum[r0 + g + 8 * h], sSum[QT + r0 + g + 8 * h]);
-    inv[h] = l > 0.0f ? __fdiv_rn(1.0f, l) : 0.0f;  // l >= fastExp(~0) ~ 1 for every valid row
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
   }
-  float amax = 0.0f;
-  const int ld = nh * HD;
-#pragma unroll
-  for (int h = 0; h < 2; ++h) {
-    const int r = r0 + g + 8 * h;
-    const bool valid = r < n_rows;
-    float* dst = out + (int64_t)(row0 + (valid ? r : 0)) * ld + head * HD + d0 + t4 * 2;
-#pragma unroll
-    for (int nt = 0; nt < 16; ++nt) {
-      float v0 = __fmul_rn(o[nt][2 * h], inv[h]);
-      float v1 = __fmul_rn(o[nt][2 * h + 1], inv[h]);
-      if (valid) {
-        *reinterpret_cast<float2*>(dst + nt * 8) = make_float2(v0, v1);
-        amax = fmaxf(amax, fmaxf(fabsf(v0), fabsf(v1)));
-      }
-    }
-  }
-  amax = warp_max(amax);
-  if (lane == 0 && absmax) atomicMax(&absmax[seq], __float_as_uint(amax));
 }
+
+namespace {
+
+PFN_cuTensorMapEncodeTiled_v12000 attn_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult qr;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &qr) == cudaSuccess &&
+        qr == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+// fp16 row-major [rows][256] with a box of 64 x box_rows, 128-byte swizzle.
+cudaError_t map_rows(CUtensorMap* m, const __half* base, int64_t rows, int box_rows) {
+  auto enc = attn_encoder();
+  if (!enc) return cudaErrorNotSupported;
+  if (reinterpret_cast<uintptr_t>(base) & 15) return cudaErrorMisalignedAddress;
+  cuuint64_t dims[2] = {(cuuint64_t)HD, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)HD * 2};
+  cuuint32_t box[2] = {64, (cuuint32_t)box_rows};
+  cuuint32_t es[2] = {1, 1};
+  return enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<__half*>(base), dims, strides, box, es,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS
+             ? cudaSuccess
+             : cudaErrorInvalidValue;
+}
+
+// q planes [T][nh][256]: 3-D map (dim, head, token) with a box of 64 x 1 x 128.
+cudaError_t map_q(CUtensorMap* m, const __half* base, int64_t T, int nh) {
+  auto enc = attn_encoder();
+  if (!enc) return cudaErrorNotSupported;
+  if (reinterpret_cast<uintptr_t>(base) & 15) return cudaErrorMisalignedAddress;
+  cuuint64_t dims[3] = {(cuuint64_t)HD, (cuuint64_t)nh, (cuuint64_t)T};
+  cuuint64_t strides[2] = {(cuuint64_t)HD * 2, (cuuint64_t)nh * HD * 2};
+  cuuint32_t box[3] = {64, 1, (cuuint32_t)QT};
+  cuuint32_t es[3] = {1, 1, 1};
+  return enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<__half*>(base), dims, strides, box, es,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS
+             ? cudaSuccess
+             : cudaErrorInvalidValue;
+}
+
+bool g_attn_attr[64];
+std::mutex g_attn_mu;
+
+}  // namespace
 
 cudaError_t launch_attention(const __half* qh, const __half* ql, const __half* kh, const __half* kl, const __half* vh,
                              const __half* vl, int num_heads, float scale, SeqMeta meta, AttnTiles tiles, float* out,
-                             uint32_t* absmax, cudaStream_t stream) {
+                             uint32_t* absmax, uint32_t* err, cudaStream_t stream) {
   if (tiles.n_tiles == 0) return cudaSuccess;
-  cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+  const int64_t T = meta.T;
+  CUtensorMap m_qh, m_ql, m_kh, m_kl, m_vh, m_vl;
+  cudaError_t e;
+  if ((e = map_q(&m_qh, qh, T, num_heads)) != cudaSuccess) return e;
+  if ((e = map_q(&m_ql, ql, T, num_heads)) != cudaSuccess) return e;
+  if ((e = map_rows(&m_kh, kh, T, KT)) != cudaSuccess) return e;
+  if ((e = map_rows(&m_kl, kl, T, KT)) != cudaSuccess) return e;
+  if ((e = map_rows(&m_vh, vh, T, KT)) != cudaSuccess) return e;
+  if ((e = map_rows(&m_vl, vl, T, KT)) != cudaSuccess) return e;
+  int dev = 0;
+  if ((e = cudaGetDevice(&dev)) != cudaSuccess) return e;
+  {
+    std::lock_guard<std::mutex> lk(g_attn_mu);
+    if (dev >= 0 && dev < 64 && !g_attn_attr[dev]) {
+      if ((e = cudaFuncSetAttribute(attention_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES)) !=
+          cudaSuccess)
+        return e;
+      g_attn_attr[dev] = true;
+    }
+  }
   dim3 grid(tiles.n_tiles, num_heads);
-  attention_kernel<<<grid, THREADS, SMEM_BYTES, stream>>>(qh, ql, kh, kl, vh, vl, num_heads, scale, meta, tiles, out,
-                                                         absmax);
+  attention_tc_kernel<<<grid, THREADS, SMEM_BYTES, stream>>>(m_qh, m_ql, m_kh, m_kl, m_vh, m_vl, num_heads, scale,
+                                                             meta, tiles, out, absmax, err);
   return cudaGetLastError();
 }
 

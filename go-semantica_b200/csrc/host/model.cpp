@@ -320,7 +320,7 @@ int upload_meta(sem_model* m, const int32_t* offsets, int B, const int32_t* dims
         h_row_seq[r] = s;
         h_row_pos[r] = r - offsets[s];
       }
-      for (int32_t r = offsets[s]; r < offsets[s + 1]; r += 64) {
+      for (int32_t r = offsets[s]; r < offsets[s + 1]; r += kAttnTileRows) {
         h_tseq[nt] = s;
         h_trow[nt] = r;
         ++nt;
@@ -393,7 +393,7 @@ int run_forward(sem_model* m, const int32_t* d_ids, const MetaPtrs& mp, float* d
     SEM_LAUNCH(kStGemmQKV, launch_gemm_q8(codes, w.qkv, w.qkv_s, (int)T, qkvN, H, slot(l, 0), sm.row_seq, big, kEpiStore, nullptr, err, st));
     SEM_LAUNCH(kStQKNormRope, launch_qk_norm_rope(big, w.q_norm, w.k_norm, m->rope_cos, m->rope_sin, c.norm_eps, nh, sm, qh, ql, kh, kl,
                                    vh, vl, st));
-    SEM_LAUNCH(kStAttention, launch_attention(qh, ql, kh, kl, vh, vl, nh, c.attention_scale, sm, mp.tiles, att, slot(l, 1), st));
+    SEM_LAUNCH(kStAttention, launch_attention(qh, ql, kh, kl, vh, vl, nh, c.attention_scale, sm, mp.tiles, att, slot(l, 1), err, st));
     SEM_LAUNCH(kStQuant, launch_quantize(att, nullptr, nullptr, H, sm, slot(l, 1), codes, st));
     SEM_LAUNCH(kStGemmO, launch_gemm_q8(codes, w.o, w.o_s, (int)T, H, H, slot(l, 1), sm.row_seq, big, kEpiStore, nullptr, err, st));
     SEM_LAUNCH(kStResidual, launch_residual_norm(big, w.post_attn, hid, w.ffn_norm, H, c.norm_eps, sm, inv, slot(l, 2), st));

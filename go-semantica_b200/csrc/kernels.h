@@ -84,14 +84,18 @@ cudaError_t launch_gemm_q8(const __half* a_codes, const __half* w_codes, const f
                            uint32_t* out_absmax, uint32_t* err, cudaStream_t stream);
 
 // ---- attention (attention.cu) ----
+constexpr int kAttnTileRows = 128;  // query rows per attention tile
 struct AttnTiles {
-  const int32_t* tile_seq;    // [n_tiles] sequence of each 64-query tile
+  const int32_t* tile_seq;    // [n_tiles] sequence of each 128-query tile
   const int32_t* tile_row0;   // [n_tiles] first packed row of the tile
   int32_t n_tiles;
 };
+// q planes [T][num_heads][256], k and v planes [T][256] (fp16 hi/lo splits),
+// all 16-byte aligned. out [T][num_heads*256] fp32, absmax[seq] atomically.
+// `err` (nullable) receives error bits if a pipeline wait times out.
 cudaError_t launch_attention(const __half* qh, const __half* ql, const __half* kh, const __half* kl,
                              const __half* vh, const __half* vl, int num_heads, float scale, SeqMeta meta,
-                             AttnTiles tiles, float* out, uint32_t* absmax, cudaStream_t stream);
+                             AttnTiles tiles, float* out, uint32_t* absmax, uint32_t* err, cudaStream_t stream);
 
 // ---- brute search (brute_kernels.cu) ----
 // Exact integer scan: scores of nq queries against rows [0, count) of an
