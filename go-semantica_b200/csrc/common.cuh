@@ -96,6 +96,23 @@ __device__ __forceinline__ int quant_code_ref(float x, float inv) {
   return (int)r;
 }
 
+// The same code computed in float32 only (the float64 conversions of
+// quant_code_ref are slow on the GPU). The exact product x * inv equals
+// p + e with p = fl(x * inv) and e = fma(x, inv, -p) (exact). With t = trunc(p),
+// p - t is exact; unless |p - t| is exactly one half, |e| (at most half an ulp
+// of p) cannot move the product across the half, and at exactly one half the
+// sign of e decides. Returns the integer code as a float.
+__device__ __forceinline__ float quant_code_f32(float x, float inv) {
+  const float p = __fmul_rn(x, inv);
+  const float e = __fmaf_rn(x, inv, -p);
+  const float t = truncf(p);
+  const float ad = fabsf(__fsub_rn(p, t));
+  const bool pos = p > 0.0f;
+  const bool away = ad > 0.5f || (ad == 0.5f && (pos ? e >= 0.0f : e <= 0.0f));
+  const float n = away ? (pos ? __fadd_rn(t, 1.0f) : __fsub_rn(t, 1.0f)) : t;
+  return fminf(fmaxf(n, -127.0f), 127.0f);
+}
+
 __device__ __forceinline__ void atomic_max_abs(uint32_t* slot, float v) {
   // non-negative floats order like their bit patterns
   atomicMax(slot, __float_as_uint(fabsf(v)));

@@ -95,9 +95,8 @@ __device__ __forceinline__ void tmem_wait_ld_regs(uint32_t (&r)[16]) {
                : "memory");
 }
 
-// GELUQuick(gate * rs) * (up * rs), kept out of line so that the epilogue's
-// rolled loop stays small.
-__device__ __noinline__ float gelu_up(float g, float u, float rs) {
+// GELUQuick(gate * rs) * (up * rs); called from a rolled loop, so one copy.
+__device__ __forceinline__ float gelu_up(float g, float u, float rs) {
   return __fmul_rn(gelu_quick_ref(__fmul_rn(g, rs)), __fmul_rn(u, rs));
 }
 

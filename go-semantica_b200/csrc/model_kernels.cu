@@ -169,6 +169,18 @@ cudaError_t launch_embed(const int32_t* ids, const int8_t* emb_codes, const floa
 // ---------------------------------------------------------------------------
 // Row statistics: 8 lanes per row, 4 rows per warp.
 // ---------------------------------------------------------------------------
+// Horizontal sum of the 8 lane accumulators of a row group in the order of
+// dotProductAVX2Asm's VEXTRACTF128/VADDPS/VHADDPS tail (simd_amd64.s:19-76).
+__device__ __forceinline__ float group_sum8_avx_order(float acc) {
+  const unsigned full = 0xffffffffu;
+  float hi = __shfl_down_sync(full, acc, 4, 8);
+  float s = __fadd_rn(acc, hi);
+  float s1 = __shfl_down_sync(full, s, 1, 8);
+  float p = __fadd_rn(s, s1);
+  float p2 = __shfl_down_sync(full, p, 2, 8);
+  return __shfl_sync(full, __fadd_rn(p, p2), 0, 8);
+}
+
 __device__ __forceinline__ float group_max8(float v) {
   v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, 1, 8));
   v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, 2, 8));
@@ -234,41 +246,56 @@ cudaError_t launch_row_stats(const float* x, const float* w, int H, float eps, S
 // ---------------------------------------------------------------------------
 // Quantisation with the per-sequence scale; 16 elements per thread.
 // ---------------------------------------------------------------------------
-__global__ void quantize_kernel(const float* __restrict__ x, const float* __restrict__ inv_rms,
-                                const float* __restrict__ w, int K, SeqMeta meta,
-                                const uint32_t* __restrict__ absmax, __half* __restrict__ codes) {
-  int per_row = K / 16;
-  int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= (int64_t)meta.T * per_row) return;
-  int64_t row = i / per_row;
-  int c = (int)(i % per_row) * 16;
-  float scale, inv;
-  seq_scale_ref(absmax[meta.row_seq ? meta.row_seq[row] : 0], &scale, &inv);
-  const float4* xp = reinterpret_cast<const float4*>(x + row * K + c);
-  float v[16];
+// One warp per row: the sequence's scale is computed once, the row moves as
+// 16-byte loads (x, and the norm weight) and 8-byte stores of four fp16 codes.
+constexpr int kQuantWarps = 8;
+constexpr int kQuantBatch = 9;  // float4 loads in flight per lane (a 1152-wide row in one batch)
+
+__global__ void __launch_bounds__(kQuantWarps * 32)
+    quantize_kernel(const float* __restrict__ x, const float* __restrict__ inv_rms, const float* __restrict__ w,
+                    int K, SeqMeta meta, const uint32_t* __restrict__ absmax, __half* __restrict__ codes) {
+  const int lane = threadIdx.x & 31;
+  const int q4 = K / 4;
+  const int64_t nwarps = (int64_t)gridDim.x * kQuantWarps;
+  for (int64_t row = (int64_t)blockIdx.x * kQuantWarps + (threadIdx.x >> 5); row < meta.T; row += nwarps) {
+    float scale, inv;
+    seq_scale_ref(absmax[meta.row_seq ? meta.row_seq[row] : 0], &scale, &inv);
+    const float r = inv_rms ? inv_rms[row] : 0.0f;
+    const float4* xr = reinterpret_cast<const float4*>(x + row * K);
+    for (int seg = 0; seg < q4; seg += 32 * kQuantBatch) {
+    float4 v[kQuantBatch];
 #pragma unroll
-  for (int k = 0; k < 4; ++k) {
-    float4 t = xp[k];
-    v[4 * k] = t.x; v[4 * k + 1] = t.y; v[4 * k + 2] = t.z; v[4 * k + 3] = t.w;
+    for (int b = 0; b < kQuantBatch; ++b) {
+      const int c4 = seg + b * 32 + lane;
+      v[b] = c4 < q4 ? xr[c4] : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+#pragma unroll
+    for (int b = 0; b < kQuantBatch; ++b) {
+      const int c4 = seg + b * 32 + lane;
+      if (c4 >= q4) continue;
+      float e[4] = {v[b].x, v[b].y, v[b].z, v[b].w};
+      if (inv_rms) {
+        const float4 wv = reinterpret_cast<const float4*>(w)[c4];
+        const float ww[4] = {wv.x, wv.y, wv.z, wv.w};
+#pragma unroll
+        for (int k = 0; k < 4; ++k) e[k] = __fmul_rn(__fmul_rn(e[k], r), ww[k]);
+      }
+      __half2 h[2];
+      h[0] = __floats2half2_rn(quant_code_f32(e[0], inv), quant_code_f32(e[1], inv));
+      h[1] = __floats2half2_rn(quant_code_f32(e[2], inv), quant_code_f32(e[3], inv));
+      *reinterpret_cast<uint2*>(codes + row * K + 4 * c4) = *reinterpret_cast<uint2*>(h);
+    }
+    }
   }
-  if (inv_rms) {
-    float r = inv_rms[row];
-#pragma unroll
-    for (int k = 0; k < 16; ++k) v[k] = __fmul_rn(__fmul_rn(v[k], r), w[c + k]);
-  }
-  __align__(16) __half h[16];
-#pragma unroll
-  for (int k = 0; k < 16; ++k) h[k] = __int2half_rn(quant_code_ref(v[k], inv));
-  uint4* dst = reinterpret_cast<uint4*>(codes + row * K + c);
-  dst[0] = reinterpret_cast<const uint4*>(h)[0];
-  dst[1] = reinterpret_cast<const uint4*>(h)[1];
 }
 
 cudaError_t launch_quantize(const float* x, const float* inv_rms, const float* w, int K, SeqMeta meta,
                             const uint32_t* absmax, __half* codes, cudaStream_t stream) {
   if (meta.T == 0) return cudaSuccess;
-  int64_t n = (int64_t)meta.T * (K / 16);
-  quantize_kernel<<<(unsigned)((n + 255) / 256), 256, 0, stream>>>(x, inv_rms, w, K, meta, absmax, codes);
+  if (K % 4 != 0) return cudaErrorInvalidValue;
+  int64_t blocks = (meta.T + kQuantWarps - 1) / kQuantWarps;
+  if (blocks > 148 * 16) blocks = 148 * 16;
+  quantize_kernel<<<(unsigned)blocks, kQuantWarps * 32, 0, stream>>>(x, inv_rms, w, K, meta, absmax, codes);
   return cudaGetLastError();
 }
 
@@ -297,52 +324,97 @@ cudaError_t launch_absmax(const float* x, int64_t n, uint32_t* slot, cudaStream_
 // ---------------------------------------------------------------------------
 constexpr int kHeadDim = 256;
 
-__global__ void qk_norm_rope_kernel(const float* __restrict__ qkv, const float* __restrict__ q_norm,
-                                    const float* __restrict__ k_norm, const float* __restrict__ rope_cos,
-                                    const float* __restrict__ rope_sin, float eps, int nh, SeqMeta meta,
-                                    __half* __restrict__ qh, __half* __restrict__ ql, __half* __restrict__ kh,
-                                    __half* __restrict__ kl, __half* __restrict__ vh, __half* __restrict__ vl) {
-  int lane = threadIdx.x & 31, g = lane >> 3, sub = lane & 7;
-  int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-  int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
-  int ld = (nh + 2) * kHeadDim;
-  for (int64_t row = warp; row < meta.T; row += nwarps) {  // uniform per warp
+constexpr int kHeadPad = kHeadDim + 8;  // head stride in shared memory: 4 heads on distinct banks
+constexpr int kQkWarps = 8;
+
+__global__ void __launch_bounds__(kQkWarps * 32)
+    qk_norm_rope_kernel(const float* __restrict__ qkv, const float* __restrict__ q_norm,
+                        const float* __restrict__ k_norm, const float* __restrict__ rope_cos,
+                        const float* __restrict__ rope_sin, float eps, int nh, SeqMeta meta,
+                        __half* __restrict__ qh, __half* __restrict__ ql, __half* __restrict__ kh,
+                        __half* __restrict__ kl, __half* __restrict__ vh, __half* __restrict__ vl) {
+  __shared__ __align__(16) float sh[kQkWarps][4 * kHeadPad];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, g = lane >> 3, sub = lane & 7;
+  const int64_t nwarps = (int64_t)gridDim.x * kQkWarps;
+  const int ld = (nh + 2) * kHeadDim;
+  float* rowbuf = sh[warp];
+  const bool active = g <= nh;
+  const float* wn = g < nh ? q_norm : k_norm;
+  for (int64_t row = (int64_t)blockIdx.x * kQkWarps + warp; row < meta.T; row += nwarps) {  // uniform per warp
     const float* base = qkv + row * ld;
-    bool active = g <= nh;
-    int gh = active ? g : nh;  // inactive groups mirror the k head and store nothing
-    const float* x = base + gh * kHeadDim;
-    const float* wn = gh < nh ? q_norm : k_norm;
-    float ss = row_sumsq_ref(x, kHeadDim, sub);
-    float inv = rms_inv_ref(ss, kHeadDim, eps);
-    int pos = meta.row_pos[row];
-    const float* cs = rope_cos + (int64_t)pos * (kHeadDim / 2);
-    const float* sn = rope_sin + (int64_t)pos * (kHeadDim / 2);
-    __half* dh = gh < nh ? qh + (row * nh + gh) * kHeadDim : kh + row * kHeadDim;
-    __half* dl = gh < nh ? ql + (row * nh + gh) * kHeadDim : kl + row * kHeadDim;
+    // q heads and the k head into shared memory (64 float4 per head)
+    for (int idx = lane; idx < (nh + 1) * 64; idx += 32) {
+      const int hd = idx >> 6, c4 = idx & 63;
+      *reinterpret_cast<float4*>(rowbuf + hd * kHeadPad + 4 * c4) = reinterpret_cast<const float4*>(base)[idx];
+    }
+    __syncwarp();
+    const float* x = rowbuf + (active ? g : nh) * kHeadPad;
+    float acc = 0.0f;
+#pragma unroll 8
+    for (int v = 0; v < kHeadDim / 8; ++v) {
+      const float t = x[8 * v + sub];
+      acc = fmaf(t, t, acc);
+    }
+    const float inv = rms_inv_ref(group_sum8_avx_order(acc), kHeadDim, eps);
     if (active) {
-#pragma unroll 4
-      for (int v = 0; v < 16; ++v) {
-        int i = 8 * v + sub;
-        // the reference skips a head norm whose weight tensor is absent (model_int8.go:374, :408)
-        float x0 = wn ? __fmul_rn(__fmul_rn(x[i], inv), wn[i]) : x[i];
-        float x1 = wn ? __fmul_rn(__fmul_rn(x[i + 128], inv), wn[i + 128]) : x[i + 128];
-        float c = cs[i], s = sn[i];
-        float r0 = __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, s));
-        float r1 = __fadd_rn(__fmul_rn(x0, s), __fmul_rn(x1, c));
-        __half h, l;
-        split_half(r0, h, l);
-        dh[i] = h; dl[i] = l;
-        split_half(r1, h, l);
-        dh[i + 128] = h; dl[i + 128] = l;
+      const int pos = meta.row_pos[row];
+      const float4* cs = reinterpret_cast<const float4*>(rope_cos + (int64_t)pos * (kHeadDim / 2));
+      const float4* sn = reinterpret_cast<const float4*>(rope_sin + (int64_t)pos * (kHeadDim / 2));
+      __half* dh = g < nh ? qh + (row * nh + g) * kHeadDim : kh + row * kHeadDim;
+      __half* dl = g < nh ? ql + (row * nh + g) * kHeadDim : kl + row * kHeadDim;
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const int i = 4 * sub + 32 * k;  // NeoX pairs (i, i + 128)
+        float a0[4], a1[4];
+        *reinterpret_cast<float4*>(a0) = *reinterpret_cast<const float4*>(x + i);
+        *reinterpret_cast<float4*>(a1) = *reinterpret_cast<const float4*>(x + i + 128);
+        float c[4], s[4];
+        *reinterpret_cast<float4*>(c) = cs[i / 4];
+        *reinterpret_cast<float4*>(s) = sn[i / 4];
+        float w0[4] = {1.f, 1.f, 1.f, 1.f}, w1[4] = {1.f, 1.f, 1.f, 1.f};
+        if (wn) {
+          *reinterpret_cast<float4*>(w0) = reinterpret_cast<const float4*>(wn + i)[0];
+          *reinterpret_cast<float4*>(w1) = reinterpret_cast<const float4*>(wn + i + 128)[0];
+        }
+        __half2 h0[2], l0[2], h1[2], l1[2];
+#pragma unroll
+        for (int u = 0; u < 4; u += 2) {
+          float r0[2], r1[2];
+#pragma unroll
+          for (int z = 0; z < 2; ++z) {
+            // the reference skips a head norm whose weight tensor is absent (model_int8.go:374, :408)
+            const float x0 = wn ? __fmul_rn(__fmul_rn(a0[u + z], inv), w0[u + z]) : a0[u + z];
+            const float x1 = wn ? __fmul_rn(__fmul_rn(a1[u + z], inv), w1[u + z]) : a1[u + z];
+            r0[z] = __fsub_rn(__fmul_rn(x0, c[u + z]), __fmul_rn(x1, s[u + z]));
+            r1[z] = __fadd_rn(__fmul_rn(x0, s[u + z]), __fmul_rn(x1, c[u + z]));
+          }
+          __half a, b, e2, f;
+          split_half(r0[0], a, b);
+          split_half(r0[1], e2, f);
+          h0[u / 2] = __halves2half2(a, e2);
+          l0[u / 2] = __halves2half2(b, f);
+          split_half(r1[0], a, b);
+          split_half(r1[1], e2, f);
+          h1[u / 2] = __halves2half2(a, e2);
+          l1[u / 2] = __halves2half2(b, f);
+        }
+        *reinterpret_cast<uint2*>(dh + i) = *reinterpret_cast<uint2*>(h0);
+        *reinterpret_cast<uint2*>(dl + i) = *reinterpret_cast<uint2*>(l0);
+        *reinterpret_cast<uint2*>(dh + i + 128) = *reinterpret_cast<uint2*>(h1);
+        *reinterpret_cast<uint2*>(dl + i + 128) = *reinterpret_cast<uint2*>(l1);
       }
     }
     // v: all 32 lanes, 8 consecutive elements each
-    const float* vx = base + (nh + 1) * kHeadDim + lane * 8;
+    const float4* vx = reinterpret_cast<const float4*>(base + (nh + 1) * kHeadDim + lane * 8);
+    float vv[8];
+    *reinterpret_cast<float4*>(vv) = vx[0];
+    *reinterpret_cast<float4*>(vv + 4) = vx[1];
     __half hv[8], lv[8];
 #pragma unroll
-    for (int k = 0; k < 8; ++k) split_half(vx[k], hv[k], lv[k]);
+    for (int k = 0; k < 8; ++k) split_half(vv[k], hv[k], lv[k]);
     *reinterpret_cast<uint4*>(vh + row * kHeadDim + lane * 8) = *reinterpret_cast<uint4*>(hv);
     *reinterpret_cast<uint4*>(vl + row * kHeadDim + lane * 8) = *reinterpret_cast<uint4*>(lv);
+    __syncwarp();  // the row buffer is reloaded next
   }
 }
 
@@ -351,10 +423,9 @@ cudaError_t launch_qk_norm_rope(const float* qkv, const float* q_norm, const flo
                                 __half* ql, __half* kh, __half* kl, __half* vh, __half* vl, cudaStream_t stream) {
   if (meta.T == 0) return cudaSuccess;
   if (num_heads < 1 || num_heads > 3) return cudaErrorInvalidValue;
-  int64_t warps = meta.T;
-  int64_t blocks = (warps * 32 + 255) / 256;
-  if (blocks > 148 * 16) blocks = 148 * 16;
-  qk_norm_rope_kernel<<<(unsigned)blocks, 256, 0, stream>>>(qkv, q_norm, k_norm, rope_cos, rope_sin, eps, num_heads,
+  int64_t blocks = (meta.T + kQkWarps - 1) / kQkWarps;
+  if (blocks > 148 * 8) blocks = 148 * 8;
+  qk_norm_rope_kernel<<<(unsigned)blocks, kQkWarps * 32, 0, stream>>>(qkv, q_norm, k_norm, rope_cos, rope_sin, eps, num_heads,
                                                             meta, qh, ql, kh, kl, vh, vl);
   return cudaGetLastError();
 }
@@ -363,58 +434,113 @@ cudaError_t launch_qk_norm_rope(const float* qkv, const float* q_norm, const flo
 // Post-norm + residual (model_int8.go:202-210, :224-232) fused with the next
 // norm's statistics (:194/:216 of the following step, or output_norm :236).
 // ---------------------------------------------------------------------------
-__global__ void residual_norm_kernel(const float* __restrict__ o, const float* __restrict__ post_w,
-                                     float* __restrict__ hidden, const float* __restrict__ next_w, int H, float eps,
-                                     SeqMeta meta, float* __restrict__ inv_rms, uint32_t* __restrict__ absmax) {
-  int lane = threadIdx.x & 31, sub = lane & 7;
-  int64_t group = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 3;
-  int64_t ngroups = ((int64_t)gridDim.x * blockDim.x) >> 3;
-  int64_t rounds = ((int64_t)meta.T + ngroups - 1) / ngroups;
-  for (int64_t it = 0; it < rounds; ++it) {
-    int64_t row = group + it * ngroups;
-    bool valid = row < meta.T;
-    int64_t rr = valid ? row : 0;
-    const float* orow = o + rr * H;
-    float* hrow = hidden + rr * H;
-    float inv1 = rms_inv_ref(row_sumsq_ref(orow, H, sub), H, eps);
-    // new hidden and its sum of squares in the same 8-lane order
-    float acc = 0.0f;
-    for (int v = 0; v < H / 8; ++v) {
-      int e = 8 * v + sub;
-      // an absent post-norm leaves o as it is (model_int8.go:203, :225)
-      float ov = post_w ? __fmul_rn(__fmul_rn(orow[e], inv1), post_w[e]) : orow[e];
-      float nv = __fadd_rn(ov, hrow[e]);
-      if (valid) hrow[e] = nv;
-      acc = fmaf(nv, nv, acc);
+// hidden = rmsnorm(o, post_w) + hidden and the statistics of the new rows
+// (model_int8.go:203-210, :225-232, then the next RMSNorm's inv_rms and the
+// per-sequence absmax of the normed rows). Each warp takes 4 rows at a time:
+// the rows move between global memory and a padded shared-memory copy with
+// 16-byte accesses, and the two sums of squares run from shared memory in the
+// reference's 8-lane order (one 8-lane group per row).
+constexpr int kRnWarps = 4;
+constexpr int kRowPad = 8;  // row stride H + 8 floats puts the 4 row groups of a warp on distinct banks
+constexpr int kRnBatch = 8;  // 16-byte loads in flight per lane
+
+
+__global__ void __launch_bounds__(kRnWarps * 32)
+    residual_norm_kernel(const float* __restrict__ o, const float* __restrict__ post_w, float* __restrict__ hidden,
+                         const float* __restrict__ next_w, int H, float eps, SeqMeta meta,
+                         float* __restrict__ inv_rms, uint32_t* __restrict__ absmax) {
+  extern __shared__ float rn_smem[];
+  const unsigned full = 0xffffffffu;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, g = lane >> 3, sub = lane & 7;
+  const int stride = H + kRowPad, q4 = H / 4;  // float4 per row (a multiple of 32)
+  float* rows = rn_smem + warp * 4 * stride;
+  float* myrow = rows + g * stride;
+  const int64_t nwarps = (int64_t)gridDim.x * kRnWarps;
+  for (int64_t row0 = ((int64_t)blockIdx.x * kRnWarps + warp) * 4; row0 < meta.T; row0 += nwarps * 4) {
+    const int64_t row = row0 + g;
+    const bool valid = row < meta.T;
+    // o rows into shared memory, eight 16-byte loads in flight per lane
+    for (int base = 0; base < 4 * q4; base += 32 * kRnBatch) {
+      float4 v[kRnBatch];
+#pragma unroll
+      for (int b = 0; b < kRnBatch; ++b) {
+        const int idx = base + b * 32 + lane, r = idx / q4, c4 = idx % q4;
+        v[b] = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (idx < 4 * q4 && row0 + r < meta.T) v[b] = reinterpret_cast<const float4*>(o + (row0 + r) * H)[c4];
+      }
+#pragma unroll
+      for (int b = 0; b < kRnBatch; ++b) {
+        const int idx = base + b * 32 + lane, r = idx / q4, c4 = idx % q4;
+        if (idx < 4 * q4) *reinterpret_cast<float4*>(rows + r * stride + 4 * c4) = v[b];
+      }
     }
-    const unsigned full = 0xffffffffu;
-    float hi = __shfl_down_sync(full, acc, 4, 8);
-    float s = __fadd_rn(acc, hi);
-    float s1 = __shfl_down_sync(full, s, 1, 8);
-    float p = __fadd_rn(s, s1);
-    float p2 = __shfl_down_sync(full, p, 2, 8);
-    float tot = __shfl_sync(full, __fadd_rn(p, p2), 0, 8);
-    float inv2 = rms_inv_ref(tot, H, eps);
+    __syncwarp();
+    float acc = 0.0f;
+#pragma unroll 8
+    for (int v = 0; v < H / 8; ++v) {
+      const float t = myrow[8 * v + sub];
+      acc = fmaf(t, t, acc);
+    }
+    const float inv1 = rms_inv_ref(group_sum8_avx_order(acc), H, eps);
+    // new hidden, written back to global memory and over o in shared memory
+    for (int base = 0; base < 4 * q4; base += 32 * kRnBatch) {
+      float4 hv[kRnBatch];
+#pragma unroll
+      for (int b = 0; b < kRnBatch; ++b) {
+        const int idx = base + b * 32 + lane, r = idx / q4, c4 = idx % q4;
+        hv[b] = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (idx < 4 * q4 && row0 + r < meta.T) hv[b] = reinterpret_cast<const float4*>(hidden + (row0 + r) * H)[c4];
+      }
+#pragma unroll
+      for (int b = 0; b < kRnBatch; ++b) {
+        const int idx = base + b * 32 + lane, r = idx / q4, c4 = idx % q4;  // r is warp-uniform (q4 % 32 == 0)
+        if (idx >= 4 * q4) continue;
+        const float i1 = __shfl_sync(full, inv1, 8 * r);
+        float4 ov = *reinterpret_cast<const float4*>(rows + r * stride + 4 * c4);
+        if (post_w) {  // an absent post-norm leaves o as it is (model_int8.go:203, :225)
+          const float4 w = reinterpret_cast<const float4*>(post_w)[c4];
+          ov = make_float4(__fmul_rn(__fmul_rn(ov.x, i1), w.x), __fmul_rn(__fmul_rn(ov.y, i1), w.y),
+                           __fmul_rn(__fmul_rn(ov.z, i1), w.z), __fmul_rn(__fmul_rn(ov.w, i1), w.w));
+        }
+        const float4 h = hv[b];
+        ov = make_float4(__fadd_rn(ov.x, h.x), __fadd_rn(ov.y, h.y), __fadd_rn(ov.z, h.z), __fadd_rn(ov.w, h.w));
+        if (row0 + r < meta.T) reinterpret_cast<float4*>(hidden + (row0 + r) * H)[c4] = ov;
+        *reinterpret_cast<float4*>(rows + r * stride + 4 * c4) = ov;
+      }
+    }
+    __syncwarp();
+    acc = 0.0f;
+#pragma unroll 8
+    for (int v = 0; v < H / 8; ++v) {
+      const float t = myrow[8 * v + sub];
+      acc = fmaf(t, t, acc);
+    }
+    const float inv2 = rms_inv_ref(group_sum8_avx_order(acc), H, eps);
     float m = 0.0f;
     if (absmax) {
-      __syncwarp();
       for (int v = 0; v < H / 8; ++v) {
-        int e = 8 * v + sub;
-        float nv = valid ? hrow[e] : 0.0f;
-        m = fmaxf(m, fabsf(__fmul_rn(__fmul_rn(nv, inv2), next_w[e])));
+        const int e = 8 * v + sub;
+        m = fmaxf(m, fabsf(__fmul_rn(__fmul_rn(myrow[e], inv2), next_w[e])));
       }
-      m = group_max8(m);
+      m = group_max8(valid ? m : 0.0f);
     }
     if (valid && sub == 0) inv_rms[row] = inv2;
     if (absmax) warp_seq_atomic_max(absmax, meta.row_seq, valid ? row : -1, m);
+    __syncwarp();  // the rows are reloaded next
   }
 }
 
 cudaError_t launch_residual_norm(const float* o, const float* post_w, float* hidden, const float* next_w, int H,
                                  float eps, SeqMeta meta, float* inv_rms, uint32_t* absmax, cudaStream_t stream) {
   if (meta.T == 0) return cudaSuccess;
-  residual_norm_kernel<<<row_grid(meta.T), 256, 0, stream>>>(o, post_w, hidden, next_w, H, eps, meta, inv_rms,
-                                                             absmax);
+  if (H % 128 != 0) return cudaErrorInvalidValue;
+  const int smem = kRnWarps * 4 * (H + kRowPad) * 4;
+  cudaError_t e = cudaFuncSetAttribute(residual_norm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e != cudaSuccess) return e;
+  int64_t blocks = (meta.T + 4 * kRnWarps - 1) / (4 * kRnWarps);
+  if (blocks > 148 * 8) blocks = 148 * 8;
+  residual_norm_kernel<<<(unsigned)blocks, kRnWarps * 32, smem, stream>>>(o, post_w, hidden, next_w, H, eps, meta,
+                                                                         inv_rms, absmax);
   return cudaGetLastError();
 }
 

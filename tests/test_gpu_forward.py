@@ -126,3 +126,33 @@ def test_q8_gemm_matches_oracle(ctx):
         got = d_c.cpu().numpy()
         np.testing.assert_allclose(got, ref, rtol=2e-5, atol=2e-5 * np.abs(ref).max())
         w.close()
+
+
+def test_quantize_ties_round_half_away(ctx):
+    # codes that fall exactly on, or one float step either side of, a half
+    # integer: the quantiser rounds the exact product half away from zero
+    # (quantize.go:92-103), which the GPU computes without float64
+    import torch
+    import oracle
+    import runtime
+    rng = np.random.default_rng(21)
+    K, N, M = 768, 128, 48
+    w = runtime.Q8Weight(ctx, synth.q8_0_blocks(rng, N, K), K, N)
+    for absmax in (127.0, 3.7, 0.011):
+        inv = np.float32(1.0) / (np.float32(absmax) / np.float32(127.0))
+        ties = ((rng.integers(-127, 127, (M, K)) + 0.5) / inv).astype(np.float32)
+        pick = rng.integers(0, 3, (M, K))
+        a = np.where(pick == 0, ties, np.where(pick == 1, np.nextafter(ties, np.float32(-1e9)),
+                                               np.nextafter(ties, np.float32(1e9)))).astype(np.float32)
+        a = np.clip(a, -absmax, absmax).astype(np.float32)
+        a[0, 0] = np.float32(absmax)
+        d_a = torch.from_numpy(a).cuda()
+        d_c = torch.empty((M, N), dtype=torch.float32, device="cuda")
+        d_codes = torch.empty((M, K), dtype=torch.float16, device="cuda")
+        d_abs = torch.zeros(4, dtype=torch.int32, device="cuda")
+        torch.cuda.synchronize()
+        w.run(d_a.data_ptr(), M, d_c.data_ptr(), d_codes.data_ptr(), d_abs.data_ptr(), ctx.stream)
+        torch.cuda.synchronize()
+        codes, _ = oracle.quantize_sym_int8(a)
+        np.testing.assert_array_equal(d_codes.cpu().numpy().astype(np.int8), codes)
+    w.close()
