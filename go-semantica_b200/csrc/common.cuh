@@ -15,33 +15,34 @@ namespace sem {
 constexpr float kFloatMagic = 12582912.0f;      // 1.5 * 2^23
 constexpr int kFloatMagicBits = 0x4B400000;     // bit pattern of kFloatMagic
 
-// fastExp (internal/kernels/activation.go:100-145), restated operation by operation.
+// fastExp (internal/kernels/activation.go:100-145), restated operation by
+// operation and without branches: every case is computed and selected, and
+// the truncation int32(y) is taken as trunc(y), whose integer value is read
+// out of the float with a 1.5 * 2^23 add (no float<->int conversion
+// instructions). The results are those of the reference's branchy code.
 __device__ __forceinline__ float fast_exp_ref(float x) {
-  if (x < -10.0f) return 0.0f;
-  if (x > 10.0f) return 22026.4657948f;
-  float y = __fmul_rn(x, 1.442695041f);
-  int ip = (int)y;  // Go int32(y): truncation toward zero
-  float f = __fsub_rn(y, (float)ip);
+  const float y = __fmul_rn(x, 1.442695041f);
+  const float yt = truncf(y);  // == (float)int32(y), truncation toward zero
+  const int ip = __float_as_int(__fadd_rn(yt, 12582912.0f)) - 0x4B400000;
+  const float f = __fsub_rn(y, yt);
   const float c1 = 0.693147180559945f, c2 = 0.240226506959101f, c3 = 0.055504108664821f,
               c4 = 0.009676036358193f;
-  float poly = __fadd_rn(
+  const float poly = __fadd_rn(
       1.0f, __fmul_rn(f, __fadd_rn(c1, __fmul_rn(f, __fadd_rn(c2, __fmul_rn(f, __fadd_rn(c3, __fmul_rn(f, c4))))))));
-  if (ip >= -126 && ip <= 127) return __fmul_rn(poly, __uint_as_float((uint32_t)(ip + 127) << 23));
-  if (ip < -126) return 0.0f;
-  return 3.402823e+38f;
+  float r = __fmul_rn(poly, __uint_as_float((uint32_t)(ip + 127) << 23));
+  r = ip < -126 ? 0.0f : r;
+  r = ip > 127 ? 3.402823e+38f : r;
+  r = x > 10.0f ? 22026.4657948f : r;
+  return x < -10.0f ? 0.0f : r;
 }
 
-// GELUQuickSIMD element (activation.go:47-95): x * sigmoid(1.702 x) through fastExp.
+// GELUQuickSIMD element (activation.go:47-95): x * sigmoid(1.702 x) through
+// fastExp. Both of the reference's branches evaluate fastExp(-|1.702 x|) and
+// divide by 1 + e; only the numerator differs (1, or e for negative x).
 __device__ __forceinline__ float gelu_quick_ref(float x) {
-  float sx = __fmul_rn(1.702f, x);
-  float sig;
-  if (sx >= 0.0f) {
-    float e = fast_exp_ref(-sx);
-    sig = __fdiv_rn(1.0f, __fadd_rn(1.0f, e));
-  } else {
-    float e = fast_exp_ref(sx);
-    sig = __fdiv_rn(e, __fadd_rn(1.0f, e));
-  }
+  const float sx = __fmul_rn(1.702f, x);
+  const float e = fast_exp_ref(-fabsf(sx));
+  const float sig = __fdiv_rn(sx >= 0.0f ? 1.0f : e, __fadd_rn(1.0f, e));
   return __fmul_rn(x, sig);
 }
 

@@ -111,7 +111,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                       const __grid_constant__ CUtensorMap tm_c, const float* __restrict__ ws, int w_rows,
                       int n_per_a, int T, int K, const uint32_t* __restrict__ a_absmax,
                       const int32_t* __restrict__ row_seq, uint32_t* __restrict__ out_absmax,
-                      uint32_t* __restrict__ err) {
+                      uint32_t* __restrict__ err, float* __restrict__ Cout) {
   using G = TileCfg<NA, NT>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
@@ -332,19 +332,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         s_seq[(cur ^ 1) * NT + etid] = nsq;
       }
 
-      // ---- output: 16-token boxes through shared memory and TMA stores ----
+      // ---- output ----
       const int tg0 = grp * TG;  // first token of this group within the tile
+      if (EPI == kEpiStore) {
+        // 16-token boxes through shared memory and TMA stores
 #pragma unroll
-      for (int sbx = 0; sbx < TG / kSubTok; ++sbx) {
-        const int box = NA == 1 ? (nstore & 1) : 0;
-        float* out = gbox + box * (kSubTok * kBM);
-        // the store that last read this box has finished reading it
-        if (leader) {
-          if (NA == 1) bulk_wait_read<1>();
-          else bulk_wait_read<0>();
-        }
-        named_bar_sync(2 + grp, 128);
-        if (EPI == kEpiStore) {
+        for (int sbx = 0; sbx < TG / kSubTok; ++sbx) {
+          float* out = gbox + (nstore & 1) * (kSubTok * kBM);
+          if (leader) bulk_wait_read<1>();  // the store that last read this box is done reading
+          named_bar_sync(2 + grp, 128);
           // dst = sum * inputScale (quantize.go:453)
 #pragma unroll
           for (int p = 0; p < kSubTok / 2; ++p) {
@@ -354,51 +350,84 @@ __global__ void __launch_bounds__(kThreads, 1)
             out[(2 * p) * kBM + ch] = __fmul_rn(v0, c_rs[i]);
             out[(2 * p + 1) * kBM + ch] = __fmul_rn(v1, c_rs[i + 1]);
           }
-        } else {
-          // runMLPINT8 (model_int8.go:523-530): gate and up scaled, GELUQuick(gate) * up,
-          // and the absmax of each sequence's rows for the next quantisation.
-          // gate goes to box 0, up to box 1; h overwrites gate (each thread its own column).
-          float* ubox = gbox + kSubTok * kBM;
+          fence_proxy_async_smem();
+          named_bar_sync(2 + grp, 128);
+          if (leader) {
+            tma_store_2d(&tm_c, out, mt * kBM, t0 + tg0 + sbx * kSubTok);
+            bulk_commit();
+          }
+          ++nstore;
+        }
+      } else {
+        // runMLPINT8 (model_int8.go:523-530): gate and up scaled, GELUQuick(gate) * up,
+        // and the absmax of each sequence's rows for the next quantisation. Gate
+        // and up of 16 tokens go through this thread's own column of two
+        // shared-memory boxes (no other thread touches it), so the GELU loop can
+        // stay short; h leaves with plain coalesced stores (one 128-byte row of
+        // channels per warp and token).
+        float* gb = gbox;
+        float* ub = gbox + kSubTok * kBM;
+        const int j = mt * kBM + ch;
+        int cur = -1;
+        float run = 0.0f;
+#pragma unroll
+        for (int sbx = 0; sbx < TG / kSubTok; ++sbx) {
 #pragma unroll
           for (int p = 0; p < kSubTok / 2; ++p) {
             float g0, g1, u0, u1;
             unpack2(acc[sbx * (kSubTok / 2) + p], g0, g1);
             unpack2(acc[NPA + sbx * (kSubTok / 2) + p], u0, u1);
-            out[(2 * p) * kBM + ch] = g0;
-            out[(2 * p + 1) * kBM + ch] = g1;
-            ubox[(2 * p) * kBM + ch] = u0;
-            ubox[(2 * p + 1) * kBM + ch] = u1;
+            gb[(2 * p) * kBM + ch] = g0;
+            gb[(2 * p + 1) * kBM + ch] = g1;
+            ub[(2 * p) * kBM + ch] = u0;
+            ub[(2 * p + 1) * kBM + ch] = u1;
           }
-          int cur = -1;
-          float run = 0.0f;
-#pragma unroll 1
-          for (int x = 0; x < kSubTok; ++x) {
-            const int i = tg0 + sbx * kSubTok + x;
-            const int sq = c_seq[i];  // the same for every lane: warp-uniform branches
-            if (sq != cur) {
+          const int i0 = tg0 + sbx * kSubTok;
+          const int sq0 = c_seq[i0];  // the same for every lane: warp-uniform branches
+          if (sq0 >= 0 && sq0 == c_seq[i0 + kSubTok - 1]) {
+            // the usual case, 16 tokens of one sequence: no reduction inside the loop,
+            // so the unrolled iterations overlap
+            if (sq0 != cur) {
               if (cur >= 0 && out_absmax) {
                 const float m = warp_max(run);
                 if (lane == 0) atomicMax(&out_absmax[cur], __float_as_uint(m));
               }
-              cur = sq;
+              cur = sq0;
               run = 0.0f;
             }
-            const float h = gelu_up(out[x * kBM + ch], ubox[x * kBM + ch], c_rs[i]);
-            out[x * kBM + ch] = h;
-            if (sq >= 0) run = fmaxf(run, fabsf(h));
-          }
-          if (cur >= 0 && out_absmax) {
-            const float m = warp_max(run);
-            if (lane == 0) atomicMax(&out_absmax[cur], __float_as_uint(m));
+            const float rs = c_rs[i0];  // one sequence, one activation scale
+            float* dst = Cout + (size_t)(t0 + i0) * n_per_a + j;
+#pragma unroll 8
+            for (int x = 0; x < kSubTok; ++x) {
+              const float h = gelu_up(gb[x * kBM + ch], ub[x * kBM + ch], rs);
+              dst[(size_t)x * n_per_a] = h;
+              run = fmaxf(run, fabsf(h));
+            }
+          } else {
+#pragma unroll 1
+            for (int x = 0; x < kSubTok; ++x) {
+              const int i = i0 + x;
+              const int sq = c_seq[i];
+              if (sq != cur) {
+                if (cur >= 0 && out_absmax) {
+                  const float m = warp_max(run);
+                  if (lane == 0) atomicMax(&out_absmax[cur], __float_as_uint(m));
+                }
+                cur = sq;
+                run = 0.0f;
+              }
+              if (sq >= 0) {
+                const float h = gelu_up(gb[x * kBM + ch], ub[x * kBM + ch], c_rs[i]);
+                Cout[(size_t)(t0 + i) * n_per_a + j] = h;
+                run = fmaxf(run, fabsf(h));
+              }
+            }
           }
         }
-        fence_proxy_async_smem();
-        named_bar_sync(2 + grp, 128);
-        if (leader) {
-          tma_store_2d(&tm_c, out, mt * kBM, t0 + tg0 + sbx * kSubTok);
-          bulk_commit();
+        if (cur >= 0 && out_absmax) {
+          const float m = warp_max(run);
+          if (lane == 0) atomicMax(&out_absmax[cur], __float_as_uint(m));
         }
-        ++nstore;
       }
     }
     if (leader) bulk_wait_all();
@@ -488,7 +517,7 @@ cudaError_t launch_tc(int slot, const __half* a_codes, int T, int K, const __hal
   const int total = (n_per_a / kBM) * ((T + NT - 1) / NT);
   const int grid = total < sms ? total : sms;
   kern<<<grid, kThreads, G::kSmem, stream>>>(tm_w, tm_a, tm_c, ws, w_rows, n_per_a, T, K, a_absmax, row_seq,
-                                             out_absmax, err);
+                                             out_absmax, err, c);
   return cudaGetLastError();
 }
 
