@@ -17,15 +17,17 @@
 // factor cancels in the normalisation.
 //
 // One CTA = 128 query rows of one (sequence, head). Q (hi and lo, 128 KB)
-// stays in shared memory; K and V stream through a ring of four 16 KB slots
-// (one fp16 plane of 64 keys x 128 dims each), loaded by TMA. Scores of a
-// 64-key tile land in TMEM (two buffers), O accumulates in TMEM (256 fp32
-// columns). Warp 0 issues TMA, warp 1 the MMAs, warps 4-11 (two per TMEM lane
-// quarter, each half of a tile's keys) do the softmax: they read scores from
-// TMEM, write P = p_hi, p_lo in the 128-byte-swizzled K-major layout the MMA
-// reads, and at the end scale O by 1/sum and store it. V is read MN-major
-// straight from its row-major [token][dim] layout, so sequences may start at
-// any token. All three query heads read the single KV head (GQA) through L2.
+// stays in shared memory; K and V stream through a ring of six 16 KB slots
+// (one fp16 plane of 64 keys x 128 dims each), loaded by TMA. TMEM holds O
+// (256 fp32 columns), the scores of a 64-key tile (two buffers of 64 columns)
+// and P (two buffers of 64 columns: p_hi and p_lo as packed fp16 pairs, row =
+// lane), so the P.V MMAs take their A operand straight from TMEM. Warp 0
+// issues TMA, warp 1 the MMAs, warps 4-11 (two per TMEM lane quarter, each
+// half of a tile's keys) do the softmax with packed fp32 arithmetic: they read
+// scores from TMEM, write P back into TMEM, and at the end scale O by 1/sum
+// and store it. V is read MN-major straight from its row-major [token][dim]
+// layout, so sequences may start at any token. All three query heads read the
+// single KV head (GQA) through L2.
 #include <cudaTypedefs.h>
 
 #include <mutex>
@@ -41,21 +43,21 @@ namespace {
 constexpr int HD = 256;      // head_dim
 constexpr int QT = 128;      // query rows per CTA (TMEM lanes)
 constexpr int KT = 64;       // keys per tile
-constexpr int NSLOT = 4;     // K/V ring slots
+constexpr int NSLOT = 6;     // K/V ring slots
 constexpr int SLOT = KT * 128 * 2;       // 16 KB: 64 keys x 128 dims, one plane
 constexpr int QBLK = QT * 128;           // 16 KB: 128 rows x 64 dims
-constexpr int PPLANE = QT * KT * 2;      // 16 KB: 128 rows x 64 keys
 constexpr int SMEM_Q = 2 * 4 * QBLK;     // hi, lo x 4 dim blocks: 128 KB
-constexpr int SMEM_RING = NSLOT * SLOT;  // 64 KB
-constexpr int SMEM_P = 2 * PPLANE;       // 32 KB
-constexpr int NBAR = 1 + 2 * NSLOT + 2 + 2 + 2 + 1 + 1;  // q, ring full/empty, S full/empty, P full/free, O, drain
-constexpr int SMEM_MISC = 160 + 2 * QT * 4;              // barriers, TMEM address, [2][QT] reductions
-constexpr int SMEM_BYTES = 1024 + SMEM_Q + SMEM_RING + SMEM_P + SMEM_MISC;
+constexpr int SMEM_RING = NSLOT * SLOT;  // 96 KB
+constexpr int NBAR = 1 + 2 * NSLOT + 2 + 2 + 2 + 2 + 1 + 1;  // q, ring full/empty, S full/empty, P full/free, O, drain
+constexpr int SMEM_MISC = 192 + 2 * QT * 4;                  // barriers, TMEM address, [2][QT] reductions
+constexpr int SMEM_BYTES = 1024 + SMEM_Q + SMEM_RING + SMEM_MISC;
 constexpr int THREADS = 384;  // warpgroup 0: TMA, MMA, 2 idle; warpgroups 1-2: softmax / epilogue
 constexpr int SM_WARPS = 8;
-constexpr uint32_t TM_O = 0, TM_S = 256;  // TMEM columns: O [0,256), scores [256,320) and [320,384)
+// TMEM columns: O [0,256), scores [256,320) and [320,384), P [384,448) and
+// [448,512) (p_hi in the first 32 columns of a P buffer, p_lo in the next 32)
+constexpr uint32_t TM_O = 0, TM_S = 256, TM_P = 384;
 static_assert(SMEM_BYTES <= 232448, "shared memory per CTA");
-static_assert(NBAR * 8 + 8 <= 160, "barrier block");
+static_assert(NBAR * 8 + 8 <= 192, "barrier block");
 
 __device__ uint32_t g_attn_error;
 
@@ -67,6 +69,28 @@ __device__ __forceinline__ void tmem_wait_regs(uint32_t (&r)[16]) {
                  "+r"(r[15])
                :
                : "memory");
+}
+
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(
+          taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+      "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+      : "memory");
+}
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+// D[tmem] (+)= A[tmem] x B[smem]^T: A (M = 128 rows = TMEM lanes) packed two
+// fp16 per 32-bit column along K.
+__device__ __forceinline__ void umma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc,
+                                            uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
 }
 
 // Shared-memory descriptor of an MN-major operand tile with 128-byte swizzle:
@@ -94,20 +118,19 @@ __global__ void __launch_bounds__(THREADS, 1)
   uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
   uint8_t* sQ = smem;                      // [plane][dblock][128 rows x 128 B]
   uint8_t* sRing = sQ + SMEM_Q;            // [slot][2 boxes of 64 keys x 128 B]
-  uint8_t* sP = sRing + SMEM_RING;         // [plane][128 rows x 128 B]
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + SMEM_P);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sRing + SMEM_RING);
   uint64_t* qfull = bars;
   uint64_t* rfull = bars + 1;
   uint64_t* rempty = rfull + NSLOT;
   uint64_t* sfull = rempty + NSLOT;
   uint64_t* sempty = sfull + 2;
   uint64_t* pfull = sempty + 2;
-  uint64_t* pfree = pfull + 1;
-  uint64_t* ofull = pfree + 1;
+  uint64_t* pfree = pfull + 2;
+  uint64_t* ofull = pfree + 2;
   uint64_t* drain = ofull + 1;
   uint32_t* s_tmem = reinterpret_cast<uint32_t*>(bars + NBAR);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(s_tmem + 1);
-  float* s_red = reinterpret_cast<float*>(sP + SMEM_P + 160);  // [2 halves][QT]: maxima, later sums
+  float* s_red = reinterpret_cast<float*>(sRing + SMEM_RING + 192);  // [2 halves][QT]: maxima, later sums
   if (!err) err = &g_attn_error;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -124,6 +147,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     mbar_init(sempty, SM_WARPS);
     mbar_init(sempty + 1, SM_WARPS);
     mbar_init(pfull, SM_WARPS);
+    mbar_init(pfull + 1, SM_WARPS);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -227,9 +251,10 @@ __global__ void __launch_bounds__(THREADS, 1)
       };
       // O += P(j) V(j), three terms
       auto pv = [&](int j) -> bool {
-        if (!mbar_wait(pfull, j & 1, abort_flag, err, 2u)) return false;
+        const uint32_t pb = j & 1;
+        if (!mbar_wait(&pfull[pb], (j >> 1) & 1, abort_flag, err, 2u)) return false;
         tc_fence_after();
-        const uint32_t p_hi = smem_u32(sP), p_lo = smem_u32(sP + PPLANE);
+        const uint32_t p_hi = tmem + TM_P + pb * 64, p_lo = p_hi + 32;
         for (int h = 0; h < 2; ++h) {
           uint32_t vh_a, vl_a;
           if (!take_slot(vh_a)) return false;
@@ -242,17 +267,17 @@ __global__ void __launch_bounds__(THREADS, 1)
           const uint32_t d_o = tmem + TM_O + h * 128;
 #pragma unroll
           for (int k16 = 0; k16 < KT / 16; ++k16) {
-            const uint32_t poff = (uint32_t)k16 * 32;    // keys 16k16.. in the 128-byte P row
+            const uint32_t pcol = (uint32_t)k16 * 8;     // keys 16k16.. as 8 packed fp16 columns
             const uint32_t voff = (uint32_t)k16 * 2048;  // two 8-key groups of V rows
             const uint32_t acc0 = (j > 0 || k16 > 0) ? 1u : 0u;
-            umma_f16(d_o, umma_desc_k_sw128(p_hi + poff), umma_desc_mn_sw128(vh_a + voff, SLOT / 2), idesc_pv, acc0);
-            umma_f16(d_o, umma_desc_k_sw128(p_hi + poff), umma_desc_mn_sw128(vl_a + voff, SLOT / 2), idesc_pv, 1u);
-            umma_f16(d_o, umma_desc_k_sw128(p_lo + poff), umma_desc_mn_sw128(vh_a + voff, SLOT / 2), idesc_pv, 1u);
+            umma_f16_ts(d_o, p_hi + pcol, umma_desc_mn_sw128(vh_a + voff, SLOT / 2), idesc_pv, acc0);
+            umma_f16_ts(d_o, p_hi + pcol, umma_desc_mn_sw128(vl_a + voff, SLOT / 2), idesc_pv, 1u);
+            umma_f16_ts(d_o, p_lo + pcol, umma_desc_mn_sw128(vh_a + voff, SLOT / 2), idesc_pv, 1u);
           }
           free_slot();
           free_slot();
         }
-        umma_commit(pfree);
+        umma_commit(&pfree[pb]);
         return true;
       };
       for (int j = 0; ok && j < nkt; ++j) ok = qk(false);
@@ -311,14 +336,14 @@ __global__ void __launch_bounds__(THREADS, 1)
     s_red[half * QT + r] = m;
     named_bar_sync(1, SM_WARPS * 32);
     m = fmaxf(s_red[r], s_red[QT + r]);
-    // ---- pass 2: p = fastExp(s - max), row sums, P for the MMA ----
-    float l = 0.0f;
-    uint8_t* prow_hi = sP + r * 128;
-    uint8_t* prow_lo = sP + PPLANE + r * 128;
+    // ---- pass 2: p = fastExp(s - max), row sums, P (split fp16) into TMEM ----
+    uint64_t l2 = 0;  // two partial row sums (even and odd keys)
+    const uint64_t scale2 = pack2(scale, scale), negm2 = pack2(-m, -m);
     for (int j = 0; j < nkt; ++j) {
       uint32_t col;
       wait_s(col);
-      if (ok && j >= 1) ok = mbar_wait(pfree, (j - 1) & 1, abort_flag, err, 4u);  // PV(j-1) is done with P
+      const uint32_t pb = j & 1;
+      if (ok && j >= 2) ok = mbar_wait(&pfree[pb], ((j >> 1) - 1) & 1, abort_flag, err, 4u);  // PV(j-2) is done
       ok = __all_sync(0xffffffffu, ok);
       if (ok) {
         uint32_t s[2][16];
@@ -328,38 +353,40 @@ __global__ void __launch_bounds__(THREADS, 1)
         reg_barrier16(s[1]);
         release_s();
         uint32_t ph[16], pl[16];  // 32 keys as packed fp16 pairs
+        const int kbase = j * KT + half * 32;
 #pragma unroll
         for (int c = 0; c < 32; c += 2) {
-          float p2[2];
-#pragma unroll
-          for (int x = 0; x < 2; ++x) {
-            const int key = j * KT + half * 32 + c + x;
-            const float sc = __fmul_rn(__uint_as_float(s[(c + x) >> 4][(c + x) & 15]), scale);  // attention.go:300
-            p2[x] = key < n_keys ? fast_exp_ref(__fsub_rn(sc, m)) : 0.0f;
-            l = __fadd_rn(l, p2[x]);
+          // score *= scale (attention.go:300), then fastExp(score - max)
+          const uint64_t sc = mul2(pack2u(s[c >> 4][c & 15], s[c >> 4][(c & 15) + 1]), scale2);
+          uint64_t p2 = fast_exp_ref2(add2(sc, negm2));
+          if (kbase + c + 1 >= n_keys) {  // keys past the sequence end weigh nothing
+            float a, b;
+            unpack2(p2, a, b);
+            p2 = pack2(kbase + c < n_keys ? a : 0.0f, 0.0f);
           }
-          __half h0, l0, h1, l1;
-          split_half(p2[0], h0, l0);
-          split_half(p2[1], h1, l1);
-          ph[c >> 1] = (uint32_t)__half_as_ushort(h0) | ((uint32_t)__half_as_ushort(h1) << 16);
-          pl[c >> 1] = (uint32_t)__half_as_ushort(l0) | ((uint32_t)__half_as_ushort(l1) << 16);
+          l2 = add2(l2, p2);
+          float a, b;
+          unpack2(p2, a, b);
+          const __half2 hi = __floats2half2_rn(a, b);
+          const float2 back = __half22float2(hi);
+          const __half2 lo = __floats2half2_rn(__fsub_rn(a, back.x), __fsub_rn(b, back.y));
+          ph[c >> 1] = *reinterpret_cast<const uint32_t*>(&hi);
+          pl[c >> 1] = *reinterpret_cast<const uint32_t*>(&lo);
         }
-        // 16-byte chunk c of the row goes to chunk (c ^ (row & 7)): the 128-byte swizzle
-#pragma unroll
-        for (int cc = 0; cc < 4; ++cc) {
-          const int chunk = (half * 4 + cc) ^ (r & 7);
-          *reinterpret_cast<uint4*>(prow_hi + chunk * 16) =
-              make_uint4(ph[4 * cc], ph[4 * cc + 1], ph[4 * cc + 2], ph[4 * cc + 3]);
-          *reinterpret_cast<uint4*>(prow_lo + chunk * 16) =
-              make_uint4(pl[4 * cc], pl[4 * cc + 1], pl[4 * cc + 2], pl[4 * cc + 3]);
-        }
-        fence_proxy_async_smem();  // generic-proxy writes before the tensor core reads P
+        const uint32_t pcol = t_lane + TM_P + pb * 64 + half * 16;
+        tmem_st16(pcol, ph);
+        tmem_st16(pcol + 32, pl);
+        tmem_wait_st();
       } else {
         release_s();
       }
+      tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(pfull);
+      if (lane == 0) mbar_arrive(&pfull[pb]);
     }
+    float l0, l1;
+    unpack2(l2, l0, l1);
+    const float l = __fadd_rn(l0, l1);
     // ---- epilogue: O / sum, store, absmax ----
     named_bar_sync(1, SM_WARPS * 32);  // every thread has read its row max from s_red
     s_red[half * QT + r] = l;

@@ -181,6 +181,47 @@ __device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
   return d;
 }
 
+__device__ __forceinline__ uint64_t mul2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ uint64_t sub2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+
+// fastExp of a pair (fast_exp_ref on each element, same roundings) with packed
+// fp32 arithmetic. For |x| <= 10 the exponent int32(x * log2e) lies in
+// [-15, 15], so only the two argument clamps remain.
+__device__ __forceinline__ uint64_t fast_exp_ref2(uint64_t x2) {
+  const uint64_t y2 = mul2(x2, pack2(1.442695041f, 1.442695041f));
+  float y0, y1;
+  unpack2(y2, y0, y1);
+  const uint64_t yt2 = pack2(truncf(y0), truncf(y1));
+  float m0, m1;
+  unpack2(add2(yt2, pack2(12582912.0f, 12582912.0f)), m0, m1);
+  const int ip0 = __float_as_int(m0) - 0x4B400000, ip1 = __float_as_int(m1) - 0x4B400000;
+  const uint64_t f2 = sub2(y2, yt2);
+  uint64_t t = mul2(f2, pack2(0.009676036358193f, 0.009676036358193f));
+  t = add2(pack2(0.055504108664821f, 0.055504108664821f), t);
+  t = mul2(f2, t);
+  t = add2(pack2(0.240226506959101f, 0.240226506959101f), t);
+  t = mul2(f2, t);
+  t = add2(pack2(0.693147180559945f, 0.693147180559945f), t);
+  t = mul2(f2, t);
+  t = add2(pack2(1.0f, 1.0f), t);
+  float r0, r1;
+  unpack2(mul2(t, pack2(__uint_as_float((uint32_t)(ip0 + 127) << 23), __uint_as_float((uint32_t)(ip1 + 127) << 23))),
+          r0, r1);
+  float x0, x1;
+  unpack2(x2, x0, x1);
+  r0 = x0 > 10.0f ? 22026.4657948f : (x0 < -10.0f ? 0.0f : r0);
+  r1 = x1 > 10.0f ? 22026.4657948f : (x1 < -10.0f ? 0.0f : r1);
+  return pack2(r0, r1);
+}
+
 // Splits x into hi + lo halves (hi = fp16(x), lo = fp16(x - hi)) for the
 // three-term fp16 products that give near-fp32 accuracy on the tensor cores.
 __device__ __forceinline__ void split_half(float x, __half& hi, __half& lo) {
