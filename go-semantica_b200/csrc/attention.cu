@@ -48,8 +48,10 @@ constexpr int SLOT = KT * 128 * 2;       // 16 KB: 64 keys x 128 dims, one plane
 constexpr int QBLK = QT * 128;           // 16 KB: 128 rows x 64 dims
 constexpr int SMEM_Q = 2 * 4 * QBLK;     // hi, lo x 4 dim blocks: 128 KB
 constexpr int SMEM_RING = NSLOT * SLOT;  // 96 KB
-constexpr int NBAR = 1 + 2 * NSLOT + 2 + 2 + 2 + 2 + 1 + 1;  // q, ring full/empty, S full/empty, P full/free, O, drain
-constexpr int SMEM_MISC = 192 + 2 * QT * 4;                  // barriers, TMEM address, [2][QT] reductions
+constexpr int NS1 = 4;  // score buffers of pass 1 (in the O columns, unused until pass 2)
+// q, ring full/empty, S full/empty, P full/free, O, drain, pass-1 S full/empty
+constexpr int NBAR = 1 + 2 * NSLOT + 2 + 2 + 2 + 2 + 1 + 1 + 2 * NS1;
+constexpr int SMEM_MISC = 256 + 2 * QT * 4;  // barriers, TMEM address, [2][QT] reductions
 constexpr int SMEM_BYTES = 1024 + SMEM_Q + SMEM_RING + SMEM_MISC;
 constexpr int THREADS = 384;  // warpgroup 0: TMA, MMA, 2 idle; warpgroups 1-2: softmax / epilogue
 constexpr int SM_WARPS = 8;
@@ -57,7 +59,7 @@ constexpr int SM_WARPS = 8;
 // [448,512) (p_hi in the first 32 columns of a P buffer, p_lo in the next 32)
 constexpr uint32_t TM_O = 0, TM_S = 256, TM_P = 384;
 static_assert(SMEM_BYTES <= 232448, "shared memory per CTA");
-static_assert(NBAR * 8 + 8 <= 192, "barrier block");
+static_assert(NBAR * 8 + 8 <= 256, "barrier block");
 
 __device__ uint32_t g_attn_error;
 
@@ -128,13 +130,17 @@ __global__ void __launch_bounds__(THREADS, 1)
   uint64_t* pfree = pfull + 2;
   uint64_t* ofull = pfree + 2;
   uint64_t* drain = ofull + 1;
+  uint64_t* s1full = drain + 1;
+  uint64_t* s1empty = s1full + NS1;
   uint32_t* s_tmem = reinterpret_cast<uint32_t*>(bars + NBAR);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(s_tmem + 1);
-  float* s_red = reinterpret_cast<float*>(sRing + SMEM_RING + 192);  // [2 halves][QT]: maxima, later sums
+  float* s_red = reinterpret_cast<float*>(sRing + SMEM_RING + 256);  // [2 halves][QT]: maxima, later sums
   if (!err) err = &g_attn_error;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int tile = blockIdx.x, head = blockIdx.y;
+  // heads vary fastest, so the CTAs of one sequence (query tiles x heads) run
+  // together and read its K and V from L2 rather than from DRAM
+  const int tile = blockIdx.x / nh, head = blockIdx.x % nh;
   const int seq = tiles.tile_seq[tile];
   const int row0 = tiles.tile_row0[tile];
   const int s_beg = meta.cu_seqlens[seq], s_end = meta.cu_seqlens[seq + 1];
@@ -148,6 +154,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     mbar_init(sempty + 1, SM_WARPS);
     mbar_init(pfull, SM_WARPS);
     mbar_init(pfull + 1, SM_WARPS);
+    for (int k = 0; k < NS1; ++k) mbar_init(&s1empty[k], SM_WARPS);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -215,12 +222,26 @@ __global__ void __launch_bounds__(THREADS, 1)
         return true;
       };
       auto free_slot = [&]() { umma_commit(&rempty[it % NSLOT]); ++it; };
-      // S[buf] = scores of key tile j (terms: 1 in pass 1, 3 in pass 2)
+      // S[buf] = scores of key tile j: pass 1 (one term) cycles through NS1
+      // buffers in the O columns, pass 2 (three terms) through two at TM_S
+      uint32_t fill1 = 0;
       auto qk = [&](bool three) -> bool {
-        const uint32_t b = sfill & 1, ub = sfill >> 1;
-        if (!mbar_wait(&sempty[b], (ub & 1) ^ 1, abort_flag, err, 2u)) return false;
+        uint32_t d_s;
+        uint64_t* full_bar;
+        if (three) {
+          const uint32_t b = sfill & 1, ub = sfill >> 1;
+          if (!mbar_wait(&sempty[b], (ub & 1) ^ 1, abort_flag, err, 2u)) return false;
+          d_s = tmem + TM_S + b * KT;
+          full_bar = &sfull[b];
+          ++sfill;
+        } else {
+          const uint32_t b = fill1 % NS1, ub = fill1 / NS1;
+          if (!mbar_wait(&s1empty[b], (ub & 1) ^ 1, abort_flag, err, 2u)) return false;
+          d_s = tmem + TM_O + b * KT;
+          full_bar = &s1full[b];
+          ++fill1;
+        }
         tc_fence_after();
-        const uint32_t d_s = tmem + TM_S + b * KT;
         for (int h = 0; h < 2; ++h) {
           uint32_t kh_a, kl_a = 0;
           if (!take_slot(kh_a)) return false;
@@ -245,8 +266,7 @@ __global__ void __launch_bounds__(THREADS, 1)
           free_slot();
           if (three) free_slot();
         }
-        umma_commit(&sfull[b]);
-        ++sfill;
+        umma_commit(full_bar);
         return true;
       };
       // O += P(j) V(j), three terms
@@ -281,6 +301,11 @@ __global__ void __launch_bounds__(THREADS, 1)
         return true;
       };
       for (int j = 0; ok && j < nkt; ++j) ok = qk(false);
+      // the softmax has read every pass-1 buffer before P.V overwrites the O columns
+      for (int k = 0; ok && k < NS1 && k < nkt; ++k) {
+        const int last = k + NS1 * ((nkt - 1 - k) / NS1);
+        ok = mbar_wait(&s1empty[k], (last / NS1) & 1, abort_flag, err, 2u);
+      }
       for (int j = 0; ok && j <= nkt; ++j) {
         if (j < nkt) ok = qk(true);
         if (ok && j >= 1) ok = pv(j - 1);
@@ -315,22 +340,29 @@ __global__ void __launch_bounds__(THREADS, 1)
     // ---- pass 1: row max of the fp16 scores ----
     float m = -INFINITY;
     for (int j = 0; j < nkt; ++j) {
-      uint32_t col;
-      wait_s(col);
+      const uint32_t b = j % NS1;
+      if (ok) ok = mbar_wait(&s1full[b], (j / NS1) & 1, abort_flag, err, 4u);
+      ok = __all_sync(0xffffffffu, ok);
+      tc_fence_after();
       if (ok) {
         uint32_t s[2][16];
+        const uint32_t col = TM_O + b * KT + half * 32;
         tmem_ld16_w(t_lane + col, s[0]);
         tmem_ld16_w(t_lane + col + 16, s[1]);
         tmem_wait_regs(s[0]);
         reg_barrier16(s[1]);
-        release_s();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&s1empty[b]);
 #pragma unroll
         for (int c = 0; c < 32; ++c) {
           const int key = j * KT + half * 32 + c;
           if (key < n_keys) m = fmaxf(m, __fmul_rn(__uint_as_float(s[c >> 4][c & 15]), scale));
         }
       } else {
-        release_s();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&s1empty[b]);
       }
     }
     s_red[half * QT + r] = m;
@@ -510,7 +542,7 @@ cudaError_t launch_attention(const __half* qh, const __half* ql, const __half* k
       g_attn_attr[dev] = true;
     }
   }
-  dim3 grid(tiles.n_tiles, num_heads);
+  dim3 grid(tiles.n_tiles * num_heads);
   attention_tc_kernel<<<grid, THREADS, SMEM_BYTES, stream>>>(m_qh, m_ql, m_kh, m_kl, m_vh, m_vl, num_heads, scale,
                                                              meta, tiles, out, absmax, err);
   return cudaGetLastError();
