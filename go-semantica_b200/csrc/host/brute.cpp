@@ -69,6 +69,20 @@ int search_keys(sem_index* x, const void* d_queries, int nq, int k, int mode, in
                 cudaStream_t st) {
   if (mode == SEM_SEARCH_EXACT && x->quant == 0)
     return set_error(SEM_EINVAL, "brute: exact search needs an int8 or int16 index");
+  if (mode == SEM_SEARCH_EXACT && scan_exact_tc_supported(elem_size(x->quant), x->row_bytes, k, x->data.p, d_queries)) {
+    // int8 rows: the tensor-core scan (exact int32 scores)
+    const TcScanPlan tp = plan_scan_exact_tc(x->count, nq);
+    const size_t need = (size_t)nq * tp.n_parts * k * sizeof(uint64_t);
+    SEM_CUDA(x->cand.ensure(need > 0 ? need : 8));
+    uint64_t* cand = x->cand.as<uint64_t>();
+    cudaError_t e = launch_scan_exact_tc(x->data.p, x->count, x->row_bytes, d_queries, nq, k, tp, row_base, cand,
+                                         nullptr, st);
+    if (e != cudaSuccess) return set_error(SEM_EDEVICE, "scan: %s", cudaGetErrorString(e));
+    e = launch_topk_merge(cand, tp.n_parts, k, (int64_t)tp.n_parts * k, nq, k, k, false, elem_size(x->quant), nullptr,
+                          nullptr, nullptr, d_keys, st);
+    if (e != cudaSuccess) return set_error(SEM_EDEVICE, "merge: %s", cudaGetErrorString(e));
+    return SEM_OK;
+  }
   ScanPlan plan = plan_for(x->count, nq);
   plan.row_base = row_base;
   size_t need = (size_t)nq * plan.chunks * k * sizeof(uint64_t);
@@ -122,7 +136,8 @@ int index_create(sem_context* ctx, int32_t dim, int32_t quant, const void* data,
   std::lock_guard<std::mutex> lk(ctx->mu);
   const size_t src_row = (size_t)dim * elem_size(quant);
   SEM_CUDA(cudaMemset2DAsync(x->data.p, x->row_bytes, 0, x->row_bytes, (size_t)count, ctx->stream));
-  SEM_CUDA(cudaMemcpy2DAsync(x->data.p, x->row_bytes, data, src_row, src_row, (size_t)count, cudaMemcpyHostToDevice,
+  // host or device source (unified addressing)
+  SEM_CUDA(cudaMemcpy2DAsync(x->data.p, x->row_bytes, data, src_row, src_row, (size_t)count, cudaMemcpyDefault,
                              ctx->stream));
   SEM_CUDA(cudaStreamSynchronize(ctx->stream));
   *out = x.release();

@@ -116,6 +116,22 @@ cudaError_t launch_scan_float(const void* corpus, int elem, int64_t count, int d
 cudaError_t launch_topk_merge(const uint64_t* cand, int lists, int64_t list_stride, int64_t q_stride, int nq, int k,
                               int k_out, bool float_keys, int elem, int32_t* out_rows, int32_t* out_scores,
                               float* out_dist, uint64_t* out_keys, cudaStream_t stream);
+// Exact int8 scan on the tensor cores (search_tc.cu): corpus rows and query
+// codes are row_bytes apart (row_bytes >= 128, a multiple of 16, at most 1024),
+// k <= 16. Writes k candidate keys per (query, part) to
+// cand[(q * n_parts + part) * k], merged by launch_topk_merge with
+// lists = n_parts, list_stride = k, q_stride = n_parts * k.
+struct TcScanPlan {
+  int32_t n_qtiles;        // 128-query tiles
+  int32_t n_parts;         // contiguous corpus parts
+  int64_t rows_per_part;   // a multiple of 256
+};
+bool scan_exact_tc_supported(int elem, int row_bytes, int k, const void* corpus, const void* qcodes);
+TcScanPlan plan_scan_exact_tc(int64_t count, int nq);
+cudaError_t launch_scan_exact_tc(const void* corpus, int64_t count, int row_bytes, const void* qcodes, int nq, int k,
+                                 TcScanPlan plan, int64_t row_base, uint64_t* cand, uint32_t* err,
+                                 cudaStream_t stream);
+
 // Row-wise normalize (optional) + quantize (quant 1/2) or copy (quant 0) into
 // rows of out_row_bytes (zero padded).
 cudaError_t launch_normalize_quantize(const float* in, int64_t count, int dim, int quant, int out_row_bytes,

@@ -1,0 +1,363 @@
+// search/brute exact scan on the sm_100a tensor cores (Index.searchNormalized,
+// search/brute/index.go:55-154, under the integer contract: the query is
+// quantised like the stored rows, quant.go:17-41, and scores are exact int32
+// dot products).
+//
+// int8 rows x int8 queries on tcgen05.mma.kind::i8 with int32 accumulators in
+// TMEM: the scores are exact, as in the CUDA-core scan. One CTA = 128 queries
+// (TMEM lanes, the query codes resident in shared memory) x one contiguous part
+// of the corpus, streamed as 256-row tiles through a TMA ring of 128-byte K
+// slices; TMEM holds two score tiles so the MMAs of tile t+1 overlap the
+// top-k filter of tile t. Warp 0 issues TMA, warp 1 the MMAs, warps 4-11 (two
+// per TMEM lane quarter, each half of a tile's rows) keep a per-query top-16
+// in registers: rows arrive in ascending order, so a candidate only enters
+// when its score is strictly above the 16th best (a tie never beats a lower
+// row). The two halves merge in shared memory and emit one list of k keys per
+// (query, part); topk_merge_kernel merges the parts. CTAs are numbered part-
+// major, so the query tiles that read one corpus part run together and share
+// it through L2.
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
+#include "common.cuh"
+#include "kernels.h"
+#include "sm100.cuh"
+
+namespace sem {
+
+namespace {
+
+constexpr int SQ = 128;                 // queries per CTA
+constexpr int SN = 256;                 // corpus rows per tile
+constexpr int SKB = 128;                // K bytes per stage / query box
+constexpr int S_TILE = SN * SKB;        // 32 KB
+constexpr int S_QBOX = SQ * SKB;        // 16 KB
+constexpr int S_THREADS = 384;
+constexpr int S_EPI_WARPS = 8;
+constexpr int S_KMAX = 16;
+constexpr int S_MAX_QBOX = 8;           // D <= 1024
+constexpr int S_BAR_BYTES = 256;
+
+__device__ uint32_t g_search_error;
+
+__device__ __forceinline__ void umma_i8(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                        uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// kind::i8: signed A and B, s32 accumulator, M x N.
+__host__ __device__ constexpr uint32_t idesc_i8(int M, int N) {
+  return (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+
+__device__ __forceinline__ void wait_ld16(uint32_t (&r)[16]) {
+  asm volatile("tcgen05.wait::ld.sync.aligned;"
+               : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
+                 "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]),
+                 "+r"(r[15])
+               :
+               : "memory");
+}
+
+struct Top16 {
+  uint64_t v[S_KMAX];  // best first; 0 = empty
+  __device__ __forceinline__ void init() {
+#pragma unroll
+    for (int i = 0; i < S_KMAX; ++i) v[i] = 0;
+  }
+  __device__ __forceinline__ void insert(uint64_t key) {
+    v[S_KMAX - 1] = key;
+#pragma unroll
+    for (int i = S_KMAX - 1; i > 0; --i)
+      if (v[i] > v[i - 1]) {
+        const uint64_t t = v[i];
+        v[i] = v[i - 1];
+        v[i - 1] = t;
+      }
+  }
+};
+
+}  // namespace
+
+__global__ void __launch_bounds__(S_THREADS, 1)
+    search_tc_kernel(const __grid_constant__ CUtensorMap tm_c, const __grid_constant__ CUtensorMap tm_q,
+                     int64_t count, int nqb, int nst, int nq, int k, int64_t rows_per_part, int n_qtiles,
+                     int n_parts, int64_t row_base, uint64_t* __restrict__ cand, uint32_t* __restrict__ err) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
+  uint8_t* sQ = smem;                    // nqb boxes of 128 queries x 128 bytes
+  uint8_t* sRing = sQ + nqb * S_QBOX;    // nst tiles of 256 rows x 128 bytes
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sRing + nst * S_TILE);
+  uint64_t* qfull = bars;
+  uint64_t* rfull = bars + 1;
+  uint64_t* rempty = rfull + 4;
+  uint64_t* tfull = rempty + 4;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* drain = tempty + 2;
+  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(s_tmem + 1);
+  if (!err) err = &g_search_error;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int part = blockIdx.x / n_qtiles, qt = blockIdx.x % n_qtiles;
+  const int64_t r0 = (int64_t)part * rows_per_part;
+  const int64_t r1 = min(count, r0 + rows_per_part);
+  const int ntiles = r0 < r1 ? (int)((r1 - r0 + SN - 1) / SN) : 0;
+
+  if (threadIdx.x == 0) {
+    mbar_init(qfull, 1);
+    for (int s = 0; s < 4; ++s) {
+      mbar_init(&rfull[s], 1);
+      mbar_init(&rempty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], S_EPI_WARPS);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) tmem_alloc(s_tmem, 512);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *s_tmem;
+
+  if (warp < 4) {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 56;");
+    if (warp == 0 && lane == 0) {
+      // ---------------- TMA producer ----------------
+      mbar_arrive_expect_tx(qfull, nqb * S_QBOX);
+      for (int b = 0; b < nqb; ++b) tma_load_2d(&tm_q, qfull, sQ + b * S_QBOX, b * SKB, qt * SQ);
+      uint32_t it = 0;
+      bool ok = true;
+      for (int t = 0; ok && t < ntiles; ++t)
+        for (int b = 0; b < nqb; ++b, ++it) {
+          const uint32_t s = it % nst, u = it / nst;
+          if (!mbar_wait(&rempty[s], (u & 1) ^ 1, abort_flag, err, 1u)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&rfull[s], S_TILE);
+          tma_load_2d(&tm_c, &rfull[s], sRing + s * S_TILE, b * SKB, (int)(r0 + (int64_t)t * SN));
+        }
+      for (uint32_t j = it > (uint32_t)nst ? it - nst : 0; j < it; ++j)
+        mbar_wait_drain(&rfull[j % nst], (j / nst) & 1);
+      mbar_wait_drain(qfull, 0);
+    } else if (warp == 1 && lane == 0) {
+      // ---------------- MMA issuer ----------------
+      constexpr uint32_t idesc = idesc_i8(SQ, SN);
+      bool ok = mbar_wait(qfull, 0, abort_flag, err, 2u);
+      tc_fence_after();
+      const uint32_t q0 = smem_u32(sQ);
+      uint32_t it = 0;
+      for (int t = 0; ok && t < ntiles; ++t) {
+        const uint32_t b = t & 1, ub = t >> 1;
+        if (!mbar_wait(&tempty[b], (ub & 1) ^ 1, abort_flag, err, 2u)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        for (int kb = 0; kb < nqb; ++kb, ++it) {
+          const uint32_t s = it % nst, u = it / nst;
+          if (!mbar_wait(&rfull[s], u & 1, abort_flag, err, 2u)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t ca = smem_u32(sRing + s * S_TILE);
+#pragma unroll
+          for (int k32 = 0; k32 < SKB / 32; ++k32)
+            umma_i8(tmem + b * SN, umma_desc_k_sw128(q0 + kb * S_QBOX + k32 * 32),
+                    umma_desc_k_sw128(ca + k32 * 32), idesc, (kb | k32) ? 1u : 0u);
+          umma_commit(&rempty[s]);
+        }
+        if (!ok) break;
+        umma_commit(&tfull[b]);
+      }
+      umma_commit(drain);
+      mbar_wait_drain(drain, 0);
+    }
+  } else {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 152;");
+    // ---------------- top-k filter ----------------
+    const int w = warp - 4;
+    const int q = warp & 3;     // TMEM lane quarter
+    const int half = w >> 2;    // rows [128 * half, +128) of each tile
+    const int lq = q * 32 + lane;  // query within the tile
+    const uint32_t t_lane = tmem + ((uint32_t)(q * 32) << 16);
+    Top16 top;
+    top.init();
+    bool ok = true;
+    for (int t = 0; t < ntiles; ++t) {
+      const uint32_t b = t & 1, ub = t >> 1;
+      if (ok) ok = mbar_wait(&tfull[b], ub & 1, abort_flag, err, 4u);
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) continue;
+      tc_fence_after();
+      const int64_t rbase = r0 + (int64_t)t * SN + half * 128;
+      // scores of 128 rows: 8 chunks of 16, two loads in flight per wait
+#pragma unroll
+      for (int cp = 0; cp < 4; ++cp) {
+        uint32_t sc[2][16];
+        tmem_ld16(t_lane + b * SN + half * 128 + cp * 32, sc[0]);
+        tmem_ld16(t_lane + b * SN + half * 128 + cp * 32 + 16, sc[1]);
+        wait_ld16(sc[0]);
+        reg_barrier16(sc[1]);
+        if (cp == 3) {  // every score of this buffer is in registers
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&tempty[b]);
+        }
+        const uint32_t thr = (uint32_t)(top.v[S_KMAX - 1] >> 32);
+#pragma unroll
+        for (int x = 0; x < 32; ++x) {
+          const uint32_t biased = sc[x >> 4][x & 15] ^ 0x80000000u;  // order-preserving score bits
+          if (biased > thr) {
+            const int64_t row = rbase + cp * 32 + x;
+            if (row < r1) top.insert(((uint64_t)biased << 32) | (uint64_t)(0xffffffffu - (uint32_t)(row_base + row)));
+          }
+        }
+      }
+    }
+    // both halves of each query -> one list of k keys per (query, part)
+    named_bar_sync(1, S_EPI_WARPS * 32);  // every tile consumed: the ring is free for the merge
+    uint64_t* sk = reinterpret_cast<uint64_t*>(sRing);  // [SQ][S_KMAX], half 1's lists
+    if (half == 1) {
+#pragma unroll
+      for (int i = 0; i < S_KMAX; ++i) sk[lq * S_KMAX + i] = top.v[i];
+    }
+    named_bar_sync(1, S_EPI_WARPS * 32);
+    const int64_t qg = (int64_t)qt * SQ + lq;
+    if (half == 0 && qg < nq) {
+      uint64_t* dst = cand + ((int64_t)qg * n_parts + part) * k;
+      const uint64_t* other = sk + lq * S_KMAX;
+      int ib = 0;
+      for (int i = 0; i < k; ++i) {
+        const uint64_t bk = ib < S_KMAX ? other[ib] : 0;
+        if (top.v[0] >= bk) {  // keys are unique except empty (0) entries
+          dst[i] = top.v[0];
+#pragma unroll
+          for (int j = 0; j < S_KMAX - 1; ++j) top.v[j] = top.v[j + 1];
+          top.v[S_KMAX - 1] = 0;
+        } else {
+          dst[i] = bk;
+          ++ib;
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+namespace {
+
+PFN_cuTensorMapEncodeTiled_v12000 search_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult qr;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &qr) == cudaSuccess &&
+        qr == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+cudaError_t map_bytes(CUtensorMap* m, const void* base, int64_t rows, int row_bytes, int box_rows) {
+  auto enc = search_encoder();
+  if (!enc) return cudaErrorNotSupported;
+  cuuint64_t dims[2] = {(cuuint64_t)row_bytes, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)row_bytes};
+  cuuint32_t box[2] = {(cuuint32_t)SKB, (cuuint32_t)box_rows};
+  cuuint32_t es[2] = {1, 1};
+  return enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, es,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS
+             ? cudaSuccess
+             : cudaErrorInvalidValue;
+}
+
+int g_search_sms[64];
+bool g_search_attr[64];
+std::mutex g_search_mu;
+
+}  // namespace
+
+bool scan_exact_tc_supported(int elem, int row_bytes, int k, const void* corpus, const void* qcodes) {
+  return elem == 1 && row_bytes >= SKB && (row_bytes + SKB - 1) / SKB <= S_MAX_QBOX && k >= 1 && k <= S_KMAX &&
+         !(reinterpret_cast<uintptr_t>(corpus) & 15) && !(reinterpret_cast<uintptr_t>(qcodes) & 15) &&
+         row_bytes % 16 == 0;
+}
+
+TcScanPlan plan_scan_exact_tc(int64_t count, int nq) {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  int sms = 148;
+  if (dev >= 0 && dev < 64) {
+    std::lock_guard<std::mutex> lk(g_search_mu);
+    if (!g_search_sms[dev]) cudaDeviceGetAttribute(&g_search_sms[dev], cudaDevAttrMultiProcessorCount, dev);
+    if (g_search_sms[dev] > 0) sms = g_search_sms[dev];
+  }
+  TcScanPlan p;
+  p.n_qtiles = (nq + SQ - 1) / SQ;
+  // parts of at most 32768 rows (25 MB at D = 768: the query tiles reading a
+  // part together keep it in L2), and at least two CTAs per SM
+  int64_t parts = (count + 32767) / 32768;
+  const int64_t want = (2LL * sms + p.n_qtiles - 1) / p.n_qtiles;
+  if (parts < want) parts = want;
+  int64_t rpp = (count + parts - 1) / parts;
+  rpp = (rpp + SN - 1) / SN * SN;
+  if (rpp < SN) rpp = SN;
+  p.rows_per_part = rpp;
+  p.n_parts = (int)((count + rpp - 1) / rpp);
+  if (p.n_parts < 1) p.n_parts = 1;
+  return p;
+}
+
+cudaError_t launch_scan_exact_tc(const void* corpus, int64_t count, int row_bytes, const void* qcodes, int nq, int k,
+                                 TcScanPlan plan, int64_t row_base, uint64_t* cand, uint32_t* err,
+                                 cudaStream_t stream) {
+  if (nq == 0 || count == 0) return cudaSuccess;
+  const int nqb = (row_bytes + SKB - 1) / SKB;
+  if (nqb > S_MAX_QBOX) return cudaErrorInvalidValue;
+  const int nst = nqb <= 6 ? 4 : 3;
+  const int smem = 1024 + nqb * S_QBOX + nst * S_TILE + S_BAR_BYTES;
+  if (smem > 232448) return cudaErrorInvalidValue;
+  CUtensorMap mc, mq;
+  cudaError_t e;
+  if ((e = map_bytes(&mc, corpus, count, row_bytes, SN)) != cudaSuccess) return e;
+  if ((e = map_bytes(&mq, qcodes, nq, row_bytes, SQ)) != cudaSuccess) return e;
+  int dev = 0;
+  if ((e = cudaGetDevice(&dev)) != cudaSuccess) return e;
+  {
+    std::lock_guard<std::mutex> lk(g_search_mu);
+    if (dev >= 0 && dev < 64 && !g_search_attr[dev]) {
+      if ((e = cudaFuncSetAttribute(search_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 232448)) !=
+          cudaSuccess)
+        return e;
+      g_search_attr[dev] = true;
+    }
+  }
+  const int64_t grid = (int64_t)plan.n_parts * plan.n_qtiles;
+  search_tc_kernel<<<(unsigned)grid, S_THREADS, smem, stream>>>(mc, mq, count, nqb, nst, nq, k, plan.rows_per_part,
+                                                                plan.n_qtiles, plan.n_parts, row_base, cand, err);
+  return cudaGetLastError();
+}
+
+}  // namespace sem

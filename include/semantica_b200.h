@@ -171,7 +171,8 @@ int sem_index_build(sem_context *ctx, int32_t dim, int32_t quant, const float *v
                     int64_t count, sem_index **out);
 
 /* An index from already-stored rows (codes as Build or Deserialize produce
- * them): data is count x dim of int8 / int16 / float32. */
+ * them): data is count x dim of int8 / int16 / float32, in host or device
+ * memory. int8 indexes with dim >= 128 search on the tensor cores. */
 int sem_index_create(sem_context *ctx, int32_t dim, int32_t quant, const void *data, const int32_t *ids, int64_t count,
                      sem_index **out);
 

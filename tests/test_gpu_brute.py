@@ -130,3 +130,37 @@ def test_sharded_keys_merge_equals_full_search(ctx):
     rrows, rscores, _ = oracle.search_exact_batch(1, codes, q, k)
     np.testing.assert_array_equal(rows.cpu().numpy(), rrows)
     np.testing.assert_array_equal(scores.cpu().numpy(), rscores)
+
+
+def test_tensor_core_scan_many_parts_and_ties(ctx):
+    # int8 rows with D >= 128 take the tensor-core scan: enough rows and queries
+    # for several corpus parts of several 256-row tiles and three 128-query
+    # tiles; duplicated rows (ties) sit in different parts and tile halves
+    dim, n, nq, k = 768, 70000, 300, 16
+    codes = oracle.quantize_int8_vec(unit_rows(31, n, dim))
+    for a, b in ((5, 60001), (130, 131), (1000, 40000)):
+        codes[b] = codes[a]
+    q = oracle.quantize_int8_vec(unit_rows(32, nq, dim))
+    q[0] = codes[5]
+    q[1] = codes[130]
+    idx = brute.Index.from_codes(ctx, codes)
+    import ctypes
+    import torch
+    import _lib
+    d_q = torch.from_numpy(q).cuda()
+    keys = torch.zeros((nq, k), dtype=torch.int64, device="cuda")
+    torch.cuda.synchronize()
+    _lib.check(_lib.load().sem_index_search_keys(idx.handle, ctypes.c_void_p(d_q.data_ptr()), nq, k, 1, 0,
+                                                 ctypes.c_void_p(keys.data_ptr()), None))
+    rows = torch.empty((nq, k), dtype=torch.int32, device="cuda")
+    scores = torch.empty((nq, k), dtype=torch.int32, device="cuda")
+    _lib.check(_lib.load().sem_topk_merge(ctx.handle, ctypes.c_void_p(keys.data_ptr()), 1, nq, k, k, 1, 1,
+                                          ctypes.c_void_p(rows.data_ptr()), ctypes.c_void_p(scores.data_ptr()),
+                                          None, ctypes.c_void_p(ctx.stream)))
+    torch.cuda.synchronize()
+    rrows, rscores, _ = oracle.search_exact_batch(1, codes, q, k, nthreads=8)
+    np.testing.assert_array_equal(scores.cpu().numpy(), rscores)
+    np.testing.assert_array_equal(rows.cpu().numpy(), rrows)
+    assert rrows[0, 0] == 5 and rrows[0, 1] == 60001
+    assert rrows[1, 0] == 130 and rrows[1, 1] == 131
+    idx.close()
