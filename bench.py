@@ -512,8 +512,267 @@ def run_gemm(args) -> None:
         dist.destroy_process_group()
 
 
+# ---------------------------------------------------------------------------
+# --workload search: BASELINE config 5, search/brute exact int8 scan + top-10
+# ---------------------------------------------------------------------------
+SEARCH_N = 1 << 22
+SEARCH_D = 768
+SEARCH_Q = 16384
+SEARCH_K = 10
+SEARCH_SMALL = (1, 8, 32)
+SEARCH_METRIC = "search QPS (4M x 768 int8 rows, 16384 int8 queries, top-10 by exact int32 score)"
+SEARCH_CHUNK = 1 << 16
+
+
+def search_config(n_gpus: int) -> dict:
+    return {"workload": f"BASELINE config 5: {SEARCH_N} pre-normalised rows of N(0,1) draws, D={SEARCH_D}, int8 "
+                        f"(x127), {SEARCH_Q} queries quantised the same way, exact int32 dot products, "
+                        f"top-{SEARCH_K} by (score desc, row asc)",
+            "parallelism": f"rows sharded across {n_gpus} GPU(s) ({SEARCH_N // n_gpus} rows each), candidate keys "
+                           "all-gathered (NCCL) and merged" if n_gpus > 1 else "1 GPU",
+            "l2": f"corpus ({SEARCH_N * SEARCH_D / 1e9:.2f} GB) is streamed by every query batch; above L2 (126 MB) "
+                  "at the configured size"}
+
+
+def search_codes(torch, rows: range, dim: int, seed0: int, device: str):
+    """Seeded N(0,1) rows, L2-normalised and scaled to int8 (x127) on the device;
+    chunk c of SEARCH_CHUNK rows always comes from seed seed0 + c, so every
+    shard layout sees the same corpus."""
+    out = torch.empty((len(rows), dim), dtype=torch.int8, device=device)
+    r = rows.start
+    while r < rows.stop:
+        c = r // SEARCH_CHUNK
+        c0, c1 = c * SEARCH_CHUNK, (c + 1) * SEARCH_CHUNK
+        g = torch.Generator(device=device)
+        g.manual_seed(seed0 + c)
+        v = torch.randn((SEARCH_CHUNK, dim), generator=g, device=device, dtype=torch.float32)
+        v = v / v.norm(dim=1, keepdim=True)
+        codes = torch.round(v.clamp(-1, 1) * 127).to(torch.int8)
+        a, b = max(r, c0), min(rows.stop, c1)
+        out[a - rows.start:b - rows.start] = codes[a - c0:b - c0]
+        r = b
+    return out
+
+
+def search_cpu_baseline(codes_host: np.ndarray, q_host: np.ndarray, target_s: float = 10.0) -> dict:
+    """Exact scan + top-10 on the host cores: batches of one query per thread
+    over a corpus sample, repeated until target_s has passed, scaled to the
+    full corpus by rows."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle  # the CPU baseline leg is one of the places allowed to run the oracle
+    threads = max(1, min(os.cpu_count() or 1, 128))
+    done, qi = 0, 0
+    t0 = time.perf_counter()
+    while True:
+        idx = [(qi + t) % q_host.shape[0] for t in range(threads)]
+        oracle.search_exact_batch(1, codes_host, q_host[idx], SEARCH_K, nthreads=threads)
+        done += threads
+        qi += threads
+        dt = time.perf_counter() - t0
+        if dt >= target_s:
+            break
+    scale = SEARCH_N / codes_host.shape[0]
+    return {"value": done / (dt * scale), "unit": "queries/s", "cores": threads, "kind": "port",
+            "sample": f"{done} queries x {codes_host.shape[0]} rows in {dt:.1f} s ({threads} threads, one query "
+                      f"per thread), scaled to the {SEARCH_N}-row corpus; C restatement of the exact int8 scan and "
+                      "top-k (oracle/semantica_oracle.c)"}
+
+
+def search_host_corpus(rows: int, nq: int):
+    """Host copy of the sample used by the reference arm: the same
+    normalise-and-quantise recipe, numpy generator."""
+    rng = np.random.default_rng(10_000)
+    codes = np.empty((rows, SEARCH_D), dtype=np.int8)
+    for r in range(0, rows, SEARCH_CHUNK):
+        v = rng.standard_normal((min(SEARCH_CHUNK, rows - r), SEARCH_D), dtype=np.float32)
+        v /= np.linalg.norm(v, axis=1, keepdims=True)
+        codes[r:r + v.shape[0]] = np.round(np.clip(v, -1, 1) * 127).astype(np.int8)
+    q = rng.standard_normal((nq, SEARCH_D), dtype=np.float32)
+    q /= np.linalg.norm(q, axis=1, keepdims=True)
+    return codes, np.round(np.clip(q, -1, 1) * 127).astype(np.int8)
+
+
+def run_search(args) -> None:
+    import ctypes as C
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        dist.init_process_group("nccl", timeout=__import__("datetime").timedelta(seconds=600))
+    torch.cuda.set_device(local)
+    import _lib
+    lib = _lib.load()
+    ctx = _lib.Context(local)
+    stream = torch.cuda.ExternalStream(ctx.stream)
+    dev = f"cuda:{local}"
+    per = SEARCH_N // world
+    row_base = rank * per
+    codes = search_codes(torch, range(row_base, row_base + per), SEARCH_D, 10_000, dev)
+    qcodes = search_codes(torch, range(0, SEARCH_Q), SEARCH_D, 90_000, dev)
+    torch.cuda.synchronize()
+    h = C.c_void_p()
+    _lib.check(lib.sem_index_create(ctx.handle, SEARCH_D, 1, C.c_void_p(codes.data_ptr()), None, per, C.byref(h)))
+    keys = torch.zeros((world, SEARCH_Q, SEARCH_K), dtype=torch.int64, device=dev)
+    rows = torch.empty((SEARCH_Q, SEARCH_K), dtype=torch.int32, device=dev)
+    scores = torch.empty((SEARCH_Q, SEARCH_K), dtype=torch.int32, device=dev)
+    st = C.c_void_p(ctx.stream)
+
+    def scan(nq: int, qsrc):
+        _lib.check(lib.sem_index_search_keys(h, C.c_void_p(qsrc.data_ptr()), nq, SEARCH_K, 1, row_base,
+                                             C.c_void_p(keys[rank].data_ptr()), st))
+
+    def step(nq: int = SEARCH_Q, qsrc=None):
+        scan(nq, qcodes if qsrc is None else qsrc)
+        if world > 1:
+            with torch.cuda.stream(stream):
+                dist.all_gather_into_tensor(keys.view(-1), keys[rank].contiguous().view(-1))
+        _lib.check(lib.sem_topk_merge(ctx.handle, C.c_void_p(keys.data_ptr()), world, nq, SEARCH_K, SEARCH_K, 1, 1,
+                                      C.c_void_p(rows.data_ptr()), C.c_void_p(scores.data_ptr()), None, st))
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    for _ in range(max(args.warmup, 0)):
+        step()
+    torch.cuda.synchronize()
+    uuid = None
+    try:
+        uuid = "GPU-" + str(torch.cuda.get_device_properties(local).uuid)
+    except Exception:
+        pass
+    clocks = ClockSampler(uuid)
+    clocks.start()
+    time.sleep(0.3)
+    barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    ms = e0.elapsed_time(e1) / args.steps
+    # the scan kernel alone (the dominant launch) for the roofline
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    f0.record(stream)
+    for _ in range(args.steps):
+        scan(SEARCH_Q, qcodes)
+    f1.record(stream)
+    torch.cuda.synchronize()
+    scan_ms = f0.elapsed_time(f1) / args.steps
+    # small-batch regime: one corpus pass per batch of 1 / 8 / 32 queries
+    small = {}
+    for nq in SEARCH_SMALL:
+        step(nq)
+        torch.cuda.synchronize()
+        g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        reps = 20
+        g0.record(stream)
+        for _ in range(reps):
+            scan(nq, qcodes)
+        g1.record(stream)
+        torch.cuda.synchronize()
+        t = g0.elapsed_time(g1) / reps
+        small[f"nq={nq}"] = {"scan_ms": round(t, 4), "qps": round(nq / (t * 1e-3), 1),
+                             "corpus_gbs": round(per * SEARCH_D / (t * 1e-3) / 1e9, 1)}
+    clk = clocks.stop()
+    # e2e: float queries from pinned host memory, quantised on the device, ids back to the host
+    qf_host = torch.empty((SEARCH_Q, SEARCH_D), dtype=torch.float32, pin_memory=True)
+    qf_host.copy_((qcodes.float() / 127.0).cpu())
+    ids_host = torch.empty((SEARCH_Q, SEARCH_K), dtype=torch.int32, pin_memory=True)
+    qf_dev = torch.empty((SEARCH_Q, SEARCH_D), dtype=torch.float32, device=dev)
+    q_dev = torch.empty_like(qcodes)
+
+    out_ids = np.empty((SEARCH_Q, SEARCH_K), dtype=np.int32)
+    out_dist = np.empty((SEARCH_Q, SEARCH_K), dtype=np.float32)
+    qf_np = qf_host.numpy()
+
+    def e2e_step():
+        if world == 1:
+            # Index.SearchVector for the whole batch through the public C ABI:
+            # host floats in, ids and distances back in host memory
+            _lib.check(lib.sem_index_search(h, C.c_void_p(qf_np.ctypes.data), SEARCH_Q, SEARCH_D, SEARCH_K, 1, 1,
+                                            C.c_void_p(out_ids.ctypes.data), C.c_void_p(out_dist.ctypes.data), None))
+            return
+        with torch.cuda.stream(stream):
+            qf_dev.copy_(qf_host, non_blocking=True)
+            n = qf_dev / qf_dev.norm(dim=1, keepdim=True)
+            q_dev.copy_(torch.round(n.clamp(-1, 1) * 127).to(torch.int8))
+        step(SEARCH_Q, q_dev)
+        with torch.cuda.stream(stream):
+            ids_host.copy_(rows, non_blocking=True)
+        stream.synchronize()
+
+    e2e_step()
+    barrier()
+    t0 = time.perf_counter()
+    n_e2e = max(1, min(args.steps, 3))
+    for _ in range(n_e2e):
+        e2e_step()
+    e2e_s = (time.perf_counter() - t0) / n_e2e
+    barrier()
+    tt = torch.tensor([ms, scan_ms, e2e_s], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+    ms, scan_ms, e2e_s = float(tt[0]), float(tt[1]), float(tt[2])
+    if rank == 0:
+        peaks = json.load(open(PEAKS_PATH)) if os.path.exists(PEAKS_PATH) else {}
+        bf16 = peaks.get("bf16_tflops") or 1590.0
+        ops = 2.0 * per * SEARCH_D * SEARCH_Q
+        ach = ops / (scan_ms * 1e-3) / 1e12
+        line = {"metric": SEARCH_METRIC, "value": SEARCH_Q / (ms * 1e-3), "unit": "queries/s", "n_gpus": world,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+                "scaling": "strong", "vs_baseline": None, "dtype": "int8 x int8 -> int32", "data": "synthetic",
+                "config": search_config(world), "clocks": clk,
+                "e2e": {"value": SEARCH_Q / e2e_s, "unit": "queries/s", "h2d_bytes_per_step": SEARCH_Q * SEARCH_D * 4,
+                        "d2h_bytes_per_step": SEARCH_Q * SEARCH_K * (8 if world == 1 else 4),
+                        "api": "sem_index_search (host fp32 queries, normalised and quantised on the device)"
+                        if world == 1 else "sem_index_search_keys per shard + NCCL all-gather + sem_topk_merge"},
+                "gpu_launches": int(args.steps * 3),
+                "roofline": {"kernel": "search_tc_kernel (rows of one GPU x 16384 queries)", "bound": "tensor",
+                             "achieved": ach, "peak": 2 * bf16, "unit": "TOP/s", "frac": ach / (2 * bf16),
+                             "peak_source": "2 x measured bf16_tflops (dense int8 runs at twice the bf16 rate; no "
+                                            "int8 figure is measured on this pool)",
+                             "algorithmic_ops_per_launch": ops, "launch_ms": scan_ms, "traffic": None,
+                             "small_batch_hbm": {"peak_gbs": peaks.get("hbm_gbs") or 6650.0, **small}}}
+        if world == 1 and not args.no_cpu_baseline:
+            line["cpu_baseline"] = search_cpu_baseline(codes[:1 << 20].cpu().numpy(), qcodes[:1024].cpu().numpy())
+        print(json.dumps(line), flush=True)
+    lib.sem_index_free(h)
+    del qf_host, ids_host
+    torch.cuda.synchronize()
+    ctx.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def run_search_reference(args) -> None:
+    if int(os.environ.get("RANK", "0")) != 0:
+        return
+    codes, qc = search_host_corpus(1 << 20, 1024)
+    for _ in range(max(args.warmup, 0)):
+        search_cpu_baseline(codes, qc, target_s=0.0)
+    vals = [search_cpu_baseline(codes, qc, target_s=5.0) for _ in range(max(args.steps, 1))]
+    cb = vals[-1]
+    value = statistics.median(x["value"] for x in vals)
+    cb["value"] = value
+    print(json.dumps({"metric": SEARCH_METRIC, "value": value, "unit": "queries/s", "n_gpus": args.gpus,
+                      "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * SEARCH_Q / value,
+                      "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+                      "dtype": "int8 x int8 -> int32", "data": "synthetic", "impl": "reference",
+                      "config": search_config(args.gpus), "cpu_baseline": cb,
+                      "e2e": {"value": value, "unit": "queries/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}),
+          flush=True)
+
+
 def main():
-    global BATCH, SEQ_LEN
+    global BATCH, SEQ_LEN, SEARCH_N, SEARCH_Q
     import faulthandler
     faulthandler.enable()  # a crash prints the Python stack
     ap = argparse.ArgumentParser()
@@ -521,14 +780,19 @@ def main():
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="embed", choices=["embed", "gemm"])
+    ap.add_argument("--workload", default="embed", choices=["embed", "gemm", "search"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--batch", type=int, default=1024, help="sequences per GPU (profiling runs use fewer)")
     ap.add_argument("--seq-len", type=int, default=512)
+    ap.add_argument("--search-rows", type=int, default=SEARCH_N, help="search corpus rows (profiling runs use fewer)")
+    ap.add_argument("--search-queries", type=int, default=SEARCH_Q)
     args = ap.parse_args()
     BATCH, SEQ_LEN = args.batch, args.seq_len
+    SEARCH_N, SEARCH_Q = args.search_rows, args.search_queries
     if args.workload == "gemm":
         run_gemm_reference(args) if args.impl == "reference" else run_gemm(args)
+    elif args.workload == "search":
+        run_search_reference(args) if args.impl == "reference" else run_search(args)
     elif args.impl == "reference":
         run_reference(args)
     else:

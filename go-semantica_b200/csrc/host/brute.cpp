@@ -16,7 +16,7 @@ struct sem_index {
   sem::DevBuf data;
   std::vector<int32_t> ids;
   std::unordered_map<int32_t, int64_t> id_to_row;
-  sem::DevBuf qin, qprep, cand, out;
+  sem::DevBuf qin, qprep, cand, out, qthr;
 };
 
 namespace sem {
@@ -74,9 +74,11 @@ int search_keys(sem_index* x, const void* d_queries, int nq, int k, int mode, in
     const TcScanPlan tp = plan_scan_exact_tc(x->count, nq);
     const size_t need = (size_t)nq * tp.n_parts * k * sizeof(uint64_t);
     SEM_CUDA(x->cand.ensure(need > 0 ? need : 8));
+    SEM_CUDA(x->qthr.ensure((size_t)(nq > 0 ? nq : 1) * 4));
+    SEM_CUDA(cudaMemsetAsync(x->qthr.p, 0, (size_t)nq * 4, st));
     uint64_t* cand = x->cand.as<uint64_t>();
     cudaError_t e = launch_scan_exact_tc(x->data.p, x->count, x->row_bytes, d_queries, nq, k, tp, row_base, cand,
-                                         nullptr, st);
+                                         x->qthr.as<uint32_t>(), nullptr, st);
     if (e != cudaSuccess) return set_error(SEM_EDEVICE, "scan: %s", cudaGetErrorString(e));
     e = launch_topk_merge(cand, tp.n_parts, k, (int64_t)tp.n_parts * k, nq, k, k, false, elem_size(x->quant), nullptr,
                           nullptr, nullptr, d_keys, st);

@@ -128,8 +128,11 @@ struct TcScanPlan {
 };
 bool scan_exact_tc_supported(int elem, int row_bytes, int k, const void* corpus, const void* qcodes);
 TcScanPlan plan_scan_exact_tc(int64_t count, int nq);
+// qthr (nullable): nq zeroed words the CTAs of one query share their k-th
+// best scores through, so that later corpus parts skip rows early; the
+// merged result does not depend on it.
 cudaError_t launch_scan_exact_tc(const void* corpus, int64_t count, int row_bytes, const void* qcodes, int nq, int k,
-                                 TcScanPlan plan, int64_t row_base, uint64_t* cand, uint32_t* err,
+                                 TcScanPlan plan, int64_t row_base, uint64_t* cand, uint32_t* qthr, uint32_t* err,
                                  cudaStream_t stream);
 
 // Row-wise normalize (optional) + quantize (quant 1/2) or copy (quant 0) into

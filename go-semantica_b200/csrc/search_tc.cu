@@ -11,11 +11,16 @@
 // top-k filter of tile t. Warp 0 issues TMA, warp 1 the MMAs, warps 4-11 (two
 // per TMEM lane quarter, each half of a tile's rows) keep a per-query top-16
 // in registers: rows arrive in ascending order, so a candidate only enters
-// when its score is strictly above the 16th best (a tie never beats a lower
-// row). The two halves merge in shared memory and emit one list of k keys per
-// (query, part); topk_merge_kernel merges the parts. CTAs are numbered part-
-// major, so the query tiles that read one corpus part run together and share
-// it through L2.
+// when its score is strictly above the k-th best (a tie never beats a lower
+// row). The k-th best score of each stream is also published, to the other
+// half through shared memory and to the CTAs of later corpus parts through a
+// per-query word in global memory; a row scoring below any published bound
+// cannot reach the final top-k (k real rows beat it), so each 16-score chunk
+// is usually rejected by one max-and-compare. The two halves merge in shared
+// memory and emit one list of k keys per (query, part), padded with empty (0)
+// keys; topk_merge_kernel merges the parts. CTAs are numbered part-major, so
+// the query tiles that read one corpus part run together and share it
+// through L2.
 #include <cudaTypedefs.h>
 
 #include <mutex>
@@ -38,6 +43,7 @@ constexpr int S_EPI_WARPS = 8;
 constexpr int S_KMAX = 16;
 constexpr int S_MAX_QBOX = 8;           // D <= 1024
 constexpr int S_BAR_BYTES = 256;
+constexpr int S_THR_BYTES = SQ * 4;     // per-query shared score bound
 
 __device__ uint32_t g_search_error;
 
@@ -65,11 +71,52 @@ __device__ __forceinline__ void wait_ld16(uint32_t (&r)[16]) {
                : "memory");
 }
 
+// (bit b of x) ? hi : lo, opaque to the optimiser so that the select tree
+// below is not turned back into an indexed (local-memory) array access.
+__device__ __forceinline__ uint32_t sel_bit(uint32_t x, uint32_t b, uint32_t lo, uint32_t hi) {
+  uint32_t r;
+  asm("{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %1, 0;\n\t"
+      "selp.b32 %0, %2, %3, p;\n\t}\n"
+      : "=r"(r)
+      : "r"(x & b), "r"(hi), "r"(lo));
+  return r;
+}
+
+// sc[x] for a lane-varying x without local memory: a 4-level select tree.
+__device__ __forceinline__ uint32_t pick16(const uint32_t (&sc)[16], uint32_t x) {
+  uint32_t a[8], c[4];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) a[i] = sel_bit(x, 1, sc[2 * i], sc[2 * i + 1]);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) c[i] = sel_bit(x, 2, a[2 * i], a[2 * i + 1]);
+  return sel_bit(x, 8, sel_bit(x, 4, c[0], c[1]), sel_bit(x, 4, c[2], c[3]));
+}
+
+__device__ __forceinline__ uint32_t ld_relaxed_u32(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
 struct Top16 {
   uint64_t v[S_KMAX];  // best first; 0 = empty
   __device__ __forceinline__ void init() {
 #pragma unroll
     for (int i = 0; i < S_KMAX; ++i) v[i] = 0;
+  }
+  // The k-th best key (1 <= k <= 16), 0 while fewer than k are held.
+  __device__ __forceinline__ uint64_t kth(int k) const {
+    uint64_t r = v[0];
+#pragma unroll
+    for (int i = 1; i < S_KMAX; ++i) {  // opaque selects: no indexed (local-memory) access of v
+      asm("{\n\t.reg .pred p;\n\t"
+          "setp.eq.s32 p, %2, %3;\n\t"
+          "selp.b64 %0, %1, %0, p;\n\t}\n"
+          : "+l"(r)
+          : "l"(v[i]), "r"(k - 1), "r"(i));
+    }
+    return r;
   }
   __device__ __forceinline__ void insert(uint64_t key) {
     v[S_KMAX - 1] = key;
@@ -83,12 +130,40 @@ struct Top16 {
   }
 };
 
+// One chunk of 16 scores of rows [row0, row0 + 16): the lane maximum rejects
+// the chunk in the common case; otherwise the rows above thr enter one by one.
+__device__ __forceinline__ void filter_chunk(const uint32_t (&sc)[16], int64_t row0, int64_t r1, int64_t row_base,
+                                             bool live, int k, uint32_t ext, uint32_t& thr, uint32_t& own,
+                                             Top16& top) {
+  const int m = max(max(__vimax3_s32((int)sc[0], (int)sc[1], (int)sc[2]),
+                        __vimax3_s32((int)sc[3], (int)sc[4], (int)sc[5])),
+                    max(__vimax3_s32((int)sc[6], (int)sc[7], (int)sc[8]),
+                        max(__vimax3_s32((int)sc[9], (int)sc[10], (int)sc[11]),
+                            __vimax3_s32((int)sc[12], (int)sc[13], max((int)sc[14], (int)sc[15])))));
+  if (!live || ((uint32_t)m ^ 0x80000000u) <= thr) return;
+  uint32_t mask = 0;
+#pragma unroll
+  for (int x = 0; x < 16; ++x) mask |= (uint32_t)((sc[x] ^ 0x80000000u) > thr) << x;
+  while (mask) {
+    const uint32_t x = __ffs(mask) - 1;
+    mask &= mask - 1;
+    const uint32_t biased = pick16(sc, x) ^ 0x80000000u;
+    const int64_t row = row0 + x;
+    if (biased > thr && row < r1) {
+      top.insert(((uint64_t)biased << 32) | (uint64_t)(0xffffffffu - (uint32_t)(row_base + row)));
+      own = (uint32_t)(top.kth(k) >> 32);
+      thr = max(own, ext ? ext - 1u : 0u);
+    }
+  }
+}
+
 }  // namespace
 
 __global__ void __launch_bounds__(S_THREADS, 1)
     search_tc_kernel(const __grid_constant__ CUtensorMap tm_c, const __grid_constant__ CUtensorMap tm_q,
                      int64_t count, int nqb, int nst, int nq, int k, int64_t rows_per_part, int n_qtiles,
-                     int n_parts, int64_t row_base, uint64_t* __restrict__ cand, uint32_t* __restrict__ err) {
+                     int n_parts, int64_t row_base, uint64_t* __restrict__ cand, uint32_t* __restrict__ qthr,
+                     uint32_t* __restrict__ err) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
   uint8_t* sQ = smem;                    // nqb boxes of 128 queries x 128 bytes
@@ -102,6 +177,7 @@ __global__ void __launch_bounds__(S_THREADS, 1)
   uint64_t* drain = tempty + 2;
   uint32_t* s_tmem = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(s_tmem + 1);
+  volatile uint32_t* s_thr = reinterpret_cast<volatile uint32_t*>(reinterpret_cast<uint8_t*>(bars) + S_BAR_BYTES);
   if (!err) err = &g_search_error;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -124,6 +200,7 @@ __global__ void __launch_bounds__(S_THREADS, 1)
     *abort_flag = 0;
     fence_mbar_init();
   }
+  if (threadIdx.x < SQ) s_thr[threadIdx.x] = 0;
   if (warp == 1) tmem_alloc(s_tmem, 512);
   tc_fence_before();
   __syncthreads();
@@ -192,9 +269,21 @@ __global__ void __launch_bounds__(S_THREADS, 1)
     const int q = warp & 3;     // TMEM lane quarter
     const int half = w >> 2;    // rows [128 * half, +128) of each tile
     const int lq = q * 32 + lane;  // query within the tile
+    const int64_t qg = (int64_t)qt * SQ + lq;
+    const bool live = qg < nq;
+    const bool warp_live = __any_sync(0xffffffffu, live);
     const uint32_t t_lane = tmem + ((uint32_t)(q * 32) << 16);
+    uint32_t* gthr = (qthr && live) ? qthr + qg : nullptr;
     Top16 top;
     top.init();
+    // Score bounds, as order-preserving (biased) score bits. own: the k-th
+    // best score of this stream (0 while it holds fewer than k). ext: the
+    // best k-th score published for this query by the other half of the
+    // tile (shared memory) or by other corpus parts (global memory). Each is
+    // the k-th best of k real rows, so a row whose score is below it cannot
+    // reach the final top-k; a row tying it can (lower row wins), so ties
+    // with ext are kept, and ties with own lose (rows arrive ascending).
+    uint32_t own = 0, ext = gthr ? ld_relaxed_u32(gthr) : 0u, pub = 0;
     bool ok = true;
     for (int t = 0; t < ntiles; ++t) {
       const uint32_t b = t & 1, ub = t >> 1;
@@ -202,9 +291,18 @@ __global__ void __launch_bounds__(S_THREADS, 1)
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) continue;
       tc_fence_after();
+      if (!warp_live) {  // no real query in this lane quarter: nothing to read
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&tempty[b]);
+        continue;
+      }
+      ext = max(ext, s_thr[lq]);
+      if (gthr && (t & 7) == 0) ext = max(ext, ld_relaxed_u32(gthr));
+      uint32_t thr = max(own, ext ? ext - 1u : 0u);  // a row enters when its biased score > thr
       const int64_t rbase = r0 + (int64_t)t * SN + half * 128;
-      // scores of 128 rows: 8 chunks of 16, two loads in flight per wait
-#pragma unroll
+      // scores of 128 rows: 4 steps of two 16-column loads in flight
+#pragma unroll 1
       for (int cp = 0; cp < 4; ++cp) {
         uint32_t sc[2][16];
         tmem_ld16(t_lane + b * SN + half * 128 + cp * 32, sc[0]);
@@ -216,15 +314,14 @@ __global__ void __launch_bounds__(S_THREADS, 1)
           __syncwarp();
           if (lane == 0) mbar_arrive(&tempty[b]);
         }
-        const uint32_t thr = (uint32_t)(top.v[S_KMAX - 1] >> 32);
-#pragma unroll
-        for (int x = 0; x < 32; ++x) {
-          const uint32_t biased = sc[x >> 4][x & 15] ^ 0x80000000u;  // order-preserving score bits
-          if (biased > thr) {
-            const int64_t row = rbase + cp * 32 + x;
-            if (row < r1) top.insert(((uint64_t)biased << 32) | (uint64_t)(0xffffffffu - (uint32_t)(row_base + row)));
-          }
-        }
+        const uint32_t own0 = own;
+        filter_chunk(sc[0], rbase + cp * 32, r1, row_base, live, k, ext, thr, own, top);
+        filter_chunk(sc[1], rbase + cp * 32 + 16, r1, row_base, live, k, ext, thr, own, top);
+        if (own != own0) atomicMax(const_cast<uint32_t*>(&s_thr[lq]), own);
+      }
+      if (gthr && own > pub && ((t & 7) == 7 || t == ntiles - 1)) {
+        atomicMax(gthr, own);
+        pub = own;
       }
     }
     // both halves of each query -> one list of k keys per (query, part)
@@ -235,8 +332,7 @@ __global__ void __launch_bounds__(S_THREADS, 1)
       for (int i = 0; i < S_KMAX; ++i) sk[lq * S_KMAX + i] = top.v[i];
     }
     named_bar_sync(1, S_EPI_WARPS * 32);
-    const int64_t qg = (int64_t)qt * SQ + lq;
-    if (half == 0 && qg < nq) {
+    if (half == 0 && live) {
       uint64_t* dst = cand + ((int64_t)qg * n_parts + part) * k;
       const uint64_t* other = sk + lq * S_KMAX;
       int ib = 0;
@@ -317,10 +413,16 @@ TcScanPlan plan_scan_exact_tc(int64_t count, int nq) {
   TcScanPlan p;
   p.n_qtiles = (nq + SQ - 1) / SQ;
   // parts of at most 32768 rows (25 MB at D = 768: the query tiles reading a
-  // part together keep it in L2), and at least two CTAs per SM
+  // part together keep it in L2)
   int64_t parts = (count + 32767) / 32768;
-  const int64_t want = (2LL * sms + p.n_qtiles - 1) / p.n_qtiles;
-  if (parts < want) parts = want;
+  // one CTA per SM: when the grid would be only a few waves, split the
+  // corpus finer so that it fills whole waves
+  const int64_t ctas = parts * p.n_qtiles;
+  if (ctas < 4LL * sms) {
+    const int64_t waves = (ctas + sms - 1) / sms;
+    const int64_t want = waves * sms / p.n_qtiles;
+    if (parts < want) parts = want;
+  }
   int64_t rpp = (count + parts - 1) / parts;
   rpp = (rpp + SN - 1) / SN * SN;
   if (rpp < SN) rpp = SN;
@@ -331,13 +433,13 @@ TcScanPlan plan_scan_exact_tc(int64_t count, int nq) {
 }
 
 cudaError_t launch_scan_exact_tc(const void* corpus, int64_t count, int row_bytes, const void* qcodes, int nq, int k,
-                                 TcScanPlan plan, int64_t row_base, uint64_t* cand, uint32_t* err,
+                                 TcScanPlan plan, int64_t row_base, uint64_t* cand, uint32_t* qthr, uint32_t* err,
                                  cudaStream_t stream) {
   if (nq == 0 || count == 0) return cudaSuccess;
   const int nqb = (row_bytes + SKB - 1) / SKB;
   if (nqb > S_MAX_QBOX) return cudaErrorInvalidValue;
   const int nst = nqb <= 6 ? 4 : 3;
-  const int smem = 1024 + nqb * S_QBOX + nst * S_TILE + S_BAR_BYTES;
+  const int smem = 1024 + nqb * S_QBOX + nst * S_TILE + S_BAR_BYTES + S_THR_BYTES;
   if (smem > 232448) return cudaErrorInvalidValue;
   CUtensorMap mc, mq;
   cudaError_t e;
@@ -356,7 +458,8 @@ cudaError_t launch_scan_exact_tc(const void* corpus, int64_t count, int row_byte
   }
   const int64_t grid = (int64_t)plan.n_parts * plan.n_qtiles;
   search_tc_kernel<<<(unsigned)grid, S_THREADS, smem, stream>>>(mc, mq, count, nqb, nst, nq, k, plan.rows_per_part,
-                                                                plan.n_qtiles, plan.n_parts, row_base, cand, err);
+                                                                plan.n_qtiles, plan.n_parts, row_base, cand, qthr,
+                                                                err);
   return cudaGetLastError();
 }
 

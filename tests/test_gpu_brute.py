@@ -164,3 +164,42 @@ def test_tensor_core_scan_many_parts_and_ties(ctx):
     assert rrows[0, 0] == 5 and rrows[0, 1] == 60001
     assert rrows[1, 0] == 130 and rrows[1, 1] == 131
     idx.close()
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("n,nq,k,distinct", [(200_000, 40, 10, 64), (150_000, 1, 1, 0), (150_000, 129, 3, 16),
+                                             (90_000, 260, 16, 5)])
+def test_tensor_core_scan_shared_bounds_with_ties(ctx, n, nq, k, distinct):
+    # The scan publishes each query's k-th best score across tile halves and
+    # corpus parts and skips rows below it. Rows drawn from a few distinct
+    # vectors make nearly every score tie with the published bounds: the
+    # result must still be the lowest rows among equal scores, as the oracle's
+    # (score desc, row asc) order gives.
+    dim = 768
+    if distinct:
+        base = oracle.quantize_int8_vec(unit_rows(41, distinct, dim))
+        codes = base[np.random.default_rng(42).integers(0, distinct, n)]
+    else:
+        codes = oracle.quantize_int8_vec(unit_rows(43, n, dim))
+    q = oracle.quantize_int8_vec(unit_rows(44, nq, dim))
+    idx = brute.Index.from_codes(ctx, codes)
+    import ctypes
+    import torch
+    import _lib
+    d_q = torch.from_numpy(q).cuda()
+    keys = torch.zeros((nq, k), dtype=torch.int64, device="cuda")
+    rows = torch.empty((nq, k), dtype=torch.int32, device="cuda")
+    scores = torch.empty((nq, k), dtype=torch.int32, device="cuda")
+    torch.cuda.synchronize()
+    lib = _lib.load()
+    for _ in range(2):  # the per-query bounds are reset for every search
+        _lib.check(lib.sem_index_search_keys(idx.handle, ctypes.c_void_p(d_q.data_ptr()), nq, k, 1, 0,
+                                             ctypes.c_void_p(keys.data_ptr()), None))
+        _lib.check(lib.sem_topk_merge(ctx.handle, ctypes.c_void_p(keys.data_ptr()), 1, nq, k, k, 1, 1,
+                                      ctypes.c_void_p(rows.data_ptr()), ctypes.c_void_p(scores.data_ptr()),
+                                      None, ctypes.c_void_p(ctx.stream)))
+        torch.cuda.synchronize()
+        rrows, rscores, _ = oracle.search_exact_batch(1, codes, q, k, nthreads=8)
+        np.testing.assert_array_equal(scores.cpu().numpy(), rscores)
+        np.testing.assert_array_equal(rows.cpu().numpy(), rrows)
+    idx.close()
