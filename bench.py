@@ -724,6 +724,10 @@ def run_search(args) -> None:
         peaks = json.load(open(PEAKS_PATH)) if os.path.exists(PEAKS_PATH) else {}
         bf16 = peaks.get("bf16_tflops") or 1590.0
         ops = 2.0 * per * SEARCH_D * SEARCH_Q
+        traffic = None
+        if os.path.exists(TRAFFIC_PATH):
+            bpr = json.load(open(TRAFFIC_PATH)).get("search_tc_bytes_per_corpus_row")
+            traffic = bpr * per if bpr else None
         ach = ops / (scan_ms * 1e-3) / 1e12
         line = {"metric": SEARCH_METRIC, "value": SEARCH_Q / (ms * 1e-3), "unit": "queries/s", "n_gpus": world,
                 "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
@@ -738,7 +742,7 @@ def run_search(args) -> None:
                              "achieved": ach, "peak": 2 * bf16, "unit": "TOP/s", "frac": ach / (2 * bf16),
                              "peak_source": "2 x measured bf16_tflops (dense int8 runs at twice the bf16 rate; no "
                                             "int8 figure is measured on this pool)",
-                             "algorithmic_ops_per_launch": ops, "launch_ms": scan_ms, "traffic": None,
+                             "algorithmic_ops_per_launch": ops, "launch_ms": scan_ms, "traffic": traffic,
                              "small_batch_hbm": {"peak_gbs": peaks.get("hbm_gbs") or 6650.0, **small}}}
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = search_cpu_baseline(codes[:1 << 20].cpu().numpy(), qcodes[:1024].cpu().numpy())
