@@ -21,9 +21,9 @@
 // (one fp16 plane of 64 keys x 128 dims each), loaded by TMA. TMEM holds O
 // (256 fp32 columns), the scores of a 64-key tile (two buffers of 64 columns)
 // and P (two buffers of 64 columns: p_hi and p_lo as packed fp16 pairs, row =
-// lane), so the P.V MMAs take their A operand straight from TMEM. Warp 0
-// issues TMA, warp 1 the MMAs, warps 4-11 (two per TMEM lane quarter, each
-// half of a tile's keys) do the softmax with packed fp32 arithmetic: they read
+// lane), so the P.V MMAs take their A operand straight from TMEM. Warps 0
+// and 2 issue TMA (alternate slots), warp 1 the MMAs, warps 4-11 (two per
+// TMEM lane quarter, each half of a tile's keys) do the softmax with packed fp32 arithmetic: they read
 // scores from TMEM, write P back into TMEM, and at the end scale O by 1/sum
 // and store it. V is read MN-major straight from its row-major [token][dim]
 // layout, so sequences may start at any token. All three query heads read the
@@ -44,6 +44,7 @@ constexpr int HD = 256;      // head_dim
 constexpr int QT = 128;      // query rows per CTA (TMEM lanes)
 constexpr int KT = 64;       // keys per tile
 constexpr int NSLOT = 6;     // K/V ring slots
+static_assert(NSLOT % 2 == 0, "the two TMA threads own alternate slots");
 constexpr int SLOT = KT * 128 * 2;       // 16 KB: 64 keys x 128 dims, one plane
 constexpr int QBLK = QT * 128;           // 16 KB: 128 rows x 64 dims
 constexpr int SMEM_Q = 2 * 4 * QBLK;     // hi, lo x 4 dim blocks: 128 KB
@@ -53,7 +54,7 @@ constexpr int NS1 = 4;  // score buffers of pass 1 (in the O columns, unused unt
 constexpr int NBAR = 1 + 2 * NSLOT + 2 + 2 + 2 + 2 + 1 + 1 + 2 * NS1;
 constexpr int SMEM_MISC = 256 + 2 * QT * 4;  // barriers, TMEM address, [2][QT] reductions
 constexpr int SMEM_BYTES = 1024 + SMEM_Q + SMEM_RING + SMEM_MISC;
-constexpr int THREADS = 384;  // warpgroup 0: TMA, MMA, 2 idle; warpgroups 1-2: softmax / epilogue
+constexpr int THREADS = 384;  // warpgroup 0: TMA (warps 0, 2), MMA (1), idle (3); warpgroups 1-2: softmax / epilogue
 constexpr int SM_WARPS = 8;
 // TMEM columns: O [0,256), scores [256,320) and [320,384), P [384,448) and
 // [448,512) (p_hi in the first 32 columns of a P buffer, p_lo in the next 32)
@@ -169,17 +170,28 @@ __global__ void __launch_bounds__(THREADS, 1)
   // item is (hi, lo) of dim half 0 then 1 (4 slots), a V(j) item the same.
   if (warp < 4) {
     asm volatile("setmaxnreg.dec.sync.aligned.u32 56;");
-    if (warp == 0 && lane == 0) {
-      // ---------------- TMA producer ----------------
+    if ((warp == 0 || warp == 2) && lane == 0) {
+      // ---------------- TMA producers ----------------
+      // Two threads (warps 0 and 2) walk the same slot sequence and issue
+      // alternate slots: one thread's loads complete at a limited rate (a few
+      // copies in flight), so a second stream doubles the rate. NSLOT is even:
+      // slot s is only ever loaded by thread s & 1.
+      const uint32_t me = warp >> 1;
       uint32_t it = 0;
       bool ok = true;
-      mbar_arrive_expect_tx(qfull, SMEM_Q);
+      if (me == 0) {
+        mbar_arrive_expect_tx(qfull, SMEM_Q);
 #pragma unroll
-      for (int b = 0; b < 4; ++b) {
-        tma_load_3d(&tm_qh, qfull, sQ + b * QBLK, b * 64, head, row0);
-        tma_load_3d(&tm_ql, qfull, sQ + (4 + b) * QBLK, b * 64, head, row0);
+        for (int b = 0; b < 4; ++b) {
+          tma_load_3d(&tm_qh, qfull, sQ + b * QBLK, b * 64, head, row0);
+          tma_load_3d(&tm_ql, qfull, sQ + (4 + b) * QBLK, b * 64, head, row0);
+        }
       }
       auto load_slot = [&](const CUtensorMap* map, int key0, int dim0) -> bool {
+        if ((it & 1) != me) {
+          ++it;
+          return true;
+        }
         const uint32_t s = it % NSLOT, u = it / NSLOT;
         if (!mbar_wait(&rempty[s], (u & 1) ^ 1, abort_flag, err, 1u)) return false;
         uint8_t* dst = sRing + s * SLOT;
@@ -204,8 +216,8 @@ __global__ void __launch_bounds__(THREADS, 1)
           }
       }
       for (uint32_t j = it > (uint32_t)NSLOT ? it - NSLOT : 0; j < it; ++j)
-        mbar_wait_drain(&rfull[j % NSLOT], (j / NSLOT) & 1);
-      mbar_wait_drain(qfull, 0);
+        if ((j & 1) == me) mbar_wait_drain(&rfull[j % NSLOT], (j / NSLOT) & 1);
+      if (me == 0) mbar_wait_drain(qfull, 0);
     } else if (warp == 1 && lane == 0) {
       // ---------------- MMA issuer ----------------
       constexpr uint32_t idesc_qk = umma_idesc_f16_f32(QT, KT);

@@ -14,8 +14,9 @@
 //
 // Roles: the weight rows (output channels) are the MMA's M = 128 (TMEM lanes),
 // so each epilogue thread owns one channel and its block scale is a scalar;
-// the tokens are N. Warp 0 issues TMA loads (128-byte swizzled K-major tiles,
-// 4-stage ring of 64-wide K slices), warp 1 issues the MMAs, warps 4-15 drain
+// the tokens are N. Warps 0 and 2 issue TMA loads for alternate stages
+// (128-byte swizzled K-major tiles, 4-stage ring of 64-wide K slices), warp 1
+// issues the MMAs, warps 4-15 drain
 // TMEM: three groups of four warps (one per TMEM lane quarter), each group a
 // third of the tile's tokens, so a thread accumulates 64 values and every
 // block costs it one batch of TMEM loads and one wait. TMEM holds two block
@@ -40,33 +41,42 @@ namespace {
 constexpr int kBM = 128;       // weight rows per tile (TMEM lanes)
 constexpr int kBKS = 64;       // K elements per pipeline stage: two Q8_0 blocks, 128 bytes of fp16
 constexpr int kStages = 4;
-constexpr int kGroups = 3;     // token groups of epilogue warps
-constexpr int kEpiWarps = 4 * kGroups;
-constexpr int kEpiThreads = kEpiWarps * 32;
-// warpgroup 0: TMA warp, MMA warp, two idle warps; warpgroups 1-3: epilogue
-constexpr int kThreads = 128 + kEpiThreads;
-// register split (setmaxnreg): 128 x 56 + 384 x 152 = 512 x 128, the launch's share
-constexpr int kRegsProducer = 56, kRegsEpilogue = 152;
-static_assert(128 * kRegsProducer + kEpiThreads * kRegsEpilogue <= kThreads * 128, "register split");
+static_assert(kStages % 2 == 0, "the two TMA threads own alternate stages");
 constexpr int kATile = kBM * kBKS * 2;      // 16 KB
 constexpr int kSubTok = 16;                 // tokens per output box
 constexpr int kOutBox = kSubTok * kBM * 4;  // 8 KB: one fp32 box of 16 tokens x 128 channels
-constexpr int kBarBytes = 112;              // 13 mbarriers + TMEM address + abort flag, 16-byte padded
+constexpr int kBarBytes = 160;              // up to 21 mbarriers + TMEM address + abort flag, 16-byte padded
+constexpr int kRegsProducer = 56;           // warpgroup 0 after setmaxnreg.dec
 
-template <int NA, int NT>
+// NA weight operands x NT tokens per tile; GR token groups of four epilogue
+// warps (one per TMEM lane quarter). Warpgroup 0: TMA warps 0 and 2, MMA warp
+// 1, idle warp 3; then GR epilogue warpgroups. TMEM holds kNB block buffers
+// (up to four), so the MMAs may run that many blocks ahead of the epilogue.
+template <int NA, int NT, int GR>
 struct TileCfg {
-  static constexpr int kTG = NT / kGroups;    // tokens per epilogue group
+  static constexpr int kGroups = GR;
+  static constexpr int kEpiWarps = 4 * GR;
+  static constexpr int kEpiThreads = kEpiWarps * 32;
+  static constexpr int kThreads = 128 + kEpiThreads;
+  // register split (setmaxnreg): the launch gets 65536 / kThreads per thread
+  // (rounded down to a multiple of 8); warpgroup 0 gives up all but 56
+  static constexpr int kRegsLaunch = (65536 / kThreads) / 8 * 8 > 255 ? 248 : (65536 / kThreads) / 8 * 8;
+  static constexpr int kRegsEpilogue = GR >= 3 ? 152 : 192;
+  static_assert(128 * kRegsProducer + kEpiThreads * kRegsEpilogue <= kThreads * kRegsLaunch, "register split");
+  static constexpr int kTG = NT / GR;         // tokens per epilogue group
   static constexpr int kCPO = kTG / 16;       // TMEM chunks of 16 columns per operand
   static constexpr int kChunks = NA * kCPO;
   static constexpr int kPairs = kChunks * 8;  // packed fp32 pairs accumulated per thread
   static constexpr int kBTile = NT * kBKS * 2;
   static constexpr int kStage = NA * kATile + kBTile;  // bytes per stage (also the TMA transaction count)
   static constexpr int kBufCols = NA * NT;             // TMEM columns of one block buffer
-  static constexpr int kTmemCols = 2 * kBufCols <= 256 ? 256 : 512;
-  static constexpr int kOutBytes = kGroups * 2 * kOutBox;  // per group: two boxes (double buffer, or gate + up)
+  static constexpr int kNB = 512 / kBufCols >= 4 ? 4 : 512 / kBufCols;
+  static constexpr int kTmemCols = kNB * kBufCols <= 256 ? 256 : 512;
+  static constexpr int kOutBytes = GR * 2 * kOutBox;  // per group: two boxes (double buffer, or gate + up)
   static constexpr int kSmem = 1024 + kStages * kStage + kOutBytes + kBarBytes + NT * 16;
-  static_assert(NT % (16 * kGroups) == 0 && kTG % kSubTok == 0, "token tile must split into 16-token boxes");
-  static_assert(2 * kBufCols <= 512, "two block buffers must fit TMEM");
+  static_assert(NT % (16 * GR) == 0 && kTG % kSubTok == 0, "token tile must split into 16-token boxes");
+  static_assert(kNB >= 2, "at least two block buffers in TMEM");
+  static_assert(2 * kStages + 2 * kNB + 1 <= (kBarBytes - 8) / 8, "barrier block");
   static_assert(kChunks <= 4, "register budget: at most 64 accumulators and 64 staging registers per thread");
   static_assert(kSmem <= 232448, "shared memory per CTA");
 };
@@ -75,10 +85,10 @@ __device__ uint32_t g_tc_error;  // error bits of launches given no error word
 
 // TMEM column of chunk c (16 columns) of a group's share of a block buffer:
 // operand c / kCPO, then the group's third of the tokens.
-template <int NA, int NT>
+template <int NA, int NT, int GR>
 __device__ __forceinline__ uint32_t chunk_col(int grp, int c) {
-  constexpr int cpo = TileCfg<NA, NT>::kCPO;
-  return (uint32_t)((c / cpo) * NT + grp * TileCfg<NA, NT>::kTG + (c % cpo) * 16);
+  constexpr int cpo = TileCfg<NA, NT, GR>::kCPO;
+  return (uint32_t)((c / cpo) * NT + grp * TileCfg<NA, NT, GR>::kTG + (c % cpo) * 16);
 }
 
 __device__ __forceinline__ float f4_get(const float4& v, int i) {
@@ -105,14 +115,16 @@ __device__ __forceinline__ float gelu_up(float g, float u, float rs) {
 // One persistent CTA per SM walks tiles (128 weight rows x NT tokens), tile
 // index = token tile * n_mt + weight tile, so the CTAs working at one time
 // share a few token tiles through L2.
-template <int NA, int NT, int EPI>
-__global__ void __launch_bounds__(kThreads, 1)
+template <int NA, int NT, int GR, int EPI>
+__global__ void __launch_bounds__(TileCfg<NA, NT, GR>::kThreads, 1)
     gemm_q8_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_a,
                       const __grid_constant__ CUtensorMap tm_c, const float* __restrict__ ws, int w_rows,
                       int n_per_a, int T, int K, const uint32_t* __restrict__ a_absmax,
                       const int32_t* __restrict__ row_seq, uint32_t* __restrict__ out_absmax,
                       uint32_t* __restrict__ err, float* __restrict__ Cout) {
-  using G = TileCfg<NA, NT>;
+  using G = TileCfg<NA, NT, GR>;
+  constexpr int NB = G::kNB;
+  constexpr int kEpiWarps = G::kEpiWarps, kEpiThreads = G::kEpiThreads;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
   uint8_t* stages = smem;
@@ -120,8 +132,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* full = reinterpret_cast<uint64_t*>(outbuf + G::kOutBytes);
   uint64_t* empty = full + kStages;
   uint64_t* tfull = empty + kStages;
-  uint64_t* tempty = tfull + 2;
-  uint64_t* drain = tempty + 2;
+  uint64_t* tempty = tfull + NB;
+  uint64_t* drain = tempty + NB;
   uint32_t* s_tmem = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(s_tmem + 1);
   float* s_rs = reinterpret_cast<float*>(outbuf + G::kOutBytes + kBarBytes);
@@ -138,7 +150,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
-    for (int b = 0; b < 2; ++b) {
+    for (int b = 0; b < NB; ++b) {
       mbar_init(&tfull[b], 1);
       mbar_init(&tempty[b], kEpiWarps);
     }
@@ -153,9 +165,13 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tmem_base = *s_tmem;
   if (warp < 4) {
   asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kRegsProducer));
-  if (warp == 0) {
-    // ---------------- TMA producer ----------------
+  if (warp == 0 || warp == 2) {
+    // ---------------- TMA producers ----------------
+    // Two threads (warps 0 and 2) issue alternate stages: the tile loads of
+    // one thread complete at a limited rate (a few copies in flight), so a
+    // second stream doubles the L2 -> SM rate of the SM.
     if (lane == 0) {
+      const uint32_t me = warp >> 1;
       tma_prefetch_desc(&tm_w);
       tma_prefetch_desc(&tm_a);
       uint32_t it = 0;
@@ -163,6 +179,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int tile = blockIdx.x; ok && tile < total; tile += gridDim.x) {
         const int tt = tile / n_mt, mt = tile % n_mt;
         for (int ks = 0; ks < nks; ++ks, ++it) {
+          if ((it & 1) != me) continue;
           const uint32_t s = it % kStages, u = it / kStages;
           if (!mbar_wait(&empty[s], (u & 1) ^ 1, abort_flag, err, 1u)) {
             ok = false;
@@ -176,8 +193,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       // the copies in flight land before the CTA's shared memory is released
+      // (`it` is one past the last iteration this thread issued or skipped;
+      // stage s is only ever used by thread s & 1, kStages being even)
       for (uint32_t j = it > (uint32_t)kStages ? it - kStages : 0; j < it; ++j)
-        mbar_wait_drain(&full[j % kStages], (j / kStages) & 1);
+        if ((j & 1) == me) mbar_wait_drain(&full[j % kStages], (j / kStages) & 1);
     }
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
@@ -195,7 +214,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           tc_fence_after();
           const uint32_t sa = smem_u32(stages + s * G::kStage);
           for (int h = 0; h < 2 && ok; ++h, ++blk) {
-            const uint32_t b = blk & 1, ub = blk >> 1;
+            const uint32_t b = blk % NB, ub = blk / NB;
             if (!mbar_wait(&tempty[b], (ub & 1) ^ 1, abort_flag, err, 2u)) {
               ok = false;
               break;
@@ -220,7 +239,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   }
   } else {
-    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kRegsEpilogue));
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(G::kRegsEpilogue));
     // ---------------- epilogue: TMEM -> scaled fp32 accumulators -> output ----------------
     constexpr int CH = G::kChunks, NP = G::kPairs, NPA = NP / NA, TG = G::kTG;
     const int e = warp - 4;
@@ -288,7 +307,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
 #pragma unroll
         for (int u = 0; u < 4; ++u, ++blk) {
-        const uint32_t b = blk & 1, ub = blk >> 1;
+        const uint32_t b = blk % NB, ub = blk / NB;
         if (ok) ok = mbar_wait(&tfull[b], ub & 1, abort_flag, err, 4u);
         ok = __all_sync(0xffffffffu, ok);  // converged (and agreed) before the .sync.aligned TMEM loads
         if (ok) {
@@ -300,8 +319,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int hh = 0; hh < CH / 2; ++hh) {
             uint32_t r[2][16];
-            tmem_ld16(tb + chunk_col<NA, NT>(grp, 2 * hh), r[0]);
-            tmem_ld16(tb + chunk_col<NA, NT>(grp, 2 * hh + 1), r[1]);
+            tmem_ld16(tb + chunk_col<NA, NT, GR>(grp, 2 * hh), r[0]);
+            tmem_ld16(tb + chunk_col<NA, NT, GR>(grp, 2 * hh + 1), r[1]);
             tmem_wait_ld_regs(r[0]);
             reg_barrier16(r[1]);
             if (hh == CH / 2 - 1) {
@@ -480,12 +499,12 @@ struct DevState {
 DevState g_dev[64];
 std::mutex g_dev_mu;
 
-template <int NA, int NT, int EPI>
+template <int NA, int NT, int GR, int EPI>
 cudaError_t launch_tc(int slot, const __half* a_codes, int T, int K, const __half* w_codes, const float* ws,
                       int w_rows, const uint32_t* a_absmax, const int32_t* row_seq, float* c, uint32_t* out_absmax,
                       uint32_t* err, cudaStream_t stream) {
-  using G = TileCfg<NA, NT>;
-  auto kern = gemm_q8_tc_kernel<NA, NT, EPI>;
+  using G = TileCfg<NA, NT, GR>;
+  auto kern = gemm_q8_tc_kernel<NA, NT, GR, EPI>;
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
@@ -516,7 +535,7 @@ cudaError_t launch_tc(int slot, const __half* a_codes, int T, int K, const __hal
     return e;
   const int total = (n_per_a / kBM) * ((T + NT - 1) / NT);
   const int grid = total < sms ? total : sms;
-  kern<<<grid, kThreads, G::kSmem, stream>>>(tm_w, tm_a, tm_c, ws, w_rows, n_per_a, T, K, a_absmax, row_seq,
+  kern<<<grid, G::kThreads, G::kSmem, stream>>>(tm_w, tm_a, tm_c, ws, w_rows, n_per_a, T, K, a_absmax, row_seq,
                                              out_absmax, err, c);
   return cudaGetLastError();
 }
@@ -530,15 +549,15 @@ cudaError_t launch_gemm_q8(const __half* a_codes, const __half* w_codes, const f
   if (M < 0 || K <= 0 || K % 128 != 0) return cudaErrorInvalidValue;  // four Q8_0 blocks per scale load
   if (epilogue == kEpiGeluUp) {
     if (N % (2 * kBM) != 0) return cudaErrorInvalidValue;
-    return launch_tc<2, 96, kEpiGeluUp>(0, a_codes, M, K, w_codes, w_scales, N, a_absmax, row_seq, c, out_absmax,
+    return launch_tc<2, 96, 3, kEpiGeluUp>(0, a_codes, M, K, w_codes, w_scales, N, a_absmax, row_seq, c, out_absmax,
                                         err, stream);
   }
   if (N % kBM != 0) return cudaErrorInvalidValue;
   // small batches: narrower token tiles keep more SMs busy
   if ((N / kBM) * ((M + 191) / 192) < 148)
-    return launch_tc<1, 96, kEpiStore>(1, a_codes, M, K, w_codes, w_scales, N, a_absmax, row_seq, c, nullptr, err,
+    return launch_tc<1, 96, 3, kEpiStore>(1, a_codes, M, K, w_codes, w_scales, N, a_absmax, row_seq, c, nullptr, err,
                                        stream);
-  return launch_tc<1, 192, kEpiStore>(2, a_codes, M, K, w_codes, w_scales, N, a_absmax, row_seq, c, nullptr, err,
+  return launch_tc<1, 192, 3, kEpiStore>(2, a_codes, M, K, w_codes, w_scales, N, a_absmax, row_seq, c, nullptr, err,
                                       stream);
 }
 

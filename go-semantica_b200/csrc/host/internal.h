@@ -101,5 +101,11 @@ struct sem_context {
 struct sem_q8_weight {
   sem_context* ctx = nullptr;
   int32_t k_in = 0, n_out = 0;
-  sem::DevBuf codes, scales;
+  sem::DevBuf codes, scales;   // fp16 codes [n_out][k_in], block scales [n_out][k_in/32]
+  sem::DevBuf hi, lo, rscale;  // split planes [n_out][k_in], row scales [n_out]
+  sem::Q8Proj proj() const {
+    return sem::Q8Proj{static_cast<const __half*>(codes.p), static_cast<const float*>(scales.p),
+                       static_cast<const __half*>(hi.p), static_cast<const __half*>(lo.p),
+                       static_cast<const float*>(rscale.p)};
+  }
 };

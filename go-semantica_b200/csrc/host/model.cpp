@@ -29,9 +29,7 @@ int set_error(int code, const char* fmt, ...) {
 const char* last_error() { return g_error.c_str(); }
 
 struct LayerW {
-  __half *qkv, *o, *gu, *down;  // fp16 codes [rows][K]; gu = gate rows then up rows
-  // block scales [rows][K/32]
-  float *qkv_s, *o_s, *gu_s, *down_s;
+  Q8Proj qkv, o, gu, down;  // gu = gate rows then up rows
   float *attn_norm, *q_norm, *k_norm, *post_attn, *ffn_norm, *post_ffw;
 };
 
@@ -48,11 +46,13 @@ struct sem_model {
   float* rope_sin = nullptr;
   std::vector<sem::LayerW> layers;
   // forward workspaces (grow only)
-  sem::DevBuf hid, big, att, codes, halves, inv_rms, meta, absmax, ids, out, errflag;
+  sem::DevBuf hid, big, att, codes, halves, inv_rms, meta, absmax, ids, ids_in, out, errflag;
   int64_t ws_T = -1;
   // cached metadata of the last batch shape
   std::vector<int32_t> last_offsets, last_dims;
   int32_t n_tiles = 0;
+  int64_t t_long = 0;     // packed rows of the long sequences (first in the packed order)
+  bool permuted = false;  // packed order differs from the caller's
   // optional per-launch timing
   bool prof = false;
   std::vector<cudaEvent_t> prof_events;  // pairs (before, after)
@@ -91,16 +91,20 @@ int upload_q8(sem_context* ctx, DevBuf& staging, const sem_tensor_view* t, int64
   return SEM_OK;
 }
 
-// Same for a projection weight: fp16 codes and fp32 block scales at rows
-// [row_off, row_off + rows) (the tensor-core GEMM's layout).
-int upload_q8_proj(sem_context* ctx, DevBuf& staging, const sem_tensor_view* t, int64_t rows, int cols, __half* codes,
-                   float* scales, int64_t row_off) {
+// Same for a projection weight, both layouts of the tensor-core GEMMs at rows
+// [row_off, row_off + rows): fp16 codes with fp32 block scales, and the split
+// fp16 planes with their row scales.
+int upload_q8_proj(sem_context* ctx, DevBuf& staging, const sem_tensor_view* t, int64_t rows, int cols,
+                   const Q8Proj& w, int64_t row_off) {
   uint64_t need = (uint64_t)rows * (cols / 32) * 34;
   if (t->nbytes < need) return set_error(SEM_EFORMAT, "tensor %s: %llu bytes, need %llu", t->name,
                                          (unsigned long long)t->nbytes, (unsigned long long)need);
   SEM_CUDA(staging.ensure(need));
   SEM_CUDA(cudaMemcpyAsync(staging.p, t->data, need, cudaMemcpyHostToDevice, ctx->stream));
-  SEM_CUDA(launch_repack_q8_0_f16(staging.as<uint8_t>(), rows, cols, codes, scales, row_off, ctx->stream));
+  SEM_CUDA(launch_repack_q8_0_f16(staging.as<uint8_t>(), rows, cols, const_cast<__half*>(w.codes),
+                                  const_cast<float*>(w.scales), row_off, ctx->stream));
+  SEM_CUDA(launch_repack_q8_0_split(staging.as<uint8_t>(), rows, cols, const_cast<__half*>(w.hi),
+                                    const_cast<__half*>(w.lo), const_cast<float*>(w.row_scale), row_off, ctx->stream));
   SEM_CUDA(cudaStreamSynchronize(ctx->stream));
   return SEM_OK;
 }
@@ -147,17 +151,24 @@ int model_load(sem_context* ctx, const sem_model_config* cfg_in, const sem_tenso
   };
   size_t o_emb = take((size_t)V * H), o_emb_s = take((size_t)V * (H / 32) * 4), o_onorm = take((size_t)H * 4);
   size_t o_cos = take((size_t)c.max_seq_len * (hd / 2) * 4), o_sin = take((size_t)c.max_seq_len * (hd / 2) * 4);
-  struct LOff { size_t qkv, o, gu, down, qkv_s, o_s, gu_s, down_s, an, qn, kn, pa, fn, pf; };
+  // one projection [rows][k]: codes, block scales, hi, lo, row scales
+  struct POff { size_t codes, scales, hi, lo, rsc; };
+  auto take_proj = [&](int64_t rows, int64_t k) {
+    POff p;
+    p.codes = take((size_t)rows * k * 2);
+    p.scales = take((size_t)rows * (k / 32) * 4);
+    p.hi = take((size_t)rows * k * 2);
+    p.lo = take((size_t)rows * k * 2);
+    p.rsc = take((size_t)rows * 4);
+    return p;
+  };
+  struct LOff { POff qkv, o, gu, down; size_t an, qn, kn, pa, fn, pf; };
   std::vector<LOff> lo(L);
   for (int l = 0; l < L; ++l) {
-    lo[l].qkv = take((size_t)qkvN * H * 2);
-    lo[l].o = take((size_t)H * H * 2);
-    lo[l].gu = take((size_t)2 * F * H * 2);
-    lo[l].down = take((size_t)H * F * 2);
-    lo[l].qkv_s = take((size_t)qkvN * (H / 32) * 4);
-    lo[l].o_s = take((size_t)H * (H / 32) * 4);
-    lo[l].gu_s = take((size_t)2 * F * (H / 32) * 4);
-    lo[l].down_s = take((size_t)H * (F / 32) * 4);
+    lo[l].qkv = take_proj(qkvN, H);
+    lo[l].o = take_proj(H, H);
+    lo[l].gu = take_proj(2 * F, H);
+    lo[l].down = take_proj(H, F);
     lo[l].an = take(H * 4); lo[l].qn = take(hd * 4); lo[l].kn = take(hd * 4);
     lo[l].pa = take(H * 4); lo[l].fn = take(H * 4); lo[l].pf = take(H * 4);
   }
@@ -203,29 +214,30 @@ int model_load(sem_context* ctx, const sem_model_config* cfg_in, const sem_tenso
     if ((rc = up_f32(P("attn_k_norm.weight"), lo[l].kn, hd, false, &w.k_norm))) return rc;
     if ((rc = up_f32(P("post_attention_norm.weight"), lo[l].pa, H, false, &w.post_attn))) return rc;
     if ((rc = up_f32(P("post_ffw_norm.weight"), lo[l].pf, H, false, &w.post_ffw))) return rc;
-    w.qkv = reinterpret_cast<__half*>(base + lo[l].qkv);
-    w.o = reinterpret_cast<__half*>(base + lo[l].o);
-    w.gu = reinterpret_cast<__half*>(base + lo[l].gu);
-    w.down = reinterpret_cast<__half*>(base + lo[l].down);
-    w.qkv_s = reinterpret_cast<float*>(base + lo[l].qkv_s);
-    w.o_s = reinterpret_cast<float*>(base + lo[l].o_s);
-    w.gu_s = reinterpret_cast<float*>(base + lo[l].gu_s);
-    w.down_s = reinterpret_cast<float*>(base + lo[l].down_s);
+    auto proj = [&](const POff& p) {
+      return Q8Proj{reinterpret_cast<const __half*>(base + p.codes), reinterpret_cast<const float*>(base + p.scales),
+                    reinterpret_cast<const __half*>(base + p.hi), reinterpret_cast<const __half*>(base + p.lo),
+                    reinterpret_cast<const float*>(base + p.rsc)};
+    };
+    w.qkv = proj(lo[l].qkv);
+    w.o = proj(lo[l].o);
+    w.gu = proj(lo[l].gu);
+    w.down = proj(lo[l].down);
     // Q|K|V fused into one [qkvN][H] matrix, gate rows then up rows in [2F][H]
-    struct { const char* n; uint64_t k, rows; __half* c; float* s; int64_t roff; } q8[] = {
-        {"attn_q.weight", (uint64_t)H, (uint64_t)nh * hd, w.qkv, w.qkv_s, 0},
-        {"attn_k.weight", (uint64_t)H, (uint64_t)hd, w.qkv, w.qkv_s, (int64_t)nh * hd},
-        {"attn_v.weight", (uint64_t)H, (uint64_t)hd, w.qkv, w.qkv_s, (int64_t)nh * hd + hd},
-        {"attn_output.weight", (uint64_t)H, (uint64_t)H, w.o, w.o_s, 0},
-        {"ffn_gate.weight", (uint64_t)H, (uint64_t)F, w.gu, w.gu_s, 0},
-        {"ffn_up.weight", (uint64_t)H, (uint64_t)F, w.gu, w.gu_s, F},
-        {"ffn_down.weight", (uint64_t)F, (uint64_t)H, w.down, w.down_s, 0},
+    struct { const char* n; uint64_t k, rows; const Q8Proj* w; int64_t roff; } q8[] = {
+        {"attn_q.weight", (uint64_t)H, (uint64_t)nh * hd, &w.qkv, 0},
+        {"attn_k.weight", (uint64_t)H, (uint64_t)hd, &w.qkv, (int64_t)nh * hd},
+        {"attn_v.weight", (uint64_t)H, (uint64_t)hd, &w.qkv, (int64_t)nh * hd + hd},
+        {"attn_output.weight", (uint64_t)H, (uint64_t)H, &w.o, 0},
+        {"ffn_gate.weight", (uint64_t)H, (uint64_t)F, &w.gu, 0},
+        {"ffn_up.weight", (uint64_t)H, (uint64_t)F, &w.gu, F},
+        {"ffn_down.weight", (uint64_t)F, (uint64_t)H, &w.down, 0},
     };
     for (auto& q : q8) {
       const char* name = P(q.n);
       const sem_tensor_view* t = find_view(tv, nt, name);
       if ((rc = check_q8(t, name, q.k, q.rows))) return rc;
-      if ((rc = upload_q8_proj(ctx, staging, t, (int64_t)q.rows, (int)q.k, q.c, q.s, q.roff))) return rc;
+      if ((rc = upload_q8_proj(ctx, staging, t, (int64_t)q.rows, (int)q.k, *q.w, q.roff))) return rc;
     }
   }
   // ---- RoPE tables (rope_cache.go:15-44) ----
@@ -263,8 +275,9 @@ int ensure_workspace(sem_model* m, int64_t T, int B, int64_t out_floats) {
   SEM_CUDA(m->codes.ensure((size_t)Tp * (F > H ? F : H) * 2));
   SEM_CUDA(m->halves.ensure((size_t)Tp * (2 * nh * hd + 4 * hd) * 2));
   SEM_CUDA(m->inv_rms.ensure((size_t)Tp * 4));
-  // meta: row_seq[T], row_pos[T], cu[B+1], tile_seq/tile_row0[2*(T/64+B)], out_dims[B], out_off (int64) [B]
-  size_t meta_ints = (size_t)2 * Tp + (B + 1) + 2 * ((size_t)Tp / 64 + B + 1) + B + 2 * (size_t)B + 8;
+  // meta: row_seq[T], row_pos[T], cu[B+1], tile_seq/tile_row0[2*(T/64+B)], out_dims[B], out_off (int64) [B],
+  // src_row[T]
+  size_t meta_ints = (size_t)3 * Tp + (B + 1) + 2 * ((size_t)Tp / 64 + B + 1) + B + 2 * (size_t)B + 10;
   SEM_CUDA(m->meta.ensure(meta_ints * 4));
   SEM_CUDA(m->absmax.ensure((size_t)(4 * c.num_layers + 1) * (B > 0 ? B : 1) * 4));
   SEM_CUDA(m->ids.ensure((size_t)Tp * 4));
@@ -278,10 +291,23 @@ struct MetaPtrs {
   AttnTiles tiles;
   int32_t* out_dims;
   int64_t* out_off;
+  int32_t* src_row;  // [T] caller's row of each packed row (valid when permuted)
+  int64_t T_long;    // packed rows [0, T_long) belong to sequences of >= kSplitMinLen tokens
+  bool permuted;     // the packed order differs from the caller's
 };
 
+// Sequences at least this long take the split-plane projections (block
+// scales folded into the weights): their GEMM outputs differ from the
+// reference's per-block float32 sums in the last bits only, which mean
+// pooling over many tokens keeps within the reference's own spread between
+// its builds. Shorter sequences take the per-block kernel, whose sums are the
+// reference's.
+constexpr int32_t kSplitMinLen = 128;
+
 // Builds the per-batch metadata on the host and uploads it (skipped when the
-// batch shape equals the previous call's).
+// batch shape equals the previous call's). Sequences are packed long ones
+// (>= kSplitMinLen tokens) first, each group in the caller's order; the
+// outputs go back to the caller's order through out_off.
 int upload_meta(sem_model* m, const int32_t* offsets, int B, const int32_t* dims, MetaPtrs* mp) {
   const int64_t T = offsets[B];
   int32_t* base = m->meta.as<int32_t>();
@@ -292,13 +318,33 @@ int upload_meta(sem_model* m, const int32_t* offsets, int B, const int32_t* dims
   int32_t* d_tseq = d_cu + (B + 1);
   int32_t* d_trow = d_tseq + max_tiles;
   int32_t* d_dims = d_trow + max_tiles;
-  uintptr_t p = reinterpret_cast<uintptr_t>(d_dims + B);
+  int32_t* d_src = d_dims + B;
+  uintptr_t p = reinterpret_cast<uintptr_t>(d_src + T);
   p = (p + 7) & ~uintptr_t(7);
   int64_t* d_off = reinterpret_cast<int64_t*>(p);
   bool same = (int)m->last_offsets.size() == B + 1 &&
               std::memcmp(m->last_offsets.data(), offsets, sizeof(int32_t) * (B + 1)) == 0 &&
               (int)m->last_dims.size() == B && std::memcmp(m->last_dims.data(), dims, sizeof(int32_t) * B) == 0;
   if (!same) {
+    // packed order: long sequences, then short ones (stable)
+    std::vector<int32_t> order;
+    order.reserve(B);
+    int64_t t_long = 0;
+    for (int s = 0; s < B; ++s)
+      if (offsets[s + 1] - offsets[s] >= kSplitMinLen) {
+        order.push_back(s);
+        t_long += offsets[s + 1] - offsets[s];
+      }
+    for (int s = 0; s < B; ++s)
+      if (offsets[s + 1] - offsets[s] < kSplitMinLen) order.push_back(s);
+    bool permuted = false;
+    for (int s = 0; s < B; ++s) permuted |= order[s] != s;
+    std::vector<int64_t> caller_off(B);
+    int64_t acc = 0;
+    for (int s = 0; s < B; ++s) {
+      caller_off[s] = acc;
+      acc += dims[s];
+    }
     size_t bytes = (size_t)(reinterpret_cast<uint8_t*>(d_off + B) - reinterpret_cast<uint8_t*>(base));
     HostBuf& hb = m->ctx->pinned;
     SEM_CUDA(cudaStreamSynchronize(m->ctx->stream));  // the pinned buffer may still feed an earlier copy
@@ -310,35 +356,44 @@ int upload_meta(sem_model* m, const int32_t* offsets, int B, const int32_t* dims
     int32_t* h_tseq = h_cu + (B + 1);
     int32_t* h_trow = h_tseq + max_tiles;
     int32_t* h_dims = h_trow + max_tiles;
+    int32_t* h_src = h_dims + B;
     int64_t* h_off = reinterpret_cast<int64_t*>(reinterpret_cast<uint8_t*>(h) +
                                                 (reinterpret_cast<uint8_t*>(d_off) - reinterpret_cast<uint8_t*>(base)));
     int32_t nt = 0;
-    int64_t acc = 0;
+    int32_t r = 0;
     for (int s = 0; s < B; ++s) {
-      h_cu[s] = offsets[s];
-      for (int32_t r = offsets[s]; r < offsets[s + 1]; ++r) {
-        h_row_seq[r] = s;
-        h_row_pos[r] = r - offsets[s];
+      const int o = order[s];
+      const int32_t len = offsets[o + 1] - offsets[o];
+      h_cu[s] = r;
+      for (int32_t i = 0; i < len; ++i) {
+        h_row_seq[r + i] = s;
+        h_row_pos[r + i] = i;
+        h_src[r + i] = offsets[o] + i;
       }
-      for (int32_t r = offsets[s]; r < offsets[s + 1]; r += kAttnTileRows) {
+      for (int32_t i = 0; i < len; i += kAttnTileRows) {
         h_tseq[nt] = s;
-        h_trow[nt] = r;
+        h_trow[nt] = r + i;
         ++nt;
       }
-      h_dims[s] = dims[s];
-      h_off[s] = acc;
-      acc += dims[s];
+      h_dims[s] = dims[o];
+      h_off[s] = caller_off[o];
+      r += len;
     }
-    h_cu[B] = offsets[B];
+    h_cu[B] = r;
     SEM_CUDA(cudaMemcpyAsync(base, h, bytes, cudaMemcpyHostToDevice, m->ctx->stream));
     m->last_offsets.assign(offsets, offsets + B + 1);
     m->last_dims.assign(dims, dims + B);
     m->n_tiles = nt;
+    m->t_long = t_long;
+    m->permuted = permuted;
   }
   mp->seq = SeqMeta{d_row_seq, d_row_pos, d_cu, (int32_t)T, (int32_t)B};
   mp->tiles = AttnTiles{d_tseq, d_trow, m->n_tiles};
   mp->out_dims = d_dims;
   mp->out_off = d_off;
+  mp->src_row = d_src;
+  mp->T_long = m->t_long;
+  mp->permuted = m->permuted;
   return SEM_OK;
 }
 
@@ -382,6 +437,21 @@ int run_forward(sem_model* m, const int32_t* d_ids, const MetaPtrs& mp, float* d
   __half *qh = hb, *ql = qh + T * nh * hd, *kh = ql + T * nh * hd, *kl = kh + T * hd, *vh = kl + T * hd,
          *vl = vh + T * hd;
   auto slot = [&](int l, int k) { return amax + (size_t)(4 * l + k) * B; };
+  // Q8_0 projection of all packed rows: rows [0, t_split) (long sequences)
+  // through launch_q8_proj, the rest through the per-block kernel. out_cols:
+  // columns of one output row (N, or N / 2 for gate/up).
+  const int q8_path = get_q8_path();
+  const int64_t t_split = q8_path == 3 ? T : q8_path == 1 ? 0 : mp.T_long;
+  auto q8 = [&](const Q8Proj& w, int N, int K, const uint32_t* a_absmax, float* out, int out_cols, int epi,
+                uint32_t* out_absmax) -> cudaError_t {
+    cudaError_t e = cudaSuccess;
+    if (t_split > 0)
+      e = launch_q8_proj(codes, w, (int)t_split, N, K, a_absmax, sm.row_seq, out, epi, out_absmax, err, st);
+    if (e == cudaSuccess && T > t_split)
+      e = launch_gemm_q8(codes + t_split * K, w.codes, w.scales, (int)(T - t_split), N, K, a_absmax,
+                         sm.row_seq + t_split, out + t_split * out_cols, epi, out_absmax, err, st);
+    return e;
+  };
   SEM_LAUNCH(kStEmbed, cudaMemsetAsync(amax, 0, (size_t)(4 * L + 1) * B * 4, st));
   SEM_LAUNCH(kStEmbed, cudaMemsetAsync(m->errflag.p, 0, 8, st));
   SEM_LAUNCH(kStEmbed, launch_embed(d_ids, m->emb, m->emb_s, c.vocab_size, H, hid, (int)T, m->errflag.as<uint32_t>(), st));
@@ -390,19 +460,18 @@ int run_forward(sem_model* m, const int32_t* d_ids, const MetaPtrs& mp, float* d
     const LayerW& w = m->layers[l];
     // attention block (model_int8.go:191-210)
     SEM_LAUNCH(kStQuant, launch_quantize(hid, inv, w.attn_norm, H, sm, slot(l, 0), codes, st));
-    SEM_LAUNCH(kStGemmQKV, launch_gemm_q8(codes, w.qkv, w.qkv_s, (int)T, qkvN, H, slot(l, 0), sm.row_seq, big, kEpiStore, nullptr, err, st));
+    SEM_LAUNCH(kStGemmQKV, q8(w.qkv, qkvN, H, slot(l, 0), big, qkvN, kEpiStore, nullptr));
     SEM_LAUNCH(kStQKNormRope, launch_qk_norm_rope(big, w.q_norm, w.k_norm, m->rope_cos, m->rope_sin, c.norm_eps, nh, sm, qh, ql, kh, kl,
                                    vh, vl, st));
     SEM_LAUNCH(kStAttention, launch_attention(qh, ql, kh, kl, vh, vl, nh, c.attention_scale, sm, mp.tiles, att, slot(l, 1), err, st));
     SEM_LAUNCH(kStQuant, launch_quantize(att, nullptr, nullptr, H, sm, slot(l, 1), codes, st));
-    SEM_LAUNCH(kStGemmO, launch_gemm_q8(codes, w.o, w.o_s, (int)T, H, H, slot(l, 1), sm.row_seq, big, kEpiStore, nullptr, err, st));
+    SEM_LAUNCH(kStGemmO, q8(w.o, H, H, slot(l, 1), big, H, kEpiStore, nullptr));
     SEM_LAUNCH(kStResidual, launch_residual_norm(big, w.post_attn, hid, w.ffn_norm, H, c.norm_eps, sm, inv, slot(l, 2), st));
     // MLP block (model_int8.go:213-232)
     SEM_LAUNCH(kStQuant, launch_quantize(hid, inv, w.ffn_norm, H, sm, slot(l, 2), codes, st));
-    SEM_LAUNCH(kStGemmGateUp, launch_gemm_q8(codes, w.gu, w.gu_s, (int)T, 2 * F, H, slot(l, 2), sm.row_seq, big, kEpiGeluUp, slot(l, 3),
-                              err, st));
+    SEM_LAUNCH(kStGemmGateUp, q8(w.gu, 2 * F, H, slot(l, 2), big, F, kEpiGeluUp, slot(l, 3)));
     SEM_LAUNCH(kStQuant, launch_quantize(big, nullptr, nullptr, F, sm, slot(l, 3), codes, st));
-    SEM_LAUNCH(kStGemmDown, launch_gemm_q8(codes, w.down, w.down_s, (int)T, H, F, slot(l, 3), sm.row_seq, att, kEpiStore, nullptr, err, st));
+    SEM_LAUNCH(kStGemmDown, q8(w.down, H, F, slot(l, 3), att, H, kEpiStore, nullptr));
     const bool last = l + 1 == L;
     const float* next_w = last ? m->out_norm : m->layers[l + 1].attn_norm;
     SEM_LAUNCH(kStResidual, launch_residual_norm(att, w.post_ffw, hid, next_w ? next_w : w.ffn_norm, H, c.norm_eps, sm, inv,
@@ -445,7 +514,13 @@ int model_embed(sem_model* m, const int32_t* ids, const int32_t* offsets, int32_
   if ((rc = ensure_workspace(m, T, B, out_floats))) return rc;
   MetaPtrs mp;
   if ((rc = upload_meta(m, offsets, B, dims.data(), &mp))) return rc;
-  SEM_CUDA(cudaMemcpyAsync(m->ids.p, ids, (size_t)T * 4, cudaMemcpyHostToDevice, ctx->stream));
+  if (mp.permuted) {  // ids in the packed order (long sequences first)
+    SEM_CUDA(m->ids_in.ensure((size_t)T * 4));
+    SEM_CUDA(cudaMemcpyAsync(m->ids_in.p, ids, (size_t)T * 4, cudaMemcpyHostToDevice, ctx->stream));
+    SEM_CUDA(launch_gather_i32(m->ids_in.as<int32_t>(), mp.src_row, m->ids.as<int32_t>(), T, ctx->stream));
+  } else {
+    SEM_CUDA(cudaMemcpyAsync(m->ids.p, ids, (size_t)T * 4, cudaMemcpyHostToDevice, ctx->stream));
+  }
   if ((rc = run_forward(m, m->ids.as<int32_t>(), mp, m->out.as<float>(), ctx->stream))) return rc;
   SEM_CUDA(cudaMemcpyAsync(out, m->out.p, (size_t)out_floats * 4, cudaMemcpyDeviceToHost, ctx->stream));
   SEM_CUDA(ctx->pinned.ensure(64));
@@ -483,6 +558,10 @@ int model_embed_device(sem_model* m, const int32_t* d_ids, const int32_t* h_offs
     SEM_CUDA(cudaStreamWaitEvent(st, ev, 0));
     cudaEventDestroy(ev);
   }
+  if (mp.permuted) {  // ids in the packed order (long sequences first)
+    SEM_CUDA(launch_gather_i32(d_ids, mp.src_row, m->ids.as<int32_t>(), h_offsets[B], st));
+    d_ids = m->ids.as<int32_t>();
+  }
   return run_forward(m, d_ids, mp, d_out, st);
 }
 
@@ -501,10 +580,13 @@ int q8_weight_create(sem_context* ctx, const void* w_q8, int32_t k_in, int32_t n
   w->n_out = n_out;
   SEM_CUDA(w->codes.ensure((size_t)k_in * n_out * 2));
   SEM_CUDA(w->scales.ensure((size_t)n_out * (k_in / 32) * 4));
+  SEM_CUDA(w->hi.ensure((size_t)k_in * n_out * 2));
+  SEM_CUDA(w->lo.ensure((size_t)k_in * n_out * 2));
+  SEM_CUDA(w->rscale.ensure((size_t)n_out * 4));
   DevBuf staging;
   sem_tensor_view t{"weight", kQ8, 2, {(uint64_t)k_in, (uint64_t)n_out, 0, 0}, w_q8,
                     (uint64_t)n_out * (k_in / 32) * 34};
-  int rc = upload_q8_proj(ctx, staging, &t, n_out, k_in, w->codes.as<__half>(), w->scales.as<float>(), 0);
+  int rc = upload_q8_proj(ctx, staging, &t, n_out, k_in, w->proj(), 0);
   if (rc) return rc;
   *out = w.release();
   return SEM_OK;
@@ -524,8 +606,8 @@ int q8_gemm(sem_q8_weight* w, const float* d_a, int32_t M, float* d_c, void* d_c
   SEM_CUDA(launch_absmax(d_a, (int64_t)M * w->k_in, d_absmax, st));
   __half* codes = static_cast<__half*>(d_codes);
   SEM_CUDA(launch_quantize(d_a, nullptr, nullptr, w->k_in, meta, d_absmax, codes, st));
-  SEM_CUDA(launch_gemm_q8(codes, w->codes.as<__half>(), w->scales.as<float>(), M, w->n_out, w->k_in, d_absmax, nullptr,
-                          d_c, kEpiStore, nullptr, nullptr, st));
+  SEM_CUDA(launch_q8_proj(codes, w->proj(), M, w->n_out, w->k_in, d_absmax, nullptr, d_c, kEpiStore, nullptr, nullptr,
+                          st));
   return SEM_OK;
 }
 
@@ -536,8 +618,8 @@ int q8_matmul_int8(sem_q8_weight* w, const void* d_codes, const uint32_t* d_absm
   if (reinterpret_cast<uintptr_t>(d_codes) & 15) return set_error(SEM_EINVAL, "q8 matmul: codes must be 16-byte aligned");
   DeviceGuard dg(w->ctx->device);
   cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : w->ctx->stream;
-  SEM_CUDA(launch_gemm_q8(static_cast<const __half*>(d_codes), w->codes.as<__half>(), w->scales.as<float>(), M, w->n_out,
-                          w->k_in, d_absmax, nullptr, d_c, kEpiStore, nullptr, nullptr, st));
+  SEM_CUDA(launch_q8_proj(static_cast<const __half*>(d_codes), w->proj(), M, w->n_out, w->k_in, d_absmax, nullptr, d_c,
+                          kEpiStore, nullptr, nullptr, st));
   return SEM_OK;
 }
 
@@ -705,6 +787,8 @@ int sem_q8_matmul_int8(sem_q8_weight* w, const void* d_codes, const uint32_t* d_
                        void* stream) {
   return sem::q8_matmul_int8(w, d_codes, d_absmax, m, d_c, stream);
 }
+
+int sem_q8_path(int32_t mode) { return sem::set_q8_path(mode); }
 
 int sem_q8_gemm(sem_q8_weight* w, const float* d_a, int32_t m, float* d_c, void* d_codes, uint32_t* d_absmax,
                 void* stream) {

@@ -27,6 +27,12 @@ cudaError_t launch_repack_q8_0(const uint8_t* raw, int64_t rows, int cols, int8_
 cudaError_t launch_repack_q8_0_f16(const uint8_t* raw, int64_t rows, int cols, __half* dst_codes,
                                    float* dst_scales, int64_t dst_row_offset, cudaStream_t stream);
 
+// Projection weights for the split-plane GEMM: Q8_0 blocks of `rows` x `cols`
+// -> fp16 planes hi/lo [dst_row_offset + r][cols] with hi + lo = q * d * 2^S_r
+// and row_scale[dst_row_offset + r] = 2^-S_r (runtime f16 decoder).
+cudaError_t launch_repack_q8_0_split(const uint8_t* raw, int64_t rows, int cols, __half* hi, __half* lo,
+                                     float* row_scale, int64_t dst_row_offset, cudaStream_t stream);
+
 // ---- forward-pass element-wise kernels (model_kernels.cu) ----
 struct SeqMeta {
   const int32_t* row_seq;   // [T] sequence of each packed row
@@ -50,6 +56,9 @@ cudaError_t launch_row_stats(const float* x, const float* w, int H, float eps, S
 // fp16 (exact), the tensor-core GEMM's operand type.
 cudaError_t launch_quantize(const float* x, const float* inv_rms, const float* w, int K, SeqMeta meta,
                             const uint32_t* absmax, __half* codes, cudaStream_t stream);
+
+// dst[i] = src[idx[i]] for i < n (packing token ids in the forward's order).
+cudaError_t launch_gather_i32(const int32_t* src, const int32_t* idx, int32_t* dst, int64_t n, cudaStream_t stream);
 
 // Max |x| over n values, atomically into slot[0].
 cudaError_t launch_absmax(const float* x, int64_t n, uint32_t* slot, cudaStream_t stream);
@@ -82,6 +91,34 @@ enum GemmEpilogue { kEpiStore = 0, kEpiGeluUp = 1 };
 cudaError_t launch_gemm_q8(const __half* a_codes, const __half* w_codes, const float* w_scales, int M, int N,
                            int K, const uint32_t* a_absmax, const int32_t* row_seq, float* c, int epilogue,
                            uint32_t* out_absmax, uint32_t* err, cudaStream_t stream);
+
+// The same product with the block scales folded into split fp16 weight planes
+// (gemm_split.cu): w_hi/w_lo [N][K], row_scale [N]; K % 64 == 0, N % 128 == 0
+// (gate/up: N/2 % 128 == 0). Same epilogues and outputs as launch_gemm_q8.
+cudaError_t launch_gemm_q8_split(const __half* a_codes, const __half* w_hi, const __half* w_lo, const float* row_scale,
+                                 int M, int N, int K, const uint32_t* a_absmax, const int32_t* row_seq, float* c,
+                                 int epilogue, uint32_t* out_absmax, uint32_t* err, cudaStream_t stream);
+
+// A Q8_0 projection weight [N][K] in both device layouts: fp16 codes with
+// fp32 block scales (launch_gemm_q8) and the split planes
+// (launch_gemm_q8_split).
+struct Q8Proj {
+  const __half* codes;     // [N][K]
+  const float* scales;     // [N][K/32]
+  const __half* hi;        // [N][K]
+  const __half* lo;        // [N][K]
+  const float* row_scale;  // [N]
+};
+// Picks the kernel for M tokens: the split-plane GEMM once its tiles fill
+// every SM, else the per-block kernel (narrower token tiles).
+cudaError_t launch_q8_proj(const __half* a_codes, const Q8Proj& w, int M, int N, int K, const uint32_t* a_absmax,
+                           const int32_t* row_seq, float* c, int epilogue, uint32_t* out_absmax, uint32_t* err,
+                           cudaStream_t stream);
+// Process-wide kernel choice: 0 auto, 1 per-block, 2 split-plane (launch_q8_proj
+// always; the forward's long-sequence rows), 3 split-plane for every forward
+// row; returns the previous one (-1: unknown mode, nothing changed).
+int set_q8_path(int mode);
+int get_q8_path();
 
 // ---- attention (attention.cu) ----
 constexpr int kAttnTileRows = 128;  // query rows per attention tile

@@ -124,6 +124,75 @@ cudaError_t launch_repack_q8_0_f16(const uint8_t* raw, int64_t rows, int cols, _
   return cudaGetLastError();
 }
 
+// Projection weights for the split-plane GEMM (gemm_split.cu): one warp per
+// row. w = q * d (exact in float32: an int8 times an fp16) is scaled by the
+// power of two 2^S that puts the row's largest |w| in [2^13, 2^14); then
+// hi = fp16(w * 2^S), lo = fp16(w * 2^S - hi) (the difference is exact) and
+// row_scale = 2^-S.
+__global__ void repack_q8_0_split_kernel(const uint8_t* __restrict__ raw, int64_t rows, int nb,
+                                         __half* __restrict__ hi, __half* __restrict__ lo,
+                                         float* __restrict__ row_scale, int64_t dst_row_offset) {
+  const int64_t r = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (r >= rows) return;  // whole warps: rows is warp-uniform
+  const uint8_t* row = raw + r * nb * 34;
+  float m = 0.0f;
+  for (int b = lane; b < nb; b += 32) {
+    const uint8_t* blk = row + (int64_t)b * 34;
+    const float d = fabsf(f16_runtime((uint16_t)(blk[0] | (blk[1] << 8))));
+    int qm = 0;
+    for (int k = 0; k < 32; ++k) qm = max(qm, abs((int)(int8_t)blk[2 + k]));
+    m = fmaxf(m, __fmul_rn((float)qm, d));
+  }
+  m = warp_max(m);
+  int e = 0;
+  if (m > 0.0f) frexpf(m, &e);  // m = f * 2^e, f in [0.5, 1)
+  const int S = m > 0.0f ? 14 - e : 0;
+  const int64_t dr = dst_row_offset + r;
+  if (lane == 0) row_scale[dr] = ldexpf(1.0f, -S);
+  for (int b = lane; b < nb; b += 32) {
+    const uint8_t* blk = row + (int64_t)b * 34;
+    const float d = f16_runtime((uint16_t)(blk[0] | (blk[1] << 8)));
+    __align__(16) __half vh[32], vl[32];
+#pragma unroll
+    for (int k = 0; k < 32; ++k) {
+      const float w = ldexpf(__fmul_rn((float)(int8_t)blk[2 + k], d), S);
+      const __half h = __float2half_rn(w);
+      vh[k] = h;
+      vl[k] = __float2half_rn(__fsub_rn(w, __half2float(h)));
+    }
+    uint4* dh = reinterpret_cast<uint4*>(hi + dr * (int64_t)nb * 32 + (int64_t)b * 32);
+    uint4* dl = reinterpret_cast<uint4*>(lo + dr * (int64_t)nb * 32 + (int64_t)b * 32);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      dh[k] = reinterpret_cast<const uint4*>(vh)[k];
+      dl[k] = reinterpret_cast<const uint4*>(vl)[k];
+    }
+  }
+}
+
+cudaError_t launch_repack_q8_0_split(const uint8_t* raw, int64_t rows, int cols, __half* hi, __half* lo,
+                                     float* row_scale, int64_t dst_row_offset, cudaStream_t stream) {
+  if (rows == 0) return cudaSuccess;
+  const int nb = cols / 32;
+  const int64_t threads = rows * 32;
+  repack_q8_0_split_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, stream>>>(raw, rows, nb, hi, lo, row_scale,
+                                                                                   dst_row_offset);
+  return cudaGetLastError();
+}
+
+__global__ void gather_i32_kernel(const int32_t* __restrict__ src, const int32_t* __restrict__ idx,
+                                  int32_t* __restrict__ dst, int64_t n) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) dst[i] = src[idx[i]];
+}
+
+cudaError_t launch_gather_i32(const int32_t* src, const int32_t* idx, int32_t* dst, int64_t n, cudaStream_t stream) {
+  if (n == 0) return cudaSuccess;
+  gather_i32_kernel<<<(unsigned)((n + 255) / 256), 256, 0, stream>>>(src, idx, dst, n);
+  return cudaGetLastError();
+}
+
 // ---------------------------------------------------------------------------
 // Token embedding: DequantizeQ8_0Row then the sqrt(H) scale
 // (model_int8.go:167-184, gguf/tensor.go:157-177). 16 elements per thread.

@@ -8,9 +8,9 @@
 // (TMEM lanes, the query codes resident in shared memory) x one contiguous part
 // of the corpus, streamed as 256-row tiles through a TMA ring of 128-byte K
 // slices; TMEM holds two score tiles so the MMAs of tile t+1 overlap the
-// top-k filter of tile t. Warp 0 issues TMA, warp 1 the MMAs, warps 4-11 (two
-// per TMEM lane quarter, each half of a tile's rows) keep a per-query top-16
-// in registers: rows arrive in ascending order, so a candidate only enters
+// top-k filter of tile t. Warps 0 and 2 issue TMA (alternate stages), warp 1
+// the MMAs, warps 4-11 (two per TMEM lane quarter, each half of a tile's rows)
+// keep a per-query top-16 in registers: rows arrive in ascending order, so a candidate only enters
 // when its score is strictly above the k-th best (a tie never beats a lower
 // row). The k-th best score of each stream is also published, to the other
 // half through shared memory and to the CTAs of later corpus parts through a
@@ -209,14 +209,21 @@ __global__ void __launch_bounds__(S_THREADS, 1)
 
   if (warp < 4) {
     asm volatile("setmaxnreg.dec.sync.aligned.u32 56;");
-    if (warp == 0 && lane == 0) {
-      // ---------------- TMA producer ----------------
-      mbar_arrive_expect_tx(qfull, nqb * S_QBOX);
-      for (int b = 0; b < nqb; ++b) tma_load_2d(&tm_q, qfull, sQ + b * S_QBOX, b * SKB, qt * SQ);
+    if ((warp == 0 || warp == 2) && lane == 0) {
+      // ---------------- TMA producers ----------------
+      // Two threads (warps 0 and 2) issue alternate ring iterations: one
+      // thread's stream of tile loads completes at about one stage per
+      // microsecond, so two streams double the L2 -> SM rate of the SM.
+      const uint32_t me = warp >> 1;
+      if (me == 0) {
+        mbar_arrive_expect_tx(qfull, nqb * S_QBOX);
+        for (int b = 0; b < nqb; ++b) tma_load_2d(&tm_q, qfull, sQ + b * S_QBOX, b * SKB, qt * SQ);
+      }
       uint32_t it = 0;
       bool ok = true;
       for (int t = 0; ok && t < ntiles; ++t)
         for (int b = 0; b < nqb; ++b, ++it) {
+          if ((it & 1) != me) continue;
           const uint32_t s = it % nst, u = it / nst;
           if (!mbar_wait(&rempty[s], (u & 1) ^ 1, abort_flag, err, 1u)) {
             ok = false;
@@ -225,9 +232,10 @@ __global__ void __launch_bounds__(S_THREADS, 1)
           mbar_arrive_expect_tx(&rfull[s], S_TILE);
           tma_load_2d(&tm_c, &rfull[s], sRing + s * S_TILE, b * SKB, (int)(r0 + (int64_t)t * SN));
         }
+      // `it` is one past the last iteration this thread issued or skipped
       for (uint32_t j = it > (uint32_t)nst ? it - nst : 0; j < it; ++j)
-        mbar_wait_drain(&rfull[j % nst], (j / nst) & 1);
-      mbar_wait_drain(qfull, 0);
+        if ((j & 1) == me) mbar_wait_drain(&rfull[j % nst], (j / nst) & 1);
+      if (me == 0) mbar_wait_drain(qfull, 0);
     } else if (warp == 1 && lane == 0) {
       // ---------------- MMA issuer ----------------
       constexpr uint32_t idesc = idesc_i8(SQ, SN);

@@ -144,6 +144,30 @@ int sem_q8_gemm(sem_q8_weight *w, const float *d_a, int32_t m, float *d_c, void 
 int sem_q8_matmul_int8(sem_q8_weight *w, const void *d_codes, const uint32_t *d_absmax, int32_t m, float *d_c,
                        void *stream);
 
+/* Which tensor-core kernel the Q8_0 projections use (process-wide, every
+ * model and weight). Two kernels exist: the per-block kernel sums each
+ * 32-element block exactly and scales it in float32 as the reference does;
+ * the split-plane kernel folds the block scales into two fp16 weight planes
+ * (one TMEM drain per tile, ~1.5x faster) and differs from the reference's
+ * sums in the last float32 bits. sem_embed packs sequences of >= 128 tokens
+ * first; only their rows may take the split-plane kernel (mean pooling over
+ * many tokens keeps the difference within the reference's own spread between
+ * its builds), shorter sequences always take the per-block kernel.
+ *   SEM_Q8_PATH_AUTO (default): long-sequence rows (all rows for
+ *     sem_q8_gemm) take the split-plane kernel when its 128 x 256-token tiles
+ *     fill every SM, else the per-block kernel;
+ *   SEM_Q8_PATH_BLOCK: the per-block kernel everywhere;
+ *   SEM_Q8_PATH_SPLIT: the split-plane kernel for long-sequence rows (all
+ *     rows for sem_q8_gemm) whatever their count;
+ *   SEM_Q8_PATH_SPLIT_ALL: the split-plane kernel for every row (testing).
+ * A tuning and testing switch with no counterpart in the reference. Returns
+ * the previous setting, or -1 for an unknown mode. */
+#define SEM_Q8_PATH_AUTO 0
+#define SEM_Q8_PATH_BLOCK 1
+#define SEM_Q8_PATH_SPLIT 2
+#define SEM_Q8_PATH_SPLIT_ALL 3
+int sem_q8_path(int32_t mode);
+
 /* sem_q8_gemm without caller scratch, for callers that cannot allocate device
  * memory (a host runtime that owns the whole device pool and passes only input
  * and output buffers, or a request path with a memory budget fixed at start-up

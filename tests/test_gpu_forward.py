@@ -65,6 +65,48 @@ def test_ragged_lengths_and_matryoshka_dims(gpu_model, oracle_model):
     check_parity(gpu_model, oracle_model, ids, offs, dims, "ragged")
 
 
+@pytest.fixture
+def split_path():
+    """Forces the split-plane projection kernel (block scales folded into two
+    fp16 weight planes) for the rows of sequences of >= 128 tokens, which the
+    automatic choice only takes when their tiles fill every SM; shorter
+    sequences keep the per-block kernel."""
+    import _lib
+    lib = _lib.load()
+    prev = lib.sem_q8_path(2)
+    yield
+    lib.sem_q8_path(prev)
+
+
+@pytest.mark.parametrize("case", ["long", "mixed", "2x512"])
+def test_split_projection_forward_parity(gpu_model, oracle_model, split_path, case):
+    if case == "long":
+        lengths = [128, 160, 200, 256, 300, 512]
+        ids, offs = synth.token_batch(111, lengths, TEST_VOCAB)
+        check_parity(gpu_model, oracle_model, ids, offs, [768, 512, 256, 128, 768, 768], "split long")
+    elif case == "mixed":
+        # short and long sequences interleaved: long ones are packed first and
+        # the outputs return in the caller's order
+        lengths = [5, 300, 17, 128, 127, 1, 260, 2, 64]
+        dims = [768, 128, 512, 768, 256, 768, 512, 768, 768]
+        ids, offs = synth.token_batch(222, lengths, TEST_VOCAB)
+        check_parity(gpu_model, oracle_model, ids, offs, dims, "split mixed")
+    else:
+        ids, offs = synth.token_batch(303, [512, 512], TEST_VOCAB)
+        check_parity(gpu_model, oracle_model, ids, offs, [768, 768], "split 2x512", strict=True)
+
+
+def test_packed_order_matches_caller_order(gpu_model):
+    # the same sequences embedded alone and inside a mixed batch that the
+    # forward repacks (long sequences first) give the same vectors
+    lengths = [3, 200, 40, 150]
+    ids, offs = synth.token_batch(333, lengths, TEST_VOCAB)
+    batch = gpu_model.forward_batch(ids, offs, 768)
+    for i in range(len(lengths)):
+        alone = gpu_model.forward_batch(ids[offs[i]:offs[i + 1]], np.array([0, lengths[i]]), 768)[0]
+        np.testing.assert_allclose(batch[i], alone, atol=1e-6)
+
+
 def test_long_sequences_512(gpu_model, oracle_model):
     # the bench's sequence length: the north_star bound holds without widening
     ids, offs = synth.token_batch(303, [512, 512], TEST_VOCAB)
@@ -101,15 +143,34 @@ def test_errors_match_reference(gpu_model):
         gpu_model.forward_with_dim([2, 5], 0)
 
 
-def test_q8_gemm_matches_oracle(ctx):
-    # BASELINE config 2 shapes (one scale for the whole activation buffer)
+@pytest.mark.parametrize("path", [0, 1, 2])
+def test_q8_gemm_matches_oracle(ctx, path):
+    # BASELINE config 2 shapes (one scale for the whole activation buffer), with
+    # the automatic kernel choice (0), the per-block kernel (1) and the
+    # split-plane kernel (2)
     import torch
     import oracle
     import runtime
+    import _lib
     rng = np.random.default_rng(11)
-    # tile edges: M below, between and above the 128/256-token tiles; K = 1152
-    # wraps the 4-stage ring several times; N = 3072 spans 24 weight tiles
-    for K, N, M in ((768, 256, 64), (1152, 768, 200), (768, 3072, 33), (768, 768, 4133), (1152, 1152, 1)):
+    prev = _lib.load().sem_q8_path(path)
+    # tile edges: M below, between and above the 96/192/256-token tiles;
+    # K = 1152 wraps the stage rings several times; N = 3072 spans 24 weight
+    # tiles; the last two are large enough for the automatic choice to take
+    # the split-plane kernel
+    shapes = [(768, 256, 64), (1152, 768, 200), (768, 3072, 33), (768, 768, 4133), (1152, 1152, 1),
+              (768, 3072, 2000), (1152, 768, 6500)]
+    try:
+        _gemm_cases(ctx, rng, shapes)
+    finally:
+        _lib.load().sem_q8_path(prev)
+
+
+def _gemm_cases(ctx, rng, shapes):
+    import torch
+    import oracle
+    import runtime
+    for K, N, M in shapes:
         raw = synth.q8_0_blocks(rng, N, K)
         a = rng.standard_normal((M, K)).astype(np.float32)
         w = runtime.Q8Weight(ctx, raw, K, N)
