@@ -16,16 +16,21 @@
 // score; fastExp(x - d) = fastExp(x) * e^-d up to O(1e-3 d), and the common
 // factor cancels in the normalisation.
 //
-// One CTA = 128 query rows of one (sequence, head). Q (hi and lo, 128 KB)
-// stays in shared memory; K and V stream through a ring of six 16 KB slots
-// (one fp16 plane of 64 keys x 128 dims each), loaded by TMA. TMEM holds O
-// (256 fp32 columns), the scores of a 64-key tile (two buffers of 64 columns)
-// and P (two buffers of 64 columns: p_hi and p_lo as packed fp16 pairs, row =
-// lane), so the P.V MMAs take their A operand straight from TMEM. Warps 0
+// One CTA = 128 query rows of one (sequence, head). Q hi (64 KB) stays in
+// shared memory and Q lo in TMEM; K and V stream through a ring of five 32 KB
+// slots (one fp16 plane of 64 keys x 256 dims each, fetched by one 3-D TMA
+// copy: a thread's tile loads complete at a rate set by the copies in flight,
+// so few large copies feed the SM fastest), deep enough that the next tile's
+// keys load while P.V runs. TMEM holds O (256 fp32
+// columns), two 64-column score buffers and Q lo (128 columns, two fp16 per
+// column, row = lane): the q_lo * k_hi MMAs take A from TMEM. The softmax
+// writes P in place over the scores it has read (per 16 keys: 8 columns of
+// p_hi then 8 of p_lo, packed fp16 pairs), so the P.V MMAs also take A from
+// TMEM, and a score buffer is free again once its P.V MMAs complete. Warps 0
 // and 2 issue TMA (alternate slots), warp 1 the MMAs, warps 4-11 (two per
-// TMEM lane quarter, each half of a tile's keys) do the softmax with packed fp32 arithmetic: they read
-// scores from TMEM, write P back into TMEM, and at the end scale O by 1/sum
-// and store it. V is read MN-major straight from its row-major [token][dim]
+// TMEM lane quarter, each half of a tile's keys) load Q lo into TMEM and do the
+// softmax with packed fp32 arithmetic: they read scores from TMEM, write P
+// back into TMEM, and at the end scale O by 1/sum and store it. V is read MN-major straight from its row-major [token][dim]
 // layout, so sequences may start at any token. All three query heads read the
 // single KV head (GQA) through L2.
 #include <cudaTypedefs.h>
@@ -43,24 +48,24 @@ namespace {
 constexpr int HD = 256;      // head_dim
 constexpr int QT = 128;      // query rows per CTA (TMEM lanes)
 constexpr int KT = 64;       // keys per tile
-constexpr int NSLOT = 6;     // K/V ring slots
-static_assert(NSLOT % 2 == 0, "the two TMA threads own alternate slots");
-constexpr int SLOT = KT * 128 * 2;       // 16 KB: 64 keys x 128 dims, one plane
+constexpr int NSLOT = 5;     // K/V ring slots
+constexpr int SLOT = KT * HD * 2;        // 32 KB: 64 keys x 256 dims of one plane, as 4 dim blocks of 64 keys x 128 B
+constexpr int DBLK = KT * 128;           // 8 KB: one dim block of a slot
 constexpr int QBLK = QT * 128;           // 16 KB: 128 rows x 64 dims
-constexpr int SMEM_Q = 2 * 4 * QBLK;     // hi, lo x 4 dim blocks: 128 KB
-constexpr int SMEM_RING = NSLOT * SLOT;  // 96 KB
+constexpr int SMEM_Q = 4 * QBLK;         // hi x 4 dim blocks: 64 KB
+constexpr int SMEM_RING = NSLOT * SLOT;  // 160 KB
 constexpr int NS1 = 4;  // score buffers of pass 1 (in the O columns, unused until pass 2)
-// q, ring full/empty, S full/empty, P full/free, O, drain, pass-1 S full/empty
-constexpr int NBAR = 1 + 2 * NSLOT + 2 + 2 + 2 + 2 + 1 + 1 + 2 * NS1;
-constexpr int SMEM_MISC = 256 + 2 * QT * 4;  // barriers, TMEM address, [2][QT] reductions
+// q, ring full/empty, S full, P full, S/P buffer free, O, drain, pass-1 S full/empty, Q lo in TMEM
+constexpr int NBAR = 1 + 2 * NSLOT + 2 + 2 + 2 + 1 + 1 + 2 * NS1 + 1;
+constexpr int BAR_BLOCK = 320;                     // barriers, TMEM address, abort flag
+constexpr int SMEM_MISC = BAR_BLOCK + 2 * QT * 4;  // + [2][QT] reductions
 constexpr int SMEM_BYTES = 1024 + SMEM_Q + SMEM_RING + SMEM_MISC;
 constexpr int THREADS = 384;  // warpgroup 0: TMA (warps 0, 2), MMA (1), idle (3); warpgroups 1-2: softmax / epilogue
 constexpr int SM_WARPS = 8;
-// TMEM columns: O [0,256), scores [256,320) and [320,384), P [384,448) and
-// [448,512) (p_hi in the first 32 columns of a P buffer, p_lo in the next 32)
-constexpr uint32_t TM_O = 0, TM_S = 256, TM_P = 384;
+// TMEM columns: O [0,256), score / P buffers [256,320) and [320,384), Q lo [384,512)
+constexpr uint32_t TM_O = 0, TM_S = 256, TM_QLO = 384;
 static_assert(SMEM_BYTES <= 232448, "shared memory per CTA");
-static_assert(NBAR * 8 + 8 <= 256, "barrier block");
+static_assert(NBAR * 8 + 8 <= BAR_BLOCK, "barrier block");
 
 __device__ uint32_t g_attn_error;
 
@@ -112,7 +117,7 @@ __device__ __forceinline__ uint64_t umma_desc_mn_sw128(uint32_t saddr, uint32_t 
 }  // namespace
 
 __global__ void __launch_bounds__(THREADS, 1)
-    attention_tc_kernel(const __grid_constant__ CUtensorMap tm_qh, const __grid_constant__ CUtensorMap tm_ql,
+    attention_tc_kernel(const __grid_constant__ CUtensorMap tm_qh, const __half* __restrict__ ql_g,
                         const __grid_constant__ CUtensorMap tm_kh, const __grid_constant__ CUtensorMap tm_kl,
                         const __grid_constant__ CUtensorMap tm_vh, const __grid_constant__ CUtensorMap tm_vl, int nh,
                         float scale, SeqMeta meta, AttnTiles tiles, float* __restrict__ out,
@@ -126,16 +131,16 @@ __global__ void __launch_bounds__(THREADS, 1)
   uint64_t* rfull = bars + 1;
   uint64_t* rempty = rfull + NSLOT;
   uint64_t* sfull = rempty + NSLOT;
-  uint64_t* sempty = sfull + 2;
-  uint64_t* pfull = sempty + 2;
-  uint64_t* pfree = pfull + 2;
+  uint64_t* pfull = sfull + 2;
+  uint64_t* pfree = pfull + 2;  // the P.V MMAs of a buffer completed: it may take new scores
   uint64_t* ofull = pfree + 2;
   uint64_t* drain = ofull + 1;
   uint64_t* s1full = drain + 1;
   uint64_t* s1empty = s1full + NS1;
+  uint64_t* qlofull = s1empty + NS1;
   uint32_t* s_tmem = reinterpret_cast<uint32_t*>(bars + NBAR);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(s_tmem + 1);
-  float* s_red = reinterpret_cast<float*>(sRing + SMEM_RING + 256);  // [2 halves][QT]: maxima, later sums
+  float* s_red = reinterpret_cast<float*>(sRing + SMEM_RING + BAR_BLOCK);  // [2 halves][QT]: maxima, later sums
   if (!err) err = &g_attn_error;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -151,11 +156,10 @@ __global__ void __launch_bounds__(THREADS, 1)
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < NBAR; ++i) mbar_init(&bars[i], 1);
-    mbar_init(sempty, SM_WARPS);
-    mbar_init(sempty + 1, SM_WARPS);
     mbar_init(pfull, SM_WARPS);
     mbar_init(pfull + 1, SM_WARPS);
     for (int k = 0; k < NS1; ++k) mbar_init(&s1empty[k], SM_WARPS);
+    mbar_init(qlofull, SM_WARPS);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -169,7 +173,7 @@ __global__ void __launch_bounds__(THREADS, 1)
   // pass 2 = K(0), then for j = 1..: K(j), V(j-1); finally V(last). A K(j)
   // item is (hi, lo) of dim half 0 then 1 (4 slots), a V(j) item the same.
   if (warp < 4) {
-    asm volatile("setmaxnreg.dec.sync.aligned.u32 56;");
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 88;  // 128 x 88 + 256 x 192 <= 384 x 168");
     if ((warp == 0 || warp == 2) && lane == 0) {
       // ---------------- TMA producers ----------------
       // Two threads (warps 0 and 2) walk the same slot sequence and issue
@@ -182,10 +186,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       if (me == 0) {
         mbar_arrive_expect_tx(qfull, SMEM_Q);
 #pragma unroll
-        for (int b = 0; b < 4; ++b) {
-          tma_load_3d(&tm_qh, qfull, sQ + b * QBLK, b * 64, head, row0);
-          tma_load_3d(&tm_ql, qfull, sQ + (4 + b) * QBLK, b * 64, head, row0);
-        }
+        for (int b = 0; b < 4; ++b) tma_load_3d(&tm_qh, qfull, sQ + b * QBLK, b * 64, head, row0);
       }
       auto load_slot = [&](const CUtensorMap* map, int key0, int dim0) -> bool {
         if ((it & 1) != me) {
@@ -194,26 +195,21 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
         const uint32_t s = it % NSLOT, u = it / NSLOT;
         if (!mbar_wait(&rempty[s], (u & 1) ^ 1, abort_flag, err, 1u)) return false;
-        uint8_t* dst = sRing + s * SLOT;
         mbar_arrive_expect_tx(&rfull[s], SLOT);
-        tma_load_2d(map, &rfull[s], dst, dim0, key0);
-        tma_load_2d(map, &rfull[s], dst + SLOT / 2, dim0 + 64, key0);
+        tma_load_3d(map, &rfull[s], sRing + s * SLOT, dim0, key0, 0);  // 64 dims x 64 keys x 4 dim blocks
         ++it;
         return true;
       };
-      for (int j = 0; ok && j < nkt; ++j)
-        for (int h = 0; ok && h < 2; ++h) ok = load_slot(&tm_kh, s_beg + j * KT, h * 128);
+      for (int j = 0; ok && j < nkt; ++j) ok = load_slot(&tm_kh, s_beg + j * KT, 0);
       for (int j = 0; ok && j <= nkt; ++j) {
-        if (j < nkt)
-          for (int h = 0; ok && h < 2; ++h) {
-            ok = ok && load_slot(&tm_kh, s_beg + j * KT, h * 128);
-            ok = ok && load_slot(&tm_kl, s_beg + j * KT, h * 128);
-          }
-        if (j >= 1)
-          for (int h = 0; ok && h < 2; ++h) {
-            ok = ok && load_slot(&tm_vh, s_beg + (j - 1) * KT, h * 128);
-            ok = ok && load_slot(&tm_vl, s_beg + (j - 1) * KT, h * 128);
-          }
+        if (j < nkt) {
+          ok = ok && load_slot(&tm_kh, s_beg + j * KT, 0);
+          ok = ok && load_slot(&tm_kl, s_beg + j * KT, 0);
+        }
+        if (j >= 1) {
+          ok = ok && load_slot(&tm_vh, s_beg + (j - 1) * KT, 0);
+          ok = ok && load_slot(&tm_vl, s_beg + (j - 1) * KT, 0);
+        }
       }
       for (uint32_t j = it > (uint32_t)NSLOT ? it - NSLOT : 0; j < it; ++j)
         if ((j & 1) == me) mbar_wait_drain(&rfull[j % NSLOT], (j / NSLOT) & 1);
@@ -225,7 +221,8 @@ __global__ void __launch_bounds__(THREADS, 1)
       uint32_t it = 0, sfill = 0;
       bool ok = mbar_wait(qfull, 0, abort_flag, err, 2u);
       tc_fence_after();
-      const uint32_t q_hi = smem_u32(sQ), q_lo = smem_u32(sQ + 4 * QBLK);
+      const uint32_t q_hi = smem_u32(sQ), q_lo_t = tmem + TM_QLO;
+      bool qlo_ready = false;
       auto take_slot = [&](uint32_t& addr) -> bool {
         const uint32_t s = it % NSLOT, u = it / NSLOT;
         if (!mbar_wait(&rfull[s], u & 1, abort_flag, err, 2u)) return false;
@@ -242,7 +239,12 @@ __global__ void __launch_bounds__(THREADS, 1)
         uint64_t* full_bar;
         if (three) {
           const uint32_t b = sfill & 1, ub = sfill >> 1;
-          if (!mbar_wait(&sempty[b], (ub & 1) ^ 1, abort_flag, err, 2u)) return false;
+          // the buffer's previous P.V MMAs have read its P (first use: no wait)
+          if (!mbar_wait(&pfree[b], (ub & 1) ^ 1, abort_flag, err, 2u)) return false;
+          if (!qlo_ready) {
+            if (!mbar_wait(qlofull, 0, abort_flag, err, 2u)) return false;
+            qlo_ready = true;
+          }
           d_s = tmem + TM_S + b * KT;
           full_bar = &sfull[b];
           ++sfill;
@@ -254,30 +256,32 @@ __global__ void __launch_bounds__(THREADS, 1)
           ++fill1;
         }
         tc_fence_after();
+        uint32_t kh_a, kl_a = 0;
+        if (!take_slot(kh_a)) return false;
+        if (three) {  // the lo plane is the next ring slot
+          const uint32_t s = (it + 1) % NSLOT, u = (it + 1) / NSLOT;
+          if (!mbar_wait(&rfull[s], u & 1, abort_flag, err, 2u)) return false;
+          tc_fence_after();
+          kl_a = smem_u32(sRing + s * SLOT);
+        }
+#pragma unroll 1
         for (int h = 0; h < 2; ++h) {
-          uint32_t kh_a, kl_a = 0;
-          if (!take_slot(kh_a)) return false;
-          if (three) {  // the lo plane is the next ring slot
-            const uint32_t s = (it + 1) % NSLOT, u = (it + 1) / NSLOT;
-            if (!mbar_wait(&rfull[s], u & 1, abort_flag, err, 2u)) return false;
-            tc_fence_after();
-            kl_a = smem_u32(sRing + s * SLOT);
-          }
 #pragma unroll
           for (int k16 = 0; k16 < 8; ++k16) {
-            const int db = 2 * h + k16 / 4;               // Q dim block
+            const int db = 2 * h + k16 / 4;               // dim block (of Q and of the K slot)
             const uint32_t koff = (uint32_t)(k16 % 4) * 32;  // K=16 slice within the 128-byte row
-            const uint32_t kb = (uint32_t)(k16 / 4) * (SLOT / 2) + koff;
+            const uint32_t kb = (uint32_t)db * DBLK + koff;
             const uint32_t acc = (h | k16) ? 1u : 0u;
             umma_f16(d_s, umma_desc_k_sw128(q_hi + db * QBLK + koff), umma_desc_k_sw128(kh_a + kb), idesc_qk, acc);
             if (three) {
               umma_f16(d_s, umma_desc_k_sw128(q_hi + db * QBLK + koff), umma_desc_k_sw128(kl_a + kb), idesc_qk, 1u);
-              umma_f16(d_s, umma_desc_k_sw128(q_lo + db * QBLK + koff), umma_desc_k_sw128(kh_a + kb), idesc_qk, 1u);
+              // q_lo from TMEM: dims 128h + 16k16.. are 8 packed columns
+              umma_f16_ts(d_s, q_lo_t + (uint32_t)(64 * h + 8 * k16), umma_desc_k_sw128(kh_a + kb), idesc_qk, 1u);
             }
           }
-          free_slot();
-          if (three) free_slot();
         }
+        free_slot();
+        if (three) free_slot();
         umma_commit(full_bar);
         return true;
       };
@@ -286,29 +290,32 @@ __global__ void __launch_bounds__(THREADS, 1)
         const uint32_t pb = j & 1;
         if (!mbar_wait(&pfull[pb], (j >> 1) & 1, abort_flag, err, 2u)) return false;
         tc_fence_after();
-        const uint32_t p_hi = tmem + TM_P + pb * 64, p_lo = p_hi + 32;
+        const uint32_t p_buf = tmem + TM_S + pb * KT;  // P written over the scores
+        uint32_t vh_a, vl_a;
+        if (!take_slot(vh_a)) return false;
+        {
+          const uint32_t s = (it + 1) % NSLOT, u = (it + 1) / NSLOT;
+          if (!mbar_wait(&rfull[s], u & 1, abort_flag, err, 2u)) return false;
+          tc_fence_after();
+          vl_a = smem_u32(sRing + s * SLOT);
+        }
+#pragma unroll 1
         for (int h = 0; h < 2; ++h) {
-          uint32_t vh_a, vl_a;
-          if (!take_slot(vh_a)) return false;
-          {
-            const uint32_t s = (it + 1) % NSLOT, u = (it + 1) / NSLOT;
-            if (!mbar_wait(&rfull[s], u & 1, abort_flag, err, 2u)) return false;
-            tc_fence_after();
-            vl_a = smem_u32(sRing + s * SLOT);
-          }
           const uint32_t d_o = tmem + TM_O + h * 128;
+          const uint32_t vdb = (uint32_t)h * 2 * DBLK;  // dims 128h..: dim blocks 2h, 2h+1
 #pragma unroll
           for (int k16 = 0; k16 < KT / 16; ++k16) {
-            const uint32_t pcol = (uint32_t)k16 * 8;     // keys 16k16.. as 8 packed fp16 columns
+            // keys 16k16..: p_hi in 8 packed fp16 columns, then p_lo in the next 8
+            const uint32_t p_hi = p_buf + (uint32_t)k16 * 16, p_lo = p_hi + 8;
             const uint32_t voff = (uint32_t)k16 * 2048;  // two 8-key groups of V rows
             const uint32_t acc0 = (j > 0 || k16 > 0) ? 1u : 0u;
-            umma_f16_ts(d_o, p_hi + pcol, umma_desc_mn_sw128(vh_a + voff, SLOT / 2), idesc_pv, acc0);
-            umma_f16_ts(d_o, p_hi + pcol, umma_desc_mn_sw128(vl_a + voff, SLOT / 2), idesc_pv, 1u);
-            umma_f16_ts(d_o, p_lo + pcol, umma_desc_mn_sw128(vh_a + voff, SLOT / 2), idesc_pv, 1u);
+            umma_f16_ts(d_o, p_hi, umma_desc_mn_sw128(vh_a + vdb + voff, DBLK), idesc_pv, acc0);
+            umma_f16_ts(d_o, p_hi, umma_desc_mn_sw128(vl_a + vdb + voff, DBLK), idesc_pv, 1u);
+            umma_f16_ts(d_o, p_lo, umma_desc_mn_sw128(vh_a + vdb + voff, DBLK), idesc_pv, 1u);
           }
-          free_slot();
-          free_slot();
         }
+        free_slot();
+        free_slot();
         umma_commit(&pfree[pb]);
         return true;
       };
@@ -343,12 +350,27 @@ __global__ void __launch_bounds__(THREADS, 1)
       tc_fence_after();
       col = TM_S + b * KT + half * 32;
     };
-    auto release_s = [&]() {
+    // ---- Q lo of this thread's row into TMEM (A of the q_lo * k_hi MMAs) ----
+    {
+      uint32_t qw[4][16];  // dims [128 half, +128) as 64 packed fp16 pairs
+      const bool in = r < n_rows;
+      const uint4* src = reinterpret_cast<const uint4*>(ql_g + ((int64_t)(row0 + (in ? r : 0)) * nh + head) * HD +
+                                                        half * 128);
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const uint4 v = in ? src[i] : make_uint4(0u, 0u, 0u, 0u);
+        qw[i >> 2][(i & 3) * 4 + 0] = v.x;
+        qw[i >> 2][(i & 3) * 4 + 1] = v.y;
+        qw[i >> 2][(i & 3) * 4 + 2] = v.z;
+        qw[i >> 2][(i & 3) * 4 + 3] = v.w;
+      }
+#pragma unroll
+      for (int c = 0; c < 4; ++c) tmem_st16(t_lane + TM_QLO + half * 64 + c * 16, qw[c]);
+      tmem_wait_st();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&sempty[sfill & 1]);
-      ++sfill;
-    };
+      if (lane == 0) mbar_arrive(qlofull);
+    }
     // ---- pass 1: row max of the fp16 scores ----
     float m = -INFINITY;
     for (int j = 0; j < nkt; ++j) {
@@ -386,16 +408,14 @@ __global__ void __launch_bounds__(THREADS, 1)
     for (int j = 0; j < nkt; ++j) {
       uint32_t col;
       wait_s(col);
+      ++sfill;
       const uint32_t pb = j & 1;
-      if (ok && j >= 2) ok = mbar_wait(&pfree[pb], ((j >> 1) - 1) & 1, abort_flag, err, 4u);  // PV(j-2) is done
-      ok = __all_sync(0xffffffffu, ok);
       if (ok) {
         uint32_t s[2][16];
         tmem_ld16_w(t_lane + col, s[0]);
         tmem_ld16_w(t_lane + col + 16, s[1]);
         tmem_wait_regs(s[0]);
         reg_barrier16(s[1]);
-        release_s();
         uint32_t ph[16], pl[16];  // 32 keys as packed fp16 pairs
         const int kbase = j * KT + half * 32;
 #pragma unroll
@@ -417,12 +437,18 @@ __global__ void __launch_bounds__(THREADS, 1)
           ph[c >> 1] = *reinterpret_cast<const uint32_t*>(&hi);
           pl[c >> 1] = *reinterpret_cast<const uint32_t*>(&lo);
         }
-        const uint32_t pcol = t_lane + TM_P + pb * 64 + half * 16;
-        tmem_st16(pcol, ph);
-        tmem_st16(pcol + 32, pl);
+        // P over the scores just read: per 16 keys, 8 columns of p_hi then 8 of p_lo
+        uint32_t w0[16], w1[16];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          w0[i] = ph[i];
+          w0[8 + i] = pl[i];
+          w1[i] = ph[8 + i];
+          w1[8 + i] = pl[8 + i];
+        }
+        tmem_st16(t_lane + col, w0);
+        tmem_st16(t_lane + col + 16, w1);
         tmem_wait_st();
-      } else {
-        release_s();
       }
       tc_fence_before();
       __syncwarp();
@@ -494,15 +520,19 @@ PFN_cuTensorMapEncodeTiled_v12000 attn_encoder() {
 }
 
 // fp16 row-major [rows][256] with a box of 64 x box_rows, 128-byte swizzle.
+// k / v planes [rows][256] as a 3-D map (64 dims, row, dim block of 64) with
+// a box of 64 x box_rows x 4: one copy lands the four 128-byte-wide dim
+// blocks of box_rows rows one after another, each in the 128-byte swizzled
+// K-major layout.
 cudaError_t map_rows(CUtensorMap* m, const __half* base, int64_t rows, int box_rows) {
   auto enc = attn_encoder();
   if (!enc) return cudaErrorNotSupported;
   if (reinterpret_cast<uintptr_t>(base) & 15) return cudaErrorMisalignedAddress;
-  cuuint64_t dims[2] = {(cuuint64_t)HD, (cuuint64_t)rows};
-  cuuint64_t strides[1] = {(cuuint64_t)HD * 2};
-  cuuint32_t box[2] = {64, (cuuint32_t)box_rows};
-  cuuint32_t es[2] = {1, 1};
-  return enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<__half*>(base), dims, strides, box, es,
+  cuuint64_t dims[3] = {64, (cuuint64_t)rows, (cuuint64_t)(HD / 64)};
+  cuuint64_t strides[2] = {(cuuint64_t)HD * 2, 128};
+  cuuint32_t box[3] = {64, (cuuint32_t)box_rows, (cuuint32_t)(HD / 64)};
+  cuuint32_t es[3] = {1, 1, 1};
+  return enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<__half*>(base), dims, strides, box, es,
              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS
              ? cudaSuccess
@@ -535,10 +565,10 @@ cudaError_t launch_attention(const __half* qh, const __half* ql, const __half* k
                              uint32_t* absmax, uint32_t* err, cudaStream_t stream) {
   if (tiles.n_tiles == 0) return cudaSuccess;
   const int64_t T = meta.T;
-  CUtensorMap m_qh, m_ql, m_kh, m_kl, m_vh, m_vl;
+  CUtensorMap m_qh, m_kh, m_kl, m_vh, m_vl;
   cudaError_t e;
+  if (reinterpret_cast<uintptr_t>(ql) & 15) return cudaErrorMisalignedAddress;
   if ((e = map_q(&m_qh, qh, T, num_heads)) != cudaSuccess) return e;
-  if ((e = map_q(&m_ql, ql, T, num_heads)) != cudaSuccess) return e;
   if ((e = map_rows(&m_kh, kh, T, KT)) != cudaSuccess) return e;
   if ((e = map_rows(&m_kl, kl, T, KT)) != cudaSuccess) return e;
   if ((e = map_rows(&m_vh, vh, T, KT)) != cudaSuccess) return e;
@@ -555,7 +585,7 @@ cudaError_t launch_attention(const __half* qh, const __half* ql, const __half* k
     }
   }
   dim3 grid(tiles.n_tiles * num_heads);
-  attention_tc_kernel<<<grid, THREADS, SMEM_BYTES, stream>>>(m_qh, m_ql, m_kh, m_kl, m_vh, m_vl, num_heads, scale,
+  attention_tc_kernel<<<grid, THREADS, SMEM_BYTES, stream>>>(m_qh, ql, m_kh, m_kl, m_vh, m_vl, num_heads, scale,
                                                              meta, tiles, out, absmax, err);
   return cudaGetLastError();
 }
