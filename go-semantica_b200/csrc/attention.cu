@@ -217,7 +217,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     } else if (warp == 1 && lane == 0) {
       // ---------------- MMA issuer ----------------
       constexpr uint32_t idesc_qk = umma_idesc_f16_f32(QT, KT);
-      constexpr uint32_t idesc_pv = umma_idesc_f16_f32(QT, 128) | (1u << 16);  // B (V) MN-major
+      constexpr uint32_t idesc_pv = umma_idesc_f16_f32(QT, HD) | (1u << 16);  // N = 256 dims, B (V) MN-major
       uint32_t it = 0, sfill = 0;
       bool ok = mbar_wait(qfull, 0, abort_flag, err, 2u);
       tc_fence_after();
@@ -299,20 +299,17 @@ __global__ void __launch_bounds__(THREADS, 1)
           tc_fence_after();
           vl_a = smem_u32(sRing + s * SLOT);
         }
-#pragma unroll 1
-        for (int h = 0; h < 2; ++h) {
-          const uint32_t d_o = tmem + TM_O + h * 128;
-          const uint32_t vdb = (uint32_t)h * 2 * DBLK;  // dims 128h..: dim blocks 2h, 2h+1
+        // N = 256: all dims at once (the four 64-dim blocks of a slot are DBLK apart)
+        const uint32_t d_o = tmem + TM_O;
 #pragma unroll
-          for (int k16 = 0; k16 < KT / 16; ++k16) {
-            // keys 16k16..: p_hi in 8 packed fp16 columns, then p_lo in the next 8
-            const uint32_t p_hi = p_buf + (uint32_t)k16 * 16, p_lo = p_hi + 8;
-            const uint32_t voff = (uint32_t)k16 * 2048;  // two 8-key groups of V rows
-            const uint32_t acc0 = (j > 0 || k16 > 0) ? 1u : 0u;
-            umma_f16_ts(d_o, p_hi, umma_desc_mn_sw128(vh_a + vdb + voff, DBLK), idesc_pv, acc0);
-            umma_f16_ts(d_o, p_hi, umma_desc_mn_sw128(vl_a + vdb + voff, DBLK), idesc_pv, 1u);
-            umma_f16_ts(d_o, p_lo, umma_desc_mn_sw128(vh_a + vdb + voff, DBLK), idesc_pv, 1u);
-          }
+        for (int k16 = 0; k16 < KT / 16; ++k16) {
+          // keys 16k16..: p_hi in 8 packed fp16 columns, then p_lo in the next 8
+          const uint32_t p_hi = p_buf + (uint32_t)k16 * 16, p_lo = p_hi + 8;
+          const uint32_t voff = (uint32_t)k16 * 2048;  // two 8-key groups of V rows
+          const uint32_t acc0 = (j > 0 || k16 > 0) ? 1u : 0u;
+          umma_f16_ts(d_o, p_hi, umma_desc_mn_sw128(vh_a + voff, DBLK), idesc_pv, acc0);
+          umma_f16_ts(d_o, p_hi, umma_desc_mn_sw128(vl_a + voff, DBLK), idesc_pv, 1u);
+          umma_f16_ts(d_o, p_lo, umma_desc_mn_sw128(vh_a + voff, DBLK), idesc_pv, 1u);
         }
         free_slot();
         free_slot();
