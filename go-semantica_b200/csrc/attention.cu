@@ -54,7 +54,9 @@ constexpr int DBLK = KT * 128;           // 8 KB: one dim block of a slot
 constexpr int QBLK = QT * 128;           // 16 KB: 128 rows x 64 dims
 constexpr int SMEM_Q = 4 * QBLK;         // hi x 4 dim blocks: 64 KB
 constexpr int SMEM_RING = NSLOT * SLOT;  // 160 KB
-constexpr int NS1 = 4;  // score buffers of pass 1 (in the O columns, unused until pass 2)
+constexpr int KT1 = 128;     // keys per pass-1 tile (N = 128 MMAs: fewer, larger tensor-core instructions)
+constexpr int DBLK1 = KT1 * 128;  // 16 KB: one dim block of a pass-1 slot (128 keys x 128 B)
+constexpr int NS1 = 2;  // score buffers of pass 1 (128 columns each, in the O columns, unused until pass 2)
 // q, ring full/empty, S full, P full, S/P buffer free, O, drain, pass-1 S full/empty, Q lo in TMEM
 constexpr int NBAR = 1 + 2 * NSLOT + 2 + 2 + 2 + 1 + 1 + 2 * NS1 + 1;
 constexpr int BAR_BLOCK = 320;                     // barriers, TMEM address, abort flag
@@ -118,7 +120,8 @@ __device__ __forceinline__ uint64_t umma_desc_mn_sw128(uint32_t saddr, uint32_t 
 
 __global__ void __launch_bounds__(THREADS, 1)
     attention_tc_kernel(const __grid_constant__ CUtensorMap tm_qh, const __half* __restrict__ ql_g,
-                        const __grid_constant__ CUtensorMap tm_kh, const __grid_constant__ CUtensorMap tm_kl,
+                        const __grid_constant__ CUtensorMap tm_k1, const __grid_constant__ CUtensorMap tm_kh,
+                        const __grid_constant__ CUtensorMap tm_kl,
                         const __grid_constant__ CUtensorMap tm_vh, const __grid_constant__ CUtensorMap tm_vl, int nh,
                         float scale, SeqMeta meta, AttnTiles tiles, float* __restrict__ out,
                         uint32_t* __restrict__ absmax, uint32_t* __restrict__ err) {
@@ -153,6 +156,7 @@ __global__ void __launch_bounds__(THREADS, 1)
   const int n_rows = min(QT, s_end - row0);
   const int n_keys = s_end - s_beg;
   const int nkt = (n_keys + KT - 1) / KT;
+  const int nkt1 = (n_keys + KT1 - 1) / KT1;
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < NBAR; ++i) mbar_init(&bars[i], 1);
@@ -169,9 +173,10 @@ __global__ void __launch_bounds__(THREADS, 1)
   tc_fence_after();
   const uint32_t tmem = *s_tmem;
 
-  // Ring consumption order: pass 1 = Kh of each key tile (two dim halves);
-  // pass 2 = K(0), then for j = 1..: K(j), V(j-1); finally V(last). A K(j)
-  // item is (hi, lo) of dim half 0 then 1 (4 slots), a V(j) item the same.
+  // Ring consumption order: pass 1 = K hi of each 128-key tile, dims 0-127
+  // then 128-255 (two slots); pass 2 = K(0), then for j = 1..: K(j), V(j-1);
+  // finally V(last), 64-key tiles. A K(j) item is the hi plane then the lo
+  // plane (two slots of all 256 dims), a V(j) item the same.
   if (warp < 4) {
     asm volatile("setmaxnreg.dec.sync.aligned.u32 88;  // 128 x 88 + 256 x 192 <= 384 x 168");
     if ((warp == 0 || warp == 2) && lane == 0) {
@@ -188,7 +193,7 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll
         for (int b = 0; b < 4; ++b) tma_load_3d(&tm_qh, qfull, sQ + b * QBLK, b * 64, head, row0);
       }
-      auto load_slot = [&](const CUtensorMap* map, int key0, int dim0) -> bool {
+      auto load_slot = [&](const CUtensorMap* map, int key0, int dblk0) -> bool {
         if ((it & 1) != me) {
           ++it;
           return true;
@@ -196,11 +201,13 @@ __global__ void __launch_bounds__(THREADS, 1)
         const uint32_t s = it % NSLOT, u = it / NSLOT;
         if (!mbar_wait(&rempty[s], (u & 1) ^ 1, abort_flag, err, 1u)) return false;
         mbar_arrive_expect_tx(&rfull[s], SLOT);
-        tma_load_3d(map, &rfull[s], sRing + s * SLOT, dim0, key0, 0);  // 64 dims x 64 keys x 4 dim blocks
+        tma_load_3d(map, &rfull[s], sRing + s * SLOT, 0, key0, dblk0);  // 64 dims x rows x dim blocks
         ++it;
         return true;
       };
-      for (int j = 0; ok && j < nkt; ++j) ok = load_slot(&tm_kh, s_beg + j * KT, 0);
+      // pass 1: K hi of 128 keys, dims 0-127 then 128-255 (two dim blocks each)
+      for (int j = 0; ok && j < nkt1; ++j)
+        for (int h = 0; ok && h < 2; ++h) ok = load_slot(&tm_k1, s_beg + j * KT1, 2 * h);
       for (int j = 0; ok && j <= nkt; ++j) {
         if (j < nkt) {
           ok = ok && load_slot(&tm_kh, s_beg + j * KT, 0);
@@ -234,6 +241,31 @@ __global__ void __launch_bounds__(THREADS, 1)
       // S[buf] = scores of key tile j: pass 1 (one term) cycles through NS1
       // buffers in the O columns, pass 2 (three terms) through two at TM_S
       uint32_t fill1 = 0;
+      constexpr uint32_t idesc_qk1 = umma_idesc_f16_f32(QT, KT1);
+      // pass 1: S1[buf] = q_hi . k_hi of a 128-key tile (two slots: dims 0-127, 128-255)
+      auto qk1 = [&]() -> bool {
+        const uint32_t b = fill1 % NS1, ub = fill1 / NS1;
+        if (!mbar_wait(&s1empty[b], (ub & 1) ^ 1, abort_flag, err, 2u)) return false;
+        const uint32_t d_s = tmem + TM_O + b * KT1;
+        ++fill1;
+        tc_fence_after();
+#pragma unroll 1
+        for (int h = 0; h < 2; ++h) {
+          uint32_t k_a;
+          if (!take_slot(k_a)) return false;
+#pragma unroll
+          for (int k16 = 0; k16 < 8; ++k16) {
+            const int db = 2 * h + k16 / 4;
+            const uint32_t koff = (uint32_t)(k16 % 4) * 32;
+            const uint32_t kb = (uint32_t)(k16 / 4) * DBLK1 + koff;
+            umma_f16(d_s, umma_desc_k_sw128(q_hi + db * QBLK + koff), umma_desc_k_sw128(k_a + kb), idesc_qk1,
+                     (h | k16) ? 1u : 0u);
+          }
+          free_slot();
+        }
+        umma_commit(&s1full[b]);
+        return true;
+      };
       auto qk = [&](bool three) -> bool {
         uint32_t d_s;
         uint64_t* full_bar;
@@ -316,10 +348,10 @@ __global__ void __launch_bounds__(THREADS, 1)
         umma_commit(&pfree[pb]);
         return true;
       };
-      for (int j = 0; ok && j < nkt; ++j) ok = qk(false);
+      for (int j = 0; ok && j < nkt1; ++j) ok = qk1();
       // the softmax has read every pass-1 buffer before P.V overwrites the O columns
-      for (int k = 0; ok && k < NS1 && k < nkt; ++k) {
-        const int last = k + NS1 * ((nkt - 1 - k) / NS1);
+      for (int k = 0; ok && k < NS1 && k < nkt1; ++k) {
+        const int last = k + NS1 * ((nkt1 - 1 - k) / NS1);
         ok = mbar_wait(&s1empty[k], (last / NS1) & 1, abort_flag, err, 2u);
       }
       for (int j = 0; ok && j <= nkt; ++j) {
@@ -370,24 +402,26 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
     // ---- pass 1: row max of the fp16 scores ----
     float m = -INFINITY;
-    for (int j = 0; j < nkt; ++j) {
+    for (int j = 0; j < nkt1; ++j) {
       const uint32_t b = j % NS1;
       if (ok) ok = mbar_wait(&s1full[b], (j / NS1) & 1, abort_flag, err, 4u);
       ok = __all_sync(0xffffffffu, ok);
       tc_fence_after();
       if (ok) {
-        uint32_t s[2][16];
-        const uint32_t col = TM_O + b * KT + half * 32;
-        tmem_ld16_w(t_lane + col, s[0]);
-        tmem_ld16_w(t_lane + col + 16, s[1]);
+        uint32_t s[4][16];  // this half's 64 keys of the 128-key tile
+        const uint32_t col = TM_O + b * KT1 + half * 64;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) tmem_ld16_w(t_lane + col + 16 * c, s[c]);
         tmem_wait_regs(s[0]);
         reg_barrier16(s[1]);
+        reg_barrier16(s[2]);
+        reg_barrier16(s[3]);
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&s1empty[b]);
 #pragma unroll
-        for (int c = 0; c < 32; ++c) {
-          const int key = j * KT + half * 32 + c;
+        for (int c = 0; c < 64; ++c) {
+          const int key = j * KT1 + half * 64 + c;
           if (key < n_keys) m = fmaxf(m, __fmul_rn(__uint_as_float(s[c >> 4][c & 15]), scale));
         }
       } else {
@@ -518,16 +552,16 @@ PFN_cuTensorMapEncodeTiled_v12000 attn_encoder() {
 
 // fp16 row-major [rows][256] with a box of 64 x box_rows, 128-byte swizzle.
 // k / v planes [rows][256] as a 3-D map (64 dims, row, dim block of 64) with
-// a box of 64 x box_rows x 4: one copy lands the four 128-byte-wide dim
-// blocks of box_rows rows one after another, each in the 128-byte swizzled
-// K-major layout.
-cudaError_t map_rows(CUtensorMap* m, const __half* base, int64_t rows, int box_rows) {
+// a box of 64 x box_rows x box_dblks: one copy lands box_dblks 128-byte-wide
+// dim blocks of box_rows rows one after another, each in the 128-byte
+// swizzled K-major layout.
+cudaError_t map_rows(CUtensorMap* m, const __half* base, int64_t rows, int box_rows, int box_dblks) {
   auto enc = attn_encoder();
   if (!enc) return cudaErrorNotSupported;
   if (reinterpret_cast<uintptr_t>(base) & 15) return cudaErrorMisalignedAddress;
   cuuint64_t dims[3] = {64, (cuuint64_t)rows, (cuuint64_t)(HD / 64)};
   cuuint64_t strides[2] = {(cuuint64_t)HD * 2, 128};
-  cuuint32_t box[3] = {64, (cuuint32_t)box_rows, (cuuint32_t)(HD / 64)};
+  cuuint32_t box[3] = {64, (cuuint32_t)box_rows, (cuuint32_t)box_dblks};
   cuuint32_t es[3] = {1, 1, 1};
   return enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<__half*>(base), dims, strides, box, es,
              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -562,14 +596,15 @@ cudaError_t launch_attention(const __half* qh, const __half* ql, const __half* k
                              uint32_t* absmax, uint32_t* err, cudaStream_t stream) {
   if (tiles.n_tiles == 0) return cudaSuccess;
   const int64_t T = meta.T;
-  CUtensorMap m_qh, m_kh, m_kl, m_vh, m_vl;
+  CUtensorMap m_qh, m_k1, m_kh, m_kl, m_vh, m_vl;
   cudaError_t e;
   if (reinterpret_cast<uintptr_t>(ql) & 15) return cudaErrorMisalignedAddress;
   if ((e = map_q(&m_qh, qh, T, num_heads)) != cudaSuccess) return e;
-  if ((e = map_rows(&m_kh, kh, T, KT)) != cudaSuccess) return e;
-  if ((e = map_rows(&m_kl, kl, T, KT)) != cudaSuccess) return e;
-  if ((e = map_rows(&m_vh, vh, T, KT)) != cudaSuccess) return e;
-  if ((e = map_rows(&m_vl, vl, T, KT)) != cudaSuccess) return e;
+  if ((e = map_rows(&m_k1, kh, T, KT1, 2)) != cudaSuccess) return e;
+  if ((e = map_rows(&m_kh, kh, T, KT, 4)) != cudaSuccess) return e;
+  if ((e = map_rows(&m_kl, kl, T, KT, 4)) != cudaSuccess) return e;
+  if ((e = map_rows(&m_vh, vh, T, KT, 4)) != cudaSuccess) return e;
+  if ((e = map_rows(&m_vl, vl, T, KT, 4)) != cudaSuccess) return e;
   int dev = 0;
   if ((e = cudaGetDevice(&dev)) != cudaSuccess) return e;
   {
@@ -582,7 +617,7 @@ cudaError_t launch_attention(const __half* qh, const __half* ql, const __half* k
     }
   }
   dim3 grid(tiles.n_tiles * num_heads);
-  attention_tc_kernel<<<grid, THREADS, SMEM_BYTES, stream>>>(m_qh, ql, m_kh, m_kl, m_vh, m_vl, num_heads, scale,
+  attention_tc_kernel<<<grid, THREADS, SMEM_BYTES, stream>>>(m_qh, ql, m_k1, m_kh, m_kl, m_vh, m_vl, num_heads, scale,
                                                              meta, tiles, out, absmax, err);
   return cudaGetLastError();
 }

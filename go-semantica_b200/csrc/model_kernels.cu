@@ -510,6 +510,7 @@ cudaError_t launch_qk_norm_rope(const float* qkv, const float* q_norm, const flo
 // 16-byte accesses, and the two sums of squares run from shared memory in the
 // reference's 8-lane order (one 8-lane group per row).
 constexpr int kRnWarps = 4;
+constexpr int kRnRows = 2;  // rows per warp: small shared-memory tiles keep many warps (and loads) in flight
 constexpr int kRowPad = 8;  // row stride H + 8 floats puts the 4 row groups of a warp on distinct banks
 constexpr int kRnBatch = 8;  // 16-byte loads in flight per lane
 
@@ -522,25 +523,25 @@ __global__ void __launch_bounds__(kRnWarps * 32)
   const unsigned full = 0xffffffffu;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, g = lane >> 3, sub = lane & 7;
   const int stride = H + kRowPad, q4 = H / 4;  // float4 per row (a multiple of 32)
-  float* rows = rn_smem + warp * 4 * stride;
-  float* myrow = rows + g * stride;
+  float* rows = rn_smem + warp * kRnRows * stride;
+  float* myrow = rows + (g < kRnRows ? g : kRnRows - 1) * stride;  // 8-lane groups past kRnRows idle
   const int64_t nwarps = (int64_t)gridDim.x * kRnWarps;
-  for (int64_t row0 = ((int64_t)blockIdx.x * kRnWarps + warp) * 4; row0 < meta.T; row0 += nwarps * 4) {
+  for (int64_t row0 = ((int64_t)blockIdx.x * kRnWarps + warp) * kRnRows; row0 < meta.T; row0 += nwarps * kRnRows) {
     const int64_t row = row0 + g;
-    const bool valid = row < meta.T;
+    const bool valid = g < kRnRows && row < meta.T;
     // o rows into shared memory, eight 16-byte loads in flight per lane
-    for (int base = 0; base < 4 * q4; base += 32 * kRnBatch) {
+    for (int base = 0; base < kRnRows * q4; base += 32 * kRnBatch) {
       float4 v[kRnBatch];
 #pragma unroll
       for (int b = 0; b < kRnBatch; ++b) {
         const int idx = base + b * 32 + lane, r = idx / q4, c4 = idx % q4;
         v[b] = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (idx < 4 * q4 && row0 + r < meta.T) v[b] = reinterpret_cast<const float4*>(o + (row0 + r) * H)[c4];
+        if (idx < kRnRows * q4 && row0 + r < meta.T) v[b] = reinterpret_cast<const float4*>(o + (row0 + r) * H)[c4];
       }
 #pragma unroll
       for (int b = 0; b < kRnBatch; ++b) {
         const int idx = base + b * 32 + lane, r = idx / q4, c4 = idx % q4;
-        if (idx < 4 * q4) *reinterpret_cast<float4*>(rows + r * stride + 4 * c4) = v[b];
+        if (idx < kRnRows * q4) *reinterpret_cast<float4*>(rows + r * stride + 4 * c4) = v[b];
       }
     }
     __syncwarp();
@@ -552,18 +553,18 @@ __global__ void __launch_bounds__(kRnWarps * 32)
     }
     const float inv1 = rms_inv_ref(group_sum8_avx_order(acc), H, eps);
     // new hidden, written back to global memory and over o in shared memory
-    for (int base = 0; base < 4 * q4; base += 32 * kRnBatch) {
+    for (int base = 0; base < kRnRows * q4; base += 32 * kRnBatch) {
       float4 hv[kRnBatch];
 #pragma unroll
       for (int b = 0; b < kRnBatch; ++b) {
         const int idx = base + b * 32 + lane, r = idx / q4, c4 = idx % q4;
         hv[b] = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (idx < 4 * q4 && row0 + r < meta.T) hv[b] = reinterpret_cast<const float4*>(hidden + (row0 + r) * H)[c4];
+        if (idx < kRnRows * q4 && row0 + r < meta.T) hv[b] = reinterpret_cast<const float4*>(hidden + (row0 + r) * H)[c4];
       }
 #pragma unroll
       for (int b = 0; b < kRnBatch; ++b) {
         const int idx = base + b * 32 + lane, r = idx / q4, c4 = idx % q4;  // r is warp-uniform (q4 % 32 == 0)
-        if (idx >= 4 * q4) continue;
+        if (idx >= kRnRows * q4) continue;
         const float i1 = __shfl_sync(full, inv1, 8 * r);
         float4 ov = *reinterpret_cast<const float4*>(rows + r * stride + 4 * c4);
         if (post_w) {  // an absent post-norm leaves o as it is (model_int8.go:203, :225)
@@ -586,11 +587,14 @@ __global__ void __launch_bounds__(kRnWarps * 32)
     }
     const float inv2 = rms_inv_ref(group_sum8_avx_order(acc), H, eps);
     float m = 0.0f;
-    if (absmax) {
+    if (absmax) {  // max is exact: four interleaved running maxima give the same result
+      float m4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll 8
       for (int v = 0; v < H / 8; ++v) {
         const int e = 8 * v + sub;
-        m = fmaxf(m, fabsf(__fmul_rn(__fmul_rn(myrow[e], inv2), next_w[e])));
+        m4[v & 3] = fmaxf(m4[v & 3], fabsf(__fmul_rn(__fmul_rn(myrow[e], inv2), next_w[e])));
       }
+      m = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
       m = group_max8(valid ? m : 0.0f);
     }
     if (valid && sub == 0) inv_rms[row] = inv2;
@@ -603,11 +607,11 @@ cudaError_t launch_residual_norm(const float* o, const float* post_w, float* hid
                                  float eps, SeqMeta meta, float* inv_rms, uint32_t* absmax, cudaStream_t stream) {
   if (meta.T == 0) return cudaSuccess;
   if (H % 128 != 0) return cudaErrorInvalidValue;
-  const int smem = kRnWarps * 4 * (H + kRowPad) * 4;
+  const int smem = kRnWarps * kRnRows * (H + kRowPad) * 4;
   cudaError_t e = cudaFuncSetAttribute(residual_norm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return e;
-  int64_t blocks = (meta.T + 4 * kRnWarps - 1) / (4 * kRnWarps);
-  if (blocks > 148 * 8) blocks = 148 * 8;
+  int64_t blocks = (meta.T + kRnRows * kRnWarps - 1) / (kRnRows * kRnWarps);
+  if (blocks > 148 * 16) blocks = 148 * 16;
   residual_norm_kernel<<<(unsigned)blocks, kRnWarps * 32, smem, stream>>>(o, post_w, hidden, next_w, H, eps, meta,
                                                                          inv_rms, absmax);
   return cudaGetLastError();
