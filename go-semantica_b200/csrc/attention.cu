@@ -51,6 +51,7 @@ constexpr int KT = 64;       // keys per tile
 constexpr int NSLOT = 5;     // K/V ring slots
 constexpr int SLOT = KT * HD * 2;        // 32 KB: 64 keys x 256 dims of one plane, as 4 dim blocks of 64 keys x 128 B
 constexpr int DBLK = KT * 128;           // 8 KB: one dim block of a slot
+constexpr int OBOX = QT * 128;           // 16 KB: one 32-float x 128-row output box
 constexpr int QBLK = QT * 128;           // 16 KB: 128 rows x 64 dims
 constexpr int SMEM_Q = 4 * QBLK;         // hi x 4 dim blocks: 64 KB
 constexpr int SMEM_RING = NSLOT * SLOT;  // 160 KB
@@ -67,6 +68,7 @@ constexpr int SM_WARPS = 8;
 // TMEM columns: O [0,256), score / P buffers [256,320) and [320,384), Q lo [384,512)
 constexpr uint32_t TM_O = 0, TM_S = 256, TM_QLO = 384;
 static_assert(SMEM_BYTES <= 232448, "shared memory per CTA");
+static_assert(8 * OBOX <= SMEM_RING, "the output tile is staged in the ring");
 static_assert(NBAR * 8 + 8 <= BAR_BLOCK, "barrier block");
 
 __device__ uint32_t g_attn_error;
@@ -122,7 +124,8 @@ __global__ void __launch_bounds__(THREADS, 1)
     attention_tc_kernel(const __grid_constant__ CUtensorMap tm_qh, const __half* __restrict__ ql_g,
                         const __grid_constant__ CUtensorMap tm_k1, const __grid_constant__ CUtensorMap tm_kh,
                         const __grid_constant__ CUtensorMap tm_kl,
-                        const __grid_constant__ CUtensorMap tm_vh, const __grid_constant__ CUtensorMap tm_vl, int nh,
+                        const __grid_constant__ CUtensorMap tm_vh, const __grid_constant__ CUtensorMap tm_vl,
+                        const __grid_constant__ CUtensorMap tm_out, int nh,
                         float scale, SeqMeta meta, AttnTiles tiles, float* __restrict__ out,
                         uint32_t* __restrict__ absmax, uint32_t* __restrict__ err) {
   extern __shared__ uint8_t smem_raw[];
@@ -499,6 +502,41 @@ __global__ void __launch_bounds__(THREADS, 1)
     const float inv = lt > 0.0f ? __fdiv_rn(1.0f, lt) : 0.0f;
     const bool valid = r < n_rows;
     float amax = 0.0f;
+    if (ok && n_rows == QT) {
+      // A full tile leaves through shared memory (the idle K/V ring) and TMA
+      // stores of 32-float x 128-row boxes in the 128-byte swizzled layout, so
+      // the writes reach memory coalesced. Box (half * 4 + seg) holds dims
+      // [32 (half * 4 + seg), +32); row r's 16-byte chunk k sits at chunk
+      // k ^ (r & 7) of its 128-byte row.
+#pragma unroll 1
+      for (int seg = 0; seg < 4; ++seg) {
+        uint32_t o[2][16];
+        tmem_ld16_w(t_lane + TM_O + half * 128 + seg * 32, o[0]);
+        tmem_ld16_w(t_lane + TM_O + half * 128 + seg * 32 + 16, o[1]);
+        tmem_wait_regs(o[0]);
+        reg_barrier16(o[1]);
+        uint8_t* box = sRing + (half * 4 + seg) * OBOX + r * 128;
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          float v[4];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            v[i] = __fmul_rn(__uint_as_float(o[k >> 2][(k & 3) * 4 + i]), inv);
+            amax = fmaxf(amax, fabsf(v[i]));
+          }
+          *reinterpret_cast<float4*>(box + ((k ^ (r & 7)) << 4)) = make_float4(v[0], v[1], v[2], v[3]);
+        }
+      }
+      fence_proxy_async_smem();
+      named_bar_sync(1, SM_WARPS * 32);
+      if (warp == 4 && lane == 0) {
+        for (int bx = 0; bx < 8; ++bx) tma_store_2d(&tm_out, sRing + bx * OBOX, head * HD + bx * 32, row0);
+        bulk_commit();
+        bulk_wait_all();  // the stores have read shared memory before the CTA exits
+      }
+      amax = warp_max(amax);
+      if (lane == 0 && absmax) atomicMax(&absmax[seq], __float_as_uint(amax));
+    } else {
     float* dst = out + (int64_t)(row0 + (valid ? r : 0)) * (nh * HD) + head * HD + half * 128;
 #pragma unroll
     for (int c = 0; c < 8; ++c) {
@@ -524,6 +562,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
     amax = warp_max(valid ? amax : 0.0f);
     if (lane == 0 && absmax) atomicMax(&absmax[seq], __float_as_uint(amax));
+    }
   }
 
   tc_fence_before();
@@ -596,7 +635,7 @@ cudaError_t launch_attention(const __half* qh, const __half* ql, const __half* k
                              uint32_t* absmax, uint32_t* err, cudaStream_t stream) {
   if (tiles.n_tiles == 0) return cudaSuccess;
   const int64_t T = meta.T;
-  CUtensorMap m_qh, m_k1, m_kh, m_kl, m_vh, m_vl;
+  CUtensorMap m_qh, m_k1, m_kh, m_kl, m_vh, m_vl, m_out;
   cudaError_t e;
   if (reinterpret_cast<uintptr_t>(ql) & 15) return cudaErrorMisalignedAddress;
   if ((e = map_q(&m_qh, qh, T, num_heads)) != cudaSuccess) return e;
@@ -605,6 +644,19 @@ cudaError_t launch_attention(const __half* qh, const __half* ql, const __half* k
   if ((e = map_rows(&m_kl, kl, T, KT, 4)) != cudaSuccess) return e;
   if ((e = map_rows(&m_vh, vh, T, KT, 4)) != cudaSuccess) return e;
   if ((e = map_rows(&m_vl, vl, T, KT, 4)) != cudaSuccess) return e;
+  {  // out [T][nh * 256] fp32: boxes of 32 floats x 128 rows, 128-byte swizzle
+    auto enc = attn_encoder();
+    if (!enc) return cudaErrorNotSupported;
+    if (reinterpret_cast<uintptr_t>(out) & 15) return cudaErrorMisalignedAddress;
+    cuuint64_t dims[2] = {(cuuint64_t)num_heads * HD, (cuuint64_t)T};
+    cuuint64_t strides[1] = {(cuuint64_t)num_heads * HD * 4};
+    cuuint32_t box[2] = {32, (cuuint32_t)QT};
+    cuuint32_t es[2] = {1, 1};
+    if (enc(&m_out, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, out, dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+            CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+      return cudaErrorInvalidValue;
+  }
   int dev = 0;
   if ((e = cudaGetDevice(&dev)) != cudaSuccess) return e;
   {
@@ -617,7 +669,8 @@ cudaError_t launch_attention(const __half* qh, const __half* ql, const __half* k
     }
   }
   dim3 grid(tiles.n_tiles * num_heads);
-  attention_tc_kernel<<<grid, THREADS, SMEM_BYTES, stream>>>(m_qh, ql, m_k1, m_kh, m_kl, m_vh, m_vl, num_heads, scale,
+  attention_tc_kernel<<<grid, THREADS, SMEM_BYTES, stream>>>(m_qh, ql, m_k1, m_kh, m_kl, m_vh, m_vl, m_out, num_heads,
+                                                             scale,
                                                              meta, tiles, out, absmax, err);
   return cudaGetLastError();
 }
