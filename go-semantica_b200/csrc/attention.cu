@@ -16,21 +16,21 @@
 // score; fastExp(x - d) = fastExp(x) * e^-d up to O(1e-3 d), and the common
 // factor cancels in the normalisation.
 //
-// One CTA = 128 query rows of one (sequence, head). Q hi (64 KB) stays in
-// shared memory and Q lo in TMEM; K and V stream through a ring of five 32 KB
-// slots (one fp16 plane of 64 keys x 256 dims each, fetched by one 3-D TMA
-// copy: a thread's tile loads complete at a rate set by the copies in flight,
-// so few large copies feed the SM fastest), deep enough that the next tile's
-// keys load while P.V runs. TMEM holds O (256 fp32
-// columns), two 64-column score buffers and Q lo (128 columns, two fp16 per
-// column, row = lane): the q_lo * k_hi MMAs take A from TMEM. The softmax
-// writes P in place over the scores it has read (per 16 keys: 8 columns of
-// p_hi then 8 of p_lo, packed fp16 pairs), so the P.V MMAs also take A from
-// TMEM, and a score buffer is free again once its P.V MMAs complete. Warps 0
-// and 2 issue TMA (alternate slots), warp 1 the MMAs, warps 4-11 (two per
-// TMEM lane quarter, each half of a tile's keys) load Q lo into TMEM and do the
-// softmax with packed fp32 arithmetic: they read scores from TMEM, write P
-// back into TMEM, and at the end scale O by 1/sum and store it. V is read MN-major straight from its row-major [token][dim]
+// One CTA = 128 query rows of one (sequence, head), keys in tiles of 128.
+// Q (hi and lo, 128 KB) stays in shared memory; K and V stream through a ring
+// of three 32 KB slots, each filled by one 3-D TMA copy: a K slot holds one
+// plane of 128 keys x 128 dims, a V slot one plane of 64 keys x 256 dims.
+// TMEM holds O (256 fp32 columns) and two 128-column score buffers, so the
+// score MMAs are N = 128 (a kind::f16 MMA costs ~100 cycles whatever its N up
+// to 128, so wider tiles do more work per instruction). The softmax writes P
+// in place over the scores it has read (per 16 keys: 8 columns of p_hi then 8
+// of p_lo, packed fp16 pairs); the P.V MMAs take A from TMEM and V MN-major
+// with N = 256 (all dims at once), and a score buffer takes new scores once
+// its P.V MMAs complete. Warps 0 and 2 issue TMA (alternate slots), warp 1 the
+// MMAs, warps 4-11 (two per TMEM lane quarter, each half of a tile's keys) do
+// the softmax with packed fp32 arithmetic and at the end scale O by 1/sum;
+// full query tiles leave through swizzled shared-memory boxes (where Q was)
+// and TMA stores. V is read MN-major straight from its row-major [token][dim]
 // layout, so sequences may start at any token. All three query heads read the
 // single KV head (GQA) through L2.
 #include <cudaTypedefs.h>
@@ -47,28 +47,27 @@ namespace {
 
 constexpr int HD = 256;      // head_dim
 constexpr int QT = 128;      // query rows per CTA (TMEM lanes)
-constexpr int KT = 64;       // keys per tile
-constexpr int NSLOT = 5;     // K/V ring slots
-constexpr int SLOT = KT * HD * 2;        // 32 KB: 64 keys x 256 dims of one plane, as 4 dim blocks of 64 keys x 128 B
-constexpr int DBLK = KT * 128;           // 8 KB: one dim block of a slot
+constexpr int KT = 128;      // keys per tile (score MMAs of N = 128)
+constexpr int NSLOT = 3;     // K/V ring slots
+constexpr int SLOT = 32768;  // 32 KB, one plane: K = 128 keys x 128 dims (2 dim blocks), V = 64 keys x 256 dims (4)
+constexpr int DBLK = 64 * 128;           // 8 KB: one dim block of a V slot (64 keys x 128 B)
+constexpr int DBLK1 = KT * 128;          // 16 KB: one dim block of a K slot (128 keys x 128 B)
 constexpr int OBOX = QT * 128;           // 16 KB: one 32-float x 128-row output box
 constexpr int QBLK = QT * 128;           // 16 KB: 128 rows x 64 dims
-constexpr int SMEM_Q = 4 * QBLK;         // hi x 4 dim blocks: 64 KB
-constexpr int SMEM_RING = NSLOT * SLOT;  // 160 KB
-constexpr int KT1 = 128;     // keys per pass-1 tile (N = 128 MMAs: fewer, larger tensor-core instructions)
-constexpr int DBLK1 = KT1 * 128;  // 16 KB: one dim block of a pass-1 slot (128 keys x 128 B)
+constexpr int SMEM_Q = 2 * 4 * QBLK;     // hi, lo x 4 dim blocks: 128 KB
+constexpr int SMEM_RING = NSLOT * SLOT;  // 96 KB
 constexpr int NS1 = 2;  // score buffers of pass 1 (128 columns each, in the O columns, unused until pass 2)
-// q, ring full/empty, S full, P full, S/P buffer free, O, drain, pass-1 S full/empty, Q lo in TMEM
-constexpr int NBAR = 1 + 2 * NSLOT + 2 + 2 + 2 + 1 + 1 + 2 * NS1 + 1;
+// q, ring full/empty, S full, P full, S/P buffer free, O, drain, pass-1 S full/empty
+constexpr int NBAR = 1 + 2 * NSLOT + 2 + 2 + 2 + 1 + 1 + 2 * NS1;
 constexpr int BAR_BLOCK = 320;                     // barriers, TMEM address, abort flag
 constexpr int SMEM_MISC = BAR_BLOCK + 2 * QT * 4;  // + [2][QT] reductions
 constexpr int SMEM_BYTES = 1024 + SMEM_Q + SMEM_RING + SMEM_MISC;
 constexpr int THREADS = 384;  // warpgroup 0: TMA (warps 0, 2), MMA (1), idle (3); warpgroups 1-2: softmax / epilogue
 constexpr int SM_WARPS = 8;
-// TMEM columns: O [0,256), score / P buffers [256,320) and [320,384), Q lo [384,512)
-constexpr uint32_t TM_O = 0, TM_S = 256, TM_QLO = 384;
+// TMEM columns: O [0,256), score / P buffers [256,384) and [384,512)
+constexpr uint32_t TM_O = 0, TM_S = 256;
 static_assert(SMEM_BYTES <= 232448, "shared memory per CTA");
-static_assert(8 * OBOX <= SMEM_RING, "the output tile is staged in the ring");
+static_assert(8 * OBOX <= SMEM_Q, "the output tile is staged where Q was");
 static_assert(NBAR * 8 + 8 <= BAR_BLOCK, "barrier block");
 
 __device__ uint32_t g_attn_error;
@@ -121,9 +120,8 @@ __device__ __forceinline__ uint64_t umma_desc_mn_sw128(uint32_t saddr, uint32_t 
 }  // namespace
 
 __global__ void __launch_bounds__(THREADS, 1)
-    attention_tc_kernel(const __grid_constant__ CUtensorMap tm_qh, const __half* __restrict__ ql_g,
-                        const __grid_constant__ CUtensorMap tm_k1, const __grid_constant__ CUtensorMap tm_kh,
-                        const __grid_constant__ CUtensorMap tm_kl,
+    attention_tc_kernel(const __grid_constant__ CUtensorMap tm_qh, const __grid_constant__ CUtensorMap tm_ql,
+                        const __grid_constant__ CUtensorMap tm_kh, const __grid_constant__ CUtensorMap tm_kl,
                         const __grid_constant__ CUtensorMap tm_vh, const __grid_constant__ CUtensorMap tm_vl,
                         const __grid_constant__ CUtensorMap tm_out, int nh,
                         float scale, SeqMeta meta, AttnTiles tiles, float* __restrict__ out,
@@ -143,7 +141,6 @@ __global__ void __launch_bounds__(THREADS, 1)
   uint64_t* drain = ofull + 1;
   uint64_t* s1full = drain + 1;
   uint64_t* s1empty = s1full + NS1;
-  uint64_t* qlofull = s1empty + NS1;
   uint32_t* s_tmem = reinterpret_cast<uint32_t*>(bars + NBAR);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(s_tmem + 1);
   float* s_red = reinterpret_cast<float*>(sRing + SMEM_RING + BAR_BLOCK);  // [2 halves][QT]: maxima, later sums
@@ -159,14 +156,12 @@ __global__ void __launch_bounds__(THREADS, 1)
   const int n_rows = min(QT, s_end - row0);
   const int n_keys = s_end - s_beg;
   const int nkt = (n_keys + KT - 1) / KT;
-  const int nkt1 = (n_keys + KT1 - 1) / KT1;
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < NBAR; ++i) mbar_init(&bars[i], 1);
     mbar_init(pfull, SM_WARPS);
     mbar_init(pfull + 1, SM_WARPS);
     for (int k = 0; k < NS1; ++k) mbar_init(&s1empty[k], SM_WARPS);
-    mbar_init(qlofull, SM_WARPS);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -176,25 +171,28 @@ __global__ void __launch_bounds__(THREADS, 1)
   tc_fence_after();
   const uint32_t tmem = *s_tmem;
 
-  // Ring consumption order: pass 1 = K hi of each 128-key tile, dims 0-127
-  // then 128-255 (two slots); pass 2 = K(0), then for j = 1..: K(j), V(j-1);
-  // finally V(last), 64-key tiles. A K(j) item is the hi plane then the lo
-  // plane (two slots of all 256 dims), a V(j) item the same.
+  // Ring consumption order (128-key tiles): pass 1 = K hi of each tile, dims
+  // 0-127 then 128-255 (two slots); pass 2 = K(0), then for j = 1..: K(j),
+  // V(j-1); finally V(last). A K(j) item is (hi, lo) of dims 0-127 then (hi,
+  // lo) of dims 128-255; a V(j) item is (hi, lo) of keys 0-63 then of keys
+  // 64-127, all 256 dims each.
   if (warp < 4) {
     asm volatile("setmaxnreg.dec.sync.aligned.u32 88;  // 128 x 88 + 256 x 192 <= 384 x 168");
     if ((warp == 0 || warp == 2) && lane == 0) {
       // ---------------- TMA producers ----------------
       // Two threads (warps 0 and 2) walk the same slot sequence and issue
       // alternate slots: one thread's loads complete at a limited rate (a few
-      // copies in flight), so a second stream doubles the rate. NSLOT is even:
-      // slot s is only ever loaded by thread s & 1.
+      // copies in flight), so a second stream doubles the rate.
       const uint32_t me = warp >> 1;
       uint32_t it = 0;
       bool ok = true;
       if (me == 0) {
         mbar_arrive_expect_tx(qfull, SMEM_Q);
 #pragma unroll
-        for (int b = 0; b < 4; ++b) tma_load_3d(&tm_qh, qfull, sQ + b * QBLK, b * 64, head, row0);
+        for (int b = 0; b < 4; ++b) {
+          tma_load_3d(&tm_qh, qfull, sQ + b * QBLK, b * 64, head, row0);
+          tma_load_3d(&tm_ql, qfull, sQ + (4 + b) * QBLK, b * 64, head, row0);
+        }
       }
       auto load_slot = [&](const CUtensorMap* map, int key0, int dblk0) -> bool {
         if ((it & 1) != me) {
@@ -208,31 +206,31 @@ __global__ void __launch_bounds__(THREADS, 1)
         ++it;
         return true;
       };
-      // pass 1: K hi of 128 keys, dims 0-127 then 128-255 (two dim blocks each)
-      for (int j = 0; ok && j < nkt1; ++j)
-        for (int h = 0; ok && h < 2; ++h) ok = load_slot(&tm_k1, s_beg + j * KT1, 2 * h);
+      for (int j = 0; ok && j < nkt; ++j)
+        for (int h = 0; ok && h < 2; ++h) ok = load_slot(&tm_kh, s_beg + j * KT, 2 * h);
       for (int j = 0; ok && j <= nkt; ++j) {
-        if (j < nkt) {
-          ok = ok && load_slot(&tm_kh, s_beg + j * KT, 0);
-          ok = ok && load_slot(&tm_kl, s_beg + j * KT, 0);
-        }
-        if (j >= 1) {
-          ok = ok && load_slot(&tm_vh, s_beg + (j - 1) * KT, 0);
-          ok = ok && load_slot(&tm_vl, s_beg + (j - 1) * KT, 0);
-        }
+        if (j < nkt)
+          for (int h = 0; ok && h < 2; ++h) {
+            ok = ok && load_slot(&tm_kh, s_beg + j * KT, 2 * h);
+            ok = ok && load_slot(&tm_kl, s_beg + j * KT, 2 * h);
+          }
+        if (j >= 1)
+          for (int kq = 0; ok && kq < 2; ++kq) {
+            ok = ok && load_slot(&tm_vh, s_beg + (j - 1) * KT + kq * 64, 0);
+            ok = ok && load_slot(&tm_vl, s_beg + (j - 1) * KT + kq * 64, 0);
+          }
       }
       for (uint32_t j = it > (uint32_t)NSLOT ? it - NSLOT : 0; j < it; ++j)
         if ((j & 1) == me) mbar_wait_drain(&rfull[j % NSLOT], (j / NSLOT) & 1);
       if (me == 0) mbar_wait_drain(qfull, 0);
     } else if (warp == 1 && lane == 0) {
       // ---------------- MMA issuer ----------------
-      constexpr uint32_t idesc_qk = umma_idesc_f16_f32(QT, KT);
+      constexpr uint32_t idesc_qk = umma_idesc_f16_f32(QT, KT);  // N = 128 keys
       constexpr uint32_t idesc_pv = umma_idesc_f16_f32(QT, HD) | (1u << 16);  // N = 256 dims, B (V) MN-major
       uint32_t it = 0, sfill = 0;
       bool ok = mbar_wait(qfull, 0, abort_flag, err, 2u);
       tc_fence_after();
-      const uint32_t q_hi = smem_u32(sQ), q_lo_t = tmem + TM_QLO;
-      bool qlo_ready = false;
+      const uint32_t q_hi = smem_u32(sQ), q_lo = smem_u32(sQ + 4 * QBLK);
       auto take_slot = [&](uint32_t& addr) -> bool {
         const uint32_t s = it % NSLOT, u = it / NSLOT;
         if (!mbar_wait(&rfull[s], u & 1, abort_flag, err, 2u)) return false;
@@ -240,20 +238,25 @@ __global__ void __launch_bounds__(THREADS, 1)
         addr = smem_u32(sRing + s * SLOT);
         return true;
       };
+      // the slot after the current one (the lo plane of a pair)
+      auto peek_slot = [&](uint32_t& addr) -> bool {
+        const uint32_t s = (it + 1) % NSLOT, u = (it + 1) / NSLOT;
+        if (!mbar_wait(&rfull[s], u & 1, abort_flag, err, 2u)) return false;
+        tc_fence_after();
+        addr = smem_u32(sRing + s * SLOT);
+        return true;
+      };
       auto free_slot = [&]() { umma_commit(&rempty[it % NSLOT]); ++it; };
-      // S[buf] = scores of key tile j: pass 1 (one term) cycles through NS1
-      // buffers in the O columns, pass 2 (three terms) through two at TM_S
+      // pass 1: S1[buf] (NS1 buffers in the O columns) = q_hi . k_hi of a tile
       uint32_t fill1 = 0;
-      constexpr uint32_t idesc_qk1 = umma_idesc_f16_f32(QT, KT1);
-      // pass 1: S1[buf] = q_hi . k_hi of a 128-key tile (two slots: dims 0-127, 128-255)
       auto qk1 = [&]() -> bool {
         const uint32_t b = fill1 % NS1, ub = fill1 / NS1;
         if (!mbar_wait(&s1empty[b], (ub & 1) ^ 1, abort_flag, err, 2u)) return false;
-        const uint32_t d_s = tmem + TM_O + b * KT1;
+        const uint32_t d_s = tmem + TM_O + b * KT;
         ++fill1;
         tc_fence_after();
 #pragma unroll 1
-        for (int h = 0; h < 2; ++h) {
+        for (int h = 0; h < 2; ++h) {  // dims 0-127, then 128-255: one slot each
           uint32_t k_a;
           if (!take_slot(k_a)) return false;
 #pragma unroll
@@ -261,7 +264,7 @@ __global__ void __launch_bounds__(THREADS, 1)
             const int db = 2 * h + k16 / 4;
             const uint32_t koff = (uint32_t)(k16 % 4) * 32;
             const uint32_t kb = (uint32_t)(k16 / 4) * DBLK1 + koff;
-            umma_f16(d_s, umma_desc_k_sw128(q_hi + db * QBLK + koff), umma_desc_k_sw128(k_a + kb), idesc_qk1,
+            umma_f16(d_s, umma_desc_k_sw128(q_hi + db * QBLK + koff), umma_desc_k_sw128(k_a + kb), idesc_qk,
                      (h | k16) ? 1u : 0u);
           }
           free_slot();
@@ -269,55 +272,32 @@ __global__ void __launch_bounds__(THREADS, 1)
         umma_commit(&s1full[b]);
         return true;
       };
-      auto qk = [&](bool three) -> bool {
-        uint32_t d_s;
-        uint64_t* full_bar;
-        if (three) {
-          const uint32_t b = sfill & 1, ub = sfill >> 1;
-          // the buffer's previous P.V MMAs have read its P (first use: no wait)
-          if (!mbar_wait(&pfree[b], (ub & 1) ^ 1, abort_flag, err, 2u)) return false;
-          if (!qlo_ready) {
-            if (!mbar_wait(qlofull, 0, abort_flag, err, 2u)) return false;
-            qlo_ready = true;
-          }
-          d_s = tmem + TM_S + b * KT;
-          full_bar = &sfull[b];
-          ++sfill;
-        } else {
-          const uint32_t b = fill1 % NS1, ub = fill1 / NS1;
-          if (!mbar_wait(&s1empty[b], (ub & 1) ^ 1, abort_flag, err, 2u)) return false;
-          d_s = tmem + TM_O + b * KT;
-          full_bar = &s1full[b];
-          ++fill1;
-        }
+      // pass 2: S[buf] (two buffers at TM_S) = three-term scores of a tile
+      auto qk = [&]() -> bool {
+        const uint32_t b = sfill & 1, ub = sfill >> 1;
+        // the buffer's previous P.V MMAs have read its P (first use: no wait)
+        if (!mbar_wait(&pfree[b], (ub & 1) ^ 1, abort_flag, err, 2u)) return false;
+        const uint32_t d_s = tmem + TM_S + b * KT;
+        ++sfill;
         tc_fence_after();
-        uint32_t kh_a, kl_a = 0;
-        if (!take_slot(kh_a)) return false;
-        if (three) {  // the lo plane is the next ring slot
-          const uint32_t s = (it + 1) % NSLOT, u = (it + 1) / NSLOT;
-          if (!mbar_wait(&rfull[s], u & 1, abort_flag, err, 2u)) return false;
-          tc_fence_after();
-          kl_a = smem_u32(sRing + s * SLOT);
-        }
 #pragma unroll 1
-        for (int h = 0; h < 2; ++h) {
+        for (int h = 0; h < 2; ++h) {  // dims 0-127, then 128-255: (hi, lo) slot pairs
+          uint32_t kh_a, kl_a;
+          if (!take_slot(kh_a) || !peek_slot(kl_a)) return false;
 #pragma unroll
           for (int k16 = 0; k16 < 8; ++k16) {
-            const int db = 2 * h + k16 / 4;               // dim block (of Q and of the K slot)
+            const int db = 2 * h + k16 / 4;               // Q dim block
             const uint32_t koff = (uint32_t)(k16 % 4) * 32;  // K=16 slice within the 128-byte row
-            const uint32_t kb = (uint32_t)db * DBLK + koff;
-            const uint32_t acc = (h | k16) ? 1u : 0u;
-            umma_f16(d_s, umma_desc_k_sw128(q_hi + db * QBLK + koff), umma_desc_k_sw128(kh_a + kb), idesc_qk, acc);
-            if (three) {
-              umma_f16(d_s, umma_desc_k_sw128(q_hi + db * QBLK + koff), umma_desc_k_sw128(kl_a + kb), idesc_qk, 1u);
-              // q_lo from TMEM: dims 128h + 16k16.. are 8 packed columns
-              umma_f16_ts(d_s, q_lo_t + (uint32_t)(64 * h + 8 * k16), umma_desc_k_sw128(kh_a + kb), idesc_qk, 1u);
-            }
+            const uint32_t qb = (uint32_t)db * QBLK + koff;
+            const uint32_t kb = (uint32_t)(k16 / 4) * DBLK1 + koff;
+            umma_f16(d_s, umma_desc_k_sw128(q_hi + qb), umma_desc_k_sw128(kh_a + kb), idesc_qk, (h | k16) ? 1u : 0u);
+            umma_f16(d_s, umma_desc_k_sw128(q_hi + qb), umma_desc_k_sw128(kl_a + kb), idesc_qk, 1u);
+            umma_f16(d_s, umma_desc_k_sw128(q_lo + qb), umma_desc_k_sw128(kh_a + kb), idesc_qk, 1u);
           }
+          free_slot();
+          free_slot();
         }
-        free_slot();
-        if (three) free_slot();
-        umma_commit(full_bar);
+        umma_commit(&sfull[b]);
         return true;
       };
       // O += P(j) V(j), three terms
@@ -326,39 +306,36 @@ __global__ void __launch_bounds__(THREADS, 1)
         if (!mbar_wait(&pfull[pb], (j >> 1) & 1, abort_flag, err, 2u)) return false;
         tc_fence_after();
         const uint32_t p_buf = tmem + TM_S + pb * KT;  // P written over the scores
-        uint32_t vh_a, vl_a;
-        if (!take_slot(vh_a)) return false;
-        {
-          const uint32_t s = (it + 1) % NSLOT, u = (it + 1) / NSLOT;
-          if (!mbar_wait(&rfull[s], u & 1, abort_flag, err, 2u)) return false;
-          tc_fence_after();
-          vl_a = smem_u32(sRing + s * SLOT);
-        }
-        // N = 256: all dims at once (the four 64-dim blocks of a slot are DBLK apart)
         const uint32_t d_o = tmem + TM_O;
+#pragma unroll 1
+        for (int kq = 0; kq < 2; ++kq) {  // keys 0-63, then 64-127: (hi, lo) slot pairs of all 256 dims
+          uint32_t vh_a, vl_a;
+          if (!take_slot(vh_a) || !peek_slot(vl_a)) return false;
 #pragma unroll
-        for (int k16 = 0; k16 < KT / 16; ++k16) {
-          // keys 16k16..: p_hi in 8 packed fp16 columns, then p_lo in the next 8
-          const uint32_t p_hi = p_buf + (uint32_t)k16 * 16, p_lo = p_hi + 8;
-          const uint32_t voff = (uint32_t)k16 * 2048;  // two 8-key groups of V rows
-          const uint32_t acc0 = (j > 0 || k16 > 0) ? 1u : 0u;
-          umma_f16_ts(d_o, p_hi, umma_desc_mn_sw128(vh_a + voff, DBLK), idesc_pv, acc0);
-          umma_f16_ts(d_o, p_hi, umma_desc_mn_sw128(vl_a + voff, DBLK), idesc_pv, 1u);
-          umma_f16_ts(d_o, p_lo, umma_desc_mn_sw128(vh_a + voff, DBLK), idesc_pv, 1u);
+          for (int k16 = 0; k16 < 4; ++k16) {
+            // keys 64kq + 16k16..: p_hi in 8 packed fp16 columns, then p_lo in the next 8
+            const uint32_t p_hi = p_buf + (uint32_t)(kq * 4 + k16) * 16, p_lo = p_hi + 8;
+            const uint32_t voff = (uint32_t)k16 * 2048;  // two 8-key groups of V rows
+            const uint32_t acc0 = (j > 0 || kq > 0 || k16 > 0) ? 1u : 0u;
+            // N = 256: all dims at once (the four 64-dim blocks of a slot are DBLK apart)
+            umma_f16_ts(d_o, p_hi, umma_desc_mn_sw128(vh_a + voff, DBLK), idesc_pv, acc0);
+            umma_f16_ts(d_o, p_hi, umma_desc_mn_sw128(vl_a + voff, DBLK), idesc_pv, 1u);
+            umma_f16_ts(d_o, p_lo, umma_desc_mn_sw128(vh_a + voff, DBLK), idesc_pv, 1u);
+          }
+          free_slot();
+          free_slot();
         }
-        free_slot();
-        free_slot();
         umma_commit(&pfree[pb]);
         return true;
       };
-      for (int j = 0; ok && j < nkt1; ++j) ok = qk1();
+      for (int j = 0; ok && j < nkt; ++j) ok = qk1();
       // the softmax has read every pass-1 buffer before P.V overwrites the O columns
-      for (int k = 0; ok && k < NS1 && k < nkt1; ++k) {
-        const int last = k + NS1 * ((nkt1 - 1 - k) / NS1);
+      for (int k = 0; ok && k < NS1 && k < nkt; ++k) {
+        const int last = k + NS1 * ((nkt - 1 - k) / NS1);
         ok = mbar_wait(&s1empty[k], (last / NS1) & 1, abort_flag, err, 2u);
       }
       for (int j = 0; ok && j <= nkt; ++j) {
-        if (j < nkt) ok = qk(true);
+        if (j < nkt) ok = qk();
         if (ok && j >= 1) ok = pv(j - 1);
       }
       umma_commit(ofull);
@@ -370,7 +347,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     // ---------------- softmax and epilogue ----------------
     const int w = warp - 4;
     const int q = warp & 3;       // TMEM lane quarter
-    const int half = w >> 2;      // keys [32*half, 32*half + 32) of each tile; O columns [128*half, +128)
+    const int half = w >> 2;      // keys [64*half, 64*half + 64) of each tile; O columns [128*half, +128)
     const int r = q * 32 + lane;  // query row within the tile
     const uint32_t t_lane = tmem + ((uint32_t)(q * 32) << 16);
     uint32_t sfill = 0;
@@ -380,39 +357,18 @@ __global__ void __launch_bounds__(THREADS, 1)
       if (ok) ok = mbar_wait(&sfull[b], ub & 1, abort_flag, err, 4u);
       ok = __all_sync(0xffffffffu, ok);
       tc_fence_after();
-      col = TM_S + b * KT + half * 32;
+      col = TM_S + b * KT + half * 64;
     };
-    // ---- Q lo of this thread's row into TMEM (A of the q_lo * k_hi MMAs) ----
-    {
-      uint32_t qw[4][16];  // dims [128 half, +128) as 64 packed fp16 pairs
-      const bool in = r < n_rows;
-      const uint4* src = reinterpret_cast<const uint4*>(ql_g + ((int64_t)(row0 + (in ? r : 0)) * nh + head) * HD +
-                                                        half * 128);
-#pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        const uint4 v = in ? src[i] : make_uint4(0u, 0u, 0u, 0u);
-        qw[i >> 2][(i & 3) * 4 + 0] = v.x;
-        qw[i >> 2][(i & 3) * 4 + 1] = v.y;
-        qw[i >> 2][(i & 3) * 4 + 2] = v.z;
-        qw[i >> 2][(i & 3) * 4 + 3] = v.w;
-      }
-#pragma unroll
-      for (int c = 0; c < 4; ++c) tmem_st16(t_lane + TM_QLO + half * 64 + c * 16, qw[c]);
-      tmem_wait_st();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(qlofull);
-    }
     // ---- pass 1: row max of the fp16 scores ----
     float m = -INFINITY;
-    for (int j = 0; j < nkt1; ++j) {
+    for (int j = 0; j < nkt; ++j) {
       const uint32_t b = j % NS1;
       if (ok) ok = mbar_wait(&s1full[b], (j / NS1) & 1, abort_flag, err, 4u);
       ok = __all_sync(0xffffffffu, ok);
       tc_fence_after();
       if (ok) {
         uint32_t s[4][16];  // this half's 64 keys of the 128-key tile
-        const uint32_t col = TM_O + b * KT1 + half * 64;
+        const uint32_t col = TM_O + b * KT + half * 64;
 #pragma unroll
         for (int c = 0; c < 4; ++c) tmem_ld16_w(t_lane + col + 16 * c, s[c]);
         tmem_wait_regs(s[0]);
@@ -424,7 +380,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         if (lane == 0) mbar_arrive(&s1empty[b]);
 #pragma unroll
         for (int c = 0; c < 64; ++c) {
-          const int key = j * KT1 + half * 64 + c;
+          const int key = j * KT + half * 64 + c;
           if (key < n_keys) m = fmaxf(m, __fmul_rn(__uint_as_float(s[c >> 4][c & 15]), scale));
         }
       } else {
@@ -444,14 +400,15 @@ __global__ void __launch_bounds__(THREADS, 1)
       wait_s(col);
       ++sfill;
       const uint32_t pb = j & 1;
-      if (ok) {
+#pragma unroll 1
+      for (int sub = 0; ok && sub < 2; ++sub, col += 32) {  // this half's 64 keys, 32 at a time
         uint32_t s[2][16];
         tmem_ld16_w(t_lane + col, s[0]);
         tmem_ld16_w(t_lane + col + 16, s[1]);
         tmem_wait_regs(s[0]);
         reg_barrier16(s[1]);
         uint32_t ph[16], pl[16];  // 32 keys as packed fp16 pairs
-        const int kbase = j * KT + half * 32;
+        const int kbase = j * KT + half * 64 + sub * 32;
 #pragma unroll
         for (int c = 0; c < 32; c += 2) {
           // score *= scale (attention.go:300), then fastExp(score - max)
@@ -503,7 +460,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     const bool valid = r < n_rows;
     float amax = 0.0f;
     if (ok && n_rows == QT) {
-      // A full tile leaves through shared memory (the idle K/V ring) and TMA
+      // A full tile leaves through shared memory (where Q was) and TMA
       // stores of 32-float x 128-row boxes in the 128-byte swizzled layout, so
       // the writes reach memory coalesced. Box (half * 4 + seg) holds dims
       // [32 (half * 4 + seg), +32); row r's 16-byte chunk k sits at chunk
@@ -515,7 +472,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         tmem_ld16_w(t_lane + TM_O + half * 128 + seg * 32 + 16, o[1]);
         tmem_wait_regs(o[0]);
         reg_barrier16(o[1]);
-        uint8_t* box = sRing + (half * 4 + seg) * OBOX + r * 128;
+        uint8_t* box = sQ + (half * 4 + seg) * OBOX + r * 128;
 #pragma unroll
         for (int k = 0; k < 8; ++k) {
           float v[4];
@@ -530,7 +487,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       fence_proxy_async_smem();
       named_bar_sync(1, SM_WARPS * 32);
       if (warp == 4 && lane == 0) {
-        for (int bx = 0; bx < 8; ++bx) tma_store_2d(&tm_out, sRing + bx * OBOX, head * HD + bx * 32, row0);
+        for (int bx = 0; bx < 8; ++bx) tma_store_2d(&tm_out, sQ + bx * OBOX, head * HD + bx * 32, row0);
         bulk_commit();
         bulk_wait_all();  // the stores have read shared memory before the CTA exits
       }
@@ -635,15 +592,15 @@ cudaError_t launch_attention(const __half* qh, const __half* ql, const __half* k
                              uint32_t* absmax, uint32_t* err, cudaStream_t stream) {
   if (tiles.n_tiles == 0) return cudaSuccess;
   const int64_t T = meta.T;
-  CUtensorMap m_qh, m_k1, m_kh, m_kl, m_vh, m_vl, m_out;
+  CUtensorMap m_qh, m_ql, m_kh, m_kl, m_vh, m_vl, m_out;
   cudaError_t e;
-  if (reinterpret_cast<uintptr_t>(ql) & 15) return cudaErrorMisalignedAddress;
   if ((e = map_q(&m_qh, qh, T, num_heads)) != cudaSuccess) return e;
-  if ((e = map_rows(&m_k1, kh, T, KT1, 2)) != cudaSuccess) return e;
-  if ((e = map_rows(&m_kh, kh, T, KT, 4)) != cudaSuccess) return e;
-  if ((e = map_rows(&m_kl, kl, T, KT, 4)) != cudaSuccess) return e;
-  if ((e = map_rows(&m_vh, vh, T, KT, 4)) != cudaSuccess) return e;
-  if ((e = map_rows(&m_vl, vl, T, KT, 4)) != cudaSuccess) return e;
+  if ((e = map_q(&m_ql, ql, T, num_heads)) != cudaSuccess) return e;
+  // K: 128 keys x 2 dim blocks per copy (one dim half); V: 64 keys x all 4 dim blocks
+  if ((e = map_rows(&m_kh, kh, T, KT, 2)) != cudaSuccess) return e;
+  if ((e = map_rows(&m_kl, kl, T, KT, 2)) != cudaSuccess) return e;
+  if ((e = map_rows(&m_vh, vh, T, 64, 4)) != cudaSuccess) return e;
+  if ((e = map_rows(&m_vl, vl, T, 64, 4)) != cudaSuccess) return e;
   {  // out [T][nh * 256] fp32: boxes of 32 floats x 128 rows, 128-byte swizzle
     auto enc = attn_encoder();
     if (!enc) return cudaErrorNotSupported;
@@ -669,9 +626,8 @@ cudaError_t launch_attention(const __half* qh, const __half* ql, const __half* k
     }
   }
   dim3 grid(tiles.n_tiles * num_heads);
-  attention_tc_kernel<<<grid, THREADS, SMEM_BYTES, stream>>>(m_qh, ql, m_k1, m_kh, m_kl, m_vh, m_vl, m_out, num_heads,
-                                                             scale,
-                                                             meta, tiles, out, absmax, err);
+  attention_tc_kernel<<<grid, THREADS, SMEM_BYTES, stream>>>(m_qh, m_ql, m_kh, m_kl, m_vh, m_vl, m_out, num_heads,
+                                                             scale, meta, tiles, out, absmax, err);
   return cudaGetLastError();
 }
 
