@@ -18,8 +18,9 @@
 //
 // One CTA = 128 query rows of one (sequence, head), keys in tiles of 128.
 // Q (hi and lo, 128 KB) stays in shared memory; K and V stream through a ring
-// of three 32 KB slots, each filled by one 3-D TMA copy: a K slot holds one
-// plane of 128 keys x 128 dims, a V slot one plane of 64 keys x 256 dims.
+// of three 32 KB slots, each filled by one 4-D TMA copy that lands both planes
+// (hi, lo) of a piece: 128 keys x 64 dims of K, or 32 keys x 256 dims of V, so
+// the MMAs consume one slot while the next two load.
 // TMEM holds O (256 fp32 columns) and two 128-column score buffers, so the
 // score MMAs are N = 128 (a kind::f16 MMA costs ~100 cycles whatever its N up
 // to 128, so wider tiles do more work per instruction). The softmax writes P
@@ -49,9 +50,11 @@ constexpr int HD = 256;      // head_dim
 constexpr int QT = 128;      // query rows per CTA (TMEM lanes)
 constexpr int KT = 128;      // keys per tile (score MMAs of N = 128)
 constexpr int NSLOT = 3;     // K/V ring slots
-constexpr int SLOT = 32768;  // 32 KB, one plane: K = 128 keys x 128 dims (2 dim blocks), V = 64 keys x 256 dims (4)
-constexpr int DBLK = 64 * 128;           // 8 KB: one dim block of a V slot (64 keys x 128 B)
-constexpr int DBLK1 = KT * 128;          // 16 KB: one dim block of a K slot (128 keys x 128 B)
+constexpr int SLOT = 32768;  // 32 KB slots (see the ring order below)
+constexpr int PLANE = SLOT / 2;          // 16 KB: the hi or lo half of a pass-2 slot
+constexpr int VKEYS = 32;                // keys per pass-2 V slot
+constexpr int VDBLK = VKEYS * 128;       // 4 KB: one dim block of a V slot plane (32 keys x 128 B)
+constexpr int DBLK1 = KT * 128;          // 16 KB: one dim block of a pass-1 K slot (128 keys x 128 B)
 constexpr int OBOX = QT * 128;           // 16 KB: one 32-float x 128-row output box
 constexpr int QBLK = QT * 128;           // 16 KB: 128 rows x 64 dims
 constexpr int SMEM_Q = 2 * 4 * QBLK;     // hi, lo x 4 dim blocks: 128 KB
@@ -121,9 +124,8 @@ __device__ __forceinline__ uint64_t umma_desc_mn_sw128(uint32_t saddr, uint32_t 
 
 __global__ void __launch_bounds__(THREADS, 1)
     attention_tc_kernel(const __grid_constant__ CUtensorMap tm_qh, const __grid_constant__ CUtensorMap tm_ql,
-                        const __grid_constant__ CUtensorMap tm_kh, const __grid_constant__ CUtensorMap tm_kl,
-                        const __grid_constant__ CUtensorMap tm_vh, const __grid_constant__ CUtensorMap tm_vl,
-                        const __grid_constant__ CUtensorMap tm_out, int nh,
+                        const __grid_constant__ CUtensorMap tm_k1, const __grid_constant__ CUtensorMap tm_k2,
+                        const __grid_constant__ CUtensorMap tm_v2, const __grid_constant__ CUtensorMap tm_out, int nh,
                         float scale, SeqMeta meta, AttnTiles tiles, float* __restrict__ out,
                         uint32_t* __restrict__ absmax, uint32_t* __restrict__ err) {
   extern __shared__ uint8_t smem_raw[];
@@ -172,10 +174,12 @@ __global__ void __launch_bounds__(THREADS, 1)
   const uint32_t tmem = *s_tmem;
 
   // Ring consumption order (128-key tiles): pass 1 = K hi of each tile, dims
-  // 0-127 then 128-255 (two slots); pass 2 = K(0), then for j = 1..: K(j),
-  // V(j-1); finally V(last). A K(j) item is (hi, lo) of dims 0-127 then (hi,
-  // lo) of dims 128-255; a V(j) item is (hi, lo) of keys 0-63 then of keys
-  // 64-127, all 256 dims each.
+  // 0-127 then 128-255 (two slots of [2 dim blocks][128 keys][128 B]); pass 2
+  // = K(0), then for j = 1..: K(j), V(j-1); finally V(last). A K(j) item is
+  // four slots, one per 64-dim block, each [hi, lo][128 keys][128 B]; a V(j)
+  // item is four slots, one per 32 keys, each [hi, lo][4 dim blocks][32 keys]
+  // [128 B]. Every pass-2 slot holds both planes its MMAs need, so the MMAs
+  // work on one slot while the other two load.
   if (warp < 4) {
     asm volatile("setmaxnreg.dec.sync.aligned.u32 88;  // 128 x 88 + 256 x 192 <= 384 x 168");
     if ((warp == 0 || warp == 2) && lane == 0) {
@@ -194,7 +198,9 @@ __global__ void __launch_bounds__(THREADS, 1)
           tma_load_3d(&tm_ql, qfull, sQ + (4 + b) * QBLK, b * 64, head, row0);
         }
       }
-      auto load_slot = [&](const CUtensorMap* map, int key0, int dblk0) -> bool {
+      // one slot: a 3-D box (pass 1) or a 4-D box whose outermost dimension is
+      // the plane (pass 2)
+      auto load_slot = [&](const CUtensorMap* map, bool four, int key0, int dblk0) -> bool {
         if ((it & 1) != me) {
           ++it;
           return true;
@@ -202,23 +208,20 @@ __global__ void __launch_bounds__(THREADS, 1)
         const uint32_t s = it % NSLOT, u = it / NSLOT;
         if (!mbar_wait(&rempty[s], (u & 1) ^ 1, abort_flag, err, 1u)) return false;
         mbar_arrive_expect_tx(&rfull[s], SLOT);
-        tma_load_3d(map, &rfull[s], sRing + s * SLOT, 0, key0, dblk0);  // 64 dims x rows x dim blocks
+        if (four)
+          tma_load_4d(map, &rfull[s], sRing + s * SLOT, 0, key0, dblk0, 0);  // 64 dims x rows x dim blocks x planes
+        else
+          tma_load_3d(map, &rfull[s], sRing + s * SLOT, 0, key0, dblk0);  // 64 dims x rows x dim blocks
         ++it;
         return true;
       };
       for (int j = 0; ok && j < nkt; ++j)
-        for (int h = 0; ok && h < 2; ++h) ok = load_slot(&tm_kh, s_beg + j * KT, 2 * h);
+        for (int h = 0; ok && h < 2; ++h) ok = load_slot(&tm_k1, false, s_beg + j * KT, 2 * h);
       for (int j = 0; ok && j <= nkt; ++j) {
         if (j < nkt)
-          for (int h = 0; ok && h < 2; ++h) {
-            ok = ok && load_slot(&tm_kh, s_beg + j * KT, 2 * h);
-            ok = ok && load_slot(&tm_kl, s_beg + j * KT, 2 * h);
-          }
+          for (int db = 0; ok && db < 4; ++db) ok = load_slot(&tm_k2, true, s_beg + j * KT, db);
         if (j >= 1)
-          for (int kq = 0; ok && kq < 2; ++kq) {
-            ok = ok && load_slot(&tm_vh, s_beg + (j - 1) * KT + kq * 64, 0);
-            ok = ok && load_slot(&tm_vl, s_beg + (j - 1) * KT + kq * 64, 0);
-          }
+          for (int kq = 0; ok && kq < KT / VKEYS; ++kq) ok = load_slot(&tm_v2, true, s_beg + (j - 1) * KT + kq * VKEYS, 0);
       }
       for (uint32_t j = it > (uint32_t)NSLOT ? it - NSLOT : 0; j < it; ++j)
         if ((j & 1) == me) mbar_wait_drain(&rfull[j % NSLOT], (j / NSLOT) & 1);
@@ -233,14 +236,6 @@ __global__ void __launch_bounds__(THREADS, 1)
       const uint32_t q_hi = smem_u32(sQ), q_lo = smem_u32(sQ + 4 * QBLK);
       auto take_slot = [&](uint32_t& addr) -> bool {
         const uint32_t s = it % NSLOT, u = it / NSLOT;
-        if (!mbar_wait(&rfull[s], u & 1, abort_flag, err, 2u)) return false;
-        tc_fence_after();
-        addr = smem_u32(sRing + s * SLOT);
-        return true;
-      };
-      // the slot after the current one (the lo plane of a pair)
-      auto peek_slot = [&](uint32_t& addr) -> bool {
-        const uint32_t s = (it + 1) % NSLOT, u = (it + 1) / NSLOT;
         if (!mbar_wait(&rfull[s], u & 1, abort_flag, err, 2u)) return false;
         tc_fence_after();
         addr = smem_u32(sRing + s * SLOT);
@@ -281,20 +276,18 @@ __global__ void __launch_bounds__(THREADS, 1)
         ++sfill;
         tc_fence_after();
 #pragma unroll 1
-        for (int h = 0; h < 2; ++h) {  // dims 0-127, then 128-255: (hi, lo) slot pairs
-          uint32_t kh_a, kl_a;
-          if (!take_slot(kh_a) || !peek_slot(kl_a)) return false;
+        for (int db = 0; db < 4; ++db) {  // one slot per 64-dim block: [hi, lo][128 keys][128 B]
+          uint32_t k_a;
+          if (!take_slot(k_a)) return false;
 #pragma unroll
-          for (int k16 = 0; k16 < 8; ++k16) {
-            const int db = 2 * h + k16 / 4;               // Q dim block
-            const uint32_t koff = (uint32_t)(k16 % 4) * 32;  // K=16 slice within the 128-byte row
+          for (int k16 = 0; k16 < 4; ++k16) {
+            const uint32_t koff = (uint32_t)k16 * 32;  // K=16 slice within the 128-byte row
             const uint32_t qb = (uint32_t)db * QBLK + koff;
-            const uint32_t kb = (uint32_t)(k16 / 4) * DBLK1 + koff;
-            umma_f16(d_s, umma_desc_k_sw128(q_hi + qb), umma_desc_k_sw128(kh_a + kb), idesc_qk, (h | k16) ? 1u : 0u);
-            umma_f16(d_s, umma_desc_k_sw128(q_hi + qb), umma_desc_k_sw128(kl_a + kb), idesc_qk, 1u);
-            umma_f16(d_s, umma_desc_k_sw128(q_lo + qb), umma_desc_k_sw128(kh_a + kb), idesc_qk, 1u);
+            umma_f16(d_s, umma_desc_k_sw128(q_hi + qb), umma_desc_k_sw128(k_a + koff), idesc_qk,
+                     (db | k16) ? 1u : 0u);
+            umma_f16(d_s, umma_desc_k_sw128(q_hi + qb), umma_desc_k_sw128(k_a + PLANE + koff), idesc_qk, 1u);
+            umma_f16(d_s, umma_desc_k_sw128(q_lo + qb), umma_desc_k_sw128(k_a + koff), idesc_qk, 1u);
           }
-          free_slot();
           free_slot();
         }
         umma_commit(&sfull[b]);
@@ -308,21 +301,20 @@ __global__ void __launch_bounds__(THREADS, 1)
         const uint32_t p_buf = tmem + TM_S + pb * KT;  // P written over the scores
         const uint32_t d_o = tmem + TM_O;
 #pragma unroll 1
-        for (int kq = 0; kq < 2; ++kq) {  // keys 0-63, then 64-127: (hi, lo) slot pairs of all 256 dims
-          uint32_t vh_a, vl_a;
-          if (!take_slot(vh_a) || !peek_slot(vl_a)) return false;
+        for (int kq = 0; kq < KT / VKEYS; ++kq) {  // one slot per 32 keys: [hi, lo][4 dim blocks][32 keys][128 B]
+          uint32_t v_a;
+          if (!take_slot(v_a)) return false;
 #pragma unroll
-          for (int k16 = 0; k16 < 4; ++k16) {
-            // keys 64kq + 16k16..: p_hi in 8 packed fp16 columns, then p_lo in the next 8
-            const uint32_t p_hi = p_buf + (uint32_t)(kq * 4 + k16) * 16, p_lo = p_hi + 8;
+          for (int k16 = 0; k16 < VKEYS / 16; ++k16) {
+            // keys 32kq + 16k16..: p_hi in 8 packed fp16 columns, then p_lo in the next 8
+            const uint32_t p_hi = p_buf + (uint32_t)(kq * (VKEYS / 16) + k16) * 16, p_lo = p_hi + 8;
             const uint32_t voff = (uint32_t)k16 * 2048;  // two 8-key groups of V rows
             const uint32_t acc0 = (j > 0 || kq > 0 || k16 > 0) ? 1u : 0u;
-            // N = 256: all dims at once (the four 64-dim blocks of a slot are DBLK apart)
-            umma_f16_ts(d_o, p_hi, umma_desc_mn_sw128(vh_a + voff, DBLK), idesc_pv, acc0);
-            umma_f16_ts(d_o, p_hi, umma_desc_mn_sw128(vl_a + voff, DBLK), idesc_pv, 1u);
-            umma_f16_ts(d_o, p_lo, umma_desc_mn_sw128(vh_a + voff, DBLK), idesc_pv, 1u);
+            // N = 256: all dims at once (the four 64-dim blocks of a plane are VDBLK apart)
+            umma_f16_ts(d_o, p_hi, umma_desc_mn_sw128(v_a + voff, VDBLK), idesc_pv, acc0);
+            umma_f16_ts(d_o, p_hi, umma_desc_mn_sw128(v_a + PLANE + voff, VDBLK), idesc_pv, 1u);
+            umma_f16_ts(d_o, p_lo, umma_desc_mn_sw128(v_a + voff, VDBLK), idesc_pv, 1u);
           }
-          free_slot();
           free_slot();
         }
         umma_commit(&pfree[pb]);
@@ -566,6 +558,25 @@ cudaError_t map_rows(CUtensorMap* m, const __half* base, int64_t rows, int box_r
              : cudaErrorInvalidValue;
 }
 
+// k or v hi and lo planes [2][rows][256] (lo right after hi) as a 4-D map
+// (64 dims, row, dim block, plane) with a box of 64 x box_rows x box_dblks x 2:
+// one copy lands [plane][dim block][row][128 B], each dim block in the
+// 128-byte swizzled layout.
+cudaError_t map_rows_pair(CUtensorMap* m, const __half* base, int64_t rows, int box_rows, int box_dblks) {
+  auto enc = attn_encoder();
+  if (!enc) return cudaErrorNotSupported;
+  if (reinterpret_cast<uintptr_t>(base) & 15) return cudaErrorMisalignedAddress;
+  cuuint64_t dims[4] = {64, (cuuint64_t)rows, (cuuint64_t)(HD / 64), 2};
+  cuuint64_t strides[3] = {(cuuint64_t)HD * 2, 128, (cuuint64_t)rows * HD * 2};
+  cuuint32_t box[4] = {64, (cuuint32_t)box_rows, (cuuint32_t)box_dblks, 2};
+  cuuint32_t es[4] = {1, 1, 1, 1};
+  return enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, const_cast<__half*>(base), dims, strides, box, es,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS
+             ? cudaSuccess
+             : cudaErrorInvalidValue;
+}
+
 // q planes [T][nh][256]: 3-D map (dim, head, token) with a box of 64 x 1 x 128.
 cudaError_t map_q(CUtensorMap* m, const __half* base, int64_t T, int nh) {
   auto enc = attn_encoder();
@@ -592,15 +603,17 @@ cudaError_t launch_attention(const __half* qh, const __half* ql, const __half* k
                              uint32_t* absmax, uint32_t* err, cudaStream_t stream) {
   if (tiles.n_tiles == 0) return cudaSuccess;
   const int64_t T = meta.T;
-  CUtensorMap m_qh, m_ql, m_kh, m_kl, m_vh, m_vl, m_out;
+  CUtensorMap m_qh, m_ql, m_k1, m_k2, m_v2, m_out;
   cudaError_t e;
+  // the lo plane of K and of V directly follows its hi plane (one 4-D map covers both)
+  if (kl != kh + T * HD || vl != vh + T * HD) return cudaErrorInvalidValue;
   if ((e = map_q(&m_qh, qh, T, num_heads)) != cudaSuccess) return e;
   if ((e = map_q(&m_ql, ql, T, num_heads)) != cudaSuccess) return e;
-  // K: 128 keys x 2 dim blocks per copy (one dim half); V: 64 keys x all 4 dim blocks
-  if ((e = map_rows(&m_kh, kh, T, KT, 2)) != cudaSuccess) return e;
-  if ((e = map_rows(&m_kl, kl, T, KT, 2)) != cudaSuccess) return e;
-  if ((e = map_rows(&m_vh, vh, T, 64, 4)) != cudaSuccess) return e;
-  if ((e = map_rows(&m_vl, vl, T, 64, 4)) != cudaSuccess) return e;
+  // pass 1: K hi, 128 keys x 2 dim blocks; pass 2: K hi+lo, 128 keys x 1 dim
+  // block; V hi+lo, 32 keys x 4 dim blocks (32 KB per copy each)
+  if ((e = map_rows(&m_k1, kh, T, KT, 2)) != cudaSuccess) return e;
+  if ((e = map_rows_pair(&m_k2, kh, T, KT, 1)) != cudaSuccess) return e;
+  if ((e = map_rows_pair(&m_v2, vh, T, VKEYS, 4)) != cudaSuccess) return e;
   {  // out [T][nh * 256] fp32: boxes of 32 floats x 128 rows, 128-byte swizzle
     auto enc = attn_encoder();
     if (!enc) return cudaErrorNotSupported;
@@ -626,8 +639,8 @@ cudaError_t launch_attention(const __half* qh, const __half* ql, const __half* k
     }
   }
   dim3 grid(tiles.n_tiles * num_heads);
-  attention_tc_kernel<<<grid, THREADS, SMEM_BYTES, stream>>>(m_qh, m_ql, m_kh, m_kl, m_vh, m_vl, m_out, num_heads,
-                                                             scale, meta, tiles, out, absmax, err);
+  attention_tc_kernel<<<grid, THREADS, SMEM_BYTES, stream>>>(m_qh, m_ql, m_k1, m_k2, m_v2, m_out, num_heads, scale, meta,
+                                                             tiles, out, absmax, err);
   return cudaGetLastError();
 }
 

@@ -127,7 +127,8 @@ struct AttnTiles {
   const int32_t* tile_row0;   // [n_tiles] first packed row of the tile
   int32_t n_tiles;
 };
-// q planes [T][num_heads][256], k and v planes [T][256] (fp16 hi/lo splits),
+// q planes [T][num_heads][256], k and v planes [T][256] (fp16 hi/lo splits;
+// kl == kh + T * 256 and vl == vh + T * 256: the lo planes follow the hi ones),
 // all 16-byte aligned. out [T][num_heads*256] fp32, absmax[seq] atomically.
 // `err` (nullable) receives error bits if a pipeline wait times out.
 cudaError_t launch_attention(const __half* qh, const __half* ql, const __half* kh, const __half* kl,
