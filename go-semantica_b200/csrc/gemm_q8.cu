@@ -54,7 +54,6 @@ constexpr int kRegsProducer = 56;           // warpgroup 0 after setmaxnreg.dec
 // (up to four), so the MMAs may run that many blocks ahead of the epilogue.
 template <int NA, int NT, int GR>
 struct TileCfg {
-  static constexpr int kGroups = GR;
   static constexpr int kEpiWarps = 4 * GR;
   static constexpr int kEpiThreads = kEpiWarps * 32;
   static constexpr int kThreads = 128 + kEpiThreads;

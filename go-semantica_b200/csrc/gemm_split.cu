@@ -75,8 +75,7 @@ __device__ __forceinline__ float gelu_up_f(float g, float u, float rs) {
 
 template <int EPI>
 __global__ void __launch_bounds__(kXThreads, 1)
-    gemm_q8_split_kernel(const __grid_constant__ CUtensorMap tm_hi, const __grid_constant__ CUtensorMap tm_lo,
-                         const __grid_constant__ CUtensorMap tm_a, const float* __restrict__ row_scale, int n_per_a,
+    gemm_q8_split_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_a, const float* __restrict__ row_scale, int n_per_a,
                          int T, int K, const uint32_t* __restrict__ a_absmax, const int32_t* __restrict__ row_seq,
                          float* __restrict__ c_out, uint32_t* __restrict__ out_absmax, uint32_t* __restrict__ err) {
   using Cf = XCfg<EPI>;
@@ -124,8 +123,7 @@ __global__ void __launch_bounds__(kXThreads, 1)
     // ---------------- TMA producers (alternate stages) ----------------
     if (lane == 0) {
       const uint32_t me = warp >> 1;
-      tma_prefetch_desc(&tm_hi);
-      tma_prefetch_desc(&tm_lo);
+      tma_prefetch_desc(&tm_w);
       tma_prefetch_desc(&tm_a);
       uint32_t it = 0;
       bool ok = true;
@@ -141,11 +139,8 @@ __global__ void __launch_bounds__(kXThreads, 1)
           uint8_t* st = stages + s * L::kStage;
           mbar_arrive_expect_tx(&full[s], L::kStage);
 #pragma unroll
-          for (int a = 0; a < NA; ++a) {
-            const int wrow = a * n_per_a + mt * kXM;
-            tma_load_2d(&tm_hi, &full[s], st + (2 * a) * kXWTile, ks * kXK, wrow);
-            tma_load_2d(&tm_lo, &full[s], st + (2 * a + 1) * kXWTile, ks * kXK, wrow);
-          }
+          for (int a = 0; a < NA; ++a)  // hi then lo rows of the tile: one 3-D copy
+            tma_load_3d(&tm_w, &full[s], st + (2 * a) * kXWTile, ks * kXK, a * n_per_a + mt * kXM, 0);
           tma_load_2d(&tm_a, &full[s], st + 2 * NA * kXWTile, ks * kXK, tt * NT);
         }
       }
@@ -283,8 +278,7 @@ constexpr int kGuSmem = 1024 + kGuStages * kGuStage + kXBarBytes + 2 * 2 * kGuCh
 static_assert(kGuSmem <= 232448, "shared memory per CTA");
 
 __global__ void __launch_bounds__(kXThreads, 1)
-    gemm_q8_gateup_kernel(const __grid_constant__ CUtensorMap tm_hi, const __grid_constant__ CUtensorMap tm_lo,
-                          const __grid_constant__ CUtensorMap tm_a, const float* __restrict__ row_scale, int F, int T,
+    gemm_q8_gateup_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_a, const float* __restrict__ row_scale, int F, int T,
                           int K, const uint32_t* __restrict__ a_absmax, const int32_t* __restrict__ row_seq,
                           float* __restrict__ h_out, uint32_t* __restrict__ out_absmax, uint32_t* __restrict__ err) {
   constexpr int ST = kGuStages;
@@ -329,8 +323,7 @@ __global__ void __launch_bounds__(kXThreads, 1)
     // ---------------- TMA producers (alternate stages) ----------------
     if (lane == 0) {
       const uint32_t me = warp >> 1;
-      tma_prefetch_desc(&tm_hi);
-      tma_prefetch_desc(&tm_lo);
+      tma_prefetch_desc(&tm_w);
       tma_prefetch_desc(&tm_a);
       uint32_t it = 0;
       bool ok = true;
@@ -346,10 +339,8 @@ __global__ void __launch_bounds__(kXThreads, 1)
           uint8_t* st = stages + s * kGuStage;
           mbar_arrive_expect_tx(&full[s], kGuStage);
           tma_load_2d(&tm_a, &full[s], st, ks * kXK, tt * kGuTok);
-          tma_load_2d(&tm_hi, &full[s], st + kGuA, ks * kXK, ct * kGuCh);                    // gate rows
-          tma_load_2d(&tm_hi, &full[s], st + kGuA + kGuB / 2, ks * kXK, F + ct * kGuCh);     // up rows
-          tma_load_2d(&tm_lo, &full[s], st + kGuA + kGuB, ks * kXK, ct * kGuCh);
-          tma_load_2d(&tm_lo, &full[s], st + kGuA + kGuB + kGuB / 2, ks * kXK, F + ct * kGuCh);
+          // [hi, lo][gate, up][128 rows][128 B]: one 4-D copy
+          tma_load_4d(&tm_w, &full[s], st + kGuA, ks * kXK, ct * kGuCh, 0, 0);
         }
       }
       for (uint32_t j = it > (uint32_t)ST ? it - ST : 0; j < it; ++j)
@@ -501,19 +492,21 @@ cudaError_t launch_split(const __half* a_codes, const __half* w_hi, const __half
     sms = g_split_sms[dev];
   }
   const int n_per_a = n_rows / Cf::NA;
-  CUtensorMap tm_hi, tm_lo, tm_a;
-  if ((e = tmap_2d(&tm_hi, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, w_hi, n_rows, K, kXK, kXM,
-                   CU_TENSOR_MAP_SWIZZLE_128B)) != cudaSuccess)
-    return e;
-  if ((e = tmap_2d(&tm_lo, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, w_lo, n_rows, K, kXK, kXM,
-                   CU_TENSOR_MAP_SWIZZLE_128B)) != cudaSuccess)
-    return e;
+  CUtensorMap tm_w, tm_a;
+  {  // (K, rows, plane): the lo plane follows the hi plane
+    const uint64_t dims[3] = {(uint64_t)K, (uint64_t)n_rows, 2};
+    const uint64_t strides[2] = {(uint64_t)K * 2, (uint64_t)n_rows * K * 2};
+    const uint32_t box[3] = {kXK, kXM, 2};
+    if ((e = tmap_nd(&tm_w, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, w_hi, 3, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B)) !=
+        cudaSuccess)
+      return e;
+  }
   if ((e = tmap_2d(&tm_a, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, a_codes, T, K, kXK, Cf::NT,
                    CU_TENSOR_MAP_SWIZZLE_128B)) != cudaSuccess)
     return e;
   const int total = (n_per_a / kXM) * ((T + Cf::NT - 1) / Cf::NT);
   const int grid = total < sms ? total : sms;
-  kern<<<grid, kXThreads, L::kSmem, stream>>>(tm_hi, tm_lo, tm_a, row_scale, n_per_a, T, K, a_absmax, row_seq, c,
+  kern<<<grid, kXThreads, L::kSmem, stream>>>(tm_w, tm_a, row_scale, n_per_a, T, K, a_absmax, row_seq, c,
                                               out_absmax, err);
   return cudaGetLastError();
 }
@@ -541,19 +534,21 @@ cudaError_t launch_gateup(const __half* a_codes, const __half* w_hi, const __hal
     }
     sms = g_split_sms[dev];
   }
-  CUtensorMap tm_hi, tm_lo, tm_a;
-  if ((e = tmap_2d(&tm_hi, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, w_hi, 2 * F, K, kXK, kGuCh,
-                   CU_TENSOR_MAP_SWIZZLE_128B)) != cudaSuccess)
-    return e;
-  if ((e = tmap_2d(&tm_lo, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, w_lo, 2 * F, K, kXK, kGuCh,
-                   CU_TENSOR_MAP_SWIZZLE_128B)) != cudaSuccess)
-    return e;
+  CUtensorMap tm_w, tm_a;
+  {  // (K, channel, gate/up, plane): up rows F below gate rows, the lo plane after the hi plane
+    const uint64_t dims[4] = {(uint64_t)K, (uint64_t)F, 2, 2};
+    const uint64_t strides[3] = {(uint64_t)K * 2, (uint64_t)F * K * 2, (uint64_t)2 * F * K * 2};
+    const uint32_t box[4] = {kXK, kGuCh, 2, 2};
+    if ((e = tmap_nd(&tm_w, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, w_hi, 4, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B)) !=
+        cudaSuccess)
+      return e;
+  }
   if ((e = tmap_2d(&tm_a, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, a_codes, T, K, kXK, kGuTok,
                    CU_TENSOR_MAP_SWIZZLE_128B)) != cudaSuccess)
     return e;
   const int total = (F / kGuCh) * ((T + kGuTok - 1) / kGuTok);
   const int grid = total < sms ? total : sms;
-  gemm_q8_gateup_kernel<<<grid, kXThreads, kGuSmem, stream>>>(tm_hi, tm_lo, tm_a, row_scale, F, T, K, a_absmax, row_seq,
+  gemm_q8_gateup_kernel<<<grid, kXThreads, kGuSmem, stream>>>(tm_w, tm_a, row_scale, F, T, K, a_absmax, row_seq,
                                                               h, out_absmax, err);
   return cudaGetLastError();
 }
@@ -565,6 +560,7 @@ cudaError_t launch_gemm_q8_split(const __half* a_codes, const __half* w_hi, cons
                                  int epilogue, uint32_t* out_absmax, uint32_t* err, cudaStream_t stream) {
   if (M == 0) return cudaSuccess;
   if (M < 0 || K <= 0 || K % kXK != 0) return cudaErrorInvalidValue;
+  if (w_lo != w_hi + (size_t)N * K) return cudaErrorInvalidValue;  // one map covers both planes
   if (epilogue == kEpiGeluUp) {
     if (N % (2 * kGuCh) != 0) return cudaErrorInvalidValue;
     return launch_gateup(a_codes, w_hi, w_lo, row_scale, M, N / 2, K, a_absmax, row_seq, c, out_absmax, err, stream);

@@ -102,10 +102,10 @@ struct sem_q8_weight {
   sem_context* ctx = nullptr;
   int32_t k_in = 0, n_out = 0;
   sem::DevBuf codes, scales;   // fp16 codes [n_out][k_in], block scales [n_out][k_in/32]
-  sem::DevBuf hi, lo, rscale;  // split planes [n_out][k_in], row scales [n_out]
+  sem::DevBuf planes, rscale;  // split planes hi then lo [2][n_out][k_in], row scales [n_out]
   sem::Q8Proj proj() const {
-    return sem::Q8Proj{static_cast<const __half*>(codes.p), static_cast<const float*>(scales.p),
-                       static_cast<const __half*>(hi.p), static_cast<const __half*>(lo.p),
-                       static_cast<const float*>(rscale.p)};
+    const __half* hi = static_cast<const __half*>(planes.p);
+    return sem::Q8Proj{static_cast<const __half*>(codes.p), static_cast<const float*>(scales.p), hi,
+                       hi ? hi + (size_t)n_out * k_in : nullptr, static_cast<const float*>(rscale.p)};
   }
 };

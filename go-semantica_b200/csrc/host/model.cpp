@@ -157,8 +157,8 @@ int model_load(sem_context* ctx, const sem_model_config* cfg_in, const sem_tenso
     POff p;
     p.codes = take((size_t)rows * k * 2);
     p.scales = take((size_t)rows * (k / 32) * 4);
-    p.hi = take((size_t)rows * k * 2);
-    p.lo = take((size_t)rows * k * 2);
+    p.hi = take((size_t)2 * rows * k * 2);  // hi plane, then the lo plane right after it
+    p.lo = p.hi + (size_t)rows * k * 2;
     p.rsc = take((size_t)rows * 4);
     return p;
   };
@@ -580,8 +580,7 @@ int q8_weight_create(sem_context* ctx, const void* w_q8, int32_t k_in, int32_t n
   w->n_out = n_out;
   SEM_CUDA(w->codes.ensure((size_t)k_in * n_out * 2));
   SEM_CUDA(w->scales.ensure((size_t)n_out * (k_in / 32) * 4));
-  SEM_CUDA(w->hi.ensure((size_t)k_in * n_out * 2));
-  SEM_CUDA(w->lo.ensure((size_t)k_in * n_out * 2));
+  SEM_CUDA(w->planes.ensure((size_t)2 * k_in * n_out * 2));
   SEM_CUDA(w->rscale.ensure((size_t)n_out * 4));
   DevBuf staging;
   sem_tensor_view t{"weight", kQ8, 2, {(uint64_t)k_in, (uint64_t)n_out, 0, 0}, w_q8,

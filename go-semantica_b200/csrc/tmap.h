@@ -40,4 +40,28 @@ inline cudaError_t tmap_2d(CUtensorMap* map, CUtensorMapDataType dtype, int esiz
   return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
 }
 
+// General map of rank 2..5: dims[0] innermost (elements), strides[i] the byte
+// stride of dimension i + 1 (multiples of 16), box[] in elements.
+inline cudaError_t tmap_nd(CUtensorMap* map, CUtensorMapDataType dtype, const void* base, int rank,
+                           const uint64_t* dims, const uint64_t* strides, const uint32_t* box,
+                           CUtensorMapSwizzle swz) {
+  auto enc = tmap_encoder();
+  if (!enc) return cudaErrorNotSupported;
+  if (rank < 2 || rank > 5 || (reinterpret_cast<uintptr_t>(base) & 15)) return cudaErrorInvalidValue;
+  cuuint64_t d[5], st[4];
+  cuuint32_t bx[5], es[5];
+  for (int i = 0; i < rank; ++i) {
+    d[i] = dims[i];
+    bx[i] = box[i];
+    es[i] = 1;
+    if (i + 1 < rank) {
+      if (strides[i] % 16) return cudaErrorMisalignedAddress;
+      st[i] = strides[i];
+    }
+  }
+  CUresult r = enc(map, dtype, (cuuint32_t)rank, const_cast<void*>(base), d, st, bx, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+}
+
 }  // namespace sem
