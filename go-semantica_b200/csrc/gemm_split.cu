@@ -597,7 +597,7 @@ cudaError_t launch_q8_proj(const __half* a_codes, const Q8Proj& w, int M, int N,
     const bool gelu = epilogue == kEpiGeluUp;
     const int nt = gelu ? kGuTok : XCfg<kEpiStore>::NT;
     const int64_t tiles = (int64_t)(N / (gelu ? 2 : 1) / kXM) * ((M + nt - 1) / nt);
-    if (tiles >= sms)
+    if (2 * tiles >= sms)  // measured crossover: from ~half a wave of split tiles it beats the per-block kernel
       return launch_gemm_q8_split(a_codes, w.hi, w.lo, w.row_scale, M, N, K, a_absmax, row_seq, c, epilogue,
                                   out_absmax, err, stream);
   }

@@ -110,7 +110,8 @@ struct Q8Proj {
   const float* row_scale;  // [N]
 };
 // Picks the kernel for M tokens: the split-plane GEMM once its tiles fill
-// every SM, else the per-block kernel (narrower token tiles).
+// half the SMs (measured crossover), else the per-block kernel (narrower
+// token tiles, half the weight bytes).
 cudaError_t launch_q8_proj(const __half* a_codes, const Q8Proj& w, int M, int N, int K, const uint32_t* a_absmax,
                            const int32_t* row_seq, float* c, int epilogue, uint32_t* out_absmax, uint32_t* err,
                            cudaStream_t stream);

@@ -155,7 +155,7 @@ int sem_q8_matmul_int8(sem_q8_weight *w, const void *d_codes, const uint32_t *d_
  * its builds), shorter sequences always take the per-block kernel.
  *   SEM_Q8_PATH_AUTO (default): long-sequence rows (all rows for
  *     sem_q8_gemm) take the split-plane kernel when its 128 x 256-token tiles
- *     fill every SM, else the per-block kernel;
+ *     fill at least half the SMs, else the per-block kernel;
  *   SEM_Q8_PATH_BLOCK: the per-block kernel everywhere;
  *   SEM_Q8_PATH_SPLIT: the split-plane kernel for long-sequence rows (all
  *     rows for sem_q8_gemm) whatever their count;
