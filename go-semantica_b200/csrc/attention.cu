@@ -61,7 +61,7 @@ constexpr int SMEM_Q = 2 * 4 * QBLK;     // hi, lo x 4 dim blocks: 128 KB
 constexpr int SMEM_RING = NSLOT * SLOT;  // 96 KB
 constexpr int NS1 = 2;  // score buffers of pass 1 (128 columns each, in the O columns, unused until pass 2)
 // q, ring full/empty, S full, P full, S/P buffer free, O, drain, pass-1 S full/empty
-constexpr int NBAR = 1 + 2 * NSLOT + 2 + 2 + 2 + 1 + 1 + 2 * NS1;
+constexpr int NBAR = 1 + 2 * NSLOT + 2 + 2 + 2 + 1 + 1 + 2 * NS1 + 1;
 constexpr int BAR_BLOCK = 320;                     // barriers, TMEM address, abort flag
 constexpr int SMEM_MISC = BAR_BLOCK + 2 * QT * 4;  // + [2][QT] reductions
 constexpr int SMEM_BYTES = 1024 + SMEM_Q + SMEM_RING + SMEM_MISC;
@@ -143,6 +143,7 @@ __global__ void __launch_bounds__(THREADS, 1)
   uint64_t* drain = ofull + 1;
   uint64_t* s1full = drain + 1;
   uint64_t* s1empty = s1full + NS1;
+  uint64_t* qlofull = s1empty + NS1;  // Q lo landed (pass 1 needs only Q hi, behind qfull)
   uint32_t* s_tmem = reinterpret_cast<uint32_t*>(bars + NBAR);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(s_tmem + 1);
   float* s_red = reinterpret_cast<float*>(sRing + SMEM_RING + BAR_BLOCK);  // [2 halves][QT]: maxima, later sums
@@ -191,12 +192,9 @@ __global__ void __launch_bounds__(THREADS, 1)
       uint32_t it = 0;
       bool ok = true;
       if (me == 0) {
-        mbar_arrive_expect_tx(qfull, SMEM_Q);
+        mbar_arrive_expect_tx(qfull, SMEM_Q / 2);
 #pragma unroll
-        for (int b = 0; b < 4; ++b) {
-          tma_load_3d(&tm_qh, qfull, sQ + b * QBLK, b * 64, head, row0);
-          tma_load_3d(&tm_ql, qfull, sQ + (4 + b) * QBLK, b * 64, head, row0);
-        }
+        for (int b = 0; b < 4; ++b) tma_load_3d(&tm_qh, qfull, sQ + b * QBLK, b * 64, head, row0);
       }
       // one slot: a 3-D box (pass 1) or a 4-D box whose outermost dimension is
       // the plane (pass 2)
@@ -215,8 +213,19 @@ __global__ void __launch_bounds__(THREADS, 1)
         ++it;
         return true;
       };
-      for (int j = 0; ok && j < nkt; ++j)
+      for (int j = 0; ok && j < nkt; ++j) {
         for (int h = 0; ok && h < 2; ++h) ok = load_slot(&tm_k1, false, s_beg + j * KT, 2 * h);
+        if (j == 0 && me == 0) {  // Q lo behind the first K tile: pass 1 does not need it
+          mbar_arrive_expect_tx(qlofull, SMEM_Q / 2);
+#pragma unroll
+          for (int b = 0; b < 4; ++b) tma_load_3d(&tm_ql, qlofull, sQ + (4 + b) * QBLK, b * 64, head, row0);
+        }
+      }
+      if (nkt == 0 && me == 0) {  // keep the barrier's one phase complete
+        mbar_arrive_expect_tx(qlofull, SMEM_Q / 2);
+#pragma unroll
+        for (int b = 0; b < 4; ++b) tma_load_3d(&tm_ql, qlofull, sQ + (4 + b) * QBLK, b * 64, head, row0);
+      }
       for (int j = 0; ok && j <= nkt; ++j) {
         if (j < nkt)
           for (int db = 0; ok && db < 4; ++db) ok = load_slot(&tm_k2, true, s_beg + j * KT, db);
@@ -225,7 +234,10 @@ __global__ void __launch_bounds__(THREADS, 1)
       }
       for (uint32_t j = it > (uint32_t)NSLOT ? it - NSLOT : 0; j < it; ++j)
         if ((j & 1) == me) mbar_wait_drain(&rfull[j % NSLOT], (j / NSLOT) & 1);
-      if (me == 0) mbar_wait_drain(qfull, 0);
+      if (me == 0) {
+        mbar_wait_drain(qfull, 0);
+        mbar_wait_drain(qlofull, 0);
+      }
     } else if (warp == 1 && lane == 0) {
       // ---------------- MMA issuer ----------------
       constexpr uint32_t idesc_qk = umma_idesc_f16_f32(QT, KT);  // N = 128 keys
@@ -321,13 +333,15 @@ __global__ void __launch_bounds__(THREADS, 1)
         return true;
       };
       for (int j = 0; ok && j < nkt; ++j) ok = qk1();
-      // the softmax has read every pass-1 buffer before P.V overwrites the O columns
-      for (int k = 0; ok && k < NS1 && k < nkt; ++k) {
-        const int last = k + NS1 * ((nkt - 1 - k) / NS1);
-        ok = mbar_wait(&s1empty[k], (last / NS1) & 1, abort_flag, err, 2u);
-      }
+      if (ok) ok = mbar_wait(qlofull, 0, abort_flag, err, 2u);
+      tc_fence_after();
       for (int j = 0; ok && j <= nkt; ++j) {
         if (j < nkt) ok = qk();
+        if (ok && j == 1)  // the softmax has read every pass-1 buffer before P.V overwrites the O columns
+          for (int k = 0; ok && k < NS1 && k < nkt; ++k) {
+            const int last = k + NS1 * ((nkt - 1 - k) / NS1);
+            ok = mbar_wait(&s1empty[k], (last / NS1) & 1, abort_flag, err, 2u);
+          }
         if (ok && j >= 1) ok = pv(j - 1);
       }
       umma_commit(ofull);
