@@ -50,7 +50,7 @@ def workload_config(n_gpus: int) -> dict:
         "global_batch": BATCH * n_gpus,
         "seq_len": SEQ_LEN,
         "parallelism": f"dp{n_gpus}",
-        "l2": "inputs larger than L2: ~10 GB of activations and 0.32 GB of weights stream per step",
+        "l2": "inputs larger than L2: ~10 GB of activations and ~0.4 GB of weight planes stream per step",
     }
 
 
@@ -168,8 +168,8 @@ def stage_roofline(stage: str, total_ms: float, launches: int, T: int, n_seqs: i
         achieved = flops / (per_ms * 1e-3) / 1e12
         peak = peaks.get("bf16_tflops_sustained") or 1415.9
         return {"kernel": stage, "bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
-                "frac": achieved / peak, "peak_source": "measured bf16_tflops_sustained (no int8 figure is measured "
-                "on this pool; int8 dense nominal is 2x bf16)", "algorithmic_flops_per_launch": flops,
+                "frac": achieved / peak, "peak_source": "measured bf16_tflops_sustained (the projections run "
+                "kind::f16 MMAs, the bf16 rate; algorithmic FLOPs: the hi and lo planes execute twice that)", "algorithmic_flops_per_launch": flops,
                 "launch_ms": per_ms}
     if stage == "attention":
         S = T // n_seqs
