@@ -747,13 +747,18 @@ def run_search(args) -> None:
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = search_cpu_baseline(codes[:1 << 20].cpu().numpy(), qcodes[:1024].cpu().numpy())
         print(json.dumps(line), flush=True)
-    lib.sem_index_free(h)
-    del qf_host, ids_host
+    # tensors used on the library's stream (the NCCL all-gather runs there) go
+    # first, then the process group, and only then the stream itself
     torch.cuda.synchronize()
-    ctx.close()
+    del qf_np, qf_host, ids_host, qf_dev, q_dev, keys, rows, scores, qcodes  # qf_np views the pinned qf_host
+    torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+    lib.sem_index_free(h)
+    del codes
+    torch.cuda.synchronize()
+    ctx.close()
 
 
 def run_search_reference(args) -> None:
