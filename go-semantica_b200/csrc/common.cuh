@@ -69,11 +69,15 @@ __device__ __forceinline__ float row_sumsq_ref(const float* __restrict__ x, int 
 }
 
 // RMSNorm inverse scale (internal/kernels/norm.go:8-36):
-// 1 / float32(sqrt(float64(sumSq/n + eps))).
+// 1 / float32(sqrt(float64(sumSq/n + eps))). Rounding a square root first to
+// float64 and then to float32 gives the correctly rounded float32 root (53 >=
+// 2 * 24 + 2 bits makes the double rounding innocuous; also checked on every
+// non-negative float), so the IEEE float32 square root computes it; 1 / rms
+// is the IEEE reciprocal.
 __device__ __forceinline__ float rms_inv_ref(float sumsq, int n, float eps) {
   float mean = __fdiv_rn(sumsq, (float)n);
-  float rms = (float)sqrt((double)__fadd_rn(mean, eps));
-  return __fdiv_rn(1.0f, rms);
+  float rms = __fsqrt_rn(__fadd_rn(mean, eps));
+  return __frcp_rn(rms);
 }
 
 // Per-sequence activation scale (quantize.go:60-61) from an absmax bit pattern.
@@ -112,6 +116,30 @@ __device__ __forceinline__ float quant_code_f32(float x, float inv) {
   const bool away = ad > 0.5f || (ad == 0.5f && (pos ? e >= 0.0f : e <= 0.0f));
   const float n = away ? (pos ? __fadd_rn(t, 1.0f) : __fsub_rn(t, 1.0f)) : t;
   return fminf(fmaxf(n, -127.0f), 127.0f);
+}
+
+// Four codes of quantizeInto as packed fp16. Rounding preserves order and
+// every half-integer of magnitude below 2^23 is a float, so round-half-away of
+// the exact product equals rint(p) of the rounded product p unless p itself is
+// a half-integer; only then (rarely) does the exact path above run. Larger
+// |p| clamp to +-127 on both paths, NaN to -127 on both.
+__device__ __forceinline__ uint2 quant_codes4(float4 x, float inv) {
+  const float e[4] = {x.x, x.y, x.z, x.w};
+  float n[4];
+  bool tie = false;
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const float p = __fmul_rn(e[k], inv);
+    n[k] = rintf(p);
+    tie |= fabsf(__fsub_rn(p, n[k])) == 0.5f;
+    n[k] = fminf(fmaxf(n[k], -127.0f), 127.0f);
+  }
+  if (tie) {
+#pragma unroll
+    for (int k = 0; k < 4; ++k) n[k] = quant_code_f32(e[k], inv);
+  }
+  __half2 h[2] = {__floats2half2_rn(n[0], n[1]), __floats2half2_rn(n[2], n[3])};
+  return *reinterpret_cast<uint2*>(h);
 }
 
 __device__ __forceinline__ void atomic_max_abs(uint32_t* slot, float v) {

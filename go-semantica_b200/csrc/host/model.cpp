@@ -456,26 +456,28 @@ int run_forward(sem_model* m, const int32_t* d_ids, const MetaPtrs& mp, float* d
   SEM_LAUNCH(kStEmbed, cudaMemsetAsync(m->errflag.p, 0, 8, st));
   SEM_LAUNCH(kStEmbed, launch_embed(d_ids, m->emb, m->emb_s, c.vocab_size, H, hid, (int)T, m->errflag.as<uint32_t>(), st));
   SEM_LAUNCH(kStRowStats, launch_row_stats(hid, m->layers[0].attn_norm, H, c.norm_eps, sm, inv, slot(0, 0), st));
+  // the first attention norm's codes; every later norm is quantized by the
+  // residual kernel before it
+  SEM_LAUNCH(kStQuant, launch_quantize(hid, inv, m->layers[0].attn_norm, H, sm, slot(0, 0), codes, st));
   for (int l = 0; l < L; ++l) {
     const LayerW& w = m->layers[l];
     // attention block (model_int8.go:191-210)
-    SEM_LAUNCH(kStQuant, launch_quantize(hid, inv, w.attn_norm, H, sm, slot(l, 0), codes, st));
     SEM_LAUNCH(kStGemmQKV, q8(w.qkv, qkvN, H, slot(l, 0), big, qkvN, kEpiStore, nullptr));
     SEM_LAUNCH(kStQKNormRope, launch_qk_norm_rope(big, w.q_norm, w.k_norm, m->rope_cos, m->rope_sin, c.norm_eps, nh, sm, qh, ql, kh, kl,
                                    vh, vl, st));
     SEM_LAUNCH(kStAttention, launch_attention(qh, ql, kh, kl, vh, vl, nh, c.attention_scale, sm, mp.tiles, att, slot(l, 1), err, st));
     SEM_LAUNCH(kStQuant, launch_quantize(att, nullptr, nullptr, H, sm, slot(l, 1), codes, st));
     SEM_LAUNCH(kStGemmO, q8(w.o, H, H, slot(l, 1), big, H, kEpiStore, nullptr));
-    SEM_LAUNCH(kStResidual, launch_residual_norm(big, w.post_attn, hid, w.ffn_norm, H, c.norm_eps, sm, inv, slot(l, 2), st));
+    SEM_LAUNCH(kStResidual, launch_residual_norm(big, w.post_attn, hid, w.ffn_norm, H, c.norm_eps, sm, inv, slot(l, 2),
+                                                 codes, st));
     // MLP block (model_int8.go:213-232)
-    SEM_LAUNCH(kStQuant, launch_quantize(hid, inv, w.ffn_norm, H, sm, slot(l, 2), codes, st));
     SEM_LAUNCH(kStGemmGateUp, q8(w.gu, 2 * F, H, slot(l, 2), big, F, kEpiGeluUp, slot(l, 3)));
     SEM_LAUNCH(kStQuant, launch_quantize(big, nullptr, nullptr, F, sm, slot(l, 3), codes, st));
     SEM_LAUNCH(kStGemmDown, q8(w.down, H, F, slot(l, 3), att, H, kEpiStore, nullptr));
     const bool last = l + 1 == L;
     const float* next_w = last ? m->out_norm : m->layers[l + 1].attn_norm;
     SEM_LAUNCH(kStResidual, launch_residual_norm(att, w.post_ffw, hid, next_w ? next_w : w.ffn_norm, H, c.norm_eps, sm, inv,
-                                    last ? nullptr : slot(l + 1, 0), st));
+                                                 last ? nullptr : slot(l + 1, 0), last ? nullptr : codes, st));
   }
   // output_norm + mean pool + L2 (model_int8.go:235-255)
   SEM_LAUNCH(kStPool, launch_pool_l2(hid, m->out_norm ? inv : nullptr, m->out_norm, H, sm, mp.out_dims, mp.out_off, d_out, st));

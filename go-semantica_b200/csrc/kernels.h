@@ -70,10 +70,15 @@ cudaError_t launch_qk_norm_rope(const float* qkv, const float* q_norm, const flo
                                 __half* ql, __half* kh, __half* kl, __half* vh, __half* vl,
                                 cudaStream_t stream);
 
-// hidden = rmsnorm(o, post_w) + hidden; then the statistics of the new hidden
-// rows for next_w (inv_rms, per-sequence absmax; absmax may be null).
+// hidden = rmsnorm(o, post_w) + hidden and inv_rms of the new rows for the
+// next norm (next_w); with codes (and absmax) also the next norm's output
+// quantized with its per-sequence scale: absmax[seq] = max |(hidden *
+// inv_rms) * next_w| over the sequence, codes as in launch_quantize. codes and
+// absmax are both null or both set. H is 256, 512 or 768; meta.cu_seqlens is
+// required (a cluster of CTAs owns one sequence at a time).
 cudaError_t launch_residual_norm(const float* o, const float* post_w, float* hidden, const float* next_w, int H,
-                                 float eps, SeqMeta meta, float* inv_rms, uint32_t* absmax, cudaStream_t stream);
+                                 float eps, SeqMeta meta, float* inv_rms, uint32_t* absmax, __half* codes,
+                                 cudaStream_t stream);
 
 // Mean pooling of the first out_dim[s] columns of (hidden * inv_rms) * w over
 // each sequence, then L2 normalisation; writes out + out_offset[s].

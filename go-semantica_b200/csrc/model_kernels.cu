@@ -7,10 +7,14 @@
 // fast-math). Rows of a batch are packed back to back; row_seq maps a row to
 // its sequence, whose activation scale is the absmax of that sequence alone
 // (the reference quantises one whole sequence per call, quantize.go:29-69).
+#include <cooperative_groups.h>
+
 #include "common.cuh"
 #include "kernels.h"
 
 namespace sem {
+
+namespace cg = cooperative_groups;
 
 // ---------------------------------------------------------------------------
 // f16 decoders. The reference has two and they differ on subnormals.
@@ -342,17 +346,13 @@ __global__ void __launch_bounds__(kQuantWarps * 32)
     for (int b = 0; b < kQuantBatch; ++b) {
       const int c4 = seg + b * 32 + lane;
       if (c4 >= q4) continue;
-      float e[4] = {v[b].x, v[b].y, v[b].z, v[b].w};
+      float4 e = v[b];
       if (inv_rms) {
         const float4 wv = reinterpret_cast<const float4*>(w)[c4];
-        const float ww[4] = {wv.x, wv.y, wv.z, wv.w};
-#pragma unroll
-        for (int k = 0; k < 4; ++k) e[k] = __fmul_rn(__fmul_rn(e[k], r), ww[k]);
+        e = make_float4(__fmul_rn(__fmul_rn(e.x, r), wv.x), __fmul_rn(__fmul_rn(e.y, r), wv.y),
+                        __fmul_rn(__fmul_rn(e.z, r), wv.z), __fmul_rn(__fmul_rn(e.w, r), wv.w));
       }
-      __half2 h[2];
-      h[0] = __floats2half2_rn(quant_code_f32(e[0], inv), quant_code_f32(e[1], inv));
-      h[1] = __floats2half2_rn(quant_code_f32(e[2], inv), quant_code_f32(e[3], inv));
-      *reinterpret_cast<uint2*>(codes + row * K + 4 * c4) = *reinterpret_cast<uint2*>(h);
+      *reinterpret_cast<uint2*>(codes + row * K + 4 * c4) = quant_codes4(e, inv);
     }
     }
   }
@@ -501,120 +501,213 @@ cudaError_t launch_qk_norm_rope(const float* qkv, const float* q_norm, const flo
 
 // ---------------------------------------------------------------------------
 // Post-norm + residual (model_int8.go:202-210, :224-232) fused with the next
-// norm's statistics (:194/:216 of the following step, or output_norm :236).
+// RMSNorm (:194 / :216 of the following step) and its INT8 quantisation
+// (QuantizeSymmetricINT8Into, quantize.go:29-69: one scale per sequence).
 // ---------------------------------------------------------------------------
-// hidden = rmsnorm(o, post_w) + hidden and the statistics of the new rows
-// (model_int8.go:203-210, :225-232, then the next RMSNorm's inv_rms and the
-// per-sequence absmax of the normed rows). Each warp takes 4 rows at a time:
-// the rows move between global memory and a padded shared-memory copy with
-// 16-byte accesses, and the two sums of squares run from shared memory in the
-// reference's 8-lane order (one 8-lane group per row).
-constexpr int kRnWarps = 4;
-constexpr int kRnRows = 2;  // rows per warp: small shared-memory tiles keep many warps (and loads) in flight
-constexpr int kRowPad = 8;  // row stride H + 8 floats puts the 4 row groups of a warp on distinct banks
-constexpr int kRnBatch = 8;  // 16-byte loads in flight per lane
+// A cluster of kRqCluster CTAs owns one sequence at a time, each CTA a
+// contiguous share of its rows.
+//  Phase 1, one warp per pair of rows: hidden = rmsnorm(o, post_w) + hidden,
+//   the next norm's inv_rms, and the CTA's max |(hidden * inv_rms) * next_w|.
+//  The CTA maxima meet in rank 0's shared memory (distributed shared memory
+//   atomics); after one cluster barrier every CTA holds the sequence absmax.
+//  Phase 2 re-reads the CTA's rows of hidden (just written: L2 hits) and
+//   writes the INT8 codes (as fp16, the projection operand type).
+// Without codes the kernel ends after phase 1 (the last layer, whose rows go
+// to output_norm and the pool).
+//
+// The sums of squares keep the reference's 8-lane AVX2 order: lane `sub` of a
+// row's 8-lane group accumulates elements 8v + sub for v = 0, 1, ... with fused
+// multiply-adds, then the lanes combine in dotProductAVX2Asm's tail order
+// (norm.go:8-36, simd_amd64.s:19-76). The rows sit in shared memory
+// transposed to [residue][v], so a lane reads its chain 16 bytes at a time.
+constexpr int kRqWarps = 8;
+constexpr int kRqCluster = 8;
 
+template <int H>
+struct RqShape {
+  static constexpr int kNV = H / 128;                   // float4 per lane per row
+  static constexpr int kTS = H / 8 + 4;                 // floats per residue column: conflict-free
+  static constexpr int kWarpFloats = 2 * 8 * kTS;       // two rows per warp
+  static constexpr int kSmem = kRqWarps * kWarpFloats * 4;
+};
 
-__global__ void __launch_bounds__(kRnWarps * 32)
-    residual_norm_kernel(const float* __restrict__ o, const float* __restrict__ post_w, float* __restrict__ hidden,
-                         const float* __restrict__ next_w, int H, float eps, SeqMeta meta,
-                         float* __restrict__ inv_rms, uint32_t* __restrict__ absmax) {
-  extern __shared__ float rn_smem[];
+// Sum of squares of one residue column in element order (one lane's chain).
+template <int H>
+__device__ __forceinline__ float chain_sumsq(const float* col) {
+  float acc = 0.0f;
+#pragma unroll 2
+  for (int j = 0; j < H / 32; ++j) {
+    const float4 t = *reinterpret_cast<const float4*>(col + 4 * j);
+    acc = fmaf(t.x, t.x, acc);
+    acc = fmaf(t.y, t.y, acc);
+    acc = fmaf(t.z, t.z, acc);
+    acc = fmaf(t.w, t.w, acc);
+  }
+  return acc;
+}
+
+template <int H>
+__global__ void __cluster_dims__(kRqCluster, 1, 1) __launch_bounds__(kRqWarps * 32, 2)
+    residual_quant_kernel(const float* __restrict__ o, const float* __restrict__ post_w, float* hidden,
+                          const float* __restrict__ next_w, float eps, SeqMeta meta, float* inv_rms,
+                          uint32_t* __restrict__ absmax, __half* __restrict__ codes) {
+  using S = RqShape<H>;
+  constexpr int NV = S::kNV, TS = S::kTS, Q4 = H / 4;
+  extern __shared__ float4 rq_smem[];
+  __shared__ uint32_t s_warpmax[kRqWarps];
+  __shared__ uint32_t s_seqmax[3];  // rank 0's slots, rotated per sequence
   const unsigned full = 0xffffffffu;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, g = lane >> 3, sub = lane & 7;
-  const int stride = H + kRowPad, q4 = H / 4;  // float4 per row (a multiple of 32)
-  float* rows = rn_smem + warp * kRnRows * stride;
-  float* myrow = rows + (g < kRnRows ? g : kRnRows - 1) * stride;  // 8-lane groups past kRnRows idle
-  const int64_t nwarps = (int64_t)gridDim.x * kRnWarps;
-  for (int64_t row0 = ((int64_t)blockIdx.x * kRnWarps + warp) * kRnRows; row0 < meta.T; row0 += nwarps * kRnRows) {
-    const int64_t row = row0 + g;
-    const bool valid = g < kRnRows && row < meta.T;
-    // o rows into shared memory, eight 16-byte loads in flight per lane
-    for (int base = 0; base < kRnRows * q4; base += 32 * kRnBatch) {
-      float4 v[kRnBatch];
+  cg::cluster_group cluster = cg::this_cluster();
+  const int crank = (int)cluster.block_rank();
+  float* rows = reinterpret_cast<float*>(rq_smem) + warp * S::kWarpFloats;
+  const float* chain = rows + (g & 1) * 8 * TS + sub * TS;  // groups 2, 3 repeat rows 0, 1
+  const bool quant = codes != nullptr;
+  if (quant) {
+    if (crank == 0 && threadIdx.x < 3) s_seqmax[threadIdx.x] = 0u;
+    cluster.sync();
+  }
+  const int nclusters = gridDim.x / kRqCluster;
+  int it = 0;
+  for (int s = blockIdx.x / kRqCluster; s < meta.B; s += nclusters, ++it) {  // uniform over the cluster
+    const int a = meta.cu_seqlens[s], len = meta.cu_seqlens[s + 1] - a;
+    const int share = (len + kRqCluster - 1) / kRqCluster;
+    const int r0 = a + min(len, crank * share), r1 = a + min(len, (crank + 1) * share);
+    float tmax = 0.0f;
+    for (int row0 = r0 + 2 * warp; row0 < r1; row0 += 2 * kRqWarps) {  // uniform per warp
+      const bool has1 = row0 + 1 < r1;
+      // lane's float4 b of the pair: row b / NV, column 4 * lane + 128 * (b % NV)
+      const int64_t lane_off = (int64_t)row0 * H + 4 * lane;
+      float* lane_col = rows + 4 * (lane & 1) * TS + (lane >> 1);
+      // o rows into shared memory (transposed)
 #pragma unroll
-      for (int b = 0; b < kRnBatch; ++b) {
-        const int idx = base + b * 32 + lane, r = idx / q4, c4 = idx % q4;
-        v[b] = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (idx < kRnRows * q4 && row0 + r < meta.T) v[b] = reinterpret_cast<const float4*>(o + (row0 + r) * H)[c4];
+      for (int b = 0; b < 2 * NV; ++b) {
+        const int rr = b / NV, cb = b % NV;
+        const float4 ov = rr == 0 || has1 ? *reinterpret_cast<const float4*>(o + lane_off + rr * H + 128 * cb)
+                                          : make_float4(0.f, 0.f, 0.f, 0.f);
+        // element 4*c4 + k (c4 = 32 cb + lane) has residue 4*(lane & 1) + k and index v = 16 cb + lane / 2
+        float* col = lane_col + rr * 8 * TS + 16 * cb;
+        col[0] = ov.x;
+        col[TS] = ov.y;
+        col[2 * TS] = ov.z;
+        col[3 * TS] = ov.w;
       }
+      // The hidden rows load while the first chains run. The compiler barrier
+      // keeps these loads after the o stores: o and hidden in registers at once
+      // would halve the CTAs per SM.
+      asm volatile("" ::: "memory");
+      float4 hv[2 * NV];
 #pragma unroll
-      for (int b = 0; b < kRnBatch; ++b) {
-        const int idx = base + b * 32 + lane, r = idx / q4, c4 = idx % q4;
-        if (idx < kRnRows * q4) *reinterpret_cast<float4*>(rows + r * stride + 4 * c4) = v[b];
+      for (int b = 0; b < 2 * NV; ++b) {
+        const int rr = b / NV, cb = b % NV;
+        hv[b] = rr == 0 || has1 ? *reinterpret_cast<const float4*>(hidden + lane_off + rr * H + 128 * cb)
+                                : make_float4(0.f, 0.f, 0.f, 0.f);
       }
-    }
-    __syncwarp();
-    float acc = 0.0f;
-#pragma unroll 8
-    for (int v = 0; v < H / 8; ++v) {
-      const float t = myrow[8 * v + sub];
-      acc = fmaf(t, t, acc);
-    }
-    const float inv1 = rms_inv_ref(group_sum8_avx_order(acc), H, eps);
-    // new hidden, written back to global memory and over o in shared memory
-    for (int base = 0; base < kRnRows * q4; base += 32 * kRnBatch) {
-      float4 hv[kRnBatch];
+      __syncwarp();
+      const float inv1 = rms_inv_ref(group_sum8_avx_order(chain_sumsq<H>(chain)), H, eps);
+      const float i1[2] = {__shfl_sync(full, inv1, 0), __shfl_sync(full, inv1, 8)};
+      __syncwarp();  // every chain has read o before the new rows replace it
 #pragma unroll
-      for (int b = 0; b < kRnBatch; ++b) {
-        const int idx = base + b * 32 + lane, r = idx / q4, c4 = idx % q4;
-        hv[b] = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (idx < kRnRows * q4 && row0 + r < meta.T) hv[b] = reinterpret_cast<const float4*>(hidden + (row0 + r) * H)[c4];
-      }
-#pragma unroll
-      for (int b = 0; b < kRnBatch; ++b) {
-        const int idx = base + b * 32 + lane, r = idx / q4, c4 = idx % q4;  // r is warp-uniform (q4 % 32 == 0)
-        if (idx >= kRnRows * q4) continue;
-        const float i1 = __shfl_sync(full, inv1, 8 * r);
-        float4 ov = *reinterpret_cast<const float4*>(rows + r * stride + 4 * c4);
+      for (int b = 0; b < 2 * NV; ++b) {
+        const int rr = b / NV, cb = b % NV;
+        float* col = lane_col + rr * 8 * TS + 16 * cb;
+        float4 ov = make_float4(col[0], col[TS], col[2 * TS], col[3 * TS]);
         if (post_w) {  // an absent post-norm leaves o as it is (model_int8.go:203, :225)
-          const float4 w = reinterpret_cast<const float4*>(post_w)[c4];
-          ov = make_float4(__fmul_rn(__fmul_rn(ov.x, i1), w.x), __fmul_rn(__fmul_rn(ov.y, i1), w.y),
-                           __fmul_rn(__fmul_rn(ov.z, i1), w.z), __fmul_rn(__fmul_rn(ov.w, i1), w.w));
+          const float4 w = *reinterpret_cast<const float4*>(post_w + 4 * lane + 128 * cb);
+          ov = make_float4(__fmul_rn(__fmul_rn(ov.x, i1[rr]), w.x), __fmul_rn(__fmul_rn(ov.y, i1[rr]), w.y),
+                           __fmul_rn(__fmul_rn(ov.z, i1[rr]), w.z), __fmul_rn(__fmul_rn(ov.w, i1[rr]), w.w));
         }
         const float4 h = hv[b];
-        ov = make_float4(__fadd_rn(ov.x, h.x), __fadd_rn(ov.y, h.y), __fadd_rn(ov.z, h.z), __fadd_rn(ov.w, h.w));
-        if (row0 + r < meta.T) reinterpret_cast<float4*>(hidden + (row0 + r) * H)[c4] = ov;
-        *reinterpret_cast<float4*>(rows + r * stride + 4 * c4) = ov;
+        const float4 nh = make_float4(__fadd_rn(ov.x, h.x), __fadd_rn(ov.y, h.y), __fadd_rn(ov.z, h.z),
+                                      __fadd_rn(ov.w, h.w));
+        if (rr == 0 || has1) *reinterpret_cast<float4*>(hidden + lane_off + rr * H + 128 * cb) = nh;
+        hv[b] = nh;
+        col[0] = nh.x;
+        col[TS] = nh.y;
+        col[2 * TS] = nh.z;
+        col[3 * TS] = nh.w;
+      }
+      __syncwarp();
+      const float inv2 = rms_inv_ref(group_sum8_avx_order(chain_sumsq<H>(chain)), H, eps);
+      if (sub == 0 && (g == 0 || (g == 1 && has1))) inv_rms[row0 + g] = inv2;
+      if (quant) {  // rows past the share are zeros: |0 * inv * w| = 0
+        const float i2[2] = {__shfl_sync(full, inv2, 0), __shfl_sync(full, inv2, 8)};
+#pragma unroll
+        for (int b = 0; b < 2 * NV; ++b) {
+          const int rr = b / NV, cb = b % NV;
+          const float4 w = *reinterpret_cast<const float4*>(next_w + 4 * lane + 128 * cb);
+          const float4 h = hv[b];
+          tmax = fmaxf(tmax, fabsf(__fmul_rn(__fmul_rn(h.x, i2[rr]), w.x)));
+          tmax = fmaxf(tmax, fabsf(__fmul_rn(__fmul_rn(h.y, i2[rr]), w.y)));
+          tmax = fmaxf(tmax, fabsf(__fmul_rn(__fmul_rn(h.z, i2[rr]), w.z)));
+          tmax = fmaxf(tmax, fabsf(__fmul_rn(__fmul_rn(h.w, i2[rr]), w.w)));
+        }
+      }
+      __syncwarp();  // the chains are done before the next pair is stored
+    }
+    if (!quant) continue;
+    // sequence absmax: warp, CTA, then cluster (rank 0's slot it % 3)
+    tmax = warp_max(tmax);
+    if (lane == 0) s_warpmax[warp] = __float_as_uint(tmax);
+    // Slot (it + 1) % 3 was last read before the barrier of the previous
+    // sequence, which rank 0 has passed; zero it for the next sequence.
+    if (crank == 0 && threadIdx.x == 0) s_seqmax[(it + 1) % 3] = 0u;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      uint32_t m = 0;
+#pragma unroll
+      for (int w = 0; w < kRqWarps; ++w) m = max(m, s_warpmax[w]);
+      atomicMax(cluster.map_shared_rank(&s_seqmax[it % 3], 0), m);
+    }
+    cluster.sync();  // release/acquire: the maxima, hidden and inv_rms of every CTA
+    const uint32_t mbits = *cluster.map_shared_rank(&s_seqmax[it % 3], 0);
+    if (crank == 0 && threadIdx.x == 0) absmax[s] = mbits;
+    float scale, qinv;
+    seq_scale_ref(mbits, &scale, &qinv);
+    // phase 2: codes = quantize((hidden * inv_rms) * next_w), a warp per row
+    for (int row = r0 + warp; row < r1; row += kRqWarps) {  // uniform per warp
+      const float r = inv_rms[row];
+      const int64_t lane_off = (int64_t)row * H + 4 * lane;
+      float4 v[NV];
+#pragma unroll
+      for (int b = 0; b < NV; ++b) v[b] = *reinterpret_cast<const float4*>(hidden + lane_off + 128 * b);
+#pragma unroll
+      for (int b = 0; b < NV; ++b) {
+        const float4 w = *reinterpret_cast<const float4*>(next_w + 4 * lane + 128 * b);
+        const float4 x = make_float4(__fmul_rn(__fmul_rn(v[b].x, r), w.x), __fmul_rn(__fmul_rn(v[b].y, r), w.y),
+                                     __fmul_rn(__fmul_rn(v[b].z, r), w.z), __fmul_rn(__fmul_rn(v[b].w, r), w.w));
+        *reinterpret_cast<uint2*>(codes + lane_off + 128 * b) = quant_codes4(x, qinv);
       }
     }
-    __syncwarp();
-    acc = 0.0f;
-#pragma unroll 8
-    for (int v = 0; v < H / 8; ++v) {
-      const float t = myrow[8 * v + sub];
-      acc = fmaf(t, t, acc);
-    }
-    const float inv2 = rms_inv_ref(group_sum8_avx_order(acc), H, eps);
-    float m = 0.0f;
-    if (absmax) {  // max is exact: four interleaved running maxima give the same result
-      float m4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-#pragma unroll 8
-      for (int v = 0; v < H / 8; ++v) {
-        const int e = 8 * v + sub;
-        m4[v & 3] = fmaxf(m4[v & 3], fabsf(__fmul_rn(__fmul_rn(myrow[e], inv2), next_w[e])));
-      }
-      m = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
-      m = group_max8(valid ? m : 0.0f);
-    }
-    if (valid && sub == 0) inv_rms[row] = inv2;
-    if (absmax) warp_seq_atomic_max(absmax, meta.row_seq, valid ? row : -1, m);
-    __syncwarp();  // the rows are reloaded next
   }
+  if (quant) cluster.sync();  // rank 0's slots stay alive until every CTA has read them
+}
+
+template <int H>
+static cudaError_t launch_rq(const float* o, const float* post_w, float* hidden, const float* next_w, float eps,
+                             SeqMeta meta, float* inv_rms, uint32_t* absmax, __half* codes, cudaStream_t stream) {
+  auto fn = residual_quant_kernel<H>;
+  const int smem = RqShape<H>::kSmem;
+  cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e != cudaSuccess) return e;
+  // one cluster per sequence: the hardware starts each as soon as a GPC has
+  // room, which also balances ragged lengths
+  fn<<<(unsigned)meta.B * kRqCluster, kRqWarps * 32, smem, stream>>>(o, post_w, hidden, next_w, eps, meta, inv_rms,
+                                                                      absmax, codes);
+  return cudaGetLastError();
 }
 
 cudaError_t launch_residual_norm(const float* o, const float* post_w, float* hidden, const float* next_w, int H,
-                                 float eps, SeqMeta meta, float* inv_rms, uint32_t* absmax, cudaStream_t stream) {
-  if (meta.T == 0) return cudaSuccess;
-  if (H % 128 != 0) return cudaErrorInvalidValue;
-  const int smem = kRnWarps * kRnRows * (H + kRowPad) * 4;
-  cudaError_t e = cudaFuncSetAttribute(residual_norm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-  if (e != cudaSuccess) return e;
-  int64_t blocks = (meta.T + kRnRows * kRnWarps - 1) / (kRnRows * kRnWarps);
-  if (blocks > 148 * 16) blocks = 148 * 16;
-  residual_norm_kernel<<<(unsigned)blocks, kRnWarps * 32, smem, stream>>>(o, post_w, hidden, next_w, H, eps, meta,
-                                                                         inv_rms, absmax);
-  return cudaGetLastError();
+                                 float eps, SeqMeta meta, float* inv_rms, uint32_t* absmax, __half* codes,
+                                 cudaStream_t stream) {
+  if (meta.T == 0 || meta.B == 0) return cudaSuccess;
+  if ((absmax == nullptr) != (codes == nullptr) || (codes && !next_w) || !meta.cu_seqlens) return cudaErrorInvalidValue;
+  switch (H) {
+    case 256: return launch_rq<256>(o, post_w, hidden, next_w, eps, meta, inv_rms, absmax, codes, stream);
+    case 512: return launch_rq<512>(o, post_w, hidden, next_w, eps, meta, inv_rms, absmax, codes, stream);
+    case 768: return launch_rq<768>(o, post_w, hidden, next_w, eps, meta, inv_rms, absmax, codes, stream);
+    default: return cudaErrorInvalidValue;
+  }
 }
 
 // ---------------------------------------------------------------------------
