@@ -220,8 +220,12 @@ __device__ __forceinline__ uint64_t sub2(uint64_t a, uint64_t b) {
   return d;
 }
 
-// fastExp of a pair (fast_exp_ref on each element, same roundings) with packed
-// fp32 arithmetic. For |x| <= 10 the exponent int32(x * log2e) lies in
+// fastExp of a pair with packed fp32 arithmetic, fast_exp_ref's operations on
+// each element. ptxas contracts a packed multiply with the add consuming it
+// into one fused multiply-add (even with .rn), so about one result in ten
+// differs from fast_exp_ref by an ulp: used only where tensor-core sums
+// already set the precision (the attention softmax), never where a result
+// must be bit-exact. For |x| <= 10 the exponent int32(x * log2e) lies in
 // [-15, 15], so only the two argument clamps remain.
 __device__ __forceinline__ uint64_t fast_exp_ref2(uint64_t x2) {
   const uint64_t y2 = mul2(x2, pack2(1.442695041f, 1.442695041f));

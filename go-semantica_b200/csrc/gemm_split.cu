@@ -17,14 +17,17 @@
 // epilogue runs once per tile: out = (acc * 2^-S_n) * inputScale
 // (quantize.go:453), the power of two being exact.
 //
-// QKV, O and down (kEpiStore): the weight rows are the MMA's M = 128 (TMEM
-// lanes), 256 tokens are N, one 256-column accumulator per tile, three 64 KB
-// stages (hi, lo, tokens). Gate/up (gemm_q8_gateup_kernel): tokens are M and
-// the gate and up rows of 128 channels together are N = 256. TMEM holds two
-// tiles' accumulators (512 columns) so the epilogue of tile i overlaps the
-// MMAs of tile i+1. One persistent CTA per SM: warps 0 and 2 issue TMA for
-// alternate stages, warp 1 the MMAs, warps 4-11 (two per TMEM lane quarter)
-// the epilogue.
+// QKV, O and down (gemm_q8_pair_kernel) run on SM pairs: clusters of two
+// CTAs whose leader issues cta_group::2 MMAs of M = 256 weight rows (128 per
+// CTA) by N = 256 tokens (128 staged per CTA), so each SM stages 48 KB per
+// 1024 MMA cycles where a single-SM tile needs 64 KB. Gate/up
+// (gemm_q8_gateup_kernel) stays on one SM: tokens are M = 128, the gate and
+// up rows of 128 channels together are N = 256, and its GELU epilogue, not
+// operand traffic, sets its pace (a pair version measured slower). Both keep
+// two tiles' accumulators in TMEM (512 columns) so the epilogue of tile i
+// overlaps the MMAs of tile i+1, with one persistent CTA per SM: warps 0 and 2
+// issue TMA for alternate stages, warp 1 (of the pair leader) the MMAs, and
+// two (store) or four (gate/up) warps per TMEM lane quarter the epilogue.
 #include <cudaTypedefs.h>
 
 #include <atomic>
@@ -39,178 +42,174 @@ namespace sem {
 
 namespace {
 
-constexpr int kXK = 64;                 // K elements per stage: 128 bytes of fp16 per row
-constexpr int kXM = 128;                // weight rows per tile (TMEM lanes)
-constexpr int kXWTile = kXM * kXK * 2;  // 16 KB: one weight plane tile of one stage
-constexpr int kXThreads = 384;
-constexpr int kXEpiWarps = 8;
+constexpr int kXK = 64;                    // K elements per stage: 128 bytes of fp16 per row
+constexpr int kXRows = 128;                // rows of each operand half per CTA (TMEM lanes)
+constexpr int kXTile = kXRows * kXK * 2;   // 16 KB: 128 rows x 128 bytes
+constexpr int kXStage = 3 * kXTile;        // 48 KB per CTA and stage: two weight planes and one token tile
+constexpr int kXStages = 4;
+constexpr int kXEpiWarps = 8;                       // two per TMEM lane quarter
+constexpr int kXThreads = 128 + 32 * kXEpiWarps;    // warps 0-3: TMA, MMA, TMA, idle
 constexpr int kXBarBytes = 256;
-
-template <int EPI>
-struct XCfg;
-template <>
-struct XCfg<kEpiStore> {
-  static constexpr int NA = 1, NT = 256, STAGES = 3;
-};
-
-template <int EPI>
-struct XLayout {
-  using C = XCfg<EPI>;
-  static constexpr int kStage = C::NA * 2 * kXWTile + C::NT * kXK * 2;  // also the TMA transaction count
-  static constexpr int kBufCols = C::NA * C::NT;                        // TMEM columns of one tile
-  static constexpr int kSmem = 1024 + C::STAGES * kStage + kXBarBytes + 2 * C::NT * 8;
-  static_assert(2 * kBufCols <= 512, "two tiles' accumulators must fit TMEM");
-  static_assert(kSmem <= 232448, "shared memory per CTA");
-  static_assert(C::NT % 32 == 0 && C::NT <= 256, "token tile: two halves of whole 16-column chunks");
-};
+constexpr int kXPairTok = 2 * kXRows;      // tokens per pair tile
+constexpr int kXSmem = 1024 + kXStages * kXStage + kXBarBytes + 2 * kXPairTok * 4;
+static_assert(kXSmem <= 232448, "shared memory per CTA");
+static_assert((2 * kXStages + 5) * 8 + 8 <= kXBarBytes, "barrier block");
+constexpr uint16_t kPairMask = 0x3;        // both CTAs of the pair
 
 __device__ uint32_t g_split_error;  // error bits of launches given no error word
 
 // GELUQuick(gate * rs) * (up * rs), the runMLPINT8 element (model_int8.go:523-530).
+// Scalar on purpose: ptxas contracts a packed (f32x2) multiply with the add
+// that consumes it into one fused multiply-add even when both carry .rn, which
+// would change fastExp's polynomial in the last bit.
 __device__ __forceinline__ float gelu_up_f(float g, float u, float rs) {
   return __fmul_rn(gelu_quick_ref(__fmul_rn(g, rs)), __fmul_rn(u, rs));
 }
 
 }  // namespace
 
-template <int EPI>
-__global__ void __launch_bounds__(kXThreads, 1)
-    gemm_q8_split_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_a, const float* __restrict__ row_scale, int n_per_a,
-                         int T, int K, const uint32_t* __restrict__ a_absmax, const int32_t* __restrict__ row_seq,
-                         float* __restrict__ c_out, uint32_t* __restrict__ out_absmax, uint32_t* __restrict__ err) {
-  using Cf = XCfg<EPI>;
-  using L = XLayout<EPI>;
-  constexpr int NA = Cf::NA, NT = Cf::NT, ST = Cf::STAGES;
+// QKV, O and down on SM pairs (clusters of two CTAs, one per SM). Per stage
+// each CTA stages 128 weight rows x 64 K of the hi and lo planes (A: rows
+// [256 mt + 128 rank, +128)) and 128 of the tile's 256 tokens (B); the
+// leader's M = 256, N = 256 MMAs read both CTAs' tiles, so each SM moves 48 KB
+// per 1024 MMA cycles instead of the 64 KB of a single-SM tile. Each CTA's
+// accumulator is its 128 output channels x the 256 tokens.
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kXThreads, 1)
+    gemm_q8_pair_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_a,
+                        const float* __restrict__ row_scale, int n_out, int T, int K,
+                        const uint32_t* __restrict__ a_absmax, const int32_t* __restrict__ row_seq,
+                        float* __restrict__ c_out, uint32_t* __restrict__ err) {
+  constexpr int ST = kXStages;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
   uint8_t* stages = smem;
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + ST * L::kStage);
-  uint64_t* empty = full + ST;
-  uint64_t* tfull = empty + ST;
-  uint64_t* tempty = tfull + 2;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + ST * kXStage);  // leader: both CTAs' bytes
+  uint64_t* empty = full + ST;                                         // each CTA: stage consumed
+  uint64_t* tfull = empty + ST;                                        // each CTA: accumulator ready
+  uint64_t* tempty = tfull + 2;                                        // leader: both epilogues done
   uint64_t* drain = tempty + 2;
   uint32_t* s_tmem = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(s_tmem + 1);
-  float* s_rs = reinterpret_cast<float*>(smem + ST * L::kStage + kXBarBytes);  // [2][NT]
-  static_assert((2 * ST + 5) * 8 + 8 <= kXBarBytes, "barrier block");
+  float* s_sc = reinterpret_cast<float*>(smem + ST * kXStage + kXBarBytes);  // [2][256] epilogue scales
   if (!err) err = &g_split_error;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int n_mt = n_per_a / kXM;
-  const int total = n_mt * ((T + NT - 1) / NT);
+  const uint32_t rank = cluster_ctarank();
+  const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
+  // output tiles: (256-token tile, 256-row weight tile); a 128-row tail leaves the peer's half empty
+  const int n_wt = (n_out + 2 * kXRows - 1) / (2 * kXRows);
+  const int total = n_wt * ((T + kXPairTok - 1) / kXPairTok);
   const int nks = K / kXK;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < ST; ++s) {
-      mbar_init(&full[s], 1);
-      mbar_init(&empty[s], 1);
+    for (int st = 0; st < ST; ++st) {
+      mbar_init(&full[st], 1);
+      mbar_init(&empty[st], 1);
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&tfull[b], 1);
-      mbar_init(&tempty[b], kXEpiWarps);
+      mbar_init(&tempty[b], 2 * kXEpiWarps);
     }
     mbar_init(drain, 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
-  if (warp == 1) tmem_alloc(s_tmem, 512);
+  if (warp == 1) tmem_alloc_pair(s_tmem, 512);
   tc_fence_before();
   __syncthreads();
+  cluster_sync_all();  // both CTAs' barriers exist before any remote arrival
   tc_fence_after();
   const uint32_t tmem = *s_tmem;
 
   if (warp == 0 || warp == 2) {
-    // ---------------- TMA producers (alternate stages) ----------------
+    // ---------------- TMA producers (alternate stages), both CTAs ----------------
     if (lane == 0) {
       const uint32_t me = warp >> 1;
+      const uint32_t lead_full = mapa_shared(smem_u32(full), 0);
       tma_prefetch_desc(&tm_w);
       tma_prefetch_desc(&tm_a);
       uint32_t it = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; ok && tile < total; tile += gridDim.x) {
-        const int tt = tile / n_mt, mt = tile % n_mt;
+      for (int tile = pair; ok && tile < total; tile += npairs) {
+        const int tt = tile / n_wt, wt = tile % n_wt;
+        const int tok = tt * kXPairTok + (int)rank * kXRows;
         for (int ks = 0; ks < nks; ++ks, ++it) {
           if ((it & 1) != me) continue;
-          const uint32_t s = it % ST, u = it / ST;
-          if (!mbar_wait(&empty[s], (u & 1) ^ 1, abort_flag, err, 1u)) {
+          const uint32_t st = it % ST, u = it / ST;
+          if (!mbar_wait(&empty[st], (u & 1) ^ 1, abort_flag, err, 1u)) {
             ok = false;
             break;
           }
-          uint8_t* st = stages + s * L::kStage;
-          mbar_arrive_expect_tx(&full[s], L::kStage);
-#pragma unroll
-          for (int a = 0; a < NA; ++a)  // hi then lo rows of the tile: one 3-D copy
-            tma_load_3d(&tm_w, &full[s], st + (2 * a) * kXWTile, ks * kXK, a * n_per_a + mt * kXM, 0);
-          tma_load_2d(&tm_a, &full[s], st + 2 * NA * kXWTile, ks * kXK, tt * NT);
+          uint8_t* sp = stages + st * kXStage;
+          const uint32_t cbar = lead_full + 8 * st;
+          if (rank == 0) mbar_arrive_expect_tx(&full[st], 2 * kXStage);
+          // [hi, lo][128 rows][128 B]: one 3-D copy, then the tokens
+          tma_load_3d_pair(&tm_w, cbar, sp, ks * kXK, (2 * wt + (int)rank) * kXRows, 0);
+          tma_load_2d_pair(&tm_a, cbar, sp + 2 * kXTile, ks * kXK, tok);
         }
       }
-      // copies in flight land before the CTA's shared memory is released;
-      // `it` is one past the last iteration this thread issued or skipped
-      for (uint32_t j = it > (uint32_t)ST ? it - ST : 0; j < it; ++j)
-        if ((j & 1) == me) mbar_wait_drain(&full[j % ST], (j / ST) & 1);
+      // The leader's full barriers count both CTAs' bytes: copies in flight
+      // land before either CTA's shared memory is released.
+      if (rank == 0)
+        for (uint32_t j = it > (uint32_t)ST ? it - ST : 0; j < it; ++j)
+          if ((j & 1) == me) mbar_wait_drain(&full[j % ST], (j / ST) & 1);
     }
   } else if (warp == 1) {
-    // ---------------- MMA issuer ----------------
-    if (lane == 0) {
-      constexpr uint32_t idesc = umma_idesc_f16_f32(kXM, NT);
+    // ---------------- MMA issuer: the leader's thread drives both SMs ----------------
+    if (lane == 0 && rank == 0) {
+      constexpr uint32_t idesc = umma_idesc_f16_f32(2 * kXRows, 2 * kXRows);
       uint32_t it = 0, tix = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; ok && tile < total; tile += gridDim.x, ++tix) {
+      for (int tile = pair; ok && tile < total; tile += npairs, ++tix) {
         const uint32_t b = tix & 1, ub = tix >> 1;
         if (!mbar_wait(&tempty[b], (ub & 1) ^ 1, abort_flag, err, 2u)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        const uint32_t d0 = tmem + b * L::kBufCols;
+        const uint32_t d0 = tmem + b * 256;
         for (int ks = 0; ks < nks; ++ks, ++it) {
-          const uint32_t s = it % ST, u = it / ST;
-          if (!mbar_wait(&full[s], u & 1, abort_flag, err, 2u)) {
+          const uint32_t st = it % ST, u = it / ST;
+          if (!mbar_wait(&full[st], u & 1, abort_flag, err, 2u)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t sw = smem_u32(stages + s * L::kStage);
-          const uint32_t sb = sw + 2 * NA * kXWTile;
+          const uint32_t sp = smem_u32(stages + st * kXStage);
 #pragma unroll
           for (int kk = 0; kk < kXK / 16; ++kk) {
-            const uint64_t bdesc = umma_desc_k_sw128(sb + kk * 32);
-#pragma unroll
-            for (int a = 0; a < NA; ++a) {
-              umma_f16(d0 + a * NT, umma_desc_k_sw128(sw + (2 * a) * kXWTile + kk * 32), bdesc, idesc,
-                       (ks | kk) ? 1u : 0u);
-              umma_f16(d0 + a * NT, umma_desc_k_sw128(sw + (2 * a + 1) * kXWTile + kk * 32), bdesc, idesc, 1u);
-            }
+            const uint64_t bdesc = umma_desc_k_sw128(sp + 2 * kXTile + kk * 32);
+            umma_f16_pair(d0, umma_desc_k_sw128(sp + kk * 32), bdesc, idesc, (ks | kk) ? 1u : 0u);
+            umma_f16_pair(d0, umma_desc_k_sw128(sp + kXTile + kk * 32), bdesc, idesc, 1u);
           }
-          umma_commit(&empty[s]);
+          umma_commit_pair_mc(&empty[st], kPairMask);
         }
         if (!ok) break;
-        umma_commit(&tfull[b]);
+        umma_commit_pair_mc(&tfull[b], kPairMask);
       }
-      umma_commit(drain);  // every MMA has finished writing TMEM before it is freed
+      umma_commit_pair_mc(drain, 0x1);  // every MMA has finished writing TMEM before it is freed
       mbar_wait_drain(drain, 0);
     }
   } else if (warp >= 4) {
-    // ---------------- epilogue ----------------
-    constexpr int TPH = NT / 2;  // tokens of a thread's half of the tile
+    // ---------------- epilogue, both CTAs: this CTA's 128 TMEM lanes ----------------
     const int e = warp - 4;
-    const int q = warp & 3;      // the TMEM lane quarter this warp may access
-    const int half = e >> 2;
+    const int q = warp & 3;    // the TMEM lane quarter this warp may access
+    const int half = e >> 2;   // half of the tile's 256 tokens
     const int etid = e * 32 + lane;
-    const int ch = q * 32 + lane;  // weight row (output channel) within the tile
     const uint32_t t_lane = tmem + ((uint32_t)(q * 32) << 16);
+    const uint32_t lead_tempty = mapa_shared(smem_u32(tempty), 0);
     bool ok = true;
     uint32_t tix = 0;
-    for (int tile = blockIdx.x; tile < total; tile += gridDim.x, ++tix) {
-      const int tt = tile / n_mt, mt = tile % n_mt;
-      const int t0 = tt * NT;
+    for (int tile = pair; tile < total; tile += npairs, ++tix) {
+      const int tt = tile / n_wt, wt = tile % n_wt;
       const int cur = tix & 1;
-      if (etid < NT) {  // per-token input scales of this tile (double-buffered across tiles)
-        const int t = t0 + etid;
+      float* sc = s_sc + cur * kXPairTok;
+      {  // the input scale of each of the tile's 256 tokens (double-buffered across tiles)
+        const int t = tt * kXPairTok + etid;
         const int sq = t < T ? (row_seq ? row_seq[t] : 0) : -1;
         float rs = 0.0f, inv;
         if (sq >= 0) seq_scale_ref(a_absmax[sq], &rs, &inv);
-        s_rs[cur * NT + etid] = rs;
+        sc[etid] = rs;
       }
       named_bar_sync(1, kXEpiWarps * 32);
       const uint32_t b = tix & 1, ub = tix >> 1;
@@ -218,45 +217,47 @@ __global__ void __launch_bounds__(kXThreads, 1)
       ok = __all_sync(0xffffffffu, ok);  // converged (and agreed) before the .sync.aligned TMEM loads
       if (!ok) continue;
       tc_fence_after();
-      const uint32_t tb = t_lane + b * L::kBufCols + half * TPH;
-      const float* c_rs = s_rs + cur * NT + half * TPH;
-      const int tok0 = t0 + half * TPH;  // first token of this thread's half
-      const int n0 = mt * kXM + ch;
-      {
-        const float rsc = row_scale[n0];
-        float* dst = c_out + (size_t)tok0 * n_per_a + n0;
+      constexpr int TPH = kXPairTok / 2;  // tokens of a thread's half of the tile
+      const int n0 = (2 * wt + (int)rank) * kXRows + q * 32 + lane;  // output channel
+      const bool live = (2 * wt + (int)rank) * kXRows < n_out;      // uniform: a 128-row tail half is empty
+      const uint32_t tb = t_lane + b * 256 + half * TPH;
+      const float* c_rs = sc + half * TPH;
+      const int tok0 = tt * kXPairTok + half * TPH;  // first token of this thread's half
+      const float rsc = live ? row_scale[n0] : 0.0f;
+      float* dst = c_out + (size_t)tok0 * n_out + n0;
 #pragma unroll 1
-        for (int c = 0; c < TPH / 16; c += 2) {
-          uint32_t r[2][16];
-          tmem_ld16(tb + c * 16, r[0]);
-          tmem_ld16(tb + c * 16 + 16, r[1]);
-          tmem_wait_ld();
-          reg_barrier16(r[0]);
-          reg_barrier16(r[1]);
-          if (c + 2 >= TPH / 16) {  // every value of this tile is in registers
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&tempty[b]);
-          }
-#pragma unroll
-          for (int cc = 0; cc < 2; ++cc)
-#pragma unroll
-            for (int i = 0; i < 16; ++i) {
-              const int x = (c + cc) * 16 + i;
-              if (tok0 + x < T)  // warp-uniform
-                dst[(size_t)x * n_per_a] = __fmul_rn(__fmul_rn(__uint_as_float(r[cc][i]), rsc), c_rs[x]);
-            }
+      for (int c = 0; c < TPH / 16; c += 2) {
+        uint32_t r[2][16];
+        tmem_ld16(tb + c * 16, r[0]);
+        tmem_ld16(tb + c * 16 + 16, r[1]);
+        tmem_wait_ld();
+        reg_barrier16(r[0]);
+        reg_barrier16(r[1]);
+        if (c + 2 >= TPH / 16) {  // every value of this tile is in registers
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive_cluster(lead_tempty + 8 * b);
         }
+        if (!live) continue;
+#pragma unroll
+        for (int cc = 0; cc < 2; ++cc)
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const int x = (c + cc) * 16 + i;
+            if (tok0 + x < T)  // warp-uniform
+              dst[(size_t)x * n_out] = __fmul_rn(__fmul_rn(__uint_as_float(r[cc][i]), rsc), c_rs[x]);
+          }
       }
     }
   }
 
   tc_fence_before();
   __syncthreads();
+  cluster_sync_all();  // the leader's MMAs have drained; no copy or arrival is still aimed at either CTA
   if (warp == 1) {
     __syncwarp();
     tc_fence_after();
-    tmem_dealloc(tmem, 512);
+    tmem_dealloc_pair(tmem, 512);
   }
 }
 
@@ -275,9 +276,11 @@ constexpr int kGuB = 2 * kGuCh * kXK * 2;       // 32 KB gate + up rows of one p
 constexpr int kGuStage = kGuA + 2 * kGuB;       // 80 KB
 constexpr int kGuStages = 2;
 constexpr int kGuSmem = 1024 + kGuStages * kGuStage + kXBarBytes + 2 * 2 * kGuCh * 4;
+constexpr int kGuEpiWarps = 16;  // four per TMEM lane quarter: the GELU epilogue costs about as much as the MMAs
+constexpr int kGuThreads = 128 + 32 * kGuEpiWarps;
 static_assert(kGuSmem <= 232448, "shared memory per CTA");
 
-__global__ void __launch_bounds__(kXThreads, 1)
+__global__ void __launch_bounds__(kGuThreads, 1)
     gemm_q8_gateup_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_a, const float* __restrict__ row_scale, int F, int T,
                           int K, const uint32_t* __restrict__ a_absmax, const int32_t* __restrict__ row_seq,
                           float* __restrict__ h_out, uint32_t* __restrict__ out_absmax, uint32_t* __restrict__ err) {
@@ -307,7 +310,7 @@ __global__ void __launch_bounds__(kXThreads, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&tfull[b], 1);
-      mbar_init(&tempty[b], kXEpiWarps);
+      mbar_init(&tempty[b], kGuEpiWarps);
     }
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -386,7 +389,7 @@ __global__ void __launch_bounds__(kXThreads, 1)
     // ---------------- epilogue ----------------
     const int e = warp - 4;
     const int q = warp & 3;     // token lane quarter
-    const int half = e >> 2;    // channels [64 half, +64) of the tile
+    const int part = e >> 2;    // channels [32 part, +32) of the tile
     const int etid = e * 32 + lane;
     const uint32_t t_lane = tmem + ((uint32_t)(q * 32) << 16);
     bool ok = true;
@@ -395,9 +398,10 @@ __global__ void __launch_bounds__(kXThreads, 1)
       const int tt = tile / n_ct, ct = tile % n_ct;
       const int cur = tix & 1;
       // the channels' row scales of this tile (double-buffered across tiles)
-      s_rsc[cur * 2 * kGuCh + etid] =
-          row_scale[(etid < kGuCh ? 0 : F - kGuCh) + ct * kGuCh + etid];  // gate rows, then up rows
-      named_bar_sync(1, kXEpiWarps * 32);
+      if (etid < 2 * kGuCh)
+        s_rsc[cur * 2 * kGuCh + etid] =
+            row_scale[(etid < kGuCh ? 0 : F - kGuCh) + ct * kGuCh + etid];  // gate rows, then up rows
+      named_bar_sync(1, kGuEpiWarps * 32);
       const uint32_t b = tix & 1, ub = tix >> 1;
       if (ok) ok = mbar_wait(&tfull[b], ub & 1, abort_flag, err, 4u);
       ok = __all_sync(0xffffffffu, ok);
@@ -408,20 +412,20 @@ __global__ void __launch_bounds__(kXThreads, 1)
       const int sq = valid ? (row_seq ? row_seq[t] : 0) : -1;
       float rs = 0.0f, inv;
       if (sq >= 0) seq_scale_ref(a_absmax[sq], &rs, &inv);
-      const float* rg = s_rsc + cur * 2 * kGuCh + half * 64;
+      const float* rg = s_rsc + cur * 2 * kGuCh + part * 32;
       const float* ru = rg + kGuCh;
-      const uint32_t tb = t_lane + b * (2 * kGuCh) + half * 64;
-      float* dst = h_out + (size_t)(valid ? t : 0) * F + ct * kGuCh + half * 64;
+      const uint32_t tb = t_lane + b * (2 * kGuCh) + part * 32;
+      float* dst = h_out + (size_t)(valid ? t : 0) * F + ct * kGuCh + part * 32;
       float run = 0.0f;
 #pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
+      for (int c = 0; c < 2; ++c) {
         uint32_t g[16], u[16];
         tmem_ld16(tb + c * 16, g);
         tmem_ld16(tb + kGuCh + c * 16, u);
         tmem_wait_ld();
         reg_barrier16(g);
         reg_barrier16(u);
-        if (c == 3) {  // every value of this tile is in registers
+        if (c == 1) {  // every value of this tile is in registers
           tc_fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive(&tempty[b]);
@@ -463,16 +467,11 @@ __global__ void __launch_bounds__(kXThreads, 1)
 namespace {
 
 int g_split_sms[64];
-bool g_split_attr[64][2];
+bool g_split_attr[64];
 std::mutex g_split_mu;
 
-template <int EPI>
-cudaError_t launch_split(const __half* a_codes, const __half* w_hi, const __half* w_lo, const float* row_scale, int T,
-                         int n_rows, int K, const uint32_t* a_absmax, const int32_t* row_seq, float* c,
-                         uint32_t* out_absmax, uint32_t* err, cudaStream_t stream) {
-  using Cf = XCfg<EPI>;
-  using L = XLayout<EPI>;
-  auto kern = gemm_q8_split_kernel<EPI>;
+cudaError_t launch_pair(const __half* a_codes, const __half* w_hi, const float* row_scale, int T, int n_out, int K,
+                        const uint32_t* a_absmax, const int32_t* row_seq, float* c, uint32_t* err, cudaStream_t stream) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
@@ -483,31 +482,31 @@ cudaError_t launch_split(const __half* a_codes, const __half* w_hi, const __half
     if (!g_split_sms[dev] &&
         (e = cudaDeviceGetAttribute(&g_split_sms[dev], cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess)
       return e;
-    const int slot = EPI == kEpiStore ? 0 : 1;
-    if (!g_split_attr[dev][slot]) {
-      if ((e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kSmem)) != cudaSuccess)
+    if (!g_split_attr[dev]) {
+      if ((e = cudaFuncSetAttribute(gemm_q8_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kXSmem)) !=
+          cudaSuccess)
         return e;
-      g_split_attr[dev][slot] = true;
+      g_split_attr[dev] = true;
     }
     sms = g_split_sms[dev];
   }
-  const int n_per_a = n_rows / Cf::NA;
   CUtensorMap tm_w, tm_a;
   {  // (K, rows, plane): the lo plane follows the hi plane
-    const uint64_t dims[3] = {(uint64_t)K, (uint64_t)n_rows, 2};
-    const uint64_t strides[2] = {(uint64_t)K * 2, (uint64_t)n_rows * K * 2};
-    const uint32_t box[3] = {kXK, kXM, 2};
-    if ((e = tmap_nd(&tm_w, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, w_hi, 3, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B)) !=
-        cudaSuccess)
+    const uint64_t dims[3] = {(uint64_t)K, (uint64_t)n_out, 2};
+    const uint64_t strides[2] = {(uint64_t)K * 2, (uint64_t)n_out * K * 2};
+    const uint32_t box[3] = {kXK, kXRows, 2};
+    if ((e = tmap_nd(&tm_w, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, w_hi, 3, dims, strides, box,
+                     CU_TENSOR_MAP_SWIZZLE_128B)) != cudaSuccess)
       return e;
   }
-  if ((e = tmap_2d(&tm_a, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, a_codes, T, K, kXK, Cf::NT,
+  if ((e = tmap_2d(&tm_a, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, a_codes, T, K, kXK, kXRows,
                    CU_TENSOR_MAP_SWIZZLE_128B)) != cudaSuccess)
     return e;
-  const int total = (n_per_a / kXM) * ((T + Cf::NT - 1) / Cf::NT);
-  const int grid = total < sms ? total : sms;
-  kern<<<grid, kXThreads, L::kSmem, stream>>>(tm_w, tm_a, row_scale, n_per_a, T, K, a_absmax, row_seq, c,
-                                              out_absmax, err);
+  const int n_wt = (n_out + 2 * kXRows - 1) / (2 * kXRows);
+  const int total = n_wt * ((T + kXPairTok - 1) / kXPairTok);
+  const int pairs = total < sms / 2 ? total : sms / 2;
+  gemm_q8_pair_kernel<<<2 * pairs, kXThreads, kXSmem, stream>>>(tm_w, tm_a, row_scale, n_out, T, K, a_absmax,
+                                                                row_seq, c, err);
   return cudaGetLastError();
 }
 
@@ -548,7 +547,7 @@ cudaError_t launch_gateup(const __half* a_codes, const __half* w_hi, const __hal
     return e;
   const int total = (F / kGuCh) * ((T + kGuTok - 1) / kGuTok);
   const int grid = total < sms ? total : sms;
-  gemm_q8_gateup_kernel<<<grid, kXThreads, kGuSmem, stream>>>(tm_w, tm_a, row_scale, F, T, K, a_absmax, row_seq,
+  gemm_q8_gateup_kernel<<<grid, kGuThreads, kGuSmem, stream>>>(tm_w, tm_a, row_scale, F, T, K, a_absmax, row_seq,
                                                               h, out_absmax, err);
   return cudaGetLastError();
 }
@@ -562,11 +561,12 @@ cudaError_t launch_gemm_q8_split(const __half* a_codes, const __half* w_hi, cons
   if (M < 0 || K <= 0 || K % kXK != 0) return cudaErrorInvalidValue;
   if (w_lo != w_hi + (size_t)N * K) return cudaErrorInvalidValue;  // one map covers both planes
   if (epilogue == kEpiGeluUp) {
-    if (N % (2 * kGuCh) != 0) return cudaErrorInvalidValue;
-    return launch_gateup(a_codes, w_hi, w_lo, row_scale, M, N / 2, K, a_absmax, row_seq, c, out_absmax, err, stream);
+    if (N % (2 * kXRows) != 0) return cudaErrorInvalidValue;
+    return launch_gateup(a_codes, w_hi, w_hi + (size_t)N * K, row_scale, M, N / 2, K, a_absmax, row_seq, c, out_absmax,
+                         err, stream);
   }
-  if (N % kXM != 0) return cudaErrorInvalidValue;
-  return launch_split<kEpiStore>(a_codes, w_hi, w_lo, row_scale, M, N, K, a_absmax, row_seq, c, nullptr, err, stream);
+  if (N % kXRows != 0) return cudaErrorInvalidValue;
+  return launch_pair(a_codes, w_hi, row_scale, M, N, K, a_absmax, row_seq, c, err, stream);
 }
 
 namespace {
@@ -594,10 +594,10 @@ cudaError_t launch_q8_proj(const __half* a_codes, const Q8Proj& w, int M, int N,
       if (!g_split_sms[dev]) cudaDeviceGetAttribute(&g_split_sms[dev], cudaDevAttrMultiProcessorCount, dev);
       if (g_split_sms[dev] > 0) sms = g_split_sms[dev];
     }
-    const bool gelu = epilogue == kEpiGeluUp;
-    const int nt = gelu ? kGuTok : XCfg<kEpiStore>::NT;
-    const int64_t tiles = (int64_t)(N / (gelu ? 2 : 1) / kXM) * ((M + nt - 1) / nt);
-    if (2 * tiles >= sms)  // measured crossover: from ~half a wave of split tiles it beats the per-block kernel
+    // 128-row x 256-token units (a pair tile is two): the measured crossover
+    // is about half a wave of them
+    const int64_t tiles = (int64_t)(N / (epilogue == kEpiGeluUp ? 2 : 1) / kXRows) * ((M + 255) / 256);
+    if (2 * tiles >= sms)
       return launch_gemm_q8_split(a_codes, w.hi, w.lo, w.row_scale, M, N, K, a_absmax, row_seq, c, epilogue,
                                   out_absmax, err, stream);
   }
