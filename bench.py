@@ -50,7 +50,8 @@ def workload_config(n_gpus: int) -> dict:
         "global_batch": BATCH * n_gpus,
         "seq_len": SEQ_LEN,
         "parallelism": f"dp{n_gpus}",
-        "l2": "inputs larger than L2: ~10 GB of activations and ~0.4 GB of weight planes stream per step",
+        "l2": "inputs larger than L2: every layer's activations (1.6 GB per fp32 hidden-size tensor) stream through "
+              "HBM, about 550 GB of element-wise traffic and 0.4 GB of weight planes per step",
     }
 
 
@@ -179,7 +180,14 @@ def stage_roofline(stage: str, total_ms: float, launches: int, T: int, n_seqs: i
         return {"kernel": stage, "bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                 "frac": achieved / peak, "peak_source": "measured bf16_tflops_sustained",
                 "algorithmic_flops_per_launch": flops, "launch_ms": per_ms}
-    bytes_per_row = {"quantize": 4 * 1152 + 1152, "residual_norm": 3 * 4 * H, "row_stats": 4 * H,
+    # per-launch averages over a forward: quantize runs once on the first
+    # attention norm and per layer on the attention output (K = H) and on the
+    # MLP product (K = F), fp32 in and fp16 codes out; the residual kernel
+    # reads o and hidden, writes hidden, and in all but the last of its 2 L
+    # launches also writes the next norm's fp16 codes
+    L = 24
+    bytes_per_row = {"quantize": 6.0 * ((L + 1) * H + L * F) / (2 * L + 1),
+                     "residual_norm": 3 * 4 * H + 2.0 * H * (2 * L - 1) / (2 * L), "row_stats": 4 * H,
                      "qk_norm_rope": 4 * (nh * hd + 2 * hd) + 2 * 2 * (nh * hd + 2 * hd), "embed": 4 * H + H,
                      "pool_l2": 4 * H}.get(stage, 4 * H)
     b = bytes_per_row * T
