@@ -505,7 +505,8 @@ cudaError_t launch_qk_norm_rope(const float* qkv, const float* q_norm, const flo
 // (QuantizeSymmetricINT8Into, quantize.go:29-69: one scale per sequence).
 // ---------------------------------------------------------------------------
 // A cluster of kRqCluster CTAs owns one sequence at a time, each CTA a
-// contiguous share of its rows.
+// contiguous share of its rows; as many clusters as fit loop over the
+// sequences.
 //  Phase 1, one warp per pair of rows: hidden = rmsnorm(o, post_w) + hidden,
 //   the next norm's inv_rms, and the CTA's max |(hidden * inv_rms) * next_w|.
 //  The CTA maxima meet in rank 0's shared memory (distributed shared memory
@@ -552,7 +553,7 @@ __global__ void __cluster_dims__(kRqCluster, 1, 1) __launch_bounds__(kRqWarps * 
                           const float* __restrict__ next_w, float eps, SeqMeta meta, float* inv_rms,
                           uint32_t* __restrict__ absmax, __half* __restrict__ codes) {
   using S = RqShape<H>;
-  constexpr int NV = S::kNV, TS = S::kTS, Q4 = H / 4;
+  constexpr int NV = S::kNV, TS = S::kTS;
   extern __shared__ float4 rq_smem[];
   __shared__ uint32_t s_warpmax[kRqWarps];
   __shared__ uint32_t s_seqmax[3];  // rank 0's slots, rotated per sequence
@@ -690,10 +691,26 @@ static cudaError_t launch_rq(const float* o, const float* post_w, float* hidden,
   const int smem = RqShape<H>::kSmem;
   cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return e;
-  // one cluster per sequence: the hardware starts each as soon as a GPC has
-  // room, which also balances ragged lengths
-  fn<<<(unsigned)meta.B * kRqCluster, kRqWarps * 32, smem, stream>>>(o, post_w, hidden, next_w, eps, meta, inv_rms,
-                                                                      absmax, codes);
+  // as many clusters as fit at once, each looping over sequences (measured
+  // ~3 % faster than one cluster per sequence); cached per device
+  static int resident_of[64];
+  int dev = 0;
+  if ((e = cudaGetDevice(&dev)) != cudaSuccess) return e;
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  int resident = __atomic_load_n(&resident_of[dev], __ATOMIC_RELAXED);
+  if (resident == 0) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(kRqCluster * 148, 1, 1);
+    cfg.blockDim = dim3(kRqWarps * 32, 1, 1);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    if ((e = cudaOccupancyMaxActiveClusters(&resident, fn, &cfg)) != cudaSuccess) return e;
+    if (resident < 1) return cudaErrorInvalidConfiguration;
+    __atomic_store_n(&resident_of[dev], resident, __ATOMIC_RELAXED);
+  }
+  const int clusters = meta.B < resident ? meta.B : resident;
+  fn<<<(unsigned)(clusters * kRqCluster), kRqWarps * 32, smem, stream>>>(o, post_w, hidden, next_w, eps, meta,
+                                                                          inv_rms, absmax, codes);
   return cudaGetLastError();
 }
 
