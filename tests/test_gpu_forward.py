@@ -107,6 +107,28 @@ def test_packed_order_matches_caller_order(gpu_model):
         np.testing.assert_allclose(batch[i], alone, atol=1e-6)
 
 
+@pytest.mark.parametrize("path", [1, 3])
+def test_batch_invariance_many_sequences(gpu_model, path):
+    # Each sequence's embedding depends on that sequence alone: inside a batch
+    # of 150 (more sequences than the residual kernel's resident clusters, so
+    # each cluster carries its absmax slots across several sequences) it is
+    # bit-identical to the same sequence embedded alone. Paths 1 (per-block
+    # projections) and 3 (split planes for every row) use one projection
+    # kernel whatever the batch, so the comparison is exact.
+    import _lib
+    lib = _lib.load()
+    prev = lib.sem_q8_path(path)
+    try:
+        lengths = [int(x) for x in synth.ragged_lengths(606, 150, 1, 300)]
+        ids, offs = synth.token_batch(607, lengths, TEST_VOCAB)
+        batch = gpu_model.forward_batch(ids, offs, 768)
+        for i in (0, 1, 37, 74, 111, 149):
+            alone = gpu_model.forward_batch(ids[offs[i]:offs[i + 1]], np.array([0, lengths[i]]), 768)[0]
+            np.testing.assert_array_equal(batch[i], alone)
+    finally:
+        lib.sem_q8_path(prev)
+
+
 def test_long_sequences_512(gpu_model, oracle_model):
     # the bench's sequence length: the north_star bound holds without widening
     ids, offs = synth.token_batch(303, [512, 512], TEST_VOCAB)
@@ -158,8 +180,10 @@ def test_q8_gemm_matches_oracle(ctx, path):
     # K = 1152 wraps the stage rings several times; N = 3072 spans 24 weight
     # tiles; the last two are large enough for the automatic choice to take
     # the split-plane kernel
+    # N = 1152 is an odd number of 128-row weight tiles: the SM-pair kernel's
+    # last tile has an empty half
     shapes = [(768, 256, 64), (1152, 768, 200), (768, 3072, 33), (768, 768, 4133), (1152, 1152, 1),
-              (768, 3072, 2000), (1152, 768, 6500)]
+              (768, 1152, 700), (768, 3072, 2000), (1152, 768, 6500)]
     try:
         _gemm_cases(ctx, rng, shapes)
     finally:
