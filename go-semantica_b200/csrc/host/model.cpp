@@ -60,6 +60,10 @@ struct sem_model {
   size_t prof_used = 0;                  // events recorded since the last read
   double prof_ms[16] = {0};
   int32_t prof_n[16] = {0};
+  // CUDA graph of the forward of the last small batch shape (sem_embed), with
+  // the buffers, projection path and stream it was captured for
+  cudaGraphExec_t fwd_graph = nullptr;
+  std::vector<const void*> fwd_graph_key;
 };
 
 
@@ -294,6 +298,7 @@ struct MetaPtrs {
   int32_t* src_row;  // [T] caller's row of each packed row (valid when permuted)
   int64_t T_long;    // packed rows [0, T_long) belong to sequences of >= kSplitMinLen tokens
   bool permuted;     // the packed order differs from the caller's
+  bool same_shape;   // the batch shape equals the previous call's (metadata not re-uploaded)
 };
 
 // Sequences at least this long take the split-plane projections (block
@@ -394,6 +399,7 @@ int upload_meta(sem_model* m, const int32_t* offsets, int B, const int32_t* dims
   mp->src_row = d_src;
   mp->T_long = m->t_long;
   mp->permuted = m->permuted;
+  mp->same_shape = same;
   return SEM_OK;
 }
 
@@ -484,6 +490,50 @@ int run_forward(sem_model* m, const int32_t* d_ids, const MetaPtrs& mp, float* d
   return SEM_OK;
 }
 
+// Batches up to this many tokens replay a CUDA graph of the forward when the
+// shape repeats: their ~240 launches would otherwise cost about as much as
+// the kernels' work.
+constexpr int64_t kGraphMaxTokens = 32768;
+
+void drop_graph(sem_model* m) {
+  if (m->fwd_graph) cudaGraphExecDestroy(m->fwd_graph);
+  m->fwd_graph = nullptr;
+  m->fwd_graph_key.clear();
+}
+
+// run_forward on the workspace ids and output, through a graph captured on
+// the first call of a small batch shape and replayed while the shape, the
+// workspace buffers, the projection path and the stream stay the same.
+int forward_maybe_graph(sem_model* m, const MetaPtrs& mp, cudaStream_t st) {
+  const int64_t T = mp.seq.T;
+  if (m->prof || T > kGraphMaxTokens) return run_forward(m, m->ids.as<int32_t>(), mp, m->out.as<float>(), st);
+  const std::vector<const void*> key = {m->hid.p,    m->big.p,   m->att.p, m->codes.p, m->halves.p,
+                                        m->inv_rms.p, m->meta.p,  m->absmax.p, m->ids.p, m->out.p,
+                                        m->errflag.p, reinterpret_cast<const void*>((intptr_t)get_q8_path()),
+                                        static_cast<const void*>(st)};
+  if (!mp.same_shape || !m->fwd_graph || key != m->fwd_graph_key) {
+    drop_graph(m);
+    SEM_CUDA(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
+    const int rc = run_forward(m, m->ids.as<int32_t>(), mp, m->out.as<float>(), st);
+    cudaGraph_t g = nullptr;
+    const cudaError_t e = cudaStreamEndCapture(st, &g);
+    if (rc) {
+      if (g) cudaGraphDestroy(g);
+      return rc;
+    }
+    if (e != cudaSuccess) return set_error(SEM_EDEVICE, "forward graph capture: %s", cudaGetErrorString(e));
+    const cudaError_t ei = cudaGraphInstantiate(&m->fwd_graph, g, 0);
+    cudaGraphDestroy(g);
+    if (ei != cudaSuccess) {
+      m->fwd_graph = nullptr;
+      return set_error(SEM_EDEVICE, "forward graph instantiate: %s", cudaGetErrorString(ei));
+    }
+    m->fwd_graph_key = key;
+  }
+  SEM_CUDA(cudaGraphLaunch(m->fwd_graph, st));
+  return SEM_OK;
+}
+
 }  // namespace
 
 int model_embed(sem_model* m, const int32_t* ids, const int32_t* offsets, int32_t B, const int32_t* dims_in,
@@ -523,7 +573,7 @@ int model_embed(sem_model* m, const int32_t* ids, const int32_t* offsets, int32_
   } else {
     SEM_CUDA(cudaMemcpyAsync(m->ids.p, ids, (size_t)T * 4, cudaMemcpyHostToDevice, ctx->stream));
   }
-  if ((rc = run_forward(m, m->ids.as<int32_t>(), mp, m->out.as<float>(), ctx->stream))) return rc;
+  if ((rc = forward_maybe_graph(m, mp, ctx->stream))) return rc;
   SEM_CUDA(cudaMemcpyAsync(out, m->out.p, (size_t)out_floats * 4, cudaMemcpyDeviceToHost, ctx->stream));
   SEM_CUDA(ctx->pinned.ensure(64));
   uint32_t* flags = ctx->pinned.as<uint32_t>();
@@ -747,6 +797,7 @@ int sem_model_free(sem_model* m) {
   sem::DeviceGuard dg(m->ctx->device);
   cudaStreamSynchronize(m->ctx->stream);
   for (cudaEvent_t e : m->prof_events) cudaEventDestroy(e);
+  if (m->fwd_graph) cudaGraphExecDestroy(m->fwd_graph);
   delete m;
   return SEM_OK;
 }

@@ -153,6 +153,23 @@ def test_deterministic(gpu_model):
         np.testing.assert_array_equal(x, y)
 
 
+def test_graph_replay_with_new_ids(gpu_model):
+    # Small batches replay a CUDA graph of the forward while their shape
+    # repeats: new ids of an already captured shape, after other shapes in
+    # between, give the vectors of a fresh capture.
+    lengths = [17, 64, 3, 40]
+    ids_x, offs = synth.token_batch(701, lengths, TEST_VOCAB)
+    ids_y, offs_y = synth.token_batch(702, lengths, TEST_VOCAB)
+    assert np.array_equal(offs, offs_y) and not np.array_equal(ids_x, ids_y)
+    fresh = gpu_model.forward_batch(ids_y, offs, 768)           # capture
+    other_ids, other_offs = synth.token_batch(703, [5, 9], TEST_VOCAB)
+    gpu_model.forward_batch(other_ids, other_offs, 768)          # another shape
+    gpu_model.forward_batch(ids_x, offs, 768)                    # capture again
+    replay = gpu_model.forward_batch(ids_y, offs, 768)           # replay with new ids
+    for a, b in zip(fresh, replay):
+        np.testing.assert_array_equal(a, b)
+
+
 def test_errors_match_reference(gpu_model):
     import _lib
     with pytest.raises(_lib.SemError, match="^empty input$"):
