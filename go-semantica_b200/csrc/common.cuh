@@ -94,15 +94,8 @@ __device__ __forceinline__ void seq_scale_ref(uint32_t absmax_bits, float* scale
 }
 
 // quantizeInto element (quantize.go:92-103): round half away from zero of the
-// exact float64 product, clamped to [-127, 127].
-__device__ __forceinline__ int quant_code_ref(float x, float inv) {
-  double r = round((double)x * (double)inv);
-  r = fmin(fmax(r, -127.0), 127.0);
-  return (int)r;
-}
-
-// The same code computed in float32 only (the float64 conversions of
-// quant_code_ref are slow on the GPU). The exact product x * inv equals
+// exact float64 product x * inv, clamped to [-127, 127], computed in float32
+// only (float64 is slow on the GPU). The exact product x * inv equals
 // p + e with p = fl(x * inv) and e = fma(x, inv, -p) (exact). With t = trunc(p),
 // p - t is exact; unless |p - t| is exactly one half, |e| (at most half an ulp
 // of p) cannot move the product across the half, and at exactly one half the
@@ -142,11 +135,6 @@ __device__ __forceinline__ uint2 quant_codes4(float4 x, float inv) {
   return *reinterpret_cast<uint2*>(h);
 }
 
-__device__ __forceinline__ void atomic_max_abs(uint32_t* slot, float v) {
-  // non-negative floats order like their bit patterns
-  atomicMax(slot, __float_as_uint(fabsf(v)));
-}
-
 __device__ __forceinline__ float warp_max(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
@@ -166,28 +154,6 @@ __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commi
 template <int N>
 __device__ __forceinline__ void cp_async_wait() {
   asm volatile("cp.async.wait_group %0;\n" ::"n"(N));
-}
-
-__device__ __forceinline__ void ldmatrix_x4(uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3,
-                                            const void* p) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];\n"
-               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
-               : "r"(smem_u32(p)));
-}
-__device__ __forceinline__ void ldmatrix_x4_trans(uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3,
-                                                  const void* p) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];\n"
-               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
-               : "r"(smem_u32(p)));
-}
-
-// D = A(16x16 f16) * B(16x8 f16) + C, fp32 accumulate.
-__device__ __forceinline__ void mma_f16(float* c, const uint32_t* a, const uint32_t* b) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-      "{%0,%1,%2,%3};\n"
-      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
-      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]));
 }
 
 // Packed fp32 pair arithmetic (sm_100+).
