@@ -644,28 +644,29 @@ def run_search(args) -> None:
     ctx = _lib.Context(local)
     stream = torch.cuda.ExternalStream(ctx.stream)
     dev = f"cuda:{local}"
-    per = SEARCH_N // world
-    row_base = rank * per
-    codes = search_codes(torch, range(row_base, row_base + per), SEARCH_D, 10_000, dev)
+    import sharded
+    row_base, row_stop = sharded.shard_rows(SEARCH_N, world, rank)
+    per = row_stop - row_base
+    codes = search_codes(torch, range(row_base, row_stop), SEARCH_D, 10_000, dev)
     qcodes = search_codes(torch, range(0, SEARCH_Q), SEARCH_D, 90_000, dev)
     torch.cuda.synchronize()
     h = C.c_void_p()
     _lib.check(lib.sem_index_create(ctx.handle, SEARCH_D, 1, C.c_void_p(codes.data_ptr()), None, per, C.byref(h)))
-    keys = torch.zeros((world, SEARCH_Q, SEARCH_K), dtype=torch.int64, device=dev)
+    keys = torch.zeros((SEARCH_Q, SEARCH_K), dtype=torch.int64, device=dev)
     rows = torch.empty((SEARCH_Q, SEARCH_K), dtype=torch.int32, device=dev)
     scores = torch.empty((SEARCH_Q, SEARCH_K), dtype=torch.int32, device=dev)
     st = C.c_void_p(ctx.stream)
 
     def scan(nq: int, qsrc):
         _lib.check(lib.sem_index_search_keys(h, C.c_void_p(qsrc.data_ptr()), nq, SEARCH_K, 1, row_base,
-                                             C.c_void_p(keys[rank].data_ptr()), st))
+                                             C.c_void_p(keys.data_ptr()), st))
 
     def step(nq: int = SEARCH_Q, qsrc=None):
+        # sharded.ShardedIndex.search_codes, with the buffers kept across steps
         scan(nq, qcodes if qsrc is None else qsrc)
-        if world > 1:
-            with torch.cuda.stream(stream):
-                dist.all_gather_into_tensor(keys.view(-1), keys[rank].contiguous().view(-1))
-        _lib.check(lib.sem_topk_merge(ctx.handle, C.c_void_p(keys.data_ptr()), world, nq, SEARCH_K, SEARCH_K, 1, 1,
+        with torch.cuda.stream(stream):
+            allk = sharded.gather_candidates(keys[:nq]).contiguous()
+        _lib.check(lib.sem_topk_merge(ctx.handle, C.c_void_p(allk.data_ptr()), world, nq, SEARCH_K, SEARCH_K, 1, 1,
                                       C.c_void_p(rows.data_ptr()), C.c_void_p(scores.data_ptr()), None, st))
 
     def barrier():

@@ -203,3 +203,24 @@ def test_tensor_core_scan_shared_bounds_with_ties(ctx, n, nq, k, distinct):
         np.testing.assert_array_equal(scores.cpu().numpy(), rscores)
         np.testing.assert_array_equal(rows.cpu().numpy(), rrows)
     idx.close()
+
+
+@pytest.mark.parametrize("row_base", [0, 2500])
+def test_sharded_index_single_rank(ctx, row_base):
+    # sharded.ShardedIndex without a process group: one shard whose rows are
+    # numbered from row_base, searched through keys + sem_topk_merge on the
+    # library's stream, against the oracle's scan of the same rows
+    import torch
+    import sharded
+    dim, n, nq, k = 256, 2500, 29, 10
+    codes = oracle.quantize_int8_vec(unit_rows(61, n, dim))
+    qc = oracle.quantize_int8_vec(unit_rows(62, nq, dim))
+    si = sharded.ShardedIndex(ctx, codes, row_base=row_base)
+    try:
+        rows, scores = si.search_codes(torch.from_numpy(qc).cuda(), k)
+        torch.cuda.synchronize()
+        want_rows, want_scores, _ = oracle.search_exact_batch(1, codes, qc, k)
+        np.testing.assert_array_equal(rows.cpu().numpy(), want_rows + row_base)
+        np.testing.assert_array_equal(scores.cpu().numpy(), want_scores)
+    finally:
+        si.close()
