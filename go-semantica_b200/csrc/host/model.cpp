@@ -64,6 +64,7 @@ struct sem_model {
   // the buffers, projection path and stream it was captured for
   cudaGraphExec_t fwd_graph = nullptr;
   std::vector<const void*> fwd_graph_key;
+  bool graphs_off = false;  // a capture failed here: forwards run without a graph
 };
 
 
@@ -506,27 +507,42 @@ void drop_graph(sem_model* m) {
 // workspace buffers, the projection path and the stream stay the same.
 int forward_maybe_graph(sem_model* m, const MetaPtrs& mp, cudaStream_t st) {
   const int64_t T = mp.seq.T;
-  if (m->prof || T > kGraphMaxTokens) return run_forward(m, m->ids.as<int32_t>(), mp, m->out.as<float>(), st);
+  auto direct = [&] { return run_forward(m, m->ids.as<int32_t>(), mp, m->out.as<float>(), st); };
+  if (m->prof || m->graphs_off || T > kGraphMaxTokens) return direct();
   const std::vector<const void*> key = {m->hid.p,    m->big.p,   m->att.p, m->codes.p, m->halves.p,
                                         m->inv_rms.p, m->meta.p,  m->absmax.p, m->ids.p, m->out.p,
                                         m->errflag.p, reinterpret_cast<const void*>((intptr_t)get_q8_path()),
                                         static_cast<const void*>(st)};
   if (!mp.same_shape || !m->fwd_graph || key != m->fwd_graph_key) {
     drop_graph(m);
-    SEM_CUDA(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
-    const int rc = run_forward(m, m->ids.as<int32_t>(), mp, m->out.as<float>(), st);
+    // A capture that the runtime refuses (the kernels were recorded, not run)
+    // turns graphs off for this model and runs the same kernels directly; an
+    // error of the forward itself is returned as it is.
+    if (cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal) != cudaSuccess) {
+      cudaGetLastError();
+      m->graphs_off = true;
+      return direct();
+    }
+    const int rc = direct();
     cudaGraph_t g = nullptr;
     const cudaError_t e = cudaStreamEndCapture(st, &g);
-    if (rc) {
+    if (e != cudaSuccess || !g) {
       if (g) cudaGraphDestroy(g);
+      cudaGetLastError();
+      m->graphs_off = true;
+      return direct();
+    }
+    if (rc) {
+      cudaGraphDestroy(g);
       return rc;
     }
-    if (e != cudaSuccess) return set_error(SEM_EDEVICE, "forward graph capture: %s", cudaGetErrorString(e));
     const cudaError_t ei = cudaGraphInstantiate(&m->fwd_graph, g, 0);
     cudaGraphDestroy(g);
     if (ei != cudaSuccess) {
       m->fwd_graph = nullptr;
-      return set_error(SEM_EDEVICE, "forward graph instantiate: %s", cudaGetErrorString(ei));
+      cudaGetLastError();
+      m->graphs_off = true;
+      return direct();
     }
     m->fwd_graph_key = key;
   }
