@@ -129,6 +129,36 @@ def test_batch_invariance_many_sequences(gpu_model, path):
         lib.sem_q8_path(prev)
 
 
+@pytest.mark.parametrize("path", [1, 3])
+def test_batch_invariance_max_length(gpu_model, path):
+    # a sequence of the model's maximum length (2048: 16 attention key tiles,
+    # 256 rows per CTA of the residual kernel's cluster) beside short ones,
+    # bit-identical to the same sequences embedded alone
+    import _lib
+    lib = _lib.load()
+    prev = lib.sem_q8_path(path)
+    try:
+        lengths = [2048, 1, 700, 129]
+        ids, offs = synth.token_batch(909, lengths, TEST_VOCAB)
+        batch = gpu_model.forward_batch(ids, offs, 768)
+        for i in range(len(lengths)):
+            alone = gpu_model.forward_batch(ids[offs[i]:offs[i + 1]], np.array([0, lengths[i]]), 768)[0]
+            np.testing.assert_array_equal(batch[i], alone)
+    finally:
+        lib.sem_q8_path(prev)
+
+
+def test_max_length_sequence_parity(gpu_model, oracle_model):
+    # the longest input the model accepts (context_length 2048), against the
+    # reference's default build; north_star's bound, strictly
+    ids, offs = synth.token_batch(808, [2048], TEST_VOCAB)
+    got = gpu_model.forward_batch(ids, offs, 768)[0]
+    ref = oracle_model.forward_with_dim(ids, 768)
+    c, a = cosine(got, ref), float(np.abs(got - ref).max())
+    print(f"2048 tokens: cosine {c:.7f} max abs {a:.2e}")
+    assert c >= COS_MIN and a <= MAX_ABS
+
+
 def test_long_sequences_512(gpu_model, oracle_model):
     # the bench's sequence length: the north_star bound holds without widening
     ids, offs = synth.token_batch(303, [512, 512], TEST_VOCAB)
