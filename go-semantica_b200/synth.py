@@ -34,8 +34,9 @@ BOS_ID = 2
 EOS_ID = 1
 FIRST_NON_SPECIAL = 4
 
-# EmbeddingGemma-300M shapes: hidden 768, 24 blocks, 3 query heads,
-# 1 KV head, head_dim 256, FFN 1152, context 2048, vocabulary 262144.
+# EmbeddingGemma-300M shapes (the config parseConfig reads, internal/runtime/
+# model.go:424-517): hidden 768, 24 blocks, 3 query heads, 1 KV head,
+# head_dim 256, FFN 1152, context 2048, vocabulary 262144.
 GEMMA_300M = dict(embed_dim=768, num_layers=24, num_heads=3, num_kv_heads=1, interm_dim=1152,
                   context_length=2048, vocab_size=262144, norm_eps=1e-6, rope_base=10000.0)
 
