@@ -89,3 +89,21 @@ def test_token_batch_layout():
     assert offs.tolist() == [0, 3, 4, 8]
     assert ids[0] == ids[3] == ids[4] == synth.BOS_ID
     assert (ids[[1, 2, 5, 6, 7]] >= synth.FIRST_NON_SPECIAL).all()
+
+
+@pytest.mark.parametrize("quant", [1, 2])
+def test_quantize_queries_matches_oracle(quant):
+    # sem_quantize_queries runs on the host (no device): quantizeInt8 /
+    # quantizeInt16 (quant.go:17-41) of normalised queries, clamped to
+    # [-1, 1], rounded half away from zero
+    import brute
+    import oracle
+    rng = np.random.default_rng(3)
+    q = rng.uniform(-1.25, 1.25, (64, 96)).astype(np.float32)
+    scale = 127.0 if quant == 1 else 32767.0
+    halves = ((np.arange(-40, 40) + 0.5) / scale).astype(np.float32)  # near-ties of v * scale
+    q[1, :80] = halves
+    q[2, :80] = np.nextafter(halves, np.float32(2))
+    q[0, :6] = [1.0, -1.0, 0.0, -0.0, 1.5, -1.5]
+    conv = oracle.quantize_int8_vec if quant == 1 else oracle.quantize_int16_vec
+    np.testing.assert_array_equal(brute.quantize_queries(q, quant), conv(q))
