@@ -49,6 +49,7 @@ _SIGNATURES = {
     "sem_embed": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int32, C.c_void_p, C.c_void_p]),
     "sem_embed_device": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int32, C.c_int32, C.c_void_p,
                                    C.c_void_p]),
+    "sem_model_check": (C.c_int, [C.c_void_p]),
     "sem_model_profile": (C.c_int, [C.c_void_p, C.c_int32]),
     "sem_model_profile_read": (C.c_int, [C.c_void_p, C.POINTER(C.c_char_p), C.POINTER(C.c_float),
                                          C.POINTER(C.c_int32), C.c_int32, C.POINTER(C.c_int32)]),

@@ -1,0 +1,294 @@
+// Q8_0 x INT8 projection on CUDA cores in the reference's VNNI lane order
+// (internal/kernels/simd_amd64.s:241-304, matmulInnerLoopVNNIAsm, and
+// quantize.go:390-458, matMulQ8_0INT8SerialRange):
+//
+//   for each 32-element block kb:   lane l (0..7) gets the exact int32 sum of
+//     the 4 products of bytes 4l..4l+3 (VPDPBUSD with the zero-point
+//     correction), converted to float32 and fused-multiply-added with the
+//     block's scale into the lane's float32 accumulator (VFMADD231PS);
+//   sum = ((l0 + l4) + (l1 + l5)) + ((l2 + l6) + (l3 + l7))   (VEXTRACTF128,
+//     VADDPS, VHADDPS, VHADDPS);
+//   dst = sum * inputScale                                     (unfused).
+//
+// Every output is therefore bit-identical to the reference's default amd64
+// build on an AVX512-VNNI host. This is the kernel for small batches and for
+// sequences shorter than 128 tokens: no tensor-core pipeline to fill, no TMEM
+// drain, and the reference's exact float32 order.
+//
+// Mapping: the 8 lane accumulators of one output live in 8 consecutive threads
+// (a "group"); the horizontal sum is three xor shuffles inside the group, in
+// the order above (float addition is commutative, so both partners of every
+// shuffle hold the same bits). A group owns a register tile of 4 tokens x 4
+// weight rows. The 4-byte partial is one dp4a whose accumulator input is the
+// bit pattern of 1.5 * 2^23, so its result read as a float is 1.5 * 2^23 +
+// partial exactly (|partial| <= 4 * 127 * 127 < 2^22) and one exact subtraction
+// gives float32(partial) without a conversion instruction.
+//
+// Data: activation codes arrive as fp16 integers (the tensor-core kernels'
+// operand type) and are packed to int8 while staged into shared memory; the
+// weights use an int8 plane whose rows are stored lane-major ([lane][block]
+// words), so a thread reads four consecutive blocks of its lane with one
+// 16-byte shared-memory load; block scales are the runtime f16 decoder's fp32
+// values (model_int8.go:543-597).
+#include <mutex>
+
+#include "common.cuh"
+#include "kernels.h"
+
+namespace sem {
+namespace {
+
+constexpr int kDpThreads = 256;  // 32 groups of 8 lane threads
+constexpr int kDpMaxLS = 36;     // padded words per (row, lane) in shared memory
+
+// Blocks per shared-memory chunk: the largest of 36, 32, ..., 4 that divides
+// the row's block count (K % 128 == 0, so 4 always does).
+__host__ __device__ inline int dp_chunk_blocks(int kb_total) {
+  for (int c = 36; c > 4; c -= 4)
+    if (kb_total % c == 0) return c;
+  return 4;
+}
+// Words between the lanes of one row: chunk / 4 sixteen-byte pieces, made odd
+// so the 8 lanes of a group read 8 different bank quads.
+__host__ __device__ inline int dp_lane_stride(int kbc) { return ((kbc / 4) & 1) ? kbc : kbc + 4; }
+
+// 8 INT8 codes held as fp16 integers in [-127, 127] -> two words of int8.
+// h + 1152 lies in [1025, 1279], where fp16 steps by 1, so the low byte of its
+// bit pattern is h + 128; xor 0x80 gives the two's complement byte of h.
+__device__ __forceinline__ uint2 codes8_to_s8(uint4 v) {
+  const __half2 mg = __halves2half2(__ushort_as_half(0x6480), __ushort_as_half(0x6480));  // 1152
+  uint32_t t[4];
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const __half2 h = __hadd2(*reinterpret_cast<const __half2*>(&w[i]), mg);
+    t[i] = *reinterpret_cast<const uint32_t*>(&h);
+  }
+  return make_uint2(__byte_perm(t[0], t[1], 0x6420) ^ 0x80808080u, __byte_perm(t[2], t[3], 0x6420) ^ 0x80808080u);
+}
+
+// One lane's block term: fma(float32(exact 4-byte partial), scale, acc).
+__device__ __forceinline__ float lane_fma(uint32_t a, uint32_t w, float s, float acc) {
+  const float x = __int_as_float(__dp4a((int)a, (int)w, kFloatMagicBits));
+  return __fmaf_rn(__fsub_rn(x, kFloatMagic), s, acc);
+}
+
+// The VNNI kernel's horizontal sum over the 8 threads of a group; every
+// thread of the group receives the same bits.
+__device__ __forceinline__ float group_hsum(float v) {
+  v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, 4));  // l + (l ^ 4)
+  v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, 1));  // (l0+l4) + (l1+l5), (l2+l6) + (l3+l7)
+  return __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, 2));
+}
+
+// GELUQuick(gate * rs) * (up * rs) (model_int8.go:523-530).
+__device__ __forceinline__ float dp_gelu_up(float g, float u, float rs) {
+  return __fmul_rn(gelu_quick_ref(__fmul_rn(g, rs)), __fmul_rn(u, rs));
+}
+
+// TGM token groups x (32 / TGM) weight-row groups per CTA: TM = 4 TGM tokens,
+// TN = 4 (32 / TGM) weight rows. kEpiGeluUp: a group's 4 rows are gate j,
+// j + 1 and up j, j + 1, so it forms two outputs h = GELUQuick(gate) * up per
+// token and the per-sequence absmax of h.
+template <int TGM, int EPI>
+__global__ void __launch_bounds__(kDpThreads, 2) gemm_q8_dp4a_kernel(
+    const __half* __restrict__ a, const uint32_t* __restrict__ wl, const float* __restrict__ ws, int M, int N, int K,
+    int kbc, const uint32_t* __restrict__ a_absmax, const int32_t* __restrict__ row_seq, float* __restrict__ c,
+    uint32_t* __restrict__ out_absmax) {
+  constexpr int TM = 4 * TGM, TN = 4 * (32 / TGM);
+  extern __shared__ __align__(16) uint32_t dp_smem[];
+  __shared__ float s_rs[TM];
+  __shared__ int s_seq[TM];
+  __shared__ uint32_t s_amax[TM];
+  const int ls = dp_lane_stride(kbc);
+  uint32_t* As = dp_smem;                                  // [TM][8][ls] activation words
+  uint32_t* Ws = As + TM * 8 * ls;                         // [TN][8][ls] weight words
+  float* Ss = reinterpret_cast<float*>(Ws + TN * 8 * ls);  // [TN][ls] block scales
+  const int tid = threadIdx.x, l = tid & 7, g = tid >> 3;
+  const int tg = g % TGM, cg = g / TGM;
+  const int KB = K / 32, KW = K / 4;  // blocks and words per row
+  const int m0 = blockIdx.y * TM;
+  const int nt = blockIdx.x;
+  const int half = N / 2;  // kEpiGeluUp: gate rows [0, half), up rows [half, N)
+  auto wrow = [&](int slot) -> int {
+    if (EPI == kEpiStore) return nt * TN + slot;
+    const int q = slot & 3;
+    const int j = nt * (TN / 2) + 2 * (slot >> 2) + (q & 1);
+    return q < 2 ? j : half + j;
+  };
+  if (tid < TM) {
+    const int m = m0 + tid;
+    int sq = -1;
+    float rs = 0.0f, inv;
+    if (m < M) {
+      sq = row_seq ? row_seq[m] : 0;
+      seq_scale_ref(a_absmax[sq], &rs, &inv);
+    }
+    s_seq[tid] = sq;
+    s_rs[tid] = rs;
+    s_amax[tid] = 0u;
+  }
+  float acc[4][4];
+#pragma unroll
+  for (int r = 0; r < 4; ++r)
+#pragma unroll
+    for (int q = 0; q < 4; ++q) acc[r][q] = 0.0f;
+
+  const int pieces = kbc / 4;  // 16-byte pieces per (row, lane) in a chunk
+  for (int kc0 = 0; kc0 < KB; kc0 += kbc) {
+    __syncthreads();  // the previous chunk is consumed
+    for (int i = tid; i < TN * 8 * pieces; i += kDpThreads) {
+      const int p = i % pieces, rest = i / pieces, ll = rest & 7, slot = rest >> 3;
+      cp_async16(Ws + (slot * 8 + ll) * ls + 4 * p, wl + (size_t)wrow(slot) * KW + ll * KB + kc0 + 4 * p, true);
+    }
+    for (int i = tid; i < TN * pieces; i += kDpThreads) {
+      const int p = i % pieces, slot = i / pieces;
+      cp_async16(Ss + slot * ls + 4 * p, ws + (size_t)wrow(slot) * KB + kc0 + 4 * p, true);
+    }
+    cp_async_commit();
+    for (int i = tid; i < TM * kbc * 4; i += kDpThreads) {
+      const int h = i & 3, kb = (i >> 2) % kbc, t = (i >> 2) / kbc;
+      const int m = m0 + t;
+      uint2 wd = make_uint2(0u, 0u);
+      if (m < M) wd = codes8_to_s8(*reinterpret_cast<const uint4*>(a + (size_t)m * K + (size_t)(kc0 + kb) * 32 + 8 * h));
+      As[(t * 8 + 2 * h) * ls + kb] = wd.x;
+      As[(t * 8 + 2 * h + 1) * ls + kb] = wd.y;
+    }
+    cp_async_wait<0>();
+    __syncthreads();
+#pragma unroll 1
+    for (int p = 0; p < pieces; ++p) {
+      uint4 av[4];
+#pragma unroll
+      for (int r = 0; r < 4; ++r) av[r] = *reinterpret_cast<const uint4*>(As + ((tg * 4 + r) * 8 + l) * ls + 4 * p);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const uint4 wv = *reinterpret_cast<const uint4*>(Ws + ((cg * 4 + q) * 8 + l) * ls + 4 * p);
+        const float4 sv = *reinterpret_cast<const float4*>(Ss + (cg * 4 + q) * ls + 4 * p);
+        // blocks 4p .. 4p + 3 of the chunk, in ascending order per accumulator
+#pragma unroll
+        for (int r = 0; r < 4; ++r) acc[r][q] = lane_fma(av[r].x, wv.x, sv.x, acc[r][q]);
+#pragma unroll
+        for (int r = 0; r < 4; ++r) acc[r][q] = lane_fma(av[r].y, wv.y, sv.y, acc[r][q]);
+#pragma unroll
+        for (int r = 0; r < 4; ++r) acc[r][q] = lane_fma(av[r].z, wv.z, sv.z, acc[r][q]);
+#pragma unroll
+        for (int r = 0; r < 4; ++r) acc[r][q] = lane_fma(av[r].w, wv.w, sv.w, acc[r][q]);
+      }
+    }
+  }
+
+  // ---- epilogue ----
+  if (EPI == kEpiStore) {
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      const int t = tg * 4 + r, m = m0 + t;
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float v = group_hsum(acc[r][q]);
+        if (((r * 4 + q) & 7) == l && m < M) c[(size_t)m * N + nt * TN + cg * 4 + q] = __fmul_rn(v, s_rs[t]);
+      }
+    }
+  } else {
+    // lane l: token r = l / 2, channel j + (l & 1)
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      const float g0 = group_hsum(acc[r][0]), g1 = group_hsum(acc[r][1]);
+      const float u0 = group_hsum(acc[r][2]), u1 = group_hsum(acc[r][3]);
+      const int t = tg * 4 + r, m = m0 + t;
+      if ((l >> 1) == r && m < M) {
+        const float h = dp_gelu_up((l & 1) ? g1 : g0, (l & 1) ? u1 : u0, s_rs[t]);
+        c[(size_t)m * half + nt * (TN / 2) + cg * 2 + (l & 1)] = h;
+        const float am = fmaxf(0.0f, fabsf(h));  // NaN folds to 0, as fmaxf does in the tensor-core epilogues
+        if (out_absmax && am > 0.0f) atomicMax(&s_amax[t], __float_as_uint(am));
+      }
+    }
+    if (out_absmax) {
+      __syncthreads();
+      if (tid < TM && s_seq[tid] >= 0 && s_amax[tid]) atomicMax(&out_absmax[s_seq[tid]], s_amax[tid]);
+    }
+  }
+}
+
+template <int TGM, int EPI>
+cudaError_t launch_dp(const __half* a, const int8_t* wl, const float* ws, int M, int N, int K, const uint32_t* a_absmax,
+                      const int32_t* row_seq, float* c, uint32_t* out_absmax, cudaStream_t stream) {
+  constexpr int TM = 4 * TGM, TN = 4 * (32 / TGM);
+  const int kbc = dp_chunk_blocks(K / 32);
+  const int ls = dp_lane_stride(kbc);
+  const size_t smem = ((size_t)(TM + TN) * 8 * ls + (size_t)TN * ls) * 4;
+  auto kern = gemm_q8_dp4a_kernel<TGM, EPI>;
+  {  // the shared-memory limit is a per-device function attribute: set once per device
+    static std::mutex mu;
+    static bool done[64] = {};
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+    std::lock_guard<std::mutex> lk(mu);
+    if (!done[dev]) {
+      const size_t max_smem = ((size_t)(TM + TN) * 8 * kDpMaxLS + (size_t)TN * kDpMaxLS) * 4;
+      if ((e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)max_smem)) != cudaSuccess)
+        return e;
+      done[dev] = true;
+    }
+  }
+  const dim3 grid((unsigned)(N / TN), (unsigned)((M + TM - 1) / TM));
+  if (grid.y > 65535u) return cudaErrorInvalidConfiguration;
+  kern<<<grid, kDpThreads, smem, stream>>>(a, reinterpret_cast<const uint32_t*>(wl), ws, M, N, K, kbc, a_absmax,
+                                           row_seq, c, out_absmax);
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+cudaError_t launch_gemm_q8_dp4a(const __half* a_codes, const int8_t* w_lanes, const float* w_scales, int M, int N,
+                                int K, const uint32_t* a_absmax, const int32_t* row_seq, float* c, int epilogue,
+                                uint32_t* out_absmax, cudaStream_t stream) {
+  if (M == 0) return cudaSuccess;
+  if (M < 0 || K <= 0 || K % 128 || N <= 0 || N % 128 || !a_codes || !w_lanes || !w_scales || !a_absmax || !c)
+    return cudaErrorInvalidValue;
+  if ((reinterpret_cast<uintptr_t>(a_codes) | reinterpret_cast<uintptr_t>(w_lanes) |
+       reinterpret_cast<uintptr_t>(w_scales)) & 15)
+    return cudaErrorMisalignedAddress;
+  // 32-token tiles halve the weight re-reads; below 17 tokens 16-row weight
+  // tiles give twice as many CTAs
+  if (epilogue == kEpiGeluUp)
+    return M <= 16 ? launch_dp<8, kEpiGeluUp>(a_codes, w_lanes, w_scales, M, N, K, a_absmax, row_seq, c, out_absmax,
+                                             stream)
+                   : launch_dp<4, kEpiGeluUp>(a_codes, w_lanes, w_scales, M, N, K, a_absmax, row_seq, c, out_absmax,
+                                             stream);
+  return M <= 16 ? launch_dp<8, kEpiStore>(a_codes, w_lanes, w_scales, M, N, K, a_absmax, row_seq, c, nullptr, stream)
+                 : launch_dp<4, kEpiStore>(a_codes, w_lanes, w_scales, M, N, K, a_absmax, row_seq, c, nullptr, stream);
+}
+
+// Q8_0 blocks of `rows` x `cols` -> the int8 plane of the CUDA-core kernel:
+// row r at dst + (dst_row_offset + r) * cols, word (lane * nb + block) holding
+// bytes 4 lane .. 4 lane + 3 of that block.
+__global__ void repack_q8_0_lanes_kernel(const uint8_t* __restrict__ raw, int64_t rows, int nb,
+                                         uint32_t* __restrict__ dst, int64_t dst_row_offset) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;  // one (row, block)
+  if (i >= rows * nb) return;
+  const int64_t r = i / nb;
+  const int b = (int)(i % nb);
+  const uint8_t* q = raw + i * 34 + 2;
+  uint32_t* row = dst + (dst_row_offset + r) * (int64_t)nb * 8;
+#pragma unroll
+  for (int l = 0; l < 8; ++l)
+    row[l * nb + b] = (uint32_t)q[4 * l] | ((uint32_t)q[4 * l + 1] << 8) | ((uint32_t)q[4 * l + 2] << 16) |
+                      ((uint32_t)q[4 * l + 3] << 24);
+}
+
+cudaError_t launch_repack_q8_0_lanes(const uint8_t* raw, int64_t rows, int cols, int8_t* dst, int64_t dst_row_offset,
+                                     cudaStream_t stream) {
+  if (rows == 0) return cudaSuccess;
+  if (cols % 32 || (reinterpret_cast<uintptr_t>(dst) & 3)) return cudaErrorInvalidValue;
+  const int nb = cols / 32;
+  const int64_t n = rows * nb;
+  repack_q8_0_lanes_kernel<<<(unsigned)((n + 255) / 256), 256, 0, stream>>>(raw, rows, nb,
+                                                                            reinterpret_cast<uint32_t*>(dst),
+                                                                            dst_row_offset);
+  return cudaGetLastError();
+}
+
+}  // namespace sem

@@ -54,7 +54,8 @@ int scratch_for_device(int device, uint8_t** out) {
 
 extern "C" int sem_q8_gemm_noalloc(sem_q8_weight* w, const float* d_a, int32_t m, float* d_c, void* stream) {
   if (!w || !d_a || !d_c) return sem::set_error(SEM_EINVAL, "null argument");
-  if (m <= 0) return sem::set_error(SEM_EINVAL, "sem_q8_gemm_noalloc: m must be positive, got %d", m);
+  if (m < 0) return sem::set_error(SEM_EINVAL, "sem_q8_gemm_noalloc: negative row count %d", m);
+  if (m == 0) return SEM_OK;  // an empty batch, as sem_q8_gemm treats it
   const size_t need = (size_t)m * (size_t)w->k_in;
   if (need > kNoAllocMaxCodes)
     return sem::set_error(SEM_EINVAL,
@@ -73,7 +74,8 @@ extern "C" int sem_q8_gemm_noalloc(sem_q8_weight* w, const float* d_a, int32_t m
   SEM_CUDA(sem::launch_absmax(d_a, (int64_t)need, absmax, st));
   sem::SeqMeta meta{nullptr, nullptr, nullptr, m, 1};
   SEM_CUDA(sem::launch_quantize(d_a, nullptr, nullptr, w->k_in, meta, absmax, codes, st));
-  SEM_CUDA(sem::launch_gemm_q8(codes, w->codes.as<__half>(), w->scales.as<float>(), m, w->n_out, w->k_in, absmax,
-                               nullptr, d_c, sem::kEpiStore, nullptr, nullptr, st));
+  // the kernel sem_q8_gemm would take for this m (sem_q8_path)
+  SEM_CUDA(sem::launch_q8_proj(codes, w->proj(), m, w->n_out, w->k_in, absmax, nullptr, d_c, sem::kEpiStore, nullptr,
+                               nullptr, st));
   return SEM_OK;
 }

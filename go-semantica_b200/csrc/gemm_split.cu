@@ -570,11 +570,12 @@ cudaError_t launch_gemm_q8_split(const __half* a_codes, const __half* w_hi, cons
 }
 
 namespace {
-std::atomic<int> g_q8_path{0};  // 0 auto, 1 per-block, 2 split (long rows), 3 split (all rows)
+// 0 auto, 1 per-block, 2 split (long rows), 3 split (all rows), 4 CUDA-core VNNI order (all rows)
+std::atomic<int> g_q8_path{0};
 }  // namespace
 
 int set_q8_path(int mode) {
-  if (mode < 0 || mode > 3) return -1;
+  if (mode < 0 || mode > 4) return -1;
   return g_q8_path.exchange(mode);
 }
 
@@ -584,6 +585,11 @@ cudaError_t launch_q8_proj(const __half* a_codes, const Q8Proj& w, int M, int N,
                            const int32_t* row_seq, float* c, int epilogue, uint32_t* out_absmax, uint32_t* err,
                            cudaStream_t stream) {
   const int path = g_q8_path.load(std::memory_order_relaxed);
+  // Below 128 rows (and everywhere under path 4) the CUDA-core kernel: the
+  // reference's VNNI float32 order exactly, and no tensor-core pipeline to
+  // fill for a handful of tiles.
+  if (w.lanes && (path == 4 || (path == 0 && M < kDp4aMaxRows)))
+    return launch_gemm_q8_dp4a(a_codes, w.lanes, w.scales, M, N, K, a_absmax, row_seq, c, epilogue, out_absmax, stream);
   if (path != 1 && w.hi && w.lo && w.row_scale && K % kXK == 0) {
     if (path >= 2)
       return launch_gemm_q8_split(a_codes, w.hi, w.lo, w.row_scale, M, N, K, a_absmax, row_seq, c, epilogue,

@@ -103,9 +103,11 @@ struct sem_q8_weight {
   int32_t k_in = 0, n_out = 0;
   sem::DevBuf codes, scales;   // fp16 codes [n_out][k_in], block scales [n_out][k_in/32]
   sem::DevBuf planes, rscale;  // split planes hi then lo [2][n_out][k_in], row scales [n_out]
+  sem::DevBuf lanes;           // int8 plane [n_out][k_in], lane-major rows (CUDA-core kernel)
   sem::Q8Proj proj() const {
     const __half* hi = static_cast<const __half*>(planes.p);
     return sem::Q8Proj{static_cast<const __half*>(codes.p), static_cast<const float*>(scales.p), hi,
-                       hi ? hi + (size_t)n_out * k_in : nullptr, static_cast<const float*>(rscale.p)};
+                       hi ? hi + (size_t)n_out * k_in : nullptr, static_cast<const float*>(rscale.p),
+                       static_cast<const int8_t*>(lanes.p)};
   }
 };

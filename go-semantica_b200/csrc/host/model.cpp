@@ -51,6 +51,7 @@ struct sem_model {
   // cached metadata of the last batch shape
   std::vector<int32_t> last_offsets, last_dims;
   int32_t n_tiles = 0;
+  int32_t n_tiles_long = 0;  // attention tiles of the long sequences (first in the tile list)
   int64_t t_long = 0;     // packed rows of the long sequences (first in the packed order)
   bool permuted = false;  // packed order differs from the caller's
   // optional per-launch timing
@@ -96,9 +97,9 @@ int upload_q8(sem_context* ctx, DevBuf& staging, const sem_tensor_view* t, int64
   return SEM_OK;
 }
 
-// Same for a projection weight, both layouts of the tensor-core GEMMs at rows
-// [row_off, row_off + rows): fp16 codes with fp32 block scales, and the split
-// fp16 planes with their row scales.
+// Same for a projection weight, every layout of the GEMMs at rows
+// [row_off, row_off + rows): fp16 codes with fp32 block scales, the split fp16
+// planes with their row scales, and the lane-major int8 plane.
 int upload_q8_proj(sem_context* ctx, DevBuf& staging, const sem_tensor_view* t, int64_t rows, int cols,
                    const Q8Proj& w, int64_t row_off) {
   uint64_t need = (uint64_t)rows * (cols / 32) * 34;
@@ -110,6 +111,8 @@ int upload_q8_proj(sem_context* ctx, DevBuf& staging, const sem_tensor_view* t, 
                                   const_cast<float*>(w.scales), row_off, ctx->stream));
   SEM_CUDA(launch_repack_q8_0_split(staging.as<uint8_t>(), rows, cols, const_cast<__half*>(w.hi),
                                     const_cast<__half*>(w.lo), const_cast<float*>(w.row_scale), row_off, ctx->stream));
+  SEM_CUDA(launch_repack_q8_0_lanes(staging.as<uint8_t>(), rows, cols, const_cast<int8_t*>(w.lanes), row_off,
+                                    ctx->stream));
   SEM_CUDA(cudaStreamSynchronize(ctx->stream));
   return SEM_OK;
 }
@@ -156,8 +159,8 @@ int model_load(sem_context* ctx, const sem_model_config* cfg_in, const sem_tenso
   };
   size_t o_emb = take((size_t)V * H), o_emb_s = take((size_t)V * (H / 32) * 4), o_onorm = take((size_t)H * 4);
   size_t o_cos = take((size_t)c.max_seq_len * (hd / 2) * 4), o_sin = take((size_t)c.max_seq_len * (hd / 2) * 4);
-  // one projection [rows][k]: codes, block scales, hi, lo, row scales
-  struct POff { size_t codes, scales, hi, lo, rsc; };
+  // one projection [rows][k]: codes, block scales, hi, lo, row scales, int8 lanes
+  struct POff { size_t codes, scales, hi, lo, rsc, lanes; };
   auto take_proj = [&](int64_t rows, int64_t k) {
     POff p;
     p.codes = take((size_t)rows * k * 2);
@@ -165,6 +168,7 @@ int model_load(sem_context* ctx, const sem_model_config* cfg_in, const sem_tenso
     p.hi = take((size_t)2 * rows * k * 2);  // hi plane, then the lo plane right after it
     p.lo = p.hi + (size_t)rows * k * 2;
     p.rsc = take((size_t)rows * 4);
+    p.lanes = take((size_t)rows * k);
     return p;
   };
   struct LOff { POff qkv, o, gu, down; size_t an, qn, kn, pa, fn, pf; };
@@ -222,7 +226,7 @@ int model_load(sem_context* ctx, const sem_model_config* cfg_in, const sem_tenso
     auto proj = [&](const POff& p) {
       return Q8Proj{reinterpret_cast<const __half*>(base + p.codes), reinterpret_cast<const float*>(base + p.scales),
                     reinterpret_cast<const __half*>(base + p.hi), reinterpret_cast<const __half*>(base + p.lo),
-                    reinterpret_cast<const float*>(base + p.rsc)};
+                    reinterpret_cast<const float*>(base + p.rsc), reinterpret_cast<const int8_t*>(base + p.lanes)};
     };
     w.qkv = proj(lo[l].qkv);
     w.o = proj(lo[l].o);
@@ -287,13 +291,19 @@ int ensure_workspace(sem_model* m, int64_t T, int B, int64_t out_floats) {
   SEM_CUDA(m->absmax.ensure((size_t)(4 * c.num_layers + 1) * (B > 0 ? B : 1) * 4));
   SEM_CUDA(m->ids.ensure((size_t)Tp * 4));
   SEM_CUDA(m->out.ensure((size_t)(out_floats > 0 ? out_floats : 1) * 4));
+  // device error words: [0] bad token id seen by the embedding kernel, [1]
+  // error bits of a timed-out pipeline wait. They accumulate over forwards
+  // until a host read (sem_embed, sem_model_check) clears them.
+  const bool new_flags = m->errflag.bytes < 16;
   SEM_CUDA(m->errflag.ensure(16));
+  if (new_flags) SEM_CUDA(cudaMemsetAsync(m->errflag.p, 0, 16, m->ctx->stream));
   return SEM_OK;
 }
 
 struct MetaPtrs {
   SeqMeta seq;
-  AttnTiles tiles;
+  AttnTiles tiles;        // 128-row attention tiles of the long sequences (tensor-core kernel)
+  AttnTiles short_tiles;  // one tile per short sequence (float32 CUDA-core kernel)
   int32_t* out_dims;
   int64_t* out_off;
   int32_t* src_row;  // [T] caller's row of each packed row (valid when permuted)
@@ -302,12 +312,14 @@ struct MetaPtrs {
   bool same_shape;   // the batch shape equals the previous call's (metadata not re-uploaded)
 };
 
-// Sequences at least this long take the split-plane projections (block
-// scales folded into the weights): their GEMM outputs differ from the
-// reference's per-block float32 sums in the last bits only, which mean
-// pooling over many tokens keeps within the reference's own spread between
-// its builds. Shorter sequences take the per-block kernel, whose sums are the
-// reference's.
+// Sequences at least this long take the tensor-core kernels: the split-plane
+// projections (block scales folded into the weights; their GEMM outputs differ
+// from the reference's per-block float32 sums in the last bits only, which
+// mean pooling over many tokens keeps within the reference's own spread
+// between its builds) and the split-fp16 tensor-core attention. Shorter
+// sequences take the CUDA-core projection and attention kernels, whose float32
+// operations are the reference's in the reference's order: their embeddings
+// are bit-identical to the reference's default build.
 constexpr int32_t kSplitMinLen = 128;
 
 // Builds the per-batch metadata on the host and uploads it (skipped when the
@@ -365,11 +377,12 @@ int upload_meta(sem_model* m, const int32_t* offsets, int B, const int32_t* dims
     int32_t* h_src = h_dims + B;
     int64_t* h_off = reinterpret_cast<int64_t*>(reinterpret_cast<uint8_t*>(h) +
                                                 (reinterpret_cast<uint8_t*>(d_off) - reinterpret_cast<uint8_t*>(base)));
-    int32_t nt = 0;
+    int32_t nt = 0, nt_long = 0;
     int32_t r = 0;
     for (int s = 0; s < B; ++s) {
       const int o = order[s];
       const int32_t len = offsets[o + 1] - offsets[o];
+      if (len >= kSplitMinLen) nt_long = nt + (len + kAttnTileRows - 1) / kAttnTileRows;
       h_cu[s] = r;
       for (int32_t i = 0; i < len; ++i) {
         h_row_seq[r + i] = s;
@@ -390,11 +403,13 @@ int upload_meta(sem_model* m, const int32_t* offsets, int B, const int32_t* dims
     m->last_offsets.assign(offsets, offsets + B + 1);
     m->last_dims.assign(dims, dims + B);
     m->n_tiles = nt;
+    m->n_tiles_long = nt_long;
     m->t_long = t_long;
     m->permuted = permuted;
   }
   mp->seq = SeqMeta{d_row_seq, d_row_pos, d_cu, (int32_t)T, (int32_t)B};
-  mp->tiles = AttnTiles{d_tseq, d_trow, m->n_tiles};
+  mp->tiles = AttnTiles{d_tseq, d_trow, m->n_tiles_long};
+  mp->short_tiles = AttnTiles{d_tseq + m->n_tiles_long, d_trow + m->n_tiles_long, m->n_tiles - m->n_tiles_long};
   mp->out_dims = d_dims;
   mp->out_off = d_off;
   mp->src_row = d_src;
@@ -406,9 +421,10 @@ int upload_meta(sem_model* m, const int32_t* offsets, int B, const int32_t* dims
 
 // Stage ids for the optional per-launch timing (sem_model_profile).
 enum Stage { kStEmbed, kStRowStats, kStQuant, kStGemmQKV, kStQKNormRope, kStAttention, kStGemmO, kStResidual,
-             kStGemmGateUp, kStGemmDown, kStPool, kStages };
+             kStGemmGateUp, kStGemmDown, kStPool, kStAttnShort, kStages };
 const char* const kStageNames[kStages] = {"embed", "row_stats", "quantize", "gemm_q8_qkv", "qk_norm_rope", "attention",
-                                          "gemm_q8_o", "residual_norm", "gemm_q8_gate_up", "gemm_q8_down", "pool_l2"};
+                                          "gemm_q8_o", "residual_norm", "gemm_q8_gate_up", "gemm_q8_down", "pool_l2",
+                                          "attention_short"};
 
 }  // namespace
 
@@ -445,22 +461,27 @@ int run_forward(sem_model* m, const int32_t* d_ids, const MetaPtrs& mp, float* d
          *vl = vh + T * hd;
   auto slot = [&](int l, int k) { return amax + (size_t)(4 * l + k) * B; };
   // Q8_0 projection of all packed rows: rows [0, t_split) (long sequences)
-  // through launch_q8_proj, the rest through the per-block kernel. out_cols:
-  // columns of one output row (N, or N / 2 for gate/up).
+  // through launch_q8_proj, the rest (short sequences) through the CUDA-core
+  // VNNI-order kernel, or the per-block tensor-core kernel under path 1.
+  // out_cols: columns of one output row (N, or N / 2 for gate/up).
   const int q8_path = get_q8_path();
-  const int64_t t_split = q8_path == 3 ? T : q8_path == 1 ? 0 : mp.T_long;
+  const int64_t t_split = q8_path == 3 || q8_path == 4 ? T : q8_path == 1 ? 0 : mp.T_long;
   auto q8 = [&](const Q8Proj& w, int N, int K, const uint32_t* a_absmax, float* out, int out_cols, int epi,
                 uint32_t* out_absmax) -> cudaError_t {
     cudaError_t e = cudaSuccess;
     if (t_split > 0)
       e = launch_q8_proj(codes, w, (int)t_split, N, K, a_absmax, sm.row_seq, out, epi, out_absmax, err, st);
-    if (e == cudaSuccess && T > t_split)
-      e = launch_gemm_q8(codes + t_split * K, w.codes, w.scales, (int)(T - t_split), N, K, a_absmax,
-                         sm.row_seq + t_split, out + t_split * out_cols, epi, out_absmax, err, st);
+    if (e == cudaSuccess && T > t_split) {
+      if (q8_path == 1)
+        e = launch_gemm_q8(codes + t_split * K, w.codes, w.scales, (int)(T - t_split), N, K, a_absmax,
+                           sm.row_seq + t_split, out + t_split * out_cols, epi, out_absmax, err, st);
+      else
+        e = launch_gemm_q8_dp4a(codes + t_split * K, w.lanes, w.scales, (int)(T - t_split), N, K, a_absmax,
+                                sm.row_seq + t_split, out + t_split * out_cols, epi, out_absmax, st);
+    }
     return e;
   };
   SEM_LAUNCH(kStEmbed, cudaMemsetAsync(amax, 0, (size_t)(4 * L + 1) * B * 4, st));
-  SEM_LAUNCH(kStEmbed, cudaMemsetAsync(m->errflag.p, 0, 8, st));
   SEM_LAUNCH(kStEmbed, launch_embed(d_ids, m->emb, m->emb_s, c.vocab_size, H, hid, (int)T, m->errflag.as<uint32_t>(), st));
   SEM_LAUNCH(kStRowStats, launch_row_stats(hid, m->layers[0].attn_norm, H, c.norm_eps, sm, inv, slot(0, 0), st));
   // the first attention norm's codes; every later norm is quantized by the
@@ -470,9 +491,14 @@ int run_forward(sem_model* m, const int32_t* d_ids, const MetaPtrs& mp, float* d
     const LayerW& w = m->layers[l];
     // attention block (model_int8.go:191-210)
     SEM_LAUNCH(kStGemmQKV, q8(w.qkv, qkvN, H, slot(l, 0), big, qkvN, kEpiStore, nullptr));
-    SEM_LAUNCH(kStQKNormRope, launch_qk_norm_rope(big, w.q_norm, w.k_norm, m->rope_cos, m->rope_sin, c.norm_eps, nh, sm, qh, ql, kh, kl,
-                                   vh, vl, st));
-    SEM_LAUNCH(kStAttention, launch_attention(qh, ql, kh, kl, vh, vl, nh, c.attention_scale, sm, mp.tiles, att, slot(l, 1), err, st));
+    SEM_LAUNCH(kStQKNormRope, launch_qk_norm_rope(big, w.q_norm, w.k_norm, m->rope_cos, m->rope_sin, c.norm_eps, nh,
+                                                  sm, qh, ql, kh, kl, vh, vl, mp.T_long, st));
+    if (mp.tiles.n_tiles)
+      SEM_LAUNCH(kStAttention, launch_attention(qh, ql, kh, kl, vh, vl, nh, c.attention_scale, sm, mp.tiles, att,
+                                                slot(l, 1), err, st));
+    if (mp.short_tiles.n_tiles)
+      SEM_LAUNCH(kStAttnShort, launch_attention_short(big, nh, c.attention_scale, sm, mp.short_tiles, att, slot(l, 1),
+                                                      st));
     SEM_LAUNCH(kStQuant, launch_quantize(att, nullptr, nullptr, H, sm, slot(l, 1), codes, st));
     SEM_LAUNCH(kStGemmO, q8(w.o, H, H, slot(l, 1), big, H, kEpiStore, nullptr));
     SEM_LAUNCH(kStResidual, launch_residual_norm(big, w.post_attn, hid, w.ffn_norm, H, c.norm_eps, sm, inv, slot(l, 2),
@@ -594,8 +620,28 @@ int model_embed(sem_model* m, const int32_t* ids, const int32_t* offsets, int32_
   SEM_CUDA(ctx->pinned.ensure(64));
   uint32_t* flags = ctx->pinned.as<uint32_t>();
   SEM_CUDA(cudaMemcpyAsync(flags, m->errflag.p, 8, cudaMemcpyDeviceToHost, ctx->stream));
+  SEM_CUDA(cudaMemsetAsync(m->errflag.p, 0, 8, ctx->stream));
   SEM_CUDA(cudaStreamSynchronize(ctx->stream));
   if (flags[1]) return set_error(SEM_EDEVICE, "forward: a tensor-core pipeline wait timed out (error bits 0x%x)", flags[1]);
+  return SEM_OK;
+}
+
+int model_check(sem_model* m) {
+  if (!m) return set_error(SEM_EINVAL, "null argument");
+  sem_context* ctx = m->ctx;
+  DeviceGuard dg(ctx->device);
+  std::lock_guard<std::mutex> lk(ctx->mu);
+  // forwards may have been enqueued on caller streams (sem_embed_device)
+  SEM_CUDA(cudaDeviceSynchronize());
+  if (!m->errflag.p) return SEM_OK;
+  SEM_CUDA(ctx->pinned.ensure(64));
+  uint32_t* flags = ctx->pinned.as<uint32_t>();
+  SEM_CUDA(cudaMemcpyAsync(flags, m->errflag.p, 8, cudaMemcpyDeviceToHost, ctx->stream));
+  SEM_CUDA(cudaMemsetAsync(m->errflag.p, 0, 8, ctx->stream));
+  SEM_CUDA(cudaStreamSynchronize(ctx->stream));
+  if (flags[1]) return set_error(SEM_EDEVICE, "forward: a tensor-core pipeline wait timed out (error bits 0x%x)", flags[1]);
+  if (flags[0])
+    return set_error(SEM_EINVAL, "token ID out of range: a device-resident id outside [0, %d)", m->cfg.vocab_size);
   return SEM_OK;
 }
 
@@ -650,6 +696,7 @@ int q8_weight_create(sem_context* ctx, const void* w_q8, int32_t k_in, int32_t n
   SEM_CUDA(w->scales.ensure((size_t)n_out * (k_in / 32) * 4));
   SEM_CUDA(w->planes.ensure((size_t)2 * k_in * n_out * 2));
   SEM_CUDA(w->rscale.ensure((size_t)n_out * 4));
+  SEM_CUDA(w->lanes.ensure((size_t)k_in * n_out));
   DevBuf staging;
   sem_tensor_view t{"weight", kQ8, 2, {(uint64_t)k_in, (uint64_t)n_out, 0, 0}, w_q8,
                     (uint64_t)n_out * (k_in / 32) * 34};
@@ -838,6 +885,8 @@ int sem_embed_device(sem_model* m, const int32_t* d_ids, const int32_t* h_offset
                      void* stream) {
   return sem::model_embed_device(m, d_ids, h_offsets, n, dim, d_out, stream);
 }
+
+int sem_model_check(sem_model* m) { return sem::model_check(m); }
 
 int sem_q8_weight_create(sem_context* ctx, const void* w_q8, int32_t k_in, int32_t n_out, sem_q8_weight** out) {
   return sem::q8_weight_create(ctx, w_q8, k_in, n_out, out);

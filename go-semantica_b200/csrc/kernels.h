@@ -65,9 +65,11 @@ cudaError_t launch_absmax(const float* x, int64_t n, uint32_t* slot, cudaStream_
 
 // Per-head RMSNorm of q (num_heads heads) and k (1 head), NeoX RoPE, and the
 // hi/lo fp16 split of q, k, v for attention. qkv rows: [q (nh*256) | k (256) | v (256)].
-cudaError_t launch_qk_norm_rope(const float* qkv, const float* q_norm, const float* k_norm, const float* rope_cos,
+// Rows >= f32_row0 also get their normed, RoPE'd q and k written back into qkv
+// as float32 (the input of launch_attention_short).
+cudaError_t launch_qk_norm_rope(float* qkv, const float* q_norm, const float* k_norm, const float* rope_cos,
                                 const float* rope_sin, float eps, int num_heads, SeqMeta meta, __half* qh,
-                                __half* ql, __half* kh, __half* kl, __half* vh, __half* vl,
+                                __half* ql, __half* kh, __half* kl, __half* vh, __half* vl, int64_t f32_row0,
                                 cudaStream_t stream);
 
 // hidden = rmsnorm(o, post_w) + hidden and inv_rms of the new rows for the
@@ -104,25 +106,44 @@ cudaError_t launch_gemm_q8_split(const __half* a_codes, const __half* w_hi, cons
                                  int M, int N, int K, const uint32_t* a_absmax, const int32_t* row_seq, float* c,
                                  int epilogue, uint32_t* out_absmax, uint32_t* err, cudaStream_t stream);
 
-// A Q8_0 projection weight [N][K] in both device layouts: fp16 codes with
-// fp32 block scales (launch_gemm_q8) and the split planes
-// (launch_gemm_q8_split).
+// The same product on CUDA cores in the reference's VNNI lane order
+// (gemm_dp4a.cu): bit-identical to matmulInnerLoopVNNIAsm + the unfused
+// inputScale multiply. w_lanes: the int8 plane [N][K] with each row stored
+// lane-major (launch_repack_q8_0_lanes); w_scales: fp32 block scales
+// [N][K/32]; K % 128 == 0, N % 128 == 0. Same epilogues and outputs as
+// launch_gemm_q8.
+cudaError_t launch_gemm_q8_dp4a(const __half* a_codes, const int8_t* w_lanes, const float* w_scales, int M, int N,
+                                int K, const uint32_t* a_absmax, const int32_t* row_seq, float* c, int epilogue,
+                                uint32_t* out_absmax, cudaStream_t stream);
+// Q8_0 blocks of `rows` x `cols` -> the lane-major int8 plane of
+// launch_gemm_q8_dp4a: row dst_row_offset + r, 32-bit word (lane * cols/32 +
+// block) = bytes 4 lane .. 4 lane + 3 of that block.
+cudaError_t launch_repack_q8_0_lanes(const uint8_t* raw, int64_t rows, int cols, int8_t* dst, int64_t dst_row_offset,
+                                     cudaStream_t stream);
+
+// A Q8_0 projection weight [N][K] in its device layouts: fp16 codes with fp32
+// block scales (launch_gemm_q8), the split planes (launch_gemm_q8_split) and
+// the lane-major int8 plane (launch_gemm_q8_dp4a, with the same block scales).
 struct Q8Proj {
   const __half* codes;     // [N][K]
   const float* scales;     // [N][K/32]
   const __half* hi;        // [N][K]
   const __half* lo;        // [N][K]
   const float* row_scale;  // [N]
+  const int8_t* lanes;     // [N][K], lane-major rows
 };
-// Picks the kernel for M tokens: the split-plane GEMM once its tiles fill
-// half the SMs (measured crossover), else the per-block kernel (narrower
-// token tiles, half the weight bytes).
+// Picks the kernel for M tokens: the CUDA-core VNNI-order kernel below
+// kDp4aMaxRows rows, the split-plane GEMM once its tiles fill half the SMs
+// (measured crossover), else the per-block kernel (narrower token tiles, half
+// the weight bytes). sem_q8_path overrides the choice.
+constexpr int kDp4aMaxRows = 128;
 cudaError_t launch_q8_proj(const __half* a_codes, const Q8Proj& w, int M, int N, int K, const uint32_t* a_absmax,
                            const int32_t* row_seq, float* c, int epilogue, uint32_t* out_absmax, uint32_t* err,
                            cudaStream_t stream);
 // Process-wide kernel choice: 0 auto, 1 per-block, 2 split-plane (launch_q8_proj
 // always; the forward's long-sequence rows), 3 split-plane for every forward
-// row; returns the previous one (-1: unknown mode, nothing changed).
+// row, 4 the CUDA-core VNNI-order kernel for every row; returns the previous
+// one (-1: unknown mode, nothing changed).
 int set_q8_path(int mode);
 int get_q8_path();
 
@@ -140,6 +161,14 @@ struct AttnTiles {
 cudaError_t launch_attention(const __half* qh, const __half* ql, const __half* kh, const __half* kl,
                              const __half* vh, const __half* vl, int num_heads, float scale, SeqMeta meta,
                              AttnTiles tiles, float* out, uint32_t* absmax, uint32_t* err, cudaStream_t stream);
+
+// Float32 attention of sequences shorter than 128 tokens in the reference's
+// order (attention_short.cu): qkv rows [q (nh*256) | k | v] float32 with q and
+// k normed and RoPE'd (launch_qk_norm_rope with f32_row0 at or below their
+// rows); `tiles` lists one 128-row tile per such sequence. out [T][nh*256],
+// absmax[seq] atomically, as launch_attention.
+cudaError_t launch_attention_short(const float* qkv, int num_heads, float scale, SeqMeta meta, AttnTiles tiles,
+                                   float* out, uint32_t* absmax, cudaStream_t stream);
 
 // ---- brute search (brute_kernels.cu) ----
 // Exact integer scan: scores of nq queries against rows [0, count) of an

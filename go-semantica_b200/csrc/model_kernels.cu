@@ -397,11 +397,12 @@ constexpr int kHeadPad = kHeadDim + 8;  // head stride in shared memory: 4 heads
 constexpr int kQkWarps = 8;
 
 __global__ void __launch_bounds__(kQkWarps * 32)
-    qk_norm_rope_kernel(const float* __restrict__ qkv, const float* __restrict__ q_norm,
+    qk_norm_rope_kernel(float* __restrict__ qkv, const float* __restrict__ q_norm,
                         const float* __restrict__ k_norm, const float* __restrict__ rope_cos,
                         const float* __restrict__ rope_sin, float eps, int nh, SeqMeta meta,
                         __half* __restrict__ qh, __half* __restrict__ ql, __half* __restrict__ kh,
-                        __half* __restrict__ kl, __half* __restrict__ vh, __half* __restrict__ vl) {
+                        __half* __restrict__ kl, __half* __restrict__ vh, __half* __restrict__ vl,
+                        int64_t f32_row0) {
   __shared__ __align__(16) float sh[kQkWarps][4 * kHeadPad];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, g = lane >> 3, sub = lane & 7;
   const int64_t nwarps = (int64_t)gridDim.x * kQkWarps;
@@ -410,7 +411,7 @@ __global__ void __launch_bounds__(kQkWarps * 32)
   const bool active = g <= nh;
   const float* wn = g < nh ? q_norm : k_norm;
   for (int64_t row = (int64_t)blockIdx.x * kQkWarps + warp; row < meta.T; row += nwarps) {  // uniform per warp
-    const float* base = qkv + row * ld;
+    float* base = qkv + row * ld;
     // q heads and the k head into shared memory (64 float4 per head)
     for (int idx = lane; idx < (nh + 1) * 64; idx += 32) {
       const int hd = idx >> 6, c4 = idx & 63;
@@ -446,6 +447,7 @@ __global__ void __launch_bounds__(kQkWarps * 32)
           *reinterpret_cast<float4*>(w1) = reinterpret_cast<const float4*>(wn + i + 128)[0];
         }
         __half2 h0[2], l0[2], h1[2], l1[2];
+        float f0[4], f1[4];  // the float32 results, kept for rows of short sequences
 #pragma unroll
         for (int u = 0; u < 4; u += 2) {
           float r0[2], r1[2];
@@ -456,6 +458,8 @@ __global__ void __launch_bounds__(kQkWarps * 32)
             const float x1 = wn ? __fmul_rn(__fmul_rn(a1[u + z], inv), w1[u + z]) : a1[u + z];
             r0[z] = __fsub_rn(__fmul_rn(x0, c[u + z]), __fmul_rn(x1, s[u + z]));
             r1[z] = __fadd_rn(__fmul_rn(x0, s[u + z]), __fmul_rn(x1, c[u + z]));
+            f0[u + z] = r0[z];
+            f1[u + z] = r1[z];
           }
           __half a, b, e2, f;
           split_half(r0[0], a, b);
@@ -471,6 +475,11 @@ __global__ void __launch_bounds__(kQkWarps * 32)
         *reinterpret_cast<uint2*>(dl + i) = *reinterpret_cast<uint2*>(l0);
         *reinterpret_cast<uint2*>(dh + i + 128) = *reinterpret_cast<uint2*>(h1);
         *reinterpret_cast<uint2*>(dl + i + 128) = *reinterpret_cast<uint2*>(l1);
+        if (row >= f32_row0) {  // the float32 attention of short sequences reads these back in place
+          float* dst = base + g * kHeadDim;  // q head g, or the k head right after the q heads
+          *reinterpret_cast<float4*>(dst + i) = *reinterpret_cast<const float4*>(f0);
+          *reinterpret_cast<float4*>(dst + i + 128) = *reinterpret_cast<const float4*>(f1);
+        }
       }
     }
     // v: all 32 lanes, 8 consecutive elements each
@@ -487,15 +496,16 @@ __global__ void __launch_bounds__(kQkWarps * 32)
   }
 }
 
-cudaError_t launch_qk_norm_rope(const float* qkv, const float* q_norm, const float* k_norm, const float* rope_cos,
+cudaError_t launch_qk_norm_rope(float* qkv, const float* q_norm, const float* k_norm, const float* rope_cos,
                                 const float* rope_sin, float eps, int num_heads, SeqMeta meta, __half* qh,
-                                __half* ql, __half* kh, __half* kl, __half* vh, __half* vl, cudaStream_t stream) {
+                                __half* ql, __half* kh, __half* kl, __half* vh, __half* vl, int64_t f32_row0,
+                                cudaStream_t stream) {
   if (meta.T == 0) return cudaSuccess;
   if (num_heads < 1 || num_heads > 3) return cudaErrorInvalidValue;
   int64_t blocks = (meta.T + kQkWarps - 1) / kQkWarps;
   if (blocks > 148 * 8) blocks = 148 * 8;
   qk_norm_rope_kernel<<<(unsigned)blocks, kQkWarps * 32, 0, stream>>>(qkv, q_norm, k_norm, rope_cos, rope_sin, eps, num_heads,
-                                                            meta, qh, ql, kh, kl, vh, vl);
+                                                            meta, qh, ql, kh, kl, vh, vl, f32_row0);
   return cudaGetLastError();
 }
 

@@ -84,6 +84,12 @@ class Model:
         check(load().sem_embed_device(self.handle, C.c_void_p(d_ids_ptr), offsets.ctypes.data, n_seqs, dim,
                                       C.c_void_p(d_out_ptr), C.c_void_p(stream or None)))
 
+    def check(self) -> None:
+        """Waits for the enqueued device-resident forwards and raises what the
+        device recorded (a token id outside the vocabulary, a timed-out
+        pipeline wait) since the last check (sem_model_check)."""
+        check(load().sem_model_check(self.handle))
+
 
 def load_model(path: str, ctx: Context | None = None) -> Model:
     """LoadModel (model.go:233-246): GGUF file -> device-resident model."""

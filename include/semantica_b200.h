@@ -107,9 +107,20 @@ int sem_embed(sem_model *model, const int32_t *ids, const int32_t *offsets, int3
 
 /* Device-resident variant (no host copies): d_ids on the device, h_offsets on
  * the host, d_out on the device (n_seqs x dim). Enqueued on `stream` (NULL =
- * the context stream); returns without synchronising. */
+ * the context stream); returns without synchronising, so errors the device
+ * detects (a token id outside the vocabulary, a timed-out pipeline wait)
+ * surface through sem_model_check. */
 int sem_embed_device(sem_model *model, const int32_t *d_ids, const int32_t *h_offsets, int32_t n_seqs, int32_t dim,
                      float *d_out, void *stream);
+
+/* Waits for the model's device to finish every forward enqueued so far and
+ * reports what the device recorded since the last check (or sem_embed call):
+ * SEM_EINVAL "token ID out of range: ..." for a device-resident id outside the
+ * vocabulary (its embedding row was written as zeros), SEM_EDEVICE when a
+ * tensor-core pipeline wait timed out (that kernel returned early and its
+ * output is incomplete). Clears the record. No reference counterpart: the
+ * reference validates ids on the host (model_int8.go:167-178). */
+int sem_model_check(sem_model *model);
 
 /* Per-stage device timing of the forward pass (diagnostics; no reference
  * counterpart). enable != 0 brackets every kernel launch of later forwards
@@ -144,28 +155,40 @@ int sem_q8_gemm(sem_q8_weight *w, const float *d_a, int32_t m, float *d_c, void 
 int sem_q8_matmul_int8(sem_q8_weight *w, const void *d_codes, const uint32_t *d_absmax, int32_t m, float *d_c,
                        void *stream);
 
-/* Which tensor-core kernel the Q8_0 projections use (process-wide, every
- * model and weight). Two kernels exist: the per-block kernel sums each
- * 32-element block exactly and scales it in float32 as the reference does;
- * the split-plane kernel folds the block scales into two fp16 weight planes
- * (one TMEM drain per tile, ~1.5x faster) and differs from the reference's
- * sums in the last float32 bits. sem_embed packs sequences of >= 128 tokens
- * first; only their rows may take the split-plane kernel (mean pooling over
- * many tokens keeps the difference within the reference's own spread between
- * its builds), shorter sequences always take the per-block kernel.
- *   SEM_Q8_PATH_AUTO (default): long-sequence rows (all rows for
- *     sem_q8_gemm) take the split-plane kernel when its 128 x 256-token tiles
- *     fill at least half the SMs, else the per-block kernel;
+/* Which kernel the Q8_0 projections use (process-wide, every model and
+ * weight). Three kernels exist:
+ *   - the CUDA-core kernel computes the reference's VNNI inner loop exactly
+ *     (simd_amd64.s:241-304: 8 float32 lane accumulators, each a fused
+ *     multiply-add of an exact 4-product int32 partial and the block scale,
+ *     then the reference's horizontal sum and the unfused inputScale
+ *     multiply): bit-identical to the reference's default amd64 build;
+ *   - the per-block tensor-core kernel sums each 32-element block exactly and
+ *     scales it in float32, accumulating the blocks in another order;
+ *   - the split-plane tensor-core kernel folds the block scales into two fp16
+ *     weight planes (one TMEM drain per tile, the fastest at scale) and differs
+ *     from the reference's sums in the last float32 bits.
+ * sem_embed packs sequences of >= 128 tokens first. Shorter sequences take the
+ * CUDA-core kernel (and a float32 attention in the reference's order), so
+ * their embeddings are bit-identical to the reference's; long-sequence rows
+ * take a tensor-core kernel (mean pooling over many tokens keeps the
+ * difference within the reference's own spread between its builds).
+ *   SEM_Q8_PATH_AUTO (default): long-sequence rows take the split-plane kernel
+ *     when its 128 x 256-token tiles fill at least half the SMs, else the
+ *     per-block kernel; sem_q8_gemm / sem_q8_matmul_int8 take the CUDA-core
+ *     kernel below 128 rows, then the same rule;
  *   SEM_Q8_PATH_BLOCK: the per-block kernel everywhere;
  *   SEM_Q8_PATH_SPLIT: the split-plane kernel for long-sequence rows (all
  *     rows for sem_q8_gemm) whatever their count;
- *   SEM_Q8_PATH_SPLIT_ALL: the split-plane kernel for every row (testing).
+ *   SEM_Q8_PATH_SPLIT_ALL: the split-plane kernel for every row (testing);
+ *   SEM_Q8_PATH_EXACT: the CUDA-core kernel for every row (bit-exact
+ *     projections at any length, slower than the tensor cores at scale).
  * A tuning and testing switch with no counterpart in the reference. Returns
  * the previous setting, or -1 for an unknown mode. */
 #define SEM_Q8_PATH_AUTO 0
 #define SEM_Q8_PATH_BLOCK 1
 #define SEM_Q8_PATH_SPLIT 2
 #define SEM_Q8_PATH_SPLIT_ALL 3
+#define SEM_Q8_PATH_EXACT 4
 int sem_q8_path(int32_t mode);
 
 /* sem_q8_gemm without caller scratch, for callers that cannot allocate device
@@ -175,12 +198,16 @@ int sem_q8_path(int32_t mode);
  * reference. The codes and the absmax word live in a static device array of
  * 16 MiB + 256 bytes that every GPU loading the library holds until exit, so
  * m * k_in must not exceed 8 Mi (8,388,608) elements (larger calls fail with
- * SEM_EINVAL); the call
- * performs no allocation. The first call on a device resolves the array's
- * address on that device (cudaGetSymbolAddress); make that first call before
- * any stream capture. All calls share the one array: calls that overlap on
- * the GPU (other streams, other threads) race on it. Enqueued on `stream`
- * (NULL = the weight's context stream). */
+ * SEM_EINVAL); m == 0 is a no-op, as for sem_q8_gemm. The kernel choice is
+ * sem_q8_gemm's (sem_q8_path). The call performs no allocation. The first
+ * call on a device resolves the array's address on that device
+ * (cudaGetSymbolAddress), which loads the library's device code there and may
+ * synchronise the device; the array's 16 MiB are committed then, not when the
+ * library is loaded. Make that first call (a warm-up call will do) at start-up,
+ * before the host runtime reserves its device pool and before any stream
+ * capture. All calls share the one array: calls that overlap on the GPU (other
+ * streams, other threads) race on it. Enqueued on `stream` (NULL = the
+ * weight's context stream). */
 int sem_q8_gemm_noalloc(sem_q8_weight *w, const float *d_a, int32_t m, float *d_c, void *stream);
 
 /* ------------------------------------------------------------------------

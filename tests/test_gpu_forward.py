@@ -52,9 +52,33 @@ def check_parity(gpu_model, oracle_model, ids, offs, dims, label, strict=False):
 
 
 def test_config1_batch_8x64(gpu_model, oracle_model):
-    # 8 sequences x 64 tokens (BOS + uniform non-special ids), 768-dim output
+    # 8 sequences x 64 tokens (BOS + uniform non-special ids),
+    # 768-dim output; north_star's bound strictly, and in fact bit equality:
+    # sequences shorter than 128 tokens run kernels whose float32 operations
+    # are the reference's default build's, in its order
     ids, offs = synth.token_batch(101, [64] * 8, TEST_VOCAB)
-    check_parity(gpu_model, oracle_model, ids, offs, [768] * 8, "8x64")
+    check_parity(gpu_model, oracle_model, ids, offs, [768] * 8, "8x64", strict=True)
+    got = gpu_model.forward_batch(ids, offs, 768)
+    for i in range(8):
+        np.testing.assert_array_equal(got[i], oracle_model.forward_with_dim(ids[offs[i]:offs[i + 1]], 768))
+
+
+def test_short_sequences_bit_exact(gpu_model, oracle_model):
+    # Every sequence shorter than 128 tokens: the CUDA-core projections
+    # (dp4a partials in the VNNI lane order, 8 float32 lane accumulators, the
+    # reference's horizontal sum) and the float32 attention (AVX2-order score
+    # dots, fastExp softmax with its 4-way sum, unfused p*v accumulation) give
+    # the reference default build's embedding bit for bit, at every Matryoshka
+    # tier, inside a batch that also holds long sequences.
+    lengths = [1, 2, 3, 7, 16, 17, 31, 32, 33, 64, 65, 100, 127, 200]
+    dims = [768, 512, 256, 128, 768, 512, 256, 128, 768, 512, 256, 128, 768, 768]
+    ids, offs = synth.token_batch(212, lengths, TEST_VOCAB)
+    got = gpu_model.forward_batch(ids, offs, dims)
+    for i, n in enumerate(lengths):
+        if n >= 128:
+            continue
+        ref = oracle_model.forward_with_dim(ids[offs[i]:offs[i + 1]], dims[i])
+        np.testing.assert_array_equal(got[i], ref, err_msg=f"length {n}")
 
 
 def test_ragged_lengths_and_matryoshka_dims(gpu_model, oracle_model):
@@ -258,6 +282,105 @@ def _gemm_cases(ctx, rng, shapes):
         got = d_c.cpu().numpy()
         np.testing.assert_allclose(got, ref, rtol=2e-5, atol=2e-5 * np.abs(ref).max())
         w.close()
+
+
+@pytest.mark.parametrize("K,N", [(768, 768), (768, 256), (768, 1152), (1152, 768), (768, 3072), (3072, 768)])
+def test_q8_gemm_small_m_bit_exact(ctx, K, N):
+    # Below 128 rows the projection takes the CUDA-core kernel, which computes
+    # the reference's VNNI inner loop exactly (simd_amd64.s:241-304 and the
+    # unfused inputScale multiply, quantize.go:453): bit equality with the
+    # oracle's default-build restatement on every BASELINE config-2 shape
+    import torch
+    import oracle
+    import runtime
+    rng = np.random.default_rng(K * 7 + N)
+    raw = synth.q8_0_blocks(rng, N, K)
+    w = runtime.Q8Weight(ctx, raw, K, N)
+    for M in (1, 64, 127):
+        a = rng.standard_normal((M, K)).astype(np.float32)
+        d_a = torch.from_numpy(a).cuda()
+        d_c = torch.empty((M, N), dtype=torch.float32, device="cuda")
+        d_codes = torch.empty((M, K), dtype=torch.float16, device="cuda")
+        d_abs = torch.zeros(4, dtype=torch.int32, device="cuda")
+        torch.cuda.synchronize()
+        w.run(d_a.data_ptr(), M, d_c.data_ptr(), d_codes.data_ptr(), d_abs.data_ptr(), ctx.stream)
+        torch.cuda.synchronize()
+        codes, scale = oracle.quantize_sym_int8(a)
+        np.testing.assert_array_equal(d_c.cpu().numpy(), oracle.matmul_q8_0_int8(raw, codes, scale, N),
+                                      err_msg=f"{K}x{N} M={M}")
+    w.close()
+
+
+def test_q8_gemm_exact_path_large_m(ctx):
+    # SEM_Q8_PATH_EXACT puts every row on the CUDA-core kernel: bit-exact at any
+    # size, K = 3072 included (several shared-memory chunks per row)
+    import torch
+    import oracle
+    import runtime
+    import _lib
+    lib = _lib.load()
+    prev = lib.sem_q8_path(4)
+    rng = np.random.default_rng(44)
+    try:
+        for K, N, M in ((768, 1152, 700), (3072, 768, 300), (1152, 768, 1025)):
+            raw = synth.q8_0_blocks(rng, N, K)
+            w = runtime.Q8Weight(ctx, raw, K, N)
+            a = rng.standard_normal((M, K)).astype(np.float32)
+            d_a = torch.from_numpy(a).cuda()
+            d_c = torch.empty((M, N), dtype=torch.float32, device="cuda")
+            d_codes = torch.empty((M, K), dtype=torch.float16, device="cuda")
+            d_abs = torch.zeros(4, dtype=torch.int32, device="cuda")
+            torch.cuda.synchronize()
+            w.run(d_a.data_ptr(), M, d_c.data_ptr(), d_codes.data_ptr(), d_abs.data_ptr(), ctx.stream)
+            torch.cuda.synchronize()
+            codes, scale = oracle.quantize_sym_int8(a)
+            np.testing.assert_array_equal(d_c.cpu().numpy(), oracle.matmul_q8_0_int8(raw, codes, scale, N))
+            w.close()
+    finally:
+        lib.sem_q8_path(prev)
+
+
+def test_exact_path_forward(gpu_model, oracle_model):
+    # SEM_Q8_PATH_EXACT also routes long sequences' projections to the CUDA-core
+    # kernel; with the tensor-core attention they stay within the bound, and
+    # short sequences beside them stay bit-exact
+    import _lib
+    lib = _lib.load()
+    prev = lib.sem_q8_path(4)
+    try:
+        lengths = [40, 300]
+        ids, offs = synth.token_batch(515, lengths, TEST_VOCAB)
+        check_parity(gpu_model, oracle_model, ids, offs, [768, 768], "exact path", strict=True)
+        got = gpu_model.forward_batch(ids, offs, 768)
+        np.testing.assert_array_equal(got[0], oracle_model.forward_with_dim(ids[:40], 768))
+    finally:
+        lib.sem_q8_path(prev)
+
+
+def test_device_ids_checked(gpu_model):
+    # sem_embed_device takes ids already on the device, so the host cannot
+    # validate them: the embedding kernel writes zeros for an id outside the
+    # vocabulary and records it; sem_model_check reports it once, then the
+    # record is clear
+    import torch
+    import _lib
+    ids, offs = synth.token_batch(818, [20, 30], TEST_VOCAB)
+    ids = ids.copy()
+    ids[25] = TEST_VOCAB + 3
+    d_ids = torch.from_numpy(ids).cuda()
+    d_out = torch.empty((2, 768), dtype=torch.float32, device="cuda")
+    torch.cuda.synchronize()
+    gpu_model.embed_device(d_ids.data_ptr(), offs, 2, 768, d_out.data_ptr())
+    with pytest.raises(_lib.SemError, match="^token ID out of range"):
+        gpu_model.check()
+    gpu_model.check()  # cleared
+    good, goffs = synth.token_batch(819, [20, 30], TEST_VOCAB)
+    d_ids = torch.from_numpy(good).cuda()
+    gpu_model.embed_device(d_ids.data_ptr(), goffs, 2, 768, d_out.data_ptr())
+    gpu_model.check()
+    ref = gpu_model.forward_batch(good, goffs, 768)
+    for i in range(2):
+        np.testing.assert_array_equal(d_out[i].cpu().numpy(), ref[i])
 
 
 def test_quantize_ties_round_half_away(ctx):
