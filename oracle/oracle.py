@@ -45,6 +45,8 @@ def lib():
         L.orc_quantize_sym_int8.argtypes = [f32p, C.c_int64, i8p, f32p]
         L.orc_matmul_q8_0_int8.argtypes = [f32p, C.c_void_p, f32p, i8p, C.c_float, C.c_int, C.c_int, C.c_int]
         L.orc_set_matmul_path.argtypes = [C.c_int]
+        L.orc_set_simd.restype = C.c_int
+        L.orc_set_simd.argtypes = [C.c_int]
         L.orc_extract_q8_0_scales.argtypes = [C.c_void_p, C.c_int64, C.c_int, f32p]
         L.orc_model_load.restype = C.c_void_p
         L.orc_model_load.argtypes = [C.c_char_p, C.c_char_p, C.c_int]
@@ -258,6 +260,14 @@ def search_exact_batch(quant: int, data: np.ndarray, qcodes: np.ndarray, topk: i
     n = lib().orc_search_exact_batch(quant, data.ctypes.data, count, dim, qcodes.ctypes.data, nq, topk,
                                      _p(rows, C.c_int32), _p(scores, C.c_int32), _p(dist, C.c_float), nthreads)
     return rows[:, :n], scores[:, :n], dist[:, :n]
+
+
+def set_simd(on: bool) -> bool:
+    """Timing only (bench.py's CPU legs): the Q8_0 inner loop and the float32
+    dot product run as AVX512-VNNI / AVX2 intrinsics that are the reference's
+    assembly instruction for instruction; results are bit-identical to the
+    plain loops. Returns whether the CPU supports it (else the switch stays off)."""
+    return bool(lib().orc_set_simd(1 if on else 0))
 
 
 def set_matmul_path(path: int) -> None:

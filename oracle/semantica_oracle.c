@@ -50,6 +50,27 @@ static inline float bits_to_f32(uint32_t b) { float f; memcpy(&f, &b, 4); return
  * summation order. */
 static int g_matmul_path = 0;
 void orc_set_matmul_path(int path) { g_matmul_path = path; }
+
+/* Vector inner loops for timing the CPU baseline (orc_set_simd). Off by
+ * default: the checker runs the plain loops below. When on, the Q8_0 inner
+ * loop of build 0 and the float32 dot product of builds 0 and 1 run as
+ * AVX512-VNNI / AVX2 intrinsics that are the reference's assembly instruction
+ * for instruction (VPDPBUSD with the zero-point correction, VCVTDQ2PS,
+ * VFMADD231PS, the same horizontal sum), so their results are the plain
+ * loops' bit for bit; only the speed differs. The switch is ignored on a CPU
+ * without AVX512-VNNI. */
+static int g_simd = 0;
+int orc_set_simd(int on) {
+#if defined(__x86_64__) && defined(__GNUC__)
+    __builtin_cpu_init();
+    g_simd = on && __builtin_cpu_supports("avx512vnni") && __builtin_cpu_supports("avx512vl") &&
+             __builtin_cpu_supports("avx2") && __builtin_cpu_supports("fma");
+#else
+    (void)on;
+    g_simd = 0;
+#endif
+    return g_simd;
+}
 static inline uint32_t f32_to_bits(float f) { uint32_t b; memcpy(&b, &f, 4); return b; }
 
 /* ------------------------------------------------------------------------
@@ -194,11 +215,57 @@ static inline float hsum8(const float acc[8]) {
     return (s0 + s1) + (s2 + s3);
 }
 
+#if defined(__x86_64__) && defined(__GNUC__)
+#include <immintrin.h>
+/* VEXTRACTF128 + VADDPS + VHADDPS + VHADDPS (simd_amd64.s:45-51). */
+__attribute__((target("avx2,fma"))) static inline float hsum256(__m256 acc) {
+    __m128 s4 = _mm_add_ps(_mm256_castps256_ps128(acc), _mm256_extractf128_ps(acc, 1));
+    s4 = _mm_hadd_ps(s4, s4);
+    s4 = _mm_hadd_ps(s4, s4);
+    return _mm_cvtss_f32(s4);
+}
+
+/* dotProductAVX2Asm (simd_amd64.s:19-76): 8 fused lane accumulators, the
+ * horizontal sum, then the unfused scalar tail. */
+__attribute__((target("avx2,fma"))) static float dot_f32_avx2(const float *a, const float *b, int n) {
+    __m256 acc = _mm256_setzero_ps();
+    int nv = n / 8;
+    for (int v = 0; v < nv; v++) acc = _mm256_fmadd_ps(_mm256_loadu_ps(a + 8 * v), _mm256_loadu_ps(b + 8 * v), acc);
+    float s = hsum256(acc);
+    for (int i = nv * 8; i < n; i++) {
+        float p = a[i] * b[i];
+        s = s + p;
+    }
+    return s;
+}
+
+/* matmulInnerLoopVNNIAsm (simd_amd64.s:241-304), instruction for instruction. */
+__attribute__((target("avx512vnni,avx512vl,avx512bw,avx512f,avx2,fma"))) static float q8_inner_vnni(
+    const int8_t *in, const uint8_t *w, const float *scales, int nblocks) {
+    const __m256i sign = _mm256_set1_epi8((char)0x80), ones = _mm256_set1_epi8(1);
+    __m256 acc = _mm256_setzero_ps();
+    for (int b = 0; b < nblocks; b++) {
+        const __m256 sc = _mm256_set1_ps(scales[b]);
+        const __m256i x = _mm256_loadu_si256((const __m256i *)(in + 32 * b));
+        const __m256i q = _mm256_loadu_si256((const __m256i *)(w + 34 * b + 2));
+        __m256i d = _mm256_dpbusd_epi32(_mm256_setzero_si256(), _mm256_xor_si256(q, sign), x); /* (w + 128) * x */
+        const __m256i sx = _mm256_dpbusd_epi32(_mm256_setzero_si256(), ones, x);             /* sum(x) */
+        d = _mm256_sub_epi32(d, _mm256_slli_epi32(sx, 7));
+        acc = _mm256_fmadd_ps(_mm256_cvtepi32_ps(d), sc, acc);
+    }
+    return hsum256(acc);
+}
+#define ORC_HAVE_SIMD 1
+#endif
+
 /* dotProductSIMD (simd_amd64.go:59-76): AVX2 assembly when n >= 8
  * (simd_amd64.s:19-76: 8 fused lane accumulators over n/8 vectors, horizontal
  * sum, then an unfused scalar tail), scalar loop otherwise. */
 float orc_dot_f32(const float *a, const float *b, int n) {
     if (n == 0) return 0.0f;
+#ifdef ORC_HAVE_SIMD
+    if (g_simd && n >= 8 && g_matmul_path != 2) return dot_f32_avx2(a, b, n);
+#endif
     if (n < 8 || g_matmul_path == 2) { /* dotProductScalar / sumSquaresScalar (simd_generic.go, norm.go:94-100) */
         float s = 0.0f;
         for (int i = 0; i < n; i++) s += a[i] * b[i];
@@ -314,6 +381,9 @@ static float q8_inner_loop(const int8_t *in, const uint8_t *w, const float *scal
         }
         return sum;
     }
+#ifdef ORC_HAVE_SIMD
+    if (g_simd && g_matmul_path == 0) return q8_inner_vnni(in, w, scales, nblocks);
+#endif
     float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
     for (int b = 0; b < nblocks; b++) {
         const int8_t *x = in + 32 * b;

@@ -35,6 +35,7 @@ void  orc_matmul_q8_0_int8(float *dst, const uint8_t *w_q8, const float *w_scale
                                                    /* quantize.go:346-458, simd_amd64.s:164-304 */
 /* reference build to follow: 0 amd64 AVX512-VNNI (default), 1 amd64 AVX2, 2 portable noasm */
 void  orc_set_matmul_path(int path);
+int   orc_set_simd(int on); /* timing only: intrinsic inner loops, bit-identical results; returns 1 if on */
 void  orc_extract_q8_0_scales(const uint8_t *w_q8, int64_t rows, int cols, float *scales);
                                                    /* model_int8.go:543-569 */
 

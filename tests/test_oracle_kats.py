@@ -259,3 +259,53 @@ class TestForwardOracle:
         assert a.shape == (128,)
         assert abs(np.linalg.norm(a) - 1) < 1e-5
         np.testing.assert_array_equal(a, b)
+
+
+class TestTimedBuildEqualsChecker:
+    """bench.py times the CPU baseline with the oracle's intrinsic inner loops
+    (oracle.set_simd): VPDPBUSD / VCVTDQ2PS / VFMADD231PS and the AVX2
+    dot product, the reference's assembly instruction for instruction. They
+    must give the plain loops' results bit for bit, or the timed baseline
+    would not be the checked computation."""
+
+    def test_matmul_and_dot(self):
+        import synth
+        rng = np.random.default_rng(31)
+        if not oracle.set_simd(True):
+            oracle.set_simd(False)
+            pytest.skip("host CPU has no AVX512-VNNI")
+        try:
+            for K, N, M in ((768, 256, 9), (1152, 128, 4), (3072, 128, 3)):
+                raw = synth.q8_0_blocks(rng, N, K)
+                codes, sc = oracle.quantize_sym_int8(rng.standard_normal((M, K)).astype(np.float32))
+                fast = oracle.matmul_q8_0_int8(raw, codes, sc, N)
+                oracle.set_simd(False)
+                plain = oracle.matmul_q8_0_int8(raw, codes, sc, N)
+                oracle.set_simd(True)
+                np.testing.assert_array_equal(fast, plain)
+            for n in (8, 9, 256, 1000):
+                a = rng.standard_normal(n).astype(np.float32)
+                b = rng.standard_normal(n).astype(np.float32)
+                x = oracle.lib().orc_dot_f32(oracle._p(a, oracle.C.c_float), oracle._p(b, oracle.C.c_float), n)
+                oracle.set_simd(False)
+                y = oracle.lib().orc_dot_f32(oracle._p(a, oracle.C.c_float), oracle._p(b, oracle.C.c_float), n)
+                oracle.set_simd(True)
+                assert np.float32(x).tobytes() == np.float32(y).tobytes()
+        finally:
+            oracle.set_simd(False)
+
+    def test_forward(self, model_path):
+        import synth
+        m = oracle.OracleModel(model_path)
+        if not oracle.set_simd(True):
+            oracle.set_simd(False)
+            pytest.skip("host CPU has no AVX512-VNNI")
+        try:
+            ids, offs = synth.token_batch(91, [40, 7], m.config.vocab_size)
+            fast = m.forward_batch(ids, offs, 768, nthreads=2)
+            oracle.set_simd(False)
+            plain = m.forward_batch(ids, offs, 768, nthreads=2)
+            np.testing.assert_array_equal(fast, plain)
+        finally:
+            oracle.set_simd(False)
+            m.close()
