@@ -36,8 +36,11 @@ constexpr int kAsMaxKeys = 127;    // sequences shorter than 128 tokens
 constexpr int kAsThreads = 256;
 constexpr int kKLane = 36;         // words per lane of a K row: 32 elements + 4 (bank spread)
 constexpr int kKRow = 8 * kKLane;  // words per K row
-constexpr int kAsKVWords = kAsMaxKeys * kKRow;  // K rows; V rows ([127][256]) reuse the space
-constexpr int kAsSmem = (kAsKVWords + kAsQ * 128 + 128 * kAsQ) * 4;
+constexpr int kAsSPWords = kAsQ * 128 + 128 * kAsQ;  // scores and probabilities
+// shared memory for sequences of up to max_len keys: K rows (V rows reuse the
+// space), then the scores and the probabilities
+__host__ __device__ inline int as_kv_words(int max_len) { return max_len * kKRow; }
+constexpr int kAsSmemMax = (kAsMaxKeys * kKRow + kAsSPWords) * 4;
 
 __device__ __forceinline__ float group_hsum8(float v) {
   v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, 4));
@@ -47,11 +50,11 @@ __device__ __forceinline__ float group_hsum8(float v) {
 
 __global__ void __launch_bounds__(kAsThreads, 1)
     attention_short_kernel(const float* __restrict__ qkv, int nh, float scale, const int32_t* __restrict__ cu,
-                           const int32_t* __restrict__ tile_seq, float* __restrict__ out,
+                           const int32_t* __restrict__ tile_seq, int max_len, float* __restrict__ out,
                            uint32_t* __restrict__ absmax) {
   extern __shared__ __align__(16) float as_smem[];
-  float* KV = as_smem;                // K [L][8][kKLane], then V [L][256]
-  float* S = KV + kAsKVWords;         // scores, then e = fastExp(s - max) [16][128]
+  float* KV = as_smem;                    // K [L][8][kKLane], then V [L][256]
+  float* S = KV + as_kv_words(max_len);   // scores, then e = fastExp(s - max) [16][128]
   float* Pt = S + kAsQ * 128;         // probabilities, transposed [128][16]
   __shared__ float red[kAsThreads / 32];
   const int per_tile = nh * kAsQBlocks;
@@ -60,7 +63,7 @@ __global__ void __launch_bounds__(kAsThreads, 1)
   const int s = tile_seq[tile];
   const int r0 = cu[s], L = cu[s + 1] - r0;
   const int q0 = qb * kAsQ;
-  if (q0 >= L || L > kAsMaxKeys) return;  // uniform over the CTA
+  if (q0 >= L || L > max_len) return;  // uniform over the CTA
   const int nq = min(kAsQ, L - q0);
   const int ld = (nh + 2) * kHd;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, l = tid & 7, g = tid >> 3;
@@ -89,20 +92,30 @@ __global__ void __launch_bounds__(kAsThreads, 1)
   }
   __syncthreads();
 
-  // ---- scores ----
-  for (int j = jpar; j < L; j += 2) {
-    const float4* kr = reinterpret_cast<const float4*>(KV + j * kKRow + l * kKLane);
-    float acc = 0.0f;
+  // ---- scores: four keys per pass (independent accumulation chains) ----
+  for (int j0 = jpar; j0 < L; j0 += 8) {
+    const float4* kr[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k)  // keys past the sequence recompute its last key and are not stored
+      kr[k] = reinterpret_cast<const float4*>(KV + min(j0 + 2 * k, L - 1) * kKRow + l * kKLane);
+    float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
     for (int u = 0; u < 8; ++u) {
-      const float4 k4 = kr[u];
-      acc = __fmaf_rn(qr[4 * u], k4.x, acc);
-      acc = __fmaf_rn(qr[4 * u + 1], k4.y, acc);
-      acc = __fmaf_rn(qr[4 * u + 2], k4.z, acc);
-      acc = __fmaf_rn(qr[4 * u + 3], k4.w, acc);
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const float4 k4 = kr[k][u];
+        acc[k] = __fmaf_rn(qr[4 * u], k4.x, acc[k]);
+        acc[k] = __fmaf_rn(qr[4 * u + 1], k4.y, acc[k]);
+        acc[k] = __fmaf_rn(qr[4 * u + 2], k4.z, acc[k]);
+        acc[k] = __fmaf_rn(qr[4 * u + 3], k4.w, acc[k]);
+      }
     }
-    const float d = group_hsum8(acc);
-    if (l == 0 && i < nq) S[i * 128 + j] = __fmul_rn(d, scale);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const float d = group_hsum8(acc[k]);
+      const int j = j0 + 2 * k;
+      if (l == 0 && i < nq && j < L) S[i * 128 + j] = __fmul_rn(d, scale);
+    }
   }
   __syncthreads();  // K consumed, scores complete
 
@@ -184,9 +197,10 @@ __global__ void __launch_bounds__(kAsThreads, 1)
 }  // namespace
 
 cudaError_t launch_attention_short(const float* qkv, int num_heads, float scale, SeqMeta meta, AttnTiles tiles,
-                                   float* out, uint32_t* absmax, cudaStream_t stream) {
+                                   int max_len, float* out, uint32_t* absmax, cudaStream_t stream) {
   if (tiles.n_tiles == 0) return cudaSuccess;
-  if (num_heads < 1 || num_heads > 3 || !qkv || !out || !meta.cu_seqlens || !tiles.tile_seq)
+  if (num_heads < 1 || num_heads > 3 || !qkv || !out || !meta.cu_seqlens || !tiles.tile_seq || max_len < 1 ||
+      max_len > kAsMaxKeys)
     return cudaErrorInvalidValue;
   {
     static std::mutex mu;
@@ -197,15 +211,16 @@ cudaError_t launch_attention_short(const float* qkv, int num_heads, float scale,
     if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
     std::lock_guard<std::mutex> lk(mu);
     if (!done[dev]) {
-      if ((e = cudaFuncSetAttribute(attention_short_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kAsSmem)) !=
-          cudaSuccess)
+      if ((e = cudaFuncSetAttribute(attention_short_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    kAsSmemMax)) != cudaSuccess)
         return e;
       done[dev] = true;
     }
   }
   const int64_t grid = (int64_t)tiles.n_tiles * num_heads * kAsQBlocks;
-  attention_short_kernel<<<(unsigned)grid, kAsThreads, kAsSmem, stream>>>(qkv, num_heads, scale, meta.cu_seqlens,
-                                                                         tiles.tile_seq, out, absmax);
+  const int smem = (as_kv_words(max_len) + kAsSPWords) * 4;
+  attention_short_kernel<<<(unsigned)grid, kAsThreads, smem, stream>>>(qkv, num_heads, scale, meta.cu_seqlens,
+                                                                      tiles.tile_seq, max_len, out, absmax);
   return cudaGetLastError();
 }
 

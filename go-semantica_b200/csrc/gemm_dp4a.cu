@@ -39,18 +39,14 @@ namespace sem {
 namespace {
 
 constexpr int kDpThreads = 256;  // 32 groups of 8 lane threads
-constexpr int kDpMaxLS = 36;     // padded words per (row, lane) in shared memory
+constexpr int kDpStages = 3;     // weight-chunk ring
+constexpr int kDpChunk = 12;     // blocks per weight chunk (K % 384 == 0), else 4
+constexpr int kDpCtasPerSm = 3;
 
-// Blocks per shared-memory chunk: the largest of 36, 32, ..., 4 that divides
-// the row's block count (K % 128 == 0, so 4 always does).
-__host__ __device__ inline int dp_chunk_blocks(int kb_total) {
-  for (int c = 36; c > 4; c -= 4)
-    if (kb_total % c == 0) return c;
-  return 4;
-}
-// Words between the lanes of one row: chunk / 4 sixteen-byte pieces, made odd
-// so the 8 lanes of a group read 8 different bank quads.
-__host__ __device__ inline int dp_lane_stride(int kbc) { return ((kbc / 4) & 1) ? kbc : kbc + 4; }
+// Words between the lanes of one row in shared memory: a multiple of 4 whose
+// quarter is odd, so the 8 lanes of a group read 8 different bank quads.
+__host__ __device__ inline int dp_lane_stride(int blocks) { return ((blocks / 4) & 1) ? blocks : blocks + 4; }
+__host__ __device__ inline int dp_chunk(int kb_total) { return kb_total % kDpChunk == 0 ? kDpChunk : 4; }
 
 // 8 INT8 codes held as fp16 integers in [-127, 127] -> two words of int8.
 // h + 1152 lies in [1025, 1279], where fp16 steps by 1, so the low byte of its
@@ -67,10 +63,20 @@ __device__ __forceinline__ uint2 codes8_to_s8(uint4 v) {
   return make_uint2(__byte_perm(t[0], t[1], 0x6420) ^ 0x80808080u, __byte_perm(t[2], t[3], 0x6420) ^ 0x80808080u);
 }
 
-// One lane's block term: fma(float32(exact 4-byte partial), scale, acc).
-__device__ __forceinline__ float lane_fma(uint32_t a, uint32_t w, float s, float acc) {
-  const float x = __int_as_float(__dp4a((int)a, (int)w, kFloatMagicBits));
-  return __fmaf_rn(__fsub_rn(x, kFloatMagic), s, acc);
+// Two tokens' terms of one lane and block, as a packed pair:
+// acc = fma(float32(exact partial) , scale, acc) for each token. The dp4a
+// accumulator input 1.5 * 2^23 makes each result's float bits 1.5 * 2^23 +
+// partial, and the packed subtraction of 1.5 * 2^23 is exact.
+__device__ __forceinline__ void lane_fma2(uint64_t& acc, uint32_t a0, uint32_t a1, uint32_t w, uint64_t ss) {
+  const uint32_t x0 = (uint32_t)__dp4a((int)a0, (int)w, kFloatMagicBits);
+  const uint32_t x1 = (uint32_t)__dp4a((int)a1, (int)w, kFloatMagicBits);
+  const uint64_t mm = 0x4B4000004B400000ull;  // (1.5 * 2^23, 1.5 * 2^23)
+  asm("{\n\t.reg .b64 t;\n\t"
+      "mov.b64 t, {%1, %2};\n\t"
+      "sub.rn.f32x2 t, t, %3;\n\t"
+      "fma.rn.f32x2 %0, t, %4, %0;\n\t}"
+      : "+l"(acc)
+      : "r"(x0), "r"(x1), "l"(mm), "l"(ss));
 }
 
 // The VNNI kernel's horizontal sum over the 8 threads of a group; every
@@ -86,36 +92,67 @@ __device__ __forceinline__ float dp_gelu_up(float g, float u, float rs) {
   return __fmul_rn(gelu_quick_ref(__fmul_rn(g, rs)), __fmul_rn(u, rs));
 }
 
-// TGM token groups x (32 / TGM) weight-row groups per CTA: TM = 4 TGM tokens,
-// TN = 4 (32 / TGM) weight rows. kEpiGeluUp: a group's 4 rows are gate j,
-// j + 1 and up j, j + 1, so it forms two outputs h = GELUQuick(gate) * up per
-// token and the per-sequence absmax of h.
+__device__ __forceinline__ void cp_async4(void* smem, const void* gmem) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;\n" ::"r"(smem_u32(smem)), "l"(gmem));
+}
+
+// TGM token groups x (32 / TGM) weight-row groups per tile: TM = 4 TGM tokens,
+// TN = 4 (32 / TGM) weight rows. A CTA stages its TM tokens' codes once (all
+// of K) and walks the weight tiles blockIdx.x, blockIdx.x + gridDim.x, ...;
+// the weights stream through a kDpStages-deep ring of (tile, K chunk) items.
+// kEpiGeluUp: a group's 4 rows are gate j, j + 1 and up j, j + 1, so it forms
+// two outputs h = GELUQuick(gate) * up per token, and the CTA the per-sequence
+// absmax of h over all its tiles.
 template <int TGM, int EPI>
-__global__ void __launch_bounds__(kDpThreads, 2) gemm_q8_dp4a_kernel(
+__global__ void __launch_bounds__(kDpThreads, kDpCtasPerSm) gemm_q8_dp4a_kernel(
     const __half* __restrict__ a, const uint32_t* __restrict__ wl, const float* __restrict__ ws, int M, int N, int K,
-    int kbc, const uint32_t* __restrict__ a_absmax, const int32_t* __restrict__ row_seq, float* __restrict__ c,
+    const uint32_t* __restrict__ a_absmax, const int32_t* __restrict__ row_seq, float* __restrict__ c,
     uint32_t* __restrict__ out_absmax) {
   constexpr int TM = 4 * TGM, TN = 4 * (32 / TGM);
   extern __shared__ __align__(16) uint32_t dp_smem[];
   __shared__ float s_rs[TM];
   __shared__ int s_seq[TM];
   __shared__ uint32_t s_amax[TM];
-  const int ls = dp_lane_stride(kbc);
-  uint32_t* As = dp_smem;                                  // [TM][8][ls] activation words
-  uint32_t* Ws = As + TM * 8 * ls;                         // [TN][8][ls] weight words
-  float* Ss = reinterpret_cast<float*>(Ws + TN * 8 * ls);  // [TN][ls] block scales
+  const int KB = K / 32, KW = K / 4;  // blocks and words per row
+  const int kbc = dp_chunk(KB), pieces = kbc / 4, nchunks = KB / kbc;
+  const int la = dp_lane_stride(KB), lw = dp_lane_stride(kbc);
+  uint32_t* As = dp_smem;                // [TM][8][la] activation words, all of K
+  uint32_t* ring = As + TM * 8 * la;     // stages of {weights [TN][8][lw] words, scale pairs [TN][lw] x 2 words}
+  const int stage_words = TN * 8 * lw + TN * lw * 2;
   const int tid = threadIdx.x, l = tid & 7, g = tid >> 3;
   const int tg = g % TGM, cg = g / TGM;
-  const int KB = K / 32, KW = K / 4;  // blocks and words per row
   const int m0 = blockIdx.y * TM;
-  const int nt = blockIdx.x;
+  const int n_tiles = N / TN;
+  const int my_tiles = (n_tiles - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x;
+  const int items = my_tiles * nchunks;
   const int half = N / 2;  // kEpiGeluUp: gate rows [0, half), up rows [half, N)
-  auto wrow = [&](int slot) -> int {
+  auto wrow = [&](int nt, int slot) -> int {
     if (EPI == kEpiStore) return nt * TN + slot;
     const int q = slot & 3;
     const int j = nt * (TN / 2) + 2 * (slot >> 2) + (q & 1);
     return q < 2 ? j : half + j;
   };
+  // one (tile, chunk) item's weights and duplicated scales into its stage;
+  // every thread commits a group per call (empty past the end) so the wait
+  // counts stay uniform
+  auto issue = [&](int item) {
+    if (item < items) {
+      const int nt = (int)blockIdx.x + (item / nchunks) * (int)gridDim.x, kc0 = (item % nchunks) * kbc;
+      uint32_t* Ws = ring + (item % kDpStages) * stage_words;
+      float* Ss = reinterpret_cast<float*>(Ws + TN * 8 * lw);
+      for (int i = tid; i < TN * 8 * pieces; i += kDpThreads) {
+        const int p = i % pieces, rest = i / pieces, ll = rest & 7, slot = rest >> 3;
+        cp_async16(Ws + (slot * 8 + ll) * lw + 4 * p, wl + (size_t)wrow(nt, slot) * KW + ll * KB + kc0 + 4 * p, true);
+      }
+      for (int i = tid; i < TN * kbc * 2; i += kDpThreads) {
+        const int dup = i & 1, kb = (i >> 1) % kbc, slot = (i >> 1) / kbc;
+        cp_async4(Ss + (slot * lw + kb) * 2 + dup, ws + (size_t)wrow(nt, slot) * KB + kc0 + kb);
+      }
+    }
+    cp_async_commit();
+  };
+  for (int i = 0; i < kDpStages - 1; ++i) issue(i);
+
   if (tid < TM) {
     const int m = m0 + tid;
     int sq = -1;
@@ -128,115 +165,146 @@ __global__ void __launch_bounds__(kDpThreads, 2) gemm_q8_dp4a_kernel(
     s_rs[tid] = rs;
     s_amax[tid] = 0u;
   }
-  float acc[4][4];
+  // activation codes: fp16 -> int8 words, lane-major, loads batched 4 deep
+  {
+    const int n = TM * KB * 4;  // 16-byte pieces of 8 codes
+    for (int i0 = tid; i0 < n; i0 += 4 * kDpThreads) {
+      uint4 v[4];
 #pragma unroll
-  for (int r = 0; r < 4; ++r)
+      for (int u = 0; u < 4; ++u) {
+        const int i = i0 + u * kDpThreads;
+        const int h = i & 3, kb = (i >> 2) % KB, t = (i >> 2) / KB;
+        v[u] = make_uint4(0x3c003c00u, 0u, 0u, 0u);
+        if (i < n && m0 + t < M)
+          v[u] = *reinterpret_cast<const uint4*>(a + (size_t)(m0 + t) * K + (size_t)kb * 32 + 8 * h);
+      }
 #pragma unroll
-    for (int q = 0; q < 4; ++q) acc[r][q] = 0.0f;
+      for (int u = 0; u < 4; ++u) {
+        const int i = i0 + u * kDpThreads;
+        if (i >= n) break;
+        const int h = i & 3, kb = (i >> 2) % KB, t = (i >> 2) / KB;
+        const uint2 wd = m0 + t < M ? codes8_to_s8(v[u]) : make_uint2(0u, 0u);
+        As[(t * 8 + 2 * h) * la + kb] = wd.x;
+        As[(t * 8 + 2 * h + 1) * la + kb] = wd.y;
+      }
+    }
+  }
 
-  const int pieces = kbc / 4;  // 16-byte pieces per (row, lane) in a chunk
-  for (int kc0 = 0; kc0 < KB; kc0 += kbc) {
-    __syncthreads();  // the previous chunk is consumed
-    for (int i = tid; i < TN * 8 * pieces; i += kDpThreads) {
-      const int p = i % pieces, rest = i / pieces, ll = rest & 7, slot = rest >> 3;
-      cp_async16(Ws + (slot * 8 + ll) * ls + 4 * p, wl + (size_t)wrow(slot) * KW + ll * KB + kc0 + 4 * p, true);
-    }
-    for (int i = tid; i < TN * pieces; i += kDpThreads) {
-      const int p = i % pieces, slot = i / pieces;
-      cp_async16(Ss + slot * ls + 4 * p, ws + (size_t)wrow(slot) * KB + kc0 + 4 * p, true);
-    }
-    cp_async_commit();
-    for (int i = tid; i < TM * kbc * 4; i += kDpThreads) {
-      const int h = i & 3, kb = (i >> 2) % kbc, t = (i >> 2) / kbc;
-      const int m = m0 + t;
-      uint2 wd = make_uint2(0u, 0u);
-      if (m < M) wd = codes8_to_s8(*reinterpret_cast<const uint4*>(a + (size_t)m * K + (size_t)(kc0 + kb) * 32 + 8 * h));
-      As[(t * 8 + 2 * h) * ls + kb] = wd.x;
-      As[(t * 8 + 2 * h + 1) * ls + kb] = wd.y;
-    }
-    cp_async_wait<0>();
-    __syncthreads();
+  uint64_t acc[2][4];  // token pairs (0,1), (2,3) x 4 weight rows
+#pragma unroll
+  for (int rp = 0; rp < 2; ++rp)
+#pragma unroll
+    for (int q = 0; q < 4; ++q) acc[rp][q] = 0ull;
+
+  for (int it = 0; it < items; ++it) {
+    issue(it + kDpStages - 1);
+    cp_async_wait<kDpStages - 1>();
+    __syncthreads();  // item `it` (and, the first time, the activation codes) visible to all
+    const uint32_t* Ws = ring + (it % kDpStages) * stage_words;
+    const uint64_t* Ss = reinterpret_cast<const uint64_t*>(Ws + TN * 8 * lw);
+    const int kc0 = (it % nchunks) * kbc;
 #pragma unroll 1
     for (int p = 0; p < pieces; ++p) {
       uint4 av[4];
 #pragma unroll
-      for (int r = 0; r < 4; ++r) av[r] = *reinterpret_cast<const uint4*>(As + ((tg * 4 + r) * 8 + l) * ls + 4 * p);
+      for (int r = 0; r < 4; ++r)
+        av[r] = *reinterpret_cast<const uint4*>(As + ((tg * 4 + r) * 8 + l) * la + kc0 + 4 * p);
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
-        const uint4 wv = *reinterpret_cast<const uint4*>(Ws + ((cg * 4 + q) * 8 + l) * ls + 4 * p);
-        const float4 sv = *reinterpret_cast<const float4*>(Ss + (cg * 4 + q) * ls + 4 * p);
+        const int slot = cg * 4 + q;
+        const uint4 wv = *reinterpret_cast<const uint4*>(Ws + (slot * 8 + l) * lw + 4 * p);
+        const ulonglong2 s01 = *reinterpret_cast<const ulonglong2*>(Ss + slot * lw + 4 * p);
+        const ulonglong2 s23 = *reinterpret_cast<const ulonglong2*>(Ss + slot * lw + 4 * p + 2);
         // blocks 4p .. 4p + 3 of the chunk, in ascending order per accumulator
 #pragma unroll
-        for (int r = 0; r < 4; ++r) acc[r][q] = lane_fma(av[r].x, wv.x, sv.x, acc[r][q]);
-#pragma unroll
-        for (int r = 0; r < 4; ++r) acc[r][q] = lane_fma(av[r].y, wv.y, sv.y, acc[r][q]);
-#pragma unroll
-        for (int r = 0; r < 4; ++r) acc[r][q] = lane_fma(av[r].z, wv.z, sv.z, acc[r][q]);
-#pragma unroll
-        for (int r = 0; r < 4; ++r) acc[r][q] = lane_fma(av[r].w, wv.w, sv.w, acc[r][q]);
+        for (int rp = 0; rp < 2; ++rp) {
+          lane_fma2(acc[rp][q], av[2 * rp].x, av[2 * rp + 1].x, wv.x, s01.x);
+          lane_fma2(acc[rp][q], av[2 * rp].y, av[2 * rp + 1].y, wv.y, s01.y);
+          lane_fma2(acc[rp][q], av[2 * rp].z, av[2 * rp + 1].z, wv.z, s23.x);
+          lane_fma2(acc[rp][q], av[2 * rp].w, av[2 * rp + 1].w, wv.w, s23.y);
+        }
       }
     }
+    if (it % nchunks == nchunks - 1) {  // the tile's last chunk: its epilogue
+      const int nt = (int)blockIdx.x + (it / nchunks) * (int)gridDim.x;
+      float v[4][4];
+#pragma unroll
+      for (int rp = 0; rp < 2; ++rp)
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          unpack2(acc[rp][q], v[2 * rp][q], v[2 * rp + 1][q]);
+          acc[rp][q] = 0ull;
+        }
+      if (EPI == kEpiStore) {
+#pragma unroll
+        for (int r = 0; r < 4; ++r) {
+          const int t = tg * 4 + r, m = m0 + t;
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const float sum = group_hsum(v[r][q]);
+            if (((r * 4 + q) & 7) == l && m < M) c[(size_t)m * N + nt * TN + cg * 4 + q] = __fmul_rn(sum, s_rs[t]);
+          }
+        }
+      } else {
+        // lane l: token r = l / 2, channel j + (l & 1)
+#pragma unroll
+        for (int r = 0; r < 4; ++r) {
+          const float g0 = group_hsum(v[r][0]), g1 = group_hsum(v[r][1]);
+          const float u0 = group_hsum(v[r][2]), u1 = group_hsum(v[r][3]);
+          const int t = tg * 4 + r, m = m0 + t;
+          if ((l >> 1) == r && m < M) {
+            const float h = dp_gelu_up((l & 1) ? g1 : g0, (l & 1) ? u1 : u0, s_rs[t]);
+            c[(size_t)m * half + nt * (TN / 2) + cg * 2 + (l & 1)] = h;
+            const float am = fmaxf(0.0f, fabsf(h));  // NaN folds to 0, as fmaxf does in the tensor-core epilogues
+            if (out_absmax && am > 0.0f) atomicMax(&s_amax[t], __float_as_uint(am));
+          }
+        }
+      }
+    }
+    __syncthreads();  // the stage of item `it` is free for item it + kDpStages
   }
-
-  // ---- epilogue ----
-  if (EPI == kEpiStore) {
-#pragma unroll
-    for (int r = 0; r < 4; ++r) {
-      const int t = tg * 4 + r, m = m0 + t;
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const float v = group_hsum(acc[r][q]);
-        if (((r * 4 + q) & 7) == l && m < M) c[(size_t)m * N + nt * TN + cg * 4 + q] = __fmul_rn(v, s_rs[t]);
-      }
-    }
-  } else {
-    // lane l: token r = l / 2, channel j + (l & 1)
-#pragma unroll
-    for (int r = 0; r < 4; ++r) {
-      const float g0 = group_hsum(acc[r][0]), g1 = group_hsum(acc[r][1]);
-      const float u0 = group_hsum(acc[r][2]), u1 = group_hsum(acc[r][3]);
-      const int t = tg * 4 + r, m = m0 + t;
-      if ((l >> 1) == r && m < M) {
-        const float h = dp_gelu_up((l & 1) ? g1 : g0, (l & 1) ? u1 : u0, s_rs[t]);
-        c[(size_t)m * half + nt * (TN / 2) + cg * 2 + (l & 1)] = h;
-        const float am = fmaxf(0.0f, fabsf(h));  // NaN folds to 0, as fmaxf does in the tensor-core epilogues
-        if (out_absmax && am > 0.0f) atomicMax(&s_amax[t], __float_as_uint(am));
-      }
-    }
-    if (out_absmax) {
-      __syncthreads();
-      if (tid < TM && s_seq[tid] >= 0 && s_amax[tid]) atomicMax(&out_absmax[s_seq[tid]], s_amax[tid]);
-    }
-  }
+  if (EPI == kEpiGeluUp && out_absmax && tid < TM && s_seq[tid] >= 0 && s_amax[tid])
+    atomicMax(&out_absmax[s_seq[tid]], s_amax[tid]);
 }
 
 template <int TGM, int EPI>
 cudaError_t launch_dp(const __half* a, const int8_t* wl, const float* ws, int M, int N, int K, const uint32_t* a_absmax,
                       const int32_t* row_seq, float* c, uint32_t* out_absmax, cudaStream_t stream) {
   constexpr int TM = 4 * TGM, TN = 4 * (32 / TGM);
-  const int kbc = dp_chunk_blocks(K / 32);
-  const int ls = dp_lane_stride(kbc);
-  const size_t smem = ((size_t)(TM + TN) * 8 * ls + (size_t)TN * ls) * 4;
+  const int KB = K / 32, kbc = dp_chunk(KB);
+  const size_t smem =
+      ((size_t)TM * 8 * dp_lane_stride(KB) + (size_t)kDpStages * (TN * 8 + TN * 2) * dp_lane_stride(kbc)) * 4;
+  if (smem > 200 * 1024) return cudaErrorInvalidValue;  // K up to 3072 fits
   auto kern = gemm_q8_dp4a_kernel<TGM, EPI>;
-  {  // the shared-memory limit is a per-device function attribute: set once per device
+  int sms = 148;
+  {  // per-device: the shared-memory limit (a function attribute) and the SM count
     static std::mutex mu;
     static bool done[64] = {};
+    static int sm_count[64] = {};
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
     if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
     std::lock_guard<std::mutex> lk(mu);
     if (!done[dev]) {
-      const size_t max_smem = ((size_t)(TM + TN) * 8 * kDpMaxLS + (size_t)TN * kDpMaxLS) * 4;
-      if ((e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)max_smem)) != cudaSuccess)
+      if ((e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024)) != cudaSuccess)
         return e;
+      if ((e = cudaDeviceGetAttribute(&sm_count[dev], cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess) return e;
       done[dev] = true;
     }
+    sms = sm_count[dev];
   }
-  const dim3 grid((unsigned)(N / TN), (unsigned)((M + TM - 1) / TM));
+  // token tiles x weight-tile groups ~ the resident CTAs; each CTA takes
+  // ceil(n_tiles / groups) weight tiles, so the activation codes are staged
+  // once per that many tiles
+  const int m_tiles = (M + TM - 1) / TM, n_tiles = N / TN;
+  const int want = (kDpCtasPerSm * sms + m_tiles - 1) / m_tiles;
+  const int per = (n_tiles + (want < 1 ? 1 : want) - 1) / (want < 1 ? 1 : want);
+  const int gx = (n_tiles + per - 1) / per;
+  const dim3 grid((unsigned)gx, (unsigned)m_tiles);
   if (grid.y > 65535u) return cudaErrorInvalidConfiguration;
-  kern<<<grid, kDpThreads, smem, stream>>>(a, reinterpret_cast<const uint32_t*>(wl), ws, M, N, K, kbc, a_absmax,
-                                           row_seq, c, out_absmax);
+  kern<<<grid, kDpThreads, smem, stream>>>(a, reinterpret_cast<const uint32_t*>(wl), ws, M, N, K, a_absmax, row_seq, c,
+                                           out_absmax);
   return cudaGetLastError();
 }
 

@@ -52,6 +52,7 @@ struct sem_model {
   std::vector<int32_t> last_offsets, last_dims;
   int32_t n_tiles = 0;
   int32_t n_tiles_long = 0;  // attention tiles of the long sequences (first in the tile list)
+  int32_t short_max_len = 0; // longest sequence under kSplitMinLen tokens
   int64_t t_long = 0;     // packed rows of the long sequences (first in the packed order)
   bool permuted = false;  // packed order differs from the caller's
   // optional per-launch timing
@@ -304,6 +305,7 @@ struct MetaPtrs {
   SeqMeta seq;
   AttnTiles tiles;        // 128-row attention tiles of the long sequences (tensor-core kernel)
   AttnTiles short_tiles;  // one tile per short sequence (float32 CUDA-core kernel)
+  int32_t short_max_len;  // longest short sequence
   int32_t* out_dims;
   int64_t* out_off;
   int32_t* src_row;  // [T] caller's row of each packed row (valid when permuted)
@@ -321,6 +323,9 @@ struct MetaPtrs {
 // operations are the reference's in the reference's order: their embeddings
 // are bit-identical to the reference's default build.
 constexpr int32_t kSplitMinLen = 128;
+// Up to this many tokens of short sequences in a batch take the exact
+// kernels under SEM_Q8_PATH_AUTO (the latency regime of small requests).
+constexpr int64_t kExactShortMaxTokens = 4096;
 
 // Builds the per-batch metadata on the host and uploads it (skipped when the
 // batch shape equals the previous call's). Sequences are packed long ones
@@ -377,12 +382,13 @@ int upload_meta(sem_model* m, const int32_t* offsets, int B, const int32_t* dims
     int32_t* h_src = h_dims + B;
     int64_t* h_off = reinterpret_cast<int64_t*>(reinterpret_cast<uint8_t*>(h) +
                                                 (reinterpret_cast<uint8_t*>(d_off) - reinterpret_cast<uint8_t*>(base)));
-    int32_t nt = 0, nt_long = 0;
+    int32_t nt = 0, nt_long = 0, short_max = 0;
     int32_t r = 0;
     for (int s = 0; s < B; ++s) {
       const int o = order[s];
       const int32_t len = offsets[o + 1] - offsets[o];
       if (len >= kSplitMinLen) nt_long = nt + (len + kAttnTileRows - 1) / kAttnTileRows;
+      else if (len > short_max) short_max = len;
       h_cu[s] = r;
       for (int32_t i = 0; i < len; ++i) {
         h_row_seq[r + i] = s;
@@ -404,11 +410,13 @@ int upload_meta(sem_model* m, const int32_t* offsets, int B, const int32_t* dims
     m->last_dims.assign(dims, dims + B);
     m->n_tiles = nt;
     m->n_tiles_long = nt_long;
+    m->short_max_len = short_max;
     m->t_long = t_long;
     m->permuted = permuted;
   }
   mp->seq = SeqMeta{d_row_seq, d_row_pos, d_cu, (int32_t)T, (int32_t)B};
   mp->tiles = AttnTiles{d_tseq, d_trow, m->n_tiles_long};
+  mp->short_max_len = m->short_max_len;
   mp->short_tiles = AttnTiles{d_tseq + m->n_tiles_long, d_trow + m->n_tiles_long, m->n_tiles - m->n_tiles_long};
   mp->out_dims = d_dims;
   mp->out_off = d_off;
@@ -466,13 +474,18 @@ int run_forward(sem_model* m, const int32_t* d_ids, const MetaPtrs& mp, float* d
   // out_cols: columns of one output row (N, or N / 2 for gate/up).
   const int q8_path = get_q8_path();
   const int64_t t_split = q8_path == 3 || q8_path == 4 ? T : q8_path == 1 ? 0 : mp.T_long;
+  // Short sequences take the exact kernels (bit-identical to the reference)
+  // under path 4, and under path 0 while their tokens are few enough for the
+  // CUDA cores to match the tensor cores' latency; otherwise the tensor-core
+  // projection and attention kernels, as long sequences do.
+  const bool exact_short = q8_path == 4 || (q8_path == 0 && T - mp.T_long <= kExactShortMaxTokens);
   auto q8 = [&](const Q8Proj& w, int N, int K, const uint32_t* a_absmax, float* out, int out_cols, int epi,
                 uint32_t* out_absmax) -> cudaError_t {
     cudaError_t e = cudaSuccess;
     if (t_split > 0)
       e = launch_q8_proj(codes, w, (int)t_split, N, K, a_absmax, sm.row_seq, out, epi, out_absmax, err, st);
     if (e == cudaSuccess && T > t_split) {
-      if (q8_path == 1)
+      if (!exact_short)
         e = launch_gemm_q8(codes + t_split * K, w.codes, w.scales, (int)(T - t_split), N, K, a_absmax,
                            sm.row_seq + t_split, out + t_split * out_cols, epi, out_absmax, err, st);
       else
@@ -492,13 +505,19 @@ int run_forward(sem_model* m, const int32_t* d_ids, const MetaPtrs& mp, float* d
     // attention block (model_int8.go:191-210)
     SEM_LAUNCH(kStGemmQKV, q8(w.qkv, qkvN, H, slot(l, 0), big, qkvN, kEpiStore, nullptr));
     SEM_LAUNCH(kStQKNormRope, launch_qk_norm_rope(big, w.q_norm, w.k_norm, m->rope_cos, m->rope_sin, c.norm_eps, nh,
-                                                  sm, qh, ql, kh, kl, vh, vl, mp.T_long, st));
-    if (mp.tiles.n_tiles)
-      SEM_LAUNCH(kStAttention, launch_attention(qh, ql, kh, kl, vh, vl, nh, c.attention_scale, sm, mp.tiles, att,
+                                                  sm, qh, ql, kh, kl, vh, vl, exact_short ? mp.T_long : T, st));
+    if (exact_short) {  // tensor cores for the long sequences' tiles, float32 CUDA cores for the short ones
+      if (mp.tiles.n_tiles)
+        SEM_LAUNCH(kStAttention, launch_attention(qh, ql, kh, kl, vh, vl, nh, c.attention_scale, sm, mp.tiles, att,
+                                                  slot(l, 1), err, st));
+      if (mp.short_tiles.n_tiles)
+        SEM_LAUNCH(kStAttnShort, launch_attention_short(big, nh, c.attention_scale, sm, mp.short_tiles,
+                                                        mp.short_max_len, att, slot(l, 1), st));
+    } else {
+      const AttnTiles all{mp.tiles.tile_seq, mp.tiles.tile_row0, mp.tiles.n_tiles + mp.short_tiles.n_tiles};
+      SEM_LAUNCH(kStAttention, launch_attention(qh, ql, kh, kl, vh, vl, nh, c.attention_scale, sm, all, att,
                                                 slot(l, 1), err, st));
-    if (mp.short_tiles.n_tiles)
-      SEM_LAUNCH(kStAttnShort, launch_attention_short(big, nh, c.attention_scale, sm, mp.short_tiles, att, slot(l, 1),
-                                                      st));
+    }
     SEM_LAUNCH(kStQuant, launch_quantize(att, nullptr, nullptr, H, sm, slot(l, 1), codes, st));
     SEM_LAUNCH(kStGemmO, q8(w.o, H, H, slot(l, 1), big, H, kEpiStore, nullptr));
     SEM_LAUNCH(kStResidual, launch_residual_norm(big, w.post_attn, hid, w.ffn_norm, H, c.norm_eps, sm, inv, slot(l, 2),

@@ -165,10 +165,11 @@ cudaError_t launch_attention(const __half* qh, const __half* ql, const __half* k
 // Float32 attention of sequences shorter than 128 tokens in the reference's
 // order (attention_short.cu): qkv rows [q (nh*256) | k | v] float32 with q and
 // k normed and RoPE'd (launch_qk_norm_rope with f32_row0 at or below their
-// rows); `tiles` lists one 128-row tile per such sequence. out [T][nh*256],
-// absmax[seq] atomically, as launch_attention.
+// rows); `tiles` lists one 128-row tile per such sequence, max_len is the
+// longest of them (at most 127). out [T][nh*256], absmax[seq] atomically, as
+// launch_attention.
 cudaError_t launch_attention_short(const float* qkv, int num_heads, float scale, SeqMeta meta, AttnTiles tiles,
-                                   float* out, uint32_t* absmax, cudaStream_t stream);
+                                   int max_len, float* out, uint32_t* absmax, cudaStream_t stream);
 
 // ---- brute search (brute_kernels.cu) ----
 // Exact integer scan: scores of nq queries against rows [0, count) of an
