@@ -63,20 +63,14 @@ __device__ __forceinline__ uint2 codes8_to_s8(uint4 v) {
   return make_uint2(__byte_perm(t[0], t[1], 0x6420) ^ 0x80808080u, __byte_perm(t[2], t[3], 0x6420) ^ 0x80808080u);
 }
 
-// Two tokens' terms of one lane and block, as a packed pair:
-// acc = fma(float32(exact partial) , scale, acc) for each token. The dp4a
-// accumulator input 1.5 * 2^23 makes each result's float bits 1.5 * 2^23 +
-// partial, and the packed subtraction of 1.5 * 2^23 is exact.
-__device__ __forceinline__ void lane_fma2(uint64_t& acc, uint32_t a0, uint32_t a1, uint32_t w, uint64_t ss) {
-  const uint32_t x0 = (uint32_t)__dp4a((int)a0, (int)w, kFloatMagicBits);
-  const uint32_t x1 = (uint32_t)__dp4a((int)a1, (int)w, kFloatMagicBits);
-  const uint64_t mm = 0x4B4000004B400000ull;  // (1.5 * 2^23, 1.5 * 2^23)
-  asm("{\n\t.reg .b64 t;\n\t"
-      "mov.b64 t, {%1, %2};\n\t"
-      "sub.rn.f32x2 t, t, %3;\n\t"
-      "fma.rn.f32x2 %0, t, %4, %0;\n\t}"
-      : "+l"(acc)
-      : "r"(x0), "r"(x1), "l"(mm), "l"(ss));
+// One lane's block term: acc = fma(float32(exact 4-byte partial), scale,
+// acc). The dp4a accumulator input 1.5 * 2^23 makes the result's float bits
+// 1.5 * 2^23 + partial, and subtracting 1.5 * 2^23 is exact. dp4a runs on the
+// heavy FMA pipe at half rate; the scalar subtraction and FMA can issue on
+// either FMA pipe (packed f32x2 forms measured slower).
+__device__ __forceinline__ float lane_fma(uint32_t a, uint32_t w, float s, float acc) {
+  const float x = __int_as_float(__dp4a((int)a, (int)w, kFloatMagicBits));
+  return __fmaf_rn(__fsub_rn(x, kFloatMagic), s, acc);
 }
 
 // The VNNI kernel's horizontal sum over the 8 threads of a group; every
@@ -90,10 +84,6 @@ __device__ __forceinline__ float group_hsum(float v) {
 // GELUQuick(gate * rs) * (up * rs) (model_int8.go:523-530).
 __device__ __forceinline__ float dp_gelu_up(float g, float u, float rs) {
   return __fmul_rn(gelu_quick_ref(__fmul_rn(g, rs)), __fmul_rn(u, rs));
-}
-
-__device__ __forceinline__ void cp_async4(void* smem, const void* gmem) {
-  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;\n" ::"r"(smem_u32(smem)), "l"(gmem));
 }
 
 // TGM token groups x (32 / TGM) weight-row groups per tile: TM = 4 TGM tokens,
@@ -117,8 +107,8 @@ __global__ void __launch_bounds__(kDpThreads, kDpCtasPerSm) gemm_q8_dp4a_kernel(
   const int kbc = dp_chunk(KB), pieces = kbc / 4, nchunks = KB / kbc;
   const int la = dp_lane_stride(KB), lw = dp_lane_stride(kbc);
   uint32_t* As = dp_smem;                // [TM][8][la] activation words, all of K
-  uint32_t* ring = As + TM * 8 * la;     // stages of {weights [TN][8][lw] words, scale pairs [TN][lw] x 2 words}
-  const int stage_words = TN * 8 * lw + TN * lw * 2;
+  uint32_t* ring = As + TM * 8 * la;     // stages of {weights [TN][8][lw] words, scales [TN][lw]}
+  const int stage_words = TN * 8 * lw + TN * lw;
   const int tid = threadIdx.x, l = tid & 7, g = tid >> 3;
   const int tg = g % TGM, cg = g / TGM;
   const int m0 = blockIdx.y * TM;
@@ -132,7 +122,7 @@ __global__ void __launch_bounds__(kDpThreads, kDpCtasPerSm) gemm_q8_dp4a_kernel(
     const int j = nt * (TN / 2) + 2 * (slot >> 2) + (q & 1);
     return q < 2 ? j : half + j;
   };
-  // one (tile, chunk) item's weights and duplicated scales into its stage;
+  // one (tile, chunk) item's weights and block scales into its stage;
   // every thread commits a group per call (empty past the end) so the wait
   // counts stay uniform
   auto issue = [&](int item) {
@@ -144,9 +134,9 @@ __global__ void __launch_bounds__(kDpThreads, kDpCtasPerSm) gemm_q8_dp4a_kernel(
         const int p = i % pieces, rest = i / pieces, ll = rest & 7, slot = rest >> 3;
         cp_async16(Ws + (slot * 8 + ll) * lw + 4 * p, wl + (size_t)wrow(nt, slot) * KW + ll * KB + kc0 + 4 * p, true);
       }
-      for (int i = tid; i < TN * kbc * 2; i += kDpThreads) {
-        const int dup = i & 1, kb = (i >> 1) % kbc, slot = (i >> 1) / kbc;
-        cp_async4(Ss + (slot * lw + kb) * 2 + dup, ws + (size_t)wrow(nt, slot) * KB + kc0 + kb);
+      for (int i = tid; i < TN * pieces; i += kDpThreads) {
+        const int p = i % pieces, slot = i / pieces;
+        cp_async16(Ss + slot * lw + 4 * p, ws + (size_t)wrow(nt, slot) * KB + kc0 + 4 * p, true);
       }
     }
     cp_async_commit();
@@ -190,18 +180,18 @@ __global__ void __launch_bounds__(kDpThreads, kDpCtasPerSm) gemm_q8_dp4a_kernel(
     }
   }
 
-  uint64_t acc[2][4];  // token pairs (0,1), (2,3) x 4 weight rows
+  float acc[4][4];  // 4 tokens x 4 weight rows
 #pragma unroll
-  for (int rp = 0; rp < 2; ++rp)
+  for (int r = 0; r < 4; ++r)
 #pragma unroll
-    for (int q = 0; q < 4; ++q) acc[rp][q] = 0ull;
+    for (int q = 0; q < 4; ++q) acc[r][q] = 0.0f;
 
   for (int it = 0; it < items; ++it) {
     issue(it + kDpStages - 1);
     cp_async_wait<kDpStages - 1>();
     __syncthreads();  // item `it` (and, the first time, the activation codes) visible to all
     const uint32_t* Ws = ring + (it % kDpStages) * stage_words;
-    const uint64_t* Ss = reinterpret_cast<const uint64_t*>(Ws + TN * 8 * lw);
+    const float* Ss = reinterpret_cast<const float*>(Ws + TN * 8 * lw);
     const int kc0 = (it % nchunks) * kbc;
 #pragma unroll 1
     for (int p = 0; p < pieces; ++p) {
@@ -213,15 +203,14 @@ __global__ void __launch_bounds__(kDpThreads, kDpCtasPerSm) gemm_q8_dp4a_kernel(
       for (int q = 0; q < 4; ++q) {
         const int slot = cg * 4 + q;
         const uint4 wv = *reinterpret_cast<const uint4*>(Ws + (slot * 8 + l) * lw + 4 * p);
-        const ulonglong2 s01 = *reinterpret_cast<const ulonglong2*>(Ss + slot * lw + 4 * p);
-        const ulonglong2 s23 = *reinterpret_cast<const ulonglong2*>(Ss + slot * lw + 4 * p + 2);
+        const float4 sv = *reinterpret_cast<const float4*>(Ss + slot * lw + 4 * p);
         // blocks 4p .. 4p + 3 of the chunk, in ascending order per accumulator
 #pragma unroll
-        for (int rp = 0; rp < 2; ++rp) {
-          lane_fma2(acc[rp][q], av[2 * rp].x, av[2 * rp + 1].x, wv.x, s01.x);
-          lane_fma2(acc[rp][q], av[2 * rp].y, av[2 * rp + 1].y, wv.y, s01.y);
-          lane_fma2(acc[rp][q], av[2 * rp].z, av[2 * rp + 1].z, wv.z, s23.x);
-          lane_fma2(acc[rp][q], av[2 * rp].w, av[2 * rp + 1].w, wv.w, s23.y);
+        for (int r = 0; r < 4; ++r) {
+          acc[r][q] = lane_fma(av[r].x, wv.x, sv.x, acc[r][q]);
+          acc[r][q] = lane_fma(av[r].y, wv.y, sv.y, acc[r][q]);
+          acc[r][q] = lane_fma(av[r].z, wv.z, sv.z, acc[r][q]);
+          acc[r][q] = lane_fma(av[r].w, wv.w, sv.w, acc[r][q]);
         }
       }
     }
@@ -229,11 +218,11 @@ __global__ void __launch_bounds__(kDpThreads, kDpCtasPerSm) gemm_q8_dp4a_kernel(
       const int nt = (int)blockIdx.x + (it / nchunks) * (int)gridDim.x;
       float v[4][4];
 #pragma unroll
-      for (int rp = 0; rp < 2; ++rp)
+      for (int r = 0; r < 4; ++r)
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
-          unpack2(acc[rp][q], v[2 * rp][q], v[2 * rp + 1][q]);
-          acc[rp][q] = 0ull;
+          v[r][q] = acc[r][q];
+          acc[r][q] = 0.0f;
         }
       if (EPI == kEpiStore) {
 #pragma unroll
@@ -273,7 +262,7 @@ cudaError_t launch_dp(const __half* a, const int8_t* wl, const float* ws, int M,
   constexpr int TM = 4 * TGM, TN = 4 * (32 / TGM);
   const int KB = K / 32, kbc = dp_chunk(KB);
   const size_t smem =
-      ((size_t)TM * 8 * dp_lane_stride(KB) + (size_t)kDpStages * (TN * 8 + TN * 2) * dp_lane_stride(kbc)) * 4;
+      ((size_t)TM * 8 * dp_lane_stride(KB) + (size_t)kDpStages * (TN * 8 + TN) * dp_lane_stride(kbc)) * 4;
   if (smem > 200 * 1024) return cudaErrorInvalidValue;  // K up to 3072 fits
   auto kern = gemm_q8_dp4a_kernel<TGM, EPI>;
   int sms = 148;
@@ -298,7 +287,7 @@ cudaError_t launch_dp(const __half* a, const int8_t* wl, const float* ws, int M,
   // ceil(n_tiles / groups) weight tiles, so the activation codes are staged
   // once per that many tiles
   const int m_tiles = (M + TM - 1) / TM, n_tiles = N / TN;
-  const int want = (kDpCtasPerSm * sms + m_tiles - 1) / m_tiles;
+  const int want = (kDpCtasPerSm * sms) / m_tiles;  // at most one wave of CTAs
   const int per = (n_tiles + (want < 1 ? 1 : want) - 1) / (want < 1 ? 1 : want);
   const int gx = (n_tiles + per - 1) / per;
   const dim3 grid((unsigned)gx, (unsigned)m_tiles);
