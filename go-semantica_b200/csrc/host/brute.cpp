@@ -17,6 +17,9 @@ struct sem_index {
   std::vector<int32_t> ids;
   std::unordered_map<int32_t, int64_t> id_to_row;
   sem::DevBuf qin, qprep, cand, out, qthr;
+  // int16 rows as byte planes (high bytes, then low bytes) for the tensor-core
+  // scan, built at the first exact search; query planes per call
+  sem::DevBuf planes, qplanes;
 };
 
 namespace sem {
@@ -69,6 +72,33 @@ int search_keys(sem_index* x, const void* d_queries, int nq, int k, int mode, in
                 cudaStream_t st) {
   if (mode == SEM_SEARCH_EXACT && x->quant == 0)
     return set_error(SEM_EINVAL, "brute: exact search needs an int8 or int16 index");
+  const int plane_bytes = ((x->dim + 15) / 16) * 16;
+  if (mode == SEM_SEARCH_EXACT && x->quant == 2 && scan_exact_tc16_supported(x->dim, plane_bytes, k)) {
+    // int16 rows: the tensor-core scan on byte planes (exact int32 scores)
+    const size_t cplane = (size_t)x->count * plane_bytes, qplane = (size_t)nq * plane_bytes;
+    if (!x->planes.p) {
+      SEM_CUDA(x->planes.ensure(2 * cplane));
+      SEM_CUDA(launch_split_int16(x->data.p, x->count, x->dim, x->row_bytes, plane_bytes, x->planes.p,
+                                  x->planes.as<uint8_t>() + cplane, st));
+    }
+    SEM_CUDA(x->qplanes.ensure(2 * qplane > 0 ? 2 * qplane : 16));
+    SEM_CUDA(launch_split_int16(d_queries, nq, x->dim, x->row_bytes, plane_bytes, x->qplanes.p,
+                                x->qplanes.as<uint8_t>() + qplane, st));
+    const TcScanPlan tp = plan_scan_exact_tc(x->count, nq);
+    const size_t need = (size_t)nq * tp.n_parts * k * sizeof(uint64_t);
+    SEM_CUDA(x->cand.ensure(need > 0 ? need : 8));
+    SEM_CUDA(x->qthr.ensure((size_t)(nq > 0 ? nq : 1) * 4));
+    SEM_CUDA(cudaMemsetAsync(x->qthr.p, 0, (size_t)nq * 4, st));
+    uint64_t* cand = x->cand.as<uint64_t>();
+    cudaError_t e = launch_scan_exact_tc16(x->planes.p, x->planes.as<uint8_t>() + cplane, x->count, plane_bytes,
+                                           x->qplanes.p, x->qplanes.as<uint8_t>() + qplane, nq, k, tp, row_base, cand,
+                                           x->qthr.as<uint32_t>(), nullptr, st);
+    if (e != cudaSuccess) return set_error(SEM_EDEVICE, "scan: %s", cudaGetErrorString(e));
+    e = launch_topk_merge(cand, tp.n_parts, k, (int64_t)tp.n_parts * k, nq, k, k, false, 2, nullptr, nullptr, nullptr,
+                          d_keys, st);
+    if (e != cudaSuccess) return set_error(SEM_EDEVICE, "merge: %s", cudaGetErrorString(e));
+    return SEM_OK;
+  }
   if (mode == SEM_SEARCH_EXACT && scan_exact_tc_supported(elem_size(x->quant), x->row_bytes, k, x->data.p, d_queries)) {
     // int8 rows: the tensor-core scan (exact int32 scores)
     const TcScanPlan tp = plan_scan_exact_tc(x->count, nq);

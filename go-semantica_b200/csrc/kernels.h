@@ -209,6 +209,20 @@ cudaError_t launch_scan_exact_tc(const void* corpus, int64_t count, int row_byte
                                  TcScanPlan plan, int64_t row_base, uint64_t* cand, uint32_t* qthr, uint32_t* err,
                                  cudaStream_t stream);
 
+// Exact int16 scan on the tensor cores (search_tc.cu): rows and queries as
+// byte planes (launch_split_int16) of plane_bytes per row (>= 128, a multiple
+// of 16, at most 768); k <= 16; plan.rows_per_part a multiple of 64 (as
+// plan_scan_exact_tc gives). Same candidate output as launch_scan_exact_tc.
+bool scan_exact_tc16_supported(int dim, int plane_bytes, int k);
+cudaError_t launch_scan_exact_tc16(const void* corpus_hi, const void* corpus_lo, int64_t count, int plane_bytes,
+                                   const void* q_hi, const void* q_lo, int nq, int k, TcScanPlan plan,
+                                   int64_t row_base, uint64_t* cand, uint32_t* qthr, uint32_t* err,
+                                   cudaStream_t stream);
+// int16 codes (rows src_row_bytes apart) -> a signed high-byte plane and an
+// unsigned low-byte plane of plane_bytes per row, zero padded past dim.
+cudaError_t launch_split_int16(const void* src, int64_t rows, int dim, int src_row_bytes, int plane_bytes, void* hi,
+                               void* lo, cudaStream_t stream);
+
 // Row-wise normalize (optional) + quantize (quant 1/2) or copy (quant 0) into
 // rows of out_row_bytes (zero padded).
 cudaError_t launch_normalize_quantize(const float* in, int64_t count, int dim, int quant, int out_row_bytes,

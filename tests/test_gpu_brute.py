@@ -224,3 +224,49 @@ def test_sharded_index_single_rank(ctx, row_base):
         np.testing.assert_array_equal(scores.cpu().numpy(), want_scores)
     finally:
         si.close()
+
+
+@pytest.mark.parametrize("dim", [768, 256, 200, 128])
+def test_tensor_core_int16_scan(ctx, dim):
+    # int16 rows with D in [113, 768] take the tensor-core scan on byte planes
+    # (high byte signed, low byte unsigned, four kind::i8 products recombined
+    # exactly in int32): several corpus parts of 64-row tiles, three 128-query
+    # tiles, a partial last K box (D = 200), duplicated rows in different
+    # parts, and sign-extreme codes (+-32767: high byte -128 or 127)
+    n, nq, k = 70000, 300, 16
+    codes = oracle.quantize_int16_vec(unit_rows(51 + dim, n, dim))
+    for a, b in ((5, 60001), (130, 131), (1000, 40000)):
+        codes[b] = codes[a]
+    e0 = np.zeros(dim, dtype=np.float32)
+    e0[0] = 1.0
+    codes[77] = oracle.quantize_int16_vec(e0[None])[0]       # [32767, 0, ...]
+    codes[78] = oracle.quantize_int16_vec(-e0[None])[0]      # [-32767, 0, ...]
+    q = oracle.quantize_int16_vec(unit_rows(52 + dim, nq, dim))
+    q[0] = codes[5]
+    q[1] = codes[130]
+    q[2] = codes[77]
+    q[3] = codes[78]
+    idx = brute.Index.from_codes(ctx, codes)
+    import ctypes
+    import torch
+    import _lib
+    lib = _lib.load()
+    d_q = torch.from_numpy(q).cuda()
+    keys = torch.zeros((nq, k), dtype=torch.int64, device="cuda")
+    rows = torch.empty((nq, k), dtype=torch.int32, device="cuda")
+    scores = torch.empty((nq, k), dtype=torch.int32, device="cuda")
+    torch.cuda.synchronize()
+    rrows, rscores, _ = oracle.search_exact_batch(2, codes, q, k, nthreads=8)
+    for _ in range(2):  # the second search reuses the byte planes built by the first
+        _lib.check(lib.sem_index_search_keys(idx.handle, ctypes.c_void_p(d_q.data_ptr()), nq, k, 1, 0,
+                                             ctypes.c_void_p(keys.data_ptr()), None))
+        _lib.check(lib.sem_topk_merge(ctx.handle, ctypes.c_void_p(keys.data_ptr()), 1, nq, k, k, 1, 2,
+                                      ctypes.c_void_p(rows.data_ptr()), ctypes.c_void_p(scores.data_ptr()),
+                                      None, ctypes.c_void_p(ctx.stream)))
+        torch.cuda.synchronize()
+        np.testing.assert_array_equal(scores.cpu().numpy(), rscores)
+        np.testing.assert_array_equal(rows.cpu().numpy(), rrows)
+    assert rrows[0, 0] == 5 and rrows[0, 1] == 60001
+    assert rrows[2, 0] == 77 and rscores[2, 0] == 32767 * 32767
+    assert rrows[3, 0] == 78 and rscores[3, 0] == 32767 * 32767
+    idx.close()
