@@ -72,5 +72,24 @@ def build(force: bool = False) -> str:
     return LIB
 
 
+TEST_SRC = os.path.join(ROOT, "tests", "kernels", "test_kernels.cu")
+TEST_LIB = os.path.join(ROOT, "tests", "_build", "libsemantica_testkernels.so")
+
+
+def build_test_kernels(force: bool = False) -> str:
+    """The tests' kernel library (tests/kernels/test_kernels.cu): the product's
+    device helpers applied element by element, and a bounded pipeline wait
+    that nothing completes. Test infrastructure; the product never links it."""
+    deps = [TEST_SRC] + [os.path.join(CSRC, h) for h in HEADERS]
+    if force or not os.path.exists(TEST_LIB) or any(os.path.getmtime(d) > os.path.getmtime(TEST_LIB) for d in deps):
+        os.makedirs(os.path.dirname(TEST_LIB), exist_ok=True)
+        cmd = [NVCC] + NVCC_FLAGS + ["-shared", TEST_SRC, "-o", TEST_LIB]
+        r = subprocess.run(cmd, capture_output=True, text=True)
+        if r.returncode != 0:
+            raise RuntimeError(f"compile failed: {' '.join(cmd)}\n{r.stdout}\n{r.stderr}")
+    return TEST_LIB
+
+
 if __name__ == "__main__":
     print(build(force="--force" in sys.argv))
+    print(build_test_kernels(force="--force" in sys.argv))

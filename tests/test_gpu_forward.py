@@ -63,6 +63,33 @@ def test_config1_batch_8x64(gpu_model, oracle_model):
         np.testing.assert_array_equal(got[i], oracle_model.forward_with_dim(ids[offs[i]:offs[i + 1]], 768))
 
 
+def test_full_vocabulary_model(ctx):
+    # The model as the bench loads it: the full 262144-row token embedding
+    # (ids drawn over the whole vocabulary, the highest rows included), short
+    # sequences bit-exact and a long one within north_star's bound
+    import oracle
+    import runtime
+    path = synth.cached_gguf("/tmp/semantica_b200_bench", seed=1234)
+    m = runtime.load_model(path, ctx)
+    ref = oracle.OracleModel(path)
+    try:
+        V = m.config().vocab_size
+        assert V == 262144
+        ids, offs = synth.token_batch(919, [9, 64, 300], V)
+        ids[1] = V - 1
+        ids[offs[1] + 1] = V - 2
+        got = m.forward_batch(ids, offs, 768)
+        for i in range(3):
+            want = ref.forward_with_dim(ids[offs[i]:offs[i + 1]], 768)
+            if offs[i + 1] - offs[i] < 128:
+                np.testing.assert_array_equal(got[i], want)
+            else:
+                assert cosine(got[i], want) >= COS_MIN and float(np.abs(got[i] - want).max()) <= MAX_ABS
+    finally:
+        m.close()
+        ref.close()
+
+
 def test_short_sequences_bit_exact(gpu_model, oracle_model):
     # Every sequence shorter than 128 tokens: the CUDA-core projections
     # (dp4a partials in the VNNI lane order, 8 float32 lane accumulators, the
