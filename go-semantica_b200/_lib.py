@@ -34,6 +34,12 @@ class TensorView(C.Structure):
                 ("data", C.c_void_p), ("nbytes", C.c_uint64)]
 
 
+class FaithfulConfig(C.Structure):
+    """sem_faithful_config: the model-faithful mode (no reference counterpart)."""
+    _fields_ = [("sliding_window", C.c_int32), ("swa_pattern", C.c_int32), ("rope_base_swa", C.c_float),
+                ("dense_head", C.c_int32)]
+
+
 # name -> (restype, argtypes)
 _SIGNATURES = {
     "sem_last_error": (C.c_char_p, []),
@@ -50,6 +56,7 @@ _SIGNATURES = {
     "sem_embed_device": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int32, C.c_int32, C.c_void_p,
                                    C.c_void_p]),
     "sem_model_check": (C.c_int, [C.c_void_p]),
+    "sem_model_set_faithful": (C.c_int, [C.c_void_p, C.c_void_p]),
     "sem_model_profile": (C.c_int, [C.c_void_p, C.c_int32]),
     "sem_model_profile_read": (C.c_int, [C.c_void_p, C.POINTER(C.c_char_p), C.POINTER(C.c_float),
                                          C.POINTER(C.c_int32), C.c_int32, C.POINTER(C.c_int32)]),

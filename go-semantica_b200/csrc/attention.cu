@@ -126,7 +126,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     attention_tc_kernel(const __grid_constant__ CUtensorMap tm_qh, const __grid_constant__ CUtensorMap tm_ql,
                         const __grid_constant__ CUtensorMap tm_k1, const __grid_constant__ CUtensorMap tm_k2,
                         const __grid_constant__ CUtensorMap tm_v2, const __grid_constant__ CUtensorMap tm_out, int nh,
-                        float scale, SeqMeta meta, AttnTiles tiles, float* __restrict__ out,
+                        float scale, int hw, SeqMeta meta, AttnTiles tiles, float* __restrict__ out,
                         uint32_t* __restrict__ absmax, uint32_t* __restrict__ err) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
@@ -158,7 +158,15 @@ __global__ void __launch_bounds__(THREADS, 1)
   const int s_beg = meta.cu_seqlens[seq], s_end = meta.cu_seqlens[seq + 1];
   const int n_rows = min(QT, s_end - row0);
   const int n_keys = s_end - s_beg;
-  const int nkt = (n_keys + KT - 1) / KT;
+  // key tiles this query tile sees: all of them, or (a sliding-window layer,
+  // query rows see keys within hw positions) the tiles its rows' windows
+  // reach; every loop below walks nkt tiles from jlo
+  const int q_pos0 = row0 - s_beg;
+  const bool windowed = hw < n_keys;
+  const int jlo = windowed ? max(0, q_pos0 - hw) / KT : 0;
+  const int jhi = windowed ? min(n_keys - 1, q_pos0 + n_rows - 1 + hw) / KT : (n_keys - 1) / KT;
+  const int nkt = n_keys > 0 ? jhi - jlo + 1 : 0;
+  const int key0 = s_beg + jlo * KT;  // first key (token row) of tile 0 of the walk
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < NBAR; ++i) mbar_init(&bars[i], 1);
@@ -214,7 +222,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         return true;
       };
       for (int j = 0; ok && j < nkt; ++j) {
-        for (int h = 0; ok && h < 2; ++h) ok = load_slot(&tm_k1, false, s_beg + j * KT, 2 * h);
+        for (int h = 0; ok && h < 2; ++h) ok = load_slot(&tm_k1, false, key0 + j * KT, 2 * h);
         if (j == 0 && me == 0) {  // Q lo behind the first K tile: pass 1 does not need it
           mbar_arrive_expect_tx(qlofull, SMEM_Q / 2);
 #pragma unroll
@@ -228,9 +236,9 @@ __global__ void __launch_bounds__(THREADS, 1)
       }
       for (int j = 0; ok && j <= nkt; ++j) {
         if (j < nkt)
-          for (int db = 0; ok && db < 4; ++db) ok = load_slot(&tm_k2, true, s_beg + j * KT, db);
+          for (int db = 0; ok && db < 4; ++db) ok = load_slot(&tm_k2, true, key0 + j * KT, db);
         if (j >= 1)
-          for (int kq = 0; ok && kq < KT / VKEYS; ++kq) ok = load_slot(&tm_v2, true, s_beg + (j - 1) * KT + kq * VKEYS, 0);
+          for (int kq = 0; ok && kq < KT / VKEYS; ++kq) ok = load_slot(&tm_v2, true, key0 + (j - 1) * KT + kq * VKEYS, 0);
       }
       for (uint32_t j = it > (uint32_t)NSLOT ? it - NSLOT : 0; j < it; ++j)
         if ((j & 1) == me) mbar_wait_drain(&rfull[j % NSLOT], (j / NSLOT) & 1);
@@ -356,6 +364,10 @@ __global__ void __launch_bounds__(THREADS, 1)
     const int half = w >> 2;      // keys [64*half, 64*half + 64) of each tile; O columns [128*half, +128)
     const int r = q * 32 + lane;  // query row within the tile
     const uint32_t t_lane = tmem + ((uint32_t)(q * 32) << 16);
+    // key k (position within the sequence) counts for this row when it exists
+    // and, in a sliding-window layer, lies within hw positions of the row
+    const int qpos = q_pos0 + r;
+    auto key_ok = [&](int k) { return k < n_keys && (!windowed || (k >= qpos - hw && k <= qpos + hw)); };
     uint32_t sfill = 0;
     bool ok = true;
     auto wait_s = [&](uint32_t& col) {
@@ -386,8 +398,8 @@ __global__ void __launch_bounds__(THREADS, 1)
         if (lane == 0) mbar_arrive(&s1empty[b]);
 #pragma unroll
         for (int c = 0; c < 64; ++c) {
-          const int key = j * KT + half * 64 + c;
-          if (key < n_keys) m = fmaxf(m, __fmul_rn(__uint_as_float(s[c >> 4][c & 15]), scale));
+          const int key = (jlo + j) * KT + half * 64 + c;
+          if (key_ok(key)) m = fmaxf(m, __fmul_rn(__uint_as_float(s[c >> 4][c & 15]), scale));
         }
       } else {
         tc_fence_before();
@@ -414,16 +426,16 @@ __global__ void __launch_bounds__(THREADS, 1)
         tmem_wait_regs(s[0]);
         reg_barrier16(s[1]);
         uint32_t ph[16], pl[16];  // 32 keys as packed fp16 pairs
-        const int kbase = j * KT + half * 64 + sub * 32;
+        const int kbase = (jlo + j) * KT + half * 64 + sub * 32;
 #pragma unroll
         for (int c = 0; c < 32; c += 2) {
           // score *= scale (attention.go:300), then fastExp(score - max)
           const uint64_t sc = mul2(pack2u(s[c >> 4][c & 15], s[c >> 4][(c & 15) + 1]), scale2);
           uint64_t p2 = fast_exp_ref2(add2(sc, negm2));
-          if (kbase + c + 1 >= n_keys) {  // keys past the sequence end weigh nothing
+          if (windowed || kbase + c + 1 >= n_keys) {  // keys past the sequence end or the window weigh nothing
             float a, b;
             unpack2(p2, a, b);
-            p2 = pack2(kbase + c < n_keys ? a : 0.0f, 0.0f);
+            p2 = pack2(key_ok(kbase + c) ? a : 0.0f, key_ok(kbase + c + 1) ? b : 0.0f);
           }
           l2 = add2(l2, p2);
           float a, b;
@@ -613,8 +625,8 @@ std::mutex g_attn_mu;
 }  // namespace
 
 cudaError_t launch_attention(const __half* qh, const __half* ql, const __half* kh, const __half* kl, const __half* vh,
-                             const __half* vl, int num_heads, float scale, SeqMeta meta, AttnTiles tiles, float* out,
-                             uint32_t* absmax, uint32_t* err, cudaStream_t stream) {
+                             const __half* vl, int num_heads, float scale, int half_window, SeqMeta meta,
+                             AttnTiles tiles, float* out, uint32_t* absmax, uint32_t* err, cudaStream_t stream) {
   if (tiles.n_tiles == 0) return cudaSuccess;
   const int64_t T = meta.T;
   CUtensorMap m_qh, m_ql, m_k1, m_k2, m_v2, m_out;
@@ -653,8 +665,9 @@ cudaError_t launch_attention(const __half* qh, const __half* ql, const __half* k
     }
   }
   dim3 grid(tiles.n_tiles * num_heads);
-  attention_tc_kernel<<<grid, THREADS, SMEM_BYTES, stream>>>(m_qh, m_ql, m_k1, m_k2, m_v2, m_out, num_heads, scale, meta,
-                                                             tiles, out, absmax, err);
+  const int hw = half_window > 0 && half_window < (1 << 24) ? half_window : (1 << 24);
+  attention_tc_kernel<<<grid, THREADS, SMEM_BYTES, stream>>>(m_qh, m_ql, m_k1, m_k2, m_v2, m_out, num_heads, scale, hw,
+                                                             meta, tiles, out, absmax, err);
   return cudaGetLastError();
 }
 

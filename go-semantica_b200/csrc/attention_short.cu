@@ -50,7 +50,7 @@ __device__ __forceinline__ float group_hsum8(float v) {
 
 __global__ void __launch_bounds__(kAsThreads, 1)
     attention_short_kernel(const float* __restrict__ qkv, int nh, float scale, const int32_t* __restrict__ cu,
-                           const int32_t* __restrict__ tile_seq, int max_len, float* __restrict__ out,
+                           const int32_t* __restrict__ tile_seq, int max_len, int hw, float* __restrict__ out,
                            uint32_t* __restrict__ absmax) {
   extern __shared__ __align__(16) float as_smem[];
   float* KV = as_smem;                    // K [L][8][kKLane], then V [L][256]
@@ -125,32 +125,35 @@ __global__ void __launch_bounds__(kAsThreads, 1)
     cp_async16(KV + (p >> 6) * kHd + 4 * (p & 63), vbase + (size_t)(p >> 6) * ld + 4 * (p & 63), true);
   cp_async_commit();
 
-  // ---- softmax, one warp per row ----
+  // ---- softmax, one warp per row, over the row's keys [lo, hi]: every key,
+  // or in a sliding-window layer those within hw positions, as one
+  // contiguous row of their own (keys outside weigh nothing) ----
   for (int r = warp; r < kAsQ; r += kAsThreads / 32) {
     if (r >= nq) {  // rows past the sequence contribute nothing
       for (int j = lane; j < L; j += 32) Pt[j * kAsQ + r] = 0.0f;
       continue;
     }
+    const int qpos = q0 + r;
+    const int lo = max(0, qpos - hw), hi = min(L - 1, qpos + hw), n = hi - lo + 1;
     float* row = S + r * 128;
     float mx = -INFINITY;
-    for (int j = lane; j < L; j += 32) mx = fmaxf(mx, row[j]);
+    for (int j = lo + lane; j <= hi; j += 32) mx = fmaxf(mx, row[j]);
     mx = warp_max(mx);
-    for (int j = lane; j < L; j += 32) row[j] = fast_exp_ref(__fsub_rn(row[j], mx));
+    for (int j = lo + lane; j <= hi; j += 32) row[j] = fast_exp_ref(__fsub_rn(row[j], mx));
     __syncwarp();
-    const int ng = L / 4;  // groups of four (at most 31: one per lane)
+    const int ng = n / 4;  // groups of four (at most 31: one per lane)
     float t = 0.0f;
-    if (lane < ng)
-      t = __fadd_rn(__fadd_rn(__fadd_rn(row[4 * lane], row[4 * lane + 1]), row[4 * lane + 2]), row[4 * lane + 3]);
+    if (lane < ng) {
+      const float* g4 = row + lo + 4 * lane;
+      t = __fadd_rn(__fadd_rn(__fadd_rn(g4[0], g4[1]), g4[2]), g4[3]);
+    }
     float sum = 0.0f;
     for (int k = 0; k < ng; ++k) sum = __fadd_rn(sum, __shfl_sync(0xffffffffu, t, k));
-    for (int k = 4 * ng; k < L; ++k) sum = __fadd_rn(sum, row[k]);
-    if (sum == 0.0f) {
-      const float u = __fdiv_rn(1.0f, (float)L);
-      for (int j = lane; j < L; j += 32) Pt[j * kAsQ + r] = u;
-    } else {
-      const float inv = __fdiv_rn(1.0f, sum);
-      for (int j = lane; j < L; j += 32) Pt[j * kAsQ + r] = __fmul_rn(row[j], inv);
-    }
+    for (int k = lo + 4 * ng; k <= hi; ++k) sum = __fadd_rn(sum, row[k]);
+    const float u = sum == 0.0f ? __fdiv_rn(1.0f, (float)n) : 0.0f;
+    const float inv = sum == 0.0f ? 0.0f : __fdiv_rn(1.0f, sum);
+    for (int j = lane; j < L; j += 32)
+      Pt[j * kAsQ + r] = (j < lo || j > hi) ? 0.0f : (sum == 0.0f ? u : __fmul_rn(row[j], inv));
   }
   cp_async_wait<0>();
   __syncthreads();
@@ -196,8 +199,8 @@ __global__ void __launch_bounds__(kAsThreads, 1)
 
 }  // namespace
 
-cudaError_t launch_attention_short(const float* qkv, int num_heads, float scale, SeqMeta meta, AttnTiles tiles,
-                                   int max_len, float* out, uint32_t* absmax, cudaStream_t stream) {
+cudaError_t launch_attention_short(const float* qkv, int num_heads, float scale, int half_window, SeqMeta meta,
+                                   AttnTiles tiles, int max_len, float* out, uint32_t* absmax, cudaStream_t stream) {
   if (tiles.n_tiles == 0) return cudaSuccess;
   if (num_heads < 1 || num_heads > 3 || !qkv || !out || !meta.cu_seqlens || !tiles.tile_seq || max_len < 1 ||
       max_len > kAsMaxKeys)
@@ -219,8 +222,9 @@ cudaError_t launch_attention_short(const float* qkv, int num_heads, float scale,
   }
   const int64_t grid = (int64_t)tiles.n_tiles * num_heads * kAsQBlocks;
   const int smem = (as_kv_words(max_len) + kAsSPWords) * 4;
+  const int hw = half_window > 0 && half_window < kAsMaxKeys ? half_window : kAsMaxKeys;
   attention_short_kernel<<<(unsigned)grid, kAsThreads, smem, stream>>>(qkv, num_heads, scale, meta.cu_seqlens,
-                                                                      tiles.tile_seq, max_len, out, absmax);
+                                                                      tiles.tile_seq, max_len, hw, out, absmax);
   return cudaGetLastError();
 }
 

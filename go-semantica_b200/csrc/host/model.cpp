@@ -67,6 +67,15 @@ struct sem_model {
   cudaGraphExec_t fwd_graph = nullptr;
   std::vector<const void*> fwd_graph_key;
   bool graphs_off = false;  // a capture failed here: forwards run without a graph
+  // model-faithful mode (sem_model_set_faithful): sliding-window layers, their
+  // RoPE tables, the dense 2/3 head (weights loaded when the file has them)
+  sem_faithful_config faithful{};
+  uint32_t faithful_gen = 0;  // changes with the mode: cached graphs are re-captured
+  sem::DevBuf rope_swa;       // cos then sin tables of the sliding layers' base
+  sem::DevBuf dense_buf;      // dense_2 and dense_3 in every projection layout
+  sem::Q8Proj dense2{}, dense3{};
+  int32_t dense_mid = 0;      // dense_2 output width
+  sem::DevBuf head_y1, head_codes, head_absmax;
 };
 
 
@@ -250,6 +259,47 @@ int model_load(sem_context* ctx, const sem_model_config* cfg_in, const sem_tenso
       if ((rc = upload_q8_proj(ctx, staging, t, (int64_t)q.rows, (int)q.k, *q.w, q.roff))) return rc;
     }
   }
+  // ---- the dense head (not read by the reference; the model-faithful mode's) ----
+  {
+    const sem_tensor_view* t2 = find_view(tv, nt, "dense_2.weight");
+    const sem_tensor_view* t3 = find_view(tv, nt, "dense_3.weight");
+    if (t2 && t3 && t2->dtype == kQ8 && t3->dtype == kQ8 && t2->n_dims >= 2 && t3->n_dims >= 2 &&
+        t2->dims[0] == (uint64_t)H && t3->dims[1] == (uint64_t)H && t3->dims[0] == t2->dims[1] &&
+        t2->dims[1] % 128 == 0) {
+      const int64_t mid = (int64_t)t2->dims[1];
+      size_t doff = 0;
+      auto dtake = [&](size_t bytes) {
+        size_t o = doff;
+        doff = align256(doff + bytes);
+        return o;
+      };
+      struct DOff { size_t codes, scales, hi, rsc, lanes; };
+      auto dproj = [&](int64_t rows, int64_t k) {
+        DOff p;
+        p.codes = dtake((size_t)rows * k * 2);
+        p.scales = dtake((size_t)rows * (k / 32) * 4);
+        p.hi = dtake((size_t)2 * rows * k * 2);
+        p.rsc = dtake((size_t)rows * 4);
+        p.lanes = dtake((size_t)rows * k);
+        return p;
+      };
+      const DOff o2 = dproj(mid, H), o3 = dproj(H, mid);
+      e = m->dense_buf.ensure(doff);
+      if (e != cudaSuccess) return set_error(SEM_ENOMEM, "device allocation of %zu bytes failed: %s", doff, cudaGetErrorString(e));
+      uint8_t* db = m->dense_buf.as<uint8_t>();
+      auto mk = [&](const DOff& p, int64_t rows, int64_t k) {
+        return Q8Proj{reinterpret_cast<const __half*>(db + p.codes), reinterpret_cast<const float*>(db + p.scales),
+                      reinterpret_cast<const __half*>(db + p.hi),
+                      reinterpret_cast<const __half*>(db + p.hi + (size_t)rows * k * 2),
+                      reinterpret_cast<const float*>(db + p.rsc), reinterpret_cast<const int8_t*>(db + p.lanes)};
+      };
+      m->dense2 = mk(o2, mid, H);
+      m->dense3 = mk(o3, H, mid);
+      if ((rc = upload_q8_proj(ctx, staging, t2, mid, H, m->dense2, 0))) return rc;
+      if ((rc = upload_q8_proj(ctx, staging, t3, H, (int)mid, m->dense3, 0))) return rc;
+      m->dense_mid = (int32_t)mid;
+    }
+  }
   // ---- RoPE tables (rope_cache.go:15-44) ----
   {
     const int half = hd / 2;
@@ -287,7 +337,7 @@ int ensure_workspace(sem_model* m, int64_t T, int B, int64_t out_floats) {
   SEM_CUDA(m->inv_rms.ensure((size_t)Tp * 4));
   // meta: row_seq[T], row_pos[T], cu[B+1], tile_seq/tile_row0[2*(T/64+B)], out_dims[B], out_off (int64) [B],
   // src_row[T]
-  size_t meta_ints = (size_t)3 * Tp + (B + 1) + 2 * ((size_t)Tp / 64 + B + 1) + B + 2 * (size_t)B + 10;
+  size_t meta_ints = (size_t)3 * Tp + (B + 1) + 2 * ((size_t)Tp / 64 + B + 1) + B + 2 * (size_t)B + B + 10;
   SEM_CUDA(m->meta.ensure(meta_ints * 4));
   SEM_CUDA(m->absmax.ensure((size_t)(4 * c.num_layers + 1) * (B > 0 ? B : 1) * 4));
   SEM_CUDA(m->ids.ensure((size_t)Tp * 4));
@@ -295,6 +345,11 @@ int ensure_workspace(sem_model* m, int64_t T, int B, int64_t out_floats) {
   // device error words: [0] bad token id seen by the embedding kernel, [1]
   // error bits of a timed-out pipeline wait. They accumulate over forwards
   // until a host read (sem_embed, sem_model_check) clears them.
+  if (m->faithful.dense_head) {
+    SEM_CUDA(m->head_y1.ensure((size_t)(B > 0 ? B : 1) * m->dense_mid * 4));
+    SEM_CUDA(m->head_codes.ensure((size_t)(B > 0 ? B : 1) * m->dense_mid * 2));
+    SEM_CUDA(m->head_absmax.ensure((size_t)2 * (B > 0 ? B : 1) * 4));
+  }
   const bool new_flags = m->errflag.bytes < 16;
   SEM_CUDA(m->errflag.ensure(16));
   if (new_flags) SEM_CUDA(cudaMemsetAsync(m->errflag.p, 0, 16, m->ctx->stream));
@@ -308,6 +363,7 @@ struct MetaPtrs {
   int32_t short_max_len;  // longest short sequence
   int32_t* out_dims;
   int64_t* out_off;
+  const int32_t* iota;  // [B] 0, 1, ..., B - 1 (one quantisation scale per pooled row)
   int32_t* src_row;  // [T] caller's row of each packed row (valid when permuted)
   int64_t T_long;    // packed rows [0, T_long) belong to sequences of >= kSplitMinLen tokens
   bool permuted;     // the packed order differs from the caller's
@@ -345,6 +401,7 @@ int upload_meta(sem_model* m, const int32_t* offsets, int B, const int32_t* dims
   uintptr_t p = reinterpret_cast<uintptr_t>(d_src + T);
   p = (p + 7) & ~uintptr_t(7);
   int64_t* d_off = reinterpret_cast<int64_t*>(p);
+  int32_t* d_iota = reinterpret_cast<int32_t*>(d_off + B);
   bool same = (int)m->last_offsets.size() == B + 1 &&
               std::memcmp(m->last_offsets.data(), offsets, sizeof(int32_t) * (B + 1)) == 0 &&
               (int)m->last_dims.size() == B && std::memcmp(m->last_dims.data(), dims, sizeof(int32_t) * B) == 0;
@@ -368,7 +425,7 @@ int upload_meta(sem_model* m, const int32_t* offsets, int B, const int32_t* dims
       caller_off[s] = acc;
       acc += dims[s];
     }
-    size_t bytes = (size_t)(reinterpret_cast<uint8_t*>(d_off + B) - reinterpret_cast<uint8_t*>(base));
+    size_t bytes = (size_t)(reinterpret_cast<uint8_t*>(d_iota + B) - reinterpret_cast<uint8_t*>(base));
     HostBuf& hb = m->ctx->pinned;
     SEM_CUDA(cudaStreamSynchronize(m->ctx->stream));  // the pinned buffer may still feed an earlier copy
     SEM_CUDA(hb.ensure(bytes));
@@ -382,6 +439,8 @@ int upload_meta(sem_model* m, const int32_t* offsets, int B, const int32_t* dims
     int32_t* h_src = h_dims + B;
     int64_t* h_off = reinterpret_cast<int64_t*>(reinterpret_cast<uint8_t*>(h) +
                                                 (reinterpret_cast<uint8_t*>(d_off) - reinterpret_cast<uint8_t*>(base)));
+    int32_t* h_iota = reinterpret_cast<int32_t*>(h_off + B);
+    for (int s = 0; s < B; ++s) h_iota[s] = s;
     int32_t nt = 0, nt_long = 0, short_max = 0;
     int32_t r = 0;
     for (int s = 0; s < B; ++s) {
@@ -420,6 +479,7 @@ int upload_meta(sem_model* m, const int32_t* offsets, int B, const int32_t* dims
   mp->short_tiles = AttnTiles{d_tseq + m->n_tiles_long, d_trow + m->n_tiles_long, m->n_tiles - m->n_tiles_long};
   mp->out_dims = d_dims;
   mp->out_off = d_off;
+  mp->iota = d_iota;
   mp->src_row = d_src;
   mp->T_long = m->t_long;
   mp->permuted = m->permuted;
@@ -500,22 +560,31 @@ int run_forward(sem_model* m, const int32_t* d_ids, const MetaPtrs& mp, float* d
   // the first attention norm's codes; every later norm is quantized by the
   // residual kernel before it
   SEM_LAUNCH(kStQuant, launch_quantize(hid, inv, m->layers[0].attn_norm, H, sm, slot(0, 0), codes, st));
+  const sem_faithful_config& fa = m->faithful;
+  const float* swa_cos = m->rope_swa.p ? m->rope_swa.as<float>() : m->rope_cos;
+  const float* swa_sin = m->rope_swa.p ? m->rope_swa.as<float>() + (size_t)c.max_seq_len * (hd / 2) : m->rope_sin;
   for (int l = 0; l < L; ++l) {
     const LayerW& w = m->layers[l];
+    // model-faithful mode: sliding layers (all but every swa_pattern-th) see
+    // keys within sliding_window / 2 positions, with their own RoPE tables;
+    // otherwise every layer attends to every key (model_int8.go:500)
+    const bool sliding = fa.sliding_window > 0 && fa.swa_pattern > 0 && (l + 1) % fa.swa_pattern != 0;
+    const int hw = sliding ? fa.sliding_window / 2 : 0;
     // attention block (model_int8.go:191-210)
     SEM_LAUNCH(kStGemmQKV, q8(w.qkv, qkvN, H, slot(l, 0), big, qkvN, kEpiStore, nullptr));
-    SEM_LAUNCH(kStQKNormRope, launch_qk_norm_rope(big, w.q_norm, w.k_norm, m->rope_cos, m->rope_sin, c.norm_eps, nh,
-                                                  sm, qh, ql, kh, kl, vh, vl, exact_short ? mp.T_long : T, st));
+    SEM_LAUNCH(kStQKNormRope, launch_qk_norm_rope(big, w.q_norm, w.k_norm, sliding ? swa_cos : m->rope_cos,
+                                                  sliding ? swa_sin : m->rope_sin, c.norm_eps, nh, sm, qh, ql, kh, kl,
+                                                  vh, vl, exact_short ? mp.T_long : T, st));
     if (exact_short) {  // tensor cores for the long sequences' tiles, float32 CUDA cores for the short ones
       if (mp.tiles.n_tiles)
-        SEM_LAUNCH(kStAttention, launch_attention(qh, ql, kh, kl, vh, vl, nh, c.attention_scale, sm, mp.tiles, att,
-                                                  slot(l, 1), err, st));
+        SEM_LAUNCH(kStAttention, launch_attention(qh, ql, kh, kl, vh, vl, nh, c.attention_scale, hw, sm, mp.tiles,
+                                                  att, slot(l, 1), err, st));
       if (mp.short_tiles.n_tiles)
-        SEM_LAUNCH(kStAttnShort, launch_attention_short(big, nh, c.attention_scale, sm, mp.short_tiles,
+        SEM_LAUNCH(kStAttnShort, launch_attention_short(big, nh, c.attention_scale, hw, sm, mp.short_tiles,
                                                         mp.short_max_len, att, slot(l, 1), st));
     } else {
       const AttnTiles all{mp.tiles.tile_seq, mp.tiles.tile_row0, mp.tiles.n_tiles + mp.short_tiles.n_tiles};
-      SEM_LAUNCH(kStAttention, launch_attention(qh, ql, kh, kl, vh, vl, nh, c.attention_scale, sm, all, att,
+      SEM_LAUNCH(kStAttention, launch_attention(qh, ql, kh, kl, vh, vl, nh, c.attention_scale, hw, sm, all, att,
                                                 slot(l, 1), err, st));
     }
     SEM_LAUNCH(kStQuant, launch_quantize(att, nullptr, nullptr, H, sm, slot(l, 1), codes, st));
@@ -530,6 +599,26 @@ int run_forward(sem_model* m, const int32_t* d_ids, const MetaPtrs& mp, float* d
     const float* next_w = last ? m->out_norm : m->layers[l + 1].attn_norm;
     SEM_LAUNCH(kStResidual, launch_residual_norm(att, w.post_ffw, hid, next_w ? next_w : w.ffn_norm, H, c.norm_eps, sm, inv,
                                                  last ? nullptr : slot(l + 1, 0), last ? nullptr : codes, st));
+  }
+  if (fa.dense_head) {
+    // model-faithful head: output_norm + mean pool of every channel, dense_2
+    // then dense_3 (each input quantised per sequence like every projection,
+    // on the kernel in the reference's VNNI order), then the first dims and L2
+    const int mid = m->dense_mid;
+    float* pooled = att;  // [B][H]
+    float* y1 = m->head_y1.as<float>();
+    __half* hc = m->head_codes.as<__half>();
+    uint32_t* ha = m->head_absmax.as<uint32_t>();
+    SEM_LAUNCH(kStPool, launch_pool_l2(hid, m->out_norm ? inv : nullptr, m->out_norm, H, sm, nullptr, nullptr, pooled,
+                                       st));
+    SEM_LAUNCH(kStPool, launch_quantize_rows(pooled, B, H, ha, hc, st));
+    SEM_LAUNCH(kStPool, launch_gemm_q8_dp4a(hc, m->dense2.lanes, m->dense2.scales, B, mid, H, ha, mp.iota, y1,
+                                            kEpiStore, nullptr, st));
+    SEM_LAUNCH(kStPool, launch_quantize_rows(y1, B, mid, ha + B, hc, st));
+    SEM_LAUNCH(kStPool, launch_gemm_q8_dp4a(hc, m->dense3.lanes, m->dense3.scales, B, H, mid, ha + B, mp.iota, pooled,
+                                            kEpiStore, nullptr, st));
+    SEM_LAUNCH(kStPool, launch_l2_rows(pooled, B, H, mp.out_dims, mp.out_off, d_out, st));
+    return SEM_OK;
   }
   // output_norm + mean pool + L2 (model_int8.go:235-255)
   SEM_LAUNCH(kStPool, launch_pool_l2(hid, m->out_norm ? inv : nullptr, m->out_norm, H, sm, mp.out_dims, mp.out_off, d_out, st));
@@ -557,7 +646,8 @@ int forward_maybe_graph(sem_model* m, const MetaPtrs& mp, cudaStream_t st) {
   const std::vector<const void*> key = {m->hid.p,    m->big.p,   m->att.p, m->codes.p, m->halves.p,
                                         m->inv_rms.p, m->meta.p,  m->absmax.p, m->ids.p, m->out.p,
                                         m->errflag.p, reinterpret_cast<const void*>((intptr_t)get_q8_path()),
-                                        static_cast<const void*>(st)};
+                                        static_cast<const void*>(st),
+                                        reinterpret_cast<const void*>((intptr_t)m->faithful_gen), m->head_y1.p};
   if (!mp.same_shape || !m->fwd_graph || key != m->fwd_graph_key) {
     drop_graph(m);
     // A capture that the runtime refuses (the kernels were recorded, not run)
@@ -642,6 +732,40 @@ int model_embed(sem_model* m, const int32_t* ids, const int32_t* offsets, int32_
   SEM_CUDA(cudaMemsetAsync(m->errflag.p, 0, 8, ctx->stream));
   SEM_CUDA(cudaStreamSynchronize(ctx->stream));
   if (flags[1]) return set_error(SEM_EDEVICE, "forward: a tensor-core pipeline wait timed out (error bits 0x%x)", flags[1]);
+  return SEM_OK;
+}
+
+int model_set_faithful(sem_model* m, const sem_faithful_config* f) {
+  if (!m) return set_error(SEM_EINVAL, "null argument");
+  sem_faithful_config cfg{};
+  if (f) cfg = *f;
+  if (cfg.sliding_window < 0 || cfg.swa_pattern < 0 || cfg.rope_base_swa < 0.0f)
+    return set_error(SEM_EINVAL, "faithful mode: negative sliding_window, swa_pattern or rope_base_swa");
+  if (cfg.dense_head && !m->dense_mid)
+    return set_error(SEM_EINVAL, "faithful mode: the model has no dense_2.weight / dense_3.weight to apply");
+  sem_context* ctx = m->ctx;
+  DeviceGuard dg(ctx->device);
+  std::lock_guard<std::mutex> lk(ctx->mu);
+  SEM_CUDA(cudaStreamSynchronize(ctx->stream));
+  const sem_model_config& c = m->cfg;
+  m->rope_swa.release();
+  if (cfg.sliding_window > 0 && cfg.rope_base_swa > 0.0f && cfg.rope_base_swa != c.rope_base) {
+    // rope_cache.go:15-44 with the sliding layers' base
+    const int half = c.head_dim / 2;
+    std::vector<float> freqs(half), tab((size_t)2 * c.max_seq_len * half);
+    for (int i = 0; i < half; ++i)
+      freqs[i] = (float)(1.0 / std::pow((double)cfg.rope_base_swa, (double)(2 * i) / (double)c.head_dim));
+    for (int p = 0; p < c.max_seq_len; ++p)
+      for (int i = 0; i < half; ++i) {
+        const float theta = (float)p * freqs[i];
+        tab[(size_t)p * half + i] = (float)std::cos((double)theta);
+        tab[(size_t)c.max_seq_len * half + (size_t)p * half + i] = (float)std::sin((double)theta);
+      }
+    SEM_CUDA(m->rope_swa.ensure(tab.size() * 4));
+    SEM_CUDA(cudaMemcpy(m->rope_swa.p, tab.data(), tab.size() * 4, cudaMemcpyHostToDevice));
+  }
+  m->faithful = cfg;
+  ++m->faithful_gen;
   return SEM_OK;
 }
 
@@ -906,6 +1030,8 @@ int sem_embed_device(sem_model* m, const int32_t* d_ids, const int32_t* h_offset
 }
 
 int sem_model_check(sem_model* m) { return sem::model_check(m); }
+
+int sem_model_set_faithful(sem_model* m, const sem_faithful_config* cfg) { return sem::model_set_faithful(m, cfg); }
 
 int sem_q8_weight_create(sem_context* ctx, const void* w_q8, int32_t k_in, int32_t n_out, sem_q8_weight** out) {
   return sem::q8_weight_create(ctx, w_q8, k_in, n_out, out);

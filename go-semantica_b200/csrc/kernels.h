@@ -83,9 +83,20 @@ cudaError_t launch_residual_norm(const float* o, const float* post_w, float* hid
                                  cudaStream_t stream);
 
 // Mean pooling of the first out_dim[s] columns of (hidden * inv_rms) * w over
-// each sequence, then L2 normalisation; writes out + out_offset[s].
+// each sequence, then L2 normalisation; writes out + out_offset[s]. With
+// out_dims null: every column, no normalisation, sequence s at out + s * H.
 cudaError_t launch_pool_l2(const float* hidden, const float* inv_rms, const float* w, int H, SeqMeta meta,
                            const int32_t* out_dims, const int64_t* out_offsets, float* out, cudaStream_t stream);
+
+// Each of `rows` rows of K floats quantised as its own INT8 buffer
+// (QuantizeSymmetricINT8Into, quantize.go:29-69): absmax bit pattern into
+// absmax[row], codes (held as fp16) into codes[row][K]. K % 4 == 0.
+cudaError_t launch_quantize_rows(const float* x, int rows, int K, uint32_t* absmax, __half* codes,
+                                 cudaStream_t stream);
+// l2Normalize (model.go:808-820) of the first out_dims[r] values of each row
+// of x ([rows][K]) into out + out_offsets[r].
+cudaError_t launch_l2_rows(const float* x, int rows, int K, const int32_t* out_dims, const int64_t* out_offsets,
+                           float* out, cudaStream_t stream);
 
 // ---- Q8_0 x INT8 projection (gemm_q8.cu) ----
 enum GemmEpilogue { kEpiStore = 0, kEpiGeluUp = 1 };
@@ -157,19 +168,22 @@ struct AttnTiles {
 // q planes [T][num_heads][256], k and v planes [T][256] (fp16 hi/lo splits;
 // kl == kh + T * 256 and vl == vh + T * 256: the lo planes follow the hi ones),
 // all 16-byte aligned. out [T][num_heads*256] fp32, absmax[seq] atomically.
-// `err` (nullable) receives error bits if a pipeline wait times out.
+// half_window > 0: a sliding-window layer, query i sees keys j with
+// |i - j| <= half_window (0: every key). `err` (nullable) receives error bits
+// if a pipeline wait times out.
 cudaError_t launch_attention(const __half* qh, const __half* ql, const __half* kh, const __half* kl,
-                             const __half* vh, const __half* vl, int num_heads, float scale, SeqMeta meta,
-                             AttnTiles tiles, float* out, uint32_t* absmax, uint32_t* err, cudaStream_t stream);
+                             const __half* vh, const __half* vl, int num_heads, float scale, int half_window,
+                             SeqMeta meta, AttnTiles tiles, float* out, uint32_t* absmax, uint32_t* err,
+                             cudaStream_t stream);
 
 // Float32 attention of sequences shorter than 128 tokens in the reference's
 // order (attention_short.cu): qkv rows [q (nh*256) | k | v] float32 with q and
 // k normed and RoPE'd (launch_qk_norm_rope with f32_row0 at or below their
 // rows); `tiles` lists one 128-row tile per such sequence, max_len is the
-// longest of them (at most 127). out [T][nh*256], absmax[seq] atomically, as
-// launch_attention.
-cudaError_t launch_attention_short(const float* qkv, int num_heads, float scale, SeqMeta meta, AttnTiles tiles,
-                                   int max_len, float* out, uint32_t* absmax, cudaStream_t stream);
+// longest of them (at most 127). half_window as launch_attention. out
+// [T][nh*256], absmax[seq] atomically, as launch_attention.
+cudaError_t launch_attention_short(const float* qkv, int num_heads, float scale, int half_window, SeqMeta meta,
+                                   AttnTiles tiles, int max_len, float* out, uint32_t* absmax, cudaStream_t stream);
 
 // ---- brute search (brute_kernels.cu) ----
 // Exact integer scan: scores of nq queries against rows [0, count) of an

@@ -750,7 +750,8 @@ __global__ void pool_l2_kernel(const float* __restrict__ hidden, const float* __
   __shared__ float s_norm;
   int s = blockIdx.x;
   int r0 = meta.cu_seqlens[s], r1 = meta.cu_seqlens[s + 1];
-  int od = out_dims[s];
+  const bool l2 = out_dims != nullptr;  // else: every column, no normalisation (the dense head's input)
+  int od = l2 ? out_dims[s] : H;
   float scale = __fdiv_rn(1.0f, (float)(r1 - r0));
   for (int i = threadIdx.x; i < od; i += blockDim.x) {
     float acc = 0.0f;
@@ -763,6 +764,10 @@ __global__ void pool_l2_kernel(const float* __restrict__ hidden, const float* __
     pooled[i] = __fmul_rn(acc, scale);
   }
   __syncthreads();
+  if (!l2) {
+    for (int i = threadIdx.x; i < H; i += blockDim.x) out[(int64_t)s * H + i] = pooled[i];
+    return;
+  }
   if (threadIdx.x == 0) {
     float ss = 0.0f;
     for (int i = 0; i < od; ++i) ss = __fadd_rn(ss, __fmul_rn(pooled[i], pooled[i]));
@@ -772,6 +777,68 @@ __global__ void pool_l2_kernel(const float* __restrict__ hidden, const float* __
   float nrm = s_norm;
   float* dst = out + out_offsets[s];
   for (int i = threadIdx.x; i < od; i += blockDim.x) dst[i] = nrm == 0.0f ? pooled[i] : __fdiv_rn(pooled[i], nrm);
+}
+
+// One CTA per row: QuantizeSymmetricINT8Into (quantize.go:29-69) of the row
+// as one buffer: absmax, scale = absmax / 127, codes of the exact product.
+__global__ void quantize_rows_kernel(const float* __restrict__ x, int K, uint32_t* __restrict__ absmax,
+                                     __half* __restrict__ codes) {
+  __shared__ float s_red[32];
+  const int row = blockIdx.x;
+  const float* xr = x + (int64_t)row * K;
+  float m = 0.0f;
+  for (int i = threadIdx.x; i < K; i += blockDim.x) m = fmaxf(m, fabsf(xr[i]));
+  m = warp_max(m);
+  if ((threadIdx.x & 31) == 0) s_red[threadIdx.x >> 5] = m;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float v = threadIdx.x < (blockDim.x >> 5) ? s_red[threadIdx.x] : 0.0f;
+    v = warp_max(v);
+    if (threadIdx.x == 0) s_red[0] = v;
+  }
+  __syncthreads();
+  const uint32_t bits = __float_as_uint(s_red[0]);
+  if (threadIdx.x == 0) absmax[row] = bits;
+  float sc, inv;
+  seq_scale_ref(bits, &sc, &inv);
+  for (int i = 4 * threadIdx.x; i < K; i += 4 * blockDim.x) {
+    const uint2 c = quant_codes4(*reinterpret_cast<const float4*>(xr + i), inv);
+    *reinterpret_cast<uint2*>(codes + (int64_t)row * K + i) = c;
+  }
+}
+
+// l2Normalize (model.go:808-820) of a row prefix: float32 sum of squares in
+// order, v / float32(sqrt(float64(sum))), unchanged when the sum is 0.
+__global__ void l2_rows_kernel(const float* __restrict__ x, int K, const int32_t* __restrict__ out_dims,
+                               const int64_t* __restrict__ out_offsets, float* __restrict__ out) {
+  __shared__ float s_norm;
+  const int row = blockIdx.x, od = out_dims[row];
+  const float* xr = x + (int64_t)row * K;
+  if (threadIdx.x == 0) {
+    float ss = 0.0f;
+    for (int i = 0; i < od; ++i) ss = __fadd_rn(ss, __fmul_rn(xr[i], xr[i]));
+    s_norm = ss == 0.0f ? 0.0f : (float)sqrt((double)ss);
+  }
+  __syncthreads();
+  const float nrm = s_norm;
+  float* dst = out + out_offsets[row];
+  for (int i = threadIdx.x; i < od; i += blockDim.x) dst[i] = nrm == 0.0f ? xr[i] : __fdiv_rn(xr[i], nrm);
+}
+
+cudaError_t launch_quantize_rows(const float* x, int rows, int K, uint32_t* absmax, __half* codes,
+                                 cudaStream_t stream) {
+  if (rows == 0) return cudaSuccess;
+  if (K % 4 || (reinterpret_cast<uintptr_t>(x) & 15) || (reinterpret_cast<uintptr_t>(codes) & 7))
+    return cudaErrorInvalidValue;
+  quantize_rows_kernel<<<rows, 256, 0, stream>>>(x, K, absmax, codes);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_l2_rows(const float* x, int rows, int K, const int32_t* out_dims, const int64_t* out_offsets,
+                           float* out, cudaStream_t stream) {
+  if (rows == 0) return cudaSuccess;
+  l2_rows_kernel<<<rows, 256, 0, stream>>>(x, K, out_dims, out_offsets, out);
+  return cudaGetLastError();
 }
 
 cudaError_t launch_pool_l2(const float* hidden, const float* inv_rms, const float* w, int H, SeqMeta meta,

@@ -84,6 +84,14 @@ class Model:
         check(load().sem_embed_device(self.handle, C.c_void_p(d_ids_ptr), offsets.ctypes.data, n_seqs, dim,
                                       C.c_void_p(d_out_ptr), C.c_void_p(stream or None)))
 
+    def set_faithful(self, sliding_window: int = 0, swa_pattern: int = 0, rope_base_swa: float = 0.0,
+                     dense_head: bool = False) -> None:
+        """Model-faithful mode (sem_model_set_faithful; no reference
+        counterpart): sliding-window layers and the dense 2/3 head. All zero
+        restores the reference's forward."""
+        cfg = _lib.FaithfulConfig(sliding_window, swa_pattern, rope_base_swa, 1 if dense_head else 0)
+        check(load().sem_model_set_faithful(self.handle, C.byref(cfg)))
+
     def check(self) -> None:
         """Waits for the enqueued device-resident forwards and raises what the
         device recorded (a token id outside the vocabulary, a timed-out

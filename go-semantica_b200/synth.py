@@ -84,8 +84,13 @@ def q8_0_blocks(rng: np.random.Generator, rows: int, cols: int, chunk_rows: int 
 
 
 def write_gguf(path: str, seed: int = 1234, vocab_size: int | None = None, num_layers: int | None = None,
-               **overrides) -> str:
-    """Writes a synthetic EmbeddingGemma-shaped GGUF v3 file and returns its path."""
+               dense_head: bool = False, **overrides) -> str:
+    """Writes a synthetic EmbeddingGemma-shaped GGUF v3 file and returns its path.
+
+    dense_head adds the EmbeddingGemma dense head the reference does not read
+    (dense_2.weight: embed -> 4 embed, dense_3.weight: 4 embed -> embed, Q8_0,
+    drawn after every other tensor so the rest of the file is unchanged) and
+    the sliding-window metadata key (512 tokens), for the model-faithful mode."""
     cfg = dict(GEMMA_300M)
     if vocab_size is not None:
         cfg["vocab_size"] = vocab_size
@@ -125,6 +130,9 @@ def write_gguf(path: str, seed: int = 1234, vocab_size: int | None = None, num_l
         add_q8(p + "ffn_up.weight", H, F)
         add_q8(p + "ffn_down.weight", F, H)
         add_norm(p + "post_ffw_norm.weight", H)
+    if dense_head:
+        add_q8("dense_2.weight", H, 4 * H)
+        add_q8("dense_3.weight", 4 * H, H)
 
     tokens = ["<pad>", "<eos>", "<bos>", "<unk>"] + [f"t{i}" for i in range(4, V)]
     kv = [
@@ -139,6 +147,8 @@ def write_gguf(path: str, seed: int = 1234, vocab_size: int | None = None, num_l
         _kv_f32(f"{arch}.rope.freq_base", cfg["rope_base"]),
         _kv_str_array("tokenizer.ggml.tokens", tokens),
     ]
+    if dense_head:
+        kv.append(_kv_u32(f"{arch}.attention.sliding_window", 512))
     infos = []
     offset = 0
     for name, dt, dims, arr in tensors:
@@ -167,14 +177,14 @@ def write_gguf(path: str, seed: int = 1234, vocab_size: int | None = None, num_l
 
 
 def cached_gguf(directory: str, seed: int = 1234, vocab_size: int | None = None,
-                num_layers: int | None = None) -> str:
+                num_layers: int | None = None, dense_head: bool = False) -> str:
     """Path of a synthetic model in `directory`, written on first use."""
     v = vocab_size or GEMMA_300M["vocab_size"]
     l = num_layers or GEMMA_300M["num_layers"]
     os.makedirs(directory, exist_ok=True)
-    path = os.path.join(directory, f"synth-gemma-s{seed}-v{v}-l{l}.gguf")
+    path = os.path.join(directory, f"synth-gemma-s{seed}-v{v}-l{l}{'-dense' if dense_head else ''}.gguf")
     if not os.path.exists(path):
-        write_gguf(path, seed=seed, vocab_size=v, num_layers=l)
+        write_gguf(path, seed=seed, vocab_size=v, num_layers=l, dense_head=dense_head)
     return path
 
 

@@ -122,6 +122,30 @@ int sem_embed_device(sem_model *model, const int32_t *d_ids, const int32_t *h_of
  * reference validates ids on the host (model_int8.go:167-178). */
 int sem_model_check(sem_model *model);
 
+/* Model-faithful mode. The reference runs full bidirectional attention in
+ * every layer and has no dense head (model_int8.go:235-255, :500); the
+ * EmbeddingGemma architecture has both, and this mode restores them. It has
+ * no counterpart in the reference and is off by default (sem_embed computes
+ * the reference's forward).
+ *   sliding_window: in sliding layers query i sees keys j with
+ *     |i - j| <= sliding_window / 2 (0: every layer sees every key);
+ *   swa_pattern: layer l (0-based) is a global layer when (l + 1) % swa_pattern
+ *     == 0, a sliding layer otherwise (EmbeddingGemma: window 512, pattern 6);
+ *   rope_base_swa: RoPE base of the sliding layers (0: the model's rope_base);
+ *   dense_head: after output_norm and mean pooling of every channel, the
+ *     dense_2.weight (embed -> mid) and dense_3.weight (mid -> embed) Q8_0
+ *     projections, each input quantised per sequence like every projection of
+ *     the forward; then the first dims[s] outputs, L2-normalised. The weights
+ *     are read at load when the tensors are present. */
+typedef struct sem_faithful_config {
+  int32_t sliding_window, swa_pattern;
+  float rope_base_swa;
+  int32_t dense_head;
+} sem_faithful_config;
+/* cfg NULL (or all zero): the reference's forward. Errors: SEM_EINVAL for
+ * negative fields or a dense head the model has no weights for. */
+int sem_model_set_faithful(sem_model *model, const sem_faithful_config *cfg);
+
 /* Per-stage device timing of the forward pass (diagnostics; no reference
  * counterpart). enable != 0 brackets every kernel launch of later forwards
  * with CUDA events on the launching stream. profile_read synchronises the

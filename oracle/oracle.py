@@ -52,6 +52,8 @@ def lib():
         L.orc_model_load.argtypes = [C.c_char_p, C.c_char_p, C.c_int]
         L.orc_model_free.argtypes = [C.c_void_p]
         L.orc_model_config.argtypes = [C.c_void_p, C.c_void_p]
+        L.orc_model_set_faithful.restype = C.c_int
+        L.orc_model_set_faithful.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_float, C.c_int]
         L.orc_forward.restype = C.c_int
         L.orc_forward.argtypes = [C.c_void_p, i32p, C.c_int, C.c_int, f32p, C.c_char_p, C.c_int]
         L.orc_forward_batch.restype = C.c_int
@@ -164,6 +166,13 @@ class OracleModel:
         cfg = OracleConfig()
         lib().orc_model_config(self._h, C.byref(cfg))
         self.config = cfg
+
+    def set_faithful(self, sliding_window: int = 0, swa_pattern: int = 0, rope_base_swa: float = 0.0,
+                     dense_head: bool = False) -> None:
+        """Model-faithful mode (no reference counterpart): sliding-window
+        layers and the dense 2/3 head. Zeros restore the reference's forward."""
+        if lib().orc_model_set_faithful(self._h, sliding_window, swa_pattern, rope_base_swa, 1 if dense_head else 0):
+            raise ValueError("the model file has no dense_2 / dense_3 weights")
 
     def close(self):
         if self._h:

@@ -614,9 +614,36 @@ struct orc_model {
     const float *output_norm;
     orc_layer *layers;
     float *rope_cos, *rope_sin; /* [max_seq_len][head_dim/2] */
+    /* model-faithful extensions (orc_model_set_faithful; the reference has
+     * neither): sliding-window layers with their own RoPE tables, and the
+     * dense 2/3 head after pooling */
+    int swa_window, swa_pattern, dense_head;
+    float *rope_cos_swa, *rope_sin_swa;
+    const uint8_t *dense2, *dense3;
+    float *sd2, *sd3;
+    int dense_mid; /* dense_2 output width */
 };
 
 void orc_model_config(const orc_model *m, orc_config *out) { *out = m->cfg; }
+
+static void rope_tables(const orc_config *c, float base, float **cs, float **sn);
+
+/* Model-faithful mode (no reference counterpart; the reference runs full
+ * attention in every layer and has no dense head, model_int8.go:235-255,
+ * :500): sliding-window layers, their RoPE base, the dense 2/3 head. All
+ * zero: the reference's forward. Returns -1 if the head is asked for and the
+ * file has no dense_2/dense_3 weights. */
+int orc_model_set_faithful(orc_model *m, int swa_window, int swa_pattern, float rope_base_swa, int dense_head) {
+    if (dense_head && !(m->dense2 && m->dense3 && m->sd2 && m->sd3)) return -1;
+    m->swa_window = swa_window > 0 ? swa_window : 0;
+    m->swa_pattern = swa_pattern > 0 ? swa_pattern : 0;
+    m->dense_head = dense_head ? 1 : 0;
+    free(m->rope_cos_swa); free(m->rope_sin_swa);
+    m->rope_cos_swa = m->rope_sin_swa = NULL;
+    if (m->swa_window && rope_base_swa > 0.0f && rope_base_swa != m->cfg.rope_base)
+        rope_tables(&m->cfg, rope_base_swa, &m->rope_cos_swa, &m->rope_sin_swa);
+    return 0;
+}
 
 static const float *load_f32(const orc_gguf *g, const char *name) {
     const orc_tensor *t = gguf_find(g, name);
@@ -631,6 +658,25 @@ static const uint8_t *load_q8(const orc_gguf *g, const char *name, char *err, in
     const uint8_t *p = gguf_data(g, t);
     if (!p) seterr(err, errlen, "tensor data out of bounds: %s", name);
     return p;
+}
+
+/* NewRoPECache (rope_cache.go:15-44): cos/sin of float32(p) * float32 freq. */
+static void rope_tables(const orc_config *c, float base, float **cs, float **sn) {
+    int half = c->head_dim / 2;
+    *cs = (float *)malloc(sizeof(float) * (size_t)c->max_seq_len * half);
+    *sn = (float *)malloc(sizeof(float) * (size_t)c->max_seq_len * half);
+    float *freqs = (float *)malloc(sizeof(float) * half);
+    for (int i = 0; i < half; i++)
+        freqs[i] = (float)(1.0 / pow((double)base, (double)(2 * i) / (double)c->head_dim));
+    for (int p = 0; p < c->max_seq_len; p++) {
+        float pf = (float)p;
+        for (int i = 0; i < half; i++) {
+            float theta = pf * freqs[i];
+            (*cs)[(size_t)p * half + i] = (float)cos((double)theta);
+            (*sn)[(size_t)p * half + i] = (float)sin((double)theta);
+        }
+    }
+    free(freqs);
 }
 
 static float *scales_for(const uint8_t *w, int64_t bytes, int cols) {
@@ -651,6 +697,8 @@ void orc_model_free(orc_model *m) {
         free(m->layers);
     }
     free(m->rope_cos); free(m->rope_sin);
+    free(m->rope_cos_swa); free(m->rope_sin_swa);
+    free(m->sd2); free(m->sd3);
     free(m->g.tensors);
     if (m->map) munmap(m->map, m->maplen);
     free(m);
@@ -690,21 +738,23 @@ orc_model *orc_model_load(const char *path, char *err, int errlen) {
     if (!m->tok_embd) { orc_model_free(m); return NULL; }
     m->output_norm = load_f32(g, "output_norm.weight");
     /* NewRoPECache (rope_cache.go:15-44) */
-    int half = c->head_dim / 2;
-    m->rope_cos = (float *)malloc(sizeof(float) * (size_t)c->max_seq_len * half);
-    m->rope_sin = (float *)malloc(sizeof(float) * (size_t)c->max_seq_len * half);
-    float *freqs = (float *)malloc(sizeof(float) * half);
-    for (int i = 0; i < half; i++)
-        freqs[i] = (float)(1.0 / pow((double)c->rope_base, (double)(2 * i) / (double)c->head_dim));
-    for (int p = 0; p < c->max_seq_len; p++) {
-        float pf = (float)p;
-        for (int i = 0; i < half; i++) {
-            float theta = pf * freqs[i];
-            m->rope_cos[(size_t)p * half + i] = (float)cos((double)theta);
-            m->rope_sin[(size_t)p * half + i] = (float)sin((double)theta);
+    rope_tables(c, c->rope_base, &m->rope_cos, &m->rope_sin);
+    /* the dense head's weights, when the file has them (not read by the
+     * reference; used only in the model-faithful mode) */
+    {
+        const orc_tensor *t2 = gguf_find(g, "dense_2.weight"), *t3 = gguf_find(g, "dense_3.weight");
+        if (t2 && t3 && t2->dtype == 8 && t3->dtype == 8 && t2->ndim == 2 && t3->ndim == 2 &&
+            t2->dims[0] == (uint64_t)c->embed_dim && t3->dims[1] == (uint64_t)c->embed_dim &&
+            t3->dims[0] == t2->dims[1]) {
+            m->dense2 = gguf_data(g, t2);
+            m->dense3 = gguf_data(g, t3);
+            m->dense_mid = (int)t2->dims[1];
+            if (m->dense2 && m->dense3) {
+                m->sd2 = scales_for(m->dense2, (int64_t)t2->size, c->embed_dim);
+                m->sd3 = scales_for(m->dense3, (int64_t)t3->size, m->dense_mid);
+            }
         }
     }
-    free(freqs);
     /* loadLayerINT8 (model_int8.go:54-119) */
     m->layers = (orc_layer *)calloc((size_t)c->num_layers, sizeof(orc_layer));
     for (int l = 0; l < c->num_layers; l++) {
@@ -743,10 +793,10 @@ static void norm_rows(float *h, const float *w, int rows, int dim, float eps) {
 
 /* RoPE with cached tables (rope_cache.go:117-260, cached branch): NeoX pairs
  * (i, i+half) per head; layout [S][nHeads*headDim]. */
-static void rope_apply(const orc_model *m, float *qk, int S, int nHeads) {
+static void rope_apply(const orc_model *m, const float *tcos, const float *tsin, float *qk, int S, int nHeads) {
     int hd = m->cfg.head_dim, half = hd / 2;
     for (int s = 0; s < S; s++) {
-        const float *cs = m->rope_cos + (size_t)s * half, *sn = m->rope_sin + (size_t)s * half;
+        const float *cs = tcos + (size_t)s * half, *sn = tsin + (size_t)s * half;
         for (int h = 0; h < nHeads; h++) {
             float *x = qk + ((size_t)s * nHeads + h) * hd;
             for (int i = 0; i < half; i++) {
@@ -827,8 +877,15 @@ int orc_forward(const orc_model *m, const int32_t *ids, int S, int target_dim, f
                     float *p = k + (size_t)s * kvd + (size_t)h * hd;
                     orc_rmsnorm(p, p, L->k_norm, hd, c->norm_eps);
                 }
-        rope_apply(m, q, S, nh);
-        rope_apply(m, k, S, nkv);
+        /* model-faithful mode: sliding layers (all but every swa_pattern-th)
+         * see keys within swa_window / 2 positions and may use their own RoPE
+         * base; otherwise every layer attends to every key (model_int8.go:500) */
+        const int sliding = m->swa_window > 0 && m->swa_pattern > 0 && (l + 1) % m->swa_pattern != 0;
+        const int hw = sliding ? m->swa_window / 2 : S;
+        const float *tc = sliding && m->rope_cos_swa ? m->rope_cos_swa : m->rope_cos;
+        const float *ts = sliding && m->rope_sin_swa ? m->rope_sin_swa : m->rope_sin;
+        rope_apply(m, tc, ts, q, S, nh);
+        rope_apply(m, tc, ts, k, S, nkv);
         /* GQA expand (:455-479) */
         int grp = nh / nkv;
         for (int s = 0; s < S; s++)
@@ -838,22 +895,27 @@ int orc_forward(const orc_model *m, const int32_t *ids, int S, int target_dim, f
                     memcpy(ke + (size_t)s * H + (size_t)qh * hd, k + (size_t)s * kvd + (size_t)kh * hd, sizeof(float) * hd);
                     memcpy(ve + (size_t)s * H + (size_t)qh * hd, v + (size_t)s * kvd + (size_t)kh * hd, sizeof(float) * hd);
                 }
-        /* MultiHeadAttentionChunked, mask nil (attention.go:178-310, :344-363) */
+        /* MultiHeadAttentionChunked, mask nil (attention.go:178-310, :344-363).
+         * Query i's row covers keys [lo, hi]: all S keys, or the sliding
+         * window, whose keys form a contiguous row of their own for the
+         * softmax and the weighted sum. */
         for (int h = 0; h < nh; h++) {
             for (int i = 0; i < S; i++) {
+                const int lo = i - hw > 0 ? i - hw : 0, hi = i + hw < S - 1 ? i + hw : S - 1;
                 const float *qr = q + (size_t)i * H + (size_t)h * hd;
-                for (int j = 0; j < S; j++) {
+                for (int j = lo; j <= hi; j++) {
                     const float *kr = ke + (size_t)j * H + (size_t)h * hd;
                     float d = g_matmul_path == 2 ? dot_inline(qr, kr, hd) : orc_dot_f32(qr, kr, hd);
-                    scores[(size_t)i * S + j] = d * c->attention_scale;
+                    scores[(size_t)i * S + (j - lo)] = d * c->attention_scale;
                 }
+                orc_softmax(scores + (size_t)i * S, scores + (size_t)i * S, hi - lo + 1);
             }
-            for (int i = 0; i < S; i++) orc_softmax(scores + (size_t)i * S, scores + (size_t)i * S, S);
             for (int i = 0; i < S; i++) {
+                const int lo = i - hw > 0 ? i - hw : 0, hi = i + hw < S - 1 ? i + hw : S - 1;
                 float *o = attn + (size_t)i * H + (size_t)h * hd;
                 for (int d = 0; d < hd; d++) o[d] = 0.0f;
-                for (int j = 0; j < S; j++) {
-                    float w = scores[(size_t)i * S + j];
+                for (int j = lo; j <= hi; j++) {
+                    float w = scores[(size_t)i * S + (j - lo)];
                     if (w == 0.0f) continue;
                     const float *vr = ve + (size_t)j * H + (size_t)h * hd;
                     for (int d = 0; d < hd; d++) scaled[d] = vr[d] * w;   /* VecScaleF32 */
@@ -882,11 +944,31 @@ int orc_forward(const orc_model *m, const int32_t *ids, int S, int target_dim, f
     {
         /* MeanPoolingPartial (attention.go:423-445) + l2Normalize (model.go:808-820) */
         int od = target_dim;
+        if (m->dense_head) {
+            /* model-faithful head: pool every channel, dense_2 then dense_3
+             * (Q8_0, each input quantised as one INT8 buffer like every
+             * projection of the forward), then the first od outputs */
+            float *pool = (float *)malloc(sizeof(float) * H), *y1 = (float *)malloc(sizeof(float) * m->dense_mid),
+                  *y2 = (float *)malloc(sizeof(float) * H);
+            int8_t *pc = (int8_t *)malloc((size_t)(m->dense_mid > H ? m->dense_mid : H));
+            for (int i = 0; i < H; i++) pool[i] = 0.0f;
+            for (int s = 0; s < S; s++)
+                for (int i = 0; i < H; i++) pool[i] += hidden[(size_t)s * H + i];
+            float invS = 1.0f / (float)S, sc2;
+            for (int i = 0; i < H; i++) pool[i] *= invS;
+            orc_quantize_sym_int8(pool, H, pc, &sc2);
+            orc_matmul_q8_0_int8(y1, m->dense2, m->sd2, pc, sc2, 1, H, m->dense_mid);
+            orc_quantize_sym_int8(y1, m->dense_mid, pc, &sc2);
+            orc_matmul_q8_0_int8(y2, m->dense3, m->sd3, pc, sc2, 1, m->dense_mid, H);
+            for (int i = 0; i < od; i++) out[i] = y2[i];
+            free(pool); free(y1); free(y2); free(pc);
+        } else {
         for (int i = 0; i < od; i++) out[i] = 0.0f;
         for (int s = 0; s < S; s++)
             for (int i = 0; i < od; i++) out[i] += hidden[(size_t)s * H + i];
         float inv = 1.0f / (float)S;
         for (int i = 0; i < od; i++) out[i] *= inv;
+        }
         float ss = 0.0f;
         for (int i = 0; i < od; i++) ss += out[i] * out[i];
         if (ss != 0.0f) {

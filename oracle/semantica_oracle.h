@@ -53,6 +53,11 @@ typedef struct {
 orc_model *orc_model_load(const char *path, char *err, int errlen);
 void orc_model_free(orc_model *m);
 void orc_model_config(const orc_model *m, orc_config *out);
+/* Model-faithful mode (no reference counterpart): sliding-window layers (all
+ * but every swa_pattern-th layer see keys within swa_window / 2 positions,
+ * with RoPE base rope_base_swa when > 0) and the dense_2 / dense_3 head after
+ * pooling. Zeros: the reference's forward. -1 if the head has no weights. */
+int orc_model_set_faithful(orc_model *m, int swa_window, int swa_pattern, float rope_base_swa, int dense_head);
 
 /* (*Model).ForwardWithDim (model.go:661-666 → model_int8.go:148-256) for ONE
  * sequence. Returns 0, or -1 with err set to the reference's message. */
