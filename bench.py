@@ -66,7 +66,6 @@ SEARCH_D = 768
 SEARCH_Q = 16384
 SEARCH_K = 10
 SEARCH_SMALL = (1, 8, 32)
-SEARCH_METRIC = "search QPS (4M x 768 int8 rows, 16384 int8 queries, top-10 by exact int32 score)"
 SEARCH_CHUNK = 1 << 16
 PARITY_SEQS = 4
 PARITY_QUERIES = 64
@@ -519,13 +518,24 @@ def leg_gemm(env: Env, steps: int, warmup: int) -> dict:
 # ---------------------------------------------------------------------------
 # search/brute quantised scan + top-10
 # ---------------------------------------------------------------------------
-def search_config(n_gpus: int) -> dict:
-    return {"workload": f"BASELINE config 5: {SEARCH_N} pre-normalised rows of N(0,1) draws, D={SEARCH_D}, int8 "
-                        f"(x127), {SEARCH_Q} queries quantised the same way, exact int32 dot products, "
+def search_metric(quant: int = 1, dim: int | None = None) -> str:
+    """The search line's metric for the configured corpus and batch (BASELINE
+    config 5's at the defaults)."""
+    dim = dim or SEARCH_D
+    t = "int8" if quant == 1 else "int16"
+    rows = f"{SEARCH_N >> 20}M" if SEARCH_N % (1 << 20) == 0 else str(SEARCH_N)
+    return f"search QPS ({rows} x {dim} {t} rows, {SEARCH_Q} {t} queries, top-{SEARCH_K} by exact int32 score)"
+
+
+def search_config(n_gpus: int, quant: int = 1, dim: int | None = None) -> dict:
+    dim = dim or SEARCH_D
+    el, scale = (1, "int8 (x127)") if quant == 1 else (2, "int16 (x32767)")
+    return {"workload": f"BASELINE config 5: {SEARCH_N} pre-normalised rows of N(0,1) draws, D={dim}, {scale}, "
+                        f"{SEARCH_Q} queries quantised the same way, exact int32 dot products, "
                         f"top-{SEARCH_K} by (score desc, row asc)",
             "parallelism": f"rows sharded across {n_gpus} GPU(s) ({SEARCH_N // n_gpus} rows each), candidate keys "
                            "all-gathered (NCCL) and merged" if n_gpus > 1 else "1 GPU",
-            "l2": f"corpus ({SEARCH_N * SEARCH_D / 1e9:.2f} GB) is streamed by every query batch; above L2 (126 MB) "
+            "l2": f"corpus ({SEARCH_N * dim * el / 1e9:.2f} GB) is streamed by every query batch; above L2 (126 MB) "
                   "at the configured size"}
 
 
@@ -668,7 +678,7 @@ def leg_search(env: Env, steps: int, warmup: int, parity: bool) -> tuple[dict, d
             res.update({"queries": SEARCH_Q, "qps": SEARCH_Q / (ms * 1e-3), "ms_per_batch": ms, "scan_ms": scan_ms,
                         "scaling": "strong",
                         "roofline": {"kernel": ("search_tc_kernel" if quant == 1 else "search_tc16_kernel")
-                                     + " (rows of one GPU x 16384 queries)", "bound": "tensor",
+                                     + f" (rows of one GPU x {SEARCH_Q} queries)", "bound": "tensor",
                                      "achieved": ach, "peak": 2 * bf16, "unit": "TOP/s", "frac": ach / (2 * bf16),
                                      "peak_source": "2 x measured bf16_tflops (dense int8 runs at twice the bf16 rate; "
                                                     "no int8 figure is measured on this pool)"
@@ -967,7 +977,8 @@ def run_search(args) -> None:
     import ctypes as C
     env = Env(args)
     torch, world, rank = env.torch, env.world, env.rank
-    var = SearchVariant(env, 1, SEARCH_D, SEARCH_Q)
+    quant, dim = args.search_quant, args.search_dim
+    var = SearchVariant(env, quant, dim, SEARCH_Q)
     for _ in range(max(args.warmup, 0)):
         var.step(SEARCH_Q)
     torch.cuda.synchronize()
@@ -982,10 +993,11 @@ def run_search(args) -> None:
     small = var.small_batches()
     clk = clocks.stop()
     # e2e: float queries from pinned host memory, quantised on the device, ids back to the host
-    qf_host = torch.empty((SEARCH_Q, SEARCH_D), dtype=torch.float32, pin_memory=True)
-    qf_host.copy_((var.qcodes.float() / 127.0).cpu())
+    qscale = 127.0 if quant == 1 else 32767.0
+    qf_host = torch.empty((SEARCH_Q, dim), dtype=torch.float32, pin_memory=True)
+    qf_host.copy_((var.qcodes.float() / qscale).cpu())
     ids_host = torch.empty((SEARCH_Q, SEARCH_K), dtype=torch.int32, pin_memory=True)
-    qf_dev = torch.empty((SEARCH_Q, SEARCH_D), dtype=torch.float32, device=env.dev)
+    qf_dev = torch.empty((SEARCH_Q, dim), dtype=torch.float32, device=env.dev)
     q_dev = torch.empty_like(var.qcodes)
     out_ids = np.empty((SEARCH_Q, SEARCH_K), dtype=np.int32)
     out_dist = np.empty((SEARCH_Q, SEARCH_K), dtype=np.float32)
@@ -995,14 +1007,14 @@ def run_search(args) -> None:
         if world == 1:
             # Index.SearchVector for the whole batch through the public C ABI:
             # host floats in, ids and distances back in host memory
-            env._lib.check(env.lib.sem_index_search(var.h, C.c_void_p(qf_np.ctypes.data), SEARCH_Q, SEARCH_D, SEARCH_K,
+            env._lib.check(env.lib.sem_index_search(var.h, C.c_void_p(qf_np.ctypes.data), SEARCH_Q, dim, SEARCH_K,
                                                     1, 1, C.c_void_p(out_ids.ctypes.data),
                                                     C.c_void_p(out_dist.ctypes.data), None))
             return
         with torch.cuda.stream(env.stream):
             qf_dev.copy_(qf_host, non_blocking=True)
             n = qf_dev / qf_dev.norm(dim=1, keepdim=True)
-            q_dev.copy_(torch.round(n.clamp(-1, 1) * 127).to(torch.int8))
+            q_dev.copy_(torch.round(n.clamp(-1, 1) * qscale).to(q_dev.dtype))
         var.step(SEARCH_Q, q_dev)
         with torch.cuda.stream(env.stream):
             ids_host.copy_(var.rows, non_blocking=True)
@@ -1019,28 +1031,32 @@ def run_search(args) -> None:
     ms, scan_ms, e2e_s = env.max_over_ranks(ms, scan_ms, e2e_s)
     if rank == 0:
         bf16 = env.peaks.get("bf16_tflops") or 1590.0
-        ops = 2.0 * var.per * SEARCH_D * SEARCH_Q
+        ops = 2.0 * var.per * dim * SEARCH_Q
         traffic = None
-        if os.path.exists(TRAFFIC_PATH):
+        if os.path.exists(TRAFFIC_PATH) and quant == 1 and dim == SEARCH_D:
             bpr = json.load(open(TRAFFIC_PATH)).get("search_tc_bytes_per_corpus_row")
             traffic = bpr * var.per if bpr else None
+        metric = search_metric(quant, dim)
         ach = ops / (scan_ms * 1e-3) / 1e12
-        line = {"metric": SEARCH_METRIC, "value": SEARCH_Q / (ms * 1e-3), "unit": "queries/s", "n_gpus": world,
+        line = {"metric": metric, "value": SEARCH_Q / (ms * 1e-3), "unit": "queries/s", "n_gpus": world,
                 "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
-                "scaling": "strong", "vs_baseline": None, "dtype": "int8 x int8 -> int32", "data": "synthetic",
-                "config": search_config(world), "clocks": clk,
-                "e2e": {"value": SEARCH_Q / e2e_s, "unit": "queries/s", "h2d_bytes_per_step": SEARCH_Q * SEARCH_D * 4,
+                "scaling": "strong", "vs_baseline": None,
+                "dtype": "int8 x int8 -> int32" if quant == 1 else "int16 x int16 -> int32 (byte planes on kind::i8)",
+                "data": "synthetic",
+                "config": search_config(world, quant, dim), "clocks": clk,
+                "e2e": {"value": SEARCH_Q / e2e_s, "unit": "queries/s", "h2d_bytes_per_step": SEARCH_Q * dim * 4,
                         "d2h_bytes_per_step": SEARCH_Q * SEARCH_K * (8 if world == 1 else 4),
                         "api": "sem_index_search (host fp32 queries, normalised and quantised on the device)"
                         if world == 1 else "sem_index_search_keys per shard + NCCL all-gather + sem_topk_merge"},
                 "gpu_launches": int(args.steps * 3),
-                "roofline": {"kernel": "search_tc_kernel (rows of one GPU x 16384 queries)", "bound": "tensor",
+                "roofline": {"kernel": ("search_tc_kernel" if quant == 1 else "search_tc16_kernel")
+                             + f" (rows of one GPU x {SEARCH_Q} queries)", "bound": "tensor",
                              "achieved": ach, "peak": 2 * bf16, "unit": "TOP/s", "frac": ach / (2 * bf16),
                              "peak_source": "2 x measured bf16_tflops (dense int8 runs at twice the bf16 rate; no "
                                             "int8 figure is measured on this pool)",
                              "algorithmic_ops_per_launch": ops, "launch_ms": scan_ms, "traffic": traffic,
                              "small_batch_hbm": {"peak_gbs": env.peaks.get("hbm_gbs") or 6650.0, **small}}}
-        if world == 1 and not args.no_cpu_baseline:
+        if world == 1 and not args.no_cpu_baseline and quant == 1:
             line["cpu_baseline"] = search_cpu_baseline(var.codes[:1 << 20].cpu().numpy(),
                                                        var.qcodes[:1024].cpu().numpy())
         print(json.dumps(line), flush=True)
@@ -1062,7 +1078,7 @@ def run_search_reference(args) -> None:
     cb = vals[-1]
     value = statistics.median(x["value"] for x in vals)
     cb["value"] = value
-    print(json.dumps({"metric": SEARCH_METRIC, "value": value, "unit": "queries/s", "n_gpus": args.gpus,
+    print(json.dumps({"metric": search_metric(), "value": value, "unit": "queries/s", "n_gpus": args.gpus,
                       "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * SEARCH_Q / value,
                       "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
                       "dtype": "int8 x int8 -> int32", "data": "synthetic", "impl": "reference",
@@ -1088,6 +1104,8 @@ def main():
     ap.add_argument("--seq-len", type=int, default=512)
     ap.add_argument("--search-rows", type=int, default=SEARCH_N, help="search corpus rows (profiling runs use fewer)")
     ap.add_argument("--search-queries", type=int, default=SEARCH_Q)
+    ap.add_argument("--search-quant", type=int, default=1, choices=[1, 2], help="--workload search: int8 (1) or int16 (2) rows")
+    ap.add_argument("--search-dim", type=int, default=SEARCH_D, help="--workload search: vector dimension")
     args = ap.parse_args()
     BATCH, SEQ_LEN = args.batch, args.seq_len
     SEARCH_N, SEARCH_Q = args.search_rows, args.search_queries

@@ -57,6 +57,14 @@ _SIGNATURES = {
                                    C.c_void_p]),
     "sem_model_check": (C.c_int, [C.c_void_p]),
     "sem_model_set_faithful": (C.c_int, [C.c_void_p, C.c_void_p]),
+    "sem_group_load": (C.c_int, [C.c_void_p, C.c_int32, C.POINTER(ModelConfig), C.POINTER(TensorView), C.c_int32,
+                                 C.POINTER(C.c_void_p)]),
+    "sem_group_load_gguf": (C.c_int, [C.c_void_p, C.c_int32, C.c_char_p, C.POINTER(C.c_void_p)]),
+    "sem_group_size": (C.c_int, [C.c_void_p, C.POINTER(C.c_int32)]),
+    "sem_group_config_get": (C.c_int, [C.c_void_p, C.POINTER(ModelConfig)]),
+    "sem_group_set_faithful": (C.c_int, [C.c_void_p, C.c_void_p]),
+    "sem_group_embed": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int32, C.c_void_p, C.c_void_p]),
+    "sem_group_free": (C.c_int, [C.c_void_p]),
     "sem_model_profile": (C.c_int, [C.c_void_p, C.c_int32]),
     "sem_model_profile_read": (C.c_int, [C.c_void_p, C.POINTER(C.c_char_p), C.POINTER(C.c_float),
                                          C.POINTER(C.c_int32), C.c_int32, C.POINTER(C.c_int32)]),

@@ -28,7 +28,7 @@ CXX_FLAGS = ["-O2", "-std=c++17", "-fPIC", "-Wall", "-Wno-unused-function", f"-I
 
 CU_SOURCES = ["model_kernels.cu", "gemm_q8.cu", "gemm_split.cu", "gemm_dp4a.cu", "attention.cu", "attention_short.cu",
               "brute_kernels.cu", "gemm_noalloc.cu", "search_tc.cu"]
-CPP_SOURCES = ["host/gguf.cpp", "host/model.cpp", "host/brute.cpp"]
+CPP_SOURCES = ["host/gguf.cpp", "host/model.cpp", "host/brute.cpp", "host/group.cpp"]
 HEADERS = ["common.cuh", "sm100.cuh", "tmap.h", "kernels.h", "host/internal.h", "host/gguf.h"]
 
 

@@ -122,6 +122,9 @@ __device__ __forceinline__ uint64_t umma_desc_mn_sw128(uint32_t saddr, uint32_t 
 
 }  // namespace
 
+// WIN: sliding-window layers (model-faithful mode). The full-attention
+// instance keeps the window tests out of its score loops.
+template <bool WIN>
 __global__ void __launch_bounds__(THREADS, 1)
     attention_tc_kernel(const __grid_constant__ CUtensorMap tm_qh, const __grid_constant__ CUtensorMap tm_ql,
                         const __grid_constant__ CUtensorMap tm_k1, const __grid_constant__ CUtensorMap tm_k2,
@@ -162,7 +165,7 @@ __global__ void __launch_bounds__(THREADS, 1)
   // query rows see keys within hw positions) the tiles its rows' windows
   // reach; every loop below walks nkt tiles from jlo
   const int q_pos0 = row0 - s_beg;
-  const bool windowed = hw < n_keys;
+  const bool windowed = WIN && hw < n_keys;
   const int jlo = windowed ? max(0, q_pos0 - hw) / KT : 0;
   const int jhi = windowed ? min(n_keys - 1, q_pos0 + n_rows - 1 + hw) / KT : (n_keys - 1) / KT;
   const int nkt = n_keys > 0 ? jhi - jlo + 1 : 0;
@@ -658,16 +661,21 @@ cudaError_t launch_attention(const __half* qh, const __half* ql, const __half* k
   {
     std::lock_guard<std::mutex> lk(g_attn_mu);
     if (dev >= 0 && dev < 64 && !g_attn_attr[dev]) {
-      if ((e = cudaFuncSetAttribute(attention_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES)) !=
-          cudaSuccess)
+      if ((e = cudaFuncSetAttribute(attention_tc_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    SMEM_BYTES)) != cudaSuccess ||
+          (e = cudaFuncSetAttribute(attention_tc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    SMEM_BYTES)) != cudaSuccess)
         return e;
       g_attn_attr[dev] = true;
     }
   }
   dim3 grid(tiles.n_tiles * num_heads);
-  const int hw = half_window > 0 && half_window < (1 << 24) ? half_window : (1 << 24);
-  attention_tc_kernel<<<grid, THREADS, SMEM_BYTES, stream>>>(m_qh, m_ql, m_k1, m_k2, m_v2, m_out, num_heads, scale, hw,
-                                                             meta, tiles, out, absmax, err);
+  if (half_window > 0 && half_window < (1 << 24))
+    attention_tc_kernel<true><<<grid, THREADS, SMEM_BYTES, stream>>>(m_qh, m_ql, m_k1, m_k2, m_v2, m_out, num_heads,
+                                                                     scale, half_window, meta, tiles, out, absmax, err);
+  else
+    attention_tc_kernel<false><<<grid, THREADS, SMEM_BYTES, stream>>>(m_qh, m_ql, m_k1, m_k2, m_v2, m_out, num_heads,
+                                                                      scale, 1 << 24, meta, tiles, out, absmax, err);
   return cudaGetLastError();
 }
 

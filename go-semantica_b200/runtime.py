@@ -99,6 +99,70 @@ class Model:
         check(load().sem_model_check(self.handle))
 
 
+class Group:
+    """Several devices as one embedding engine (sem_group_*): a model replica
+    per device, each request split across them by token count and embedded on
+    all devices at once. forward_batch keeps Model.forward_batch's contract."""
+
+    def __init__(self, handle):
+        self.handle = handle
+        cfg = ModelConfig()
+        check(load().sem_group_config_get(self.handle, C.byref(cfg)))
+        self._config = cfg
+        n = C.c_int32()
+        check(load().sem_group_size(self.handle, C.byref(n)))
+        self.size = n.value
+
+    def config(self) -> ModelConfig:
+        return self._config
+
+    def close(self) -> None:
+        if self.handle:
+            load().sem_group_free(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def forward_with_dim(self, token_ids, target_dim: int) -> np.ndarray:
+        ids = np.ascontiguousarray(token_ids, dtype=np.int32)
+        return self.forward_batch(ids, np.array([0, ids.size], dtype=np.int32), [target_dim])[0]
+
+    def forward_batch(self, ids, offsets, dims=None) -> list[np.ndarray]:
+        ids = np.ascontiguousarray(ids, dtype=np.int32)
+        offsets = np.ascontiguousarray(offsets, dtype=np.int32)
+        n = offsets.size - 1
+        if dims is None:
+            dims = [self._config.embed_dim] * n
+        elif np.isscalar(dims):
+            dims = [int(dims)] * n
+        d = np.ascontiguousarray(dims, dtype=np.int32)
+        out = np.empty(max(int(d[d > 0].sum()) if n else 0, 1), dtype=np.float32)
+        check(load().sem_group_embed(self.handle, ids.ctypes.data, offsets.ctypes.data, n, d.ctypes.data,
+                                     out.ctypes.data))
+        res, o = [], 0
+        for k in d:
+            res.append(out[o:o + int(k)].copy())
+            o += int(k)
+        return res
+
+    def set_faithful(self, sliding_window: int = 0, swa_pattern: int = 0, rope_base_swa: float = 0.0,
+                     dense_head: bool = False) -> None:
+        cfg = _lib.FaithfulConfig(sliding_window, swa_pattern, rope_base_swa, 1 if dense_head else 0)
+        check(load().sem_group_set_faithful(self.handle, C.byref(cfg)))
+
+
+def load_group(path: str, devices) -> Group:
+    """The model of a GGUF file on every device in `devices` (sem_group_load_gguf)."""
+    devs = np.ascontiguousarray(list(devices), dtype=np.int32)
+    h = C.c_void_p()
+    check(load().sem_group_load_gguf(devs.ctypes.data, devs.size, path.encode(), C.byref(h)))
+    return Group(h)
+
+
 def load_model(path: str, ctx: Context | None = None) -> Model:
     """LoadModel (model.go:233-246): GGUF file -> device-resident model."""
     ctx = ctx or Context(0)

@@ -37,6 +37,7 @@ typedef struct sem_context sem_context;
 typedef struct sem_model sem_model;
 typedef struct sem_index sem_index;
 typedef struct sem_q8_weight sem_q8_weight;
+typedef struct sem_group sem_group;
 
 /* Message of the last failed call on this thread (never NULL). */
 const char *sem_last_error(void);
@@ -145,6 +146,31 @@ typedef struct sem_faithful_config {
 /* cfg NULL (or all zero): the reference's forward. Errors: SEM_EINVAL for
  * negative fields or a dense head the model has no weights for. */
 int sem_model_set_faithful(sem_model *model, const sem_faithful_config *cfg);
+
+/* ------------------------------------------------------------------------
+ * Several GPUs of one host as one embedding engine. The reference fans the
+ * sequences of a request out over goroutines (pkg/ggufembed/api.go:237-295);
+ * a group fans them out over devices: one context and one model replica per
+ * device, each request split by token count (longest sequence first to the
+ * device holding the fewest tokens) and embedded on every device at once from
+ * one host thread per device. No collective: replicas share nothing.
+ * ---------------------------------------------------------------------- */
+
+/* Loads the model on each of the n_devices distinct devices (in parallel). */
+int sem_group_load(const int32_t *devices, int32_t n_devices, const sem_model_config *cfg,
+                   const sem_tensor_view *tensors, int32_t n_tensors, sem_group **out);
+int sem_group_load_gguf(const int32_t *devices, int32_t n_devices, const char *path, sem_group **out);
+int sem_group_size(const sem_group *group, int32_t *out);
+int sem_group_config_get(const sem_group *group, sem_model_config *out);
+/* sem_model_set_faithful on every replica. */
+int sem_group_set_faithful(sem_group *group, const sem_faithful_config *cfg);
+/* sem_embed's contract (same arguments, errors and output layout); the
+ * request is validated on the host before any device starts, and a device's
+ * error is returned as "device N: <message>". One request at a time per
+ * group; concurrent callers wait. */
+int sem_group_embed(sem_group *group, const int32_t *ids, const int32_t *offsets, int32_t n_seqs,
+                    const int32_t *dims, float *out);
+int sem_group_free(sem_group *group);
 
 /* Per-stage device timing of the forward pass (diagnostics; no reference
  * counterpart). enable != 0 brackets every kernel launch of later forwards
