@@ -55,6 +55,9 @@ _SIGNATURES = {
     "sem_embed": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int32, C.c_void_p, C.c_void_p]),
     "sem_embed_device": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int32, C.c_int32, C.c_void_p,
                                    C.c_void_p]),
+    "sem_embed_submit": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int32, C.c_void_p,
+                                   C.POINTER(C.c_uint64)]),
+    "sem_embed_wait": (C.c_int, [C.c_void_p, C.c_uint64, C.c_void_p]),
     "sem_model_check": (C.c_int, [C.c_void_p]),
     "sem_model_set_faithful": (C.c_int, [C.c_void_p, C.c_void_p]),
     "sem_group_load": (C.c_int, [C.c_void_p, C.c_int32, C.POINTER(ModelConfig), C.POINTER(TensorView), C.c_int32,

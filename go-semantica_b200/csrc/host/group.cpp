@@ -149,27 +149,14 @@ int sem_group_set_faithful(sem_group* g, const sem_faithful_config* cfg) {
 
 int sem_group_embed(sem_group* g, const int32_t* ids, const int32_t* offsets, int32_t B, const int32_t* dims_in,
                     float* out) {
-  if (!g || (!ids && B > 0) || !offsets || (!out && B > 0)) return sem::set_error(SEM_EINVAL, "null argument");
-  if (B < 0) return sem::set_error(SEM_EINVAL, "negative sequence count");
-  const sem_model_config& c = g->cfg;
-  // the reference's checks first (model_int8.go:149-178), so that a bad
-  // request fails before any device starts
-  std::vector<int32_t> dims(B);
-  std::vector<int64_t> out_off(B + 1, 0);
-  for (int s = 0; s < B; ++s) {
-    const int d = dims_in ? dims_in[s] : c.embed_dim;
-    if (d <= 0 || d > c.embed_dim)
-      return sem::set_error(SEM_EINVAL, "target dimension %d out of range (1..%d)", d, c.embed_dim);
-    const int len = offsets[s + 1] - offsets[s];
-    if (len <= 0) return sem::set_error(SEM_EINVAL, "empty input");
-    if (len > c.max_seq_len) return sem::set_error(SEM_EINVAL, "sequence too long: %d > %d", len, c.max_seq_len);
-    for (int32_t r = offsets[s]; r < offsets[s + 1]; ++r)
-      if (ids[r] < 0 || ids[r] >= c.vocab_size) return sem::set_error(SEM_EINVAL, "token ID out of range: %d", ids[r]);
-    dims[s] = d;
-    out_off[s + 1] = out_off[s] + d;
-  }
+  if (!g) return sem::set_error(SEM_EINVAL, "null argument");
+  // the request is checked before any device starts
+  std::vector<int32_t> dims;
+  int64_t out_floats = 0;
+  if (int rc = sem::validate_embed_request(g->cfg, ids, offsets, B, dims_in, out, &dims, &out_floats)) return rc;
   if (B == 0) return SEM_OK;
-  if (offsets[0] != 0) return sem::set_error(SEM_EINVAL, "offsets[0] must be 0");
+  std::vector<int64_t> out_off(B + 1, 0);
+  for (int s = 0; s < B; ++s) out_off[s + 1] = out_off[s] + dims[s];
   std::lock_guard<std::mutex> lk(g->mu);
   const int n = (int)g->models.size();
   const auto parts = sem::split_by_tokens(offsets, B, n);

@@ -20,6 +20,11 @@ namespace sem {
 int set_error(int code, const char* fmt, ...);
 const char* last_error();
 
+// sem_embed's host checks in the reference's order (model_int8.go:149-178):
+// fills dims (NULL dims_in = embed_dim) and the total output floats.
+int validate_embed_request(const sem_model_config& c, const int32_t* ids, const int32_t* offsets, int32_t B,
+                           const int32_t* dims_in, float* out, std::vector<int32_t>* dims, int64_t* out_floats);
+
 #define SEM_CUDA(call)                                                                             \
   do {                                                                                             \
     cudaError_t e_ = (call);                                                                       \

@@ -1,6 +1,7 @@
 // Model loading and the batched forward pass (the host side of
 // internal/runtime: LoadModel model.go:233-315, ForwardWithDim model.go:661-666,
 // forwardINT8WithDim model_int8.go:148-256).
+#include <algorithm>
 #include <cmath>
 #include <cstring>
 #include <memory>
@@ -62,11 +63,30 @@ struct sem_model {
   size_t prof_used = 0;                  // events recorded since the last read
   double prof_ms[16] = {0};
   int32_t prof_n[16] = {0};
-  // CUDA graph of the forward of the last small batch shape (sem_embed), with
-  // the buffers, projection path and stream it was captured for
-  cudaGraphExec_t fwd_graph = nullptr;
-  std::vector<const void*> fwd_graph_key;
+  // CUDA graphs of the forwards of recent small batch shapes (sem_embed,
+  // sem_embed_submit), each with the buffers, projection path, stream and
+  // shape it was captured for; the least recently replayed goes first
+  struct Graph {
+    std::vector<const void*> key;
+    std::vector<int32_t> shape;  // offsets[0..B] then dims[0..B)
+    cudaGraphExec_t exec = nullptr;
+    uint64_t used = 0;
+  };
+  std::vector<Graph> graphs;
+  uint64_t graph_tick = 0;
   bool graphs_off = false;  // a capture failed here: forwards run without a graph
+  // sem_embed_submit / sem_embed_wait: two request slots, each with pinned
+  // staging for its ids, metadata, outputs and error words, so the host
+  // prepares one request while the device runs the other
+  struct Slot {
+    sem::HostBuf ids, meta, out, flags;
+    cudaEvent_t done = nullptr;
+    uint64_t ticket = 0;
+    bool busy = false;
+    int64_t out_floats = 0;
+  };
+  Slot slots[2];
+  uint64_t next_ticket = 1;
   // model-faithful mode (sem_model_set_faithful): sliding-window layers, their
   // RoPE tables, the dense 2/3 head (weights loaded when the file has them)
   sem_faithful_config faithful{};
@@ -367,7 +387,6 @@ struct MetaPtrs {
   int32_t* src_row;  // [T] caller's row of each packed row (valid when permuted)
   int64_t T_long;    // packed rows [0, T_long) belong to sequences of >= kSplitMinLen tokens
   bool permuted;     // the packed order differs from the caller's
-  bool same_shape;   // the batch shape equals the previous call's (metadata not re-uploaded)
 };
 
 // Sequences at least this long take the tensor-core kernels: the split-plane
@@ -387,7 +406,8 @@ constexpr int64_t kExactShortMaxTokens = 4096;
 // batch shape equals the previous call's). Sequences are packed long ones
 // (>= kSplitMinLen tokens) first, each group in the caller's order; the
 // outputs go back to the caller's order through out_off.
-int upload_meta(sem_model* m, const int32_t* offsets, int B, const int32_t* dims, MetaPtrs* mp) {
+int upload_meta(sem_model* m, const int32_t* offsets, int B, const int32_t* dims, MetaPtrs* mp,
+                HostBuf* staging = nullptr) {
   const int64_t T = offsets[B];
   int32_t* base = m->meta.as<int32_t>();
   int32_t* d_row_seq = base;
@@ -426,8 +446,10 @@ int upload_meta(sem_model* m, const int32_t* offsets, int B, const int32_t* dims
       acc += dims[s];
     }
     size_t bytes = (size_t)(reinterpret_cast<uint8_t*>(d_iota + B) - reinterpret_cast<uint8_t*>(base));
-    HostBuf& hb = m->ctx->pinned;
-    SEM_CUDA(cudaStreamSynchronize(m->ctx->stream));  // the pinned buffer may still feed an earlier copy
+    // a request slot's own staging is free (its previous request completed);
+    // the shared pinned buffer may still feed an earlier copy
+    HostBuf& hb = staging ? *staging : m->ctx->pinned;
+    if (!staging) SEM_CUDA(cudaStreamSynchronize(m->ctx->stream));
     SEM_CUDA(hb.ensure(bytes));
     int32_t* h = hb.as<int32_t>();
     int32_t* h_row_seq = h;
@@ -483,7 +505,6 @@ int upload_meta(sem_model* m, const int32_t* offsets, int B, const int32_t* dims
   mp->src_row = d_src;
   mp->T_long = m->t_long;
   mp->permuted = m->permuted;
-  mp->same_shape = same;
   return SEM_OK;
 }
 
@@ -630,17 +651,22 @@ int run_forward(sem_model* m, const int32_t* d_ids, const MetaPtrs& mp, float* d
 // the kernels' work.
 constexpr int64_t kGraphMaxTokens = 32768;
 
-void drop_graph(sem_model* m) {
-  if (m->fwd_graph) cudaGraphExecDestroy(m->fwd_graph);
-  m->fwd_graph = nullptr;
-  m->fwd_graph_key.clear();
+constexpr size_t kGraphCacheSize = 8;
+
+void drop_graphs(sem_model* m) {
+  for (auto& g : m->graphs)
+    if (g.exec) cudaGraphExecDestroy(g.exec);
+  m->graphs.clear();
 }
 
 // run_forward on the workspace ids and output, through a graph captured on
 // the first call of a small batch shape and replayed while the shape, the
-// workspace buffers, the projection path and the stream stay the same.
-int forward_maybe_graph(sem_model* m, const MetaPtrs& mp, cudaStream_t st) {
+// workspace buffers, the projection path, the mode and the stream stay the
+// same. Up to kGraphCacheSize shapes keep their graphs.
+int forward_maybe_graph(sem_model* m, const MetaPtrs& mp, const int32_t* offsets, const int32_t* dims,
+                        cudaStream_t st) {
   const int64_t T = mp.seq.T;
+  const int B = mp.seq.B;
   auto direct = [&] { return run_forward(m, m->ids.as<int32_t>(), mp, m->out.as<float>(), st); };
   if (m->prof || m->graphs_off || T > kGraphMaxTokens) return direct();
   const std::vector<const void*> key = {m->hid.p,    m->big.p,   m->att.p, m->codes.p, m->halves.p,
@@ -648,8 +674,20 @@ int forward_maybe_graph(sem_model* m, const MetaPtrs& mp, cudaStream_t st) {
                                         m->errflag.p, reinterpret_cast<const void*>((intptr_t)get_q8_path()),
                                         static_cast<const void*>(st),
                                         reinterpret_cast<const void*>((intptr_t)m->faithful_gen), m->head_y1.p};
-  if (!mp.same_shape || !m->fwd_graph || key != m->fwd_graph_key) {
-    drop_graph(m);
+  std::vector<int32_t> shape(offsets, offsets + B + 1);
+  shape.insert(shape.end(), dims, dims + B);
+  // graphs of other buffers (the workspace grew) can never replay again
+  for (size_t i = 0; i < m->graphs.size();)
+    if (m->graphs[i].key != key) {
+      cudaGraphExecDestroy(m->graphs[i].exec);
+      m->graphs.erase(m->graphs.begin() + i);
+    } else {
+      ++i;
+    }
+  sem_model::Graph* hit = nullptr;
+  for (auto& g : m->graphs)
+    if (g.shape == shape) hit = &g;
+  if (!hit) {
     // A capture that the runtime refuses (the kernels were recorded, not run)
     // turns graphs off for this model and runs the same kernels directly; an
     // error of the forward itself is returned as it is.
@@ -671,29 +709,37 @@ int forward_maybe_graph(sem_model* m, const MetaPtrs& mp, cudaStream_t st) {
       cudaGraphDestroy(g);
       return rc;
     }
-    const cudaError_t ei = cudaGraphInstantiate(&m->fwd_graph, g, 0);
+    cudaGraphExec_t exec = nullptr;
+    const cudaError_t ei = cudaGraphInstantiate(&exec, g, 0);
     cudaGraphDestroy(g);
     if (ei != cudaSuccess) {
-      m->fwd_graph = nullptr;
       cudaGetLastError();
       m->graphs_off = true;
       return direct();
     }
-    m->fwd_graph_key = key;
+    if (m->graphs.size() >= kGraphCacheSize) {
+      auto lru = std::min_element(m->graphs.begin(), m->graphs.end(),
+                                  [](const sem_model::Graph& a, const sem_model::Graph& b) { return a.used < b.used; });
+      cudaGraphExecDestroy(lru->exec);
+      m->graphs.erase(lru);
+    }
+    m->graphs.push_back(sem_model::Graph{key, std::move(shape), exec, 0});
+    hit = &m->graphs.back();
   }
-  SEM_CUDA(cudaGraphLaunch(m->fwd_graph, st));
+  hit->used = ++m->graph_tick;
+  SEM_CUDA(cudaGraphLaunch(hit->exec, st));
   return SEM_OK;
 }
 
 }  // namespace
 
-int model_embed(sem_model* m, const int32_t* ids, const int32_t* offsets, int32_t B, const int32_t* dims_in,
-                float* out) {
-  if (!m || (!ids && B > 0) || !offsets || (!out && B > 0)) return set_error(SEM_EINVAL, "null argument");
+int validate_embed_request(const sem_model_config& c, const int32_t* ids, const int32_t* offsets, int32_t B,
+                           const int32_t* dims_in, float* out, std::vector<int32_t>* dims, int64_t* out_floats) {
+  if ((!ids && B > 0) || !offsets || (!out && B > 0)) return set_error(SEM_EINVAL, "null argument");
   if (B < 0) return set_error(SEM_EINVAL, "negative sequence count");
-  const sem_model_config& c = m->cfg;
-  std::vector<int32_t> dims(B);
-  int64_t out_floats = 0;
+  if (B > 0 && offsets[0] != 0) return set_error(SEM_EINVAL, "offsets[0] must be 0");
+  dims->assign(B, 0);
+  *out_floats = 0;
   for (int s = 0; s < B; ++s) {
     int d = dims_in ? dims_in[s] : c.embed_dim;
     // ForwardWithDim (model.go:661-666) then forwardINT8WithDim (model_int8.go:149-171)
@@ -704,11 +750,19 @@ int model_embed(sem_model* m, const int32_t* ids, const int32_t* offsets, int32_
     if (len > c.max_seq_len) return set_error(SEM_EINVAL, "sequence too long: %d > %d", len, c.max_seq_len);
     for (int32_t r = offsets[s]; r < offsets[s + 1]; ++r)
       if (ids[r] < 0 || ids[r] >= c.vocab_size) return set_error(SEM_EINVAL, "token ID out of range: %d", ids[r]);
-    dims[s] = d;
-    out_floats += d;
+    (*dims)[s] = d;
+    *out_floats += d;
   }
+  return SEM_OK;
+}
+
+int model_embed(sem_model* m, const int32_t* ids, const int32_t* offsets, int32_t B, const int32_t* dims_in,
+                float* out) {
+  if (!m) return set_error(SEM_EINVAL, "null argument");
+  std::vector<int32_t> dims;
+  int64_t out_floats = 0;
+  if (int rc = validate_embed_request(m->cfg, ids, offsets, B, dims_in, out, &dims, &out_floats)) return rc;
   if (B == 0) return SEM_OK;
-  if (offsets[0] != 0) return set_error(SEM_EINVAL, "offsets[0] must be 0");
   sem_context* ctx = m->ctx;
   DeviceGuard dg(ctx->device);
   std::lock_guard<std::mutex> lk(ctx->mu);
@@ -724,7 +778,7 @@ int model_embed(sem_model* m, const int32_t* ids, const int32_t* offsets, int32_
   } else {
     SEM_CUDA(cudaMemcpyAsync(m->ids.p, ids, (size_t)T * 4, cudaMemcpyHostToDevice, ctx->stream));
   }
-  if ((rc = forward_maybe_graph(m, mp, ctx->stream))) return rc;
+  if ((rc = forward_maybe_graph(m, mp, offsets, dims.data(), ctx->stream))) return rc;
   SEM_CUDA(cudaMemcpyAsync(out, m->out.p, (size_t)out_floats * 4, cudaMemcpyDeviceToHost, ctx->stream));
   SEM_CUDA(ctx->pinned.ensure(64));
   uint32_t* flags = ctx->pinned.as<uint32_t>();
@@ -732,6 +786,83 @@ int model_embed(sem_model* m, const int32_t* ids, const int32_t* offsets, int32_
   SEM_CUDA(cudaMemsetAsync(m->errflag.p, 0, 8, ctx->stream));
   SEM_CUDA(cudaStreamSynchronize(ctx->stream));
   if (flags[1]) return set_error(SEM_EDEVICE, "forward: a tensor-core pipeline wait timed out (error bits 0x%x)", flags[1]);
+  return SEM_OK;
+}
+
+// The request pipeline: submit validates a request, stages its ids and
+// metadata in a slot's pinned buffers and enqueues the upload, the forward and
+// the download of its outputs and error words, then returns; wait blocks on
+// that request alone and hands its outputs over. With two slots the host
+// prepares (and tokenises) request i + 1 while the device runs request i, the
+// overlap the reference gets from one goroutine per prompt
+// (pkg/ggufembed/api.go:237-295).
+int model_embed_submit(sem_model* m, const int32_t* ids, const int32_t* offsets, int32_t B, const int32_t* dims_in,
+                       uint64_t* ticket) {
+  if (!m || !ticket) return set_error(SEM_EINVAL, "null argument");
+  std::vector<int32_t> dims;
+  int64_t out_floats = 0;
+  float dummy = 0.0f;
+  if (int rc = validate_embed_request(m->cfg, ids, offsets, B, dims_in, &dummy, &dims, &out_floats)) return rc;
+  sem_context* ctx = m->ctx;
+  DeviceGuard dg(ctx->device);
+  std::lock_guard<std::mutex> lk(ctx->mu);
+  sem_model::Slot& sl = m->slots[m->next_ticket & 1];
+  if (sl.busy) return set_error(SEM_EINVAL, "two requests in flight: wait for one before submitting another");
+  if (!sl.done) SEM_CUDA(cudaEventCreateWithFlags(&sl.done, cudaEventDisableTiming));
+  SEM_CUDA(sl.flags.ensure(64));
+  uint32_t* flags = sl.flags.as<uint32_t>();
+  flags[0] = flags[1] = 0;
+  sl.out_floats = out_floats;
+  if (B > 0) {
+    const int64_t T = offsets[B];
+    int rc;
+    if ((rc = ensure_workspace(m, T, B, out_floats))) return rc;
+    MetaPtrs mp;
+    if ((rc = upload_meta(m, offsets, B, dims.data(), &mp, &sl.meta))) return rc;
+    SEM_CUDA(sl.ids.ensure((size_t)T * 4));
+    std::memcpy(sl.ids.p, ids, (size_t)T * 4);
+    if (mp.permuted) {
+      SEM_CUDA(m->ids_in.ensure((size_t)T * 4));
+      SEM_CUDA(cudaMemcpyAsync(m->ids_in.p, sl.ids.p, (size_t)T * 4, cudaMemcpyHostToDevice, ctx->stream));
+      SEM_CUDA(launch_gather_i32(m->ids_in.as<int32_t>(), mp.src_row, m->ids.as<int32_t>(), T, ctx->stream));
+    } else {
+      SEM_CUDA(cudaMemcpyAsync(m->ids.p, sl.ids.p, (size_t)T * 4, cudaMemcpyHostToDevice, ctx->stream));
+    }
+    if ((rc = forward_maybe_graph(m, mp, offsets, dims.data(), ctx->stream))) return rc;
+    SEM_CUDA(sl.out.ensure((size_t)out_floats * 4));
+    SEM_CUDA(cudaMemcpyAsync(sl.out.p, m->out.p, (size_t)out_floats * 4, cudaMemcpyDeviceToHost, ctx->stream));
+    SEM_CUDA(cudaMemcpyAsync(flags, m->errflag.p, 8, cudaMemcpyDeviceToHost, ctx->stream));
+    SEM_CUDA(cudaMemsetAsync(m->errflag.p, 0, 8, ctx->stream));
+  }
+  SEM_CUDA(cudaEventRecord(sl.done, ctx->stream));
+  sl.busy = true;
+  sl.ticket = m->next_ticket++;
+  *ticket = sl.ticket;
+  return SEM_OK;
+}
+
+int model_embed_wait(sem_model* m, uint64_t ticket, float* out) {
+  if (!m) return set_error(SEM_EINVAL, "null argument");
+  sem_context* ctx = m->ctx;
+  DeviceGuard dg(ctx->device);
+  sem_model::Slot* sl = nullptr;
+  cudaEvent_t ev = nullptr;
+  {
+    std::lock_guard<std::mutex> lk(ctx->mu);
+    for (auto& x : m->slots)
+      if (x.busy && x.ticket == ticket) sl = &x;
+    if (!sl) return set_error(SEM_EINVAL, "no request in flight with ticket %llu", (unsigned long long)ticket);
+    if (!out && sl->out_floats > 0) return set_error(SEM_EINVAL, "null argument");
+    ev = sl->done;
+  }
+  // outside the lock: the other slot's submit may enqueue meanwhile
+  const cudaError_t es = cudaEventSynchronize(ev);
+  std::lock_guard<std::mutex> lk(ctx->mu);
+  sl->busy = false;
+  if (es != cudaSuccess) return set_error(SEM_EDEVICE, "cudaEventSynchronize: %s", cudaGetErrorString(es));
+  const uint32_t* flags = sl->flags.as<uint32_t>();
+  if (flags[1]) return set_error(SEM_EDEVICE, "forward: a tensor-core pipeline wait timed out (error bits 0x%x)", flags[1]);
+  if (sl->out_floats > 0) std::memcpy(out, sl->out.p, (size_t)sl->out_floats * 4);
   return SEM_OK;
 }
 
@@ -1003,7 +1134,9 @@ int sem_model_free(sem_model* m) {
   sem::DeviceGuard dg(m->ctx->device);
   cudaStreamSynchronize(m->ctx->stream);
   for (cudaEvent_t e : m->prof_events) cudaEventDestroy(e);
-  if (m->fwd_graph) cudaGraphExecDestroy(m->fwd_graph);
+  sem::drop_graphs(m);
+  for (auto& sl : m->slots)
+    if (sl.done) cudaEventDestroy(sl.done);
   delete m;
   return SEM_OK;
 }
@@ -1023,6 +1156,13 @@ int sem_model_profile_read(sem_model* m, const char** names, float* total_ms, in
 int sem_embed(sem_model* m, const int32_t* ids, const int32_t* offsets, int32_t n, const int32_t* dims, float* out) {
   return sem::model_embed(m, ids, offsets, n, dims, out);
 }
+
+int sem_embed_submit(sem_model* m, const int32_t* ids, const int32_t* offsets, int32_t n, const int32_t* dims,
+                     uint64_t* ticket) {
+  return sem::model_embed_submit(m, ids, offsets, n, dims, ticket);
+}
+
+int sem_embed_wait(sem_model* m, uint64_t ticket, float* out) { return sem::model_embed_wait(m, ticket, out); }
 
 int sem_embed_device(sem_model* m, const int32_t* d_ids, const int32_t* h_offsets, int32_t n, int32_t dim, float* d_out,
                      void* stream) {

@@ -8,7 +8,7 @@ every prompt of a request to the device in one batched call.
 from __future__ import annotations
 
 from dataclasses import dataclass
-from typing import Callable, Sequence
+from typing import Callable, Iterable, Iterator, Sequence
 
 import numpy as np
 
@@ -108,6 +108,10 @@ class Runtime:
         """EmbedInputs (api.go:168-187) → one batched forward for every prompt."""
         if len(inputs) == 0:
             return []
+        ids, offsets, dims = self._request(inputs)
+        return self.model.forward_batch(ids, offsets, dims)
+
+    def _request(self, inputs: Sequence[EmbedInput]):
         ids, offsets, dims = [], [0], []
         for i, inp in enumerate(inputs):
             try:
@@ -124,7 +128,17 @@ class Runtime:
             ids.extend(toks)
             offsets.append(len(ids))
             dims.append(dim)
-        return self.model.forward_batch(np.asarray(ids, dtype=np.int32), np.asarray(offsets, dtype=np.int32), dims)
+        return np.asarray(ids, dtype=np.int32), np.asarray(offsets, dtype=np.int32), dims
+
+    def embed_inputs_stream(self, batches: Iterable[Sequence[EmbedInput]]) -> Iterator[list[np.ndarray]]:
+        """EmbedInputs over a stream of batches through the request pipeline
+        (Model.embed_stream): batch i + 1 is tokenised and submitted while the
+        device embeds batch i. Yields each batch's vectors in order; empty
+        batches yield []."""
+        def requests():
+            for inputs in batches:
+                yield self._request(inputs)
+        yield from self.model.embed_stream(requests())
 
     def embed(self, texts: Sequence[str], task: int = TaskSearchQuery, dim: int = DimensionsAuto) -> list[np.ndarray]:
         """semantica.Runtime.Embed (api.go:90-107)."""

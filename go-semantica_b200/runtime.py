@@ -65,6 +65,56 @@ class Model:
             o += int(k)
         return res
 
+    # ---- request pipeline ----
+    def submit(self, ids, offsets, dims=None) -> tuple:
+        """sem_embed_submit: enqueues a request and returns its ticket without
+        waiting; at most two requests are in flight."""
+        ids = np.ascontiguousarray(ids, dtype=np.int32)
+        offsets = np.ascontiguousarray(offsets, dtype=np.int32)
+        n = offsets.size - 1
+        if dims is None:
+            dims = [self._config.embed_dim] * n
+        elif np.isscalar(dims):
+            dims = [int(dims)] * n
+        d = np.ascontiguousarray(dims, dtype=np.int32)
+        t = C.c_uint64()
+        check(load().sem_embed_submit(self.handle, ids.ctypes.data, offsets.ctypes.data, n, d.ctypes.data,
+                                      C.byref(t)))
+        return (t.value, d)
+
+    def wait(self, ticket) -> list[np.ndarray]:
+        """sem_embed_wait: the outputs of a submitted request."""
+        t, d = ticket
+        out = np.empty(max(int(d.sum()) if d.size else 0, 1), dtype=np.float32)
+        check(load().sem_embed_wait(self.handle, C.c_uint64(t), out.ctypes.data))
+        res, o = [], 0
+        for k in d:
+            res.append(out[o:o + int(k)].copy())
+            o += int(k)
+        return res
+
+    def embed_stream(self, requests):
+        """Embeds an iterable of (ids, offsets, dims) requests through the
+        pipeline, yielding each request's vectors in order. The next request
+        is drawn from the iterable (e.g. tokenised) and submitted while the
+        device runs the current one."""
+        pending = None
+        try:
+            for ids, offsets, dims in requests:
+                t = self.submit(ids, offsets, dims)
+                prev, pending = pending, t
+                if prev is not None:
+                    yield self.wait(prev)
+            if pending is not None:
+                last, pending = pending, None
+                yield self.wait(last)
+        finally:
+            if pending is not None:  # abandoned or failed: free the slot
+                try:
+                    self.wait(pending)
+                except Exception:
+                    pass
+
     def profile(self, enable: bool) -> None:
         check(load().sem_model_profile(self.handle, 1 if enable else 0))
 

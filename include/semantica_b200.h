@@ -114,6 +114,23 @@ int sem_embed(sem_model *model, const int32_t *ids, const int32_t *offsets, int3
 int sem_embed_device(sem_model *model, const int32_t *d_ids, const int32_t *h_offsets, int32_t n_seqs, int32_t dim,
                      float *d_out, void *stream);
 
+/* The request pipeline (no reference counterpart; it stands in for the
+ * reference's one goroutine per prompt, pkg/ggufembed/api.go:237-295, at the
+ * level of whole requests). sem_embed_submit checks a request exactly as
+ * sem_embed does, copies its ids and metadata into one of the model's two
+ * request slots (pinned host staging), enqueues the upload, the forward and
+ * the download of its outputs, and returns a ticket without waiting.
+ * sem_embed_wait(ticket) blocks until that request is done and writes its
+ * outputs (sem_embed's layout) to `out`. While one request runs on the
+ * device the host prepares (tokenises, submits) the next. At most two
+ * requests are in flight: a third submit fails with SEM_EINVAL until one is
+ * waited for. Requests run in submission order; each ticket is waited for
+ * once. Errors the device reports (a timed-out pipeline wait) are returned by
+ * sem_embed_wait. */
+int sem_embed_submit(sem_model *model, const int32_t *ids, const int32_t *offsets, int32_t n_seqs,
+                     const int32_t *dims, uint64_t *ticket);
+int sem_embed_wait(sem_model *model, uint64_t ticket, float *out);
+
 /* Waits for the model's device to finish every forward enqueued so far and
  * reports what the device recorded since the last check (or sem_embed call):
  * SEM_EINVAL "token ID out of range: ..." for a device-resident id outside the

@@ -107,3 +107,56 @@ def test_quantize_queries_matches_oracle(quant):
     q[0, :6] = [1.0, -1.0, 0.0, -0.0, 1.5, -1.5]
     conv = oracle.quantize_int8_vec if quant == 1 else oracle.quantize_int16_vec
     np.testing.assert_array_equal(brute.quantize_queries(q, quant), conv(q))
+
+
+class _FakePipelineModel:
+    """Host-side stand-in for runtime.Model's submit/wait (no GPU): records
+    the order of calls and enforces the two-slot limit."""
+
+    def __init__(self):
+        import runtime
+        self.log, self.inflight, self.next = [], set(), 1
+        self.embed_stream = runtime.Model.embed_stream.__get__(self)
+
+    def submit(self, ids, offsets, dims):
+        if len(self.inflight) == 2:
+            raise RuntimeError("two requests in flight")
+        t = self.next
+        self.next += 1
+        self.inflight.add(t)
+        self.log.append(("submit", t))
+        return (t, len(offsets) - 1)
+
+    def wait(self, ticket):
+        t, n = ticket
+        self.inflight.remove(t)
+        self.log.append(("wait", t))
+        return [np.full(1, t, np.float32)] * n
+
+
+def test_embed_stream_overlaps_next_submit_with_current_request():
+    m = _FakePipelineModel()
+    reqs = [(np.ones(3, np.int32), np.array([0, 3], np.int32), [768]) for _ in range(4)]
+    out = list(m.embed_stream(iter(reqs)))
+    assert [o[0][0] for o in out] == [1, 2, 3, 4]
+    # request i + 1 is submitted before request i is waited for
+    assert m.log == [("submit", 1), ("submit", 2), ("wait", 1), ("submit", 3), ("wait", 2), ("submit", 4),
+                     ("wait", 3), ("wait", 4)]
+    assert not m.inflight
+
+
+def test_embed_stream_frees_slots_when_abandoned_or_failing():
+    m = _FakePipelineModel()
+    reqs = [(np.ones(3, np.int32), np.array([0, 3], np.int32), [768]) for _ in range(5)]
+    s = m.embed_stream(iter(reqs))
+    next(s)
+    s.close()
+    assert not m.inflight
+
+    def failing():
+        yield reqs[0]
+        raise ValueError("tokenizer failed")
+
+    with pytest.raises(ValueError, match="tokenizer failed"):
+        list(m.embed_stream(failing()))
+    assert not m.inflight
