@@ -234,9 +234,11 @@ int sem_q8_matmul_int8(sem_q8_weight *w, const void *d_codes, const uint32_t *d_
  *   - the split-plane tensor-core kernel folds the block scales into two fp16
  *     weight planes (one TMEM drain per tile, the fastest at scale) and differs
  *     from the reference's sums in the last float32 bits.
- * sem_embed packs sequences of >= 128 tokens first. Shorter sequences take the
- * CUDA-core kernel (and a float32 attention in the reference's order), so
- * their embeddings are bit-identical to the reference's; long-sequence rows
+ * sem_embed packs sequences of >= 128 tokens first. Shorter sequences (while
+ * a batch holds at most 4096 of their tokens; beyond that they take the
+ * tensor-core kernels as long rows do) take the CUDA-core kernel (and a
+ * float32 attention in the reference's order), so their embeddings are
+ * bit-identical to the reference's; long-sequence rows
  * take a tensor-core kernel (mean pooling over many tokens keeps the
  * difference within the reference's own spread between its builds).
  *   SEM_Q8_PATH_AUTO (default): long-sequence rows take the split-plane kernel
