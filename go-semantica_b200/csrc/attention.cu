@@ -107,6 +107,18 @@ __device__ __forceinline__ void umma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, ui
       : "memory");
 }
 
+// The same on an SM pair: M = 256 rows, A from both CTAs' TMEM at d/a, B
+// halves in both CTAs' shared memory at the descriptor's offsets.
+__device__ __forceinline__ void umma_f16_ts_pair(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc,
+                                                 uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], [%1], %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
 // Shared-memory descriptor of an MN-major operand tile with 128-byte swizzle:
 // rows of 128 bytes hold 64 consecutive MN elements, 8-row groups along K are
 // 1024 bytes apart (SBO), and the next 64 MN elements sit `lbo` bytes further.
@@ -123,8 +135,16 @@ __device__ __forceinline__ uint64_t umma_desc_mn_sw128(uint32_t saddr, uint32_t 
 }  // namespace
 
 // WIN: sliding-window layers (model-faithful mode). The full-attention
-// instance keeps the window tests out of its score loops.
-template <bool WIN>
+// instances keep the window tests out of their score loops.
+// PAIR: a cluster of two CTAs on an SM pair shares one 256-row query tile of
+// a (sequence, head): CTA r owns rows [128 r, +128) (its Q, TMEM rows, softmax
+// and output), and the leader's cta_group::2 MMAs (M = 256) read B halves from
+// both CTAs: keys [64 r, +64) of each 128-key tile for the scores, dims
+// [128 r, +128) of V for P.V. Each SM thus stages half the K/V bytes and reads
+// 6 KB of shared memory per score MMA instead of 8 KB (shared-memory bandwidth
+// bounds the single-SM kernel's N = 128 score MMAs). TMA copies of both CTAs
+// complete on the leader's barriers; MMA commits reach both CTAs'.
+template <bool WIN, bool PAIR>
 __global__ void __launch_bounds__(THREADS, 1)
     attention_tc_kernel(const __grid_constant__ CUtensorMap tm_qh, const __grid_constant__ CUtensorMap tm_ql,
                         const __grid_constant__ CUtensorMap tm_k1, const __grid_constant__ CUtensorMap tm_k2,
@@ -153,11 +173,13 @@ __global__ void __launch_bounds__(THREADS, 1)
   if (!err) err = &g_attn_error;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = PAIR ? cluster_ctarank() : 0u;
   // heads vary fastest, so the CTAs of one sequence (query tiles x heads) run
   // together and read its K and V from L2 rather than from DRAM
-  const int tile = blockIdx.x / nh, head = blockIdx.x % nh;
+  const int unit = PAIR ? (int)(blockIdx.x >> 1) : (int)blockIdx.x;
+  const int tile = unit / nh, head = unit % nh;
   const int seq = tiles.tile_seq[tile];
-  const int row0 = tiles.tile_row0[tile];
+  const int row0 = tiles.tile_row0[tile] + (int)rank * QT;  // this CTA's query rows
   const int s_beg = meta.cu_seqlens[seq], s_end = meta.cu_seqlens[seq + 1];
   const int n_rows = min(QT, s_end - row0);
   const int n_keys = s_end - s_beg;
@@ -171,19 +193,31 @@ __global__ void __launch_bounds__(THREADS, 1)
   const int nkt = n_keys > 0 ? jhi - jlo + 1 : 0;
   const int key0 = s_beg + jlo * KT;  // first key (token row) of tile 0 of the walk
 
+  constexpr int NCTA = PAIR ? 2 : 1;
   if (threadIdx.x == 0) {
     for (int i = 0; i < NBAR; ++i) mbar_init(&bars[i], 1);
-    mbar_init(pfull, SM_WARPS);
-    mbar_init(pfull + 1, SM_WARPS);
-    for (int k = 0; k < NS1; ++k) mbar_init(&s1empty[k], SM_WARPS);
+    mbar_init(pfull, NCTA * SM_WARPS);  // (the leader's) both CTAs' softmax warps
+    mbar_init(pfull + 1, NCTA * SM_WARPS);
+    for (int k = 0; k < NS1; ++k) mbar_init(&s1empty[k], NCTA * SM_WARPS);
     *abort_flag = 0;
     fence_mbar_init();
   }
-  if (warp == 1) tmem_alloc(s_tmem, 512);
+  if (warp == 1) {
+    if (PAIR)
+      tmem_alloc_pair(s_tmem, 512);
+    else
+      tmem_alloc(s_tmem, 512);
+  }
   tc_fence_before();
   __syncthreads();
+  if (PAIR) cluster_sync_all();  // both CTAs' barriers exist before any remote arrival
   tc_fence_after();
   const uint32_t tmem = *s_tmem;
+  // the leader's copy of one of this CTA's barriers (a shared::cluster address)
+  const uint32_t lead_bars = PAIR ? mapa_shared(smem_u32(bars), 0) : smem_u32(bars);
+  auto lbar = [&](const uint64_t* b) -> uint32_t {
+    return lead_bars + (uint32_t)(reinterpret_cast<const uint8_t*>(b) - reinterpret_cast<const uint8_t*>(bars));
+  };
 
   // Ring consumption order (128-key tiles): pass 1 = K hi of each tile, dims
   // 0-127 then 128-255 (two slots of [2 dim blocks][128 keys][128 B]); pass 2
@@ -202,57 +236,112 @@ __global__ void __launch_bounds__(THREADS, 1)
       const uint32_t me = warp >> 1;
       uint32_t it = 0;
       bool ok = true;
-      if (me == 0) {
-        mbar_arrive_expect_tx(qfull, SMEM_Q / 2);
+      // Q hi / Q lo of this CTA's rows (on a pair: completing on the leader's
+      // barrier, which expects both CTAs' bytes)
+      auto load_q = [&](const CUtensorMap* map, uint64_t* bar, uint8_t* dst) {
+        if (PAIR) {
+          if (rank == 0) mbar_arrive_expect_tx(bar, SMEM_Q);
 #pragma unroll
-        for (int b = 0; b < 4; ++b) tma_load_3d(&tm_qh, qfull, sQ + b * QBLK, b * 64, head, row0);
-      }
+          for (int b = 0; b < 4; ++b) tma_load_3d_pair(map, lbar(bar), dst + b * QBLK, b * 64, head, row0);
+        } else {
+          mbar_arrive_expect_tx(bar, SMEM_Q / 2);
+#pragma unroll
+          for (int b = 0; b < 4; ++b) tma_load_3d(map, bar, dst + b * QBLK, b * 64, head, row0);
+        }
+      };
+      if (me == 0) load_q(&tm_qh, qfull, sQ);
       // one slot: a 3-D box (pass 1) or a 4-D box whose outermost dimension is
       // the plane (pass 2)
-      auto load_slot = [&](const CUtensorMap* map, bool four, int key0, int dblk0) -> bool {
+      auto load_slot = [&](const CUtensorMap* map, bool four, int row, int dblk0) -> bool {
         if ((it & 1) != me) {
           ++it;
           return true;
         }
         const uint32_t s = it % NSLOT, u = it / NSLOT;
         if (!mbar_wait(&rempty[s], (u & 1) ^ 1, abort_flag, err, 1u)) return false;
-        mbar_arrive_expect_tx(&rfull[s], SLOT);
-        if (four)
-          tma_load_4d(map, &rfull[s], sRing + s * SLOT, 0, key0, dblk0, 0);  // 64 dims x rows x dim blocks x planes
-        else
-          tma_load_3d(map, &rfull[s], sRing + s * SLOT, 0, key0, dblk0);  // 64 dims x rows x dim blocks
+        if (PAIR) {
+          if (rank == 0) mbar_arrive_expect_tx(&rfull[s], 2 * SLOT);
+          if (four)
+            tma_load_4d_pair(map, lbar(&rfull[s]), sRing + s * SLOT, 0, row, dblk0, 0);
+          else
+            tma_load_3d_pair(map, lbar(&rfull[s]), sRing + s * SLOT, 0, row, dblk0);
+        } else {
+          mbar_arrive_expect_tx(&rfull[s], SLOT);
+          if (four)
+            tma_load_4d(map, &rfull[s], sRing + s * SLOT, 0, row, dblk0, 0);  // 64 dims x rows x dim blocks x planes
+          else
+            tma_load_3d(map, &rfull[s], sRing + s * SLOT, 0, row, dblk0);  // 64 dims x rows x dim blocks
+        }
         ++it;
         return true;
       };
+      // On a pair every slot holds this CTA's half: keys [64 r, +64) of a
+      // 128-key tile (K), or dims [128 r, +128) of 64 keys (V).
+      const int khalf = PAIR ? 64 * (int)rank : 0;
       for (int j = 0; ok && j < nkt; ++j) {
-        for (int h = 0; ok && h < 2; ++h) ok = load_slot(&tm_k1, false, key0 + j * KT, 2 * h);
-        if (j == 0 && me == 0) {  // Q lo behind the first K tile: pass 1 does not need it
-          mbar_arrive_expect_tx(qlofull, SMEM_Q / 2);
-#pragma unroll
-          for (int b = 0; b < 4; ++b) tma_load_3d(&tm_ql, qlofull, sQ + (4 + b) * QBLK, b * 64, head, row0);
+        if (PAIR)
+          ok = load_slot(&tm_k1, false, key0 + j * KT + khalf, 0);  // [4 dim blocks][64 keys][128 B]
+        else
+          for (int h = 0; ok && h < 2; ++h) ok = load_slot(&tm_k1, false, key0 + j * KT, 2 * h);
+        if (j == 0 && me == 0) load_q(&tm_ql, qlofull, sQ + 4 * QBLK);  // Q lo behind the first K tile
+      }
+      if (nkt == 0 && me == 0) load_q(&tm_ql, qlofull, sQ + 4 * QBLK);  // keep the barrier's one phase complete
+      for (int j = 0; ok && j <= nkt; ++j) {
+        if (PAIR) {
+          if (j < nkt)  // [hi, lo][2 dim blocks][64 keys][128 B], dim blocks 2h, 2h + 1
+            for (int h = 0; ok && h < 2; ++h) ok = load_slot(&tm_k2, true, key0 + j * KT + khalf, 2 * h);
+          if (j >= 1)  // [hi, lo][dim blocks 2r, 2r + 1][64 keys][128 B]
+            for (int kq = 0; ok && kq < 2; ++kq)
+              ok = load_slot(&tm_v2, true, key0 + (j - 1) * KT + 64 * kq, 2 * (int)rank);
+        } else {
+          if (j < nkt)
+            for (int db = 0; ok && db < 4; ++db) ok = load_slot(&tm_k2, true, key0 + j * KT, db);
+          if (j >= 1)
+            for (int kq = 0; ok && kq < KT / VKEYS; ++kq)
+              ok = load_slot(&tm_v2, true, key0 + (j - 1) * KT + kq * VKEYS, 0);
         }
       }
-      if (nkt == 0 && me == 0) {  // keep the barrier's one phase complete
-        mbar_arrive_expect_tx(qlofull, SMEM_Q / 2);
-#pragma unroll
-        for (int b = 0; b < 4; ++b) tma_load_3d(&tm_ql, qlofull, sQ + (4 + b) * QBLK, b * 64, head, row0);
+      // copies in flight land before shared memory is released (on a pair the
+      // leader's barriers count both CTAs' bytes, and the final cluster
+      // barrier keeps the peer alive until then)
+      if (rank == 0) {
+        for (uint32_t j = it > (uint32_t)NSLOT ? it - NSLOT : 0; j < it; ++j)
+          if ((j & 1) == me) mbar_wait_drain(&rfull[j % NSLOT], (j / NSLOT) & 1);
+        if (me == 0) {
+          mbar_wait_drain(qfull, 0);
+          mbar_wait_drain(qlofull, 0);
+        }
       }
-      for (int j = 0; ok && j <= nkt; ++j) {
-        if (j < nkt)
-          for (int db = 0; ok && db < 4; ++db) ok = load_slot(&tm_k2, true, key0 + j * KT, db);
-        if (j >= 1)
-          for (int kq = 0; ok && kq < KT / VKEYS; ++kq) ok = load_slot(&tm_v2, true, key0 + (j - 1) * KT + kq * VKEYS, 0);
-      }
-      for (uint32_t j = it > (uint32_t)NSLOT ? it - NSLOT : 0; j < it; ++j)
-        if ((j & 1) == me) mbar_wait_drain(&rfull[j % NSLOT], (j / NSLOT) & 1);
-      if (me == 0) {
-        mbar_wait_drain(qfull, 0);
-        mbar_wait_drain(qlofull, 0);
-      }
-    } else if (warp == 1 && lane == 0) {
-      // ---------------- MMA issuer ----------------
-      constexpr uint32_t idesc_qk = umma_idesc_f16_f32(QT, KT);  // N = 128 keys
-      constexpr uint32_t idesc_pv = umma_idesc_f16_f32(QT, HD) | (1u << 16);  // N = 256 dims, B (V) MN-major
+    } else if (warp == 1 && lane == 0 && rank == 0) {
+      // ---------------- MMA issuer (on a pair: the leader's, for both SMs) ----------------
+      constexpr uint32_t idesc_qk = umma_idesc_f16_f32(NCTA * QT, KT);  // N = 128 keys
+      constexpr uint32_t idesc_pv = umma_idesc_f16_f32(NCTA * QT, HD) | (1u << 16);  // N = 256 dims, B (V) MN-major
+      auto mma_ss = [&](uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+        if (PAIR)
+          umma_f16_pair(d, a, b, idesc, acc);
+        else
+          umma_f16(d, a, b, idesc, acc);
+      };
+      auto mma_ts = [&](uint32_t d, uint32_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+        if (PAIR)
+          umma_f16_ts_pair(d, a, b, idesc, acc);
+        else
+          umma_f16_ts(d, a, b, idesc, acc);
+      };
+      // completion of every MMA issued so far, signalled to both CTAs' (all)
+      // or only this CTA's (lead) copy of a barrier
+      auto commit_all = [&](uint64_t* bar) {
+        if (PAIR)
+          umma_commit_pair_mc(bar, 0x3);
+        else
+          umma_commit(bar);
+      };
+      auto commit_lead = [&](uint64_t* bar) {
+        if (PAIR)
+          umma_commit_pair_mc(bar, 0x1);
+        else
+          umma_commit(bar);
+      };
       uint32_t it = 0, sfill = 0;
       bool ok = mbar_wait(qfull, 0, abort_flag, err, 2u);
       tc_fence_after();
@@ -264,7 +353,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         addr = smem_u32(sRing + s * SLOT);
         return true;
       };
-      auto free_slot = [&]() { umma_commit(&rempty[it % NSLOT]); ++it; };
+      auto free_slot = [&]() { commit_all(&rempty[it % NSLOT]); ++it; };
       // pass 1: S1[buf] (NS1 buffers in the O columns) = q_hi . k_hi of a tile
       uint32_t fill1 = 0;
       auto qk1 = [&]() -> bool {
@@ -273,21 +362,34 @@ __global__ void __launch_bounds__(THREADS, 1)
         const uint32_t d_s = tmem + TM_O + b * KT;
         ++fill1;
         tc_fence_after();
-#pragma unroll 1
-        for (int h = 0; h < 2; ++h) {  // dims 0-127, then 128-255: one slot each
+        if (PAIR) {  // one slot: [4 dim blocks][64 keys][128 B] per CTA
           uint32_t k_a;
           if (!take_slot(k_a)) return false;
 #pragma unroll
-          for (int k16 = 0; k16 < 8; ++k16) {
-            const int db = 2 * h + k16 / 4;
+          for (int k16 = 0; k16 < 16; ++k16) {
+            const int db = k16 / 4;
             const uint32_t koff = (uint32_t)(k16 % 4) * 32;
-            const uint32_t kb = (uint32_t)(k16 / 4) * DBLK1 + koff;
-            umma_f16(d_s, umma_desc_k_sw128(q_hi + db * QBLK + koff), umma_desc_k_sw128(k_a + kb), idesc_qk,
-                     (h | k16) ? 1u : 0u);
+            mma_ss(d_s, umma_desc_k_sw128(q_hi + db * QBLK + koff), umma_desc_k_sw128(k_a + db * (64 * 128) + koff),
+                   idesc_qk, k16 ? 1u : 0u);
           }
           free_slot();
+        } else {
+#pragma unroll 1
+          for (int h = 0; h < 2; ++h) {  // dims 0-127, then 128-255: one slot each
+            uint32_t k_a;
+            if (!take_slot(k_a)) return false;
+#pragma unroll
+            for (int k16 = 0; k16 < 8; ++k16) {
+              const int db = 2 * h + k16 / 4;
+              const uint32_t koff = (uint32_t)(k16 % 4) * 32;
+              const uint32_t kb = (uint32_t)(k16 / 4) * DBLK1 + koff;
+              mma_ss(d_s, umma_desc_k_sw128(q_hi + db * QBLK + koff), umma_desc_k_sw128(k_a + kb), idesc_qk,
+                     (h | k16) ? 1u : 0u);
+            }
+            free_slot();
+          }
         }
-        umma_commit(&s1full[b]);
+        commit_all(&s1full[b]);
         return true;
       };
       // pass 2: S[buf] (two buffers at TM_S) = three-term scores of a tile
@@ -298,22 +400,40 @@ __global__ void __launch_bounds__(THREADS, 1)
         const uint32_t d_s = tmem + TM_S + b * KT;
         ++sfill;
         tc_fence_after();
+        if (PAIR) {
 #pragma unroll 1
-        for (int db = 0; db < 4; ++db) {  // one slot per 64-dim block: [hi, lo][128 keys][128 B]
-          uint32_t k_a;
-          if (!take_slot(k_a)) return false;
+          for (int h = 0; h < 2; ++h) {  // one slot per two 64-dim blocks: [hi, lo][2 dim blocks][64 keys][128 B]
+            uint32_t k_a;
+            if (!take_slot(k_a)) return false;
 #pragma unroll
-          for (int k16 = 0; k16 < 4; ++k16) {
-            const uint32_t koff = (uint32_t)k16 * 32;  // K=16 slice within the 128-byte row
-            const uint32_t qb = (uint32_t)db * QBLK + koff;
-            umma_f16(d_s, umma_desc_k_sw128(q_hi + qb), umma_desc_k_sw128(k_a + koff), idesc_qk,
-                     (db | k16) ? 1u : 0u);
-            umma_f16(d_s, umma_desc_k_sw128(q_hi + qb), umma_desc_k_sw128(k_a + PLANE + koff), idesc_qk, 1u);
-            umma_f16(d_s, umma_desc_k_sw128(q_lo + qb), umma_desc_k_sw128(k_a + koff), idesc_qk, 1u);
+            for (int k16 = 0; k16 < 8; ++k16) {
+              const int dbl = k16 / 4;
+              const uint32_t koff = (uint32_t)(k16 % 4) * 32;
+              const uint32_t qb = (uint32_t)(2 * h + dbl) * QBLK + koff;
+              const uint32_t kb = (uint32_t)dbl * (64 * 128) + koff;
+              mma_ss(d_s, umma_desc_k_sw128(q_hi + qb), umma_desc_k_sw128(k_a + kb), idesc_qk, (h | k16) ? 1u : 0u);
+              mma_ss(d_s, umma_desc_k_sw128(q_hi + qb), umma_desc_k_sw128(k_a + SLOT / 2 + kb), idesc_qk, 1u);
+              mma_ss(d_s, umma_desc_k_sw128(q_lo + qb), umma_desc_k_sw128(k_a + kb), idesc_qk, 1u);
+            }
+            free_slot();
           }
-          free_slot();
+        } else {
+#pragma unroll 1
+          for (int db = 0; db < 4; ++db) {  // one slot per 64-dim block: [hi, lo][128 keys][128 B]
+            uint32_t k_a;
+            if (!take_slot(k_a)) return false;
+#pragma unroll
+            for (int k16 = 0; k16 < 4; ++k16) {
+              const uint32_t koff = (uint32_t)k16 * 32;  // K=16 slice within the 128-byte row
+              const uint32_t qb = (uint32_t)db * QBLK + koff;
+              mma_ss(d_s, umma_desc_k_sw128(q_hi + qb), umma_desc_k_sw128(k_a + koff), idesc_qk, (db | k16) ? 1u : 0u);
+              mma_ss(d_s, umma_desc_k_sw128(q_hi + qb), umma_desc_k_sw128(k_a + PLANE + koff), idesc_qk, 1u);
+              mma_ss(d_s, umma_desc_k_sw128(q_lo + qb), umma_desc_k_sw128(k_a + koff), idesc_qk, 1u);
+            }
+            free_slot();
+          }
         }
-        umma_commit(&sfull[b]);
+        commit_all(&sfull[b]);
         return true;
       };
       // O += P(j) V(j), three terms
@@ -323,24 +443,27 @@ __global__ void __launch_bounds__(THREADS, 1)
         tc_fence_after();
         const uint32_t p_buf = tmem + TM_S + pb * KT;  // P written over the scores
         const uint32_t d_o = tmem + TM_O;
+        // a slot holds `keys` keys: [hi, lo][dim blocks][keys][128 B]; per CTA
+        // N = 256 dims (4 dim blocks VDBLK apart) or, on a pair, 128 (2 blocks)
+        constexpr int keys = PAIR ? 64 : VKEYS;
+        constexpr uint32_t lbo = PAIR ? 64 * 128 : VDBLK;
 #pragma unroll 1
-        for (int kq = 0; kq < KT / VKEYS; ++kq) {  // one slot per 32 keys: [hi, lo][4 dim blocks][32 keys][128 B]
+        for (int kq = 0; kq < KT / keys; ++kq) {
           uint32_t v_a;
           if (!take_slot(v_a)) return false;
 #pragma unroll
-          for (int k16 = 0; k16 < VKEYS / 16; ++k16) {
-            // keys 32kq + 16k16..: p_hi in 8 packed fp16 columns, then p_lo in the next 8
-            const uint32_t p_hi = p_buf + (uint32_t)(kq * (VKEYS / 16) + k16) * 16, p_lo = p_hi + 8;
+          for (int k16 = 0; k16 < keys / 16; ++k16) {
+            // keys (keys kq + 16 k16)..: p_hi in 8 packed fp16 columns, then p_lo in the next 8
+            const uint32_t p_hi = p_buf + (uint32_t)(kq * (keys / 16) + k16) * 16, p_lo = p_hi + 8;
             const uint32_t voff = (uint32_t)k16 * 2048;  // two 8-key groups of V rows
             const uint32_t acc0 = (j > 0 || kq > 0 || k16 > 0) ? 1u : 0u;
-            // N = 256: all dims at once (the four 64-dim blocks of a plane are VDBLK apart)
-            umma_f16_ts(d_o, p_hi, umma_desc_mn_sw128(v_a + voff, VDBLK), idesc_pv, acc0);
-            umma_f16_ts(d_o, p_hi, umma_desc_mn_sw128(v_a + PLANE + voff, VDBLK), idesc_pv, 1u);
-            umma_f16_ts(d_o, p_lo, umma_desc_mn_sw128(v_a + voff, VDBLK), idesc_pv, 1u);
+            mma_ts(d_o, p_hi, umma_desc_mn_sw128(v_a + voff, lbo), idesc_pv, acc0);
+            mma_ts(d_o, p_hi, umma_desc_mn_sw128(v_a + SLOT / 2 + voff, lbo), idesc_pv, 1u);
+            mma_ts(d_o, p_lo, umma_desc_mn_sw128(v_a + voff, lbo), idesc_pv, 1u);
           }
           free_slot();
         }
-        umma_commit(&pfree[pb]);
+        commit_lead(&pfree[pb]);
         return true;
       };
       for (int j = 0; ok && j < nkt; ++j) ok = qk1();
@@ -355,13 +478,20 @@ __global__ void __launch_bounds__(THREADS, 1)
           }
         if (ok && j >= 1) ok = pv(j - 1);
       }
-      umma_commit(ofull);
-      umma_commit(drain);
+      commit_all(ofull);
+      commit_lead(drain);
       mbar_wait_drain(drain, 0);
     }
   } else {
     asm volatile("setmaxnreg.inc.sync.aligned.u32 192;");
     // ---------------- softmax and epilogue ----------------
+    // arrivals the MMA issuer waits for go to the leader's barrier on a pair
+    auto arrive_lead = [&](uint64_t* b) {
+      if (PAIR)
+        mbar_arrive_cluster(lbar(b));
+      else
+        mbar_arrive(b);
+    };
     const int w = warp - 4;
     const int q = warp & 3;       // TMEM lane quarter
     const int half = w >> 2;      // keys [64*half, 64*half + 64) of each tile; O columns [128*half, +128)
@@ -398,7 +528,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         reg_barrier16(s[3]);
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&s1empty[b]);
+        if (lane == 0) arrive_lead(&s1empty[b]);
 #pragma unroll
         for (int c = 0; c < 64; ++c) {
           const int key = (jlo + j) * KT + half * 64 + c;
@@ -407,7 +537,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       } else {
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&s1empty[b]);
+        if (lane == 0) arrive_lead(&s1empty[b]);
       }
     }
     s_red[half * QT + r] = m;
@@ -464,7 +594,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&pfull[pb]);
+      if (lane == 0) arrive_lead(&pfull[pb]);
     }
     float l0, l1;
     unpack2(l2, l0, l1);
@@ -545,10 +675,16 @@ __global__ void __launch_bounds__(THREADS, 1)
 
   tc_fence_before();
   __syncthreads();
+  // on a pair: the leader's MMAs have drained and no copy or arrival is still
+  // aimed at either CTA
+  if (PAIR) cluster_sync_all();
   if (warp == 1) {
     __syncwarp();
     tc_fence_after();
-    tmem_dealloc(tmem, 512);
+    if (PAIR)
+      tmem_dealloc_pair(tmem, 512);
+    else
+      tmem_dealloc(tmem, 512);
   }
 }
 
@@ -629,8 +765,11 @@ std::mutex g_attn_mu;
 
 cudaError_t launch_attention(const __half* qh, const __half* ql, const __half* kh, const __half* kl, const __half* vh,
                              const __half* vl, int num_heads, float scale, int half_window, SeqMeta meta,
-                             AttnTiles tiles, float* out, uint32_t* absmax, uint32_t* err, cudaStream_t stream) {
-  if (tiles.n_tiles == 0) return cudaSuccess;
+                             AttnTiles tiles, AttnTiles pair_tiles, float* out, uint32_t* absmax, uint32_t* err,
+                             cudaStream_t stream) {
+  const bool windowed = half_window > 0 && half_window < (1 << 24);
+  const bool pair = !windowed && pair_tiles.n_tiles > 0;
+  if ((pair ? pair_tiles.n_tiles : tiles.n_tiles) == 0) return cudaSuccess;
   const int64_t T = meta.T;
   CUtensorMap m_qh, m_ql, m_k1, m_k2, m_v2, m_out;
   cudaError_t e;
@@ -638,11 +777,13 @@ cudaError_t launch_attention(const __half* qh, const __half* ql, const __half* k
   if (kl != kh + T * HD || vl != vh + T * HD) return cudaErrorInvalidValue;
   if ((e = map_q(&m_qh, qh, T, num_heads)) != cudaSuccess) return e;
   if ((e = map_q(&m_ql, ql, T, num_heads)) != cudaSuccess) return e;
-  // pass 1: K hi, 128 keys x 2 dim blocks; pass 2: K hi+lo, 128 keys x 1 dim
-  // block; V hi+lo, 32 keys x 4 dim blocks (32 KB per copy each)
-  if ((e = map_rows(&m_k1, kh, T, KT, 2)) != cudaSuccess) return e;
-  if ((e = map_rows_pair(&m_k2, kh, T, KT, 1)) != cudaSuccess) return e;
-  if ((e = map_rows_pair(&m_v2, vh, T, VKEYS, 4)) != cudaSuccess) return e;
+  // One CTA: pass 1 K hi, 128 keys x 2 dim blocks; pass 2 K hi+lo, 128 keys x
+  // 1 dim block; V hi+lo, 32 keys x 4 dim blocks. A pair's CTA: pass 1 K hi,
+  // 64 keys x 4 dim blocks; pass 2 K hi+lo, 64 keys x 2 dim blocks; V hi+lo,
+  // 64 keys x 2 dim blocks. 32 KB per copy in every case.
+  if ((e = map_rows(&m_k1, kh, T, pair ? 64 : KT, pair ? 4 : 2)) != cudaSuccess) return e;
+  if ((e = map_rows_pair(&m_k2, kh, T, pair ? 64 : KT, pair ? 2 : 1)) != cudaSuccess) return e;
+  if ((e = map_rows_pair(&m_v2, vh, T, pair ? 64 : VKEYS, pair ? 2 : 4)) != cudaSuccess) return e;
   {  // out [T][nh * 256] fp32: boxes of 32 floats x 128 rows, 128-byte swizzle
     auto enc = attn_encoder();
     if (!enc) return cudaErrorNotSupported;
@@ -661,21 +802,39 @@ cudaError_t launch_attention(const __half* qh, const __half* ql, const __half* k
   {
     std::lock_guard<std::mutex> lk(g_attn_mu);
     if (dev >= 0 && dev < 64 && !g_attn_attr[dev]) {
-      if ((e = cudaFuncSetAttribute(attention_tc_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+      if ((e = cudaFuncSetAttribute(attention_tc_kernel<false, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                     SMEM_BYTES)) != cudaSuccess ||
-          (e = cudaFuncSetAttribute(attention_tc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+          (e = cudaFuncSetAttribute(attention_tc_kernel<true, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    SMEM_BYTES)) != cudaSuccess ||
+          (e = cudaFuncSetAttribute(attention_tc_kernel<false, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                     SMEM_BYTES)) != cudaSuccess)
         return e;
       g_attn_attr[dev] = true;
     }
   }
+  if (pair) {  // clusters of two CTAs: 256-row query tiles
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * pair_tiles.n_tiles * num_heads);
+    cfg.blockDim = dim3(THREADS);
+    cfg.dynamicSmemBytes = SMEM_BYTES;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, attention_tc_kernel<false, true>, m_qh, m_ql, m_k1, m_k2, m_v2, m_out, num_heads,
+                              scale, 1 << 24, meta, pair_tiles, out, absmax, err);
+  }
   dim3 grid(tiles.n_tiles * num_heads);
-  if (half_window > 0 && half_window < (1 << 24))
-    attention_tc_kernel<true><<<grid, THREADS, SMEM_BYTES, stream>>>(m_qh, m_ql, m_k1, m_k2, m_v2, m_out, num_heads,
-                                                                     scale, half_window, meta, tiles, out, absmax, err);
+  if (windowed)
+    attention_tc_kernel<true, false><<<grid, THREADS, SMEM_BYTES, stream>>>(
+        m_qh, m_ql, m_k1, m_k2, m_v2, m_out, num_heads, scale, half_window, meta, tiles, out, absmax, err);
   else
-    attention_tc_kernel<false><<<grid, THREADS, SMEM_BYTES, stream>>>(m_qh, m_ql, m_k1, m_k2, m_v2, m_out, num_heads,
-                                                                      scale, 1 << 24, meta, tiles, out, absmax, err);
+    attention_tc_kernel<false, false><<<grid, THREADS, SMEM_BYTES, stream>>>(
+        m_qh, m_ql, m_k1, m_k2, m_v2, m_out, num_heads, scale, 1 << 24, meta, tiles, out, absmax, err);
   return cudaGetLastError();
 }
 

@@ -53,6 +53,7 @@ struct sem_model {
   std::vector<int32_t> last_offsets, last_dims;
   int32_t n_tiles = 0;
   int32_t n_tiles_long = 0;  // attention tiles of the long sequences (first in the tile list)
+  int32_t n_ptiles = 0, n_ptiles_long = 0;  // 256-row tiles of the SM-pair attention (all, long sequences')
   int32_t short_max_len = 0; // longest sequence under kSplitMinLen tokens
   int64_t t_long = 0;     // packed rows of the long sequences (first in the packed order)
   bool permuted = false;  // packed order differs from the caller's
@@ -357,7 +358,8 @@ int ensure_workspace(sem_model* m, int64_t T, int B, int64_t out_floats) {
   SEM_CUDA(m->inv_rms.ensure((size_t)Tp * 4));
   // meta: row_seq[T], row_pos[T], cu[B+1], tile_seq/tile_row0[2*(T/64+B)], out_dims[B], out_off (int64) [B],
   // src_row[T]
-  size_t meta_ints = (size_t)3 * Tp + (B + 1) + 2 * ((size_t)Tp / 64 + B + 1) + B + 2 * (size_t)B + B + 10;
+  size_t meta_ints = (size_t)3 * Tp + (B + 1) + 2 * ((size_t)Tp / 64 + B + 1) + B + 2 * (size_t)B + B +
+                     2 * ((size_t)Tp / 256 + B + 1) + 10;
   SEM_CUDA(m->meta.ensure(meta_ints * 4));
   SEM_CUDA(m->absmax.ensure((size_t)(4 * c.num_layers + 1) * (B > 0 ? B : 1) * 4));
   SEM_CUDA(m->ids.ensure((size_t)Tp * 4));
@@ -380,6 +382,8 @@ struct MetaPtrs {
   SeqMeta seq;
   AttnTiles tiles;        // 128-row attention tiles of the long sequences (tensor-core kernel)
   AttnTiles short_tiles;  // one tile per short sequence (float32 CUDA-core kernel)
+  AttnTiles pair_tiles;   // 256-row tiles of the long sequences (SM-pair tensor-core kernel)
+  AttnTiles pair_all;     // 256-row tiles of every sequence
   int32_t short_max_len;  // longest short sequence
   int32_t* out_dims;
   int64_t* out_off;
@@ -422,6 +426,9 @@ int upload_meta(sem_model* m, const int32_t* offsets, int B, const int32_t* dims
   p = (p + 7) & ~uintptr_t(7);
   int64_t* d_off = reinterpret_cast<int64_t*>(p);
   int32_t* d_iota = reinterpret_cast<int32_t*>(d_off + B);
+  const int64_t max_ptiles = T / 256 + B + 1;
+  int32_t* d_pseq = d_iota + B;
+  int32_t* d_prow = d_pseq + max_ptiles;
   bool same = (int)m->last_offsets.size() == B + 1 &&
               std::memcmp(m->last_offsets.data(), offsets, sizeof(int32_t) * (B + 1)) == 0 &&
               (int)m->last_dims.size() == B && std::memcmp(m->last_dims.data(), dims, sizeof(int32_t) * B) == 0;
@@ -445,7 +452,7 @@ int upload_meta(sem_model* m, const int32_t* offsets, int B, const int32_t* dims
       caller_off[s] = acc;
       acc += dims[s];
     }
-    size_t bytes = (size_t)(reinterpret_cast<uint8_t*>(d_iota + B) - reinterpret_cast<uint8_t*>(base));
+    size_t bytes = (size_t)(reinterpret_cast<uint8_t*>(d_prow + max_ptiles) - reinterpret_cast<uint8_t*>(base));
     // a request slot's own staging is free (its previous request completed);
     // the shared pinned buffer may still feed an earlier copy
     HostBuf& hb = staging ? *staging : m->ctx->pinned;
@@ -462,8 +469,10 @@ int upload_meta(sem_model* m, const int32_t* offsets, int B, const int32_t* dims
     int64_t* h_off = reinterpret_cast<int64_t*>(reinterpret_cast<uint8_t*>(h) +
                                                 (reinterpret_cast<uint8_t*>(d_off) - reinterpret_cast<uint8_t*>(base)));
     int32_t* h_iota = reinterpret_cast<int32_t*>(h_off + B);
+    int32_t* h_pseq = h_iota + B;
+    int32_t* h_prow = h_pseq + max_ptiles;
     for (int s = 0; s < B; ++s) h_iota[s] = s;
-    int32_t nt = 0, nt_long = 0, short_max = 0;
+    int32_t nt = 0, nt_long = 0, short_max = 0, np = 0, np_long = 0;
     int32_t r = 0;
     for (int s = 0; s < B; ++s) {
       const int o = order[s];
@@ -481,6 +490,12 @@ int upload_meta(sem_model* m, const int32_t* offsets, int B, const int32_t* dims
         h_trow[nt] = r + i;
         ++nt;
       }
+      for (int32_t i = 0; i < len; i += 2 * kAttnTileRows) {
+        h_pseq[np] = s;
+        h_prow[np] = r + i;
+        ++np;
+      }
+      if (len >= kSplitMinLen) np_long = np;
       h_dims[s] = dims[o];
       h_off[s] = caller_off[o];
       r += len;
@@ -491,6 +506,8 @@ int upload_meta(sem_model* m, const int32_t* offsets, int B, const int32_t* dims
     m->last_dims.assign(dims, dims + B);
     m->n_tiles = nt;
     m->n_tiles_long = nt_long;
+    m->n_ptiles = np;
+    m->n_ptiles_long = np_long;
     m->short_max_len = short_max;
     m->t_long = t_long;
     m->permuted = permuted;
@@ -499,6 +516,12 @@ int upload_meta(sem_model* m, const int32_t* offsets, int B, const int32_t* dims
   mp->tiles = AttnTiles{d_tseq, d_trow, m->n_tiles_long};
   mp->short_max_len = m->short_max_len;
   mp->short_tiles = AttnTiles{d_tseq + m->n_tiles_long, d_trow + m->n_tiles_long, m->n_tiles - m->n_tiles_long};
+  // SM-pair attention (256-row tiles) unless sequences of 128-255 tokens would
+  // leave more than a quarter of its CTAs without rows: then 128-row tiles
+  const bool pairs_long = 8 * m->n_ptiles_long <= 5 * m->n_tiles_long;
+  const bool pairs_all = 8 * m->n_ptiles <= 5 * m->n_tiles;
+  mp->pair_tiles = AttnTiles{d_pseq, d_prow, pairs_long ? m->n_ptiles_long : 0};
+  mp->pair_all = AttnTiles{d_pseq, d_prow, pairs_all ? m->n_ptiles : 0};
   mp->out_dims = d_dims;
   mp->out_off = d_off;
   mp->iota = d_iota;
@@ -599,14 +622,14 @@ int run_forward(sem_model* m, const int32_t* d_ids, const MetaPtrs& mp, float* d
     if (exact_short) {  // tensor cores for the long sequences' tiles, float32 CUDA cores for the short ones
       if (mp.tiles.n_tiles)
         SEM_LAUNCH(kStAttention, launch_attention(qh, ql, kh, kl, vh, vl, nh, c.attention_scale, hw, sm, mp.tiles,
-                                                  att, slot(l, 1), err, st));
+                                                  mp.pair_tiles, att, slot(l, 1), err, st));
       if (mp.short_tiles.n_tiles)
         SEM_LAUNCH(kStAttnShort, launch_attention_short(big, nh, c.attention_scale, hw, sm, mp.short_tiles,
                                                         mp.short_max_len, att, slot(l, 1), st));
     } else {
       const AttnTiles all{mp.tiles.tile_seq, mp.tiles.tile_row0, mp.tiles.n_tiles + mp.short_tiles.n_tiles};
-      SEM_LAUNCH(kStAttention, launch_attention(qh, ql, kh, kl, vh, vl, nh, c.attention_scale, hw, sm, all, att,
-                                                slot(l, 1), err, st));
+      SEM_LAUNCH(kStAttention, launch_attention(qh, ql, kh, kl, vh, vl, nh, c.attention_scale, hw, sm, all,
+                                                mp.pair_all, att, slot(l, 1), err, st));
     }
     SEM_LAUNCH(kStQuant, launch_quantize(att, nullptr, nullptr, H, sm, slot(l, 1), codes, st));
     SEM_LAUNCH(kStGemmO, q8(w.o, H, H, slot(l, 1), big, H, kEpiStore, nullptr));

@@ -169,12 +169,14 @@ struct AttnTiles {
 // kl == kh + T * 256 and vl == vh + T * 256: the lo planes follow the hi ones),
 // all 16-byte aligned. out [T][num_heads*256] fp32, absmax[seq] atomically.
 // half_window > 0: a sliding-window layer, query i sees keys j with
-// |i - j| <= half_window (0: every key). `err` (nullable) receives error bits
-// if a pipeline wait times out.
+// |i - j| <= half_window (0: every key). Full attention with pair_tiles (256-
+// row query tiles: tile_row0 and tile_row0 + 128, n_tiles > 0) runs on SM
+// pairs; otherwise one CTA per 128-row tile of `tiles`. `err` (nullable)
+// receives error bits if a pipeline wait times out.
 cudaError_t launch_attention(const __half* qh, const __half* ql, const __half* kh, const __half* kl,
                              const __half* vh, const __half* vl, int num_heads, float scale, int half_window,
-                             SeqMeta meta, AttnTiles tiles, float* out, uint32_t* absmax, uint32_t* err,
-                             cudaStream_t stream);
+                             SeqMeta meta, AttnTiles tiles, AttnTiles pair_tiles, float* out, uint32_t* absmax,
+                             uint32_t* err, cudaStream_t stream);
 
 // Float32 attention of sequences shorter than 128 tokens in the reference's
 // order (attention_short.cu): qkv rows [q (nh*256) | k | v] float32 with q and

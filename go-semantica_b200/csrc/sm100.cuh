@@ -268,6 +268,14 @@ __device__ __forceinline__ void tma_load_3d_pair(const CUtensorMap* map, uint32_
       "l"(map), "r"(cbar), "r"(c0), "r"(c1), "r"(c2)
       : "memory");
 }
+__device__ __forceinline__ void tma_load_4d_pair(const CUtensorMap* map, uint32_t cbar, void* dst, int c0, int c1,
+                                                 int c2, int c3) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, "
+      "%5, %6}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(map), "r"(cbar), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+      : "memory");
+}
 // TMEM of both CTAs: one warp with the same warp index in each CTA.
 __device__ __forceinline__ void tmem_alloc_pair(uint32_t* dst_smem, uint32_t ncols) {
   asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst_smem)),
