@@ -16,7 +16,7 @@
 // kernel (attention.cu) serves longer sequences, whose keys do not fit in
 // shared memory as float32.
 //
-// One CTA = 16 queries of one head of one sequence. K (float32, the lanes of
+// One CTA = 8 queries of one head of one sequence. K (float32, the lanes of
 // each row apart so a lane reads its 32 elements with eight 16-byte loads)
 // fills shared memory for the scores; V then replaces it for the weighted sum.
 // q and k are the head-normed, RoPE'd float32 rows the Q/K norm kernel writes
@@ -30,8 +30,9 @@ namespace sem {
 namespace {
 
 constexpr int kHd = 256;
-constexpr int kAsQ = 16;           // queries per CTA
-constexpr int kAsQBlocks = 8;      // 8 x 16 covers a 127-token sequence
+constexpr int kAsQ = 8;            // queries per CTA
+constexpr int kAsQBlocks = 16;     // 16 x 8 covers a 127-token sequence
+constexpr int kAsKParts = 32 / kAsQ;  // 8-lane groups per query: each scores every kAsKParts-th key
 constexpr int kAsMaxKeys = 127;    // sequences shorter than 128 tokens
 constexpr int kAsThreads = 256;
 constexpr int kKLane = 36;         // words per lane of a K row: 32 elements + 4 (bank spread)
@@ -54,8 +55,8 @@ __global__ void __launch_bounds__(kAsThreads, 1)
                            uint32_t* __restrict__ absmax) {
   extern __shared__ __align__(16) float as_smem[];
   float* KV = as_smem;                    // K [L][8][kKLane], then V [L][256]
-  float* S = KV + as_kv_words(max_len);   // scores, then e = fastExp(s - max) [16][128]
-  float* Pt = S + kAsQ * 128;         // probabilities, transposed [128][16]
+  float* S = KV + as_kv_words(max_len);   // scores, then e = fastExp(s - max) [kAsQ][128]
+  float* Pt = S + kAsQ * 128;         // probabilities, transposed [128][kAsQ]
   __shared__ float red[kAsThreads / 32];
   const int per_tile = nh * kAsQBlocks;
   const int tile = blockIdx.x / per_tile;
@@ -69,18 +70,29 @@ __global__ void __launch_bounds__(kAsThreads, 1)
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, l = tid & 7, g = tid >> 3;
 
   // ---- K rows: element 8v + lane at [j][lane][v] ----
+  // (loads batched eight deep: the stores wait for them, the next loads do not)
   const float* kbase = qkv + (size_t)r0 * ld + nh * kHd;
-  for (int i = tid; i < L * 64; i += kAsThreads) {
-    const int j = i >> 6, p = i & 63;  // elements 4p .. 4p + 3: lanes 4 (p & 1) + e, v = p / 2
-    const float4 x = *reinterpret_cast<const float4*>(kbase + (size_t)j * ld + 4 * p);
-    float* dst = KV + j * kKRow + 4 * (p & 1) * kKLane + (p >> 1);
-    dst[0] = x.x;
-    dst[kKLane] = x.y;
-    dst[2 * kKLane] = x.z;
-    dst[3 * kKLane] = x.w;
+  for (int i0 = tid; i0 < L * 64; i0 += 8 * kAsThreads) {
+    float4 x[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int i = i0 + u * kAsThreads;
+      if (i < L * 64) x[u] = *reinterpret_cast<const float4*>(kbase + (size_t)(i >> 6) * ld + 4 * (i & 63));
+    }
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int i = i0 + u * kAsThreads;
+      if (i >= L * 64) break;
+      const int j = i >> 6, p = i & 63;  // elements 4p .. 4p + 3: lanes 4 (p & 1) + e, v = p / 2
+      float* dst = KV + j * kKRow + 4 * (p & 1) * kKLane + (p >> 1);
+      dst[0] = x[u].x;
+      dst[kKLane] = x[u].y;
+      dst[2 * kKLane] = x[u].z;
+      dst[3 * kKLane] = x[u].w;
+    }
   }
   // ---- this group's query lane: elements 8v + l of q_i ----
-  const int i = g & 15, jpar = g >> 4;  // groups of one warp share jpar: uniform loop bounds
+  const int i = g % kAsQ, jpar = g / kAsQ;  // groups of one warp share jpar: uniform loop bounds
   float qr[32];
   if (i < nq) {
     const float* qrow = qkv + (size_t)(r0 + q0 + i) * ld + h * kHd + l;
@@ -93,11 +105,11 @@ __global__ void __launch_bounds__(kAsThreads, 1)
   __syncthreads();
 
   // ---- scores: four keys per pass (independent accumulation chains) ----
-  for (int j0 = jpar; j0 < L; j0 += 8) {
+  for (int j0 = jpar; j0 < L; j0 += 4 * kAsKParts) {
     const float4* kr[4];
 #pragma unroll
     for (int k = 0; k < 4; ++k)  // keys past the sequence recompute its last key and are not stored
-      kr[k] = reinterpret_cast<const float4*>(KV + min(j0 + 2 * k, L - 1) * kKRow + l * kKLane);
+      kr[k] = reinterpret_cast<const float4*>(KV + min(j0 + kAsKParts * k, L - 1) * kKRow + l * kKLane);
     float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
     for (int u = 0; u < 8; ++u) {
@@ -113,7 +125,7 @@ __global__ void __launch_bounds__(kAsThreads, 1)
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
       const float d = group_hsum8(acc[k]);
-      const int j = j0 + 2 * k;
+      const int j = j0 + kAsKParts * k;
       if (l == 0 && i < nq && j < L) S[i * 128 + j] = __fmul_rn(d, scale);
     }
   }
@@ -158,7 +170,7 @@ __global__ void __launch_bounds__(kAsThreads, 1)
   cp_async_wait<0>();
   __syncthreads();
 
-  // ---- out_i[d] for the 16 queries, thread d ----
+  // ---- out_i[d] for the CTA's queries, thread d ----
   const int d = tid;
   float o[kAsQ];
 #pragma unroll

@@ -31,6 +31,7 @@
 // 16-byte shared-memory load; block scales are the runtime f16 decoder's fp32
 // values (model_int8.go:543-597).
 #include <mutex>
+#include <type_traits>
 
 #include "common.cuh"
 #include "kernels.h"
@@ -41,12 +42,12 @@ namespace {
 constexpr int kDpThreads = 256;  // 32 groups of 8 lane threads
 constexpr int kDpStages = 3;     // weight-chunk ring
 constexpr int kDpChunk = 12;     // blocks per weight chunk (K % 384 == 0), else 4
-constexpr int kDpCtasPerSm = 3;
+constexpr int kDpCtasPerSm = 2;
 
 // Words between the lanes of one row in shared memory: a multiple of 4 whose
 // quarter is odd, so the 8 lanes of a group read 8 different bank quads.
-__host__ __device__ inline int dp_lane_stride(int blocks) { return ((blocks / 4) & 1) ? blocks : blocks + 4; }
-__host__ __device__ inline int dp_chunk(int kb_total) { return kb_total % kDpChunk == 0 ? kDpChunk : 4; }
+__host__ __device__ constexpr int dp_lane_stride(int blocks) { return ((blocks / 4) & 1) ? blocks : blocks + 4; }
+__host__ __device__ constexpr int dp_chunk(int kb_total) { return kb_total % kDpChunk == 0 ? kDpChunk : 4; }
 
 // 8 INT8 codes held as fp16 integers in [-127, 127] -> two words of int8.
 // h + 1152 lies in [1025, 1279], where fp16 steps by 1, so the low byte of its
@@ -93,7 +94,10 @@ __device__ __forceinline__ float dp_gelu_up(float g, float u, float rs) {
 // kEpiGeluUp: a group's 4 rows are gate j, j + 1 and up j, j + 1, so it forms
 // two outputs h = GELUQuick(gate) * up per token, and the CTA the per-sequence
 // absmax of h over all its tiles.
-template <int TGM, int EPI>
+// KBT: the blocks per row (K / 32) when known at compile time (the model's
+// K = 768, 1152 and 3072), so the shared-memory strides fold into the load
+// instructions; 0 takes K at run time.
+template <int TGM, int EPI, int KBT>
 __global__ void __launch_bounds__(kDpThreads, kDpCtasPerSm) gemm_q8_dp4a_kernel(
     const __half* __restrict__ a, const uint32_t* __restrict__ wl, const float* __restrict__ ws, int M, int N, int K,
     const uint32_t* __restrict__ a_absmax, const int32_t* __restrict__ row_seq, float* __restrict__ c,
@@ -103,7 +107,7 @@ __global__ void __launch_bounds__(kDpThreads, kDpCtasPerSm) gemm_q8_dp4a_kernel(
   __shared__ float s_rs[TM];
   __shared__ int s_seq[TM];
   __shared__ uint32_t s_amax[TM];
-  const int KB = K / 32, KW = K / 4;  // blocks and words per row
+  const int KB = KBT > 0 ? KBT : K / 32, KW = 8 * KB;  // blocks and words per row
   const int kbc = dp_chunk(KB), pieces = kbc / 4, nchunks = KB / kbc;
   const int la = dp_lane_stride(KB), lw = dp_lane_stride(kbc);
   uint32_t* As = dp_smem;                // [TM][8][la] activation words, all of K
@@ -122,22 +126,46 @@ __global__ void __launch_bounds__(kDpThreads, kDpCtasPerSm) gemm_q8_dp4a_kernel(
     const int j = nt * (TN / 2) + 2 * (slot >> 2) + (q & 1);
     return q < 2 ? j : half + j;
   };
+  // This thread's share of every item's copies is the same list of (shared
+  // offset, global offset) pairs, shifted per item by the weight tile and the
+  // K chunk: computed once here (a weight tile's rows move by TN rows per
+  // tile, or TN / 2 gate and up rows each under kEpiGeluUp).
+  constexpr int kMaxW = (TN * 8 * 3 + kDpThreads - 1) / kDpThreads;  // pieces <= 3
+  const int64_t tile_rows = EPI == kEpiStore ? TN : TN / 2;
+  int w_soff[kMaxW], w_goff[kMaxW];  // word offsets (a weight plane holds < 2^31 words)
+  int n_w = 0;
+#pragma unroll
+  for (int k = 0; k < kMaxW; ++k) {
+    const int i = tid + k * kDpThreads;
+    w_soff[k] = 0;
+    w_goff[k] = 0;
+    if (i < TN * 8 * pieces) {
+      const int p = i % pieces, rest = i / pieces, ll = rest & 7, slot = rest >> 3;
+      w_soff[k] = (slot * 8 + ll) * lw + 4 * p;
+      w_goff[k] = wrow(0, slot) * KW + ll * KB + 4 * p;
+      n_w = k + 1;
+    }
+  }
+  int s_soff = -1, s_goff = 0;
+  if (tid < TN * pieces) {
+    const int p = tid % pieces, slot = tid / pieces;
+    s_soff = slot * lw + 4 * p;
+    s_goff = wrow(0, slot) * KB + 4 * p;
+  }
   // one (tile, chunk) item's weights and block scales into its stage;
   // every thread commits a group per call (empty past the end) so the wait
   // counts stay uniform
   auto issue = [&](int item) {
     if (item < items) {
-      const int nt = (int)blockIdx.x + (item / nchunks) * (int)gridDim.x, kc0 = (item % nchunks) * kbc;
+      const int tix = item / nchunks, kc0 = (item - tix * nchunks) * kbc;
+      const int64_t nt = (int64_t)blockIdx.x + (int64_t)tix * gridDim.x;
       uint32_t* Ws = ring + (item % kDpStages) * stage_words;
       float* Ss = reinterpret_cast<float*>(Ws + TN * 8 * lw);
-      for (int i = tid; i < TN * 8 * pieces; i += kDpThreads) {
-        const int p = i % pieces, rest = i / pieces, ll = rest & 7, slot = rest >> 3;
-        cp_async16(Ws + (slot * 8 + ll) * lw + 4 * p, wl + (size_t)wrow(nt, slot) * KW + ll * KB + kc0 + 4 * p, true);
-      }
-      for (int i = tid; i < TN * pieces; i += kDpThreads) {
-        const int p = i % pieces, slot = i / pieces;
-        cp_async16(Ss + slot * lw + 4 * p, ws + (size_t)wrow(nt, slot) * KB + kc0 + 4 * p, true);
-      }
+      const uint32_t* wsrc = wl + nt * tile_rows * KW + kc0;
+#pragma unroll
+      for (int k = 0; k < kMaxW; ++k)
+        if (k < n_w) cp_async16(Ws + w_soff[k], wsrc + w_goff[k], true);
+      if (s_soff >= 0) cp_async16(Ss + s_soff, ws + nt * tile_rows * KB + kc0 + s_goff, true);
     }
     cp_async_commit();
   };
@@ -193,7 +221,7 @@ __global__ void __launch_bounds__(kDpThreads, kDpCtasPerSm) gemm_q8_dp4a_kernel(
     const uint32_t* Ws = ring + (it % kDpStages) * stage_words;
     const float* Ss = reinterpret_cast<const float*>(Ws + TN * 8 * lw);
     const int kc0 = (it % nchunks) * kbc;
-#pragma unroll 1
+#pragma unroll
     for (int p = 0; p < pieces; ++p) {
       uint4 av[4];
 #pragma unroll
@@ -256,7 +284,7 @@ __global__ void __launch_bounds__(kDpThreads, kDpCtasPerSm) gemm_q8_dp4a_kernel(
     atomicMax(&out_absmax[s_seq[tid]], s_amax[tid]);
 }
 
-template <int TGM, int EPI>
+template <int TGM, int EPI, int KBT>
 cudaError_t launch_dp(const __half* a, const int8_t* wl, const float* ws, int M, int N, int K, const uint32_t* a_absmax,
                       const int32_t* row_seq, float* c, uint32_t* out_absmax, cudaStream_t stream) {
   constexpr int TM = 4 * TGM, TN = 4 * (32 / TGM);
@@ -264,7 +292,7 @@ cudaError_t launch_dp(const __half* a, const int8_t* wl, const float* ws, int M,
   const size_t smem =
       ((size_t)TM * 8 * dp_lane_stride(KB) + (size_t)kDpStages * (TN * 8 + TN) * dp_lane_stride(kbc)) * 4;
   if (smem > 200 * 1024) return cudaErrorInvalidValue;  // K up to 3072 fits
-  auto kern = gemm_q8_dp4a_kernel<TGM, EPI>;
+  auto kern = gemm_q8_dp4a_kernel<TGM, EPI, KBT>;
   int sms = 148;
   {  // per-device: the shared-memory limit (a function attribute) and the SM count
     static std::mutex mu;
@@ -297,6 +325,18 @@ cudaError_t launch_dp(const __half* a, const int8_t* wl, const float* ws, int M,
   return cudaGetLastError();
 }
 
+// Calls f with std::integral_constant<int, K / 32> for the model's K values,
+// else with 0 (K at run time).
+template <class F>
+cudaError_t dispatch_dp(int K, F&& f) {
+  switch (K) {
+    case 768: return f(std::integral_constant<int, 24>{});
+    case 1152: return f(std::integral_constant<int, 36>{});
+    case 3072: return f(std::integral_constant<int, 96>{});
+    default: return f(std::integral_constant<int, 0>{});
+  }
+}
+
 }  // namespace
 
 cudaError_t launch_gemm_q8_dp4a(const __half* a_codes, const int8_t* w_lanes, const float* w_scales, int M, int N,
@@ -310,13 +350,18 @@ cudaError_t launch_gemm_q8_dp4a(const __half* a_codes, const int8_t* w_lanes, co
     return cudaErrorMisalignedAddress;
   // 32-token tiles halve the weight re-reads; below 17 tokens 16-row weight
   // tiles give twice as many CTAs
-  if (epilogue == kEpiGeluUp)
-    return M <= 16 ? launch_dp<8, kEpiGeluUp>(a_codes, w_lanes, w_scales, M, N, K, a_absmax, row_seq, c, out_absmax,
-                                             stream)
-                   : launch_dp<4, kEpiGeluUp>(a_codes, w_lanes, w_scales, M, N, K, a_absmax, row_seq, c, out_absmax,
-                                             stream);
-  return M <= 16 ? launch_dp<8, kEpiStore>(a_codes, w_lanes, w_scales, M, N, K, a_absmax, row_seq, c, nullptr, stream)
-                 : launch_dp<4, kEpiStore>(a_codes, w_lanes, w_scales, M, N, K, a_absmax, row_seq, c, nullptr, stream);
+  return dispatch_dp(K, [&](auto kbt) {
+    constexpr int KBT = decltype(kbt)::value;
+    if (epilogue == kEpiGeluUp)
+      return M <= 16 ? launch_dp<8, kEpiGeluUp, KBT>(a_codes, w_lanes, w_scales, M, N, K, a_absmax, row_seq, c,
+                                                    out_absmax, stream)
+                     : launch_dp<4, kEpiGeluUp, KBT>(a_codes, w_lanes, w_scales, M, N, K, a_absmax, row_seq, c,
+                                                    out_absmax, stream);
+    return M <= 16 ? launch_dp<8, kEpiStore, KBT>(a_codes, w_lanes, w_scales, M, N, K, a_absmax, row_seq, c, nullptr,
+                                                 stream)
+                   : launch_dp<4, kEpiStore, KBT>(a_codes, w_lanes, w_scales, M, N, K, a_absmax, row_seq, c, nullptr,
+                                                 stream);
+  });
 }
 
 // Q8_0 blocks of `rows` x `cols` -> the int8 plane of the CUDA-core kernel:
