@@ -486,8 +486,9 @@ __global__ void __launch_bounds__(THREADS, 1)
     asm volatile("setmaxnreg.inc.sync.aligned.u32 192;");
     // ---------------- softmax and epilogue ----------------
     // arrivals the MMA issuer waits for go to the leader's barrier on a pair
+    // (the leader's own warps arrive locally: no cluster-scope release)
     auto arrive_lead = [&](uint64_t* b) {
-      if (PAIR)
+      if (PAIR && rank != 0)
         mbar_arrive_cluster(lbar(b));
       else
         mbar_arrive(b);
