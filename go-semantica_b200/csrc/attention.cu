@@ -192,6 +192,11 @@ __global__ void __launch_bounds__(THREADS, 1)
   const int jhi = windowed ? min(n_keys - 1, q_pos0 + n_rows - 1 + hw) / KT : (n_keys - 1) / KT;
   const int nkt = n_keys > 0 ? jhi - jlo + 1 : 0;
   const int key0 = s_beg + jlo * KT;  // first key (token row) of tile 0 of the walk
+  // pass 1 (row maxima) takes 256-key tiles on a pair (N = 256 MMAs into
+  // O's columns and the two score buffers, all free until pass 2), 128-key
+  // tiles on one CTA
+  constexpr int KT1 = PAIR ? 2 * KT : KT;
+  const int nkt1 = PAIR ? (n_keys + KT1 - 1) / KT1 : nkt;
 
   constexpr int NCTA = PAIR ? 2 : 1;
   if (threadIdx.x == 0) {
@@ -278,11 +283,10 @@ __global__ void __launch_bounds__(THREADS, 1)
       // On a pair every slot holds this CTA's half: keys [64 r, +64) of a
       // 128-key tile (K), or dims [128 r, +128) of 64 keys (V).
       const int khalf = PAIR ? 64 * (int)rank : 0;
-      for (int j = 0; ok && j < nkt; ++j) {
-        if (PAIR)
-          ok = load_slot(&tm_k1, false, key0 + j * KT + khalf, 0);  // [4 dim blocks][64 keys][128 B]
-        else
-          for (int h = 0; ok && h < 2; ++h) ok = load_slot(&tm_k1, false, key0 + j * KT, 2 * h);
+      // pass 1: per key tile (KT1 keys; on a pair this CTA's half of 256)
+      // two slots, [2 dim blocks][128 keys][128 B] each
+      for (int j = 0; ok && j < nkt1; ++j) {
+        for (int h = 0; ok && h < 2; ++h) ok = load_slot(&tm_k1, false, key0 + j * KT1 + 2 * khalf, 2 * h);
         if (j == 0 && me == 0) load_q(&tm_ql, qlofull, sQ + 4 * QBLK);  // Q lo behind the first K tile
       }
       if (nkt == 0 && me == 0) load_q(&tm_ql, qlofull, sQ + 4 * QBLK);  // keep the barrier's one phase complete
@@ -354,40 +358,30 @@ __global__ void __launch_bounds__(THREADS, 1)
         return true;
       };
       auto free_slot = [&]() { commit_all(&rempty[it % NSLOT]); ++it; };
-      // pass 1: S1[buf] (NS1 buffers in the O columns) = q_hi . k_hi of a tile
+      // pass 1: S1[buf] = q_hi . k_hi of a tile; one CTA: NS1 128-column
+      // buffers in the O columns; a pair: N = 256, buffer 0 in O's columns,
+      // buffer 1 in the two score buffers' (pass 2 has not started)
+      constexpr uint32_t idesc_qk1 = umma_idesc_f16_f32(NCTA * QT, KT1);
       uint32_t fill1 = 0;
       auto qk1 = [&]() -> bool {
         const uint32_t b = fill1 % NS1, ub = fill1 / NS1;
         if (!mbar_wait(&s1empty[b], (ub & 1) ^ 1, abort_flag, err, 2u)) return false;
-        const uint32_t d_s = tmem + TM_O + b * KT;
+        const uint32_t d_s = PAIR ? tmem + (b ? TM_S : TM_O) : tmem + TM_O + b * KT;
         ++fill1;
         tc_fence_after();
-        if (PAIR) {  // one slot: [4 dim blocks][64 keys][128 B] per CTA
+#pragma unroll 1
+        for (int h = 0; h < 2; ++h) {  // dims 0-127, then 128-255: one slot each ([2 dim blocks][128 keys][128 B])
           uint32_t k_a;
           if (!take_slot(k_a)) return false;
 #pragma unroll
-          for (int k16 = 0; k16 < 16; ++k16) {
-            const int db = k16 / 4;
+          for (int k16 = 0; k16 < 8; ++k16) {
+            const int db = 2 * h + k16 / 4;
             const uint32_t koff = (uint32_t)(k16 % 4) * 32;
-            mma_ss(d_s, umma_desc_k_sw128(q_hi + db * QBLK + koff), umma_desc_k_sw128(k_a + db * (64 * 128) + koff),
-                   idesc_qk, k16 ? 1u : 0u);
+            const uint32_t kb = (uint32_t)(k16 / 4) * DBLK1 + koff;
+            mma_ss(d_s, umma_desc_k_sw128(q_hi + db * QBLK + koff), umma_desc_k_sw128(k_a + kb), idesc_qk1,
+                   (h | k16) ? 1u : 0u);
           }
           free_slot();
-        } else {
-#pragma unroll 1
-          for (int h = 0; h < 2; ++h) {  // dims 0-127, then 128-255: one slot each
-            uint32_t k_a;
-            if (!take_slot(k_a)) return false;
-#pragma unroll
-            for (int k16 = 0; k16 < 8; ++k16) {
-              const int db = 2 * h + k16 / 4;
-              const uint32_t koff = (uint32_t)(k16 % 4) * 32;
-              const uint32_t kb = (uint32_t)(k16 / 4) * DBLK1 + koff;
-              mma_ss(d_s, umma_desc_k_sw128(q_hi + db * QBLK + koff), umma_desc_k_sw128(k_a + kb), idesc_qk,
-                     (h | k16) ? 1u : 0u);
-            }
-            free_slot();
-          }
         }
         commit_all(&s1full[b]);
         return true;
@@ -466,16 +460,22 @@ __global__ void __launch_bounds__(THREADS, 1)
         commit_lead(&pfree[pb]);
         return true;
       };
-      for (int j = 0; ok && j < nkt; ++j) ok = qk1();
+      for (int j = 0; ok && j < nkt1; ++j) ok = qk1();
       if (ok) ok = mbar_wait(qlofull, 0, abort_flag, err, 2u);
+      // the softmax has read every pass-1 buffer before pass 2 writes the
+      // score buffers (a pair) or P.V the O columns (one CTA)
+      auto drained1 = [&]() -> bool {
+        for (int k = 0; k < NS1 && k < nkt1; ++k) {
+          const int last = k + NS1 * ((nkt1 - 1 - k) / NS1);
+          if (!mbar_wait(&s1empty[k], (last / NS1) & 1, abort_flag, err, 2u)) return false;
+        }
+        return true;
+      };
+      if (PAIR && ok) ok = drained1();
       tc_fence_after();
       for (int j = 0; ok && j <= nkt; ++j) {
         if (j < nkt) ok = qk();
-        if (ok && j == 1)  // the softmax has read every pass-1 buffer before P.V overwrites the O columns
-          for (int k = 0; ok && k < NS1 && k < nkt; ++k) {
-            const int last = k + NS1 * ((nkt - 1 - k) / NS1);
-            ok = mbar_wait(&s1empty[k], (last / NS1) & 1, abort_flag, err, 2u);
-          }
+        if (!PAIR && ok && j == 1) ok = drained1();
         if (ok && j >= 1) ok = pv(j - 1);
       }
       commit_all(ofull);
@@ -513,27 +513,34 @@ __global__ void __launch_bounds__(THREADS, 1)
     };
     // ---- pass 1: row max of the fp16 scores ----
     float m = -INFINITY;
-    for (int j = 0; j < nkt; ++j) {
+    for (int j = 0; j < nkt1; ++j) {
       const uint32_t b = j % NS1;
       if (ok) ok = mbar_wait(&s1full[b], (j / NS1) & 1, abort_flag, err, 4u);
       ok = __all_sync(0xffffffffu, ok);
       tc_fence_after();
       if (ok) {
-        uint32_t s[4][16];  // this half's 64 keys of the 128-key tile
-        const uint32_t col = TM_O + b * KT + half * 64;
+        // this half's KT1 / 2 keys of the tile, 64 at a time
+        const uint32_t col0 = PAIR ? (b ? TM_S : TM_O) + half * (KT1 / 2) : TM_O + b * KT + half * 64;
+#pragma unroll 1
+        for (int sub = 0; sub < KT1 / 128; ++sub) {
+          uint32_t s[4][16];
+          const uint32_t col = col0 + sub * 64;
 #pragma unroll
-        for (int c = 0; c < 4; ++c) tmem_ld16_w(t_lane + col + 16 * c, s[c]);
-        tmem_wait_regs(s[0]);
-        reg_barrier16(s[1]);
-        reg_barrier16(s[2]);
-        reg_barrier16(s[3]);
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) arrive_lead(&s1empty[b]);
+          for (int c = 0; c < 4; ++c) tmem_ld16_w(t_lane + col + 16 * c, s[c]);
+          tmem_wait_regs(s[0]);
+          reg_barrier16(s[1]);
+          reg_barrier16(s[2]);
+          reg_barrier16(s[3]);
+          if (sub + 1 == KT1 / 128) {  // every score of the buffer is in registers
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) arrive_lead(&s1empty[b]);
+          }
 #pragma unroll
-        for (int c = 0; c < 64; ++c) {
-          const int key = (jlo + j) * KT + half * 64 + c;
-          if (key_ok(key)) m = fmaxf(m, __fmul_rn(__uint_as_float(s[c >> 4][c & 15]), scale));
+          for (int c = 0; c < 64; ++c) {
+            const int key = (jlo * KT) + j * KT1 + half * (KT1 / 2) + sub * 64 + c;
+            if (key_ok(key)) m = fmaxf(m, __fmul_rn(__uint_as_float(s[c >> 4][c & 15]), scale));
+          }
         }
       } else {
         tc_fence_before();
@@ -780,9 +787,9 @@ cudaError_t launch_attention(const __half* qh, const __half* ql, const __half* k
   if ((e = map_q(&m_ql, ql, T, num_heads)) != cudaSuccess) return e;
   // One CTA: pass 1 K hi, 128 keys x 2 dim blocks; pass 2 K hi+lo, 128 keys x
   // 1 dim block; V hi+lo, 32 keys x 4 dim blocks. A pair's CTA: pass 1 K hi,
-  // 64 keys x 4 dim blocks; pass 2 K hi+lo, 64 keys x 2 dim blocks; V hi+lo,
-  // 64 keys x 2 dim blocks. 32 KB per copy in every case.
-  if ((e = map_rows(&m_k1, kh, T, pair ? 64 : KT, pair ? 4 : 2)) != cudaSuccess) return e;
+  // 128 keys (its half of 256) x 2 dim blocks; pass 2 K hi+lo, 64 keys x 2
+  // dim blocks; V hi+lo, 64 keys x 2 dim blocks. 32 KB per copy in every case.
+  if ((e = map_rows(&m_k1, kh, T, KT, 2)) != cudaSuccess) return e;
   if ((e = map_rows_pair(&m_k2, kh, T, pair ? 64 : KT, pair ? 2 : 1)) != cudaSuccess) return e;
   if ((e = map_rows_pair(&m_v2, vh, T, pair ? 64 : VKEYS, pair ? 2 : 4)) != cudaSuccess) return e;
   {  // out [T][nh * 256] fp32: boxes of 32 floats x 128 rows, 128-byte swizzle
