@@ -836,13 +836,15 @@ int model_embed_submit(sem_model* m, const int32_t* ids, const int32_t* offsets,
   uint32_t* flags = sl.flags.as<uint32_t>();
   flags[0] = flags[1] = 0;
   sl.out_floats = out_floats;
-  if (B > 0) {
+  auto enqueue = [&]() -> int {
+    if (B == 0) return SEM_OK;
     const int64_t T = offsets[B];
     int rc;
     if ((rc = ensure_workspace(m, T, B, out_floats))) return rc;
     MetaPtrs mp;
     if ((rc = upload_meta(m, offsets, B, dims.data(), &mp, &sl.meta))) return rc;
     SEM_CUDA(sl.ids.ensure((size_t)T * 4));
+    SEM_CUDA(sl.out.ensure((size_t)out_floats * 4));
     std::memcpy(sl.ids.p, ids, (size_t)T * 4);
     if (mp.permuted) {
       SEM_CUDA(m->ids_in.ensure((size_t)T * 4));
@@ -852,10 +854,16 @@ int model_embed_submit(sem_model* m, const int32_t* ids, const int32_t* offsets,
       SEM_CUDA(cudaMemcpyAsync(m->ids.p, sl.ids.p, (size_t)T * 4, cudaMemcpyHostToDevice, ctx->stream));
     }
     if ((rc = forward_maybe_graph(m, mp, offsets, dims.data(), ctx->stream))) return rc;
-    SEM_CUDA(sl.out.ensure((size_t)out_floats * 4));
     SEM_CUDA(cudaMemcpyAsync(sl.out.p, m->out.p, (size_t)out_floats * 4, cudaMemcpyDeviceToHost, ctx->stream));
     SEM_CUDA(cudaMemcpyAsync(flags, m->errflag.p, 8, cudaMemcpyDeviceToHost, ctx->stream));
     SEM_CUDA(cudaMemsetAsync(m->errflag.p, 0, 8, ctx->stream));
+    return SEM_OK;
+  };
+  if (int rc = enqueue()) {
+    // part of the request may be enqueued already and still read the
+    // slot's pinned buffers: let it finish before the slot is reused
+    cudaStreamSynchronize(ctx->stream);
+    return rc;
   }
   SEM_CUDA(cudaEventRecord(sl.done, ctx->stream));
   sl.busy = true;
