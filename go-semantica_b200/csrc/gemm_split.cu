@@ -78,7 +78,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kXThreads, 1)
     gemm_q8_pair_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_a,
                         const float* __restrict__ row_scale, int n_out, int T, int K,
                         const uint32_t* __restrict__ a_absmax, const int32_t* __restrict__ row_seq,
-                        float* __restrict__ c_out, uint32_t* __restrict__ err) {
+                        float* __restrict__ c_out, uint32_t* __restrict__ err, VPlanes vp) {
   constexpr int ST = kXStages;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
@@ -225,6 +225,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kXThreads, 1)
       const int tok0 = tt * kXPairTok + half * TPH;  // first token of this thread's half
       const float rsc = live ? row_scale[n0] : 0.0f;
       float* dst = c_out + (size_t)tok0 * n_out + n0;
+      // a tile of V columns (uniform: the V block starts on a 128-row tile)
+      // goes to the attention's fp16 hi / lo planes instead
+      const bool vtile = vp.hi && (2 * wt + (int)rank) * kXRows >= vp.col0;
+      __half* vhp = vtile ? vp.hi + (size_t)tok0 * 256 + (n0 - vp.col0) : nullptr;
+      __half* vlp = vtile ? vhp + (size_t)vp.rows * 256 : nullptr;
 #pragma unroll 1
       for (int c = 0; c < TPH / 16; c += 2) {
         uint32_t r[2][16];
@@ -239,14 +244,30 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kXThreads, 1)
           if (lane == 0) mbar_arrive_cluster(lead_tempty + 8 * b);
         }
         if (!live) continue;
+        if (!vtile) {
 #pragma unroll
-        for (int cc = 0; cc < 2; ++cc)
+          for (int cc = 0; cc < 2; ++cc)
 #pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            const int x = (c + cc) * 16 + i;
-            if (tok0 + x < T)  // warp-uniform
-              dst[(size_t)x * n_out] = __fmul_rn(__fmul_rn(__uint_as_float(r[cc][i]), rsc), c_rs[x]);
-          }
+            for (int i = 0; i < 16; ++i) {
+              const int x = (c + cc) * 16 + i;
+              if (tok0 + x < T)  // warp-uniform
+                dst[(size_t)x * n_out] = __fmul_rn(__fmul_rn(__uint_as_float(r[cc][i]), rsc), c_rs[x]);
+            }
+        } else {
+#pragma unroll
+          for (int cc = 0; cc < 2; ++cc)
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+              const int x = (c + cc) * 16 + i;
+              if (tok0 + x < T) {  // warp-uniform
+                const float v = __fmul_rn(__fmul_rn(__uint_as_float(r[cc][i]), rsc), c_rs[x]);
+                __half hi, lo;
+                split_half(v, hi, lo);
+                vhp[(size_t)x * 256] = hi;
+                vlp[(size_t)x * 256] = lo;
+              }
+            }
+        }
       }
     }
   }
@@ -471,7 +492,9 @@ bool g_split_attr[64];
 std::mutex g_split_mu;
 
 cudaError_t launch_pair(const __half* a_codes, const __half* w_hi, const float* row_scale, int T, int n_out, int K,
-                        const uint32_t* a_absmax, const int32_t* row_seq, float* c, uint32_t* err, cudaStream_t stream) {
+                        const uint32_t* a_absmax, const int32_t* row_seq, float* c, uint32_t* err, cudaStream_t stream,
+                        const VPlanes& vp) {
+  if (vp.hi && (vp.col0 % kXRows != 0 || n_out - vp.col0 != 256 || vp.rows < T)) return cudaErrorInvalidValue;
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
@@ -506,7 +529,7 @@ cudaError_t launch_pair(const __half* a_codes, const __half* w_hi, const float* 
   const int total = n_wt * ((T + kXPairTok - 1) / kXPairTok);
   const int pairs = total < sms / 2 ? total : sms / 2;
   gemm_q8_pair_kernel<<<2 * pairs, kXThreads, kXSmem, stream>>>(tm_w, tm_a, row_scale, n_out, T, K, a_absmax,
-                                                                row_seq, c, err);
+                                                                row_seq, c, err, vp);
   return cudaGetLastError();
 }
 
@@ -556,7 +579,8 @@ cudaError_t launch_gateup(const __half* a_codes, const __half* w_hi, const __hal
 
 cudaError_t launch_gemm_q8_split(const __half* a_codes, const __half* w_hi, const __half* w_lo, const float* row_scale,
                                  int M, int N, int K, const uint32_t* a_absmax, const int32_t* row_seq, float* c,
-                                 int epilogue, uint32_t* out_absmax, uint32_t* err, cudaStream_t stream) {
+                                 int epilogue, uint32_t* out_absmax, uint32_t* err, cudaStream_t stream,
+                                 const VPlanes& vp) {
   if (M == 0) return cudaSuccess;
   if (M < 0 || K <= 0 || K % kXK != 0) return cudaErrorInvalidValue;
   if (w_lo != w_hi + (size_t)N * K) return cudaErrorInvalidValue;  // one map covers both planes
@@ -566,7 +590,7 @@ cudaError_t launch_gemm_q8_split(const __half* a_codes, const __half* w_hi, cons
                          err, stream);
   }
   if (N % kXRows != 0) return cudaErrorInvalidValue;
-  return launch_pair(a_codes, w_hi, row_scale, M, N, K, a_absmax, row_seq, c, err, stream);
+  return launch_pair(a_codes, w_hi, row_scale, M, N, K, a_absmax, row_seq, c, err, stream, vp);
 }
 
 namespace {
@@ -581,19 +605,18 @@ int set_q8_path(int mode) {
 
 int get_q8_path() { return g_q8_path.load(std::memory_order_relaxed); }
 
-cudaError_t launch_q8_proj(const __half* a_codes, const Q8Proj& w, int M, int N, int K, const uint32_t* a_absmax,
-                           const int32_t* row_seq, float* c, int epilogue, uint32_t* out_absmax, uint32_t* err,
-                           cudaStream_t stream) {
+namespace {
+enum Q8Kernel { kQ8Dp4a, kQ8Split, kQ8Block };
+
+// The kernel launch_q8_proj takes for these operands (see kernels.h).
+Q8Kernel q8_choice(const Q8Proj& w, int M, int N, int K, int epilogue) {
   const int path = g_q8_path.load(std::memory_order_relaxed);
   // Below 128 rows (and everywhere under path 4) the CUDA-core kernel: the
   // reference's VNNI float32 order exactly, and no tensor-core pipeline to
   // fill for a handful of tiles.
-  if (w.lanes && (path == 4 || (path == 0 && M < kDp4aMaxRows)))
-    return launch_gemm_q8_dp4a(a_codes, w.lanes, w.scales, M, N, K, a_absmax, row_seq, c, epilogue, out_absmax, stream);
+  if (w.lanes && (path == 4 || (path == 0 && M < kDp4aMaxRows))) return kQ8Dp4a;
   if (path != 1 && w.hi && w.lo && w.row_scale && K % kXK == 0) {
-    if (path >= 2)
-      return launch_gemm_q8_split(a_codes, w.hi, w.lo, w.row_scale, M, N, K, a_absmax, row_seq, c, epilogue,
-                                  out_absmax, err, stream);
+    if (path >= 2) return kQ8Split;
     int dev = 0, sms = 148;
     if (cudaGetDevice(&dev) == cudaSuccess && dev >= 0 && dev < 64) {
       std::lock_guard<std::mutex> lk(g_split_mu);
@@ -603,11 +626,30 @@ cudaError_t launch_q8_proj(const __half* a_codes, const Q8Proj& w, int M, int N,
     // 128-row x 256-token units (a pair tile is two): the measured crossover
     // is about half a wave of them
     const int64_t tiles = (int64_t)(N / (epilogue == kEpiGeluUp ? 2 : 1) / kXRows) * ((M + 255) / 256);
-    if (2 * tiles >= sms)
-      return launch_gemm_q8_split(a_codes, w.hi, w.lo, w.row_scale, M, N, K, a_absmax, row_seq, c, epilogue,
-                                  out_absmax, err, stream);
+    if (2 * tiles >= sms) return kQ8Split;
   }
-  return launch_gemm_q8(a_codes, w.codes, w.scales, M, N, K, a_absmax, row_seq, c, epilogue, out_absmax, err, stream);
+  return kQ8Block;
+}
+}  // namespace
+
+bool q8_proj_writes_v(const Q8Proj& w, int M, int N, int K, int epilogue) {
+  return M > 0 && epilogue == kEpiStore && q8_choice(w, M, N, K, epilogue) == kQ8Split;
+}
+
+cudaError_t launch_q8_proj(const __half* a_codes, const Q8Proj& w, int M, int N, int K, const uint32_t* a_absmax,
+                           const int32_t* row_seq, float* c, int epilogue, uint32_t* out_absmax, uint32_t* err,
+                           cudaStream_t stream, const VPlanes& vp) {
+  switch (q8_choice(w, M, N, K, epilogue)) {
+    case kQ8Dp4a:
+      return launch_gemm_q8_dp4a(a_codes, w.lanes, w.scales, M, N, K, a_absmax, row_seq, c, epilogue, out_absmax,
+                                 stream);
+    case kQ8Split:
+      return launch_gemm_q8_split(a_codes, w.hi, w.lo, w.row_scale, M, N, K, a_absmax, row_seq, c, epilogue,
+                                  out_absmax, err, stream, epilogue == kEpiStore ? vp : VPlanes{});
+    default:
+      return launch_gemm_q8(a_codes, w.codes, w.scales, M, N, K, a_absmax, row_seq, c, epilogue, out_absmax, err,
+                            stream);
+  }
 }
 
 }  // namespace sem

@@ -584,10 +584,10 @@ int run_forward(sem_model* m, const int32_t* d_ids, const MetaPtrs& mp, float* d
   // projection and attention kernels, as long sequences do.
   const bool exact_short = q8_path == 4 || (q8_path == 0 && T - mp.T_long <= kExactShortMaxTokens);
   auto q8 = [&](const Q8Proj& w, int N, int K, const uint32_t* a_absmax, float* out, int out_cols, int epi,
-                uint32_t* out_absmax) -> cudaError_t {
+                uint32_t* out_absmax, const VPlanes& vp = VPlanes{}) -> cudaError_t {
     cudaError_t e = cudaSuccess;
     if (t_split > 0)
-      e = launch_q8_proj(codes, w, (int)t_split, N, K, a_absmax, sm.row_seq, out, epi, out_absmax, err, st);
+      e = launch_q8_proj(codes, w, (int)t_split, N, K, a_absmax, sm.row_seq, out, epi, out_absmax, err, st, vp);
     if (e == cudaSuccess && T > t_split) {
       if (!exact_short)
         e = launch_gemm_q8(codes + t_split * K, w.codes, w.scales, (int)(T - t_split), N, K, a_absmax,
@@ -615,10 +615,15 @@ int run_forward(sem_model* m, const int32_t* d_ids, const MetaPtrs& mp, float* d
     const bool sliding = fa.sliding_window > 0 && fa.swa_pattern > 0 && (l + 1) % fa.swa_pattern != 0;
     const int hw = sliding ? fa.sliding_window / 2 : 0;
     // attention block (model_int8.go:191-210)
-    SEM_LAUNCH(kStGemmQKV, q8(w.qkv, qkvN, H, slot(l, 0), big, qkvN, kEpiStore, nullptr));
+    // the long rows' V columns go straight to the attention's hi / lo planes
+    // when the split-plane kernel projects them
+    const bool v_planes = t_split > 0 && q8_proj_writes_v(w.qkv, (int)t_split, qkvN, H, kEpiStore);
+    SEM_LAUNCH(kStGemmQKV, q8(w.qkv, qkvN, H, slot(l, 0), big, qkvN, kEpiStore, nullptr,
+                              v_planes ? VPlanes{vh, T, nh * hd + hd} : VPlanes{}));
     SEM_LAUNCH(kStQKNormRope, launch_qk_norm_rope(big, w.q_norm, w.k_norm, sliding ? swa_cos : m->rope_cos,
                                                   sliding ? swa_sin : m->rope_sin, c.norm_eps, nh, sm, qh, ql, kh, kl,
-                                                  vh, vl, exact_short ? mp.T_long : T, st));
+                                                  vh, vl, exact_short ? mp.T_long : T,
+                                                  v_planes ? t_split : 0, st));
     if (exact_short) {  // tensor cores for the long sequences' tiles, float32 CUDA cores for the short ones
       if (mp.tiles.n_tiles)
         SEM_LAUNCH(kStAttention, launch_attention(qh, ql, kh, kl, vh, vl, nh, c.attention_scale, hw, sm, mp.tiles,

@@ -42,6 +42,16 @@ struct SeqMeta {
   int32_t B;                // sequences
 };
 
+// Where a QKV projection may put its V columns: [col0, col0 + 256) of each
+// row as the attention's fp16 hi and lo planes (hi[row][256], lo = hi + rows
+// * 256) instead of the float32 output. Only the split-plane kernel does so
+// (q8_proj_writes_v says whether a call will).
+struct VPlanes {
+  __half* hi = nullptr;
+  int64_t rows = 0;
+  int col0 = 0;
+};
+
 cudaError_t launch_embed(const int32_t* ids, const int8_t* emb_codes, const float* emb_scales, int vocab,
                          int H, float* hidden, int T, uint32_t* err_flag, cudaStream_t stream);
 
@@ -67,10 +77,11 @@ cudaError_t launch_absmax(const float* x, int64_t n, uint32_t* slot, cudaStream_
 // hi/lo fp16 split of q, k, v for attention. qkv rows: [q (nh*256) | k (256) | v (256)].
 // Rows >= f32_row0 also get their normed, RoPE'd q and k written back into qkv
 // as float32 (the input of launch_attention_short).
+// Rows below v_row0 have their V planes already (written by the projection).
 cudaError_t launch_qk_norm_rope(float* qkv, const float* q_norm, const float* k_norm, const float* rope_cos,
                                 const float* rope_sin, float eps, int num_heads, SeqMeta meta, __half* qh,
                                 __half* ql, __half* kh, __half* kl, __half* vh, __half* vl, int64_t f32_row0,
-                                cudaStream_t stream);
+                                int64_t v_row0, cudaStream_t stream);
 
 // hidden = rmsnorm(o, post_w) + hidden and inv_rms of the new rows for the
 // next norm (next_w); with codes (and absmax) also the next norm's output
@@ -115,7 +126,8 @@ cudaError_t launch_gemm_q8(const __half* a_codes, const __half* w_codes, const f
 // (gate/up: N/2 % 128 == 0). Same epilogues and outputs as launch_gemm_q8.
 cudaError_t launch_gemm_q8_split(const __half* a_codes, const __half* w_hi, const __half* w_lo, const float* row_scale,
                                  int M, int N, int K, const uint32_t* a_absmax, const int32_t* row_seq, float* c,
-                                 int epilogue, uint32_t* out_absmax, uint32_t* err, cudaStream_t stream);
+                                 int epilogue, uint32_t* out_absmax, uint32_t* err, cudaStream_t stream,
+                                 const VPlanes& vp = VPlanes{});
 
 // The same product on CUDA cores in the reference's VNNI lane order
 // (gemm_dp4a.cu): bit-identical to matmulInnerLoopVNNIAsm + the unfused
@@ -150,7 +162,8 @@ struct Q8Proj {
 constexpr int kDp4aMaxRows = 128;
 cudaError_t launch_q8_proj(const __half* a_codes, const Q8Proj& w, int M, int N, int K, const uint32_t* a_absmax,
                            const int32_t* row_seq, float* c, int epilogue, uint32_t* out_absmax, uint32_t* err,
-                           cudaStream_t stream);
+                           cudaStream_t stream, const VPlanes& vp = VPlanes{});
+bool q8_proj_writes_v(const Q8Proj& w, int M, int N, int K, int epilogue);
 // Process-wide kernel choice: 0 auto, 1 per-block, 2 split-plane (launch_q8_proj
 // always; the forward's long-sequence rows), 3 split-plane for every forward
 // row, 4 the CUDA-core VNNI-order kernel for every row; returns the previous

@@ -402,7 +402,7 @@ __global__ void __launch_bounds__(kQkWarps * 32)
                         const float* __restrict__ rope_sin, float eps, int nh, SeqMeta meta,
                         __half* __restrict__ qh, __half* __restrict__ ql, __half* __restrict__ kh,
                         __half* __restrict__ kl, __half* __restrict__ vh, __half* __restrict__ vl,
-                        int64_t f32_row0) {
+                        int64_t f32_row0, int64_t v_row0) {
   __shared__ __align__(16) float sh[kQkWarps][4 * kHeadPad];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, g = lane >> 3, sub = lane & 7;
   const int64_t nwarps = (int64_t)gridDim.x * kQkWarps;
@@ -482,16 +482,19 @@ __global__ void __launch_bounds__(kQkWarps * 32)
         }
       }
     }
-    // v: all 32 lanes, 8 consecutive elements each
-    const float4* vx = reinterpret_cast<const float4*>(base + (nh + 1) * kHeadDim + lane * 8);
-    float vv[8];
-    *reinterpret_cast<float4*>(vv) = vx[0];
-    *reinterpret_cast<float4*>(vv + 4) = vx[1];
-    __half hv[8], lv[8];
+    // v: all 32 lanes, 8 consecutive elements each (rows below v_row0: the
+    // projection wrote the planes)
+    if (row >= v_row0) {
+      const float4* vx = reinterpret_cast<const float4*>(base + (nh + 1) * kHeadDim + lane * 8);
+      float vv[8];
+      *reinterpret_cast<float4*>(vv) = vx[0];
+      *reinterpret_cast<float4*>(vv + 4) = vx[1];
+      __half hv[8], lv[8];
 #pragma unroll
-    for (int k = 0; k < 8; ++k) split_half(vv[k], hv[k], lv[k]);
-    *reinterpret_cast<uint4*>(vh + row * kHeadDim + lane * 8) = *reinterpret_cast<uint4*>(hv);
-    *reinterpret_cast<uint4*>(vl + row * kHeadDim + lane * 8) = *reinterpret_cast<uint4*>(lv);
+      for (int k = 0; k < 8; ++k) split_half(vv[k], hv[k], lv[k]);
+      *reinterpret_cast<uint4*>(vh + row * kHeadDim + lane * 8) = *reinterpret_cast<uint4*>(hv);
+      *reinterpret_cast<uint4*>(vl + row * kHeadDim + lane * 8) = *reinterpret_cast<uint4*>(lv);
+    }
     __syncwarp();  // the row buffer is reloaded next
   }
 }
@@ -499,13 +502,13 @@ __global__ void __launch_bounds__(kQkWarps * 32)
 cudaError_t launch_qk_norm_rope(float* qkv, const float* q_norm, const float* k_norm, const float* rope_cos,
                                 const float* rope_sin, float eps, int num_heads, SeqMeta meta, __half* qh,
                                 __half* ql, __half* kh, __half* kl, __half* vh, __half* vl, int64_t f32_row0,
-                                cudaStream_t stream) {
+                                int64_t v_row0, cudaStream_t stream) {
   if (meta.T == 0) return cudaSuccess;
   if (num_heads < 1 || num_heads > 3) return cudaErrorInvalidValue;
   int64_t blocks = (meta.T + kQkWarps - 1) / kQkWarps;
   if (blocks > 148 * 8) blocks = 148 * 8;
   qk_norm_rope_kernel<<<(unsigned)blocks, kQkWarps * 32, 0, stream>>>(qkv, q_norm, k_norm, rope_cos, rope_sin, eps, num_heads,
-                                                            meta, qh, ql, kh, kl, vh, vl, f32_row0);
+                                                            meta, qh, ql, kh, kl, vh, vl, f32_row0, v_row0);
   return cudaGetLastError();
 }
 
