@@ -632,20 +632,19 @@ Q8Kernel q8_choice(const Q8Proj& w, int M, int N, int K, int epilogue) {
 }
 }  // namespace
 
-bool q8_proj_writes_v(const Q8Proj& w, int M, int N, int K, int epilogue) {
-  return M > 0 && epilogue == kEpiStore && q8_choice(w, M, N, K, epilogue) == kQ8Split;
-}
-
 cudaError_t launch_q8_proj(const __half* a_codes, const Q8Proj& w, int M, int N, int K, const uint32_t* a_absmax,
                            const int32_t* row_seq, float* c, int epilogue, uint32_t* out_absmax, uint32_t* err,
                            cudaStream_t stream, const VPlanes& vp) {
-  switch (q8_choice(w, M, N, K, epilogue)) {
+  const Q8Kernel kern = q8_choice(w, M, N, K, epilogue);
+  const bool v = vp.hi && M > 0 && epilogue == kEpiStore && kern == kQ8Split;
+  if (vp.written) *vp.written = v;
+  switch (kern) {
     case kQ8Dp4a:
       return launch_gemm_q8_dp4a(a_codes, w.lanes, w.scales, M, N, K, a_absmax, row_seq, c, epilogue, out_absmax,
                                  stream);
     case kQ8Split:
       return launch_gemm_q8_split(a_codes, w.hi, w.lo, w.row_scale, M, N, K, a_absmax, row_seq, c, epilogue,
-                                  out_absmax, err, stream, epilogue == kEpiStore ? vp : VPlanes{});
+                                  out_absmax, err, stream, v ? vp : VPlanes{});
     default:
       return launch_gemm_q8(a_codes, w.codes, w.scales, M, N, K, a_absmax, row_seq, c, epilogue, out_absmax, err,
                             stream);

@@ -616,10 +616,10 @@ int run_forward(sem_model* m, const int32_t* d_ids, const MetaPtrs& mp, float* d
     const int hw = sliding ? fa.sliding_window / 2 : 0;
     // attention block (model_int8.go:191-210)
     // the long rows' V columns go straight to the attention's hi / lo planes
-    // when the split-plane kernel projects them
-    const bool v_planes = t_split > 0 && q8_proj_writes_v(w.qkv, (int)t_split, qkvN, H, kEpiStore);
+    // when the split-plane kernel projects them (v_planes: it did)
+    bool v_planes = false;
     SEM_LAUNCH(kStGemmQKV, q8(w.qkv, qkvN, H, slot(l, 0), big, qkvN, kEpiStore, nullptr,
-                              v_planes ? VPlanes{vh, T, nh * hd + hd} : VPlanes{}));
+                              VPlanes{vh, T, nh * hd + hd, &v_planes}));
     SEM_LAUNCH(kStQKNormRope, launch_qk_norm_rope(big, w.q_norm, w.k_norm, sliding ? swa_cos : m->rope_cos,
                                                   sliding ? swa_sin : m->rope_sin, c.norm_eps, nh, sm, qh, ql, kh, kl,
                                                   vh, vl, exact_short ? mp.T_long : T,

@@ -44,12 +44,13 @@ struct SeqMeta {
 
 // Where a QKV projection may put its V columns: [col0, col0 + 256) of each
 // row as the attention's fp16 hi and lo planes (hi[row][256], lo = hi + rows
-// * 256) instead of the float32 output. Only the split-plane kernel does so
-// (q8_proj_writes_v says whether a call will).
+// * 256) instead of the float32 output. Only the split-plane kernel does so;
+// launch_q8_proj sets *written to whether this call did.
 struct VPlanes {
   __half* hi = nullptr;
   int64_t rows = 0;
   int col0 = 0;
+  bool* written = nullptr;
 };
 
 cudaError_t launch_embed(const int32_t* ids, const int8_t* emb_codes, const float* emb_scales, int vocab,
@@ -163,7 +164,6 @@ constexpr int kDp4aMaxRows = 128;
 cudaError_t launch_q8_proj(const __half* a_codes, const Q8Proj& w, int M, int N, int K, const uint32_t* a_absmax,
                            const int32_t* row_seq, float* c, int epilogue, uint32_t* out_absmax, uint32_t* err,
                            cudaStream_t stream, const VPlanes& vp = VPlanes{});
-bool q8_proj_writes_v(const Q8Proj& w, int M, int N, int K, int epilogue);
 // Process-wide kernel choice: 0 auto, 1 per-block, 2 split-plane (launch_q8_proj
 // always; the forward's long-sequence rows), 3 split-plane for every forward
 // row, 4 the CUDA-core VNNI-order kernel for every row; returns the previous
