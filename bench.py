@@ -866,8 +866,10 @@ def run_ours(args) -> None:
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
             "config": workload_config(world), "clocks": clk,
-            "e2e": {"value": BATCH * world / e2e_s, "unit": UNIT, "h2d_bytes_per_step": int(T * 4 + (BATCH + 1) * 4),
-                    "d2h_bytes_per_step": int(BATCH * 768 * 4)},
+            "e2e": {"value": BATCH * world / e2e_s, "unit": UNIT, "h2d_bytes_per_step": int(T * 4),
+                    "d2h_bytes_per_step": int(BATCH * 768 * 4),
+                    "api": "sem_embed (host token ids in, embeddings out; the batch shape repeats, so only the ids "
+                           "are uploaded)"},
             "gpu_launches": int(launches_per_step * args.steps),
             "roofline": roof,
         }
