@@ -180,6 +180,26 @@ def test_batch_invariance_many_sequences(gpu_model, path):
         lib.sem_q8_path(prev)
 
 
+def test_pair_and_single_cta_attention_identical(gpu_model):
+    # The tensor-core attention runs on SM pairs (256-row query tiles) unless
+    # half-empty pair tiles would waste over a quarter of the CTAs; both
+    # kernels sum every element in the same order. With the split projection
+    # for every row, a 300-token sequence alone takes 128-row tiles (2 pair
+    # tiles for 3 single ones) and beside four 512-token ones takes pairs:
+    # the two embeddings are bit-identical.
+    import _lib
+    lib = _lib.load()
+    prev = lib.sem_q8_path(3)
+    try:
+        lengths = [300, 512, 512, 512, 512]
+        ids, offs = synth.token_batch(911, lengths, TEST_VOCAB)
+        batch = gpu_model.forward_batch(ids, offs, 768)
+        alone = gpu_model.forward_batch(ids[:300], np.array([0, 300]), 768)[0]
+        np.testing.assert_array_equal(batch[0], alone)
+    finally:
+        lib.sem_q8_path(prev)
+
+
 @pytest.mark.parametrize("path", [1, 3])
 def test_batch_invariance_max_length(gpu_model, path):
     # a sequence of the model's maximum length (2048: 16 attention key tiles,
