@@ -261,10 +261,12 @@ def stage_roofline(stage: str, total_ms: float, launches: int, T: int, seq_lens,
     # attention norm and per layer on the attention output (K = H) and on the
     # MLP product (K = F), fp32 in and fp16 codes out; the residual kernel
     # reads o and hidden, writes hidden, and in all but the last of its 2 L
-    # launches also writes the next norm's fp16 codes
+    # launches also writes the next norm's fp16 codes; the Q/K norm kernel
+    # reads the float32 q and k heads and writes their fp16 hi / lo planes
+    # (the QKV projection writes V's planes itself on the bench's workload)
     bytes_per_row = {"quantize": 6.0 * ((L + 1) * H + L * F) / (2 * L + 1),
                      "residual_norm": 3 * 4 * H + 2.0 * H * (2 * L - 1) / (2 * L), "row_stats": 4 * H,
-                     "qk_norm_rope": 4 * (NH * HD + 2 * HD) + 2 * 2 * (NH * HD + 2 * HD), "embed": 4 * H + H,
+                     "qk_norm_rope": 4 * (NH * HD + HD) + 2 * 2 * (NH * HD + HD), "embed": 4 * H + H,
                      "pool_l2": 4 * H}.get(stage, 4 * H)
     b = bytes_per_row * T
     achieved = b / (per_ms * 1e-3) / 1e9
