@@ -36,12 +36,29 @@ __device__ __forceinline__ float fast_exp_ref(float x) {
   return x < -10.0f ? 0.0f : r;
 }
 
+// fast_exp_ref for x <= 0: from -10 up the exponent int32(x * log2e) lies in
+// [-14, 0], so of the four clamps only x < -10 can act and the result is
+// fast_exp_ref's bit for bit (for a NaN argument it is NaN where fast_exp_ref
+// gives its overflow value; the one caller's result is NaN either way).
+__device__ __forceinline__ float fast_exp_nonpos(float x) {
+  const float y = __fmul_rn(x, 1.442695041f);
+  const float yt = truncf(y);
+  const int ip = __float_as_int(__fadd_rn(yt, 12582912.0f)) - 0x4B400000;
+  const float f = __fsub_rn(y, yt);
+  const float c1 = 0.693147180559945f, c2 = 0.240226506959101f, c3 = 0.055504108664821f,
+              c4 = 0.009676036358193f;
+  const float poly = __fadd_rn(
+      1.0f, __fmul_rn(f, __fadd_rn(c1, __fmul_rn(f, __fadd_rn(c2, __fmul_rn(f, __fadd_rn(c3, __fmul_rn(f, c4))))))));
+  const float r = __fmul_rn(poly, __uint_as_float((uint32_t)(ip + 127) << 23));
+  return x < -10.0f ? 0.0f : r;
+}
+
 // GELUQuickSIMD element (activation.go:47-95): x * sigmoid(1.702 x) through
 // fastExp. Both of the reference's branches evaluate fastExp(-|1.702 x|) and
 // divide by 1 + e; only the numerator differs (1, or e for negative x).
 __device__ __forceinline__ float gelu_quick_ref(float x) {
   const float sx = __fmul_rn(1.702f, x);
-  const float e = fast_exp_ref(-fabsf(sx));
+  const float e = fast_exp_nonpos(-fabsf(sx));
   const float sig = __fdiv_rn(sx >= 0.0f ? 1.0f : e, __fadd_rn(1.0f, e));
   return __fmul_rn(x, sig);
 }

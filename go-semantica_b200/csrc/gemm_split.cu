@@ -244,6 +244,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kXThreads, 1)
           if (lane == 0) mbar_arrive_cluster(lead_tempty + 8 * b);
         }
         if (!live) continue;
+        float crs[2][16];  // the tokens' input scales, four 16-byte loads per 16 tokens
+#pragma unroll
+        for (int cc = 0; cc < 2; ++cc)
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+            reinterpret_cast<float4*>(crs[cc])[i] = reinterpret_cast<const float4*>(c_rs + (c + cc) * 16)[i];
         if (!vtile) {
 #pragma unroll
           for (int cc = 0; cc < 2; ++cc)
@@ -251,7 +257,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kXThreads, 1)
             for (int i = 0; i < 16; ++i) {
               const int x = (c + cc) * 16 + i;
               if (tok0 + x < T)  // warp-uniform
-                dst[(size_t)x * n_out] = __fmul_rn(__fmul_rn(__uint_as_float(r[cc][i]), rsc), c_rs[x]);
+                dst[(size_t)x * n_out] = __fmul_rn(__fmul_rn(__uint_as_float(r[cc][i]), rsc), crs[cc][i]);
             }
         } else {
 #pragma unroll
@@ -260,7 +266,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kXThreads, 1)
             for (int i = 0; i < 16; ++i) {
               const int x = (c + cc) * 16 + i;
               if (tok0 + x < T) {  // warp-uniform
-                const float v = __fmul_rn(__fmul_rn(__uint_as_float(r[cc][i]), rsc), c_rs[x]);
+                const float v = __fmul_rn(__fmul_rn(__uint_as_float(r[cc][i]), rsc), crs[cc][i]);
                 __half hi, lo;
                 split_half(v, hi, lo);
                 vhp[(size_t)x * 256] = hi;
@@ -451,11 +457,15 @@ __global__ void __launch_bounds__(kGuThreads, 1)
           __syncwarp();
           if (lane == 0) mbar_arrive(&tempty[b]);
         }
-        float hv[16];
+        float hv[16], sg[16], su[16];  // the channels' row scales, four 16-byte loads each
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          reinterpret_cast<float4*>(sg)[i] = reinterpret_cast<const float4*>(rg + c * 16)[i];
+          reinterpret_cast<float4*>(su)[i] = reinterpret_cast<const float4*>(ru + c * 16)[i];
+        }
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
-          hv[i] = gelu_up_f(__fmul_rn(__uint_as_float(g[i]), rg[c * 16 + i]),
-                            __fmul_rn(__uint_as_float(u[i]), ru[c * 16 + i]), rs);
+          hv[i] = gelu_up_f(__fmul_rn(__uint_as_float(g[i]), sg[i]), __fmul_rn(__uint_as_float(u[i]), su[i]), rs);
           run = fmaxf(run, fabsf(hv[i]));
         }
         if (valid) {
