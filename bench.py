@@ -81,7 +81,7 @@ def workload_config(n_gpus: int) -> dict:
         "seq_len": SEQ_LEN,
         "parallelism": f"dp{n_gpus}",
         "l2": "inputs larger than L2: every layer's activations (1.6 GB per fp32 hidden-size tensor) stream through "
-              "HBM, about 550 GB of element-wise traffic and 0.4 GB of weight planes per step",
+              "HBM, about 520 GB of element-wise traffic and 0.4 GB of weight planes per step",
     }
 
 
