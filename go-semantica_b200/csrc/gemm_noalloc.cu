@@ -53,29 +53,31 @@ int scratch_for_device(int device, uint8_t** out) {
 }  // namespace
 
 extern "C" int sem_q8_gemm_noalloc(sem_q8_weight* w, const float* d_a, int32_t m, float* d_c, void* stream) {
-  if (!w || !d_a || !d_c) return sem::set_error(SEM_EINVAL, "null argument");
-  if (m < 0) return sem::set_error(SEM_EINVAL, "sem_q8_gemm_noalloc: negative row count %d", m);
-  if (m == 0) return SEM_OK;  // an empty batch, as sem_q8_gemm treats it
-  const size_t need = (size_t)m * (size_t)w->k_in;
-  if (need > kNoAllocMaxCodes)
-    return sem::set_error(SEM_EINVAL,
-                          "sem_q8_gemm_noalloc: %d rows x %d inputs need %zu activation codes of scratch, above the "
-                          "static maximum of %zu (at most %zu rows for this weight)",
-                          m, w->k_in, need, kNoAllocMaxCodes, kNoAllocMaxCodes / (size_t)w->k_in);
-  sem::DeviceGuard dg(w->ctx->device);
-  uint8_t* scratch = nullptr;
-  int rc = scratch_for_device(w->ctx->device, &scratch);
-  if (rc) return rc;
-  uint32_t* absmax = reinterpret_cast<uint32_t*>(scratch);
-  __half* codes = reinterpret_cast<__half*>(scratch + kNoAllocHeaderBytes);
-  cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : w->ctx->stream;
-  // The array keeps the previous call's contents: the absmax word must start at zero.
-  SEM_CUDA(cudaMemsetAsync(absmax, 0, sizeof(uint32_t), st));
-  SEM_CUDA(sem::launch_absmax(d_a, (int64_t)need, absmax, st));
-  sem::SeqMeta meta{nullptr, nullptr, nullptr, m, 1};
-  SEM_CUDA(sem::launch_quantize(d_a, nullptr, nullptr, w->k_in, meta, absmax, codes, st));
-  // the kernel sem_q8_gemm would take for this m (sem_q8_path)
-  SEM_CUDA(sem::launch_q8_proj(codes, w->proj(), m, w->n_out, w->k_in, absmax, nullptr, d_c, sem::kEpiStore, nullptr,
-                               nullptr, st));
-  return SEM_OK;
+  return sem::guarded([&]() -> int {
+    if (!w || !d_a || !d_c) return sem::set_error(SEM_EINVAL, "null argument");
+    if (m < 0) return sem::set_error(SEM_EINVAL, "sem_q8_gemm_noalloc: negative row count %d", m);
+    if (m == 0) return SEM_OK;  // an empty batch, as sem_q8_gemm treats it
+    const size_t need = (size_t)m * (size_t)w->k_in;
+    if (need > kNoAllocMaxCodes)
+      return sem::set_error(SEM_EINVAL,
+                            "sem_q8_gemm_noalloc: %d rows x %d inputs need %zu activation codes of scratch, above the "
+                            "static maximum of %zu (at most %zu rows for this weight)",
+                            m, w->k_in, need, kNoAllocMaxCodes, kNoAllocMaxCodes / (size_t)w->k_in);
+    sem::DeviceGuard dg(w->ctx->device);
+    uint8_t* scratch = nullptr;
+    int rc = scratch_for_device(w->ctx->device, &scratch);
+    if (rc) return rc;
+    uint32_t* absmax = reinterpret_cast<uint32_t*>(scratch);
+    __half* codes = reinterpret_cast<__half*>(scratch + kNoAllocHeaderBytes);
+    cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : w->ctx->stream;
+    // The array keeps the previous call's contents: the absmax word must start at zero.
+    SEM_CUDA(cudaMemsetAsync(absmax, 0, sizeof(uint32_t), st));
+    SEM_CUDA(sem::launch_absmax(d_a, (int64_t)need, absmax, st));
+    sem::SeqMeta meta{nullptr, nullptr, nullptr, m, 1};
+    SEM_CUDA(sem::launch_quantize(d_a, nullptr, nullptr, w->k_in, meta, absmax, codes, st));
+    // the kernel sem_q8_gemm would take for this m (sem_q8_path)
+    SEM_CUDA(sem::launch_q8_proj(codes, w->proj(), m, w->n_out, w->k_in, absmax, nullptr, d_c, sem::kEpiStore, nullptr,
+                                 nullptr, st));
+    return SEM_OK;
+  });
 }

@@ -313,90 +313,116 @@ extern "C" {
 
 int sem_index_build(sem_context* ctx, int32_t dim, int32_t quant, const float* vectors, const int32_t* ids, int64_t count,
                     sem_index** out) {
-  return sem::index_build(ctx, dim, quant, vectors, ids, count, out);
+  return sem::guarded([&]() -> int {
+    return sem::index_build(ctx, dim, quant, vectors, ids, count, out);
+  });
 }
 
 int sem_index_create(sem_context* ctx, int32_t dim, int32_t quant, const void* data, const int32_t* ids, int64_t count,
                      sem_index** out) {
-  return sem::index_create(ctx, dim, quant, data, ids, count, out);
+  return sem::guarded([&]() -> int {
+    return sem::index_create(ctx, dim, quant, data, ids, count, out);
+  });
 }
 
 int sem_index_free(sem_index* x) {
-  if (!x) return SEM_OK;
-  sem::DeviceGuard dg(x->ctx->device);
-  cudaStreamSynchronize(x->ctx->stream);
-  delete x;
-  return SEM_OK;
+  return sem::guarded([&]() -> int {
+    if (!x) return SEM_OK;
+    sem::DeviceGuard dg(x->ctx->device);
+    cudaStreamSynchronize(x->ctx->stream);
+    delete x;
+    return SEM_OK;
+  });
 }
 
 int sem_index_count(const sem_index* x, int64_t* out) {
-  if (!x || !out) return sem::set_error(SEM_EINVAL, "null argument");
-  *out = x->count;
-  return SEM_OK;
+  return sem::guarded([&]() -> int {
+    if (!x || !out) return sem::set_error(SEM_EINVAL, "null argument");
+    *out = x->count;
+    return SEM_OK;
+  });
 }
 
 int sem_index_dimension(const sem_index* x, int32_t* out) {
-  if (!x || !out) return sem::set_error(SEM_EINVAL, "null argument");
-  *out = x->dim;
-  return SEM_OK;
+  return sem::guarded([&]() -> int {
+    if (!x || !out) return sem::set_error(SEM_EINVAL, "null argument");
+    *out = x->dim;
+    return SEM_OK;
+  });
 }
 
 int sem_index_quantization(const sem_index* x, int32_t* out) {
-  if (!x || !out) return sem::set_error(SEM_EINVAL, "null argument");
-  *out = x->quant;
-  return SEM_OK;
+  return sem::guarded([&]() -> int {
+    if (!x || !out) return sem::set_error(SEM_EINVAL, "null argument");
+    *out = x->quant;
+    return SEM_OK;
+  });
 }
 
 int sem_index_search(sem_index* x, const float* queries, int32_t nq, int32_t dim, int32_t k, int32_t mode,
                      int32_t normalize, int32_t* out_ids, float* out_dist, int32_t* out_scores) {
-  return sem::index_search(x, queries, nq, dim, k, mode, normalize, out_ids, out_dist, out_scores);
+  return sem::guarded([&]() -> int {
+    return sem::index_search(x, queries, nq, dim, k, mode, normalize, out_ids, out_dist, out_scores);
+  });
 }
 
 int sem_index_search_keys(sem_index* x, const void* d_queries, int32_t nq, int32_t k, int32_t mode, int64_t row_base,
                           uint64_t* d_keys, void* stream) {
-  if (!x || !d_queries || !d_keys) return sem::set_error(SEM_EINVAL, "null argument");
-  if (k <= 0 || k > 64) return sem::set_error(SEM_EINVAL, "brute: topK must be in 1..64 on the device path");
-  sem::DeviceGuard dg(x->ctx->device);
-  std::lock_guard<std::mutex> lk(x->ctx->mu);
-  cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : x->ctx->stream;
-  return sem::search_keys(x, d_queries, nq, k, mode, row_base, d_keys, st);
+  return sem::guarded([&]() -> int {
+    if (!x || !d_queries || !d_keys) return sem::set_error(SEM_EINVAL, "null argument");
+    if (k <= 0 || k > 64) return sem::set_error(SEM_EINVAL, "brute: topK must be in 1..64 on the device path");
+    sem::DeviceGuard dg(x->ctx->device);
+    std::lock_guard<std::mutex> lk(x->ctx->mu);
+    cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : x->ctx->stream;
+    return sem::search_keys(x, d_queries, nq, k, mode, row_base, d_keys, st);
+  });
 }
 
 int sem_topk_merge(sem_context* ctx, const uint64_t* d_keys, int32_t lists, int32_t nq, int32_t k, int32_t k_out,
                    int32_t mode, int32_t quant, int32_t* d_rows, int32_t* d_scores, float* d_dist, void* stream) {
-  if (!ctx || !d_keys) return sem::set_error(SEM_EINVAL, "null argument");
-  if (k_out <= 0 || k_out > k || k_out > 64) return sem::set_error(SEM_EINVAL, "invalid k_out %d", k_out);
-  sem::DeviceGuard dg(ctx->device);
-  cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : ctx->stream;
-  // d_keys: lists x nq x k (one list per shard, as an all-gather lays them out)
-  cudaError_t e = sem::launch_topk_merge(d_keys, lists, (int64_t)nq * k, k, nq, k, k_out, mode != SEM_SEARCH_EXACT,
-                                         quant == 2 ? 2 : 1, d_rows, d_scores, d_dist, nullptr, st);
-  if (e != cudaSuccess) return sem::set_error(SEM_EDEVICE, "merge: %s", cudaGetErrorString(e));
-  return SEM_OK;
+  return sem::guarded([&]() -> int {
+    if (!ctx || !d_keys) return sem::set_error(SEM_EINVAL, "null argument");
+    if (k_out <= 0 || k_out > k || k_out > 64) return sem::set_error(SEM_EINVAL, "invalid k_out %d", k_out);
+    sem::DeviceGuard dg(ctx->device);
+    cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : ctx->stream;
+    // d_keys: lists x nq x k (one list per shard, as an all-gather lays them out)
+    cudaError_t e = sem::launch_topk_merge(d_keys, lists, (int64_t)nq * k, k, nq, k, k_out, mode != SEM_SEARCH_EXACT,
+                                           quant == 2 ? 2 : 1, d_rows, d_scores, d_dist, nullptr, st);
+    if (e != cudaSuccess) return sem::set_error(SEM_EDEVICE, "merge: %s", cudaGetErrorString(e));
+    return SEM_OK;
+  });
 }
 
 int sem_quantize_queries(const float* queries, int32_t nq, int32_t dim, int32_t quant, void* out_codes) {
-  if (!queries || !out_codes) return sem::set_error(SEM_EINVAL, "null argument");
-  if (quant != 1 && quant != 2) return sem::set_error(SEM_EINVAL, "quant must be 1 or 2");
-  // quantizeInt8 / quantizeInt16 (quant.go:17-41) of already-normalised values
-  for (int64_t i = 0; i < (int64_t)nq * dim; ++i) {
-    float v = queries[i];
-    if (v > 1.0f) v = 1.0f;
-    else if (v < -1.0f) v = -1.0f;
-    if (quant == 1) static_cast<int8_t*>(out_codes)[i] = (int8_t)(int32_t)std::round((double)v * 127.0);
-    else static_cast<int16_t*>(out_codes)[i] = (int16_t)(int32_t)std::round((double)v * 32767.0);
-  }
-  return SEM_OK;
+  return sem::guarded([&]() -> int {
+    if (!queries || !out_codes) return sem::set_error(SEM_EINVAL, "null argument");
+    if (quant != 1 && quant != 2) return sem::set_error(SEM_EINVAL, "quant must be 1 or 2");
+    // quantizeInt8 / quantizeInt16 (quant.go:17-41) of already-normalised values
+    for (int64_t i = 0; i < (int64_t)nq * dim; ++i) {
+      float v = queries[i];
+      if (v > 1.0f) v = 1.0f;
+      else if (v < -1.0f) v = -1.0f;
+      if (quant == 1) static_cast<int8_t*>(out_codes)[i] = (int8_t)(int32_t)std::round((double)v * 127.0);
+      else static_cast<int16_t*>(out_codes)[i] = (int16_t)(int32_t)std::round((double)v * 32767.0);
+    }
+    return SEM_OK;
+  });
 }
 
-int sem_index_vector(sem_index* x, int32_t id, float* out) { return sem::index_vector(x, id, out); }
+int sem_index_vector(sem_index* x, int32_t id, float* out) {
+  return sem::guarded([&]() -> int { return sem::index_vector(x, id, out); });
+}
 
 int sem_index_serialize(sem_index* x, void* buf, size_t cap, size_t* written) {
-  return sem::index_serialize(x, buf, cap, written);
+  return sem::guarded([&]() -> int {
+    return sem::index_serialize(x, buf, cap, written);
+  });
 }
 
 int sem_index_deserialize(sem_context* ctx, const void* bytes, size_t n, sem_index** out) {
-  return sem::index_deserialize(ctx, bytes, n, out);
+  return sem::guarded([&]() -> int {
+    return sem::index_deserialize(ctx, bytes, n, out);
+  });
 }
 
 }  // extern "C"

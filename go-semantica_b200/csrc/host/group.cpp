@@ -99,110 +99,124 @@ extern "C" {
 
 int sem_group_load(const int32_t* devices, int32_t n_devices, const sem_model_config* cfg,
                    const sem_tensor_view* tensors, int32_t n_tensors, sem_group** out) {
-  return sem::load_group(devices, n_devices, cfg, tensors, n_tensors, out);
+  return sem::guarded([&]() -> int {
+    return sem::load_group(devices, n_devices, cfg, tensors, n_tensors, out);
+  });
 }
 
 int sem_group_load_gguf(const int32_t* devices, int32_t n_devices, const char* path, sem_group** out) {
-  if (int rc = sem::check_devices(devices, n_devices)) return rc;
-  if (!path) return sem::set_error(SEM_EINVAL, "null argument");
-  sem::GgufFile f;
-  int rc = f.open(path);
-  if (rc) return rc;
-  sem_model_config cfg;
-  if ((rc = sem::gguf_config(f, &cfg))) return rc;
-  std::vector<sem_tensor_view> views;
-  views.reserve(f.tensors.size());
-  for (const auto& t : f.tensors) {
-    sem_tensor_view v{};
-    v.name = t.name.c_str();
-    v.dtype = t.dtype;
-    v.n_dims = (uint32_t)t.dims.size();
-    for (size_t k = 0; k < t.dims.size() && k < 4; ++k) v.dims[k] = t.dims[k];
-    v.data = f.tensor_data(t);
-    v.nbytes = t.size;
-    views.push_back(v);
-  }
-  return sem::load_group(devices, n_devices, &cfg, views.data(), (int32_t)views.size(), out);
+  return sem::guarded([&]() -> int {
+    if (int rc = sem::check_devices(devices, n_devices)) return rc;
+    if (!path) return sem::set_error(SEM_EINVAL, "null argument");
+    sem::GgufFile f;
+    int rc = f.open(path);
+    if (rc) return rc;
+    sem_model_config cfg;
+    if ((rc = sem::gguf_config(f, &cfg))) return rc;
+    std::vector<sem_tensor_view> views;
+    views.reserve(f.tensors.size());
+    for (const auto& t : f.tensors) {
+      sem_tensor_view v{};
+      v.name = t.name.c_str();
+      v.dtype = t.dtype;
+      v.n_dims = (uint32_t)t.dims.size();
+      for (size_t k = 0; k < t.dims.size() && k < 4; ++k) v.dims[k] = t.dims[k];
+      v.data = f.tensor_data(t);
+      v.nbytes = t.size;
+      views.push_back(v);
+    }
+    return sem::load_group(devices, n_devices, &cfg, views.data(), (int32_t)views.size(), out);
+  });
 }
 
 int sem_group_size(const sem_group* g, int32_t* out) {
-  if (!g || !out) return sem::set_error(SEM_EINVAL, "null argument");
-  *out = (int32_t)g->models.size();
-  return SEM_OK;
+  return sem::guarded([&]() -> int {
+    if (!g || !out) return sem::set_error(SEM_EINVAL, "null argument");
+    *out = (int32_t)g->models.size();
+    return SEM_OK;
+  });
 }
 
 int sem_group_config_get(const sem_group* g, sem_model_config* out) {
-  if (!g || !out) return sem::set_error(SEM_EINVAL, "null argument");
-  *out = g->cfg;
-  return SEM_OK;
+  return sem::guarded([&]() -> int {
+    if (!g || !out) return sem::set_error(SEM_EINVAL, "null argument");
+    *out = g->cfg;
+    return SEM_OK;
+  });
 }
 
 int sem_group_set_faithful(sem_group* g, const sem_faithful_config* cfg) {
-  if (!g) return sem::set_error(SEM_EINVAL, "null argument");
-  std::lock_guard<std::mutex> lk(g->mu);
-  for (sem_model* m : g->models) {
-    const int rc = sem_model_set_faithful(m, cfg);
-    if (rc) return rc;
-  }
-  return SEM_OK;
+  return sem::guarded([&]() -> int {
+    if (!g) return sem::set_error(SEM_EINVAL, "null argument");
+    std::lock_guard<std::mutex> lk(g->mu);
+    for (sem_model* m : g->models) {
+      const int rc = sem_model_set_faithful(m, cfg);
+      if (rc) return rc;
+    }
+    return SEM_OK;
+  });
 }
 
 int sem_group_embed(sem_group* g, const int32_t* ids, const int32_t* offsets, int32_t B, const int32_t* dims_in,
                     float* out) {
-  if (!g) return sem::set_error(SEM_EINVAL, "null argument");
-  // the request is checked before any device starts
-  std::vector<int32_t> dims;
-  int64_t out_floats = 0;
-  if (int rc = sem::validate_embed_request(g->cfg, ids, offsets, B, dims_in, out, &dims, &out_floats)) return rc;
-  if (B == 0) return SEM_OK;
-  std::vector<int64_t> out_off(B + 1, 0);
-  for (int s = 0; s < B; ++s) out_off[s + 1] = out_off[s] + dims[s];
-  std::lock_guard<std::mutex> lk(g->mu);
-  const int n = (int)g->models.size();
-  const auto parts = sem::split_by_tokens(offsets, B, n);
-  struct Share {
-    std::vector<int32_t> ids, offsets, dims;
-    std::vector<float> out;
-    int rc = SEM_OK;
-    std::string msg;
-  };
-  std::vector<Share> sh(n);
-  std::vector<std::thread> th;
-  for (int d = 0; d < n; ++d) {
-    if (parts[d].empty()) continue;
-    Share& x = sh[d];
-    x.offsets.push_back(0);
-    int64_t floats = 0;
-    for (int s : parts[d]) {
-      x.ids.insert(x.ids.end(), ids + offsets[s], ids + offsets[s + 1]);
-      x.offsets.push_back((int32_t)x.ids.size());
-      x.dims.push_back(dims[s]);
-      floats += dims[s];
+  return sem::guarded([&]() -> int {
+    if (!g) return sem::set_error(SEM_EINVAL, "null argument");
+    // the request is checked before any device starts
+    std::vector<int32_t> dims;
+    int64_t out_floats = 0;
+    if (int rc = sem::validate_embed_request(g->cfg, ids, offsets, B, dims_in, out, &dims, &out_floats)) return rc;
+    if (B == 0) return SEM_OK;
+    std::vector<int64_t> out_off(B + 1, 0);
+    for (int s = 0; s < B; ++s) out_off[s + 1] = out_off[s] + dims[s];
+    std::lock_guard<std::mutex> lk(g->mu);
+    const int n = (int)g->models.size();
+    const auto parts = sem::split_by_tokens(offsets, B, n);
+    struct Share {
+      std::vector<int32_t> ids, offsets, dims;
+      std::vector<float> out;
+      int rc = SEM_OK;
+      std::string msg;
+    };
+    std::vector<Share> sh(n);
+    std::vector<std::thread> th;
+    for (int d = 0; d < n; ++d) {
+      if (parts[d].empty()) continue;
+      Share& x = sh[d];
+      x.offsets.push_back(0);
+      int64_t floats = 0;
+      for (int s : parts[d]) {
+        x.ids.insert(x.ids.end(), ids + offsets[s], ids + offsets[s + 1]);
+        x.offsets.push_back((int32_t)x.ids.size());
+        x.dims.push_back(dims[s]);
+        floats += dims[s];
+      }
+      x.out.resize((size_t)floats);
+      th.emplace_back([&g, &x, d] {
+        x.rc = sem_embed(g->models[d], x.ids.data(), x.offsets.data(), (int32_t)x.dims.size(), x.dims.data(),
+                         x.out.data());
+        if (x.rc) x.msg = sem_last_error();
+      });
     }
-    x.out.resize((size_t)floats);
-    th.emplace_back([&g, &x, d] {
-      x.rc = sem_embed(g->models[d], x.ids.data(), x.offsets.data(), (int32_t)x.dims.size(), x.dims.data(),
-                       x.out.data());
-      if (x.rc) x.msg = sem_last_error();
-    });
-  }
-  for (auto& t : th) t.join();
-  for (int d = 0; d < n; ++d)
-    if (sh[d].rc) return sem::set_error(sh[d].rc, "device %d: %s", g->ctxs[d]->device, sh[d].msg.c_str());
-  for (int d = 0; d < n; ++d) {
-    int64_t o = 0;
-    for (size_t k = 0; k < parts[d].size(); ++k) {
-      const int s = parts[d][k];
-      std::copy(sh[d].out.begin() + o, sh[d].out.begin() + o + dims[s], out + out_off[s]);
-      o += dims[s];
+    for (auto& t : th) t.join();
+    for (int d = 0; d < n; ++d)
+      if (sh[d].rc) return sem::set_error(sh[d].rc, "device %d: %s", g->ctxs[d]->device, sh[d].msg.c_str());
+    for (int d = 0; d < n; ++d) {
+      int64_t o = 0;
+      for (size_t k = 0; k < parts[d].size(); ++k) {
+        const int s = parts[d][k];
+        std::copy(sh[d].out.begin() + o, sh[d].out.begin() + o + dims[s], out + out_off[s]);
+        o += dims[s];
+      }
     }
-  }
-  return SEM_OK;
+    return SEM_OK;
+  });
 }
 
 int sem_group_free(sem_group* g) {
-  sem::free_group(g);
-  return SEM_OK;
+  return sem::guarded([&]() -> int {
+    sem::free_group(g);
+    return SEM_OK;
+  });
 }
 
 }  // extern "C"

@@ -7,7 +7,9 @@
 #include <cstdarg>
 #include <cstdint>
 #include <cstdio>
+#include <exception>
 #include <mutex>
+#include <new>
 #include <string>
 #include <vector>
 
@@ -19,6 +21,23 @@ namespace sem {
 // ---- thread-local error message ----
 int set_error(int code, const char* fmt, ...);
 const char* last_error();
+
+// Runs the body of a C entry point so that no C++ exception crosses the C
+// ABI (unwinding into a cgo or C caller ends its process): a failed host
+// allocation returns SEM_ENOMEM, any other exception SEM_EINTERNAL, each with
+// its message in sem_last_error.
+template <class F>
+int guarded(F&& body) noexcept {
+  try {
+    return body();
+  } catch (const std::bad_alloc&) {
+    return set_error(SEM_ENOMEM, "host allocation failed");
+  } catch (const std::exception& e) {
+    return set_error(SEM_EINTERNAL, "%s", e.what());
+  } catch (...) {
+    return set_error(SEM_EINTERNAL, "unknown exception");
+  }
+}
 
 // sem_embed's host checks in the reference's order (model_int8.go:149-178):
 // fills dims (NULL dims_in = embed_dim) and the total output floats.

@@ -1092,145 +1092,186 @@ extern "C" {
 const char* sem_last_error(void) { return sem::last_error(); }
 
 int sem_device_count(int* out) {
-  if (!out) return sem::set_error(SEM_EINVAL, "null argument");
-  int n = 0;
-  cudaError_t e = cudaGetDeviceCount(&n);
-  if (e != cudaSuccess) {
-    *out = 0;
-    return sem::set_error(SEM_EDEVICE, "cudaGetDeviceCount: %s", cudaGetErrorString(e));
-  }
-  *out = n;
-  return SEM_OK;
+  return sem::guarded([&]() -> int {
+    if (!out) return sem::set_error(SEM_EINVAL, "null argument");
+    int n = 0;
+    cudaError_t e = cudaGetDeviceCount(&n);
+    if (e != cudaSuccess) {
+      *out = 0;
+      return sem::set_error(SEM_EDEVICE, "cudaGetDeviceCount: %s", cudaGetErrorString(e));
+    }
+    *out = n;
+    return SEM_OK;
+  });
 }
 
 int sem_context_create(int device, sem_context** out) {
-  if (!out) return sem::set_error(SEM_EINVAL, "null argument");
-  int n = 0;
-  cudaError_t e = cudaGetDeviceCount(&n);
-  if (e != cudaSuccess || device < 0 || device >= n)
-    return sem::set_error(SEM_EDEVICE, "no CUDA device %d (%s)", device, e == cudaSuccess ? "out of range" : cudaGetErrorString(e));
-  sem::DeviceGuard dg(device);
-  std::unique_ptr<sem_context> c(new sem_context());
-  c->device = device;
-  e = cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking);
-  if (e != cudaSuccess) return sem::set_error(SEM_EDEVICE, "cudaStreamCreate: %s", cudaGetErrorString(e));
-  *out = c.release();
-  return SEM_OK;
+  return sem::guarded([&]() -> int {
+    if (!out) return sem::set_error(SEM_EINVAL, "null argument");
+    int n = 0;
+    cudaError_t e = cudaGetDeviceCount(&n);
+    if (e != cudaSuccess || device < 0 || device >= n)
+      return sem::set_error(SEM_EDEVICE, "no CUDA device %d (%s)", device,
+                            e == cudaSuccess ? "out of range" : cudaGetErrorString(e));
+    sem::DeviceGuard dg(device);
+    std::unique_ptr<sem_context> c(new sem_context());
+    c->device = device;
+    e = cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking);
+    if (e != cudaSuccess) return sem::set_error(SEM_EDEVICE, "cudaStreamCreate: %s", cudaGetErrorString(e));
+    *out = c.release();
+    return SEM_OK;
+  });
 }
 
 int sem_context_destroy(sem_context* ctx) {
-  if (!ctx) return SEM_OK;
-  {
-    sem::DeviceGuard dg(ctx->device);
-    cudaStreamSynchronize(ctx->stream);
-    ctx->scratch.release();
-    cudaStreamDestroy(ctx->stream);
-  }
-  delete ctx;
-  return SEM_OK;
+  return sem::guarded([&]() -> int {
+    if (!ctx) return SEM_OK;
+    {
+      sem::DeviceGuard dg(ctx->device);
+      cudaStreamSynchronize(ctx->stream);
+      ctx->scratch.release();
+      cudaStreamDestroy(ctx->stream);
+    }
+    delete ctx;
+    return SEM_OK;
+  });
 }
 
 void* sem_context_stream(sem_context* ctx) { return ctx ? static_cast<void*>(ctx->stream) : nullptr; }
 
 int sem_model_load(sem_context* ctx, const sem_model_config* cfg, const sem_tensor_view* tensors, int32_t n,
                    sem_model** out) {
-  return sem::model_load(ctx, cfg, tensors, n, out);
+  return sem::guarded([&]() -> int {
+    return sem::model_load(ctx, cfg, tensors, n, out);
+  });
 }
 
 int sem_model_load_gguf(sem_context* ctx, const char* path, sem_model** out) {
-  if (!ctx || !path || !out) return sem::set_error(SEM_EINVAL, "null argument");
-  sem::GgufFile f;
-  int rc = f.open(path);
-  if (rc) return rc;
-  sem_model_config cfg;
-  if ((rc = sem::gguf_config(f, &cfg))) return rc;
-  std::vector<sem_tensor_view> views;
-  views.reserve(f.tensors.size());
-  for (const auto& t : f.tensors) {
-    sem_tensor_view v{};
-    v.name = t.name.c_str();
-    v.dtype = t.dtype;
-    v.n_dims = (uint32_t)t.dims.size();
-    for (size_t k = 0; k < t.dims.size() && k < 4; ++k) v.dims[k] = t.dims[k];
-    v.data = f.tensor_data(t);
-    v.nbytes = t.size;
-    views.push_back(v);
-  }
-  return sem::model_load(ctx, &cfg, views.data(), (int32_t)views.size(), out);
+  return sem::guarded([&]() -> int {
+    if (!ctx || !path || !out) return sem::set_error(SEM_EINVAL, "null argument");
+    sem::GgufFile f;
+    int rc = f.open(path);
+    if (rc) return rc;
+    sem_model_config cfg;
+    if ((rc = sem::gguf_config(f, &cfg))) return rc;
+    std::vector<sem_tensor_view> views;
+    views.reserve(f.tensors.size());
+    for (const auto& t : f.tensors) {
+      sem_tensor_view v{};
+      v.name = t.name.c_str();
+      v.dtype = t.dtype;
+      v.n_dims = (uint32_t)t.dims.size();
+      for (size_t k = 0; k < t.dims.size() && k < 4; ++k) v.dims[k] = t.dims[k];
+      v.data = f.tensor_data(t);
+      v.nbytes = t.size;
+      views.push_back(v);
+    }
+    return sem::model_load(ctx, &cfg, views.data(), (int32_t)views.size(), out);
+  });
 }
 
 int sem_model_config_get(const sem_model* m, sem_model_config* out) {
-  if (!m || !out) return sem::set_error(SEM_EINVAL, "null argument");
-  *out = m->cfg;
-  return SEM_OK;
+  return sem::guarded([&]() -> int {
+    if (!m || !out) return sem::set_error(SEM_EINVAL, "null argument");
+    *out = m->cfg;
+    return SEM_OK;
+  });
 }
 
 int sem_model_free(sem_model* m) {
-  if (!m) return SEM_OK;
-  sem::DeviceGuard dg(m->ctx->device);
-  cudaStreamSynchronize(m->ctx->stream);
-  for (cudaEvent_t e : m->prof_events) cudaEventDestroy(e);
-  sem::drop_graphs(m);
-  for (auto& sl : m->slots)
-    if (sl.done) cudaEventDestroy(sl.done);
-  delete m;
-  return SEM_OK;
+  return sem::guarded([&]() -> int {
+    if (!m) return SEM_OK;
+    sem::DeviceGuard dg(m->ctx->device);
+    cudaStreamSynchronize(m->ctx->stream);
+    for (cudaEvent_t e : m->prof_events) cudaEventDestroy(e);
+    sem::drop_graphs(m);
+    for (auto& sl : m->slots)
+      if (sl.done) cudaEventDestroy(sl.done);
+    delete m;
+    return SEM_OK;
+  });
 }
 
 int sem_model_profile(sem_model* m, int32_t enable) {
-  if (!m) return sem::set_error(SEM_EINVAL, "null argument");
-  m->prof = enable != 0;
-  return SEM_OK;
+  return sem::guarded([&]() -> int {
+    if (!m) return sem::set_error(SEM_EINVAL, "null argument");
+    m->prof = enable != 0;
+    return SEM_OK;
+  });
 }
 
 int sem_model_profile_read(sem_model* m, const char** names, float* total_ms, int32_t* launches, int32_t cap,
                            int32_t* n_out) {
-  if (!m) return sem::set_error(SEM_EINVAL, "null argument");
-  return sem::profile_read(m, names, total_ms, launches, cap, n_out);
+  return sem::guarded([&]() -> int {
+    if (!m) return sem::set_error(SEM_EINVAL, "null argument");
+    return sem::profile_read(m, names, total_ms, launches, cap, n_out);
+  });
 }
 
 int sem_embed(sem_model* m, const int32_t* ids, const int32_t* offsets, int32_t n, const int32_t* dims, float* out) {
-  return sem::model_embed(m, ids, offsets, n, dims, out);
+  return sem::guarded([&]() -> int {
+    return sem::model_embed(m, ids, offsets, n, dims, out);
+  });
 }
 
 int sem_embed_submit(sem_model* m, const int32_t* ids, const int32_t* offsets, int32_t n, const int32_t* dims,
                      uint64_t* ticket) {
-  return sem::model_embed_submit(m, ids, offsets, n, dims, ticket);
+  return sem::guarded([&]() -> int {
+    return sem::model_embed_submit(m, ids, offsets, n, dims, ticket);
+  });
 }
 
-int sem_embed_wait(sem_model* m, uint64_t ticket, float* out) { return sem::model_embed_wait(m, ticket, out); }
+int sem_embed_wait(sem_model* m, uint64_t ticket, float* out) {
+  return sem::guarded([&]() -> int { return sem::model_embed_wait(m, ticket, out); });
+}
 
 int sem_embed_device(sem_model* m, const int32_t* d_ids, const int32_t* h_offsets, int32_t n, int32_t dim, float* d_out,
                      void* stream) {
-  return sem::model_embed_device(m, d_ids, h_offsets, n, dim, d_out, stream);
+  return sem::guarded([&]() -> int {
+    return sem::model_embed_device(m, d_ids, h_offsets, n, dim, d_out, stream);
+  });
 }
 
-int sem_model_check(sem_model* m) { return sem::model_check(m); }
+int sem_model_check(sem_model* m) {
+  return sem::guarded([&]() -> int { return sem::model_check(m); });
+}
 
-int sem_model_set_faithful(sem_model* m, const sem_faithful_config* cfg) { return sem::model_set_faithful(m, cfg); }
+int sem_model_set_faithful(sem_model* m, const sem_faithful_config* cfg) {
+  return sem::guarded([&]() -> int { return sem::model_set_faithful(m, cfg); });
+}
 
 int sem_q8_weight_create(sem_context* ctx, const void* w_q8, int32_t k_in, int32_t n_out, sem_q8_weight** out) {
-  return sem::q8_weight_create(ctx, w_q8, k_in, n_out, out);
+  return sem::guarded([&]() -> int {
+    return sem::q8_weight_create(ctx, w_q8, k_in, n_out, out);
+  });
 }
 
 int sem_q8_weight_free(sem_q8_weight* w) {
-  if (!w) return SEM_OK;
-  sem::DeviceGuard dg(w->ctx->device);
-  cudaStreamSynchronize(w->ctx->stream);
-  delete w;
-  return SEM_OK;
+  return sem::guarded([&]() -> int {
+    if (!w) return SEM_OK;
+    sem::DeviceGuard dg(w->ctx->device);
+    cudaStreamSynchronize(w->ctx->stream);
+    delete w;
+    return SEM_OK;
+  });
 }
 
 int sem_q8_matmul_int8(sem_q8_weight* w, const void* d_codes, const uint32_t* d_absmax, int32_t m, float* d_c,
                        void* stream) {
-  return sem::q8_matmul_int8(w, d_codes, d_absmax, m, d_c, stream);
+  return sem::guarded([&]() -> int {
+    return sem::q8_matmul_int8(w, d_codes, d_absmax, m, d_c, stream);
+  });
 }
 
-int sem_q8_path(int32_t mode) { return sem::set_q8_path(mode); }
+int sem_q8_path(int32_t mode) {
+  return sem::guarded([&]() -> int { return sem::set_q8_path(mode); });
+}
 
 int sem_q8_gemm(sem_q8_weight* w, const float* d_a, int32_t m, float* d_c, void* d_codes, uint32_t* d_absmax,
                 void* stream) {
-  return sem::q8_gemm(w, d_a, m, d_c, d_codes, d_absmax, stream);
+  return sem::guarded([&]() -> int {
+    return sem::q8_gemm(w, d_a, m, d_c, d_codes, d_absmax, stream);
+  });
 }
 
 }  // extern "C"

@@ -32,6 +32,7 @@ extern "C" {
 #define SEM_ENOMEM 3    /* device or host allocation failed */
 #define SEM_EFORMAT 4   /* malformed GGUF or BRUT bytes */
 #define SEM_ENOTFOUND 5 /* tensor / id not found */
+#define SEM_EINTERNAL 6 /* a host-side failure inside the library (e.g. a thread could not start) */
 
 typedef struct sem_context sem_context;
 typedef struct sem_model sem_model;
