@@ -10,7 +10,7 @@ import os
 HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "libsemantica_b200.so")
 
-SEM_OK, SEM_EINVAL, SEM_EDEVICE, SEM_ENOMEM, SEM_EFORMAT, SEM_ENOTFOUND = range(6)
+SEM_OK, SEM_EINVAL, SEM_EDEVICE, SEM_ENOMEM, SEM_EFORMAT, SEM_ENOTFOUND, SEM_EINTERNAL = range(7)
 SEARCH_REFERENCE, SEARCH_EXACT = 0, 1
 
 

@@ -57,3 +57,14 @@ def test_c_consumer_embeds_like_python(consumer, model_path, gpu_model, tmp_path
     want = np.concatenate(gpu_model.forward_batch(ids, offs, dims))
     assert got.shape == want.shape
     np.testing.assert_array_equal(got, want)
+
+
+def test_status_codes_match_header():
+    # the Python binding's SEM_* status codes are the header's
+    import re
+    import _lib
+    text = open(os.path.join(ROOT, "include", "semantica_b200.h")).read()
+    codes = {m.group(1): int(m.group(2)) for m in re.finditer(r"#define (SEM_(?:OK|E[A-Z]+)) (\d+)", text)}
+    assert codes["SEM_EINTERNAL"] == 6
+    for name, value in codes.items():
+        assert getattr(_lib, name) == value, name
