@@ -6,6 +6,7 @@
 // thread, and the vectors return in the caller's order.
 #include <algorithm>
 #include <memory>
+#include <mutex>
 #include <string>
 #include <thread>
 #include <vector>
@@ -149,9 +150,15 @@ int sem_group_set_faithful(sem_group* g, const sem_faithful_config* cfg) {
   return sem::guarded([&]() -> int {
     if (!g) return sem::set_error(SEM_EINVAL, "null argument");
     std::lock_guard<std::mutex> lk(g->mu);
-    for (sem_model* m : g->models) {
-      const int rc = sem_model_set_faithful(m, cfg);
-      if (rc) return rc;
+    std::vector<sem_faithful_config> prev;
+    for (sem_model* m : g->models) prev.push_back(sem::model_faithful_get(m));
+    for (size_t i = 0; i < g->models.size(); ++i) {
+      const int rc = sem_model_set_faithful(g->models[i], cfg);
+      if (rc) {  // the devices already switched go back: every replica keeps one setting
+        const std::string msg = sem_last_error();
+        for (size_t j = 0; j < i; ++j) sem_model_set_faithful(g->models[j], &prev[j]);
+        return sem::set_error(rc, "device %d: %s", g->ctxs[i]->device, msg.c_str());
+      }
     }
     return SEM_OK;
   });

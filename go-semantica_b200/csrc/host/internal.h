@@ -39,6 +39,9 @@ int guarded(F&& body) noexcept {
   }
 }
 
+// The model's current faithful-mode setting (sem_model_set_faithful).
+sem_faithful_config model_faithful_get(const sem_model* m);
+
 // sem_embed's host checks in the reference's order (model_int8.go:149-178):
 // fills dims (NULL dims_in = embed_dim) and the total output floats.
 int validate_embed_request(const sem_model_config& c, const int32_t* ids, const int32_t* offsets, int32_t B,

@@ -915,7 +915,7 @@ int model_set_faithful(sem_model* m, const sem_faithful_config* f) {
   std::lock_guard<std::mutex> lk(ctx->mu);
   SEM_CUDA(cudaStreamSynchronize(ctx->stream));
   const sem_model_config& c = m->cfg;
-  m->rope_swa.release();
+  DevBuf table;  // built before anything changes: a failure leaves the model's setting and tables as they were
   if (cfg.sliding_window > 0 && cfg.rope_base_swa > 0.0f && cfg.rope_base_swa != c.rope_base) {
     // rope_cache.go:15-44 with the sliding layers' base
     const int half = c.head_dim / 2;
@@ -928,13 +928,17 @@ int model_set_faithful(sem_model* m, const sem_faithful_config* f) {
         tab[(size_t)p * half + i] = (float)std::cos((double)theta);
         tab[(size_t)c.max_seq_len * half + (size_t)p * half + i] = (float)std::sin((double)theta);
       }
-    SEM_CUDA(m->rope_swa.ensure(tab.size() * 4));
-    SEM_CUDA(cudaMemcpy(m->rope_swa.p, tab.data(), tab.size() * 4, cudaMemcpyHostToDevice));
+    SEM_CUDA(table.ensure(tab.size() * 4));
+    SEM_CUDA(cudaMemcpy(table.p, tab.data(), tab.size() * 4, cudaMemcpyHostToDevice));
   }
+  std::swap(m->rope_swa.p, table.p);  // the old table is freed with `table`
+  std::swap(m->rope_swa.bytes, table.bytes);
   m->faithful = cfg;
   ++m->faithful_gen;
   return SEM_OK;
 }
+
+sem_faithful_config model_faithful_get(const sem_model* m) { return m->faithful; }
 
 int model_check(sem_model* m) {
   if (!m) return set_error(SEM_EINVAL, "null argument");

@@ -74,3 +74,28 @@ def test_group_errors_and_empty_request(group):
     ids, _ = synth.token_batch(3, [5], TEST_VOCAB)
     v = group.forward_with_dim(ids, 768)
     assert abs(float(np.linalg.norm(v)) - 1.0) < 1e-5
+
+
+@pytest.mark.gpu
+def test_group_faithful_mode(group, gpu_model):
+    # sem_group_set_faithful sets every replica or none: a setting the model
+    # rejects leaves the group's vectors as they were; a sliding window gives
+    # the single device's vectors (short sequences: bit-identical), and the
+    # default setting restores the first ones exactly
+    import _lib
+    ids, offs = synth.token_batch(73, [100, 40, 127], TEST_VOCAB)
+    base = group.forward_batch(ids, offs)
+    with pytest.raises(_lib.SemError, match=r"^device \d+: faithful mode: the model has no dense_2"):
+        group.set_faithful(0, 0, 0.0, True)
+    assert all(np.array_equal(a, b) for a, b in zip(group.forward_batch(ids, offs), base))
+    try:
+        group.set_faithful(64, 2)
+        gpu_model.set_faithful(64, 2)
+        got = group.forward_batch(ids, offs)
+        one = gpu_model.forward_batch(ids, offs)
+        assert all(np.array_equal(a, b) for a, b in zip(got, one))
+        assert not np.array_equal(got[0], base[0])  # 100 tokens reach past the 32-position half window
+    finally:
+        group.set_faithful()
+        gpu_model.set_faithful()
+    assert all(np.array_equal(a, b) for a, b in zip(group.forward_batch(ids, offs), base))
