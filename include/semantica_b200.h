@@ -180,7 +180,9 @@ int sem_group_load(const int32_t *devices, int32_t n_devices, const sem_model_co
 int sem_group_load_gguf(const int32_t *devices, int32_t n_devices, const char *path, sem_group **out);
 int sem_group_size(const sem_group *group, int32_t *out);
 int sem_group_config_get(const sem_group *group, sem_model_config *out);
-/* sem_model_set_faithful on every replica. */
+/* sem_model_set_faithful on every replica, or on none: when one replica fails,
+ * those already switched return to their previous setting and the error names
+ * the device. */
 int sem_group_set_faithful(sem_group *group, const sem_faithful_config *cfg);
 /* sem_embed's contract (same arguments, errors and output layout); the
  * request is validated on the host before any device starts, and a device's
