@@ -40,7 +40,9 @@ typedef struct sem_index sem_index;
 typedef struct sem_q8_weight sem_q8_weight;
 typedef struct sem_group sem_group;
 
-/* Message of the last failed call on this thread (never NULL). */
+/* Message of the last failed call on this thread (never NULL). A Go caller
+ * holds its OS thread (runtime.LockOSThread) from the failing call until it
+ * has read the message: a goroutine may change threads between cgo calls. */
 const char *sem_last_error(void);
 
 /* Number of visible CUDA devices. */
