@@ -9,6 +9,8 @@
 // (the reference quantises one whole sequence per call, quantize.go:29-69).
 #include <cooperative_groups.h>
 
+#include <atomic>
+
 #include "common.cuh"
 #include "kernels.h"
 
@@ -358,12 +360,33 @@ __global__ void __launch_bounds__(kQuantWarps * 32)
   }
 }
 
+// Blocks of one full wave of a grid-stride kernel on the current device (its
+// resident blocks per SM x the SMs), cached per device: a larger grid leaves
+// a partial last wave running alone.
+template <class Kern>
+static int64_t wave_blocks(Kern kernel, int threads, std::atomic<int>* cache) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+  int n = cache[dev].load(std::memory_order_relaxed);
+  if (n == 0) {
+    int per_sm = 0, sms = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, threads, 0) != cudaSuccess || per_sm < 1)
+      per_sm = 1;
+    if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms < 1) sms = 148;
+    n = per_sm * sms;
+    cache[dev].store(n, std::memory_order_relaxed);
+  }
+  return n;
+}
+
 cudaError_t launch_quantize(const float* x, const float* inv_rms, const float* w, int K, SeqMeta meta,
                             const uint32_t* absmax, __half* codes, cudaStream_t stream) {
   if (meta.T == 0) return cudaSuccess;
   if (K % 4 != 0) return cudaErrorInvalidValue;
+  static std::atomic<int> wave[64];
   int64_t blocks = (meta.T + kQuantWarps - 1) / kQuantWarps;
-  if (blocks > 148 * 16) blocks = 148 * 16;
+  const int64_t full = wave_blocks(quantize_kernel, kQuantWarps * 32, wave);
+  if (blocks > full) blocks = full;
   quantize_kernel<<<(unsigned)blocks, kQuantWarps * 32, 0, stream>>>(x, inv_rms, w, K, meta, absmax, codes);
   return cudaGetLastError();
 }
